@@ -1,0 +1,344 @@
+"""Benchmark of the voom_b200 weight-page decode path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1_rans]
+
+A step is one pass of the hot path over one batch of synthetic input with
+the shape of a BASELINE config (see `--workload`).  `value` is device
+throughput with inputs resident in HBM (per-step CUDA events on the launching
+stream, L2 flushed between steps, max over ranks); `e2e` is the same metric
+through the public API with pinned host buffers and the host<->device copies
+inside the timed region.  `--impl reference` times the CPU restatement of the
+reference algorithm (the oracle port: the reference is pure Python and its
+checkout does not travel to the GPU host) on all host cores.
+
+Multi-GPU: one process per GPU (torchrun); pages/frames are independent
+units, so every rank decodes its own copy of the workload with no collective
+(weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workloads
+class C1Rans:
+    """Config 1: one 4096x4096 BF16 tensor (N(0,0.02), 0.1% outlier columns x50)
+    as a VRN1 frame with the reference's default 1 MiB tiles; a step is one full
+    cold decode of the frame (64 independent plane streams)."""
+
+    name = "c1_rans_4096x4096"
+    metric = "BF16 weight-page decode GB/s (bit-exact)"
+    unit = "GB/s"
+    dtype = "u8"
+
+    def __init__(self, device, rank: int):
+        import torch
+
+        from voom_b200 import _device, synthetic
+        from voom_b200.formats import bf16_rans as R
+
+        self.torch = torch
+        self.R = R
+        self.dev = device
+        self.raw = synthetic.outlier_matrix(4096, 4096, seed=rank).tobytes()
+        self.frame, self.stats = R.encode(self.raw, tile_bytes=1 << 20)
+        self.plan = R.plan(self.frame)
+        self.src = _device.upload(self.frame, device)
+        self.tiles = _device.tensor_from_numpy(self.plan.tiles, device)
+        self.out = torch.empty(len(self.raw), dtype=torch.uint8, device=device)
+        self.status = torch.zeros(self.plan.info.n_tiles, dtype=torch.int32, device=device)
+        self.n_tiles = int(self.plan.info.n_tiles)
+        self.pinned_frame = _device.pinned_empty(len(self.frame))
+        self.pinned_frame.numpy()[:] = np.frombuffer(self.frame, np.uint8)
+        self.pinned_out = _device.pinned_empty(len(self.raw))
+        self.units_per_step = len(self.raw)  # decoded bytes
+        self.algo_bytes = len(self.frame) + len(self.raw)
+        self.streams = 2 * int((self.plan.tiles["mode"] == 1).sum())
+
+    def step_device(self, stream_ptr: int):
+        from voom_b200._lib import check, load
+
+        check(load().voom_rans_decode(self.src.data_ptr(), self.tiles.data_ptr(), self.n_tiles,
+                                      self.out.data_ptr(), self.status.data_ptr(), None, None, 0, stream_ptr),
+              "voom_rans_decode")
+
+    def verify(self) -> bool:
+        st = self.status.cpu().numpy()
+        return bool((st == 0).all()) and self.out.cpu().numpy().tobytes() == self.raw
+
+    def step_e2e(self):
+        out = self.R.decode_device(self.pinned_frame, device=self.dev)
+        self.pinned_out.copy_(out, non_blocking=True)
+        return len(self.frame) + 8 * self.n_tiles, len(self.raw) + 4 * self.n_tiles
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        """Oracle (C restatement of bf16_rans.decode) on whole frames, one frame
+        per thread, repeated until `budget_s` of wall time."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import rans as orans
+
+        assert orans.decode(self.frame) == self.raw
+        done = 0
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            while time.perf_counter() - t0 < budget_s:
+                list(pool.map(lambda _: orans.decode(self.frame), range(threads)))
+                done += threads
+        dt = time.perf_counter() - t0
+        return {"value": done * len(self.raw) / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{done} full C1 frame decodes ({len(self.raw)} B each) by the C oracle on {threads} "
+                          f"thread(s), {dt:.1f} s"}
+
+    def config(self) -> dict:
+        return {"workload": self.name, "tile_bytes": 1 << 20, "tiles": self.n_tiles,
+                "independent_streams": self.streams, "frame_bytes": len(self.frame),
+                "raw_bytes": len(self.raw), "ratio": round(len(self.raw) / len(self.frame), 4),
+                "l2": "flushed between steps (512 MiB write)"}
+
+
+WORKLOADS = {"c1_rans": C1Rans}
+DEFAULT_WORKLOAD = "c1_rans"
+
+
+# ------------------------------------------------------------------- main
+def dist_init():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the oracle port of the reference CPU path, rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    wl = WORKLOADS[args.workload]
+    # build the workload's inputs on the host only
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    w = wl(dev, 0)
+    times = []
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = w.cpu_sample(threads, budget_s=args.ref_seconds)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            times.append(w.units_per_step / (r["value"] * 1e9) * 1e3)
+    v = statistics.median(vals)
+    line = {
+        "metric": w.metric, "value": v, "unit": w.unit, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": statistics.median(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded)",
+        "config": w.config(), "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": w.unit, "cores": threads, "kind": "port",
+                         "sample": r["sample"]},
+        "e2e": {"value": v, "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--ref-seconds", type=float, default=4.0)
+    ap.add_argument("--cpu-seconds", type=float, default=6.0)
+    args = ap.parse_args()
+
+    import torch
+
+    world, rank, local = dist_init()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peaks, peaks_kind = load_peaks()
+    w = WORKLOADS[args.workload](dev, rank)
+    stream = torch.cuda.current_stream(dev)
+    sptr = int(stream.cuda_stream)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+
+    # correctness of the measured path on this input
+    w.step_device(sptr)
+    torch.cuda.synchronize()
+    if not w.verify():
+        raise SystemExit("bench: device decode is not bit-exact")
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        w.step_device(sptr)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)  # evict the previous step's data from L2
+        starts[i].record(stream)
+        w.step_device(sptr)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = sum(step_ms) / len(step_ms)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = w.units_per_step * world / (ms * 1e-3) / 1e9
+
+    # end to end through the public API, pinned host buffers, copies inside
+    for _ in range(2):
+        w.step_e2e()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    bi = bo = 0
+    for _ in range(args.steps):
+        bi, bo = w.step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = w.units_per_step * world / (e2e_ms * 1e-3) / 1e9
+
+    achieved = w.algo_bytes / (ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": getattr(w, "traffic", None),
+            "peak_kind": f"{peaks_kind} (hbm_gbs)"}
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = w.cpu_sample(1, budget_s=args.cpu_seconds)
+    if rank == 0:
+        line = {
+            "metric": w.metric, "value": round(value, 4), "unit": w.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+            "data": "synthetic (seeded numpy; BF16 N(0,0.02) with 0.1% outlier columns)",
+            "config": dict(w.config(), parallelism=f"replicas x{world}" if world > 1 else "single"),
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 4), "unit": w.unit, "h2d_bytes_per_step": bi,
+                    "d2h_bytes_per_step": bo},
+            "gpu_launches": args.steps * getattr(w, "launches_per_step", 1), "clocks": clocks,
+            "step_ms_min": round(min(step_ms), 5), "step_ms_max": round(max(step_ms), 5),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+/*
+ * voom_b200.h - C ABI of the B200 (sm_100a) weight-page codec library.
+ *
+ * The library decodes vOOM's lossless BF16 weight-page formats on the GPU:
+ *   - "VRN1" rANS frames            (reference: formats/bf16_rans.py)
+ *   - vpack / vpack2 byte-plane bodies, zstd hi plane + raw lo plane
+ *                                   (reference: formats/packed.py, formats/packed2.py)
+ *   - kv_paged compressed spill pages (reference: runtime/kv_paged.py)
+ * and fuses the rANS page decode with the MoE expert SwiGLU GEMV that consumes
+ * the pages (reference: runtime/layer_runner.py _swiglu / run_moe_mlp).
+ *
+ * Conventions for every entry point:
+ *   - Plain pointers and sizes only.  "d_" pointers are device memory, "h_"
+ *     pointers are host memory.  `stream` is a cudaStream_t passed as void*.
+ *   - Device entry points only enqueue work on `stream`; results (outputs and
+ *     per-item status words) are valid once the stream has been synchronised.
+ *   - Every entry point is re-entrant: no global mutable host state, so two
+ *     host threads may call concurrently on different streams.
+ *   - Return value: VOOM_OK, a negative VOOM_E_* for API misuse or a CUDA
+ *     launch failure, or a positive format status (the codes below), which the
+ *     Python layer maps to the exception the reference raises.
+ */
+#ifndef VOOM_B200_H
+#define VOOM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum {
+  VOOM_OK = 0,
+  VOOM_E_INVALID_ARG = -1, /* null pointer, bad size, misaligned buffer      */
+  VOOM_E_CUDA = -2,        /* a CUDA launch or runtime call failed            */
+  VOOM_E_CAPACITY = -3,    /* caller-provided array or buffer is too small    */
+  VOOM_E_UNSUPPORTED = -4, /* a valid input outside what this build decodes   */
+
+  /* formats/bf16_rans.py decode() ValueError messages, in the order the
+   * reference checks them (bf16_rans.py:97-130, 180-222). */
+  VOOM_RANS_TRUNC_FRAME = 101,         /* "truncated rANS frame"               */
+  VOOM_RANS_NOT_FRAME = 102,           /* "not a vOOM rANS frame"              */
+  VOOM_RANS_TRUNC_TILE_HEADER = 103,   /* "truncated rANS tile header"         */
+  VOOM_RANS_TRUNC_TILE_PAYLOAD = 104,  /* "truncated rANS tile payload"        */
+  VOOM_RANS_RAW_SIZE_MISMATCH = 105,   /* "raw rANS tile size mismatch"        */
+  VOOM_RANS_TRUNC_PLANE_HEADER = 106,  /* "truncated rANS plane header"        */
+  VOOM_RANS_TRUNC_PLANE_PAYLOAD = 107, /* "truncated rANS plane payload"       */
+  VOOM_RANS_BAD_FREQ_TOTAL = 108,      /* "invalid rANS frequency total"       */
+  VOOM_RANS_TRAILING_RENORM = 109,     /* "rANS plane has trailing renormalization bytes" */
+  VOOM_RANS_TILE_TRAILING = 110,       /* "compressed rANS tile has trailing bytes" */
+  VOOM_RANS_UNKNOWN_MODE = 111,        /* "unknown rANS tile mode {mode}"      */
+  VOOM_RANS_CHECKSUM = 112,            /* "rANS tile checksum mismatch"        */
+  VOOM_RANS_LENGTH_MISMATCH = 113      /* "rANS frame length mismatch"         */
+};
+
+/* ------------------------------------------------------------ bf16_rans */
+
+/* Per-tile decode plan.  Offsets are absolute byte offsets into the device
+ * source buffer (src) and the device output buffer (dst), so one plan array
+ * can describe tiles of many frames packed into one buffer. */
+typedef struct voom_rans_tile {
+  uint64_t src;         /* mode 0: first payload byte; mode 1: unused        */
+  uint64_t dst;         /* output offset of the tile's first decoded byte    */
+  uint64_t low_freq;    /* mode 1: offset of the low plane's 256 x u16 table */
+  uint64_t high_freq;   /* mode 1: offset of the high plane's table          */
+  uint32_t low_payload; /* mode 1: low plane payload bytes (>= 4)            */
+  uint32_t high_payload;/* mode 1: high plane payload bytes (>= 4)           */
+  uint32_t raw_len;     /* decoded bytes of this tile                         */
+  uint32_t crc32;       /* expected zlib CRC-32 of the decoded tile          */
+  uint32_t mode;        /* 0 = stored verbatim, 1 = two rANS byte planes     */
+  uint32_t flags;       /* VOOM_RANS_DO_* bits                               */
+} voom_rans_tile;
+
+enum {
+  VOOM_RANS_DO_LOW = 1u,  /* decode the low plane                           */
+  VOOM_RANS_DO_HIGH = 2u, /* decode the high plane                          */
+  VOOM_RANS_DO_CRC = 4u,  /* verify the tile CRC-32 (or copy a mode 0 tile) */
+  VOOM_RANS_DO_COPY = 8u  /* mode 0: copy the stored bytes                  */
+};
+
+/* Bits of the per-tile status word written by voom_rans_decode. */
+enum {
+  VOOM_RANS_ST_LOW_TRAILING = 1u,  /* low plane left renormalisation bytes  */
+  VOOM_RANS_ST_HIGH_TRAILING = 2u, /* high plane left renormalisation bytes */
+  VOOM_RANS_ST_CRC_MISMATCH = 4u   /* decoded tile fails its CRC-32          */
+};
+
+typedef struct voom_rans_plan_info {
+  uint64_t raw_size;      /* frame header raw size                          */
+  uint64_t out_bytes;     /* sum of raw_len over planned tiles              */
+  uint32_t tile_bytes;    /* frame header tile size                          */
+  uint32_t tile_count;    /* frame header tile count                         */
+  uint32_t n_tiles;       /* planned tiles (descriptors needed)             */
+  int32_t struct_error;   /* first structural error (0 = none)             */
+  uint32_t struct_tile;   /* tile index of struct_error                     */
+  uint32_t struct_ordinal;/* position of struct_error within the tile       */
+  uint32_t bad_mode;      /* mode byte for VOOM_RANS_UNKNOWN_MODE           */
+  uint32_t frame_end;     /* 1 if the walk reached the end-of-frame checks  */
+} voom_rans_plan_info;
+
+/* Walks one VRN1 frame held in host memory the way formats/bf16_rans.py:180-222
+ * and _decode_plane (:97-130) walk it, without decoding any symbol: frame and
+ * tile headers, plane headers, payload bounds and frequency totals.  Stops at
+ * the first structural error; every tile before it (and the planes of the
+ * failing tile that the reference decodes before failing) is planned.
+ * `src_base`/`dst_base` are added to every offset written.  With
+ * max_tiles == 0 only `info` is filled (sizing pass).
+ * Returns VOOM_OK, or VOOM_E_CAPACITY if max_tiles < info->n_tiles.
+ * Replaces: formats/bf16_rans.py:180-222 (header walk of decode()). */
+int voom_rans_plan(const uint8_t* h_frame, uint64_t frame_len, uint64_t src_base,
+                   uint64_t dst_base, voom_rans_tile* h_tiles, uint32_t max_tiles,
+                   voom_rans_plan_info* info);
+
+/* Decodes planned tiles on the GPU: per-plane rANS decode (bf16_rans.py:97-130),
+ * byte-plane interleave into the output (:211-213), CRC-32 check (:217).
+ * d_src holds the frame bytes, padded to a multiple of 16 bytes with at least
+ * 16 readable bytes after the last frame byte.  d_out receives decoded bytes at
+ * each tile's dst.  d_status (n_tiles words) receives VOOM_RANS_ST_* bits.
+ * If d_ckpt is non-null, the low/high plane decoders record a checkpoint
+ * (state, cursor) every `ckpt_every` symbols (a power of two >= 64) at
+ * d_ckpt[ckpt_base[t] + 2*k + plane] as two u32 words; ckpt_base is a device
+ * array of n_tiles u32 (pass NULL when d_ckpt is NULL).
+ * Replaces: formats/bf16_rans.py:180-222 decode() (symbol work). */
+int voom_rans_decode(const uint8_t* d_src, const voom_rans_tile* d_tiles, uint32_t n_tiles,
+                     uint8_t* d_out, uint32_t* d_status, uint32_t* d_ckpt,
+                     const uint32_t* d_ckpt_base, uint32_t ckpt_every, void* stream);
+
+/* Decodes planned tiles from a checkpoint index built by voom_rans_decode:
+ * each (tile, plane, segment of ckpt_every symbols) is decoded independently
+ * and must land exactly on the next checkpoint; the CRC is verified when the
+ * tile has VOOM_RANS_DO_CRC.  Same status bits as voom_rans_decode; a segment
+ * that does not meet its successor checkpoint sets the *_TRAILING bit.
+ * Replaces: formats/bf16_rans.py:180-222 decode() for pages kept resident
+ * in HBM and decoded on every use. */
+int voom_rans_decode_indexed(const uint8_t* d_src, const voom_rans_tile* d_tiles,
+                             uint32_t n_tiles, uint8_t* d_out, uint32_t* d_status,
+                             const uint32_t* d_ckpt, const uint32_t* d_ckpt_base,
+                             uint32_t ckpt_every, void* stream);
+
+/* Checkpoint words a tile needs for a given interval (2 per plane-segment
+ * boundary, both planes).  Host helper. */
+uint64_t voom_rans_ckpt_words(uint32_t raw_len, uint32_t ckpt_every);
+
+/* Pack side: encodes n bytes into a VRN1 frame byte-identical to
+ * formats/bf16_rans.py encode() (:148-177), tiles encoded on `threads` host
+ * threads (<= 0: all cores).  With h_out == NULL, *out_len receives the
+ * worst-case frame size (size the buffer with it).  stats (may be NULL):
+ * [0] tiles, [1] tiles stored compressed.
+ * Replaces: formats/bf16_rans.py:148-177 (encode, _encode_plane,
+ * _normalize_frequencies). */
+int voom_rans_encode(const uint8_t* h_data, uint64_t n, uint32_t tile_bytes, uint8_t* h_out,
+                     uint64_t out_cap, uint64_t* out_len, uint64_t* stats, int threads);
+
+/* Combines the plan's structural error with the per-tile GPU status (host
+ * copies) into the error formats/bf16_rans.py decode() raises first.
+ * Returns VOOM_OK or a VOOM_RANS_* code; *err_tile receives the tile index. */
+int voom_rans_resolve(const voom_rans_plan_info* info, const uint32_t* h_status,
+                      uint32_t n_tiles, uint32_t* err_tile);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VOOM_B200_H */

@@ -1,0 +1,575 @@
+// GPU decoder for vOOM "VRN1" BF16 rANS frames (reference: formats/bf16_rans.py).
+//
+// Format (bf16_rans.py:26-33): frame header <4sIII> (magic, raw_size,
+// tile_bytes, tile_count); per tile <BIII> (mode, raw_len, payload_len, crc32);
+// mode 1 = two planes (low = even bytes, high = odd bytes), each
+// <I payload_len><256 x u16 freq (sum 4096)><u32 initial state><renorm bytes>.
+//
+// Parallelism: the format's independent unit is one (tile, plane) stream, a
+// serial chain of 32-bit rANS states.  The cold kernel gives each tile one
+// CTA; lanes 0 and 1 of warp 0 decode the low and high plane in lockstep,
+// exchange 8 bytes by shuffle every 16 symbols and write the interleaved BF16
+// bytes with 128-bit stores.  The decode table (4096 slots, one u32 each:
+// symbol | (freq-1) << 8 | (slot - cum) << 20) lives in shared memory, so a
+// symbol costs one shared load.  Renormalisation bytes come from a 64-bit
+// register buffer refilled one aligned word ahead.  While decoding, the cold
+// kernel can record (state, cursor) checkpoints; the indexed kernel then
+// decodes every checkpoint segment in parallel (one lane pair per segment)
+// and checks that each segment lands on its successor checkpoint.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace voom {
+namespace {
+
+constexpr uint32_t kRansL = 1u << 23;
+constexpr int kThreads = 256;
+
+__device__ const CrcTables g_crc = make_crc_tables();
+__device__ const CrcPow2 g_pow2 = make_crc_pow2();
+
+// Position of each check inside a tile, in the order bf16_rans.py performs it.
+enum : uint32_t {
+  ORD_TILE_HEADER = 1,
+  ORD_TILE_PAYLOAD = 2,
+  ORD_RAW_SIZE = 3,
+  ORD_LOW_HEADER = 4,
+  ORD_LOW_PAYLOAD = 5,
+  ORD_LOW_TOTAL = 6,
+  ORD_LOW_TRAILING = 7,
+  ORD_HIGH_HEADER = 8,
+  ORD_HIGH_PAYLOAD = 9,
+  ORD_HIGH_TOTAL = 10,
+  ORD_HIGH_TRAILING = 11,
+  ORD_TILE_TRAILING = 12,
+  ORD_UNKNOWN_MODE = 13,
+  ORD_CRC = 14
+};
+
+struct SharedPlanes {
+  uint32_t lut[2][4096];  // reused as the CRC slicing table after decoding
+  uint32_t cum[2][257];
+  uint32_t pow2[64];
+  uint32_t red[kThreads / 32];
+  uint32_t flags;
+  uint32_t degenerate[2];
+};
+
+__device__ __forceinline__ uint32_t ld_u8(const uint8_t* p) { return __ldg(p); }
+__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
+  return ld_u8(p) | (ld_u8(p + 1) << 8) | (ld_u8(p + 2) << 16) | (ld_u8(p + 3) << 24);
+}
+
+// Renormalisation byte source: bytes at payload[cur..] little-endian in `bb`,
+// refilled from aligned 32-bit words one word ahead of use.
+struct ByteReader {
+  uint64_t bb;
+  int nbits;
+  const uint32_t* wp;
+  uint32_t pending;
+
+  __device__ __forceinline__ void init(const uint8_t* p) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    int o = int(a & 3u);
+    bb = uint64_t(__ldg(w) >> (8 * o));
+    nbits = 32 - 8 * o;
+    bb |= uint64_t(__ldg(w + 1)) << nbits;
+    nbits += 32;
+    pending = __ldg(w + 2);
+    wp = w + 3;
+  }
+  __device__ __forceinline__ void refill() {
+    if (nbits <= 32) {
+      bb |= uint64_t(pending) << nbits;
+      nbits += 32;
+      pending = __ldg(wp);
+      wp++;
+    }
+  }
+  __device__ __forceinline__ uint32_t take() {
+    uint32_t b = uint32_t(bb) & 0xFFu;
+    bb >>= 8;
+    nbits -= 8;
+    return b;
+  }
+};
+
+// One decoded symbol of a non-degenerate plane, with the reference's
+// renormalisation loop `while state < L and cursor < len` (bf16_rans.py:125).
+__device__ __forceinline__ uint32_t rans_step(const uint32_t* __restrict__ lut, uint32_t& x,
+                                              uint32_t& cur, uint32_t len, ByteReader& rd) {
+  uint32_t slot = x & 4095u;
+  uint32_t e = lut[slot];
+  x = (((e >> 8) & 4095u) + 1u) * (x >> 12) + (e >> 20);
+  if (x < kRansL) {
+    if (cur < len) {
+      x = (x << 8) | rd.take();
+      cur++;
+      if (x < kRansL && cur < len) {
+        x = (x << 8) | rd.take();
+        cur++;
+        while (x < kRansL && cur < len) {  // only reachable from malformed states
+          rd.refill();
+          x = (x << 8) | rd.take();
+          cur++;
+        }
+      }
+    }
+  }
+  rd.refill();
+  return e & 0xFFu;
+}
+
+// Degenerate plane (all frequencies zero): the reference's lookup is all
+// symbol 0 with frequency 0, so the next state is the slot itself.
+__device__ __forceinline__ uint32_t rans_step_degenerate(uint32_t& x, uint32_t& cur, uint32_t len,
+                                                         ByteReader& rd) {
+  x = x & 4095u;
+  while (x < kRansL && cur < len) {
+    rd.refill();
+    x = (x << 8) | rd.take();
+    cur++;
+  }
+  rd.refill();
+  return 0;
+}
+
+// Builds the decode table of one plane from its 256 x u16 frequency table.
+// All threads of the block participate.  Sets sh.degenerate[p].
+__device__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
+  const int tid = threadIdx.x;
+  uint32_t f = 0;
+  if (tid < 256) f = ld_u8(freq + 2 * tid) | (ld_u8(freq + 2 * tid + 1) << 8);
+  // exclusive block scan over 256 values (kThreads == 256)
+  uint32_t v = f;
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int o = 1; o < 32; o <<= 1) {
+    uint32_t n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) sh.red[warp] = v;
+  __syncthreads();
+  uint32_t base = 0;
+  for (int w = 0; w < warp; w++) base += sh.red[w];
+  if (tid < 256) sh.cum[p][tid] = base + v - f;
+  if (tid == 255) sh.cum[p][256] = base + v;
+  __syncthreads();
+  const uint32_t total = sh.cum[p][256];
+  if (tid == 0) sh.degenerate[p] = (total == 0);
+  if (total == 4096u) {
+    for (int slot = tid; slot < 4096; slot += kThreads) {
+      // last symbol s with cum[s] <= slot (zero-frequency symbols are skipped)
+      int lo = 0, hi = 256;
+      while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (sh.cum[p][mid] <= uint32_t(slot)) lo = mid; else hi = mid - 1;
+      }
+      uint32_t c = sh.cum[p][lo];
+      uint32_t fs = sh.cum[p][lo + 1] - c;
+      sh.lut[p][slot] = uint32_t(lo) | ((fs - 1u) << 8) | ((uint32_t(slot) - c) << 20);
+    }
+  }
+  __syncthreads();
+}
+
+// Interleaves this lane's 16 symbols (a0..a3) with its partner's into the 32
+// output bytes of the chunk; lane 0 (low plane) writes the first 16 bytes,
+// lane 1 (high plane) the second.  `dst` is 16-byte aligned.
+__device__ __forceinline__ void store_pair16(uint8_t* dst, uint32_t lane, uint32_t a0, uint32_t a1,
+                                             uint32_t a2, uint32_t a3, unsigned mask) {
+  uint32_t s0 = lane ? a0 : a2, s1 = lane ? a1 : a3;
+  uint32_t r0 = __shfl_xor_sync(mask, s0, 1);
+  uint32_t r1 = __shfl_xor_sync(mask, s1, 1);
+  uint32_t lo0 = lane ? r0 : a0, lo1 = lane ? r1 : a1;
+  uint32_t hi0 = lane ? a2 : r0, hi1 = lane ? a3 : r1;
+  uint4 o;
+  o.x = __byte_perm(lo0, hi0, 0x5140);
+  o.y = __byte_perm(lo0, hi0, 0x7362);
+  o.z = __byte_perm(lo1, hi1, 0x5140);
+  o.w = __byte_perm(lo1, hi1, 0x7362);
+  *reinterpret_cast<uint4*>(dst + 16 * lane) = o;
+}
+
+struct PlaneRun {
+  uint32_t x, cur, len;
+  ByteReader rd;
+};
+
+// Decodes `n` symbols of one plane with one byte store per symbol (stride 2).
+// Used for tails, unaligned tiles, degenerate planes and partial tiles.
+__device__ __forceinline__ void decode_generic(const uint32_t* lut, bool degenerate, PlaneRun& r, uint32_t n,
+                               uint32_t first, uint8_t* out, uint32_t* ckpt, uint32_t every,
+                               uint32_t limit_k, uint32_t plane) {
+  for (uint32_t i = 0; i < n; i++) {
+    uint32_t s = degenerate ? rans_step_degenerate(r.x, r.cur, r.len, r.rd)
+                            : rans_step(lut, r.x, r.cur, r.len, r.rd);
+    out[2u * i] = uint8_t(s);
+    if (ckpt) {
+      uint32_t done = first + i + 1;
+      if ((done & (every - 1)) == 0) {
+        uint32_t k = done / every;
+        if (k <= limit_k) {
+          ckpt[(k - 1) * 4 + plane * 2] = r.x;
+          ckpt[(k - 1) * 4 + plane * 2 + 1] = r.cur;
+        }
+      }
+    }
+  }
+}
+
+// Lockstep pair decode of `nchunks` x 16 symbols: lane 0 low plane, lane 1
+// high plane; both planes must be non-degenerate and `out` 16-byte aligned.
+__device__ __forceinline__ void decode_pair_fast(const uint32_t* lut, PlaneRun& r, uint32_t nchunks, uint32_t first,
+                                 uint8_t* out, uint32_t lane, uint32_t* ckpt, uint32_t every,
+                                 uint32_t limit_k, unsigned mask) {
+  for (uint32_t c = 0; c < nchunks; c++) {
+    uint32_t a[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      uint32_t s0 = rans_step(lut, r.x, r.cur, r.len, r.rd);
+      uint32_t s1 = rans_step(lut, r.x, r.cur, r.len, r.rd);
+      uint32_t s2 = rans_step(lut, r.x, r.cur, r.len, r.rd);
+      uint32_t s3 = rans_step(lut, r.x, r.cur, r.len, r.rd);
+      a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+    }
+    store_pair16(out + 32u * c, lane, a[0], a[1], a[2], a[3], mask);
+    if (ckpt) {
+      uint32_t done = first + 16u * (c + 1);
+      if ((done & (every - 1)) == 0) {
+        uint32_t k = done / every;
+        if (k <= limit_k) {
+          ckpt[(k - 1) * 4 + lane * 2] = r.x;
+          ckpt[(k - 1) * 4 + lane * 2 + 1] = r.cur;
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void plane_start(PlaneRun& r, const uint8_t* src, uint64_t freq_off,
+                                            uint32_t payload_len, uint32_t x0, uint32_t cur0,
+                                            bool from_ckpt) {
+  const uint8_t* payload = src + freq_off + 512;
+  r.len = payload_len;
+  r.x = from_ckpt ? x0 : ld_u32_unaligned(payload);
+  r.cur = from_ckpt ? cur0 : 4u;
+  r.rd.init(payload + r.cur);
+}
+
+__device__ __forceinline__ void load_crc_tables(SharedPlanes& sh) {
+  uint32_t* t = &sh.lut[0][0];
+  const uint32_t* g = &g_crc.t[0][0];
+  for (int i = threadIdx.x; i < 8 * 256; i += kThreads) t[i] = g[i];
+  if (threadIdx.x < 64) sh.pow2[threadIdx.x] = g_pow2.p[threadIdx.x];
+  __syncthreads();
+}
+
+__device__ __forceinline__ void finish_tile(SharedPlanes& sh, const voom_rans_tile& tl, const uint8_t* src,
+                            uint8_t* out, uint32_t* status) {
+  __syncthreads();  // decoded bytes visible, LUT no longer needed
+  uint32_t st = sh.flags;
+  if ((tl.flags & VOOM_RANS_DO_CRC) && !(st & (VOOM_RANS_ST_LOW_TRAILING | VOOM_RANS_ST_HIGH_TRAILING))) {
+    load_crc_tables(sh);
+    const uint8_t* p = tl.mode == 0 ? src + tl.src : out + tl.dst;
+    uint32_t crc = block_crc32(reinterpret_cast<const uint32_t(*)[256]>(&sh.lut[0][0]), sh.pow2, p,
+                               tl.raw_len, sh.red);
+    if (crc != tl.crc32) st |= VOOM_RANS_ST_CRC_MISMATCH;
+  }
+  if (threadIdx.x == 0) status[blockIdx.x] = st;
+}
+
+__device__ __forceinline__ void copy_stored(const uint8_t* src, uint8_t* dst, uint64_t n) {
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0) {
+    uint64_t nv = n >> 4;
+    for (uint64_t i = threadIdx.x; i < nv; i += kThreads)
+      reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+    for (uint64_t i = (nv << 4) + threadIdx.x; i < n; i += kThreads) dst[i] = src[i];
+  } else {
+    for (uint64_t i = threadIdx.x; i < n; i += kThreads) dst[i] = src[i];
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* __restrict__ src,
+                                                             const voom_rans_tile* __restrict__ tiles,
+                                                             uint8_t* __restrict__ out,
+                                                             uint32_t* __restrict__ status,
+                                                             uint32_t* __restrict__ ckpt,
+                                                             const uint32_t* __restrict__ ckpt_base,
+                                                             uint32_t every) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SharedPlanes& sh = *reinterpret_cast<SharedPlanes*>(smem_raw);
+  const voom_rans_tile tl = tiles[blockIdx.x];
+  if (threadIdx.x == 0) sh.flags = 0;
+  if (tl.mode == 0) {
+    if (tl.flags & VOOM_RANS_DO_COPY) copy_stored(src + tl.src, out + tl.dst, tl.raw_len);
+    finish_tile(sh, tl, src, out, status);
+    return;
+  }
+  const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
+  if (do_low) build_lut(sh, 0, src + tl.low_freq);
+  if (do_high) build_lut(sh, 1, src + tl.high_freq);
+  const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
+  uint32_t* ck = ckpt ? ckpt + ckpt_base[blockIdx.x] : nullptr;
+  const uint32_t nseg = (n_low + every - 1) / (every ? every : 1);
+  const uint32_t limit_k = nseg ? nseg - 1 : 0;
+  if (threadIdx.x < 2) {
+    const uint32_t lane = threadIdx.x;
+    const bool active = lane ? do_high : do_low;
+    if (active) {
+      PlaneRun r;
+      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
+                  0, 0, false);
+      const uint32_t n = lane ? n_high : n_low;
+      uint8_t* o = out + tl.dst + lane;
+      const bool fast = do_low && do_high && !sh.degenerate[0] && !sh.degenerate[1] &&
+                        ((reinterpret_cast<uintptr_t>(out + tl.dst) & 15u) == 0);
+      uint32_t done = 0;
+      if (fast) {
+        uint32_t nchunks = n_high / 16;  // n_high <= n_low
+        decode_pair_fast(sh.lut[lane], r, nchunks, 0, out + tl.dst, lane, ck, every, limit_k, 0x3u);
+        done = 16 * nchunks;
+      }
+      decode_generic(sh.lut[lane], sh.degenerate[lane], r, n - done, done, o + 2 * done, ck, every,
+                     limit_k, lane);
+      if (r.cur != r.len)
+        atomicOr(&sh.flags, lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING);
+    }
+  }
+  finish_tile(sh, tl, src, out, status);
+}
+
+__global__ void __launch_bounds__(kThreads) rans_indexed_kernel(
+    const uint8_t* __restrict__ src, const voom_rans_tile* __restrict__ tiles, uint8_t* __restrict__ out,
+    uint32_t* __restrict__ status, const uint32_t* __restrict__ ckpt,
+    const uint32_t* __restrict__ ckpt_base, uint32_t every) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SharedPlanes& sh = *reinterpret_cast<SharedPlanes*>(smem_raw);
+  const voom_rans_tile tl = tiles[blockIdx.x];
+  if (threadIdx.x == 0) sh.flags = 0;
+  if (tl.mode == 0) {
+    if (tl.flags & VOOM_RANS_DO_COPY) copy_stored(src + tl.src, out + tl.dst, tl.raw_len);
+    finish_tile(sh, tl, src, out, status);
+    return;
+  }
+  const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
+  if (do_low) build_lut(sh, 0, src + tl.low_freq);
+  if (do_high) build_lut(sh, 1, src + tl.high_freq);
+  const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
+  const uint32_t nseg = n_low ? (n_low + every - 1) / every : 1;
+  const uint32_t nb = nseg - 1;  // checkpoint boundaries 1..nb
+  const uint32_t* ck = ckpt + ckpt_base[blockIdx.x];
+  const uint32_t lane = threadIdx.x & 1u;
+  const unsigned mask = 0x3u << (threadIdx.x & 30u);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(out + tl.dst) & 15u) == 0);
+  const bool fast_ok = do_low && do_high && !sh.degenerate[0] && !sh.degenerate[1] && aligned;
+  const bool active = lane ? do_high : do_low;
+  const uint32_t n = lane ? n_high : n_low;
+  uint32_t bad = 0;
+  for (uint32_t seg = threadIdx.x >> 1; seg < nseg; seg += kThreads / 2) {
+    const uint32_t first = seg * every;
+    const uint32_t cnt = first < n ? min(every, n - first) : 0u;
+    PlaneRun r;
+    if (active) {
+      uint32_t x0 = 0, c0 = 0;
+      if (seg) {
+        x0 = ck[(seg - 1) * 4 + lane * 2];
+        c0 = ck[(seg - 1) * 4 + lane * 2 + 1];
+      }
+      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
+                  x0, c0, seg != 0);
+    }
+    // Both lanes of a pair run the fast path together only when both planes
+    // have a full segment; otherwise each lane takes the generic path.
+    const uint32_t cnt_high = first < n_high ? min(every, n_high - first) : 0u;
+    const bool pair_fast = fast_ok && cnt_high == every;  // then the low count is `every` too
+    uint32_t done = 0;
+    if (pair_fast) {
+      decode_pair_fast(sh.lut[lane], r, every / 16, first, out + tl.dst + 2u * first, lane, nullptr,
+                       every, 0, mask);
+      done = every;
+    }
+    if (active) {
+      decode_generic(sh.lut[lane], sh.degenerate[lane], r, cnt - done, first + done,
+                     out + tl.dst + lane + 2u * (first + done), nullptr, every, 0, lane);
+      const bool last = (seg + 1 > nb) || ((seg + 1) * every > n);
+      if (last) {
+        if (r.cur != r.len) bad |= lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING;
+      } else if (r.x != ck[seg * 4 + lane * 2] || r.cur != ck[seg * 4 + lane * 2 + 1]) {
+        bad |= lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING;
+      }
+    }
+  }
+  if (bad) atomicOr(&sh.flags, bad);
+  finish_tile(sh, tl, src, out, status);
+}
+
+inline uint32_t rd32(const uint8_t* p) {
+  return uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16) | (uint32_t(p[3]) << 24);
+}
+
+bool valid_every(uint32_t e) { return e >= 64 && (e & (e - 1)) == 0; }
+
+}  // namespace
+}  // namespace voom
+
+using namespace voom;
+
+VOOM_API uint64_t voom_rans_ckpt_words(uint32_t raw_len, uint32_t every) {
+  if (!valid_every(every)) return 0;
+  uint64_t n_low = (uint64_t(raw_len) + 1) / 2;
+  uint64_t nseg = n_low ? (n_low + every - 1) / every : 1;
+  return 4 * (nseg - 1);
+}
+
+VOOM_API int voom_rans_plan(const uint8_t* f, uint64_t n, uint64_t src_base, uint64_t dst_base,
+                            voom_rans_tile* tiles, uint32_t max_tiles, voom_rans_plan_info* info) {
+  if (!info || (!f && n)) return VOOM_E_INVALID_ARG;
+  memset(info, 0, sizeof(*info));
+  uint32_t planned = 0;
+  auto emit = [&](const voom_rans_tile& d) {
+    if (tiles && planned < max_tiles) tiles[planned] = d;
+    planned++;
+  };
+  auto fail = [&](int code, uint32_t tile, uint32_t ord) {
+    info->struct_error = code;
+    info->struct_tile = tile;
+    info->struct_ordinal = ord;
+  };
+  if (n < 16) {
+    fail(VOOM_RANS_TRUNC_FRAME, 0, 0);
+  } else if (memcmp(f, "VRN1", 4) != 0) {
+    fail(VOOM_RANS_NOT_FRAME, 0, 0);
+  } else {
+    info->raw_size = rd32(f + 4);
+    info->tile_bytes = rd32(f + 8);
+    info->tile_count = rd32(f + 12);
+    uint64_t pos = 16, out = 0;
+    bool broke = false;
+    for (uint64_t t = 0; t < info->tile_count && !broke; t++) {
+      const uint32_t ti = uint32_t(t);
+      if (pos + 13 > n) { fail(VOOM_RANS_TRUNC_TILE_HEADER, ti, ORD_TILE_HEADER); broke = true; break; }
+      const uint32_t mode = f[pos];
+      const uint32_t raw = rd32(f + pos + 1), pay = rd32(f + pos + 5), crc = rd32(f + pos + 9);
+      pos += 13;
+      const uint64_t end = pos + pay;
+      if (end > n) { fail(VOOM_RANS_TRUNC_TILE_PAYLOAD, ti, ORD_TILE_PAYLOAD); broke = true; break; }
+      voom_rans_tile d;
+      memset(&d, 0, sizeof d);
+      d.dst = dst_base + out;
+      d.raw_len = raw;
+      d.crc32 = crc;
+      d.mode = mode;
+      if (mode == 0) {
+        if (pay != raw) { fail(VOOM_RANS_RAW_SIZE_MISMATCH, ti, ORD_RAW_SIZE); broke = true; break; }
+        d.src = src_base + pos;
+        d.flags = VOOM_RANS_DO_COPY | VOOM_RANS_DO_CRC;
+      } else if (mode == 1) {
+        // low plane (bf16_rans.py:97-114)
+        uint64_t avail = pay, p = pos;
+        if (avail < 516) { fail(VOOM_RANS_TRUNC_PLANE_HEADER, ti, ORD_LOW_HEADER); broke = true; break; }
+        uint64_t psz = rd32(f + p);
+        if (psz < 4 || 516 + psz > avail) { fail(VOOM_RANS_TRUNC_PLANE_PAYLOAD, ti, ORD_LOW_PAYLOAD); broke = true; break; }
+        uint64_t tot = 0;
+        for (int s = 0; s < 256; s++) tot += uint32_t(f[p + 4 + 2 * s]) | (uint32_t(f[p + 5 + 2 * s]) << 8);
+        if (tot != 0 && tot != 4096) { fail(VOOM_RANS_BAD_FREQ_TOTAL, ti, ORD_LOW_TOTAL); broke = true; break; }
+        d.low_freq = src_base + p + 4;
+        d.low_payload = uint32_t(psz);
+        d.flags = VOOM_RANS_DO_LOW;
+        uint64_t used = 516 + psz;
+        // high plane
+        uint64_t avail2 = avail - used, p2 = pos + used;
+        if (avail2 < 516) { fail(VOOM_RANS_TRUNC_PLANE_HEADER, ti, ORD_HIGH_HEADER); emit(d); out += raw; broke = true; break; }
+        uint64_t psz2 = rd32(f + p2);
+        if (psz2 < 4 || 516 + psz2 > avail2) { fail(VOOM_RANS_TRUNC_PLANE_PAYLOAD, ti, ORD_HIGH_PAYLOAD); emit(d); out += raw; broke = true; break; }
+        uint64_t tot2 = 0;
+        for (int s = 0; s < 256; s++) tot2 += uint32_t(f[p2 + 4 + 2 * s]) | (uint32_t(f[p2 + 5 + 2 * s]) << 8);
+        if (tot2 != 0 && tot2 != 4096) { fail(VOOM_RANS_BAD_FREQ_TOTAL, ti, ORD_HIGH_TOTAL); emit(d); out += raw; broke = true; break; }
+        d.high_freq = src_base + p2 + 4;
+        d.high_payload = uint32_t(psz2);
+        d.flags |= VOOM_RANS_DO_HIGH;
+        if (used + 516 + psz2 != pay) { fail(VOOM_RANS_TILE_TRAILING, ti, ORD_TILE_TRAILING); emit(d); out += raw; broke = true; break; }
+        d.flags |= VOOM_RANS_DO_CRC;
+      } else {
+        fail(VOOM_RANS_UNKNOWN_MODE, ti, ORD_UNKNOWN_MODE);
+        info->bad_mode = mode;
+        broke = true;
+        break;
+      }
+      emit(d);
+      out += raw;
+      pos = end;
+    }
+    info->out_bytes = out;
+    if (!broke) {
+      info->frame_end = 1;
+      if (pos != n || out != info->raw_size) fail(VOOM_RANS_LENGTH_MISMATCH, info->tile_count, 0);
+    }
+  }
+  info->n_tiles = planned;
+  if (tiles && planned > max_tiles) return VOOM_E_CAPACITY;
+  return VOOM_OK;
+}
+
+VOOM_API int voom_rans_resolve(const voom_rans_plan_info* info, const uint32_t* st, uint32_t n_tiles,
+                               uint32_t* err_tile) {
+  if (!info || (n_tiles && !st)) return VOOM_E_INVALID_ARG;
+  uint32_t dummy;
+  if (!err_tile) err_tile = &dummy;
+  *err_tile = 0;
+  for (uint32_t t = 0; t < n_tiles; t++) {
+    const bool here = info->struct_error && t == info->struct_tile;
+    const uint32_t lim = here ? info->struct_ordinal : 0xFFFFFFFFu;
+    *err_tile = t;
+    if ((st[t] & VOOM_RANS_ST_LOW_TRAILING) && ORD_LOW_TRAILING < lim) return VOOM_RANS_TRAILING_RENORM;
+    if ((st[t] & VOOM_RANS_ST_HIGH_TRAILING) && ORD_HIGH_TRAILING < lim) return VOOM_RANS_TRAILING_RENORM;
+    if ((st[t] & VOOM_RANS_ST_CRC_MISMATCH) && ORD_CRC < lim) return VOOM_RANS_CHECKSUM;
+    if (here) return info->struct_error;
+  }
+  if (info->struct_error) {
+    *err_tile = info->struct_tile;
+    return info->struct_error;
+  }
+  return VOOM_OK;
+}
+
+static int launch_rans(bool indexed, const uint8_t* src, const voom_rans_tile* tiles, uint32_t n_tiles,
+                       uint8_t* out, uint32_t* status, uint32_t* ckpt, const uint32_t* ckpt_base,
+                       uint32_t every, void* stream) {
+  if (n_tiles == 0) return VOOM_OK;
+  if (!src || !tiles || !out || !status) return VOOM_E_INVALID_ARG;
+  if ((ckpt || indexed) && (!ckpt_base || !valid_every(every))) return VOOM_E_INVALID_ARG;
+  if (indexed && !ckpt) return VOOM_E_INVALID_ARG;
+  const size_t smem = sizeof(SharedPlanes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (indexed) {
+    e = cudaFuncSetAttribute(rans_indexed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return VOOM_E_CUDA;
+    rans_indexed_kernel<<<n_tiles, kThreads, smem, s>>>(src, tiles, out, status, ckpt, ckpt_base, every);
+  } else {
+    e = cudaFuncSetAttribute(rans_cold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return VOOM_E_CUDA;
+    rans_cold_kernel<<<n_tiles, kThreads, smem, s>>>(src, tiles, out, status, ckpt, ckpt_base,
+                                                     ckpt ? every : 64u);
+  }
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+VOOM_API int voom_rans_decode(const uint8_t* d_src, const voom_rans_tile* d_tiles, uint32_t n_tiles,
+                              uint8_t* d_out, uint32_t* d_status, uint32_t* d_ckpt,
+                              const uint32_t* d_ckpt_base, uint32_t ckpt_every, void* stream) {
+  return launch_rans(false, d_src, d_tiles, n_tiles, d_out, d_status, d_ckpt, d_ckpt_base, ckpt_every,
+                     stream);
+}
+
+VOOM_API int voom_rans_decode_indexed(const uint8_t* d_src, const voom_rans_tile* d_tiles,
+                                      uint32_t n_tiles, uint8_t* d_out, uint32_t* d_status,
+                                      const uint32_t* d_ckpt, const uint32_t* d_ckpt_base,
+                                      uint32_t ckpt_every, void* stream) {
+  return launch_rans(true, d_src, d_tiles, n_tiles, d_out, d_status, const_cast<uint32_t*>(d_ckpt),
+                     d_ckpt_base, ckpt_every, stream);
+}
