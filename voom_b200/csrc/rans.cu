@@ -63,11 +63,12 @@ __device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
   return ld_u8(p) | (ld_u8(p + 1) << 8) | (ld_u8(p + 2) << 16) | (ld_u8(p + 3) << 24);
 }
 
-// Renormalisation byte source: bytes at payload[cur..] little-endian in `bb`,
-// refilled from aligned 32-bit words one word ahead of use.
+// Renormalisation byte source, big-endian: the next payload byte sits in
+// bits 63..56 of `bb`, so taking k bytes into the state is one funnel shift.
+// Refilled from aligned 32-bit words one word ahead of use.
 struct ByteReader {
   uint64_t bb;
-  int nbits;
+  int nbits;  // valid bits at the top of bb
   const uint32_t* wp;
   uint32_t pending;
 
@@ -75,67 +76,73 @@ struct ByteReader {
     uintptr_t a = reinterpret_cast<uintptr_t>(p);
     const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
     int o = int(a & 3u);
-    bb = uint64_t(__ldg(w) >> (8 * o));
+    bb = uint64_t(__byte_perm(__ldg(w), 0, 0x0123) << (8 * o)) << 32;
     nbits = 32 - 8 * o;
-    bb |= uint64_t(__ldg(w + 1)) << nbits;
+    bb |= uint64_t(__byte_perm(__ldg(w + 1), 0, 0x0123)) << (32 - nbits);
     nbits += 32;
     pending = __ldg(w + 2);
     wp = w + 3;
   }
   __device__ __forceinline__ void refill() {
     if (nbits <= 32) {
-      bb |= uint64_t(pending) << nbits;
+      bb |= uint64_t(__byte_perm(pending, 0, 0x0123)) << (32 - nbits);
       nbits += 32;
       pending = __ldg(wp);
       wp++;
     }
   }
   __device__ __forceinline__ uint32_t take() {
-    uint32_t b = uint32_t(bb) & 0xFFu;
-    bb >>= 8;
+    uint32_t b = uint32_t(bb >> 56);
+    bb <<= 8;
     nbits -= 8;
     return b;
   }
 };
 
-// One decoded symbol of a non-degenerate plane, with the reference's
-// renormalisation loop `while state < L and cursor < len` (bf16_rans.py:125).
-__device__ __forceinline__ uint32_t rans_step(const uint32_t* __restrict__ lut, uint32_t& x,
-                                              uint32_t& cur, uint32_t len, ByteReader& rd) {
-  uint32_t slot = x & 4095u;
-  uint32_t e = lut[slot];
-  x = (((e >> 8) & 4095u) + 1u) * (x >> 12) + (e >> 20);
-  if (x < kRansL) {
-    if (cur < len) {
-      x = (x << 8) | rd.take();
-      cur++;
-      if (x < kRansL && cur < len) {
-        x = (x << 8) | rd.take();
-        cur++;
-        while (x < kRansL && cur < len) {  // only reachable from malformed states
-          rd.refill();
-          x = (x << 8) | rd.take();
-          cur++;
-        }
-      }
-    }
-  }
-  rd.refill();
-  return e & 0xFFu;
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
 }
 
-// Degenerate plane (all frequencies zero): the reference's lookup is all
-// symbol 0 with frequency 0, so the next state is the slot itself.
-__device__ __forceinline__ uint32_t rans_step_degenerate(uint32_t& x, uint32_t& cur, uint32_t len,
-                                                         ByteReader& rd) {
-  x = x & 4095u;
+// One decoded symbol with the reference's exact renormalisation loop
+// `while state < L and cursor < len` (bf16_rans.py:117-127).  Used near the
+// end of a stream, for degenerate tables and for malformed states.
+__device__ __forceinline__ uint32_t rans_step_exact(uint32_t lut_s, bool degenerate, uint32_t& x,
+                                                    uint32_t& cur, uint32_t len, ByteReader& rd) {
+  uint32_t slot = x & 4095u, sym = 0;
+  if (degenerate) {
+    x = slot;  // all frequencies zero: symbol 0, frequency 0, cumulative 0
+  } else {
+    uint32_t e = lds32(lut_s + 4u * slot);
+    x = (((e >> 8) & 4095u) + 1u) * (x >> 12) + (e >> 20);
+    sym = e & 0xFFu;
+  }
   while (x < kRansL && cur < len) {
     rd.refill();
     x = (x << 8) | rd.take();
     cur++;
   }
   rd.refill();
-  return 0;
+  return sym;
+}
+
+// Branch-free symbol step for the bulk of a stream.  Preconditions: x >= L,
+// non-degenerate table, at least 2 payload bytes left, >= 16 buffered bits.
+// From x >= 2^23 and freq >= 1 the new state is >= 2^11, so at most two
+// renormalisation bytes are needed: k = (x < 2^23) + (x < 2^15).
+__device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, uint32_t& x, uint32_t& cur,
+                                                   ByteReader& rd) {
+  uint32_t e = lds32(lut_s + 4u * (x & 4095u));
+  uint32_t xs = x >> 12;
+  x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
+  uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
+  x = __funnelshift_l(uint32_t(rd.bb >> 32), x, 8u * k);
+  rd.bb <<= 8u * k;
+  rd.nbits -= int(8u * k);
+  cur += k;
+  rd.refill();
+  return e & 0xFFu;
 }
 
 // Builds the decode table of one plane from its 256 x u16 frequency table.
@@ -199,14 +206,15 @@ struct PlaneRun {
   ByteReader rd;
 };
 
-// Decodes `n` symbols of one plane with one byte store per symbol (stride 2).
-// Used for tails, unaligned tiles, degenerate planes and partial tiles.
-__device__ __forceinline__ void decode_generic(const uint32_t* lut, bool degenerate, PlaneRun& r, uint32_t n,
-                               uint32_t first, uint8_t* out, uint32_t* ckpt, uint32_t every,
-                               uint32_t limit_k, uint32_t plane) {
+// Decodes `n` symbols of one plane with one byte store per symbol (stride 2)
+// and exact reference semantics.  Used for stream ends, unaligned tiles,
+// degenerate planes and partial tiles.
+__device__ __forceinline__ void decode_generic(uint32_t lut_s, bool degenerate, PlaneRun& r,
+                                               uint32_t n, uint32_t first, uint8_t* out,
+                                               uint32_t* ckpt, uint32_t every, uint32_t limit_k,
+                                               uint32_t plane) {
   for (uint32_t i = 0; i < n; i++) {
-    uint32_t s = degenerate ? rans_step_degenerate(r.x, r.cur, r.len, r.rd)
-                            : rans_step(lut, r.x, r.cur, r.len, r.rd);
+    uint32_t s = rans_step_exact(lut_s, degenerate, r.x, r.cur, r.len, r.rd);
     out[2u * i] = uint8_t(s);
     if (ckpt) {
       uint32_t done = first + i + 1;
@@ -221,19 +229,26 @@ __device__ __forceinline__ void decode_generic(const uint32_t* lut, bool degener
   }
 }
 
-// Lockstep pair decode of `nchunks` x 16 symbols: lane 0 low plane, lane 1
-// high plane; both planes must be non-degenerate and `out` 16-byte aligned.
-__device__ __forceinline__ void decode_pair_fast(const uint32_t* lut, PlaneRun& r, uint32_t nchunks, uint32_t first,
-                                 uint8_t* out, uint32_t lane, uint32_t* ckpt, uint32_t every,
-                                 uint32_t limit_k, unsigned mask) {
-  for (uint32_t c = 0; c < nchunks; c++) {
+// Lockstep pair decode of up to `nchunks` x 16 symbols: lane 0 low plane,
+// lane 1 high plane (both non-degenerate), `out` 16-byte aligned.  A chunk
+// runs on the branch-free step only when both lanes have >= 32 payload bytes
+// left and a normal state; otherwise the pair stops and the caller finishes
+// each plane with decode_generic.  Returns the chunks decoded.
+__device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r, uint32_t nchunks,
+                                                     uint32_t first, uint8_t* out, uint32_t lane,
+                                                     uint32_t* ckpt, uint32_t every,
+                                                     uint32_t limit_k, unsigned mask) {
+  uint32_t c = 0;
+  for (; c < nchunks; c++) {
+    const bool ok = (r.len - r.cur >= 32u) && (r.x >= kRansL);
+    if (!__all_sync(mask, ok)) break;
     uint32_t a[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      uint32_t s0 = rans_step(lut, r.x, r.cur, r.len, r.rd);
-      uint32_t s1 = rans_step(lut, r.x, r.cur, r.len, r.rd);
-      uint32_t s2 = rans_step(lut, r.x, r.cur, r.len, r.rd);
-      uint32_t s3 = rans_step(lut, r.x, r.cur, r.len, r.rd);
+      uint32_t s0 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
+      uint32_t s1 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
+      uint32_t s2 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
+      uint32_t s3 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
       a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
     }
     store_pair16(out + 32u * c, lane, a[0], a[1], a[2], a[3], mask);
@@ -248,6 +263,7 @@ __device__ __forceinline__ void decode_pair_fast(const uint32_t* lut, PlaneRun& 
       }
     }
   }
+  return c;
 }
 
 __device__ __forceinline__ void plane_start(PlaneRun& r, const uint8_t* src, uint64_t freq_off,
@@ -328,13 +344,13 @@ __global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* _
       const bool fast = do_low && do_high && !sh.degenerate[0] && !sh.degenerate[1] &&
                         ((reinterpret_cast<uintptr_t>(out + tl.dst) & 15u) == 0);
       uint32_t done = 0;
+      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
       if (fast) {
         uint32_t nchunks = n_high / 16;  // n_high <= n_low
-        decode_pair_fast(sh.lut[lane], r, nchunks, 0, out + tl.dst, lane, ck, every, limit_k, 0x3u);
-        done = 16 * nchunks;
+        done = 16u * decode_pair_fast(lut_s, r, nchunks, 0, out + tl.dst, lane, ck, every, limit_k, 0x3u);
       }
-      decode_generic(sh.lut[lane], sh.degenerate[lane], r, n - done, done, o + 2 * done, ck, every,
-                     limit_k, lane);
+      decode_generic(lut_s, sh.degenerate[lane], r, n - done, done, o + 2 * done, ck, every, limit_k,
+                     lane);
       if (r.cur != r.len)
         atomicOr(&sh.flags, lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING);
     }
@@ -342,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* _
   finish_tile(sh, tl, src, out, status);
 }
 
-__global__ void __launch_bounds__(kThreads) rans_indexed_kernel(
+__global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
     const uint8_t* __restrict__ src, const voom_rans_tile* __restrict__ tiles, uint8_t* __restrict__ out,
     uint32_t* __restrict__ status, const uint32_t* __restrict__ ckpt,
     const uint32_t* __restrict__ ckpt_base, uint32_t every) {
@@ -387,13 +403,13 @@ __global__ void __launch_bounds__(kThreads) rans_indexed_kernel(
     const uint32_t cnt_high = first < n_high ? min(every, n_high - first) : 0u;
     const bool pair_fast = fast_ok && cnt_high == every;  // then the low count is `every` too
     uint32_t done = 0;
+    const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
     if (pair_fast) {
-      decode_pair_fast(sh.lut[lane], r, every / 16, first, out + tl.dst + 2u * first, lane, nullptr,
-                       every, 0, mask);
-      done = every;
+      done = 16u * decode_pair_fast(lut_s, r, every / 16, first, out + tl.dst + 2u * first, lane,
+                                    nullptr, every, 0, mask);
     }
     if (active) {
-      decode_generic(sh.lut[lane], sh.degenerate[lane], r, cnt - done, first + done,
+      decode_generic(lut_s, sh.degenerate[lane], r, cnt - done, first + done,
                      out + tl.dst + lane + 2u * (first + done), nullptr, every, 0, lane);
       const bool last = (seg + 1 > nb) || ((seg + 1) * every > n);
       if (last) {
