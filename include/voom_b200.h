@@ -127,17 +127,32 @@ int voom_rans_decode(const uint8_t* d_src, const voom_rans_tile* d_tiles, uint32
                      uint8_t* d_out, uint32_t* d_status, uint32_t* d_ckpt,
                      const uint32_t* d_ckpt_base, uint32_t ckpt_every, void* stream);
 
+/* Work unit of the indexed decoder: up to 128 checkpoint segments of one tile
+ * (a stored tile is one unit).  Built by voom_rans_chunks. */
+typedef struct voom_rans_chunk {
+  uint32_t tile;       /* tile index                                */
+  uint32_t seg_begin;  /* first checkpoint segment                   */
+  uint32_t seg_end;    /* one past the last segment                  */
+  uint32_t n_in_tile;  /* units of this tile (for the CRC assembly)  */
+} voom_rans_chunk;
+
+/* Host helper: splits planned tiles into indexed-decode units.  With
+ * chunks == NULL only *n_chunks is set. */
+int voom_rans_chunks(const voom_rans_tile* h_tiles, uint32_t n_tiles, uint32_t ckpt_every,
+                     voom_rans_chunk* h_chunks, uint32_t max_chunks, uint32_t* n_chunks);
+
 /* Decodes planned tiles from a checkpoint index built by voom_rans_decode:
- * each (tile, plane, segment of ckpt_every symbols) is decoded independently
- * and must land exactly on the next checkpoint; the CRC is verified when the
- * tile has VOOM_RANS_DO_CRC.  Same status bits as voom_rans_decode; a segment
- * that does not meet its successor checkpoint sets the *_TRAILING bit.
+ * every (tile, plane, segment of ckpt_every symbols) is decoded independently
+ * and must land exactly on the next checkpoint (else the *_TRAILING bit);
+ * the CRC-32 of each tile is assembled from its units and verified when the
+ * tile has VOOM_RANS_DO_CRC.  d_tile_scratch: 4 u32 per tile, zero before the
+ * first call; every call leaves it zero again.  d_status gets one word per tile.
  * Replaces: formats/bf16_rans.py:180-222 decode() for pages kept resident
  * in HBM and decoded on every use. */
 int voom_rans_decode_indexed(const uint8_t* d_src, const voom_rans_tile* d_tiles,
-                             uint32_t n_tiles, uint8_t* d_out, uint32_t* d_status,
-                             const uint32_t* d_ckpt, const uint32_t* d_ckpt_base,
-                             uint32_t ckpt_every, void* stream);
+                             const voom_rans_chunk* d_chunks, uint32_t n_chunks, uint8_t* d_out,
+                             uint32_t* d_status, const uint32_t* d_ckpt, const uint32_t* d_ckpt_base,
+                             uint32_t ckpt_every, uint32_t* d_tile_scratch, void* stream);
 
 /* Checkpoint words a tile needs for a given interval (2 per plane-segment
  * boundary, both planes).  Host helper. */
@@ -158,6 +173,75 @@ int voom_rans_encode(const uint8_t* h_data, uint64_t n, uint32_t tile_bytes, uin
  * Returns VOOM_OK or a VOOM_RANS_* code; *err_tile receives the tile index. */
 int voom_rans_resolve(const voom_rans_plan_info* info, const uint32_t* h_status,
                       uint32_t n_tiles, uint32_t* err_tile);
+
+/* ------------------------------------------------------------------ zstd */
+/* One decompression job = one `compression.zstd.decompress(data)` call of the
+ * reference (one or more concatenated frames, skippable frames allowed),
+ * optionally interleaved with a raw byte plane as vpack bodies are
+ * (formats/packed2.py:178-191: out[0::2] = lo, out[1::2] = hi). */
+typedef struct voom_zstd_job {
+  uint64_t src;     /* offset of the compressed bytes in the source buffer    */
+  uint64_t src_len; /* compressed bytes                                       */
+  uint64_t dst;     /* output offset of the first decoded byte                */
+  uint64_t dst_len; /* decoded zstd bytes the job must produce                */
+  uint64_t lo_src;  /* VOOM_ZSTD_INTERLEAVE: offset of the raw lo plane       */
+  uint32_t flags;   /* VOOM_ZSTD_* bits                                       */
+  uint32_t pad;
+} voom_zstd_job;
+
+enum {
+  VOOM_ZSTD_INTERLEAVE = 1u /* out[dst+2k] = lo[k], out[dst+2k+1] = decoded[k] */
+};
+
+/* Per-job status bits written by the decoder (0 = exact). */
+enum {
+  VOOM_ZSTD_ST_FORMAT = 1u,    /* malformed frame/block header or table (host plan) */
+  VOOM_ZSTD_ST_LITERALS = 2u,  /* Huffman stream not consumed exactly / overrun */
+  VOOM_ZSTD_ST_SEQUENCES = 4u, /* FSE bitstream not consumed exactly / bad code */
+  VOOM_ZSTD_ST_OFFSET = 8u,    /* match reaches before the frame start / zero   */
+  VOOM_ZSTD_ST_SIZE = 16u,     /* content size / block size / job length mismatch */
+  VOOM_ZSTD_ST_CHECKSUM = 32u, /* XXH64 content checksum mismatch */
+  VOOM_ZSTD_ST_UNRESOLVED = 64u /* match chains not resolved (internal limit) */
+};
+
+typedef struct voom_zstd_plan_info {
+  uint32_t n_jobs, n_frames, n_blocks, n_huf, n_fse;
+  uint32_t n_bad_jobs;      /* jobs with a structural error (not planned)   */
+  uint64_t lit_bytes;       /* literal scratch bytes                         */
+  uint64_t n_seq;           /* sequences over all blocks                     */
+  uint64_t decoded_bytes;   /* sum of dst_len over planned jobs              */
+  uint64_t scratch_bytes;   /* device scratch voom_zstd_decode needs         */
+  uint64_t plan_bytes;      /* bytes of the device plan image                */
+} voom_zstd_plan_info;
+
+/* Host plan of a batch of jobs whose bytes are in host memory h_src: walks
+ * frame headers (RFC 8878 3.1.1), block headers, literal and sequence section
+ * headers, decodes Huffman tree descriptions and FSE table descriptions; the
+ * entropy-coded payloads are left to the GPU.  Returns an opaque handle (NULL
+ * on bad arguments).  Jobs with a structural error are marked in the plan and
+ * skipped by the decoder.  `threads` <= 0 uses all cores.
+ * Replaces: the frame/block header walk inside libzstd ZSTD_decompress as
+ * reached from formats/packed2.py:178-191 and runtime/kv_paged.py:98-113. */
+void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, const voom_zstd_job* jobs,
+                            uint32_t n_jobs, int threads);
+int voom_zstd_plan_info_get(const void* plan, voom_zstd_plan_info* info);
+/* Writes the device plan image (info.plan_bytes) to host memory h_image; copy
+ * it to device memory unchanged and pass it to voom_zstd_decode. */
+int voom_zstd_plan_image(const void* plan, void* h_image, uint64_t cap);
+/* Per-job structural status (VOOM_ZSTD_ST_FORMAT or 0), n_jobs words. */
+int voom_zstd_plan_job_status(const void* plan, uint32_t* h_status);
+void voom_zstd_plan_destroy(void* plan);
+
+/* GPU decode of a planned batch: d_src = the same bytes as h_src (16 bytes of
+ * readable padding after the end), d_plan = the plan image in device memory,
+ * d_scratch = info.scratch_bytes of device memory (contents ignored),
+ * d_out = output, d_status = n_jobs u32 status words (VOOM_ZSTD_ST_* bits,
+ * accumulated: clear before the call).  Enqueues on `stream`; the match
+ * resolution loop synchronises with `stream` between passes.
+ * Replaces: compression.zstd.decompress + the lo/hi interleave of
+ * formats/packed2.py:178-191 (decode_body) and runtime/kv_paged.py:98-113. */
+int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
+                     uint8_t* d_out, uint32_t* d_status, void* stream);
 
 #ifdef __cplusplus
 }

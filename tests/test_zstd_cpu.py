@@ -1,0 +1,93 @@
+"""CPU tests for the zstd path: the oracle (RFC 8878 restatement) pinned
+against libzstd, and the GPU decoder's host planner."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import zstd as oz
+from tests.zstd_cases import cases
+
+
+@pytest.fixture(scope="module")
+def frames():
+    return cases()
+
+
+def test_oracle_matches_libzstd(frames):
+    for name, fr, raw in frames:
+        assert oz.decompress(fr, capacity=len(raw) + 64) == raw, name
+        assert oz.libzstd_decompress(fr, len(raw) + 64) == raw, name
+
+
+def test_oracle_rejects_corruption_libzstd_rejects(frames):
+    name, fr, raw = frames[0]
+    rng = np.random.default_rng(7)
+    both_reject = 0
+    for _ in range(40):
+        b = bytearray(fr)
+        b[int(rng.integers(0, len(b)))] ^= int(rng.integers(1, 256))
+        try:
+            ref = oz.libzstd_decompress(bytes(b), len(raw) + 64)
+        except oz.ZstdError:
+            ref = None
+        try:
+            got = oz.decompress(bytes(b), capacity=len(raw) + 64)
+        except oz.ZstdError:
+            got = None
+        if ref is None:
+            both_reject += got is None
+        # when libzstd accepts a damaged frame the oracle must produce the same bytes
+        if ref is not None and got is not None:
+            assert ref == got
+    assert both_reject > 10
+
+
+def test_xxh64_known_answers():
+    # published XXH64 test values (seed 0)
+    assert oz.xxh64(b"") == 0xEF46DB3751D8E999
+    assert oz.xxh64(b"a") == 0xD24EC4F1A98C6E5B
+    assert oz.xxh64(b"abc") == 0x44BC2CF5AD770999
+
+
+def test_planner_walks_frames(built_lib, frames):
+    from voom_b200.formats import zstd_gpu as Z
+
+    src = b"".join(fr for _, fr, _ in frames)
+    jobs = np.zeros(len(frames), dtype=Z.JOB_DTYPE)
+    off = dst = 0
+    for i, (_, fr, raw) in enumerate(frames):
+        jobs[i] = (off, len(fr), dst, len(raw), 0, 0, 0)
+        off += len(fr)
+        dst += len(raw)
+    plan = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs)
+    assert plan.info.n_bad_jobs == 0
+    assert plan.info.n_jobs == len(frames)
+    assert plan.info.n_frames == len(frames) + 1  # one job holds two frames
+    assert plan.info.scratch_bytes > 4 * sum(len(r) for _, _, r in frames)
+    assert not plan.plan_status[: len(frames)].any()
+
+
+def test_planner_flags_structural_damage(built_lib, frames):
+    from voom_b200.formats import zstd_gpu as Z
+
+    _, fr, raw = frames[0]
+    bad = bytearray(fr)
+    bad[0] ^= 0xFF  # magic
+    jobs = np.zeros(2, dtype=Z.JOB_DTYPE)
+    jobs[0] = (0, len(fr), 0, len(raw), 0, 0, 0)
+    jobs[1] = (len(fr), len(fr), 0, len(raw), 0, 0, 0)
+    plan = Z.ZstdPlan(np.frombuffer(bytes(fr) + bytes(bad), np.uint8), jobs)
+    assert plan.plan_status[0] == 0 and plan.plan_status[1] == Z.ST_FORMAT
+
+
+def test_frame_content_size(frames):
+    from voom_b200.formats import zstd_gpu as Z
+
+    for name, fr, raw in frames:
+        fcs = Z.frame_content_size(fr)
+        if name.startswith("streamed"):
+            assert fcs is None
+        else:
+            assert fcs == len(raw), name

@@ -46,6 +46,8 @@ RANS_TILE_DTYPE = np.dtype([
 ])
 assert RANS_TILE_DTYPE.itemsize == 56
 
+RANS_CHUNK_DTYPE = np.dtype([("tile", "<u4"), ("seg_begin", "<u4"), ("seg_end", "<u4"), ("n_in_tile", "<u4")])
+
 
 class RansPlanInfo(ctypes.Structure):
     _fields_ = [
@@ -72,10 +74,17 @@ _vp = ctypes.c_void_p
 SIGNATURES: dict[str, tuple] = {
     "voom_rans_plan": (_i32, [_vp, _u64, _u64, _u64, _vp, _u32, ctypes.POINTER(RansPlanInfo)]),
     "voom_rans_decode": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
-    "voom_rans_decode_indexed": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _vp]),
+    "voom_rans_decode_indexed": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp, _vp, _vp, _u32, _vp, _vp]),
+    "voom_rans_chunks": (_i32, [_vp, _u32, _u32, _vp, _u32, ctypes.POINTER(_u32)]),
     "voom_rans_ckpt_words": (_u64, [_u32, _u32]),
     "voom_rans_resolve": (_i32, [ctypes.POINTER(RansPlanInfo), _vp, _u32, ctypes.POINTER(_u32)]),
     "voom_rans_encode": (_i32, [_vp, _u64, _u32, _vp, _u64, ctypes.POINTER(_u64), _vp, _i32]),
+    "voom_zstd_plan_create": (_vp, [_vp, _u64, _vp, _u32, _i32]),
+    "voom_zstd_plan_info_get": (_i32, [_vp, _vp]),
+    "voom_zstd_plan_image": (_i32, [_vp, _vp, _u64]),
+    "voom_zstd_plan_job_status": (_i32, [_vp, _vp]),
+    "voom_zstd_plan_destroy": (None, [_vp]),
+    "voom_zstd_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -109,31 +109,37 @@ __device__ __forceinline__ uint32_t crc_run(const uint32_t (*t)[256], uint32_t c
   return c;
 }
 
-// Block-wide CRC-32 of [p, p+n).  Every thread of the block must call it;
-// `t` is the slicing table in shared memory, `pow2` the x^(2^k) table,
-// `red` a shared scratch of blockDim.x/32 words.  Returns the CRC on every thread.
-__device__ __forceinline__ uint32_t block_crc32(const uint32_t (*t)[256], const uint32_t* pow2,
-                                                const uint8_t* p, uint64_t n, uint32_t* red) {
+// Block-wide raw CRC register of [p, p+n) starting from `init` (no final
+// inversion).  Every thread of the block must call it; `t` is the slicing
+// table in shared memory, `pow2` the x^(2^k) table, `red` a shared scratch of
+// blockDim.x/32 words.  Each thread folds an aligned slice, shifts its
+// register to the end of the range (x^(8*bytes after it) mod P) and the
+// registers are XOR-reduced.  Returns the register on every thread.
+__device__ __forceinline__ uint32_t block_crc_reg(const uint32_t (*t)[256], const uint32_t* pow2,
+                                                  const uint8_t* p, uint64_t n, uint32_t init,
+                                                  uint32_t* red) {
   const uint32_t nt = blockDim.x, tid = threadIdx.x;
-  // Chunk boundaries on 16-byte multiples so each thread streams aligned words.
   uint64_t chunk = ((n + nt - 1) / nt + 15) & ~uint64_t(15);
   if (chunk == 0) chunk = 16;
   uint64_t b = (uint64_t)tid * chunk;
   uint64_t e = b + chunk;
   if (b > n) b = n;
   if (e > n) e = n;
-  uint32_t c = crc_run(t, tid == 0 ? 0xFFFFFFFFu : 0u, p + b, e - b);
-  // Contribution of this chunk to the register at the end of the message.
-  c = gf2_mulmod(crc_zeros_op(pow2, n - e), c);
+  uint32_t c = crc_run(t, tid == 0 ? init : 0u, p + b, e - b);
+  if (n - e) c = gf2_mulmod(crc_zeros_op(pow2, n - e), c);
   for (int o = 16; o; o >>= 1) c ^= __shfl_xor_sync(0xFFFFFFFFu, c, o);
   if ((tid & 31) == 0) red[tid >> 5] = c;
   __syncthreads();
   uint32_t r = 0;
   for (uint32_t w = 0; w < nt / 32; w++) r ^= red[w];
-  // n == 0 keeps the preset register, so CRC(empty) = 0.
-  if (n == 0) r = 0xFFFFFFFFu;
   __syncthreads();
-  return r ^ 0xFFFFFFFFu;
+  return r;
+}
+
+// Block-wide zlib CRC-32 of [p, p+n).
+__device__ __forceinline__ uint32_t block_crc32(const uint32_t (*t)[256], const uint32_t* pow2,
+                                                const uint8_t* p, uint64_t n, uint32_t* red) {
+  return block_crc_reg(t, pow2, p, n, 0xFFFFFFFFu, red) ^ 0xFFFFFFFFu;
 }
 
 }  // namespace voom

@@ -6,16 +6,21 @@
 // <I payload_len><256 x u16 freq (sum 4096)><u32 initial state><renorm bytes>.
 //
 // Parallelism: the format's independent unit is one (tile, plane) stream, a
-// serial chain of 32-bit rANS states.  The cold kernel gives each tile one
-// CTA; lanes 0 and 1 of warp 0 decode the low and high plane in lockstep,
-// exchange 8 bytes by shuffle every 16 symbols and write the interleaved BF16
-// bytes with 128-bit stores.  The decode table (4096 slots, one u32 each:
+// serial chain of 32-bit rANS states.  Lanes 2k and 2k+1 of a warp decode the
+// low and high plane of the same range in lockstep, exchange 8 bytes by
+// shuffle every 16 symbols and write the interleaved BF16 bytes with 128-bit
+// stores.  The decode table (4096 slots, one u32 each:
 // symbol | (freq-1) << 8 | (slot - cum) << 20) lives in shared memory, so a
-// symbol costs one shared load.  Renormalisation bytes come from a 64-bit
-// register buffer refilled one aligned word ahead.  While decoding, the cold
-// kernel can record (state, cursor) checkpoints; the indexed kernel then
-// decodes every checkpoint segment in parallel (one lane pair per segment)
-// and checks that each segment lands on its successor checkpoint.
+// symbol costs one shared load; the renormalisation bytes at the stream
+// cursor are fetched with two L1-cached aligned loads in parallel with it and
+// folded in with one funnel shift.
+//
+// Cold kernel: one CTA per tile, one lane pair decodes the whole tile and can
+// record a (state, cursor) checkpoint every `every` symbols.  Indexed kernel:
+// with those checkpoints every segment is independent; one CTA decodes 128
+// segment pairs of one tile, and the per-tile CRC-32 is assembled from the
+// chunks' CRC registers (GF(2) shift to the tile end, XOR) by whichever CTA of
+// the tile finishes last.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -27,6 +32,7 @@ namespace {
 
 constexpr uint32_t kRansL = 1u << 23;
 constexpr int kThreads = 256;
+constexpr uint32_t kSegsPerChunk = kThreads / 2;
 
 __device__ const CrcTables g_crc = make_crc_tables();
 __device__ const CrcPow2 g_pow2 = make_crc_pow2();
@@ -56,6 +62,7 @@ struct SharedPlanes {
   uint32_t red[kThreads / 32];
   uint32_t flags;
   uint32_t degenerate[2];
+  uint32_t last;
 };
 
 __device__ __forceinline__ uint32_t ld_u8(const uint8_t* p) { return __ldg(p); }
@@ -63,95 +70,65 @@ __device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
   return ld_u8(p) | (ld_u8(p + 1) << 8) | (ld_u8(p + 2) << 16) | (ld_u8(p + 3) << 24);
 }
 
-// Renormalisation byte source, big-endian: the next payload byte sits in
-// bits 63..56 of `bb`, so taking k bytes into the state is one funnel shift.
-// Refilled from aligned 32-bit words one word ahead of use.
-struct ByteReader {
-  uint64_t bb;
-  int nbits;  // valid bits at the top of bb
-  const uint32_t* wp;
-  uint32_t pending;
-
-  __device__ __forceinline__ void init(const uint8_t* p) {
-    uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    int o = int(a & 3u);
-    bb = uint64_t(__byte_perm(__ldg(w), 0, 0x0123) << (8 * o)) << 32;
-    nbits = 32 - 8 * o;
-    bb |= uint64_t(__byte_perm(__ldg(w + 1), 0, 0x0123)) << (32 - nbits);
-    nbits += 32;
-    pending = __ldg(w + 2);
-    wp = w + 3;
-  }
-  __device__ __forceinline__ void refill() {
-    if (nbits <= 32) {
-      bb |= uint64_t(__byte_perm(pending, 0, 0x0123)) << (32 - nbits);
-      nbits += 32;
-      pending = __ldg(wp);
-      wp++;
-    }
-  }
-  __device__ __forceinline__ uint32_t take() {
-    uint32_t b = uint32_t(bb >> 56);
-    bb <<= 8;
-    nbits -= 8;
-    return b;
-  }
-};
-
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 
+// The 4 bytes at p as a big-endian word (first byte most significant), from
+// two aligned L1-cached loads.  p[0..7] must be readable.
+__device__ __forceinline__ uint32_t load4_be(const uint8_t* p) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t v = __funnelshift_r(__ldg(w), __ldg(w + 1), uint32_t(a & 3u) * 8u);
+  return __byte_perm(v, 0, 0x0123);
+}
+
+struct PlaneRun {
+  const uint8_t* payload;  // plane payload: u32 initial state, renorm bytes
+  uint32_t x, cur, len;
+};
+
 // One decoded symbol with the reference's exact renormalisation loop
 // `while state < L and cursor < len` (bf16_rans.py:117-127).  Used near the
 // end of a stream, for degenerate tables and for malformed states.
-__device__ __forceinline__ uint32_t rans_step_exact(uint32_t lut_s, bool degenerate, uint32_t& x,
-                                                    uint32_t& cur, uint32_t len, ByteReader& rd) {
-  uint32_t slot = x & 4095u, sym = 0;
+__device__ __forceinline__ uint32_t rans_step_exact(uint32_t lut_s, bool degenerate, PlaneRun& r) {
+  uint32_t slot = r.x & 4095u, sym = 0;
   if (degenerate) {
-    x = slot;  // all frequencies zero: symbol 0, frequency 0, cumulative 0
+    r.x = slot;  // all frequencies zero: symbol 0, frequency 0, cumulative 0
   } else {
     uint32_t e = lds32(lut_s + 4u * slot);
-    x = (((e >> 8) & 4095u) + 1u) * (x >> 12) + (e >> 20);
+    r.x = (((e >> 8) & 4095u) + 1u) * (r.x >> 12) + (e >> 20);
     sym = e & 0xFFu;
   }
-  while (x < kRansL && cur < len) {
-    rd.refill();
-    x = (x << 8) | rd.take();
-    cur++;
+  while (r.x < kRansL && r.cur < r.len) {
+    r.x = (r.x << 8) | ld_u8(r.payload + r.cur);
+    r.cur++;
   }
-  rd.refill();
   return sym;
 }
 
 // Branch-free symbol step for the bulk of a stream.  Preconditions: x >= L,
-// non-degenerate table, at least 2 payload bytes left, >= 16 buffered bits.
-// From x >= 2^23 and freq >= 1 the new state is >= 2^11, so at most two
-// renormalisation bytes are needed: k = (x < 2^23) + (x < 2^15).
-__device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, uint32_t& x, uint32_t& cur,
-                                                   ByteReader& rd) {
-  uint32_t e = lds32(lut_s + 4u * (x & 4095u));
-  uint32_t xs = x >> 12;
-  x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
-  uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
-  x = __funnelshift_l(uint32_t(rd.bb >> 32), x, 8u * k);
-  rd.bb <<= 8u * k;
-  rd.nbits -= int(8u * k);
-  cur += k;
-  rd.refill();
+// non-degenerate table, at least 8 payload bytes left.  From x >= 2^23 and
+// freq >= 1 the new state is >= 2^11, so at most two renormalisation bytes
+// are needed: k = (x < 2^23) + (x < 2^15).
+__device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, PlaneRun& r) {
+  const uint32_t be = load4_be(r.payload + r.cur);
+  const uint32_t e = lds32(lut_s + 4u * (r.x & 4095u));
+  const uint32_t xs = r.x >> 12;
+  uint32_t x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
+  const uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
+  r.x = __funnelshift_l(be, x, 8u * k);
+  r.cur += k;
   return e & 0xFFu;
 }
 
 // Builds the decode table of one plane from its 256 x u16 frequency table.
 // All threads of the block participate.  Sets sh.degenerate[p].
-__device__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
+__device__ __forceinline__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
   const int tid = threadIdx.x;
-  uint32_t f = 0;
-  if (tid < 256) f = ld_u8(freq + 2 * tid) | (ld_u8(freq + 2 * tid + 1) << 8);
-  // exclusive block scan over 256 values (kThreads == 256)
+  const uint32_t f = ld_u8(freq + 2 * tid) | (ld_u8(freq + 2 * tid + 1) << 8);  // kThreads == 256
   uint32_t v = f;
   const int lane = tid & 31, warp = tid >> 5;
   for (int o = 1; o < 32; o <<= 1) {
@@ -162,7 +139,7 @@ __device__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
   __syncthreads();
   uint32_t base = 0;
   for (int w = 0; w < warp; w++) base += sh.red[w];
-  if (tid < 256) sh.cum[p][tid] = base + v - f;
+  sh.cum[p][tid] = base + v - f;
   if (tid == 255) sh.cum[p][256] = base + v;
   __syncthreads();
   const uint32_t total = sh.cum[p][256];
@@ -184,8 +161,8 @@ __device__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
 }
 
 // Interleaves this lane's 16 symbols (a0..a3) with its partner's into the 32
-// output bytes of the chunk; lane 0 (low plane) writes the first 16 bytes,
-// lane 1 (high plane) the second.  `dst` is 16-byte aligned.
+// output bytes of the chunk; the low-plane lane writes the first 16 bytes,
+// the high-plane lane the second.  `dst` is 16-byte aligned.
 __device__ __forceinline__ void store_pair16(uint8_t* dst, uint32_t lane, uint32_t a0, uint32_t a1,
                                              uint32_t a2, uint32_t a3, unsigned mask) {
   uint32_t s0 = lane ? a0 : a2, s1 = lane ? a1 : a3;
@@ -201,10 +178,16 @@ __device__ __forceinline__ void store_pair16(uint8_t* dst, uint32_t lane, uint32
   *reinterpret_cast<uint4*>(dst + 16 * lane) = o;
 }
 
-struct PlaneRun {
-  uint32_t x, cur, len;
-  ByteReader rd;
-};
+__device__ __forceinline__ void record_ckpt(uint32_t* ckpt, uint32_t done, uint32_t every,
+                                            uint32_t limit_k, uint32_t plane, const PlaneRun& r) {
+  if ((done & (every - 1)) == 0) {
+    const uint32_t k = done / every;
+    if (k >= 1 && k <= limit_k) {
+      ckpt[(k - 1) * 4 + plane * 2] = r.x;
+      ckpt[(k - 1) * 4 + plane * 2 + 1] = r.cur;
+    }
+  }
+}
 
 // Decodes `n` symbols of one plane with one byte store per symbol (stride 2)
 // and exact reference semantics.  Used for stream ends, unaligned tiles,
@@ -214,54 +197,36 @@ __device__ __forceinline__ void decode_generic(uint32_t lut_s, bool degenerate, 
                                                uint32_t* ckpt, uint32_t every, uint32_t limit_k,
                                                uint32_t plane) {
   for (uint32_t i = 0; i < n; i++) {
-    uint32_t s = rans_step_exact(lut_s, degenerate, r.x, r.cur, r.len, r.rd);
-    out[2u * i] = uint8_t(s);
-    if (ckpt) {
-      uint32_t done = first + i + 1;
-      if ((done & (every - 1)) == 0) {
-        uint32_t k = done / every;
-        if (k <= limit_k) {
-          ckpt[(k - 1) * 4 + plane * 2] = r.x;
-          ckpt[(k - 1) * 4 + plane * 2 + 1] = r.cur;
-        }
-      }
-    }
+    out[2u * i] = uint8_t(rans_step_exact(lut_s, degenerate, r));
+    if (ckpt) record_ckpt(ckpt, first + i + 1, every, limit_k, plane, r);
   }
 }
 
-// Lockstep pair decode of up to `nchunks` x 16 symbols: lane 0 low plane,
-// lane 1 high plane (both non-degenerate), `out` 16-byte aligned.  A chunk
-// runs on the branch-free step only when both lanes have >= 32 payload bytes
-// left and a normal state; otherwise the pair stops and the caller finishes
-// each plane with decode_generic.  Returns the chunks decoded.
+// Lockstep pair decode of up to `nchunks` x 16 symbols (low plane on the even
+// lane, high plane on the odd lane, both non-degenerate, `out` 16-byte
+// aligned).  A chunk runs on the branch-free step only when both lanes have
+// >= 40 payload bytes left and a normal state; otherwise the pair stops and
+// the caller finishes each plane with decode_generic.  Returns chunks done.
 __device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r, uint32_t nchunks,
                                                      uint32_t first, uint8_t* out, uint32_t lane,
                                                      uint32_t* ckpt, uint32_t every,
                                                      uint32_t limit_k, unsigned mask) {
   uint32_t c = 0;
   for (; c < nchunks; c++) {
-    const bool ok = (r.len - r.cur >= 32u) && (r.x >= kRansL);
+    const bool ok = (r.len - r.cur >= 40u) && (r.x >= kRansL);
     if (!__all_sync(mask, ok)) break;
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(r.payload + r.cur + 256));
     uint32_t a[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      uint32_t s0 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
-      uint32_t s1 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
-      uint32_t s2 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
-      uint32_t s3 = rans_step_fast(lut_s, r.x, r.cur, r.rd);
+      const uint32_t s0 = rans_step_fast(lut_s, r);
+      const uint32_t s1 = rans_step_fast(lut_s, r);
+      const uint32_t s2 = rans_step_fast(lut_s, r);
+      const uint32_t s3 = rans_step_fast(lut_s, r);
       a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
     }
     store_pair16(out + 32u * c, lane, a[0], a[1], a[2], a[3], mask);
-    if (ckpt) {
-      uint32_t done = first + 16u * (c + 1);
-      if ((done & (every - 1)) == 0) {
-        uint32_t k = done / every;
-        if (k <= limit_k) {
-          ckpt[(k - 1) * 4 + lane * 2] = r.x;
-          ckpt[(k - 1) * 4 + lane * 2 + 1] = r.cur;
-        }
-      }
-    }
+    if (ckpt) record_ckpt(ckpt, first + 16u * (c + 1), every, limit_k, lane, r);
   }
   return c;
 }
@@ -269,11 +234,10 @@ __device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r
 __device__ __forceinline__ void plane_start(PlaneRun& r, const uint8_t* src, uint64_t freq_off,
                                             uint32_t payload_len, uint32_t x0, uint32_t cur0,
                                             bool from_ckpt) {
-  const uint8_t* payload = src + freq_off + 512;
+  r.payload = src + freq_off + 512;
   r.len = payload_len;
-  r.x = from_ckpt ? x0 : ld_u32_unaligned(payload);
+  r.x = from_ckpt ? x0 : ld_u32_unaligned(r.payload);
   r.cur = from_ckpt ? cur0 : 4u;
-  r.rd.init(payload + r.cur);
 }
 
 __device__ __forceinline__ void load_crc_tables(SharedPlanes& sh) {
@@ -284,18 +248,8 @@ __device__ __forceinline__ void load_crc_tables(SharedPlanes& sh) {
   __syncthreads();
 }
 
-__device__ __forceinline__ void finish_tile(SharedPlanes& sh, const voom_rans_tile& tl, const uint8_t* src,
-                            uint8_t* out, uint32_t* status) {
-  __syncthreads();  // decoded bytes visible, LUT no longer needed
-  uint32_t st = sh.flags;
-  if ((tl.flags & VOOM_RANS_DO_CRC) && !(st & (VOOM_RANS_ST_LOW_TRAILING | VOOM_RANS_ST_HIGH_TRAILING))) {
-    load_crc_tables(sh);
-    const uint8_t* p = tl.mode == 0 ? src + tl.src : out + tl.dst;
-    uint32_t crc = block_crc32(reinterpret_cast<const uint32_t(*)[256]>(&sh.lut[0][0]), sh.pow2, p,
-                               tl.raw_len, sh.red);
-    if (crc != tl.crc32) st |= VOOM_RANS_ST_CRC_MISMATCH;
-  }
-  if (threadIdx.x == 0) status[blockIdx.x] = st;
+__device__ __forceinline__ const uint32_t (*crc_tab(SharedPlanes& sh))[256] {
+  return reinterpret_cast<const uint32_t(*)[256]>(&sh.lut[0][0]);
 }
 
 __device__ __forceinline__ void copy_stored(const uint8_t* src, uint8_t* dst, uint64_t n) {
@@ -309,20 +263,34 @@ __device__ __forceinline__ void copy_stored(const uint8_t* src, uint8_t* dst, ui
   }
 }
 
+// Whole-tile status for one-CTA tiles: trailing flags, then CRC.
+__device__ __forceinline__ void finish_whole_tile(SharedPlanes& sh, const voom_rans_tile& tl,
+                                                  const uint8_t* src, uint8_t* out, uint32_t* status,
+                                                  uint32_t tile) {
+  __syncthreads();  // decoded bytes visible, LUT no longer needed
+  uint32_t st = sh.flags;
+  if ((tl.flags & VOOM_RANS_DO_CRC) && !(st & (VOOM_RANS_ST_LOW_TRAILING | VOOM_RANS_ST_HIGH_TRAILING))) {
+    load_crc_tables(sh);
+    const uint8_t* p = tl.mode == 0 ? src + tl.src : out + tl.dst;
+    if (block_crc32(crc_tab(sh), sh.pow2, p, tl.raw_len, sh.red) != tl.crc32) st |= VOOM_RANS_ST_CRC_MISMATCH;
+  }
+  if (threadIdx.x == 0) status[tile] = st;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* __restrict__ src,
-                                                             const voom_rans_tile* __restrict__ tiles,
-                                                             uint8_t* __restrict__ out,
-                                                             uint32_t* __restrict__ status,
-                                                             uint32_t* __restrict__ ckpt,
-                                                             const uint32_t* __restrict__ ckpt_base,
-                                                             uint32_t every) {
+                                                                const voom_rans_tile* __restrict__ tiles,
+                                                                uint8_t* __restrict__ out,
+                                                                uint32_t* __restrict__ status,
+                                                                uint32_t* __restrict__ ckpt,
+                                                                const uint32_t* __restrict__ ckpt_base,
+                                                                uint32_t every) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SharedPlanes& sh = *reinterpret_cast<SharedPlanes*>(smem_raw);
   const voom_rans_tile tl = tiles[blockIdx.x];
   if (threadIdx.x == 0) sh.flags = 0;
   if (tl.mode == 0) {
     if (tl.flags & VOOM_RANS_DO_COPY) copy_stored(src + tl.src, out + tl.dst, tl.raw_len);
-    finish_tile(sh, tl, src, out, status);
+    finish_whole_tile(sh, tl, src, out, status, blockIdx.x);
     return;
   }
   const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
@@ -330,45 +298,42 @@ __global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* _
   if (do_high) build_lut(sh, 1, src + tl.high_freq);
   const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
   uint32_t* ck = ckpt ? ckpt + ckpt_base[blockIdx.x] : nullptr;
-  const uint32_t nseg = (n_low + every - 1) / (every ? every : 1);
-  const uint32_t limit_k = nseg ? nseg - 1 : 0;
+  const uint32_t nseg = n_low ? (n_low + every - 1) / every : 1;
+  const uint32_t limit_k = nseg - 1;
   if (threadIdx.x < 2) {
     const uint32_t lane = threadIdx.x;
     const bool active = lane ? do_high : do_low;
     if (active) {
       PlaneRun r;
-      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
-                  0, 0, false);
+      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload, 0, 0,
+                  false);
       const uint32_t n = lane ? n_high : n_low;
-      uint8_t* o = out + tl.dst + lane;
+      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
       const bool fast = do_low && do_high && !sh.degenerate[0] && !sh.degenerate[1] &&
                         ((reinterpret_cast<uintptr_t>(out + tl.dst) & 15u) == 0);
       uint32_t done = 0;
-      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
-      if (fast) {
-        uint32_t nchunks = n_high / 16;  // n_high <= n_low
-        done = 16u * decode_pair_fast(lut_s, r, nchunks, 0, out + tl.dst, lane, ck, every, limit_k, 0x3u);
-      }
-      decode_generic(lut_s, sh.degenerate[lane], r, n - done, done, o + 2 * done, ck, every, limit_k,
-                     lane);
-      if (r.cur != r.len)
-        atomicOr(&sh.flags, lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING);
+      if (fast) done = 16u * decode_pair_fast(lut_s, r, n_high / 16, 0, out + tl.dst, lane, ck, every, limit_k, 0x3u);
+      decode_generic(lut_s, sh.degenerate[lane], r, n - done, done, out + tl.dst + lane + 2 * done, ck, every,
+                     limit_k, lane);
+      if (r.cur != r.len) atomicOr(&sh.flags, lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING);
     }
   }
-  finish_tile(sh, tl, src, out, status);
+  finish_whole_tile(sh, tl, src, out, status, blockIdx.x);
 }
 
 __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
-    const uint8_t* __restrict__ src, const voom_rans_tile* __restrict__ tiles, uint8_t* __restrict__ out,
-    uint32_t* __restrict__ status, const uint32_t* __restrict__ ckpt,
-    const uint32_t* __restrict__ ckpt_base, uint32_t every) {
+    const uint8_t* __restrict__ src, const voom_rans_tile* __restrict__ tiles,
+    const voom_rans_chunk* __restrict__ chunks, uint8_t* __restrict__ out, uint32_t* __restrict__ status,
+    const uint32_t* __restrict__ ckpt, const uint32_t* __restrict__ ckpt_base, uint32_t every,
+    uint32_t* __restrict__ tile_scratch) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SharedPlanes& sh = *reinterpret_cast<SharedPlanes*>(smem_raw);
-  const voom_rans_tile tl = tiles[blockIdx.x];
+  const voom_rans_chunk ch = chunks[blockIdx.x];
+  const voom_rans_tile tl = tiles[ch.tile];
   if (threadIdx.x == 0) sh.flags = 0;
-  if (tl.mode == 0) {
+  if (tl.mode == 0) {  // stored tile: always a single chunk
     if (tl.flags & VOOM_RANS_DO_COPY) copy_stored(src + tl.src, out + tl.dst, tl.raw_len);
-    finish_tile(sh, tl, src, out, status);
+    finish_whole_tile(sh, tl, src, out, status, ch.tile);
     return;
   }
   const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
@@ -377,15 +342,17 @@ __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
   const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
   const uint32_t nseg = n_low ? (n_low + every - 1) / every : 1;
   const uint32_t nb = nseg - 1;  // checkpoint boundaries 1..nb
-  const uint32_t* ck = ckpt + ckpt_base[blockIdx.x];
+  const uint32_t* ck = ckpt + ckpt_base[ch.tile];
   const uint32_t lane = threadIdx.x & 1u;
   const unsigned mask = 0x3u << (threadIdx.x & 30u);
   const bool aligned = ((reinterpret_cast<uintptr_t>(out + tl.dst) & 15u) == 0);
   const bool fast_ok = do_low && do_high && !sh.degenerate[0] && !sh.degenerate[1] && aligned;
   const bool active = lane ? do_high : do_low;
   const uint32_t n = lane ? n_high : n_low;
+  const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
   uint32_t bad = 0;
-  for (uint32_t seg = threadIdx.x >> 1; seg < nseg; seg += kThreads / 2) {
+  const uint32_t seg = ch.seg_begin + (threadIdx.x >> 1);
+  if (seg < ch.seg_end) {
     const uint32_t first = seg * every;
     const uint32_t cnt = first < n ? min(every, n - first) : 0u;
     PlaneRun r;
@@ -395,19 +362,16 @@ __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
         x0 = ck[(seg - 1) * 4 + lane * 2];
         c0 = ck[(seg - 1) * 4 + lane * 2 + 1];
       }
-      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
-                  x0, c0, seg != 0);
+      plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload, x0,
+                  c0, seg != 0);
     }
-    // Both lanes of a pair run the fast path together only when both planes
-    // have a full segment; otherwise each lane takes the generic path.
+    // The pair runs the fast path together only when both planes have a full
+    // segment; otherwise each lane finishes on the exact path.
     const uint32_t cnt_high = first < n_high ? min(every, n_high - first) : 0u;
-    const bool pair_fast = fast_ok && cnt_high == every;  // then the low count is `every` too
     uint32_t done = 0;
-    const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
-    if (pair_fast) {
-      done = 16u * decode_pair_fast(lut_s, r, every / 16, first, out + tl.dst + 2u * first, lane,
-                                    nullptr, every, 0, mask);
-    }
+    if (fast_ok && cnt_high == every)
+      done = 16u * decode_pair_fast(lut_s, r, every / 16, first, out + tl.dst + 2u * first, lane, nullptr,
+                                    every, 0, mask);
     if (active) {
       decode_generic(lut_s, sh.degenerate[lane], r, cnt - done, first + done,
                      out + tl.dst + lane + 2u * (first + done), nullptr, every, 0, lane);
@@ -420,7 +384,34 @@ __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
     }
   }
   if (bad) atomicOr(&sh.flags, bad);
-  finish_tile(sh, tl, src, out, status);
+  __syncthreads();  // this chunk's bytes are written; LUT no longer needed
+  // CRC register of this chunk's byte range, moved to the end of the tile.
+  const uint64_t b = min(uint64_t(2) * ch.seg_begin * every, uint64_t(tl.raw_len));
+  const uint64_t e = min(uint64_t(2) * ch.seg_end * every, uint64_t(tl.raw_len));
+  uint32_t contrib = 0;
+  if (tl.flags & VOOM_RANS_DO_CRC) {
+    load_crc_tables(sh);
+    contrib = block_crc_reg(crc_tab(sh), sh.pow2, out + tl.dst + b, e - b, b == 0 ? 0xFFFFFFFFu : 0u, sh.red);
+    if (tl.raw_len - e) contrib = gf2_mulmod(crc_zeros_op(sh.pow2, tl.raw_len - e), contrib);
+  }
+  uint32_t* ts = tile_scratch + 4u * ch.tile;  // [0] CRC xor, [1] finished chunks, [2] flags
+  if (threadIdx.x == 0) {
+    if (contrib) atomicXor(&ts[0], contrib);
+    if (sh.flags) atomicOr(&ts[2], sh.flags);
+    __threadfence();
+    sh.last = (atomicAdd(&ts[1], 1u) == ch.n_in_tile - 1);
+  }
+  __syncthreads();
+  if (sh.last && threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t reg = atomicExch(&ts[0], 0u);
+    uint32_t st = atomicExch(&ts[2], 0u);
+    atomicExch(&ts[1], 0u);
+    if ((tl.flags & VOOM_RANS_DO_CRC) && !(st & (VOOM_RANS_ST_LOW_TRAILING | VOOM_RANS_ST_HIGH_TRAILING)) &&
+        (reg ^ 0xFFFFFFFFu) != tl.crc32)
+      st |= VOOM_RANS_ST_CRC_MISMATCH;
+    status[ch.tile] = st;
+  }
 }
 
 inline uint32_t rd32(const uint8_t* p) {
@@ -429,6 +420,11 @@ inline uint32_t rd32(const uint8_t* p) {
 
 bool valid_every(uint32_t e) { return e >= 64 && (e & (e - 1)) == 0; }
 
+uint32_t tile_segments(uint32_t raw_len, uint32_t every) {
+  const uint32_t n_low = (raw_len + 1) / 2;
+  return n_low ? (n_low + every - 1) / every : 1;
+}
+
 }  // namespace
 }  // namespace voom
 
@@ -436,9 +432,27 @@ using namespace voom;
 
 VOOM_API uint64_t voom_rans_ckpt_words(uint32_t raw_len, uint32_t every) {
   if (!valid_every(every)) return 0;
-  uint64_t n_low = (uint64_t(raw_len) + 1) / 2;
-  uint64_t nseg = n_low ? (n_low + every - 1) / every : 1;
-  return 4 * (nseg - 1);
+  return 4ull * (tile_segments(raw_len, every) - 1);
+}
+
+VOOM_API int voom_rans_chunks(const voom_rans_tile* tiles, uint32_t n_tiles, uint32_t every,
+                              voom_rans_chunk* chunks, uint32_t max_chunks, uint32_t* n_chunks) {
+  if (!n_chunks || (n_tiles && !tiles) || !valid_every(every)) return VOOM_E_INVALID_ARG;
+  uint32_t k = 0;
+  for (uint32_t t = 0; t < n_tiles; t++) {
+    const uint32_t nseg = tiles[t].mode == 0 ? 1 : tile_segments(tiles[t].raw_len, every);
+    const uint32_t nc = tiles[t].mode == 0 ? 1 : (nseg + kSegsPerChunk - 1) / kSegsPerChunk;
+    for (uint32_t c = 0; c < nc; c++, k++) {
+      if (chunks && k < max_chunks) {
+        chunks[k].tile = t;
+        chunks[k].seg_begin = c * kSegsPerChunk;
+        chunks[k].seg_end = min((c + 1) * kSegsPerChunk, nseg);
+        chunks[k].n_in_tile = nc;
+      }
+    }
+  }
+  *n_chunks = k;
+  return (chunks && k > max_chunks) ? VOOM_E_CAPACITY : VOOM_OK;
 }
 
 VOOM_API int voom_rans_plan(const uint8_t* f, uint64_t n, uint64_t src_base, uint64_t dst_base,
@@ -454,6 +468,11 @@ VOOM_API int voom_rans_plan(const uint8_t* f, uint64_t n, uint64_t src_base, uin
     info->struct_error = code;
     info->struct_tile = tile;
     info->struct_ordinal = ord;
+  };
+  auto freq_total = [&](uint64_t at) {
+    uint64_t tot = 0;
+    for (int s = 0; s < 256; s++) tot += uint32_t(f[at + 2 * s]) | (uint32_t(f[at + 2 * s + 1]) << 8);
+    return tot;
   };
   if (n < 16) {
     fail(VOOM_RANS_TRUNC_FRAME, 0, 0);
@@ -485,29 +504,43 @@ VOOM_API int voom_rans_plan(const uint8_t* f, uint64_t n, uint64_t src_base, uin
         d.flags = VOOM_RANS_DO_COPY | VOOM_RANS_DO_CRC;
       } else if (mode == 1) {
         // low plane (bf16_rans.py:97-114)
-        uint64_t avail = pay, p = pos;
+        const uint64_t avail = pay, p = pos;
         if (avail < 516) { fail(VOOM_RANS_TRUNC_PLANE_HEADER, ti, ORD_LOW_HEADER); broke = true; break; }
-        uint64_t psz = rd32(f + p);
+        const uint64_t psz = rd32(f + p);
         if (psz < 4 || 516 + psz > avail) { fail(VOOM_RANS_TRUNC_PLANE_PAYLOAD, ti, ORD_LOW_PAYLOAD); broke = true; break; }
-        uint64_t tot = 0;
-        for (int s = 0; s < 256; s++) tot += uint32_t(f[p + 4 + 2 * s]) | (uint32_t(f[p + 5 + 2 * s]) << 8);
+        const uint64_t tot = freq_total(p + 4);
         if (tot != 0 && tot != 4096) { fail(VOOM_RANS_BAD_FREQ_TOTAL, ti, ORD_LOW_TOTAL); broke = true; break; }
         d.low_freq = src_base + p + 4;
         d.low_payload = uint32_t(psz);
         d.flags = VOOM_RANS_DO_LOW;
-        uint64_t used = 516 + psz;
-        // high plane
-        uint64_t avail2 = avail - used, p2 = pos + used;
-        if (avail2 < 516) { fail(VOOM_RANS_TRUNC_PLANE_HEADER, ti, ORD_HIGH_HEADER); emit(d); out += raw; broke = true; break; }
-        uint64_t psz2 = rd32(f + p2);
-        if (psz2 < 4 || 516 + psz2 > avail2) { fail(VOOM_RANS_TRUNC_PLANE_PAYLOAD, ti, ORD_HIGH_PAYLOAD); emit(d); out += raw; broke = true; break; }
-        uint64_t tot2 = 0;
-        for (int s = 0; s < 256; s++) tot2 += uint32_t(f[p2 + 4 + 2 * s]) | (uint32_t(f[p2 + 5 + 2 * s]) << 8);
-        if (tot2 != 0 && tot2 != 4096) { fail(VOOM_RANS_BAD_FREQ_TOTAL, ti, ORD_HIGH_TOTAL); emit(d); out += raw; broke = true; break; }
-        d.high_freq = src_base + p2 + 4;
-        d.high_payload = uint32_t(psz2);
-        d.flags |= VOOM_RANS_DO_HIGH;
-        if (used + 516 + psz2 != pay) { fail(VOOM_RANS_TILE_TRAILING, ti, ORD_TILE_TRAILING); emit(d); out += raw; broke = true; break; }
+        const uint64_t used = 516 + psz;
+        // high plane: failures here come after the low plane's decode
+        const uint64_t avail2 = avail - used, p2 = pos + used;
+        int err = 0;
+        uint32_t ord = 0;
+        uint64_t psz2 = 0;
+        if (avail2 < 516) { err = VOOM_RANS_TRUNC_PLANE_HEADER; ord = ORD_HIGH_HEADER; }
+        else {
+          psz2 = rd32(f + p2);
+          if (psz2 < 4 || 516 + psz2 > avail2) { err = VOOM_RANS_TRUNC_PLANE_PAYLOAD; ord = ORD_HIGH_PAYLOAD; }
+          else {
+            const uint64_t tot2 = freq_total(p2 + 4);
+            if (tot2 != 0 && tot2 != 4096) { err = VOOM_RANS_BAD_FREQ_TOTAL; ord = ORD_HIGH_TOTAL; }
+          }
+        }
+        if (!err) {
+          d.high_freq = src_base + p2 + 4;
+          d.high_payload = uint32_t(psz2);
+          d.flags |= VOOM_RANS_DO_HIGH;
+          if (used + 516 + psz2 != pay) { err = VOOM_RANS_TILE_TRAILING; ord = ORD_TILE_TRAILING; }
+        }
+        if (err) {
+          fail(err, ti, ord);
+          emit(d);
+          out += raw;
+          broke = true;
+          break;
+        }
         d.flags |= VOOM_RANS_DO_CRC;
       } else {
         fail(VOOM_RANS_UNKNOWN_MODE, ti, ORD_UNKNOWN_MODE);
@@ -552,40 +585,35 @@ VOOM_API int voom_rans_resolve(const voom_rans_plan_info* info, const uint32_t* 
   return VOOM_OK;
 }
 
-static int launch_rans(bool indexed, const uint8_t* src, const voom_rans_tile* tiles, uint32_t n_tiles,
-                       uint8_t* out, uint32_t* status, uint32_t* ckpt, const uint32_t* ckpt_base,
-                       uint32_t every, void* stream) {
-  if (n_tiles == 0) return VOOM_OK;
-  if (!src || !tiles || !out || !status) return VOOM_E_INVALID_ARG;
-  if ((ckpt || indexed) && (!ckpt_base || !valid_every(every))) return VOOM_E_INVALID_ARG;
-  if (indexed && !ckpt) return VOOM_E_INVALID_ARG;
-  const size_t smem = sizeof(SharedPlanes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  if (indexed) {
-    e = cudaFuncSetAttribute(rans_indexed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return VOOM_E_CUDA;
-    rans_indexed_kernel<<<n_tiles, kThreads, smem, s>>>(src, tiles, out, status, ckpt, ckpt_base, every);
-  } else {
-    e = cudaFuncSetAttribute(rans_cold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return VOOM_E_CUDA;
-    rans_cold_kernel<<<n_tiles, kThreads, smem, s>>>(src, tiles, out, status, ckpt, ckpt_base,
-                                                     ckpt ? every : 64u);
-  }
-  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
-}
-
 VOOM_API int voom_rans_decode(const uint8_t* d_src, const voom_rans_tile* d_tiles, uint32_t n_tiles,
                               uint8_t* d_out, uint32_t* d_status, uint32_t* d_ckpt,
                               const uint32_t* d_ckpt_base, uint32_t ckpt_every, void* stream) {
-  return launch_rans(false, d_src, d_tiles, n_tiles, d_out, d_status, d_ckpt, d_ckpt_base, ckpt_every,
-                     stream);
+  if (n_tiles == 0) return VOOM_OK;
+  if (!d_src || !d_tiles || !d_out || !d_status) return VOOM_E_INVALID_ARG;
+  if (d_ckpt && (!d_ckpt_base || !valid_every(ckpt_every))) return VOOM_E_INVALID_ARG;
+  const size_t smem = sizeof(SharedPlanes);
+  if (cudaFuncSetAttribute(rans_cold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return VOOM_E_CUDA;
+  rans_cold_kernel<<<n_tiles, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      d_src, d_tiles, d_out, d_status, d_ckpt, d_ckpt_base, d_ckpt ? ckpt_every : 64u);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
 
 VOOM_API int voom_rans_decode_indexed(const uint8_t* d_src, const voom_rans_tile* d_tiles,
-                                      uint32_t n_tiles, uint8_t* d_out, uint32_t* d_status,
-                                      const uint32_t* d_ckpt, const uint32_t* d_ckpt_base,
-                                      uint32_t ckpt_every, void* stream) {
-  return launch_rans(true, d_src, d_tiles, n_tiles, d_out, d_status, const_cast<uint32_t*>(d_ckpt),
-                     d_ckpt_base, ckpt_every, stream);
+                                      const voom_rans_chunk* d_chunks, uint32_t n_chunks, uint8_t* d_out,
+                                      uint32_t* d_status, const uint32_t* d_ckpt,
+                                      const uint32_t* d_ckpt_base, uint32_t ckpt_every,
+                                      uint32_t* d_tile_scratch, void* stream) {
+  if (n_chunks == 0) return VOOM_OK;
+  if (!d_src || !d_tiles || !d_chunks || !d_out || !d_status || !d_ckpt || !d_ckpt_base || !d_tile_scratch ||
+      !valid_every(ckpt_every))
+    return VOOM_E_INVALID_ARG;
+  const size_t smem = sizeof(SharedPlanes);
+  if (cudaFuncSetAttribute(rans_indexed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return VOOM_E_CUDA;
+  rans_indexed_kernel<<<n_chunks, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      d_src, d_tiles, d_chunks, d_out, d_status, d_ckpt, d_ckpt_base, ckpt_every, d_tile_scratch);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

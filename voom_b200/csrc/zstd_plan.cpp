@@ -1,0 +1,640 @@
+// Host planner for the GPU zstd decoder.
+//
+// Walks every job's frames exactly as RFC 8878 lays them out -- frame header
+// (3.1.1.1), block headers (3.1.1.2), the literals section header and Huffman
+// tree description (3.1.1.3.1, 4.2.1), the sequences section header and FSE
+// table descriptions (3.1.1.3.2, 4.1.1) -- and records where each block's
+// entropy-coded payloads start.  Those payloads (Huffman literal streams, the
+// FSE sequence bitstream) and everything after them are decoded on the GPU.
+// Jobs are planned on a pool of host threads; each job is independent.
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+#include <thread>
+#include <vector>
+
+#include "../../include/voom_b200.h"
+#include "zstd_plan.h"
+
+#define VOOM_API extern "C" __attribute__((visibility("default")))
+
+using namespace voom::zstd;
+
+namespace {
+
+constexpr uint32_t kPredef = 0x80000000u;  // local marker: predefined table k
+
+inline int hb32(uint32_t v) { return 31 - __builtin_clz(v); }
+
+inline uint64_t le(const uint8_t* p, int n) {
+  uint64_t v = 0;
+  for (int i = 0; i < n; i++) v |= uint64_t(p[i]) << (8 * i);
+  return v;
+}
+
+// ------------------------------------------------ table-description readers
+struct FwdBits {
+  const uint8_t* p;
+  size_t n;
+  uint64_t pos = 0;
+  uint32_t peek(int nb) const {
+    uint32_t v = 0;
+    for (int i = 0; i < nb; i++) {
+      const uint64_t q = pos + uint64_t(i);
+      v |= (q / 8 < n ? (uint32_t(p[q / 8]) >> (q % 8)) & 1u : 0u) << i;
+    }
+    return v;
+  }
+  uint32_t get(int nb) {
+    uint32_t v = peek(nb);
+    pos += uint64_t(nb);
+    return v;
+  }
+};
+
+// FSE normalized counts (RFC 8878 4.1.1).  Returns the symbol count or -1.
+int read_ncount(const uint8_t* p, size_t n, int max_al, int max_sym, int16_t* norm, int* al_out,
+                size_t* used) {
+  if (n == 0) return -1;
+  FwdBits r{p, n};
+  const int al = int(r.get(4)) + 5;
+  if (al > max_al) return -1;
+  int remaining = (1 << al) + 1, threshold = 1 << al, nb = al + 1, sym = 0;
+  for (int i = 0; i <= max_sym; i++) norm[i] = 0;
+  while (remaining > 1) {
+    if (sym > max_sym) return -1;
+    const int mx = (2 * threshold - 1) - remaining;
+    int count;
+    const uint32_t low = r.peek(nb - 1);
+    if (int(low) < mx) {
+      count = int(low);
+      r.pos += uint64_t(nb - 1);
+    } else {
+      uint32_t v = r.peek(nb);
+      if (int(v) >= threshold) v -= uint32_t(mx);
+      count = int(v);
+      r.pos += uint64_t(nb);
+    }
+    count -= 1;
+    remaining -= count < 0 ? -count : count;
+    norm[sym++] = int16_t(count);
+    if (count == 0) {
+      for (;;) {
+        const uint32_t rep = r.get(2);
+        for (uint32_t k = 0; k < rep; k++) {
+          if (sym > max_sym) return -1;
+          norm[sym++] = 0;
+        }
+        if (rep != 3) break;
+      }
+    }
+    while (remaining < threshold) {
+      nb--;
+      threshold >>= 1;
+    }
+  }
+  if (remaining != 1 || r.pos > 8 * uint64_t(n)) return -1;
+  *used = size_t((r.pos + 7) / 8);
+  *al_out = al;
+  return sym;
+}
+
+struct FseCell {
+  uint8_t sym, nb;
+  uint16_t base;
+};
+
+bool fse_build(const int16_t* norm, int nsym, int al, FseCell* t) {
+  const int size = 1 << al;
+  int high = size - 1;
+  uint32_t next[256];
+  uint8_t symtab[512];
+  for (int s = 0; s < nsym; s++) {
+    if (norm[s] == -1) {
+      symtab[high--] = uint8_t(s);
+      next[s] = 1;
+    } else {
+      next[s] = uint32_t(std::max<int>(norm[s], 0));
+    }
+  }
+  int pos = 0;
+  const int step = (size >> 1) + (size >> 3) + 3, mask = size - 1;
+  for (int s = 0; s < nsym; s++)
+    for (int i = 0; i < norm[s]; i++) {
+      symtab[pos] = uint8_t(s);
+      do pos = (pos + step) & mask; while (pos > high);
+    }
+  if (pos != 0) return false;
+  for (int u = 0; u < size; u++) {
+    const int s = symtab[u];
+    const uint32_t x = next[s]++;
+    const int nbits = al - hb32(x);
+    t[u].sym = uint8_t(s);
+    t[u].nb = uint8_t(nbits);
+    t[u].base = uint16_t((x << nbits) - uint32_t(size));
+  }
+  return true;
+}
+
+// Backward bit reader over a small buffer (Huffman weight streams only).
+struct BwdBits {
+  const uint8_t* p;
+  size_t n;
+  int64_t pos;
+  bool init(const uint8_t* b, size_t len) {
+    if (len == 0 || b[len - 1] == 0) return false;
+    p = b;
+    n = len;
+    pos = int64_t(8 * (len - 1)) + hb32(b[len - 1]);
+    return true;
+  }
+  uint32_t read(int nb) {
+    uint32_t v = 0;
+    for (int i = nb - 1; i >= 0; i--) {
+      const int64_t q = pos - nb + i;
+      const uint32_t bit = q >= 0 ? (uint32_t(p[q / 8]) >> (q % 8)) & 1u : 0u;
+      v |= bit << i;
+    }
+    pos -= nb;
+    return v;
+  }
+};
+
+// Huffman tree description (RFC 8878 4.2.1) -> weights of every symbol.
+bool read_huffman(const uint8_t* p, size_t n, ZHuf* h, size_t* used) {
+  uint8_t w[256];
+  int nw = 0;
+  if (n < 1) return false;
+  const int hbyte = p[0];
+  if (hbyte >= 128) {
+    nw = hbyte - 127;
+    const size_t bytes = size_t(nw + 1) / 2;
+    if (1 + bytes > n) return false;
+    for (int i = 0; i < nw; i++) w[i] = (i % 2 == 0) ? p[1 + i / 2] >> 4 : p[1 + i / 2] & 15;
+    *used = 1 + bytes;
+  } else {
+    if (hbyte == 0 || size_t(1 + hbyte) > n) return false;
+    const uint8_t* q = p + 1;
+    int16_t norm[256];
+    int al;
+    size_t hdr;
+    const int ns = read_ncount(q, size_t(hbyte), 6, 255, norm, &al, &hdr);
+    if (ns < 0 || hdr >= size_t(hbyte)) return false;
+    FseCell ft[64];
+    if (!fse_build(norm, ns, al, ft)) return false;
+    BwdBits r;
+    if (!r.init(q + hdr, size_t(hbyte) - hdr)) return false;
+    uint32_t s1 = r.read(al), s2 = r.read(al);
+    for (;;) {
+      if (nw > 253) return false;
+      w[nw++] = ft[s1].sym;
+      s1 = ft[s1].base + r.read(ft[s1].nb);
+      if (r.pos < 0) { w[nw++] = ft[s2].sym; break; }
+      w[nw++] = ft[s2].sym;
+      s2 = ft[s2].base + r.read(ft[s2].nb);
+      if (r.pos < 0) { w[nw++] = ft[s1].sym; break; }
+    }
+    *used = 1 + size_t(hbyte);
+  }
+  uint32_t total = 0;
+  for (int i = 0; i < nw; i++) {
+    if (w[i] > 11) return false;
+    if (w[i]) total += 1u << (w[i] - 1);
+  }
+  if (total == 0) return false;
+  const int maxbits = hb32(total) + 1;
+  if (maxbits > 11) return false;
+  const uint32_t rest = (1u << maxbits) - total;
+  if (rest & (rest - 1)) return false;
+  w[nw++] = uint8_t(hb32(rest) + 1);
+  memset(h, 0, sizeof(*h));
+  memcpy(h->w, w, size_t(nw));
+  h->nsym = uint16_t(nw);
+  h->maxbits = uint8_t(maxbits);
+  return true;
+}
+
+// --------------------------------------------------------------- job plan
+struct JobPlan {
+  std::vector<ZFrame> frames;
+  std::vector<ZBlock> blocks;
+  std::vector<ZHuf> huf;
+  std::vector<ZFse> fse;
+  bool bad = false;
+};
+
+bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZBlock& b, uint32_t& last_huf,
+                     uint32_t last_fse[3]) {
+  const uint8_t* p = base + at;
+  if (n < 1) return false;
+  // literals section header (RFC 8878 3.1.1.3.1.1)
+  const int type = p[0] & 3, sf = (p[0] >> 2) & 3;
+  size_t used;
+  if (type <= 1) {
+    size_t regen, hsz;
+    if (sf == 0 || sf == 2) { regen = p[0] >> 3; hsz = 1; }
+    else if (sf == 1) { if (n < 2) return false; regen = (p[0] >> 4) + (size_t(p[1]) << 4); hsz = 2; }
+    else { if (n < 3) return false; regen = (p[0] >> 4) + (size_t(p[1]) << 4) + (size_t(p[2]) << 12); hsz = 3; }
+    if (regen > kBlockMax) return false;
+    b.lit_type = uint32_t(type);
+    b.lit_regen = uint32_t(regen);
+    b.src = at + hsz;
+    if (type == 0) {
+      if (hsz + regen > n) return false;
+      used = hsz + regen;
+    } else {
+      if (hsz + 1 > n) return false;
+      used = hsz + 1;
+    }
+    b.lit_streams = 0;
+  } else {
+    const int streams = sf == 0 ? 1 : 4;
+    const int hsz = sf <= 1 ? 3 : (sf == 2 ? 4 : 5);
+    const int bits = sf <= 1 ? 10 : (sf == 2 ? 14 : 18);
+    if (size_t(hsz) > n) return false;
+    const uint64_t hv = le(p, hsz);
+    const size_t regen = size_t((hv >> 4) & ((1u << bits) - 1));
+    const size_t csize = size_t((hv >> (4 + bits)) & ((1u << bits) - 1));
+    if (regen > kBlockMax || size_t(hsz) + csize > n) return false;
+    size_t q = size_t(hsz), avail = csize;
+    if (type == 2) {
+      ZHuf h;
+      size_t wu;
+      if (!read_huffman(p + q, avail, &h, &wu)) return false;
+      last_huf = uint32_t(jp.huf.size());
+      jp.huf.push_back(h);
+      q += wu;
+      avail -= wu;
+    } else if (last_huf == kNone) {
+      return false;  // treeless literals without a previous table
+    }
+    b.lit_type = 2;
+    b.lit_regen = uint32_t(regen);
+    b.lit_streams = uint32_t(streams);
+    b.huf = last_huf;
+    if (streams == 1) {
+      if (avail == 0) return false;
+      b.src = at + q;
+      b.lit_len[0] = uint32_t(avail);
+    } else {
+      if (avail < 10) return false;
+      const size_t s1 = p[q] | (p[q + 1] << 8), s2 = p[q + 2] | (p[q + 3] << 8), s3 = p[q + 4] | (p[q + 5] << 8);
+      if (6 + s1 + s2 + s3 >= avail || !s1 || !s2 || !s3) return false;
+      const size_t seg = (regen + 3) / 4;
+      if (3 * seg > regen) return false;
+      b.src = at + q + 6;
+      b.lit_len[0] = uint32_t(s1);
+      b.lit_len[1] = uint32_t(s2);
+      b.lit_len[2] = uint32_t(s3);
+      b.lit_len[3] = uint32_t(avail - 6 - s1 - s2 - s3);
+    }
+    used = size_t(hsz) + csize;
+  }
+  // sequences section header (RFC 8878 3.1.1.3.2.1)
+  p += used;
+  at += used;
+  n -= used;
+  if (n < 1) return false;
+  size_t nseq, hsz;
+  if (p[0] == 0) {
+    if (n != 1) return false;
+    b.nseq = 0;
+    return true;
+  } else if (p[0] < 128) {
+    nseq = p[0];
+    hsz = 1;
+  } else if (p[0] < 255) {
+    if (n < 2) return false;
+    nseq = (size_t(p[0] - 128) << 8) + p[1];
+    hsz = 2;
+  } else {
+    if (n < 3) return false;
+    nseq = p[1] + (size_t(p[2]) << 8) + 0x7F00;
+    hsz = 3;
+  }
+  if (hsz >= n) return false;
+  const uint8_t modes = p[hsz++];
+  if (modes & 3) return false;
+  static const int kMaxAl[3] = {9, 8, 9}, kMaxSym[3] = {35, 31, 52};
+  const int mode[3] = {modes >> 6, (modes >> 4) & 3, (modes >> 2) & 3};  // LL, OF, ML
+  for (int k = 0; k < 3; k++) {
+    if (mode[k] == 0) {
+      b.fse[k] = kPredef | uint32_t(k);
+    } else if (mode[k] == 1) {
+      if (hsz >= n || p[hsz] > kMaxSym[k]) return false;
+      ZFse f;
+      memset(&f, 0, sizeof f);
+      f.rle = 1;
+      f.rle_sym = p[hsz++];
+      b.fse[k] = uint32_t(jp.fse.size());
+      jp.fse.push_back(f);
+    } else if (mode[k] == 2) {
+      ZFse f;
+      memset(&f, 0, sizeof f);
+      int al;
+      size_t u;
+      const int ns = read_ncount(p + hsz, n - hsz, kMaxAl[k], kMaxSym[k], f.norm, &al, &u);
+      if (ns < 0) return false;
+      FseCell tmp[512];
+      if (!fse_build(f.norm, ns, al, tmp)) return false;
+      f.nsym = uint16_t(ns);
+      f.al = uint8_t(al);
+      b.fse[k] = uint32_t(jp.fse.size());
+      jp.fse.push_back(f);
+      hsz += u;
+    } else {
+      if (last_fse[k] == kNone) return false;
+      b.fse[k] = last_fse[k];
+    }
+  }
+  for (int k = 0; k < 3; k++) last_fse[k] = b.fse[k];
+  if (hsz >= n || p[n - 1] == 0) return false;
+  b.nseq = uint32_t(nseq);
+  b.seq_src = at + hsz;
+  b.seq_len = uint32_t(n - hsz);
+  return true;
+}
+
+void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
+  uint64_t pos = job.src;
+  const uint64_t end = job.src + job.src_len;
+  if (job.src_len == 0) { jp.bad = true; return; }
+  while (pos < end) {
+    if (end - pos < 4) { jp.bad = true; return; }
+    const uint32_t magic = uint32_t(le(base + pos, 4));
+    if ((magic & 0xFFFFFFF0u) == 0x184D2A50u) {  // skippable frame
+      if (end - pos < 8) { jp.bad = true; return; }
+      const uint64_t sz = le(base + pos + 4, 4);
+      if (pos + 8 + sz > end) { jp.bad = true; return; }
+      pos += 8 + sz;
+      continue;
+    }
+    if (magic != 0xFD2FB528u) { jp.bad = true; return; }
+    pos += 4;
+    if (pos >= end) { jp.bad = true; return; }
+    const uint8_t fhd = base[pos++];
+    const int fcs_flag = fhd >> 6, single = (fhd >> 5) & 1, csum = (fhd >> 2) & 1, did = fhd & 3;
+    if (fhd & 8) { jp.bad = true; return; }
+    uint64_t wsize = 0;
+    if (!single) {
+      if (pos >= end) { jp.bad = true; return; }
+      const uint8_t wd = base[pos++];
+      const uint64_t wbase = 1ull << (10 + (wd >> 3));
+      wsize = wbase + (wbase / 8) * (wd & 7);
+    }
+    static const int kDid[4] = {0, 1, 2, 4};
+    if (pos + uint64_t(kDid[did]) > end) { jp.bad = true; return; }
+    if (kDid[did] && le(base + pos, kDid[did]) != 0) { jp.bad = true; return; }  // no dictionaries
+    pos += uint64_t(kDid[did]);
+    const int fcs_sz = fcs_flag == 0 ? (single ? 1 : 0) : (fcs_flag == 1 ? 2 : (fcs_flag == 2 ? 4 : 8));
+    if (pos + uint64_t(fcs_sz) > end) { jp.bad = true; return; }
+    ZFrame fr;
+    memset(&fr, 0, sizeof fr);
+    fr.fcs = fcs_sz ? le(base + pos, fcs_sz) + (fcs_sz == 2 ? 256 : 0) : ~0ull;
+    pos += uint64_t(fcs_sz);
+    if (single) wsize = fr.fcs;
+    const uint64_t block_max = std::min<uint64_t>(wsize, kBlockMax);
+    fr.block_first = uint32_t(jp.blocks.size());
+    const uint32_t frame_index = uint32_t(jp.frames.size());
+    uint32_t last_huf = kNone, last_fse[3] = {kNone, kNone, kNone};
+    for (;;) {
+      if (pos + 3 > end) { jp.bad = true; return; }
+      const uint32_t bh = uint32_t(le(base + pos, 3));
+      pos += 3;
+      const int last = bh & 1, type = (bh >> 1) & 3;
+      const uint64_t bs = bh >> 3;
+      if (type == 3 || bs > block_max) { jp.bad = true; return; }
+      ZBlock b;
+      memset(&b, 0, sizeof b);
+      b.type = uint32_t(type);
+      b.frame = frame_index;
+      b.huf = kNone;
+      b.fse[0] = b.fse[1] = b.fse[2] = kNone;
+      if (type == 0) {
+        if (pos + bs > end) { jp.bad = true; return; }
+        b.src = pos;
+        b.size = uint32_t(bs);
+        pos += bs;
+      } else if (type == 1) {
+        if (pos + 1 > end) { jp.bad = true; return; }
+        b.src = pos;
+        b.size = uint32_t(bs);
+        pos += 1;
+      } else {
+        if (pos + bs > end) { jp.bad = true; return; }
+        if (!plan_compressed(base, pos, size_t(bs), jp, b, last_huf, last_fse)) { jp.bad = true; return; }
+        pos += bs;
+      }
+      jp.blocks.push_back(b);
+      if (last) break;
+    }
+    fr.n_blocks = uint32_t(jp.blocks.size()) - fr.block_first;
+    fr.csum_flag = uint32_t(csum);
+    if (csum) {
+      if (pos + 4 > end) { jp.bad = true; return; }
+      fr.csum = uint32_t(le(base + pos, 4));
+      pos += 4;
+    }
+    jp.frames.push_back(fr);
+  }
+}
+
+struct Plan {
+  std::vector<ZJob> jobs;
+  std::vector<ZFrame> frames;
+  std::vector<ZBlock> blocks;
+  std::vector<ZHuf> huf;
+  std::vector<ZFse> fse;
+  std::vector<ZOutTile> tiles;
+  std::vector<uint32_t> status;
+  ZPlanHeader hdr;
+  uint64_t image_bytes = 0;
+  uint32_t n_bad = 0;
+};
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+const int16_t kLLDef[36] = {4, 3, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 1, 1, 1, 2, 2,
+                            2, 2, 2, 2, 2, 2, 2, 3, 2, 1, 1, 1, 1, 1, -1, -1, -1, -1};
+const int16_t kOFDef[29] = {1, 1, 1, 1, 1, 1, 2, 2, 2, 1, 1, 1, 1, 1, 1,
+                            1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1};
+const int16_t kMLDef[53] = {1, 4, 3, 2, 2, 2, 2, 2, 2, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                            1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                            1, 1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1, -1, -1};
+
+}  // namespace
+
+VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, const voom_zstd_job* jobs,
+                                     uint32_t n_jobs, int threads) {
+  if ((!h_src && src_len) || (!jobs && n_jobs)) return nullptr;
+  Plan* P = new (std::nothrow) Plan();
+  if (!P) return nullptr;
+  std::vector<JobPlan> jp(n_jobs);
+  int nt = threads > 0 ? threads : int(std::max(1u, std::thread::hardware_concurrency()));
+  nt = std::max(1, std::min<int>(nt, int(n_jobs)));
+  auto work = [&](int w) {
+    for (uint32_t j = uint32_t(w); j < n_jobs; j += uint32_t(nt)) {
+      if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; continue; }
+      plan_job(h_src, jobs[j], jp[j]);
+    }
+  };
+  std::vector<std::thread> pool;
+  for (int w = 1; w < nt; w++) pool.emplace_back(work, w);
+  if (n_jobs) work(0);
+  for (auto& t : pool) t.join();
+
+  // predefined sequence tables occupy fse[0..2]
+  for (int k = 0; k < 3; k++) {
+    ZFse f;
+    memset(&f, 0, sizeof f);
+    const int16_t* d = k == 0 ? kLLDef : (k == 1 ? kOFDef : kMLDef);
+    const int n = k == 0 ? 36 : (k == 1 ? 29 : 53);
+    for (int i = 0; i < n; i++) f.norm[i] = d[i];
+    f.nsym = uint16_t(n);
+    f.al = uint8_t(k == 1 ? 5 : 6);
+    P->fse.push_back(f);
+  }
+  uint64_t zoff = 0, lit = 0, nseq = 0;
+  P->status.assign(n_jobs, 0);
+  for (uint32_t j = 0; j < n_jobs; j++) {
+    ZJob zj;
+    memset(&zj, 0, sizeof zj);
+    zj.src = jobs[j].src;
+    zj.src_len = jobs[j].src_len;
+    zj.dst = jobs[j].dst;
+    zj.dst_len = jobs[j].dst_len;
+    zj.lo_src = jobs[j].lo_src;
+    zj.flags = jobs[j].flags;
+    zj.zoff = zoff;
+    zoff += align_up(jobs[j].dst_len, 16);
+    JobPlan& q = jp[j];
+    if (q.bad) {
+      zj.bad = 1;
+      P->status[j] = VOOM_ZSTD_ST_FORMAT;
+      P->n_bad++;
+      P->jobs.push_back(zj);
+      continue;
+    }
+    const uint32_t fbase = uint32_t(P->frames.size()), bbase = uint32_t(P->blocks.size());
+    const uint32_t hbase = uint32_t(P->huf.size()), sbase = uint32_t(P->fse.size());
+    zj.frame_first = fbase;
+    zj.n_frames = uint32_t(q.frames.size());
+    for (auto f : q.frames) {
+      f.block_first += bbase;
+      f.job = j;
+      P->frames.push_back(f);
+    }
+    for (auto b : q.blocks) {
+      b.frame += fbase;
+      b.job = j;
+      if (b.huf != kNone) b.huf += hbase;
+      for (int k = 0; k < 3; k++) {
+        if (b.fse[k] == kNone) continue;
+        b.fse[k] = (b.fse[k] & kPredef) ? (b.fse[k] & 3u) : b.fse[k] + sbase;
+      }
+      b.src += 0;
+      b.lit_off = lit;
+      b.seq_off = nseq;
+      if (b.type == 2) {
+        lit += align_up(b.lit_regen, 16);
+        nseq += b.nseq;
+      }
+      P->blocks.push_back(b);
+    }
+    P->huf.insert(P->huf.end(), q.huf.begin(), q.huf.end());
+    P->fse.insert(P->fse.end(), q.fse.begin(), q.fse.end());
+    for (uint64_t s = 0; s < jobs[j].dst_len; s += kOutTile) {
+      ZOutTile t;
+      memset(&t, 0, sizeof t);
+      t.job = j;
+      t.begin = s;
+      t.len = std::min<uint64_t>(kOutTile, jobs[j].dst_len - s);
+      P->tiles.push_back(t);
+    }
+    P->jobs.push_back(zj);
+  }
+  ZPlanHeader& h = P->hdr;
+  memset(&h, 0, sizeof h);
+  h.n_jobs = n_jobs;
+  h.n_frames = uint32_t(P->frames.size());
+  h.n_blocks = uint32_t(P->blocks.size());
+  h.n_huf = uint32_t(P->huf.size());
+  h.n_fse = uint32_t(P->fse.size());
+  h.n_tiles = uint32_t(P->tiles.size());
+  uint64_t o = align_up(sizeof(ZPlanHeader), 256);
+  h.off_jobs = o; o = align_up(o + sizeof(ZJob) * P->jobs.size(), 256);
+  h.off_frames = o; o = align_up(o + sizeof(ZFrame) * P->frames.size(), 256);
+  h.off_blocks = o; o = align_up(o + sizeof(ZBlock) * P->blocks.size(), 256);
+  h.off_huf = o; o = align_up(o + sizeof(ZHuf) * P->huf.size(), 256);
+  h.off_fse = o; o = align_up(o + sizeof(ZFse) * P->fse.size(), 256);
+  h.off_tiles = o; o = align_up(o + sizeof(ZOutTile) * P->tiles.size(), 256);
+  P->image_bytes = o;
+  h.lit_bytes = lit;
+  h.n_seq = nseq;
+  h.zbytes = zoff;
+  uint64_t s = 0;
+  h.s_res = s; s = align_up(s + 4 * zoff, 256);
+  h.s_lit = s; s = align_up(s + lit + 64, 256);
+  h.s_seq = s; s = align_up(s + sizeof(ZSeq) * nseq, 256);
+  h.s_blk = s; s = align_up(s + sizeof(ZBlockRt) * P->blocks.size(), 256);
+  h.s_ctr = s; s = align_up(s + 4 * P->tiles.size() + 256, 256);
+  h.s_total = s;
+  return P;
+}
+
+VOOM_API int voom_zstd_plan_info_get(const void* plan, voom_zstd_plan_info* info) {
+  if (!plan || !info) return VOOM_E_INVALID_ARG;
+  const Plan* P = static_cast<const Plan*>(plan);
+  memset(info, 0, sizeof(*info));
+  info->n_jobs = P->hdr.n_jobs;
+  info->n_frames = P->hdr.n_frames;
+  info->n_blocks = P->hdr.n_blocks;
+  info->n_huf = P->hdr.n_huf;
+  info->n_fse = P->hdr.n_fse;
+  info->n_bad_jobs = P->n_bad;
+  info->lit_bytes = P->hdr.lit_bytes;
+  info->n_seq = P->hdr.n_seq;
+  info->decoded_bytes = P->hdr.zbytes;
+  info->scratch_bytes = P->hdr.s_total;
+  info->plan_bytes = P->image_bytes;
+  return VOOM_OK;
+}
+
+VOOM_API int voom_zstd_plan_image(const void* plan, void* h_image, uint64_t cap) {
+  if (!plan || !h_image) return VOOM_E_INVALID_ARG;
+  const Plan* P = static_cast<const Plan*>(plan);
+  if (cap < P->image_bytes) return VOOM_E_CAPACITY;
+  uint8_t* img = static_cast<uint8_t*>(h_image);
+  memset(img, 0, P->image_bytes);
+  const ZPlanHeader& h = P->hdr;
+  memcpy(img, &h, sizeof h);
+  if (!P->jobs.empty()) memcpy(img + h.off_jobs, P->jobs.data(), sizeof(ZJob) * P->jobs.size());
+  if (!P->frames.empty()) memcpy(img + h.off_frames, P->frames.data(), sizeof(ZFrame) * P->frames.size());
+  if (!P->blocks.empty()) memcpy(img + h.off_blocks, P->blocks.data(), sizeof(ZBlock) * P->blocks.size());
+  if (!P->huf.empty()) memcpy(img + h.off_huf, P->huf.data(), sizeof(ZHuf) * P->huf.size());
+  if (!P->fse.empty()) memcpy(img + h.off_fse, P->fse.data(), sizeof(ZFse) * P->fse.size());
+  if (!P->tiles.empty()) memcpy(img + h.off_tiles, P->tiles.data(), sizeof(ZOutTile) * P->tiles.size());
+  return VOOM_OK;
+}
+
+VOOM_API int voom_zstd_plan_job_status(const void* plan, uint32_t* h_status) {
+  if (!plan || !h_status) return VOOM_E_INVALID_ARG;
+  const Plan* P = static_cast<const Plan*>(plan);
+  for (size_t j = 0; j < P->status.size(); j++) h_status[j] = P->status[j];
+  return VOOM_OK;
+}
+
+VOOM_API void voom_zstd_plan_destroy(void* plan) { delete static_cast<Plan*>(plan); }
+
+namespace voom {
+namespace zstd {
+// Launch sizes for voom_zstd_decode, read from the host plan handle.
+bool plan_counts(const void* plan, ZPlanHeader* out) {
+  if (!plan) return false;
+  *out = static_cast<const Plan*>(plan)->hdr;
+  return true;
+}
+}  // namespace zstd
+}  // namespace voom

@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from .. import _device
-from .._lib import RANS_MESSAGES, RANS_TILE_DTYPE, RansPlanInfo, VoomError, check, load
+from .._lib import RANS_CHUNK_DTYPE, RANS_MESSAGES, RANS_TILE_DTYPE, RansPlanInfo, VoomError, check, load
 
 _MAGIC = b"VRN1"
 _SCALE_BITS = 12
@@ -197,6 +197,16 @@ class RansPage:
             code = resolve(self.plan, st)
             if code:
                 _raise(code, self.plan.info)
+            nch = ctypes.c_uint32(0)
+            tiles_h = np.ascontiguousarray(self.plan.tiles)
+            check(lib.voom_rans_chunks(tiles_h.ctypes.data if n else None, n, self.every, None, 0,
+                                       ctypes.byref(nch)), "voom_rans_chunks(size)")
+            chunks = np.zeros(max(nch.value, 1), dtype=RANS_CHUNK_DTYPE)
+            check(lib.voom_rans_chunks(tiles_h.ctypes.data if n else None, n, self.every, chunks.ctypes.data,
+                                       chunks.size, ctypes.byref(nch)), "voom_rans_chunks")
+            self.n_chunks = int(nch.value)
+            self.chunks = _device.tensor_from_numpy(chunks, self.device)
+            self.tile_scratch = torch.zeros(4 * max(n, 1), dtype=torch.int32, device=self.device)
         self.raw_size = self.plan.raw_size
         self.compressed_bytes = int(self.src.numel() - _device.PAD)
 
@@ -206,9 +216,10 @@ class RansPage:
         one u32 per tile (0 = exact).  No host synchronisation."""
         lib = load()
         if self.n_tiles:
-            check(lib.voom_rans_decode_indexed(self.src.data_ptr(), self.tiles.data_ptr(), self.n_tiles,
-                                               out.data_ptr(), status.data_ptr(), self.ckpt.data_ptr(),
-                                               self.ckpt_base.data_ptr(), self.every,
+            check(lib.voom_rans_decode_indexed(self.src.data_ptr(), self.tiles.data_ptr(), self.chunks.data_ptr(),
+                                               self.n_chunks, out.data_ptr(), status.data_ptr(),
+                                               self.ckpt.data_ptr(), self.ckpt_base.data_ptr(), self.every,
+                                               self.tile_scratch.data_ptr(),
                                                _device.stream_ptr(self.device, stream)),
                   "voom_rans_decode_indexed")
 

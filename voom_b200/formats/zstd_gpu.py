@@ -1,0 +1,171 @@
+"""GPU Zstandard decompression (RFC 8878) through libvoom_b200.
+
+`decompress(data)` is the drop-in for `compression.zstd.decompress` as the
+reference uses it (formats/packed.py:376-378, formats/packed2.py:182-191,
+runtime/kv_paged.py:102-103) but returns a CUDA uint8 tensor.  `ZstdBatch`
+decodes many independent jobs (frames, optionally interleaved with a raw lo
+plane as vpack bodies are) in one set of launches: the host plans frame and
+block headers, the GPU decodes the entropy-coded payloads, executes the
+sequences and writes the output.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from .. import _device
+from .._lib import VoomError, check, load
+
+JOB_DTYPE = np.dtype([("src", "<u8"), ("src_len", "<u8"), ("dst", "<u8"), ("dst_len", "<u8"),
+                      ("lo_src", "<u8"), ("flags", "<u4"), ("pad", "<u4")])
+assert JOB_DTYPE.itemsize == 48
+
+INTERLEAVE = 1
+ST_FORMAT, ST_LITERALS, ST_SEQUENCES, ST_OFFSET, ST_SIZE, ST_CHECKSUM, ST_UNRESOLVED = 1, 2, 4, 8, 16, 32, 64
+_ST_NAMES = {ST_FORMAT: "malformed frame", ST_LITERALS: "corrupt literals", ST_SEQUENCES: "corrupt sequences",
+             ST_OFFSET: "offset out of range", ST_SIZE: "content size mismatch",
+             ST_CHECKSUM: "content checksum mismatch", ST_UNRESOLVED: "unresolved match chain"}
+
+
+class ZstdError(Exception):
+    """A job failed to decode (mirrors compression.zstd.ZstdError)."""
+
+
+def describe(status: int) -> str:
+    return ", ".join(n for b, n in _ST_NAMES.items() if status & b) or "ok"
+
+
+class PlanInfo(ctypes.Structure):
+    _fields_ = [("n_jobs", ctypes.c_uint32), ("n_frames", ctypes.c_uint32), ("n_blocks", ctypes.c_uint32),
+                ("n_huf", ctypes.c_uint32), ("n_fse", ctypes.c_uint32), ("n_bad_jobs", ctypes.c_uint32),
+                ("lit_bytes", ctypes.c_uint64), ("n_seq", ctypes.c_uint64), ("decoded_bytes", ctypes.c_uint64),
+                ("scratch_bytes", ctypes.c_uint64), ("plan_bytes", ctypes.c_uint64)]
+
+
+def frame_content_size(data) -> int | None:
+    """Sum of Frame_Content_Size over the frames in `data` (skippable frames
+    skipped); None when a frame does not record its size."""
+    b = memoryview(_device.as_u8(data))
+    pos, total = 0, 0
+    n = len(b)
+    while pos < n:
+        if n - pos < 5:
+            return None
+        magic = int.from_bytes(b[pos:pos + 4], "little")
+        if (magic & 0xFFFFFFF0) == 0x184D2A50:
+            pos += 8 + int.from_bytes(b[pos + 4:pos + 8], "little")
+            continue
+        if magic != 0xFD2FB528:
+            return None
+        fhd = b[pos + 4]
+        single = (fhd >> 5) & 1
+        fcs_flag = fhd >> 6
+        did = (0, 1, 2, 4)[fhd & 3]
+        q = pos + 5 + (0 if single else 1) + did
+        fcs_sz = (1 if single else 0) if fcs_flag == 0 else (2, 4, 8)[fcs_flag - 1]
+        if fcs_sz == 0:
+            return None
+        v = int.from_bytes(b[q:q + fcs_sz], "little") + (256 if fcs_sz == 2 else 0)
+        total += v
+        # walk blocks to find the next frame
+        q += fcs_sz
+        while True:
+            if q + 3 > n:
+                return None
+            bh = int.from_bytes(b[q:q + 3], "little")
+            q += 3
+            btype, bsize = (bh >> 1) & 3, bh >> 3
+            q += 1 if btype == 1 else bsize
+            if bh & 1:
+                break
+        if (fhd >> 2) & 1:
+            q += 4
+        pos = q
+    return total
+
+
+class ZstdPlan:
+    """Host plan of a batch of jobs; owns the native plan handle."""
+
+    def __init__(self, src_host: np.ndarray, jobs: np.ndarray, threads: int = 0):
+        self._lib = load()
+        self.jobs = np.ascontiguousarray(jobs, dtype=JOB_DTYPE)
+        src = np.ascontiguousarray(src_host).reshape(-1).view(np.uint8)
+        self.handle = self._lib.voom_zstd_plan_create(src.ctypes.data if src.size else None, src.size,
+                                                      self.jobs.ctypes.data if self.jobs.size else None,
+                                                      self.jobs.size, int(threads))
+        if not self.handle:
+            raise VoomError("voom_zstd_plan_create failed")
+        self.info = PlanInfo()
+        check(self._lib.voom_zstd_plan_info_get(self.handle, ctypes.byref(self.info)), "voom_zstd_plan_info_get")
+        self.image = np.zeros(max(self.info.plan_bytes, 1), dtype=np.uint8)
+        check(self._lib.voom_zstd_plan_image(self.handle, self.image.ctypes.data, self.image.size),
+              "voom_zstd_plan_image")
+        self.plan_status = np.zeros(max(self.jobs.size, 1), dtype=np.uint32)
+        check(self._lib.voom_zstd_plan_job_status(self.handle, self.plan_status.ctypes.data),
+              "voom_zstd_plan_job_status")
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h:
+            self._lib.voom_zstd_plan_destroy(h)
+            self.handle = None
+
+
+class ZstdBatch:
+    """A planned batch resident on one device: plan image + scratch."""
+
+    def __init__(self, plan: ZstdPlan, device, scratch: torch.Tensor | None = None):
+        self.plan = plan
+        self.device = device
+        self.d_plan = _device.tensor_from_numpy(plan.image, device)
+        need = int(plan.info.scratch_bytes)
+        if scratch is None or scratch.numel() < need:
+            scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+        self.scratch = scratch
+        self.status = torch.zeros(max(plan.jobs.size, 1), dtype=torch.int32, device=device)
+
+    def run(self, d_src: torch.Tensor, d_out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+        """Enqueue the decode; statuses accumulate into self.status (cleared here)."""
+        self.status.zero_()
+        check(load().voom_zstd_decode(d_src.data_ptr(), self.d_plan.data_ptr(), self.plan.handle,
+                                      self.scratch.data_ptr(), d_out.data_ptr(), self.status.data_ptr(),
+                                      _device.stream_ptr(self.device, stream)), "voom_zstd_decode")
+
+    def job_status(self) -> np.ndarray:
+        n = self.plan.jobs.size
+        st = self.status[:n].cpu().numpy().view(np.uint32) if n else np.zeros(0, np.uint32)
+        return st | self.plan.plan_status[:n]
+
+
+def decompress_device(data, size: int | None = None, *, device=None,
+                      stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """GPU zstd.decompress(data) -> CUDA uint8 tensor of the decoded bytes."""
+    dev = _device.require_cuda(device)
+    arr = _device.as_u8(data)
+    if size is None:
+        size = frame_content_size(arr)
+        if size is None:
+            raise ZstdError("frame content size unknown; pass size=")
+    jobs = np.zeros(1, dtype=JOB_DTYPE)
+    jobs[0] = (0, arr.size, 0, size, 0, 0, 0)
+    plan = ZstdPlan(arr, jobs)
+    if plan.plan_status[0]:
+        raise ZstdError(describe(int(plan.plan_status[0])))
+    with torch.cuda.device(dev):
+        d_src = _device.upload(arr, dev, stream=stream)
+        out = torch.empty(max(size, 1), dtype=torch.uint8, device=dev)
+        batch = ZstdBatch(plan, dev)
+        batch.run(d_src, out, stream)
+        st = batch.job_status()
+    if st[0]:
+        raise ZstdError(describe(int(st[0])))
+    return out[:size]
+
+
+def decompress(data, size: int | None = None) -> bytes:
+    """Drop-in for compression.zstd.decompress(data) (bytes in, bytes out)."""
+    return decompress_device(data, size).cpu().numpy().tobytes()
