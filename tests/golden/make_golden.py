@@ -105,10 +105,64 @@ def apply_mutation(frame: bytes, m: dict) -> bytes:
     raise ValueError(m["op"])
 
 
+TINY = dict(layers=2, hidden=64, intermediate=128, heads=4, kv_heads=2, head_dim=16, vocab=256)
+
+
+def write_safetensors(path: Path, tensors: list[tuple[str, str, list[int], bytes]]) -> None:
+    header, off = {}, 0
+    for name, dtype, shape, raw in tensors:
+        header[name] = {"dtype": dtype, "shape": shape, "data_offsets": [off, off + len(raw)]}
+        off += len(raw)
+    hj = json.dumps(header).encode()
+    with open(path, "wb") as f:
+        f.write(len(hj).to_bytes(8, "little") + hj)
+        for _, _, _, raw in tensors:
+            f.write(raw)
+
+
+def vpack_fixture(ref: Path) -> None:
+    """A tiny SmolLM2-shaped checkpoint (plus one fused BF16 expert tensor and
+    one F32 tensor) packed by the reference's pack_model + build_from_vpack."""
+    import shutil
+    import tempfile
+
+    sys.path.insert(0, str(HERE / "_shim"))
+    from formats import packed, packed2  # the reference modules, unmodified
+
+    tensors = []
+    for i, (name, shape) in enumerate(synthetic.smollm2_tensors(TINY)):
+        tensors.append((name, "BF16", list(shape), synthetic.bf16_normal(shape, 0.02, 500 + i).tobytes()))
+    tensors.append(("model.layers.1.mlp.experts.gate_up_proj", "BF16", [4, 32, 64],
+                    synthetic.bf16_normal((4, 32, 64), 0.02, 99).tobytes()))
+    tensors.append(("model.layers.1.mlp.router.scale", "F32", [8],
+                    np.arange(8, dtype=np.float32).tobytes()))
+    tmp = Path(tempfile.mkdtemp())
+    try:
+        write_safetensors(tmp / "model.safetensors", tensors)
+        packed.pack_model(tmp, level=1)
+        packed2.build_from_vpack(tmp)
+        archive = (tmp / "weights.vpack2").read_bytes()
+        index = json.loads((tmp / "weights.vpack2.index.json").read_text())
+        decoded = {}
+        for name, e in index.items():
+            raw = packed2.decode_body(e["head"], archive[e["off"]:e["off"] + e["len"]])
+            decoded[name] = sha(raw.tobytes() if isinstance(raw, np.ndarray) else bytes(raw))
+        (HERE / "vpack2_tiny.bin").write_bytes(archive)
+        (HERE / "vpack2_tiny.index.json").write_text(json.dumps(index, indent=0))
+        (HERE / "vpack2_tiny.decoded.json").write_text(json.dumps(
+            {"decoded_sha256": decoded, "source": [(n, d, s) for n, d, s, _ in tensors],
+             "source_sha256": {n: sha(r) for n, _, _, r in tensors}}, indent=0))
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    print(f"vpack2 fixture: {len(index)} bodies, {len(archive)} bytes")
+
+
 def main() -> None:
     ref = _reference_path()
     sys.path.insert(0, str(ref))
     from formats import bf16_rans as R  # the reference module, unmodified
+
+    vpack_fixture(ref)
 
     manifest = []
     frames = {}

@@ -1,0 +1,113 @@
+"""GPU parity for vpack / vpack2 decode (batched zstd + lo/hi interleave on the
+device) against the reference's archive and its decoded bytes."""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import shutil
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import vpack as ov
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def sha(b) -> str:
+    return hashlib.sha256(bytes(b)).hexdigest()
+
+
+@pytest.fixture()
+def archive_dir(tmp_path, built_lib):
+    shutil.copy(GOLDEN / "vpack2_tiny.bin", tmp_path / "weights.vpack2")
+    shutil.copy(GOLDEN / "vpack2_tiny.index.json", tmp_path / "weights.vpack2.index.json")
+    return tmp_path
+
+
+@pytest.fixture(scope="module")
+def decoded():
+    return json.loads((GOLDEN / "vpack2_tiny.decoded.json").read_text())["decoded_sha256"]
+
+
+def test_reader_fetch_matches_reference(archive_dir, decoded):
+    from voom_b200.formats.packed import TORCH_DTYPES
+    from voom_b200.formats.packed2 import Vpack2Reader
+
+    r = Vpack2Reader(archive_dir, require_hashes=True)
+    names = list(r.index)
+    tensors, secs, nbytes = r.fetch(names)
+    assert set(tensors) == set(names)
+    assert nbytes == (archive_dir / "weights.vpack2").stat().st_size
+    for n in names:
+        t = tensors[n]
+        head = r.index[n]["head"]
+        assert t.is_cuda and t.dtype == TORCH_DTYPES[head["dtype"]] and list(t.shape) == head["shape"]
+        assert sha(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()) == decoded[n], n
+
+
+def test_reader_fetch_subset_and_runs(archive_dir, decoded):
+    from voom_b200.formats.packed2 import Vpack2Reader
+
+    r = Vpack2Reader(archive_dir)
+    names = [n for n in r.index if ".experts." in n][::3] + ["model.embed_tokens.weight"]
+    tensors, _, _ = r.fetch(names, parallel=2)
+    for n in names:
+        assert sha(tensors[n].view(torch.uint8).cpu().numpy().tobytes()) == decoded[n]
+
+
+def test_decode_body_each(archive_dir, decoded):
+    from voom_b200.formats.packed2 import decode_body
+
+    archive = (archive_dir / "weights.vpack2").read_bytes()
+    index = json.loads((archive_dir / "weights.vpack2.index.json").read_text())
+    for n, e in index.items():
+        got = decode_body(e["head"], archive[e["off"]:e["off"] + e["len"]])
+        assert sha(got.cpu().numpy().tobytes()) == decoded[n]
+
+
+def test_streamed_variant(built_lib):
+    from voom_b200 import synthetic
+    from voom_b200.formats import packed
+    from voom_b200.formats.packed2 import decode_body
+
+    raw = synthetic.bf16_normal((3, 700_001), 0.02, 8).view(np.uint8)  # odd element count, 3 zstd calls
+    head, body = packed.streamed_body(raw, level=1, chunk=1 << 20)
+    assert head["streamed"] and head["lo"] == raw.size // 2
+    got = decode_body(head, body).cpu().numpy()
+    assert np.array_equal(got, raw.reshape(-1))
+    assert np.array_equal(ov.decode_body(head, body), raw.reshape(-1))
+
+
+def test_corrupt_body_hash_caught_before_decode(archive_dir):
+    from voom_b200.formats.packed2 import Vpack2Reader
+
+    data = bytearray((archive_dir / "weights.vpack2").read_bytes())
+    data[100] ^= 1
+    (archive_dir / "weights.vpack2").write_bytes(bytes(data))
+    r = Vpack2Reader(archive_dir)
+    with pytest.raises(IOError, match="hash mismatch"):
+        r.fetch(list(r.index))
+
+
+def test_smollm2_scaled_archive(built_lib):
+    from voom_b200 import synthetic
+    from voom_b200.formats import packed
+
+    cfg = dict(synthetic.SMOLLM2_135M, layers=2)
+    heads, bodies, raws = [], [], []
+    for i, (name, shape) in enumerate(synthetic.smollm2_tensors(cfg)):
+        bits = synthetic.bf16_normal(shape, 0.02, 40 + i)
+        h, b = packed.body_for("BF16", bits.view(np.uint8))
+        heads.append({"dtype": "BF16", "shape": list(shape), **h})
+        bodies.append(b)
+        raws.append(bits.view(np.uint8).reshape(-1))
+    offs = np.cumsum([0] + [len(b) for b in bodies[:-1]]).tolist()
+    buf = np.frombuffer(b"".join(bodies), np.uint8)
+    out, spans = packed.decode_bodies(heads, buf, offs, [len(b) for b in bodies])
+    got = out.cpu().numpy()
+    for (d, n), r in zip(spans, raws):
+        assert np.array_equal(got[d:d + n], r)

@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(64) zstd_block_decode(const uint8_t* __restric
   __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t st = sh.st;
-    if (sh.out_size > kBlockMax) st |= VOOM_ZSTD_ST_SIZE;
+    if (sh.out_size > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
     rt->out_size = sh.out_size;
     rt->status = st;
     for (int k = 0; k < 3; k++) {

@@ -412,6 +412,7 @@ void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
       b.frame = frame_index;
       b.huf = kNone;
       b.fse[0] = b.fse[1] = b.fse[2] = kNone;
+      b.max_out = uint32_t(block_max);
       if (type == 0) {
         if (pos + bs > end) { jp.bad = true; return; }
         b.src = pos;

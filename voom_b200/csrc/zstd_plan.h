@@ -44,7 +44,7 @@ struct ZBlock {
   uint32_t nseq;
   uint32_t seq_len;
   uint32_t fse[3];  // LL, OF, ML
-  uint32_t pad;
+  uint32_t max_out;  // largest decoded size a block of this frame may have
 };
 
 struct ZHuf {

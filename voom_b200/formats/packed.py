@@ -1,0 +1,201 @@
+"""vpack: lossless byte-plane compressed weight store (GPU decode).
+
+Same on-disk layout as vOOM's formats/packed.py: one `.vt` file per tensor,
+an 8-byte little-endian header length, a JSON head, then the body.  For
+BF16/F16 the body is `hi_z` (zstd of the odd bytes) followed by `lo` (the even
+bytes, raw); tensors above STREAM_THRESHOLD use the streamed variant (lo raw
+first, then one zstd stream of the hi plane to EOF); other dtypes are stored
+raw.  `pack_model` writes that layout (pack side, host zstd);
+`read_tensor_bytes` and `to_torch` decode on the GPU.
+
+Reference interface replaced: formats/packed.py:63-81 (streamed pack),
+:125-358 (pack_model), :361-379 (read_tensor_bytes), :385-397 (to_mx).
+"""
+
+from __future__ import annotations
+
+import json
+import re
+import struct
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import zstd_host
+from .zstd_gpu import INTERLEAVE, JOB_DTYPE, ZstdBatch, ZstdError, ZstdPlan, describe
+
+PLANE_DTYPES = {"BF16", "F16"}
+STREAM_THRESHOLD = 256 * 1024 * 1024
+CHUNK = 64 * 1024 * 1024
+
+_FUSED_BF16_EXPERT_RE = re.compile(r"^(.*\.mlp\.experts)\.(gate_up_proj|down_proj)$")
+
+TORCH_DTYPES = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32, "I64": torch.int64,
+                "U8": torch.uint8, "I32": torch.int32, "I8": torch.int8, "U32": torch.uint32}
+
+
+def body_for(dtype: str, raw, level: int = 1) -> tuple[dict, bytes]:
+    """(head, body) of one tensor in ordinary vpack form."""
+    a = np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.reshape(-1).view(np.uint8)
+    if dtype in PLANE_DTYPES:
+        hi_z = zstd_host.compress(a[1::2], level)
+        lo = a[0::2].tobytes()
+        return {"hi_z": len(hi_z), "lo": len(lo)}, hi_z + lo
+    return {"raw": a.size}, a.tobytes()
+
+
+def streamed_body(raw, level: int = 1, chunk: int = CHUNK) -> tuple[dict, bytes]:
+    """Streamed variant (formats/packed.py:63-81): lo raw, then the hi zstd stream."""
+    a = np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.reshape(-1).view(np.uint8)
+    comp = zstd_host.ZstdCompressor(level=level)
+    parts = []
+    for s in range(0, a.size, chunk):
+        parts.append(comp.compress(a[s:s + chunk][1::2]))
+    parts.append(comp.flush())
+    return {"lo": a.size // 2, "streamed": True}, a[0::2].tobytes() + b"".join(parts)
+
+
+def write_vt(path: Path, head: dict, body: bytes) -> int:
+    hj = json.dumps(head).encode()
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)) + hj + body)
+    return len(hj) + 8 + len(body)
+
+
+def _iter_safetensors(path: Path):
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        header = json.loads(f.read(n))
+        base = 8 + n
+        for name, meta in header.items():
+            if name == "__metadata__":
+                continue
+            a, b = meta["data_offsets"]
+            f.seek(base + a)
+            yield name, meta, f.read(b - a)
+
+
+def pack_model(model_dir: str | Path, out_dir: str | Path | None = None, level: int = 1) -> Path:
+    """Pack every *.safetensors tensor of model_dir into a vpack directory
+    (formats/packed.py:125-358 layout, including the per-expert split of fused
+    BF16 MoE tensors and the streamed variant above STREAM_THRESHOLD)."""
+    model_dir = Path(model_dir)
+    out = Path(out_dir) if out_dir else model_dir / "weights.vpack"
+    out.mkdir(parents=True, exist_ok=True)
+    manifest: dict[str, str] = {}
+    t0 = time.perf_counter()
+    total_in = total_out = 0
+    for shard in sorted(model_dir.glob("*.safetensors")):
+        for name, meta, raw in _iter_safetensors(shard):
+            fused = _FUSED_BF16_EXPERT_RE.match(name)
+            if fused and len(meta["shape"]) == 3 and meta["shape"][0] > 1 and meta["dtype"] in PLANE_DTYPES:
+                n_e = meta["shape"][0]
+                row = len(raw) // n_e
+                for e in range(n_e):
+                    raw_e = raw[e * row:(e + 1) * row]
+                    if fused.group(2) == "gate_up_proj":
+                        half, inter = row // 2, meta["shape"][1] // 2
+                        parts = (("gate_proj.weight", [inter, meta["shape"][2]], raw_e[:half]),
+                                 ("up_proj.weight", [inter, meta["shape"][2]], raw_e[half:]))
+                    else:
+                        parts = (("down_proj.weight", list(meta["shape"][1:]), raw_e),)
+                    for proj, shape, sub in parts:
+                        sub_name = f"{fused.group(1)}.{e}.{proj}"
+                        head, body = body_for(meta["dtype"], sub, level)
+                        fname = sub_name.replace("/", "__") + ".vt"
+                        total_out += write_vt(out / fname, {"dtype": meta["dtype"], "shape": shape, **head}, body)
+                        manifest[sub_name] = fname
+                total_in += len(raw)
+                continue
+            fname = name.replace("/", "__") + ".vt"
+            if meta["dtype"] in PLANE_DTYPES and len(raw) > STREAM_THRESHOLD:
+                head, body = streamed_body(raw, level)
+            else:
+                head, body = body_for(meta["dtype"], raw, level)
+            total_out += write_vt(out / fname, {"dtype": meta["dtype"], "shape": meta["shape"], **head}, body)
+            manifest[name] = fname
+            total_in += len(raw)
+    (out / "manifest.json").write_text(json.dumps(manifest))
+    dt = time.perf_counter() - t0
+    print(f"packed {total_in / 1e9:.3f}GB -> {total_out / 1e9:.3f}GB "
+          f"({total_in / max(total_out, 1):.3f}x) in {dt:.1f}s")
+    return out
+
+
+def body_job(head: dict, body_off: int, body_len: int, dst: int) -> tuple[np.ndarray | None, int]:
+    """GPU job for one vpack body held at body_off in a source buffer:
+    returns (job record or None for raw bodies, decoded byte count)."""
+    if "raw" in head:
+        return None, int(head["raw"])
+    lo = int(head["lo"])
+    job = np.zeros(1, dtype=JOB_DTYPE)
+    if head.get("streamed"):
+        job[0] = (body_off + lo, body_len - lo, dst, lo, body_off, INTERLEAVE, 0)
+    else:
+        hz = int(head["hi_z"])
+        job[0] = (body_off, hz, dst, lo, body_off + hz, INTERLEAVE, 0)
+    return job, 2 * lo
+
+
+def decode_bodies(heads: list[dict], host_buf: np.ndarray, offsets: list[int], lengths: list[int], *,
+                  device=None, src_dev: torch.Tensor | None = None, align: int = 256,
+                  stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, list[tuple[int, int]]]:
+    """Decode many vpack bodies that sit in one host buffer (and optionally
+    already in `src_dev`) with one batched GPU decode.  Returns the device
+    output buffer and each body's (offset, length) in it."""
+    from .. import _device
+
+    dev = _device.require_cuda(device)
+    jobs, spans, raw_copies = [], [], []
+    dst = 0
+    for head, off, ln in zip(heads, offsets, lengths):
+        job, n = body_job(head, off, ln, dst)
+        if job is None:
+            if ln < n:
+                raise EOFError("vpack raw body shorter than its head")
+            raw_copies.append((off, dst, n))
+        else:
+            if "streamed" not in head and int(head["hi_z"]) + int(head["lo"]) > ln:
+                raise EOFError("vpack body shorter than its head")
+            jobs.append(job)
+        spans.append((dst, n))
+        dst += (n + align - 1) // align * align
+    with torch.cuda.device(dev):
+        if src_dev is None:
+            src_dev = _device.upload(host_buf, dev, stream=stream)
+        out = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
+        for off, d, n in raw_copies:
+            out[d:d + n].copy_(src_dev[off:off + n])
+        if jobs:
+            jarr = np.concatenate(jobs)
+            plan = ZstdPlan(host_buf, jarr)
+            batch = ZstdBatch(plan, dev)
+            batch.run(src_dev, out, stream)
+            st = batch.job_status()
+            if st.any():
+                bad = int(np.nonzero(st)[0][0])
+                raise ZstdError(describe(int(st[bad])))
+    return out, spans
+
+
+def read_tensor_bytes(vpack_dir: str | Path, fname: str, *, device=None) -> tuple[dict, torch.Tensor]:
+    """Read + decode one `.vt` tensor to its original raw bytes on the GPU."""
+    with open(Path(vpack_dir) / fname, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        head = json.loads(f.read(n))
+        body = f.read()
+    buf = np.frombuffer(body, np.uint8)
+    out, spans = decode_bodies([head], buf, [0], [len(body)], device=device)
+    d, ln = spans[0]
+    return head, out[d:d + ln]
+
+
+def to_torch(head: dict, raw: torch.Tensor) -> torch.Tensor:
+    """Decoded bytes -> typed tensor of head['shape'] (formats/packed.py:385-397)."""
+    dt = TORCH_DTYPES[head["dtype"]]
+    return raw.view(dt).reshape(head["shape"])
+
+
+to_mx = to_torch  # the reference's name for the same step

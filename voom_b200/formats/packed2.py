@@ -1,0 +1,306 @@
+"""vpack2: single-file access-ordered archive of vpack bodies (GPU decode).
+
+Same files as vOOM's formats/packed2.py: `weights.vpack2` (bodies back to
+back) + `weights.vpack2.index.json` ({name: {off, len, head, sha}}, sha = the
+first 32 hex digits of SHA-256 of the body), optional `vpack2.CURRENT`
+generation pointer.  `Vpack2Reader.fetch` keeps the reference's contract
+(coalesced runs with RUN_GAP, short-read and hash checks, fail-closed index
+validation, immutable-archive check, `(tensors, seconds, bytes_read)`), but
+every body of the request is decoded in ONE batched GPU decode and the
+tensors are returned on the CUDA device.
+
+Reference interface replaced: formats/packed2.py:42-60, 63-99, 123-175,
+178-191, 194-255, 258-406.
+"""
+
+from __future__ import annotations
+
+import concurrent.futures as cf
+import hashlib
+import json
+import os
+import re
+import struct
+import time
+import warnings
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from .packed import decode_bodies, to_torch
+
+RUN_GAP = 2 * 1024 * 1024
+_COPY_CHUNK = 64 * 1024 * 1024
+
+
+def _pread_exact(fd: int, length: int, offset: int, out: memoryview | None = None) -> bytes | memoryview:
+    """Read one extent completely or raise EOFError (formats/packed2.py:42-60)."""
+    buf = out if out is not None else memoryview(bytearray(length))
+    done = 0
+    while done < length:
+        n = os.preadv(fd, [buf[done:length]], offset + done)
+        if n == 0:
+            raise EOFError(f"unexpected EOF at archive offset {offset + done}; wanted {length - done} more bytes")
+        done += n
+    return buf if out is not None else bytes(buf)
+
+
+def access_order(names: list[str], expert_rank: dict | None = None) -> list[str]:
+    """embed -> layers (non-expert tensors, then experts by id or heat rank) -> rest."""
+
+    def key(n: str):
+        if "embed_tokens" in n:
+            return (0, 0, 0, 0, n)
+        m = re.match(r"(?:model\.layers|model\.language_model\.layers|language_model\.model\.layers)\."
+                     r"(\d+)\.(?:mlp\.experts\.(\d+)\.)?", n)
+        if m:
+            layer = int(m.group(1))
+            if m.group(2) is None:
+                return (1, layer, 0, 0, n)
+            e = int(m.group(2))
+            rank = expert_rank.get((layer, e), 10**9) if expert_rank else e
+            return (1, layer, 1, rank, n)
+        return (2, 0, 0, 0, n)
+
+    return sorted(names, key=key)
+
+
+def build_from_vpack(model_dir: str | Path, expert_rank: dict | None = None) -> Path:
+    """Concatenate a vpack directory's bodies in access order into weights.vpack2."""
+    model_dir = Path(model_dir)
+    vpack = model_dir / "weights.vpack"
+    manifest = json.loads((vpack / "manifest.json").read_text())
+    archive = model_dir / "weights.vpack2"
+    index: dict[str, dict] = {}
+    with open(archive, "wb") as out:
+        for name in access_order(list(manifest), expert_rank):
+            with open(vpack / manifest[name], "rb") as f:
+                n = struct.unpack("<Q", f.read(8))[0]
+                head = json.loads(f.read(n))
+                off = out.tell()
+                h = hashlib.sha256()
+                while True:
+                    chunk = f.read(_COPY_CHUNK)
+                    if not chunk:
+                        break
+                    h.update(chunk)
+                    out.write(chunk)
+                index[name] = {"off": off, "len": out.tell() - off, "head": head, "sha": h.hexdigest()[:32]}
+    (model_dir / "weights.vpack2.index.json").write_text(json.dumps(index))
+    return archive
+
+
+def write_archive(model_dir: str | Path, tensors: list[tuple[str, dict, bytes]]) -> Path:
+    """Write (name, head, body) triples in access order as weights.vpack2 + index."""
+    model_dir = Path(model_dir)
+    model_dir.mkdir(parents=True, exist_ok=True)
+    by_name = {n: (h, b) for n, h, b in tensors}
+    index = {}
+    with open(model_dir / "weights.vpack2", "wb") as out:
+        for name in access_order(list(by_name)):
+            head, body = by_name[name]
+            off = out.tell()
+            out.write(body)
+            index[name] = {"off": off, "len": len(body), "head": head,
+                           "sha": hashlib.sha256(body).hexdigest()[:32]}
+    (model_dir / "weights.vpack2.index.json").write_text(json.dumps(index))
+    return model_dir / "weights.vpack2"
+
+
+def decode_body(head: dict, body, *, device=None) -> torch.Tensor:
+    """vpack body -> original raw bytes as a CUDA uint8 tensor (packed2.py:178-191)."""
+    buf = np.frombuffer(body, np.uint8) if not isinstance(body, np.ndarray) else body.reshape(-1).view(np.uint8)
+    if "raw" in head:
+        from .. import _device
+
+        dev = _device.require_cuda(device)
+        return torch.from_numpy(buf.copy()).to(dev)
+    out, spans = decode_bodies([head], buf, [0], [buf.size], device=device)
+    d, n = spans[0]
+    return out[d:d + n]
+
+
+def resolve_generation(model_dir: Path) -> tuple[Path, Path]:
+    cur = model_dir / "vpack2.CURRENT"
+    if cur.exists():
+        gen = cur.read_text().strip()
+        if not gen or not re.fullmatch(r"[A-Za-z0-9._-]+", gen):
+            raise ValueError(f"invalid vpack2 generation name: {gen!r}")
+        return model_dir / f"weights.{gen}.vpack2", model_dir / f"weights.{gen}.index.json"
+    return model_dir / "weights.vpack2", model_dir / "weights.vpack2.index.json"
+
+
+def verify_generation(model_dir: str | Path, decode: bool = True, paths: tuple[Path, Path] | None = None) -> dict:
+    """Full extent + hash (+ GPU decode) audit of the active generation."""
+    model_dir = Path(model_dir)
+    report = {"tensors": 0, "hashed": 0, "decoded": 0, "errors": []}
+    try:
+        archive, index_path = paths if paths is not None else resolve_generation(model_dir)
+        index = json.loads(index_path.read_text())
+    except Exception as exc:
+        report["errors"].append(f"index unreadable: {exc}")
+        return report
+    if not archive.exists():
+        report["errors"].append(f"archive missing: {archive.name}")
+        return report
+    size = archive.stat().st_size
+    entries = sorted(index.items(), key=lambda kv: kv[1]["off"])
+    report["tensors"] = len(entries)
+    pos = 0
+    for name, e in entries:
+        if e["off"] != pos:
+            report["errors"].append(f"extent gap/overlap at {name}: off {e['off']} != {pos}")
+            pos = e["off"]
+        pos += e["len"]
+    if pos != size:
+        report["errors"].append(f"archive size {size} != indexed extent end {pos}")
+    with open(archive, "rb") as f:
+        for name, e in entries:
+            f.seek(e["off"])
+            body = f.read(e["len"])
+            if len(body) != e["len"]:
+                report["errors"].append(f"short read at {name}")
+                continue
+            if e.get("sha"):
+                report["hashed"] += 1
+                if hashlib.sha256(body).hexdigest()[:32] != e["sha"]:
+                    report["errors"].append(f"hash mismatch at {name}")
+                    continue
+            if decode:
+                try:
+                    decode_body(e["head"], body)
+                    report["decoded"] += 1
+                except Exception as exc:
+                    report["errors"].append(f"decode failure at {name}: {exc}")
+    return report
+
+
+class Vpack2Reader:
+    def __init__(self, model_dir: str | Path, *, require_hashes: bool = False, device=None):
+        model_dir = Path(model_dir)
+        self.archive, index_path = resolve_generation(model_dir)
+        self.index_path = index_path
+        self.index = json.loads(index_path.read_text())
+        self.require_hashes = require_hashes
+        self.device = device
+        self._validate_index()
+        self.unhashed_entries = sum(not e.get("sha") for e in self.index.values())
+        self.integrity_mode = "sha-per-body" if not self.unhashed_entries else "legacy-unhashed"
+        if self.unhashed_entries:
+            warnings.warn(f"vpack2 archive has {self.unhashed_entries}/{len(self.index)} unhashed bodies; "
+                          "readable for compatibility but not a proof artifact", RuntimeWarning, stacklevel=2)
+        st = self.archive.stat()
+        self._archive_identity = (st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns)
+        self.runs_read = 0
+        self.tensors_read = 0
+
+    def _validate_index(self) -> None:
+        size = self.archive.stat().st_size
+        pos = 0
+        for name, entry in sorted(self.index.items(), key=lambda item: item[1].get("off", -1)):
+            off, length = entry.get("off"), entry.get("len")
+            if not isinstance(off, int) or not isinstance(length, int) or length < 0:
+                raise ValueError(f"invalid vpack2 extent for {name}")
+            if off != pos:
+                raise ValueError(f"vpack2 extent gap/overlap at {name}: offset {off}, expected {pos}")
+            if not isinstance(entry.get("head"), dict):
+                raise ValueError(f"missing vpack2 tensor header for {name}")
+            digest = entry.get("sha")
+            if digest is not None and (not isinstance(digest, str) or not re.fullmatch(r"[0-9a-f]{32}", digest)):
+                raise ValueError(f"invalid vpack2 body hash for {name}")
+            if self.require_hashes and digest is None:
+                raise ValueError(f"missing/invalid vpack2 body hash for {name}")
+            pos += length
+        if pos != size:
+            raise ValueError(f"vpack2 archive size {size} != indexed extent end {pos}")
+
+    def _assert_archive_immutable(self) -> None:
+        st = self.archive.stat()
+        if (st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns) != self._archive_identity:
+            raise IOError("vpack2 archive changed after reader initialization")
+
+    def _checked_body(self, name: str, entry: dict, body) -> bytes:
+        expected = entry.get("sha")
+        if expected is None:
+            if self.require_hashes:
+                raise IOError(f"unhashed vpack2 body refused: {name}")
+            return body
+        actual = hashlib.sha256(body).hexdigest()[:32]
+        if actual != expected:
+            raise IOError(f"vpack2 body hash mismatch for {name}: {actual} != {expected}")
+        return body
+
+    def has(self, name: str) -> bool:
+        return name in self.index
+
+    def read_body(self, name: str) -> tuple[dict, bytes]:
+        self._assert_archive_immutable()
+        entry = self.index[name]
+        fd = os.open(self.archive, os.O_RDONLY)
+        try:
+            body = _pread_exact(fd, int(entry["len"]), int(entry["off"]))
+        finally:
+            os.close(fd)
+        return entry["head"], self._checked_body(name, entry, body)
+
+    def fetch(self, names: list[str], parallel: int = 4) -> tuple[dict, float, int]:
+        """Coalesce the request into sequential runs, read + hash them on a host
+        thread pool into one pinned buffer, decode every body in one batched
+        GPU decode.  Returns (name -> CUDA tensor, seconds, bytes read)."""
+        t0 = time.perf_counter()
+        self._assert_archive_immutable()
+        entries = sorted(((self.index[n], n) for n in names), key=lambda e: e[0]["off"])
+        runs: list[tuple[int, int, list]] = []
+        i = 0
+        while i < len(entries):
+            start = entries[i][0]["off"]
+            end = start + entries[i][0]["len"]
+            j = i + 1
+            while j < len(entries) and entries[j][0]["off"] - end <= RUN_GAP:
+                end = max(end, entries[j][0]["off"] + entries[j][0]["len"])
+                j += 1
+            runs.append((start, end, entries[i:j]))
+            i = j
+        total = sum(e - s for s, e, _ in runs)
+        from .. import _device
+
+        host = _device.pinned_empty(max(total, 1))
+        hv = memoryview(host.numpy())
+        run_base, pos = [], 0
+        for s, e, _ in runs:
+            run_base.append(pos)
+            pos += e - s
+        fd = os.open(self.archive, os.O_RDONLY)
+        try:
+            def read_run(k):
+                s, e, ents = runs[k]
+                view = hv[run_base[k]:run_base[k] + (e - s)]
+                _pread_exact(fd, e - s, s, view)
+                for ent, name in ents:
+                    rel = ent["off"] - s
+                    self._checked_body(name, ent, view[rel:rel + ent["len"]])
+                return e - s
+
+            if len(runs) <= 1 or parallel <= 1:
+                sizes = [read_run(k) for k in range(len(runs))]
+            else:
+                with cf.ThreadPoolExecutor(max_workers=min(parallel, len(runs))) as pool:
+                    sizes = list(pool.map(read_run, range(len(runs))))
+        finally:
+            os.close(fd)
+        heads, offs, lens, order = [], [], [], []
+        for k, (s, _e, ents) in enumerate(runs):
+            for ent, name in ents:
+                heads.append(ent["head"])
+                offs.append(run_base[k] + ent["off"] - s)
+                lens.append(ent["len"])
+                order.append(name)
+        out, spans = decode_bodies(heads, host.numpy(), offs, lens, device=self.device)
+        result = {}
+        for name, head, (d, n) in zip(order, heads, spans):
+            result[name] = to_torch(head, out[d:d + n])
+            self.tensors_read += 1
+        self.runs_read += len(runs)
+        torch.cuda.current_stream().synchronize()
+        return result, time.perf_counter() - t0, int(sum(sizes))
