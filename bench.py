@@ -279,7 +279,7 @@ class C2Vpack:
             return False
         got = self.out.cpu().numpy()
         for n, (d, ln) in zip(self.names, self.spans):
-            if not np.array_equal(got[d:d + ln], self.raws[n].view(np.uint8)):
+            if not np.array_equal(got[d:d + ln], self.raws[n].reshape(-1).view(np.uint8)):
                 return False
         return True
 
@@ -299,7 +299,7 @@ class C2Vpack:
         arch = self.archive
         items = list(zip(self.heads, self.offs, self.lens))
         ok = ov.decode_body(items[1][0], arch[items[1][1]:items[1][1] + items[1][2]])
-        assert np.array_equal(ok, self.raws[self.names[1]].view(np.uint8))
+        assert np.array_equal(ok, self.raws[self.names[1]].reshape(-1).view(np.uint8))
         done = 0
         t0 = time.perf_counter()
         with ThreadPoolExecutor(max_workers=threads) as pool:
