@@ -243,6 +243,60 @@ void voom_zstd_plan_destroy(void* plan);
 int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                      uint8_t* d_out, uint32_t* d_status, void* stream);
 
+/* ---------------------------------------------------- fused MoE experts */
+/* One projection (rows x cols BF16, row-major, HF layout) of one expert kept
+ * compressed in HBM as a VRN1 frame with its tile plan and checkpoint index
+ * (device pointers; tile src/dst offsets relative to `src` / the matrix).
+ * The fused kernels need: every tile holding whole rows, `cols` a multiple of
+ * `every`, at most 128 segments of `every` symbols per tile. */
+typedef struct voom_expert_proj {
+  const uint8_t* src;
+  const voom_rans_tile* tiles;
+  const uint32_t* ckpt;
+  const uint32_t* ckpt_base;
+  uint32_t n_tiles;
+  uint32_t every;
+  uint32_t rows;
+  uint32_t cols;
+} voom_expert_proj;
+
+typedef struct voom_expert_pages {
+  voom_expert_proj gate; /* I x H */
+  voom_expert_proj up;   /* I x H */
+  voom_expert_proj down; /* H x I */
+} voom_expert_pages;
+
+/* Scratch bytes voom_moe_layer needs. */
+uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k);
+
+/* One MoE layer for T tokens, entirely on the device: RMSNorm (d_norm_w may
+ * be NULL), router GEMV, fp32 softmax, top-k, optional renormalisation,
+ * fused rANS-decode + SwiGLU GEMV of every routed expert straight from its
+ * compressed pages, route-weighted BF16 accumulation in the reference's order
+ * and the residual add: d_x_out = x + moe(x).  gate_tiles / down_tiles: the
+ * largest tile count of any expert's gate / down frame (grid size).  Bit 0 of
+ * *d_status is set if a page segment misses its checkpoint.
+ * Replaces: runtime/layer_runner.py:347-394 (run_moe_mlp) with
+ * :185-190 (_swiglu) over pages fetched by weight_cache.py:191 get_many. */
+int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                   const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
+                   uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
+                   uint32_t down_tiles, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
+                   void* stream);
+
+/* Fused decode + SwiGLU for experts routed on the host (the
+ * consume_expert_batches path): unique expert u = d_expert_ids[u] (index into
+ * d_pages) takes the tokens d_upair[off_u .. off_u + d_ntok[u]), off_u the sum
+ * of earlier counts (n_rows in total); y row off_u + i (H BF16) receives
+ * expert u's output for its i-th token, unweighted.  d_h: T x H BF16.
+ * Scratch: voom_moe_scratch_bytes(n_rows, H, I, 1) suffices.
+ * Replaces: runtime/expert_batching.py:13-41 consume callback body
+ * (qwen35.py:617-633 / glm.py:466-480 / layer_runner.py:387-393 _swiglu). */
+int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t* d_expert_ids, uint32_t n_unique,
+                       const uint32_t* d_ntok, const uint32_t* d_upair, uint32_t n_rows, uint32_t T,
+                       const uint16_t* d_h, uint32_t H, uint32_t I, uint32_t gate_tiles, uint32_t down_tiles,
+                       uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,102 @@
+"""GPU parity for the fused decode + SwiGLU expert path (through the C ABI)
+against the torch-CPU restatement of the reference's MoE layer math, within
+rel-L2 1e-2 in BF16 (the bar in BASELINE.json)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as om
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def make(E, H, I, std, seed):
+    g = torch.Generator().manual_seed(seed)
+    ex = [tuple((torch.randn(shape, generator=g) * std).to(torch.bfloat16) for shape in ((I, H), (I, H), (H, I)))
+          for _ in range(E)]
+    wr = torch.randn((E, H), generator=g).to(torch.bfloat16)
+    nw = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    return ex, wr, nw
+
+
+@pytest.fixture(scope="module")
+def small(built_lib):
+    from voom_b200.runtime import moe
+
+    E, H, I = 16, 512, 256
+    ex, wr, nw = make(E, H, I, 0.02, 1)
+    store = moe.ExpertStore([tuple(bits(w) for w in e) for e in ex], "cuda:0")
+    return store, ex, wr, nw
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 17])
+def test_layer_matches_oracle(small, T):
+    from voom_b200.runtime import moe
+
+    store, ex, wr, nw = small
+    g = torch.Generator().manual_seed(100 + T)
+    x = torch.randn((T, 512), generator=g).to(torch.bfloat16)
+    layer = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=4, norm_topk=True)
+    got = layer(x.cuda()).cpu()
+    torch.cuda.synchronize()
+    assert int(layer.status.item()) == 0
+    ref = om.moe_layer(x, wr, nw, ex, 4, True)
+    err = om.rel_l2(got - x, ref - x)  # compare the MoE contribution itself
+    assert err < TOL, err
+
+
+def test_grouped_experts_match_swiglu(small):
+    from voom_b200.runtime import moe
+
+    store, ex, _, _ = small
+    g = torch.Generator().manual_seed(7)
+    h = torch.randn((9, 512), generator=g).to(torch.bfloat16)
+    ids = [3, 0, 11]
+    toks = [[0, 4, 8], [1], list(range(9))]
+    y = moe.swiglu_grouped(store, ids, toks, h.cuda()).cpu()
+    row = 0
+    for e, tl in zip(ids, toks):
+        ref = om.swiglu(h[tl], *ex[e])
+        assert om.rel_l2(y[row:row + len(tl)], ref) < TOL
+        row += len(tl)
+
+
+def test_corrupted_page_is_detected(small):
+    from voom_b200.runtime import moe
+
+    store, ex, wr, nw = small
+    gate = store.pages[5][0].page
+    t1 = gate.plan.tiles[1]
+    pos = int(t1["high_freq"]) + 512 + 4 + 200
+    gate.src[pos] ^= 0x5A
+    try:
+        with pytest.raises(ValueError):
+            moe.swiglu_grouped(store, [5], [[0]], torch.zeros((1, 512), dtype=torch.bfloat16, device="cuda"))
+    finally:
+        gate.src[pos] ^= 0x5A
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_config3_layer_full_size(built_lib, T):
+    """H 2048, E 128, I 768, top-8 (config 3), one layer vs the oracle."""
+    from voom_b200.runtime import moe
+
+    E, H, I = 128, 2048, 768
+    ex, wr, nw = make(E, H, I, 0.02, 33)
+    store = moe.ExpertStore([tuple(bits(w) for w in e) for e in ex], "cuda:0")
+    assert store.compressed_bytes < 0.75 * store.raw_bytes
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+    layer = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=8, norm_topk=True)
+    got = layer(x.cuda()).cpu()
+    assert int(layer.status.item()) == 0
+    ref = om.moe_layer(x, wr, nw, ex, 8, True)
+    assert om.rel_l2(got - x, ref - x) < TOL

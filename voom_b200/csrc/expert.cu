@@ -1,0 +1,478 @@
+// Fused MoE expert path on compressed pages: rANS page decode -> SwiGLU GEMV.
+//
+// Reference math (runtime/layer_runner.py run_moe_mlp :347-394, _swiglu
+// :185-190; runtime/quant.py matmul :431-444): per layer
+//   h      = rms_norm(x, w_post_ln)                              (BF16)
+//   logits = h @ Wr.T                                            (BF16 result)
+//   probs  = softmax(fp32(logits)); top-k; optional renormalisation
+//   for each routed expert e (first-appearance order over positions, top-k slots):
+//     g = h_e @ Wg.T, u = h_e @ Wu.T  (BF16 results, fp32 accumulation)
+//     a = bf16(bf16(bf16(sigmoid(g)) * g) * u)
+//     y = a @ Wd.T                                               (BF16)
+//     out[pos] = bf16(out[pos] + bf16(y * w_bf16))
+//   x_out = bf16(x + out)
+//
+// Expert weights stay compressed in HBM as VRN1 frames with a checkpoint
+// index (every 256 symbols).  A CTA takes one tile of a projection (whole
+// rows) for one routed expert; each lane pair decodes one 256-element
+// segment of a row straight into fp32 dot products with the routed tokens'
+// activations (read through L1), so decoded weights never touch HBM.  Every
+// segment must land exactly on its successor checkpoint (integrity of the
+// compressed page; the tile CRC-32 was verified when the index was built).
+// Partial row sums meet in shared memory; the CTA applies the reference's
+// BF16 rounding points.  Kernels: router, route plan, gate/up+activation,
+// down, ordered combine.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "rans_core.cuh"
+
+using namespace voom;
+using namespace voom::rans;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kPairs = kThreads / 2;
+constexpr int kTok = 8;          // tokens per expert pass
+constexpr int kMaxTK = 512;      // T * top_k
+constexpr int kMaxE = 1024;      // experts
+
+struct Routes {
+  uint32_t n_unique;
+  uint32_t T, k, pad;
+  uint32_t expert[kMaxTK];      // unique experts in first-appearance order
+  uint32_t ntok[kMaxTK];        // tokens routed to unique expert u
+  uint32_t uoff[kMaxTK + 1];    // first route row of unique expert u
+  uint32_t upair[kMaxTK];       // [uoff[u] + i] -> token of the i-th route of u
+  uint32_t tok_order[kMaxTK];   // [t*k + j] -> route row, sorted by u per token
+  uint16_t w_bf16[kMaxTK];      // [route row] route weight in BF16
+  uint16_t pad2[kMaxTK];
+  uint32_t idx[kMaxTK];         // [t*k + j] expert
+  float w[kMaxTK];              // [t*k + j] route weight (fp32)
+};
+
+__device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }
+__device__ __forceinline__ uint32_t f2bf(float f) {  // round to nearest even
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7F800000u) == 0x7F800000u) return (u >> 16) | ((u & 0xFFFFu) ? 0x40u : 0u);
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+
+// ------------------------------------------------------------------ router
+// One CTA per token: RMSNorm (optional), logits = h @ Wr.T rounded to BF16,
+// fp32 softmax, top-k (largest first; ties -> lower expert id), optional
+// renormalisation.  Writes h (BF16) for the expert kernels.
+__global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restrict__ x,
+                                                       const uint16_t* __restrict__ norm_w, float eps,
+                                                       const uint16_t* __restrict__ wr, uint32_t E, uint32_t H,
+                                                       uint32_t k, uint32_t norm_topk, uint16_t* __restrict__ h,
+                                                       Routes* routes) {
+  __shared__ float s_red[kThreads / 32];
+  __shared__ float s_p[kMaxE];
+  __shared__ float s_scale;
+  const uint32_t t = blockIdx.x, tid = threadIdx.x;
+  const uint16_t* xt = x + size_t(t) * H;
+  uint16_t* ht = h + size_t(t) * H;
+  float ss = 0.f;
+  for (uint32_t i = tid; i < H; i += kThreads) {
+    const float v = bf2f(xt[i]);
+    ss += v * v;
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
+    s_scale = rsqrtf(tot / float(H) + eps);
+  }
+  __syncthreads();
+  for (uint32_t i = tid; i < H; i += kThreads) {
+    const float v = bf2f(xt[i]);
+    ht[i] = uint16_t(norm_w ? f2bf(v * s_scale * bf2f(norm_w[i])) : xt[i]);
+  }
+  __syncthreads();
+  // logits: one warp per expert row
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  for (uint32_t e = warp; e < E; e += kThreads / 32) {
+    const uint16_t* we = wr + size_t(e) * H;
+    float acc = 0.f;
+    for (uint32_t i = lane; i < H; i += 32) acc += bf2f(ht[i]) * bf2f(we[i]);
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (lane == 0) s_p[e] = rbf(acc);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float mx = -INFINITY;
+    for (uint32_t e = 0; e < E; e++) mx = fmaxf(mx, s_p[e]);
+    float sum = 0.f;
+    for (uint32_t e = 0; e < E; e++) {
+      s_p[e] = __expf(s_p[e] - mx);
+      sum += s_p[e];
+    }
+    float sel = 0.f;
+    uint32_t chosen[64];
+    float pw[64];
+    for (uint32_t j = 0; j < k; j++) {
+      float best = -1.f;
+      uint32_t bi = 0;
+      for (uint32_t e = 0; e < E; e++) {
+        bool used = false;
+        for (uint32_t q = 0; q < j; q++) used |= (chosen[q] == e);
+        if (!used && s_p[e] > best) { best = s_p[e]; bi = e; }
+      }
+      chosen[j] = bi;
+      pw[j] = best / sum;
+      sel += pw[j];
+    }
+    for (uint32_t j = 0; j < k; j++) {
+      routes->idx[t * k + j] = chosen[j];
+      routes->w[t * k + j] = norm_topk ? pw[j] / sel : pw[j];
+    }
+  }
+}
+
+// One thread: unique experts in first-appearance order (positions, then
+// slots), tokens per expert, and each token's contributions ordered by that
+// expert order (the order the reference accumulates them in).
+__global__ void moe_route_plan(Routes* r, uint32_t T, uint32_t k) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  r->T = T;
+  r->k = k;
+  uint32_t nu = 0;
+  for (uint32_t p = 0; p < T * k; p++) {
+    const uint32_t e = r->idx[p];
+    uint32_t u = 0;
+    while (u < nu && r->expert[u] != e) u++;
+    if (u == nu) {
+      r->expert[nu] = e;
+      r->ntok[nu] = 0;
+      nu++;
+    }
+    r->ntok[u]++;
+  }
+  r->n_unique = nu;
+  r->uoff[0] = 0;
+  for (uint32_t u = 0; u < nu; u++) r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
+  uint32_t fill[kMaxTK];
+  for (uint32_t u = 0; u < nu; u++) fill[u] = 0;
+  for (uint32_t p = 0; p < T * k; p++) {
+    uint32_t u = 0;
+    while (r->expert[u] != r->idx[p]) u++;
+    const uint32_t q = r->uoff[u] + fill[u]++;
+    r->upair[q] = p / k;
+    r->w_bf16[q] = uint16_t(f2bf(r->w[p]));
+  }
+  for (uint32_t t = 0; t < T; t++) {
+    uint32_t n = 0;
+    for (uint32_t u = 0; u < nu; u++)
+      for (uint32_t q = r->uoff[u]; q < r->uoff[u + 1]; q++)
+        if (r->upair[q] == t) r->tok_order[t * k + n++] = q;
+  }
+}
+
+// Route rows for experts given by the host: uoff from ntok.
+__global__ void moe_route_offsets(Routes* r, uint32_t n_unique, uint32_t T) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  r->n_unique = n_unique;
+  r->T = T;
+  r->uoff[0] = 0;
+  for (uint32_t u = 0; u < n_unique; u++) r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
+}
+
+// -------------------------------------------------------- fused decode-GEMV
+struct GemvShared {
+  uint32_t lut[2][4096];
+  uint32_t cum[2][257];
+  uint32_t red[8];
+  uint32_t degenerate[2];
+  float acc[2][128][kTok];  // [projection][row in tile][token]
+  uint32_t tok[kTok];
+  uint32_t status;
+};
+
+// 8 BF16 weights (one uint4) times 8 activations at column k of each token.
+__device__ __forceinline__ void dot8(const uint4 w, const uint16_t* __restrict__ act, uint32_t ld,
+                                     const uint32_t* tok, uint32_t ntk, uint32_t k, float* acc) {
+  const float w0 = bf2f(w.x & 0xFFFFu), w1 = __uint_as_float(w.x & 0xFFFF0000u);
+  const float w2 = bf2f(w.y & 0xFFFFu), w3 = __uint_as_float(w.y & 0xFFFF0000u);
+  const float w4 = bf2f(w.z & 0xFFFFu), w5 = __uint_as_float(w.z & 0xFFFF0000u);
+  const float w6 = bf2f(w.w & 0xFFFFu), w7 = __uint_as_float(w.w & 0xFFFF0000u);
+#pragma unroll
+  for (int j = 0; j < kTok; j++) {
+    if (j < int(ntk)) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(act + size_t(tok[j]) * ld + k));
+      float s = acc[j];
+      s = fmaf(w0, bf2f(a.x & 0xFFFFu), s);
+      s = fmaf(w1, __uint_as_float(a.x & 0xFFFF0000u), s);
+      s = fmaf(w2, bf2f(a.y & 0xFFFFu), s);
+      s = fmaf(w3, __uint_as_float(a.y & 0xFFFF0000u), s);
+      s = fmaf(w4, bf2f(a.z & 0xFFFFu), s);
+      s = fmaf(w5, __uint_as_float(a.z & 0xFFFF0000u), s);
+      s = fmaf(w6, bf2f(a.w & 0xFFFFu), s);
+      s = fmaf(w7, __uint_as_float(a.w & 0xFFFF0000u), s);
+      acc[j] = s;
+    }
+  }
+}
+
+// Decodes tile `t` of one projection for the CTA's tokens and adds every
+// row's dot products into sh.acc[slot].  Rows of `cols` elements; each lane
+// pair owns one `every`-element segment.  Returns nothing; errors -> sh.status.
+__device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t, int slot,
+                          const uint16_t* __restrict__ act, uint32_t ld, uint32_t ntk) {
+  const voom_rans_tile tl = P.tiles[t];
+  const uint32_t row_bytes = 2u * P.cols, every = P.every;
+  const uint32_t rows = tl.raw_len / row_bytes;
+  const uint32_t spr = P.cols / every;  // segments per row
+  const uint32_t nseg = rows * spr;
+  const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1;
+  if (tl.mode == 1) {
+    build_lut(sh.lut[0], sh.cum[0], sh.red, &sh.degenerate[0], P.src + tl.low_freq);
+    build_lut(sh.lut[1], sh.cum[1], sh.red, &sh.degenerate[1], P.src + tl.high_freq);
+  }
+  float acc[kTok];
+#pragma unroll
+  for (int j = 0; j < kTok; j++) acc[j] = 0.f;
+  uint32_t row_local = 0;
+  if (p < nseg) {
+    row_local = p / spr;
+    const uint32_t k0 = (p % spr) * every;
+    if (tl.mode == 0) {  // stored tile: weights read directly
+      const uint8_t* wsrc = P.src + tl.src + size_t(p) * every * 2;
+      for (uint32_t c = lane * 8; c < every; c += 16) {
+        uint4 w;
+        uint32_t v[4];
+        for (int q = 0; q < 4; q++)
+          v[q] = uint32_t(wsrc[2 * (c + 2 * q)]) | (uint32_t(wsrc[2 * (c + 2 * q) + 1]) << 8) |
+                 (uint32_t(wsrc[2 * (c + 2 * q) + 2]) << 16) | (uint32_t(wsrc[2 * (c + 2 * q) + 3]) << 24);
+        w = make_uint4(v[0], v[1], v[2], v[3]);
+        dot8(w, act, ld, sh.tok, ntk, k0 + c, acc);
+      }
+    } else {
+      const uint32_t* ck = P.ckpt + P.ckpt_base[t];
+      PlaneRun r;
+      if (p == 0) {
+        plane_start(r, P.src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload, 0, 0,
+                    false);
+      } else {
+        plane_start(r, P.src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
+                    ck[(p - 1) * 4 + lane * 2], ck[(p - 1) * 4 + lane * 2 + 1], true);
+      }
+      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
+      const unsigned mask = 0x3u << (tid & 30u);
+      uint32_t done = 0;
+      for (; done < every; done += 16) {
+        const bool ok = (r.len - r.cur >= 40u) && (r.x >= kRansL);
+        if (!__all_sync(mask, ok)) break;
+        uint32_t a[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const uint32_t s0 = rans_step_fast(lut_s, r);
+          const uint32_t s1 = rans_step_fast(lut_s, r);
+          const uint32_t s2 = rans_step_fast(lut_s, r);
+          const uint32_t s3 = rans_step_fast(lut_s, r);
+          a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+        }
+        const uint4 w = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
+        dot8(w, act, ld, sh.tok, ntk, k0 + done + 8 * lane, acc);
+      }
+      // exact tail in lockstep: both planes have the same count left
+      for (; done < every; done++) {
+        const uint32_t s = rans_step_exact(lut_s, false, r);
+        const uint32_t o = __shfl_xor_sync(mask, s, 1);
+        if (lane == 0) {
+          const float w = bf2f(s | (o << 8));
+          for (uint32_t j = 0; j < ntk; j++) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
+        }
+      }
+      const bool last = (p + 1 == nseg);
+      const bool landed = last ? (r.cur == r.len)
+                               : (r.x == ck[p * 4 + lane * 2] && r.cur == ck[p * 4 + lane * 2 + 1]);
+      if (!landed) atomicOr(&sh.status, 1u);
+    }
+  }
+  // pair reduce, then rows meet in shared memory
+#pragma unroll
+  for (int j = 0; j < kTok; j++) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 1);
+  if (p < nseg && lane == 0)
+    for (uint32_t j = 0; j < ntk; j++) atomicAdd(&sh.acc[slot][row_local][j], acc[j]);
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool setup_tokens(GemvShared& sh, const Routes* R, uint32_t u, uint32_t grp,
+                                             uint32_t* ntk_out) {
+  if (u >= R->n_unique) return false;
+  const uint32_t n = R->ntok[u];
+  if (grp * kTok >= n) return false;
+  const uint32_t ntk = min(uint32_t(kTok), n - grp * kTok);
+  if (threadIdx.x < kTok)
+    sh.tok[threadIdx.x] = threadIdx.x < ntk ? R->upair[R->uoff[u] + grp * kTok + threadIdx.x] : 0;
+  *ntk_out = ntk;
+  return true;
+}
+
+// gate + up tiles of one routed expert -> activation rows (BF16) per token.
+__global__ void __launch_bounds__(kThreads, 1) moe_gate_up(const voom_expert_pages* __restrict__ pages,
+                                                           const Routes* __restrict__ R,
+                                                           const uint16_t* __restrict__ h, uint32_t H, uint32_t I,
+                                                           uint16_t* __restrict__ act_out, uint32_t* status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
+  const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
+  uint32_t ntk;
+  if (!setup_tokens(sh, R, u, grp, &ntk)) return;
+  const voom_expert_pages& E = pages[R->expert[u]];
+  if (t >= E.gate.n_tiles) return;
+  for (int i = threadIdx.x; i < 2 * 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
+  if (threadIdx.x == 0) sh.status = 0;
+  __syncthreads();
+  gemv_tile(sh, E.gate, t, 0, h, H, ntk);
+  gemv_tile(sh, E.up, t, 1, h, H, ntk);
+  const voom_rans_tile tl = E.gate.tiles[t];
+  const uint32_t rows = tl.raw_len / (2u * H), row0 = uint32_t(tl.dst / (2u * H));
+  for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
+    const uint32_t row = q / ntk, j = q % ntk;
+    const float g = rbf(sh.acc[0][row][j]), up = rbf(sh.acc[1][row][j]);
+    const float s = rbf(1.f / (1.f + __expf(-g)));
+    const float a = rbf(rbf(s * g) * up);
+    act_out[size_t(R->uoff[u] + grp * kTok + j) * I + row0 + row] = uint16_t(f2bf(a));
+  }
+  if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
+}
+
+// down tile of one routed expert -> y rows (BF16) per token.
+__global__ void __launch_bounds__(kThreads, 1) moe_down(const voom_expert_pages* __restrict__ pages,
+                                                        const Routes* __restrict__ R,
+                                                        const uint16_t* __restrict__ act, uint32_t H, uint32_t I,
+                                                        uint16_t* __restrict__ y_out, uint32_t* status) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
+  const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
+  uint32_t ntk;
+  if (!setup_tokens(sh, R, u, grp, &ntk)) return;
+  const voom_expert_pages& E = pages[R->expert[u]];
+  if (t >= E.down.n_tiles) return;
+  // the down projection reads this expert's activation rows
+  if (threadIdx.x < kTok) sh.tok[threadIdx.x] = R->uoff[u] + grp * kTok + threadIdx.x;
+  for (int i = threadIdx.x; i < 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
+  if (threadIdx.x == 0) sh.status = 0;
+  __syncthreads();
+  gemv_tile(sh, E.down, t, 0, act, I, ntk);
+  const voom_rans_tile tl = E.down.tiles[t];
+  const uint32_t rows = tl.raw_len / (2u * I), row0 = uint32_t(tl.dst / (2u * I));
+  for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
+    const uint32_t row = q / ntk, j = q % ntk;
+    y_out[size_t(R->uoff[u] + grp * kTok + j) * H + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
+  }
+  if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
+}
+
+// out[t] = ordered BF16 sum of bf16(y * w); x_out = bf16(x + out).
+__global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __restrict__ y,
+                            const uint16_t* __restrict__ x, uint16_t* __restrict__ x_out, uint32_t H,
+                            uint32_t residual) {
+  const uint32_t t = blockIdx.y;
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  const uint32_t k = R->k;
+  float o = 0.f;
+  for (uint32_t j = 0; j < k; j++) {
+    const uint32_t q = R->tok_order[t * k + j];
+    o = rbf(o + rbf(bf2f(y[size_t(q) * H + c]) * bf2f(R->w_bf16[q])));
+  }
+  const float base = residual ? bf2f(x[size_t(t) * H + c]) : 0.f;
+  x_out[size_t(t) * H + c] = uint16_t(f2bf(base + o));
+}
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+struct ScratchLayout {
+  uint64_t routes, h, act, y, total;
+};
+
+ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
+  ScratchLayout s;
+  uint64_t o = 0;
+  s.routes = o; o = align256(o + sizeof(Routes));
+  s.h = o; o = align256(o + uint64_t(T) * H * 2 + 16);
+  s.act = o; o = align256(o + uint64_t(T) * k * I * 2 + 16);
+  s.y = o; o = align256(o + uint64_t(T) * k * H * 2 + 16);
+  s.total = o;
+  return s;
+}
+
+}  // namespace
+
+VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k) {
+  return layout(T, H, I, top_k).total;
+}
+
+VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                            const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
+                            uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
+                            uint32_t down_tiles, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
+                            void* stream) {
+  if (!d_pages || !d_router_w || !d_x || !d_x_out || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+  if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
+      top_k > n_experts || H % 8 || I % 8)
+    return VOOM_E_INVALID_ARG;
+  const ScratchLayout L = layout(T, H, I, top_k);
+  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
+  uint8_t* s = static_cast<uint8_t*>(d_scratch);
+  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
+  uint16_t* h = reinterpret_cast<uint16_t*>(s + L.h);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
+  uint16_t* y = reinterpret_cast<uint16_t*>(s + L.y);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, n_experts, H, top_k, norm_topk, h, R);
+  moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
+  const uint32_t max_unique = min(n_experts, T * top_k);
+  const uint32_t groups = (T + kTok - 1) / kTok;
+  const size_t smem = sizeof(GemvShared);
+  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
+      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return VOOM_E_CUDA;
+  moe_gate_up<<<dim3(gate_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
+  moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
+  moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, 1);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+// Experts given by the host (routing already grouped, e.g. by
+// consume_expert_batches): expert u takes tokens upair[off_u .. off_u +
+// ntok[u]) (off_u = sum of earlier ntok); y row off_u + i receives expert u's
+// output for its i-th token.  No combine.
+VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t* d_expert_ids, uint32_t n_unique,
+                                const uint32_t* d_ntok, const uint32_t* d_upair, uint32_t n_rows, uint32_t T,
+                                const uint16_t* d_h,
+                                uint32_t H, uint32_t I, uint32_t gate_tiles, uint32_t down_tiles, uint16_t* d_y,
+                                void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  if (!d_pages || !d_expert_ids || !d_ntok || !d_upair || !d_h || !d_y || !d_scratch || !d_status)
+    return VOOM_E_INVALID_ARG;
+  if (T == 0 || n_unique == 0 || n_rows == 0 || n_rows > kMaxTK || n_unique > n_rows || H % 8 || I % 8)
+    return VOOM_E_INVALID_ARG;
+  const uint64_t need = align256(sizeof(Routes)) + align256(uint64_t(n_rows) * I * 2 + 16);
+  if (scratch_bytes < need) return VOOM_E_CAPACITY;
+  uint8_t* s = static_cast<uint8_t*>(d_scratch);
+  Routes* R = reinterpret_cast<Routes*>(s);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + align256(sizeof(Routes)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the route header lives in scratch: fill n_unique, T, expert, ntok, upair
+  if (cudaMemcpyAsync(&R->expert[0], d_expert_ids, 4ull * n_unique, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(&R->ntok[0], d_ntok, 4ull * n_unique, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(&R->upair[0], d_upair, 4ull * n_rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return VOOM_E_CUDA;
+  moe_route_offsets<<<1, 32, 0, st>>>(R, n_unique, T);
+  const uint32_t groups = (T + kTok - 1) / kTok;
+  const size_t smem = sizeof(GemvShared);
+  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
+      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return VOOM_E_CUDA;
+  moe_gate_up<<<dim3(gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, d_h, H, I, act, d_status);
+  moe_down<<<dim3(down_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, d_y, d_status);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}

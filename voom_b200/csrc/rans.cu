@@ -26,11 +26,12 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "rans_core.cuh"
 
 namespace voom {
 namespace {
 
-constexpr uint32_t kRansL = 1u << 23;
+using namespace voom::rans;
 constexpr int kThreads = 256;
 constexpr uint32_t kSegsPerChunk = kThreads / 2;
 
@@ -64,119 +65,6 @@ struct SharedPlanes {
   uint32_t degenerate[2];
   uint32_t last;
 };
-
-__device__ __forceinline__ uint32_t ld_u8(const uint8_t* p) { return __ldg(p); }
-__device__ __forceinline__ uint32_t ld_u32_unaligned(const uint8_t* p) {
-  return ld_u8(p) | (ld_u8(p + 1) << 8) | (ld_u8(p + 2) << 16) | (ld_u8(p + 3) << 24);
-}
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-// The 4 bytes at p as a big-endian word (first byte most significant), from
-// two aligned L1-cached loads.  p[0..7] must be readable.
-__device__ __forceinline__ uint32_t load4_be(const uint8_t* p) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-  const uint32_t v = __funnelshift_r(__ldg(w), __ldg(w + 1), uint32_t(a & 3u) * 8u);
-  return __byte_perm(v, 0, 0x0123);
-}
-
-struct PlaneRun {
-  const uint8_t* payload;  // plane payload: u32 initial state, renorm bytes
-  uint32_t x, cur, len;
-};
-
-// One decoded symbol with the reference's exact renormalisation loop
-// `while state < L and cursor < len` (bf16_rans.py:117-127).  Used near the
-// end of a stream, for degenerate tables and for malformed states.
-__device__ __forceinline__ uint32_t rans_step_exact(uint32_t lut_s, bool degenerate, PlaneRun& r) {
-  uint32_t slot = r.x & 4095u, sym = 0;
-  if (degenerate) {
-    r.x = slot;  // all frequencies zero: symbol 0, frequency 0, cumulative 0
-  } else {
-    uint32_t e = lds32(lut_s + 4u * slot);
-    r.x = (((e >> 8) & 4095u) + 1u) * (r.x >> 12) + (e >> 20);
-    sym = e & 0xFFu;
-  }
-  while (r.x < kRansL && r.cur < r.len) {
-    r.x = (r.x << 8) | ld_u8(r.payload + r.cur);
-    r.cur++;
-  }
-  return sym;
-}
-
-// Branch-free symbol step for the bulk of a stream.  Preconditions: x >= L,
-// non-degenerate table, at least 8 payload bytes left.  From x >= 2^23 and
-// freq >= 1 the new state is >= 2^11, so at most two renormalisation bytes
-// are needed: k = (x < 2^23) + (x < 2^15).
-__device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, PlaneRun& r) {
-  const uint32_t be = load4_be(r.payload + r.cur);
-  const uint32_t e = lds32(lut_s + 4u * (r.x & 4095u));
-  const uint32_t xs = r.x >> 12;
-  uint32_t x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
-  const uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
-  r.x = __funnelshift_l(be, x, 8u * k);
-  r.cur += k;
-  return e & 0xFFu;
-}
-
-// Builds the decode table of one plane from its 256 x u16 frequency table.
-// All threads of the block participate.  Sets sh.degenerate[p].
-__device__ __forceinline__ void build_lut(SharedPlanes& sh, int p, const uint8_t* freq) {
-  const int tid = threadIdx.x;
-  const uint32_t f = ld_u8(freq + 2 * tid) | (ld_u8(freq + 2 * tid + 1) << 8);  // kThreads == 256
-  uint32_t v = f;
-  const int lane = tid & 31, warp = tid >> 5;
-  for (int o = 1; o < 32; o <<= 1) {
-    uint32_t n = __shfl_up_sync(0xFFFFFFFFu, v, o);
-    if (lane >= o) v += n;
-  }
-  if (lane == 31) sh.red[warp] = v;
-  __syncthreads();
-  uint32_t base = 0;
-  for (int w = 0; w < warp; w++) base += sh.red[w];
-  sh.cum[p][tid] = base + v - f;
-  if (tid == 255) sh.cum[p][256] = base + v;
-  __syncthreads();
-  const uint32_t total = sh.cum[p][256];
-  if (tid == 0) sh.degenerate[p] = (total == 0);
-  if (total == 4096u) {
-    for (int slot = tid; slot < 4096; slot += kThreads) {
-      // last symbol s with cum[s] <= slot (zero-frequency symbols are skipped)
-      int lo = 0, hi = 256;
-      while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (sh.cum[p][mid] <= uint32_t(slot)) lo = mid; else hi = mid - 1;
-      }
-      uint32_t c = sh.cum[p][lo];
-      uint32_t fs = sh.cum[p][lo + 1] - c;
-      sh.lut[p][slot] = uint32_t(lo) | ((fs - 1u) << 8) | ((uint32_t(slot) - c) << 20);
-    }
-  }
-  __syncthreads();
-}
-
-// Interleaves this lane's 16 symbols (a0..a3) with its partner's into the 32
-// output bytes of the chunk; the low-plane lane writes the first 16 bytes,
-// the high-plane lane the second.  `dst` is 16-byte aligned.
-__device__ __forceinline__ void store_pair16(uint8_t* dst, uint32_t lane, uint32_t a0, uint32_t a1,
-                                             uint32_t a2, uint32_t a3, unsigned mask) {
-  uint32_t s0 = lane ? a0 : a2, s1 = lane ? a1 : a3;
-  uint32_t r0 = __shfl_xor_sync(mask, s0, 1);
-  uint32_t r1 = __shfl_xor_sync(mask, s1, 1);
-  uint32_t lo0 = lane ? r0 : a0, lo1 = lane ? r1 : a1;
-  uint32_t hi0 = lane ? a2 : r0, hi1 = lane ? a3 : r1;
-  uint4 o;
-  o.x = __byte_perm(lo0, hi0, 0x5140);
-  o.y = __byte_perm(lo0, hi0, 0x7362);
-  o.z = __byte_perm(lo1, hi1, 0x5140);
-  o.w = __byte_perm(lo1, hi1, 0x7362);
-  *reinterpret_cast<uint4*>(dst + 16 * lane) = o;
-}
 
 __device__ __forceinline__ void record_ckpt(uint32_t* ckpt, uint32_t done, uint32_t every,
                                             uint32_t limit_k, uint32_t plane, const PlaneRun& r) {
@@ -225,19 +113,10 @@ __device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r
       const uint32_t s3 = rans_step_fast(lut_s, r);
       a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
     }
-    store_pair16(out + 32u * c, lane, a[0], a[1], a[2], a[3], mask);
+    *reinterpret_cast<uint4*>(out + 32u * c + 16u * lane) = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
     if (ckpt) record_ckpt(ckpt, first + 16u * (c + 1), every, limit_k, lane, r);
   }
   return c;
-}
-
-__device__ __forceinline__ void plane_start(PlaneRun& r, const uint8_t* src, uint64_t freq_off,
-                                            uint32_t payload_len, uint32_t x0, uint32_t cur0,
-                                            bool from_ckpt) {
-  r.payload = src + freq_off + 512;
-  r.len = payload_len;
-  r.x = from_ckpt ? x0 : ld_u32_unaligned(r.payload);
-  r.cur = from_ckpt ? cur0 : 4u;
 }
 
 __device__ __forceinline__ void load_crc_tables(SharedPlanes& sh) {
@@ -294,8 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1) rans_cold_kernel(const uint8_t* _
     return;
   }
   const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
-  if (do_low) build_lut(sh, 0, src + tl.low_freq);
-  if (do_high) build_lut(sh, 1, src + tl.high_freq);
+  if (do_low) build_lut(sh.lut[0], sh.cum[0], sh.red, &sh.degenerate[0], src + tl.low_freq);
+  if (do_high) build_lut(sh.lut[1], sh.cum[1], sh.red, &sh.degenerate[1], src + tl.high_freq);
   const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
   uint32_t* ck = ckpt ? ckpt + ckpt_base[blockIdx.x] : nullptr;
   const uint32_t nseg = n_low ? (n_low + every - 1) / every : 1;
@@ -337,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
     return;
   }
   const bool do_low = tl.flags & VOOM_RANS_DO_LOW, do_high = tl.flags & VOOM_RANS_DO_HIGH;
-  if (do_low) build_lut(sh, 0, src + tl.low_freq);
-  if (do_high) build_lut(sh, 1, src + tl.high_freq);
+  if (do_low) build_lut(sh.lut[0], sh.cum[0], sh.red, &sh.degenerate[0], src + tl.low_freq);
+  if (do_high) build_lut(sh.lut[1], sh.cum[1], sh.red, &sh.degenerate[1], src + tl.high_freq);
   const uint32_t n_low = (tl.raw_len + 1) / 2, n_high = tl.raw_len / 2;
   const uint32_t nseg = n_low ? (n_low + every - 1) / every : 1;
   const uint32_t nb = nseg - 1;  // checkpoint boundaries 1..nb

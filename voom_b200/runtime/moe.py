@@ -1,0 +1,145 @@
+"""MoE expert SwiGLU on compressed expert pages (fused rANS decode + GEMV).
+
+Expert projections stay in HBM as VRN1 frames (bf16_rans format) with a
+checkpoint index; every forward decodes them inside the GEMV kernels.
+
+  ExpertStore      - per-expert gate/up/down pages + the device page table.
+  MoeLayer         - one layer on the device: RMSNorm, router, top-k,
+                     fused experts, ordered combine, residual
+                     (runtime/layer_runner.py:347-394 run_moe_mlp).
+  swiglu_grouped   - experts chosen on the host (consume_expert_batches path,
+                     runtime/expert_batching.py:13-41).
+
+Reference interface replaced: runtime/layer_runner.py:185-190, 347-394;
+runtime/qwen35.py:584-638 (route + consume); runtime/quant.py:431-444.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from .. import _device
+from .._lib import check, load
+from ..formats import bf16_rans
+
+EVERY = 256
+PROJ_DTYPE = np.dtype([("src", "<u8"), ("tiles", "<u8"), ("ckpt", "<u8"), ("ckpt_base", "<u8"),
+                       ("n_tiles", "<u4"), ("every", "<u4"), ("rows", "<u4"), ("cols", "<u4")])
+PAGES_DTYPE = np.dtype([("gate", PROJ_DTYPE), ("up", PROJ_DTYPE), ("down", PROJ_DTYPE)])
+assert PAGES_DTYPE.itemsize == 144
+
+
+def tile_bytes_for(cols: int, every: int = EVERY, max_tile: int = 1 << 16) -> int:
+    """Tile size for a projection with rows of `cols` BF16: whole rows, at most
+    128 checkpoint segments and at most `max_tile` bytes per tile."""
+    if cols % every:
+        raise ValueError(f"row length {cols} is not a multiple of the checkpoint interval {every}")
+    row_bytes = 2 * cols
+    rows = max(1, min(128 // (cols // every), max_tile // row_bytes))
+    return rows * row_bytes
+
+
+class ProjPage:
+    """One expert projection as a resident compressed page."""
+
+    def __init__(self, w_bits: np.ndarray, device, every: int = EVERY, frame: bytes | None = None):
+        rows, cols = w_bits.shape
+        self.rows, self.cols = int(rows), int(cols)
+        if frame is None:
+            frame, _ = bf16_rans.encode(np.ascontiguousarray(w_bits).view(np.uint8),
+                                        tile_bytes=tile_bytes_for(cols, every))
+        self.page = bf16_rans.RansPage(frame, device=device, every=every)
+        self.frame_bytes = len(frame)
+
+    def record(self) -> tuple:
+        p = self.page
+        return (p.src.data_ptr(), p.tiles.data_ptr(), p.ckpt.data_ptr(), p.ckpt_base.data_ptr(), p.n_tiles,
+                p.every, self.rows, self.cols)
+
+
+class ExpertStore:
+    """Compressed gate/up/down pages of E experts and their device page table."""
+
+    def __init__(self, experts: list[tuple[np.ndarray, np.ndarray, np.ndarray]], device, every: int = EVERY):
+        self.device = _device.require_cuda(device)
+        self.pages = [(ProjPage(g, self.device, every), ProjPage(u, self.device, every),
+                       ProjPage(d, self.device, every)) for g, u, d in experts]
+        self.I, self.H = experts[0][0].shape
+        tab = np.zeros(len(self.pages), dtype=PAGES_DTYPE)
+        for i, (g, u, d) in enumerate(self.pages):
+            tab[i] = (g.record(), u.record(), d.record())
+        self.table = _device.tensor_from_numpy(tab, self.device)
+        self.gate_tiles = max(g.page.n_tiles for g, _, _ in self.pages)
+        self.down_tiles = max(d.page.n_tiles for _, _, d in self.pages)
+        self.compressed_bytes = sum(p.frame_bytes for t in self.pages for p in t)
+        self.raw_bytes = sum(2 * p.rows * p.cols for t in self.pages for p in t)
+
+    def __len__(self) -> int:
+        return len(self.pages)
+
+
+class MoeLayer:
+    """Device-side MoE layer (routing on the GPU, no host synchronisation)."""
+
+    def __init__(self, store: ExpertStore, router_w: torch.Tensor, norm_w: torch.Tensor | None, *,
+                 top_k: int, norm_topk: bool = True, eps: float = 1e-6):
+        self.store = store
+        self.router_w = router_w.contiguous()
+        self.norm_w = None if norm_w is None else norm_w.contiguous()
+        self.top_k = int(top_k)
+        self.norm_topk = bool(norm_topk)
+        self.eps = float(eps)
+        self._scratch: dict[int, torch.Tensor] = {}
+        self.status = torch.zeros(1, dtype=torch.int32, device=store.device)
+
+    def scratch(self, T: int) -> torch.Tensor:
+        if T not in self._scratch:
+            n = load().voom_moe_scratch_bytes(T, self.store.H, self.store.I, self.top_k)
+            self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=self.store.device)
+        return self._scratch[T]
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """x: (T, H) BF16 on the device -> x + moe(x) (T, H) BF16."""
+        T, H = x.shape
+        x = x.contiguous()
+        out = torch.empty_like(x) if out is None else out
+        s = self.scratch(T)
+        st = self.store
+        check(load().voom_moe_layer(st.table.data_ptr(), len(st), self.router_w.data_ptr(),
+                                    None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                    x.data_ptr(), out.data_ptr(), T, H, st.I, self.top_k, int(self.norm_topk),
+                                    st.gate_tiles, st.down_tiles, s.data_ptr(), s.numel(), self.status.data_ptr(),
+                                    _device.stream_ptr(st.device, stream)), "voom_moe_layer")
+        return out
+
+    __call__ = forward
+
+
+def swiglu_grouped(store: ExpertStore, expert_ids: list[int], token_lists: list[list[int]], h: torch.Tensor,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Experts grouped on the host: returns y (sum(len(tokens)), H) BF16, rows in
+    (expert, token) order, unweighted -- what `_swiglu(h[:, pos], experts[e])`
+    yields for each expert of a consume_expert_batches batch."""
+    dev = store.device
+    ntok = np.array([len(t) for t in token_lists], dtype=np.uint32)
+    upair = np.concatenate([np.asarray(t, dtype=np.uint32) for t in token_lists])
+    n_rows = int(upair.size)
+    T = int(h.shape[0])
+    d_ids = _device.tensor_from_numpy(np.asarray(expert_ids, dtype=np.uint32), dev)
+    d_ntok = _device.tensor_from_numpy(ntok, dev)
+    d_upair = _device.tensor_from_numpy(upair, dev)
+    y = torch.empty((n_rows, store.H), dtype=torch.bfloat16, device=dev)
+    need = int(load().voom_moe_scratch_bytes(n_rows, store.H, store.I, 1))
+    scratch = torch.empty(need, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(load().voom_expert_swiglu(store.table.data_ptr(), d_ids.data_ptr(), len(expert_ids), d_ntok.data_ptr(),
+                                    d_upair.data_ptr(), n_rows, T, h.contiguous().data_ptr(), store.H, store.I,
+                                    store.gate_tiles, store.down_tiles, y.data_ptr(), scratch.data_ptr(), need,
+                                    status.data_ptr(), _device.stream_ptr(dev, stream)), "voom_expert_swiglu")
+    if int(status.item()):
+        raise ValueError("compressed expert page failed its checkpoint verification")
+    return y
