@@ -273,7 +273,8 @@ uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top
  * be NULL), router GEMV, fp32 softmax, top-k, optional renormalisation,
  * fused rANS-decode + SwiGLU GEMV of every routed expert straight from its
  * compressed pages, route-weighted BF16 accumulation in the reference's order
- * and the residual add: d_x_out = x + moe(x).  gate_tiles / down_tiles: the
+ * and the residual add: d_x_out = x + moe(x) (residual = 1) or moe(x)
+ * (residual = 0).  gate_tiles / down_tiles: the
  * largest tile count of any expert's gate / down frame (grid size).  Bit 0 of
  * *d_status is set if a page segment misses its checkpoint.
  * Replaces: runtime/layer_runner.py:347-394 (run_moe_mlp) with
@@ -281,8 +282,8 @@ uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top
 int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
                    const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
                    uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
-                   uint32_t down_tiles, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
-                   void* stream);
+                   uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
+                   uint32_t* d_status, void* stream);
 
 /* Fused decode + SwiGLU for experts routed on the host (the
  * consume_expert_batches path): unique expert u = d_expert_ids[u] (index into

@@ -47,8 +47,8 @@ def swiglu(h: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor
 
 
 def moe_layer(x: torch.Tensor, wr: torch.Tensor, norm_w: torch.Tensor | None, experts, k: int,
-              norm_topk: bool = True, eps: float = 1e-6) -> torch.Tensor:
-    """x: (T, H) BF16; experts[e] = (Wg, Wu, Wd) BF16.  Returns x + moe(x)."""
+              norm_topk: bool = True, eps: float = 1e-6, residual: bool = True) -> torch.Tensor:
+    """x: (T, H) BF16; experts[e] = (Wg, Wu, Wd) BF16.  Returns x + moe(x) (or moe(x))."""
     h = rms_norm(x, norm_w, eps)
     idx, pw = route(h, wr, k, norm_topk)
     groups: dict[int, list[tuple[int, float]]] = {}
@@ -62,7 +62,7 @@ def moe_layer(x: torch.Tensor, wr: torch.Tensor, norm_w: torch.Tensor | None, ex
         y = swiglu(h[positions], *experts[e])
         contrib = (y.float() * w.float()[:, None]).to(bf16)
         out[positions] = (out[positions].float() + contrib.float()).to(bf16)
-    return (x.float() + out.float()).to(bf16)
+    return (x.float() + out.float()).to(bf16) if residual else out
 
 
 def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:

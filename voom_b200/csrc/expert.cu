@@ -414,8 +414,8 @@ VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uin
 VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
                             const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
                             uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
-                            uint32_t down_tiles, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status,
-                            void* stream) {
+                            uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
+                            uint32_t* d_status, void* stream) {
   if (!d_pages || !d_router_w || !d_x || !d_x_out || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
   if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
       top_k > n_experts || H % 8 || I % 8)
@@ -438,7 +438,7 @@ VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts
     return VOOM_E_CUDA;
   moe_gate_up<<<dim3(gate_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
   moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
-  moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, 1);
+  moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
 

@@ -102,8 +102,8 @@ class MoeLayer:
         return self._scratch[T]
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None,
-                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-        """x: (T, H) BF16 on the device -> x + moe(x) (T, H) BF16."""
+                stream: torch.cuda.Stream | None = None, residual: bool = True) -> torch.Tensor:
+        """x: (T, H) BF16 on the device -> x + moe(x) (or moe(x)), (T, H) BF16."""
         T, H = x.shape
         x = x.contiguous()
         out = torch.empty_like(x) if out is None else out
@@ -112,7 +112,8 @@ class MoeLayer:
         check(load().voom_moe_layer(st.table.data_ptr(), len(st), self.router_w.data_ptr(),
                                     None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
                                     x.data_ptr(), out.data_ptr(), T, H, st.I, self.top_k, int(self.norm_topk),
-                                    st.gate_tiles, st.down_tiles, s.data_ptr(), s.numel(), self.status.data_ptr(),
+                                    st.gate_tiles, st.down_tiles, int(residual), s.data_ptr(), s.numel(),
+                                    self.status.data_ptr(),
                                     _device.stream_ptr(st.device, stream)), "voom_moe_layer")
         return out
 
