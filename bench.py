@@ -112,6 +112,7 @@ class C1Rans:
     cold decode of the frame (64 independent plane streams)."""
 
     name = "c1_rans_4096x4096"
+    data = "synthetic (seeded numpy): BF16 N(0, 0.02), 0.1% of columns x50"
     metric = "BF16 weight-page decode GB/s (bit-exact)"
     unit = "GB/s"
     dtype = "u8"
@@ -213,11 +214,12 @@ class C2Vpack:
     decode."""
 
     name = "c2_vpack2_smollm2_135m"
+    data = "synthetic (seeded numpy): random-init SmolLM2-135M shapes, every tensor BF16 N(0, 0.02)"
     metric = "BF16 weight-page decode GB/s (bit-exact)"
     unit = "GB/s"
     dtype = "u8"
 
-    def __init__(self, device, rank: int):
+    def __init__(self, device, rank: int, layers: int = 30):
         import torch
         from concurrent.futures import ThreadPoolExecutor
 
@@ -227,7 +229,9 @@ class C2Vpack:
         self.torch = torch
         self.dev = device
         self.packed = packed
-        specs = synthetic.smollm2_tensors()
+        specs = synthetic.smollm2_tensors(dict(synthetic.SMOLLM2_135M, layers=layers))
+        if layers != 30:
+            self.name = f"c2_vpack2_smollm2_135m_{layers}layers"
         import zlib
 
         def make(spec):
@@ -319,7 +323,139 @@ class C2Vpack:
                 "l2": "flushed between steps (512 MiB write); inputs 184 MB + output 269 MB exceed L2"}
 
 
-WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack}
+class C3Moe:
+    """Config 3: MoE expert streaming decode step -- hidden 2048, 128 experts
+    with SwiGLU gate/up 2048->768 and down 768->2048 (BF16 N(0, 0.02)) kept as
+    rANS-coded pages in HBM, top-8 softmax routing from a random router, 48
+    layers, fused decode + GEMV.  A step runs all 48 layers for T tokens
+    (`--tokens`, 1 or 8); the metric is tokens per second.  The 48 layers
+    share one set of 128 experts' pages (each layer has its own router), so
+    the per-layer decode work is the configuration's while the page set is
+    128 x 9 MiB instead of 48 x 128 x 9 MiB."""
+
+    metric = "fused expert GEMV tok/s (48-layer MoE decode step)"
+    data = "synthetic (seeded torch): experts BF16 N(0, 0.02), router N(0, 1), tokens N(0, 1)"
+    unit = "tok/s"
+    dtype = "bf16"
+
+    def __init__(self, device, rank: int, tokens: int = 1, layers: int = 48):
+        import torch
+
+        from voom_b200.runtime import moe
+
+        self.torch = torch
+        self.dev = device
+        self.T = tokens
+        self.L = layers
+        self.name = f"c3_moe_h2048_e128_i768_top8_T{tokens}_L{layers}"
+        E, H, I = 128, 2048, 768
+        g = torch.Generator().manual_seed(4242 + rank)
+
+        def bits(t):
+            return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+        experts = []
+        for _ in range(E):
+            experts.append(tuple(bits((torch.randn(sh, generator=g) * 0.02).to(torch.bfloat16))
+                                 for sh in ((I, H), (I, H), (H, I))))
+        self.store = moe.ExpertStore(experts, device)
+        self.layers = []
+        for _ in range(layers):
+            wr = torch.randn((E, H), generator=g).to(torch.bfloat16).to(device)
+            self.layers.append(moe.MoeLayer(self.store, wr, None, top_k=8, norm_topk=True))
+        self.x0 = torch.randn((tokens, H), generator=g).to(torch.bfloat16).to(device)
+        self.bufs = [torch.empty_like(self.x0) for _ in range(2)]
+        self.x_host = torch.randn((tokens, H), generator=g).to(torch.bfloat16).pin_memory()
+        self.y_host = torch.empty((tokens, H), dtype=torch.bfloat16).pin_memory()
+        self.units_per_step = tokens
+        per_expert = self.store.compressed_bytes / E
+        self.routed = None
+        self.per_expert_bytes = per_expert
+        self.algo_bytes = None  # set after a routing pass (distinct experts per layer)
+        self.launches_per_step = 5 * layers
+        self.experts_raw = experts
+
+    def _run(self, x, stream):
+        a, b = self.bufs
+        cur = x
+        for i, layer in enumerate(self.layers):
+            out = a if i % 2 == 0 else b
+            layer(cur, out=out, stream=stream)
+            cur = out
+        return cur
+
+    def step_device(self, stream_ptr: int):
+        self._run(self.x0, self.torch.cuda.current_stream(self.dev))
+        if self.algo_bytes is None:
+            self.torch.cuda.synchronize()
+            # distinct routed experts per layer from the route tables (T*k <= 64)
+            import ctypes
+            n = 0
+            for layer in self.layers:
+                n += int(layer.scratch(self.T)[:4].view(self.torch.int32).item())
+            self.distinct = n
+            self.algo_bytes = int(n * self.per_expert_bytes + 2 * 2 * self.T * 2048 * self.L)
+
+    def verify(self) -> bool:
+        from oracle import moe as om
+
+        torch = self.torch
+        layer = self.layers[0]
+        out = layer(self.x0, residual=False).cpu()
+        ex = [tuple(torch.from_numpy(w.view(np.int16)).view(torch.bfloat16) for w in e) for e in self.experts_raw]
+        ref = om.moe_layer(self.x0.cpu(), layer.router_w.cpu(), None, ex, 8, True, residual=False)
+        ok = om.rel_l2(out, ref) < 1e-2 and all(int(l.status.item()) == 0 for l in self.layers)
+        return ok
+
+    def step_e2e(self):
+        x = self.x_host.to(self.dev, non_blocking=True)
+        y = self._run(x, self.torch.cuda.current_stream(self.dev))
+        self.y_host.copy_(y, non_blocking=True)
+        return self.T * 2048 * 2, self.T * 2048 * 2
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        """The reference's layer math restated in torch-CPU with rANS page
+        decode by the C oracle (one layer per sample unit)."""
+        from oracle import moe as om
+        from oracle import rans as orans
+
+        torch = self.torch
+        torch.set_num_threads(threads)
+        layer = self.layers[0]
+        wr = layer.router_w.cpu()
+        x = self.x0.cpu()
+        frames = [[bytes(p.page.src[: p.frame_bytes].cpu().numpy()) for p in trip] for trip in self.store.pages]
+        done = 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or done == 0:
+            h = x
+            idx, _ = om.route(h, wr, 8, True)
+            needed = sorted({int(e) for e in idx.flatten()})
+            ex = {}
+            for e in needed:  # decode the routed experts' pages (the reference decodes on fetch)
+                ws = []
+                for fr, (rows, cols) in zip(frames[e], ((768, 2048), (768, 2048), (2048, 768))):
+                    raw = np.frombuffer(orans.decode(fr), np.int16).reshape(rows, cols)
+                    ws.append(torch.from_numpy(raw.copy()).view(torch.bfloat16))
+                ex[e] = tuple(ws)
+            om.moe_layer(h, wr, None, ex, 8, True)
+            done += 1
+        dt = time.perf_counter() - t0
+        tok_s = self.T / (dt / done * self.L)
+        return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"{done} layer(s) of T={self.T}: C-oracle rANS decode of the routed experts + torch-CPU "
+                          f"layer math on {threads} thread(s), {dt:.1f} s, scaled to {self.L} layers"}
+
+    def config(self) -> dict:
+        return {"workload": self.name, "tokens": self.T, "layers": self.L, "experts": 128, "hidden": 2048,
+                "intermediate": 768, "top_k": 8, "page_bytes_compressed": int(self.store.compressed_bytes),
+                "page_bytes_raw": int(self.store.raw_bytes),
+                "ratio": round(self.store.raw_bytes / self.store.compressed_bytes, 4),
+                "distinct_experts_per_step": getattr(self, "distinct", None),
+                "l2": "flushed between steps (512 MiB write); 128 experts' pages (~770 MB) exceed L2"}
+
+
+WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe}
 DEFAULT_WORKLOAD = "c2_vpack"
 
 
@@ -348,9 +484,8 @@ def run_reference(args, world, rank):
 
     threads = os.cpu_count() or 1
     wl = WORKLOADS[args.workload]
-    # build the workload's inputs on the host only
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    w = wl(dev, 0)
+    w = wl(dev, 0, tokens=args.tokens) if wl is C3Moe else wl(dev, 0)
     times = []
     vals = []
     for i in range(args.warmup + args.steps):
@@ -362,7 +497,7 @@ def run_reference(args, world, rank):
     line = {
         "metric": w.metric, "value": v, "unit": w.unit, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": statistics.median(times), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": "synthetic (seeded)",
+        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": w.data,
         "config": w.config(), "impl": "reference",
         "cpu_baseline": {"value": v, "unit": w.unit, "cores": threads, "kind": "port",
                          "sample": r["sample"]},
@@ -380,6 +515,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--ref-seconds", type=float, default=4.0)
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
+    ap.add_argument("--tokens", type=int, default=1, help="c3_moe: tokens per step (1 or 8)")
+    ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
     args = ap.parse_args()
 
     import torch
@@ -393,7 +530,13 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     peaks, peaks_kind = load_peaks()
-    w = WORKLOADS[args.workload](dev, rank)
+    wl = WORKLOADS[args.workload]
+    if wl is C3Moe:
+        w = wl(dev, rank, tokens=args.tokens)
+    elif wl is C2Vpack:
+        w = wl(dev, rank, layers=args.c2_layers)
+    else:
+        w = wl(dev, rank)
     stream = torch.cuda.current_stream(dev)
     sptr = int(stream.cuda_stream)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
@@ -453,6 +596,9 @@ def main():
 
     extra = w.extra(stream, args.steps, flush) if hasattr(w, "extra") else {}
     achieved = w.algo_bytes / (ms * 1e-3) / 1e9
+    if w.unit != "GB/s":
+        value = w.units_per_step * world / (ms * 1e-3)
+        e2e_value = w.units_per_step * world / (e2e_ms * 1e-3)
     roof = {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": getattr(w, "traffic", None),
             "peak_kind": f"{peaks_kind} (hbm_gbs)"}
@@ -464,7 +610,7 @@ def main():
             "metric": w.metric, "value": round(value, 4), "unit": w.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
-            "data": "synthetic (seeded numpy; BF16 N(0,0.02) with 0.1% outlier columns)",
+            "data": w.data,
             "config": dict(w.config(), parallelism=f"replicas x{world}" if world > 1 else "single"),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 4), "unit": w.unit, "h2d_bytes_per_step": bi,

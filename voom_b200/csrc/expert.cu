@@ -411,7 +411,7 @@ VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uin
   return layout(T, H, I, top_k).total;
 }
 
-VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
                             const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
                             uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
                             uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
@@ -440,6 +440,15 @@ VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts
   moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                            const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
+                            uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
+                            uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
+                            uint32_t* d_status, void* stream) {
+  return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
+                        gate_tiles, down_tiles, residual, d_scratch, scratch_bytes, d_status, stream);
 }
 
 // Experts given by the host (routing already grouped, e.g. by

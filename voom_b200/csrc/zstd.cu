@@ -257,6 +257,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
     r.ensure(26);
     uint32_t sll = r.read(sh.al[0]), sof = r.read(sh.al[1]), sml = r.read(sh.al[2]);
     ZSeq* out = v.seq + b.seq_off;
+    uint32_t dst = 0;
     for (uint32_t i = 0; i < b.nseq; i++) {
       const uint32_t eLL = sh.ll[sll], eOF = sh.of[sof], eML = sh.ml[sml];
       const uint32_t ofc = eOF & 0xFFu, mlc = eML & 0xFFu, llc = eLL & 0xFFu;
@@ -265,38 +266,45 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       r.ensure(32);
       const uint32_t ml = c_ml_base[mlc] + r.read(c_ml_bits[mlc]);
       const uint32_t ll = c_ll_base[llc] + r.read(c_ll_bits[llc]);
+      // repeat-offset rules (RFC 8878 3.1.2.5) on symbolic slots
+      uint32_t ok, ov;
+      if (ofv > 3) {
+        ok = 3;
+        ov = ofv - 3;
+        rk[2] = rk[1]; rv[2] = rv[1];
+        rk[1] = rk[0]; rv[1] = rv[0];
+        rk[0] = ok; rv[0] = ov;
+      } else {
+        const uint32_t idx = ofv - 1 + (ll == 0);
+        if (idx == 0) {
+          ok = rk[0]; ov = rv[0];
+        } else if (idx == 1) {
+          ok = rk[1]; ov = rv[1];
+          rk[1] = rk[0]; rv[1] = rv[0];
+          rk[0] = ok; rv[0] = ov;
+        } else if (idx == 2) {
+          ok = rk[2]; ov = rv[2];
+          rk[2] = rk[1]; rv[2] = rv[1];
+          rk[1] = rk[0]; rv[1] = rv[0];
+          rk[0] = ok; rv[0] = ov;
+        } else {
+          ok = rk[0]; ov = rk[0] == 3 ? rv[0] - 1 : rv[0] + 1;
+          rk[2] = rk[1]; rv[2] = rv[1];
+          rk[1] = rk[0]; rv[1] = rv[0];
+          rk[0] = ok; rv[0] = ov;
+        }
+      }
       ZSeq s;
       s.ll = ll;
       s.ml = ml;
-      s.ofv = ofv;
-      s.dst = 0;
-      s.lit = 0;
-      s.pad = 0;
+      s.oval = ov;
+      s.okind = ok;
+      s.dst = dst;
+      s.lit = sum_ll;
       out[i] = s;
+      dst += ll + ml;
       sum_ml += ml;
       sum_ll += ll;
-      if (ofv > 3) {
-        rk[2] = rk[1]; rv[2] = rv[1];
-        rk[1] = rk[0]; rv[1] = rv[0];
-        rk[0] = 3; rv[0] = ofv - 3;
-      } else {
-        const uint32_t idx = ofv - 1 + (ll == 0);
-        if (idx == 1) {
-          uint32_t tk = rk[0], tv = rv[0];
-          rk[0] = rk[1]; rv[0] = rv[1];
-          rk[1] = tk; rv[1] = tv;
-        } else if (idx == 2) {
-          uint32_t tk = rk[2], tv = rv[2];
-          rk[2] = rk[1]; rv[2] = rv[1];
-          rk[1] = rk[0]; rv[1] = rv[0];
-          rk[0] = tk; rv[0] = tv;
-        } else if (idx == 3) {
-          uint32_t tk = rk[0], tv = rk[0] == 3 ? rv[0] - 1 : rv[0] + 1;
-          rk[2] = rk[1]; rv[2] = rv[1];
-          rk[1] = rk[0]; rv[1] = rv[0];
-          rk[0] = tk; rv[0] = tv;
-        }
-      }
       if (i + 1 < b.nseq) {
         r.ensure(26);
         sll = (eLL >> 16) + r.read(int((eLL >> 8) & 0xFFu));
@@ -404,53 +412,29 @@ __global__ void __launch_bounds__(128) zstd_block_execute(const uint8_t* __restr
     return;
   }
   if (rt.status) return;  // the job already failed in K1
-  ZSeq* seq = v.seq + b.seq_off;
+  const ZSeq* seq = v.seq + b.seq_off;
   const uint8_t* lit = v.lit + b.lit_off;
-  if (threadIdx.x == 0) {
-    uint32_t rep[3] = {rt.init_rep[0], rt.init_rep[1], rt.init_rep[2]};
-    const uint64_t before = rt.zstart - rt.frame_zstart;
-    uint32_t pos = 0, litp = 0, st = 0;
-    for (uint32_t i = 0; i < b.nseq; i++) {
-      ZSeq s = seq[i];
-      uint32_t off;
-      if (s.ofv > 3) {
-        off = s.ofv - 3;
-        rep[2] = rep[1];
-        rep[1] = rep[0];
-        rep[0] = off;
-      } else {
-        const uint32_t idx = s.ofv - 1 + (s.ll == 0);
-        if (idx == 0) {
-          off = rep[0];
-        } else {
-          off = idx == 3 ? rep[0] - 1 : rep[idx];
-          if (idx != 1) rep[2] = rep[1];
-          rep[1] = rep[0];
-          rep[0] = off;
-        }
-      }
-      if (off == 0 || uint64_t(off) > before + pos + s.ll) {
-        st = VOOM_ZSTD_ST_OFFSET;
-        off = 0;
-      }
-      s.ofv = off;
-      s.dst = pos;
-      s.lit = litp;
-      seq[i] = s;
-      pos += s.ll + s.ml;
-      litp += s.ll;
-    }
-    s_end[0] = pos;
-    s_end[1] = litp;
-    if (st) atomicOr(status + b.job, st);
-  }
-  __syncthreads();
+  const uint64_t before = rt.zstart - rt.frame_zstart;
+  uint32_t bad = 0;
   for (uint32_t i = threadIdx.x; i < b.nseq; i += blockDim.x) {
     const ZSeq s = seq[i];
+    const uint32_t off = s.okind == 3 ? s.oval : rt.init_rep[s.okind] - s.oval;
+    const bool ok = off != 0 && uint64_t(off) <= before + s.dst + s.ll;
+    bad |= !ok;
     for (uint32_t k = 0; k < s.ll; k++) res[s.dst + k] = kResolved | lit[s.lit + k];
     const uint64_t m = rt.zstart + s.dst + s.ll;
-    for (uint32_t k = 0; k < s.ml; k++) res[s.dst + s.ll + k] = s.ofv ? uint32_t(m + k - s.ofv) : kResolved;
+    for (uint32_t k = 0; k < s.ml; k++) res[s.dst + s.ll + k] = ok ? uint32_t(m + k - off) : kResolved;
+    if (i + 1 == b.nseq && threadIdx.x == (b.nseq - 1) % blockDim.x) {
+      s_end[0] = s.dst + s.ll + s.ml;
+      s_end[1] = s.lit + s.ll;
+    }
   }
+  if (threadIdx.x == 0 && b.nseq == 0) {
+    s_end[0] = 0;
+    s_end[1] = 0;
+  }
+  if (bad) atomicOr(status + b.job, VOOM_ZSTD_ST_OFFSET);
+  __syncthreads();
   const uint32_t pos = s_end[0], litp = s_end[1];
   for (uint32_t k = threadIdx.x; k < b.lit_regen - litp; k += blockDim.x) res[pos + k] = kResolved | lit[litp + k];
 }

@@ -79,12 +79,14 @@ struct ZPlanHeader {
   uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_total;
 };
 
-// Per-sequence record in scratch.
+// Per-sequence record in scratch.  The offset is stored symbolically, as
+// the block decoder knows it before the block's repeat offsets are known:
+// okind 0..2 = repeat slot okind at block start minus oval, 3 = constant oval.
 struct ZSeq {
-  uint32_t ll, ml, ofv;  // ofv: offset value, replaced by the resolved offset
-  uint32_t dst;          // block-relative output position of the literal run
-  uint32_t lit;          // block-relative literal position
-  uint32_t pad;
+  uint32_t ll, ml;
+  uint32_t oval, okind;
+  uint32_t dst;  // block-relative output position of the literal run
+  uint32_t lit;  // block-relative literal position
 };
 
 // Per-block runtime record in scratch.
