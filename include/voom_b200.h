@@ -285,6 +285,29 @@ int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const u
                    uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
                    uint32_t* d_status, void* stream);
 
+/* voom_moe_layer without any device allocation, for callers that cannot
+ * allocate device memory themselves: runtimes that own every byte of the GPU
+ * through their own pool, serving loops that must not hit the allocator (and
+ * its device-wide synchronisation) between decode steps, and foreign hosts
+ * that reach this library only through the C ABI and have no CUDA allocator.
+ * It has no counterpart in the reference.
+ * Same arguments and results as voom_moe_layer minus d_scratch /
+ * scratch_bytes: the scratch is one fixed device array (about 7 MiB) per GPU,
+ * loaded with the library and held until the process exits.  Limits:
+ * T <= 64, T * top_k <= 256, H <= 8192, I <= 4096; larger calls return
+ * VOOM_E_CAPACITY without launching anything.  Nothing in the array needs
+ * clearing between calls (every call writes what it reads).  Calls share the
+ * array: two calls that overlap on the GPU (different streams, or different
+ * host threads on one device) race and corrupt each other's results, so
+ * serialise them.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture.  Pass a stream of the current device. */
+int voom_moe_layer_noalloc(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                           const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out,
+                           uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk,
+                           uint32_t gate_tiles, uint32_t down_tiles, uint32_t residual, uint32_t* d_status,
+                           void* stream);
+
 /* Fused decode + SwiGLU for experts routed on the host (the
  * consume_expert_batches path): unique expert u = d_expert_ids[u] (index into
  * d_pages) takes the tokens d_upair[off_u .. off_u + d_ntok[u]), off_u the sum

@@ -25,6 +25,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "rans_core.cuh"
 
@@ -449,6 +451,53 @@ VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts
                             uint32_t* d_status, void* stream) {
   return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
                         gate_tiles, down_tiles, residual, d_scratch, scratch_bytes, d_status, stream);
+}
+
+// ------------------------------------------------------ no-allocation variant
+// Scratch of voom_moe_layer_noalloc: one fixed device array per GPU, sized
+// for T <= 64 tokens, T * top_k <= 256 routes, H <= 8192, I <= 4096.
+namespace {
+constexpr uint32_t kNoAllocMaxT = 64, kNoAllocMaxRoutes = 256, kNoAllocMaxH = 8192, kNoAllocMaxI = 4096;
+constexpr uint64_t kNoAllocBytes =
+    ((sizeof(Routes) + 255) & ~uint64_t(255)) +
+    ((uint64_t(kNoAllocMaxT) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255)) +
+    ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxI * 2 + 16 + 255) & ~uint64_t(255)) +
+    ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255));
+
+__device__ __align__(256) uint8_t g_moe_scratch[kNoAllocBytes];
+
+// Device address of g_moe_scratch on the current device.  In host code the
+// symbol names a host-side stand-in, so its address is looked up once per
+// device (that device current) with cudaGetSymbolAddress and cached.
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[256];
+
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return VOOM_E_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_moe_scratch) != cudaSuccess || !p) return VOOM_E_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return VOOM_OK;
+}
+}  // namespace
+
+VOOM_API int voom_moe_layer_noalloc(const voom_expert_pages* d_pages, uint32_t n_experts,
+                                    const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps,
+                                    const uint16_t* d_x, uint16_t* d_x_out, uint32_t T, uint32_t H, uint32_t I,
+                                    uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles, uint32_t down_tiles,
+                                    uint32_t residual, uint32_t* d_status, void* stream) {
+  if (T > kNoAllocMaxT || uint64_t(T) * top_k > kNoAllocMaxRoutes || H > kNoAllocMaxH || I > kNoAllocMaxI)
+    return VOOM_E_CAPACITY;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != VOOM_OK) return rc;
+  return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
+                        gate_tiles, down_tiles, residual, scratch, kNoAllocBytes, d_status, stream);
 }
 
 // Experts given by the host (routing already grouped, e.g. by
