@@ -455,7 +455,111 @@ class C3Moe:
                 "l2": "flushed between steps (512 MiB write); 128 experts' pages (~770 MB) exceed L2"}
 
 
-WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe}
+class C4MoeEP:
+    """Config 4: one large-MoE layer step -- hidden 6144, 160 experts with
+    intermediate 2048 (BF16 N(0, 0.015)) as rANS-coded pages, top-8 routing,
+    expert popularity Zipf(1.1) (seeded permutation) placed over the ranks by
+    LPT, T tokens (`--tokens`), expert outputs combined with one NCCL
+    all-reduce over NVLink.  Each rank encodes `distinct` real page sets and
+    its other experts alias them (identical decode work, smaller setup); the
+    router is biased by log-popularity so routing follows the Zipf law.
+    Metric: tokens per second of the layer step (whole job)."""
+
+    metric = "fused expert GEMV tok/s through one MoE layer (expert parallel)"
+    unit = "tok/s"
+    dtype = "bf16"
+    data = "synthetic (seeded torch): experts BF16 N(0, 0.015), Zipf(1.1) expert popularity"
+
+    def __init__(self, device, rank: int, tokens: int = 8, world: int = 1, layers: int = 8, distinct: int = 8):
+        import torch
+
+        from voom_b200.runtime import moe
+
+        self.torch = torch
+        self.dev = device
+        self.T = tokens
+        self.name = f"c4_moe_ep_h6144_e160_i2048_top8_T{tokens}_x{world}"
+        E, H, I = 160, 6144, 2048
+        pop = moe.zipf_popularity(E, 1.1, seed=11)
+        self.owned = moe.place_experts(pop, world)[rank]
+        g = torch.Generator().manual_seed(777 + rank)
+
+        def bits(t):
+            return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+        base = [tuple(bits((torch.randn(sh, generator=g) * 0.015).to(torch.bfloat16))
+                      for sh in ((I, H), (I, H), (H, I))) for _ in range(min(distinct, len(self.owned)))]
+        experts: list = [None] * E
+        alias = {}
+        for j, e in enumerate(self.owned):
+            if j < len(base):
+                experts[e] = base[j]
+            else:
+                experts[e] = base[0]
+                alias[e] = self.owned[j % len(base)]
+        self.store = moe.ExpertStore(experts, device, alias=alias)
+        gr = torch.Generator().manual_seed(4242)  # identical router on every rank
+        logp = torch.from_numpy(np.log(pop)).float()
+        self.layers = []
+        for _ in range(layers):
+            wr = (torch.randn((E, H), generator=gr) * 0.02).to(torch.bfloat16).to(device)
+            self.layers.append(moe.ExpertParallelMoeLayer(self.store, wr, None, top_k=8,
+                                                          router_bias=(4.0 * logp).to(device)))
+        self.x0 = torch.randn((tokens, H), generator=gr).to(torch.bfloat16).to(device)
+        self.bufs = [torch.empty_like(self.x0) for _ in range(2)]
+        self.x_host = self.x0.cpu().pin_memory()
+        self.y_host = torch.empty_like(self.x_host).pin_memory()
+        self.units_per_step = tokens * layers  # token-layers: value = tok/s through one layer
+        self.replicated_units = True  # every rank serves the same tokens: no x world
+        self.scaling = "strong"
+        self.L = layers
+        self.algo_bytes = 1  # replaced after the first step (routed local pages)
+        self.launches_per_step = 6 * layers
+
+    def _run(self, x):
+        cur = x
+        for i, layer in enumerate(self.layers):
+            out = self.bufs[i % 2]
+            layer(cur, out=out)
+            cur = out
+        return cur
+
+    def step_device(self, stream_ptr: int):
+        self._run(self.x0)
+        if self.algo_bytes <= 1:
+            torch = self.torch
+            torch.cuda.synchronize()
+            per_expert = self.store.compressed_bytes / max(1, len({id(t) for t in self.store.pages if t}))
+            owned = set(self.owned)
+            n = 0
+            for layer in self.layers:
+                words = layer._scratch[self.T][:16 + 4 * 512].view(torch.int32).cpu().numpy()
+                nu = int(words[0])
+                n += sum(1 for e in words[4:4 + nu] if int(e) in owned)
+            self.local_routed = n
+            self.algo_bytes = int(n * per_expert + 2 * 2 * self.T * 6144 * self.L)
+
+    def verify(self) -> bool:
+        return all(int(l.status.item()) == 0 for l in self.layers)
+
+    def step_e2e(self):
+        x = self.x_host.to(self.dev, non_blocking=True)
+        y = self._run(x)
+        self.y_host.copy_(y, non_blocking=True)
+        return self.T * 6144 * 2, self.T * 6144 * 2
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        return {"value": None, "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": "not sampled for config 4 (see c3_moe for the CPU port of the same layer math)"}
+
+    def config(self) -> dict:
+        return {"workload": self.name, "tokens": self.T, "layers": self.L, "experts": 160, "hidden": 6144,
+                "intermediate": 2048, "top_k": 8, "local_experts": len(self.owned),
+                "popularity": "Zipf(1.1), LPT placement", "combine": "NCCL all-reduce of expert rows",
+                "l2": "flushed between steps (512 MiB write)"}
+
+
+WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe, "c4_moe_ep": C4MoeEP}
 DEFAULT_WORKLOAD = "c2_vpack"
 
 
@@ -533,6 +637,8 @@ def main():
     wl = WORKLOADS[args.workload]
     if wl is C3Moe:
         w = wl(dev, rank, tokens=args.tokens)
+    elif wl is C4MoeEP:
+        w = wl(dev, rank, tokens=args.tokens, world=world)
     elif wl is C2Vpack:
         w = wl(dev, rank, layers=args.c2_layers)
     else:
@@ -571,7 +677,8 @@ def main():
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = w.units_per_step * world / (ms * 1e-3) / 1e9
+    mult = 1 if getattr(w, "replicated_units", False) else world
+    value = w.units_per_step * mult / (ms * 1e-3) / 1e9
 
     # end to end through the public API, pinned host buffers, copies inside
     for _ in range(2):
@@ -592,13 +699,13 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = w.units_per_step * world / (e2e_ms * 1e-3) / 1e9
+    e2e_value = w.units_per_step * (1 if getattr(w, "replicated_units", False) else world) / (e2e_ms * 1e-3) / 1e9
 
     extra = w.extra(stream, args.steps, flush) if hasattr(w, "extra") else {}
     achieved = w.algo_bytes / (ms * 1e-3) / 1e9
     if w.unit != "GB/s":
-        value = w.units_per_step * world / (ms * 1e-3)
-        e2e_value = w.units_per_step * world / (e2e_ms * 1e-3)
+        value = w.units_per_step * mult / (ms * 1e-3)
+        e2e_value = w.units_per_step * mult / (e2e_ms * 1e-3)
     roof = {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": getattr(w, "traffic", None),
             "peak_kind": f"{peaks_kind} (hbm_gbs)"}
@@ -609,7 +716,8 @@ def main():
         line = {
             "metric": w.metric, "value": round(value, 4), "unit": w.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": w.dtype,
+            "higher_is_better": True, "scaling": getattr(w, "scaling", "weak"), "vs_baseline": None,
+            "dtype": w.dtype,
             "data": w.data,
             "config": dict(w.config(), parallelism=f"replicas x{world}" if world > 1 else "single"),
             "roofline": roof, "cpu_baseline": cpu,

@@ -285,6 +285,27 @@ int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const u
                    uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
                    uint32_t* d_status, void* stream);
 
+/* Expert-parallel form of voom_moe_layer, split at the collective.
+ * voom_moe_experts: RMSNorm, router and top-k for all T tokens (replicated on
+ * every rank), then the fused decode + SwiGLU only for experts whose pages
+ * are present in d_pages (n_tiles > 0; other experts' entries have zero
+ * tiles).  d_y (T*top_k rows of H BF16, zeroed here) receives the unweighted
+ * output of each route row; rows of absent experts stay zero, so summing d_y
+ * over ranks (NCCL all-reduce) reproduces the single-GPU rows exactly.  The
+ * routes stay in d_scratch for voom_moe_combine, which applies the route
+ * weights in the reference's accumulation order and the residual.
+ * d_router_bias (E floats, may be NULL) is added to the BF16 router logits
+ * before the softmax.
+ * Replaces: runtime/layer_runner.py:347-394 across experts spread over GPUs
+ * (the reference has no multi-device path). */
+int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                     const float* d_router_bias, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                     uint32_t T, uint32_t H,
+                     uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles, uint32_t down_tiles,
+                     uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream);
+int voom_moe_combine(const void* d_scratch, const uint16_t* d_y, const uint16_t* d_x, uint16_t* d_x_out,
+                     uint32_t T, uint32_t H, uint32_t residual, void* stream);
+
 /* voom_moe_layer without any device allocation, for callers that cannot
  * allocate device memory themselves: runtimes that own every byte of the GPU
  * through their own pool, serving loops that must not hit the allocator (and

@@ -101,3 +101,39 @@ def test_config3_layer_full_size(built_lib, T):
     assert int(layer.status.item()) == 0
     ref = om.moe_layer(x, wr, nw, ex, 8, True, residual=False)
     assert om.rel_l2(got, ref) < TOL
+
+
+def test_expert_parallel_split_matches_full_layer(built_lib):
+    """voom_moe_experts on two disjoint expert subsets, rows summed (what the
+    NCCL all-reduce does across ranks), then voom_moe_combine == voom_moe_layer."""
+    from voom_b200 import _device
+    from voom_b200._lib import check, load
+    from voom_b200.runtime import moe
+
+    E, H, I, k = 12, 512, 256, 4
+    ex, wr, nw = make(E, H, I, 0.02, 21)
+    allw = [tuple(bits(w) for w in e) for e in ex]
+    owned = moe.place_experts(np.ones(E), 2)
+    stores = [moe.ExpertStore([w if e in owned[r] else None for e, w in enumerate(allw)], "cuda:0")
+              for r in range(2)]
+    full = moe.ExpertStore(allw, "cuda:0")
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn((6, H), generator=g).to(torch.bfloat16).cuda()
+    want = moe.MoeLayer(full, wr.cuda(), nw.cuda(), top_k=k)(x)
+    T = x.shape[0]
+    ys, scratch = [], None
+    for st in stores:
+        n = int(load().voom_moe_scratch_bytes(T, H, I, k))
+        scratch = torch.empty(n, dtype=torch.uint8, device="cuda")
+        y = torch.empty((T * k, H), dtype=torch.bfloat16, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        check(load().voom_moe_experts(st.table.data_ptr(), E, wr.cuda().data_ptr(), None, nw.cuda().data_ptr(), 1e-6,
+                                      x.data_ptr(), T, H, I, k, 1, st.gate_tiles, st.down_tiles, y.data_ptr(),
+                                      scratch.data_ptr(), n, status.data_ptr(), _device.stream_ptr(x.device)),
+              "voom_moe_experts")
+        ys.append(y)
+    y = ys[0] + ys[1]  # disjoint rows: exact
+    out = torch.empty_like(x)
+    check(load().voom_moe_combine(scratch.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, 1,
+                                  _device.stream_ptr(x.device)), "voom_moe_combine")
+    assert torch.equal(out, want)

@@ -69,7 +69,8 @@ __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 // renormalisation.  Writes h (BF16) for the expert kernels.
 __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restrict__ x,
                                                        const uint16_t* __restrict__ norm_w, float eps,
-                                                       const uint16_t* __restrict__ wr, uint32_t E, uint32_t H,
+                                                       const uint16_t* __restrict__ wr,
+                                                       const float* __restrict__ bias, uint32_t E, uint32_t H,
                                                        uint32_t k, uint32_t norm_topk, uint16_t* __restrict__ h,
                                                        Routes* routes) {
   __shared__ float s_red[kThreads / 32];
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restric
     float acc = 0.f;
     for (uint32_t i = lane; i < H; i += 32) acc += bf2f(ht[i]) * bf2f(we[i]);
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) s_p[e] = rbf(acc);
+    if (lane == 0) s_p[e] = rbf(acc) + (bias ? bias[e] : 0.f);
   }
   __syncthreads();
   if (tid == 0) {
@@ -430,7 +431,8 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
   uint16_t* y = reinterpret_cast<uint16_t*>(s + L.y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, n_experts, H, top_k, norm_topk, h, R);
+  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, top_k, norm_topk, h,
+                                      R);
   moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   const uint32_t groups = (T + kTok - 1) / kTok;
@@ -451,6 +453,51 @@ VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts
                             uint32_t* d_status, void* stream) {
   return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
                         gate_tiles, down_tiles, residual, d_scratch, scratch_bytes, d_status, stream);
+}
+
+// Expert-parallel split of the layer: phase 1 leaves the unweighted expert
+// outputs in d_y (T*top_k rows of H, route-row order; rows of experts whose
+// pages have no tiles on this rank stay zero) and the routes in d_scratch;
+// the caller sums d_y over ranks; phase 2 combines.
+VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
+                              const float* d_router_bias, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                              uint32_t T, uint32_t H,
+                              uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
+                              uint32_t down_tiles, uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes,
+                              uint32_t* d_status, void* stream) {
+  if (!d_pages || !d_router_w || !d_x || !d_y || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+  if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
+      top_k > n_experts || H % 8 || I % 8)
+    return VOOM_E_INVALID_ARG;
+  const ScratchLayout L = layout(T, H, I, top_k);
+  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
+  uint8_t* s = static_cast<uint8_t*>(d_scratch);
+  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
+  uint16_t* h = reinterpret_cast<uint16_t*>(s + L.h);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_y, 0, size_t(T) * top_k * H * 2, st) != cudaSuccess) return VOOM_E_CUDA;
+  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, top_k, norm_topk,
+                                      h, R);
+  moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
+  const uint32_t max_unique = min(n_experts, T * top_k);
+  const uint32_t groups = (T + kTok - 1) / kTok;
+  const size_t smem = sizeof(GemvShared);
+  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
+      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return VOOM_E_CUDA;
+  moe_gate_up<<<dim3(gate_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
+  moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, d_y, d_status);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+VOOM_API int voom_moe_combine(const void* d_scratch, const uint16_t* d_y, const uint16_t* d_x, uint16_t* d_x_out,
+                              uint32_t T, uint32_t H, uint32_t residual, void* stream) {
+  if (!d_scratch || !d_y || !d_x || !d_x_out || T == 0) return VOOM_E_INVALID_ARG;
+  const Routes* R = reinterpret_cast<const Routes*>(d_scratch);  // routes sit at the start of the scratch
+  moe_combine<<<dim3((H + 255) / 256, T), 256, 0, static_cast<cudaStream_t>(stream)>>>(R, d_y, d_x, d_x_out, H,
+                                                                                        residual);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
 
 // ------------------------------------------------------ no-allocation variant

@@ -61,21 +61,39 @@ class ProjPage:
 
 
 class ExpertStore:
-    """Compressed gate/up/down pages of E experts and their device page table."""
+    """Compressed gate/up/down pages of E experts and their device page table.
 
-    def __init__(self, experts: list[tuple[np.ndarray, np.ndarray, np.ndarray]], device, every: int = EVERY):
+    `experts[e]` is (Wg, Wu, Wd) as BF16 bit arrays, or None for an expert whose
+    pages live on another GPU (its table entry has zero tiles, so the fused
+    kernels skip it).  `alias` maps an expert id to another expert whose pages it
+    shares (synthetic workloads that reuse one page set)."""
+
+    def __init__(self, experts: list, device, every: int = EVERY, alias: dict[int, int] | None = None):
         self.device = _device.require_cuda(device)
-        self.pages = [(ProjPage(g, self.device, every), ProjPage(u, self.device, every),
-                       ProjPage(d, self.device, every)) for g, u, d in experts]
-        self.I, self.H = experts[0][0].shape
+        alias = alias or {}
+        self.pages: list = [None] * len(experts)
+        for e, ws in enumerate(experts):
+            if ws is not None and e not in alias:
+                g, u, d = ws
+                self.pages[e] = (ProjPage(g, self.device, every), ProjPage(u, self.device, every),
+                                 ProjPage(d, self.device, every))
+        for e, src in alias.items():
+            self.pages[e] = self.pages[src]
+        first = next(ws for ws in experts if ws is not None)
+        self.I, self.H = first[0].shape
         tab = np.zeros(len(self.pages), dtype=PAGES_DTYPE)
-        for i, (g, u, d) in enumerate(self.pages):
-            tab[i] = (g.record(), u.record(), d.record())
+        for i, trip in enumerate(self.pages):
+            if trip is not None:
+                g, u, d = trip
+                tab[i] = (g.record(), u.record(), d.record())
         self.table = _device.tensor_from_numpy(tab, self.device)
-        self.gate_tiles = max(g.page.n_tiles for g, _, _ in self.pages)
-        self.down_tiles = max(d.page.n_tiles for _, _, d in self.pages)
-        self.compressed_bytes = sum(p.frame_bytes for t in self.pages for p in t)
-        self.raw_bytes = sum(2 * p.rows * p.cols for t in self.pages for p in t)
+        present = [t for t in self.pages if t is not None]
+        self.local = [e for e, t in enumerate(self.pages) if t is not None]
+        self.gate_tiles = max(g.page.n_tiles for g, _, _ in present)
+        self.down_tiles = max(d.page.n_tiles for _, _, d in present)
+        distinct = {id(t): t for t in present}.values()
+        self.compressed_bytes = sum(p.frame_bytes for t in distinct for p in t)
+        self.raw_bytes = sum(2 * p.rows * p.cols for t in distinct for p in t)
 
     def __len__(self) -> int:
         return len(self.pages)
@@ -115,6 +133,100 @@ class MoeLayer:
                                     st.gate_tiles, st.down_tiles, int(residual), s.data_ptr(), s.numel(),
                                     self.status.data_ptr(),
                                     _device.stream_ptr(st.device, stream)), "voom_moe_layer")
+        return out
+
+    __call__ = forward
+
+
+def route_rows(idx: np.ndarray):
+    """Host mirror of the device route plan: unique experts in first-appearance
+    order over (position, slot), tokens per expert, route-row offsets, the token
+    of every route row, and each token's rows ordered by that expert order (the
+    order runtime/layer_runner.py:387-394 accumulates contributions in)."""
+    T, k = idx.shape
+    order: list[int] = []
+    rows: dict[int, list[int]] = {}
+    for p in range(T * k):
+        e = int(idx[p // k, p % k])
+        if e not in rows:
+            order.append(e)
+            rows[e] = []
+        rows[e].append(p // k)
+    ntok = [len(rows[e]) for e in order]
+    uoff = np.concatenate([[0], np.cumsum(ntok)]).astype(np.int64)
+    upair = [t for e in order for t in rows[e]]
+    tok_order = [[q for u in range(len(order)) for q in range(uoff[u], uoff[u + 1]) if upair[q] == t]
+                 for t in range(T)]
+    return order, ntok, uoff, upair, tok_order
+
+
+def zipf_popularity(n_experts: int, s: float = 1.1, seed: int = 0) -> np.ndarray:
+    """Expert popularity Zipf(s) over ranks, assigned to experts by a seeded permutation."""
+    w = 1.0 / np.arange(1, n_experts + 1, dtype=np.float64) ** s
+    perm = np.random.default_rng(seed).permutation(n_experts)
+    p = np.empty(n_experts)
+    p[perm] = w / w.sum()
+    return p
+
+
+def place_experts(load, world: int) -> list[list[int]]:
+    """Longest-processing-time placement: experts by descending expected load,
+    each to the currently least-loaded rank.  Returns the experts of each rank."""
+    load = np.asarray(load, dtype=np.float64)
+    bins = [[] for _ in range(world)]
+    tot = np.zeros(world)
+    for e in sorted(range(load.size), key=lambda i: (-load[i], i)):
+        r = int(np.argmin(tot))
+        bins[r].append(e)
+        tot[r] += load[e]
+    return [sorted(b) for b in bins]
+
+
+class ExpertParallelMoeLayer:
+    """MoE layer with experts spread over the ranks of a process group (NCCL).
+
+    Every rank routes all tokens (replicated router), runs the fused decode +
+    SwiGLU for its own experts only, the route rows are summed over ranks
+    with one all-reduce (each row has exactly one nonzero contributor, so the
+    sum is exact), and every rank applies the same ordered combine."""
+
+    def __init__(self, store: ExpertStore, router_w: torch.Tensor, norm_w: torch.Tensor | None, *, top_k: int,
+                 norm_topk: bool = True, eps: float = 1e-6, group=None, router_bias: torch.Tensor | None = None):
+        self.store = store
+        self.router_w = router_w.contiguous()
+        self.router_bias = None if router_bias is None else router_bias.float().contiguous()
+        self.norm_w = None if norm_w is None else norm_w.contiguous()
+        self.top_k = int(top_k)
+        self.norm_topk = bool(norm_topk)
+        self.eps = float(eps)
+        self.group = group
+        self._scratch: dict[int, torch.Tensor] = {}
+        self._y: dict[int, torch.Tensor] = {}
+        self.status = torch.zeros(1, dtype=torch.int32, device=store.device)
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, residual: bool = True) -> torch.Tensor:
+        import torch.distributed as dist
+
+        T, H = x.shape
+        st = self.store
+        if T not in self._scratch:
+            n = load().voom_moe_scratch_bytes(T, H, st.I, self.top_k)
+            self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=st.device)
+            self._y[T] = torch.empty((T * self.top_k, H), dtype=torch.bfloat16, device=st.device)
+        s, y = self._scratch[T], self._y[T]
+        x = x.contiguous()
+        out = torch.empty_like(x) if out is None else out
+        sp = _device.stream_ptr(st.device, None)
+        check(load().voom_moe_experts(st.table.data_ptr(), len(st), self.router_w.data_ptr(),
+                                      None if self.router_bias is None else self.router_bias.data_ptr(),
+                                      None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                      x.data_ptr(), T, H, st.I, self.top_k, int(self.norm_topk), st.gate_tiles,
+                                      st.down_tiles, y.data_ptr(), s.data_ptr(), s.numel(), self.status.data_ptr(),
+                                      sp), "voom_moe_experts")
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        check(load().voom_moe_combine(s.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, int(residual),
+                                      sp), "voom_moe_combine")
         return out
 
     __call__ = forward
