@@ -362,7 +362,9 @@ class C3Moe:
         self.layers = []
         for _ in range(layers):
             wr = torch.randn((E, H), generator=g).to(torch.bfloat16).to(device)
-            self.layers.append(moe.MoeLayer(self.store, wr, None, top_k=8, norm_topk=True))
+            # post-attention RMSNorm weight of the layer (keeps the 48-layer chain finite)
+            nw = (1.0 + 0.05 * torch.randn(H, generator=g)).to(torch.bfloat16).to(device)
+            self.layers.append(moe.MoeLayer(self.store, wr, nw, top_k=8, norm_topk=True))
         self.x0 = torch.randn((tokens, H), generator=g).to(torch.bfloat16).to(device)
         self.bufs = [torch.empty_like(self.x0) for _ in range(2)]
         self.x_host = torch.randn((tokens, H), generator=g).to(torch.bfloat16).pin_memory()
@@ -403,7 +405,7 @@ class C3Moe:
         layer = self.layers[0]
         out = layer(self.x0, residual=False).cpu()
         ex = [tuple(torch.from_numpy(w.view(np.int16)).view(torch.bfloat16) for w in e) for e in self.experts_raw]
-        ref = om.moe_layer(self.x0.cpu(), layer.router_w.cpu(), None, ex, 8, True, residual=False)
+        ref = om.moe_layer(self.x0.cpu(), layer.router_w.cpu(), layer.norm_w.cpu(), ex, 8, True, residual=False)
         ok = om.rel_l2(out, ref) < 1e-2 and all(int(l.status.item()) == 0 for l in self.layers)
         return ok
 
@@ -423,12 +425,13 @@ class C3Moe:
         torch.set_num_threads(threads)
         layer = self.layers[0]
         wr = layer.router_w.cpu()
+        nw = layer.norm_w.cpu()
         x = self.x0.cpu()
         frames = [[bytes(p.page.src[: p.frame_bytes].cpu().numpy()) for p in trip] for trip in self.store.pages]
         done = 0
         t0 = time.perf_counter()
         while time.perf_counter() - t0 < budget_s or done == 0:
-            h = x
+            h = om.rms_norm(x, nw, 1e-6)
             idx, _ = om.route(h, wr, 8, True)
             needed = sorted({int(e) for e in idx.flatten()})
             ex = {}
@@ -438,7 +441,7 @@ class C3Moe:
                     raw = np.frombuffer(orans.decode(fr), np.int16).reshape(rows, cols)
                     ws.append(torch.from_numpy(raw.copy()).view(torch.bfloat16))
                 ex[e] = tuple(ws)
-            om.moe_layer(h, wr, None, ex, 8, True)
+            om.moe_layer(x, wr, nw, ex, 8, True)
             done += 1
         dt = time.perf_counter() - t0
         tok_s = self.T / (dt / done * self.L)
@@ -503,7 +506,8 @@ class C4MoeEP:
         self.layers = []
         for _ in range(layers):
             wr = (torch.randn((E, H), generator=gr) * 0.02).to(torch.bfloat16).to(device)
-            self.layers.append(moe.ExpertParallelMoeLayer(self.store, wr, None, top_k=8,
+            nw = (1.0 + 0.05 * torch.randn(H, generator=gr)).to(torch.bfloat16).to(device)
+            self.layers.append(moe.ExpertParallelMoeLayer(self.store, wr, nw, top_k=8,
                                                           router_bias=(4.0 * logp).to(device)))
         self.x0 = torch.randn((tokens, H), generator=gr).to(torch.bfloat16).to(device)
         self.bufs = [torch.empty_like(self.x0) for _ in range(2)]

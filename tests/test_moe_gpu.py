@@ -119,7 +119,8 @@ def test_expert_parallel_split_matches_full_layer(built_lib):
     full = moe.ExpertStore(allw, "cuda:0")
     g = torch.Generator().manual_seed(9)
     x = torch.randn((6, H), generator=g).to(torch.bfloat16).cuda()
-    want = moe.MoeLayer(full, wr.cuda(), nw.cuda(), top_k=k)(x)
+    wr_d, nw_d = wr.cuda(), nw.cuda()  # held for the asynchronous launches below
+    want = moe.MoeLayer(full, wr_d, nw_d, top_k=k)(x)
     T = x.shape[0]
     ys, scratch = [], None
     for st in stores:
@@ -127,7 +128,7 @@ def test_expert_parallel_split_matches_full_layer(built_lib):
         scratch = torch.empty(n, dtype=torch.uint8, device="cuda")
         y = torch.empty((T * k, H), dtype=torch.bfloat16, device="cuda")
         status = torch.zeros(1, dtype=torch.int32, device="cuda")
-        check(load().voom_moe_experts(st.table.data_ptr(), E, wr.cuda().data_ptr(), None, nw.cuda().data_ptr(), 1e-6,
+        check(load().voom_moe_experts(st.table.data_ptr(), E, wr_d.data_ptr(), None, nw_d.data_ptr(), 1e-6,
                                       x.data_ptr(), T, H, I, k, 1, st.gate_tiles, st.down_tiles, y.data_ptr(),
                                       scratch.data_ptr(), n, status.data_ptr(), _device.stream_ptr(x.device)),
               "voom_moe_experts")

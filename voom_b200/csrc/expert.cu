@@ -36,7 +36,6 @@ using namespace voom::rans;
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kPairs = kThreads / 2;
 constexpr int kTok = 8;          // tokens per expert pass
 constexpr int kMaxTK = 512;      // T * top_k
 constexpr int kMaxE = 1024;      // experts
@@ -64,19 +63,33 @@ __device__ __forceinline__ uint32_t f2bf(float f) {  // round to nearest even
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 
 // ------------------------------------------------------------------ router
-// One CTA per token: RMSNorm (optional), logits = h @ Wr.T rounded to BF16,
-// fp32 softmax, top-k (largest first; ties -> lower expert id), optional
-// renormalisation.  Writes h (BF16) for the expert kernels.
+// One CTA per token: RMSNorm (optional), logits = h @ Wr.T rounded to BF16
+// (+ optional bias), fp32 softmax, top-k (largest first; ties -> lower expert
+// id) by k rounds of block arg-max, optional renormalisation.  Writes h (BF16)
+// for the expert kernels.
+constexpr int kMaxH = 8192;
+
+__device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restrict__ x,
                                                        const uint16_t* __restrict__ norm_w, float eps,
                                                        const uint16_t* __restrict__ wr,
                                                        const float* __restrict__ bias, uint32_t E, uint32_t H,
                                                        uint32_t k, uint32_t norm_topk, uint16_t* __restrict__ h,
                                                        Routes* routes) {
-  __shared__ float s_red[kThreads / 32];
+  __shared__ float s_h[kMaxH];
   __shared__ float s_p[kMaxE];
-  __shared__ float s_scale;
-  const uint32_t t = blockIdx.x, tid = threadIdx.x;
+  __shared__ float s_redf[kThreads / 32];
+  __shared__ int s_redi[kThreads / 32];
+  __shared__ float s_scale, s_max, s_sum;
+  __shared__ uint8_t s_used[kMaxE];
+  __shared__ int s_pick[64];
+  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint16_t* xt = x + size_t(t) * H;
   uint16_t* ht = h + size_t(t) * H;
   float ss = 0.f;
@@ -85,55 +98,102 @@ __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restric
     ss += v * v;
   }
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+  if (lane == 0) s_redf[warp] = ss;
   __syncthreads();
   if (tid == 0) {
     float tot = 0.f;
-    for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
+    for (int w = 0; w < kThreads / 32; w++) tot += s_redf[w];
     s_scale = rsqrtf(tot / float(H) + eps);
   }
   __syncthreads();
   for (uint32_t i = tid; i < H; i += kThreads) {
-    const float v = bf2f(xt[i]);
-    ht[i] = uint16_t(norm_w ? f2bf(v * s_scale * bf2f(norm_w[i])) : xt[i]);
+    const uint32_t hb = norm_w ? f2bf(bf2f(xt[i]) * s_scale * bf2f(norm_w[i])) : xt[i];
+    ht[i] = uint16_t(hb);
+    s_h[i] = bf2f(hb);
   }
+  for (uint32_t e = tid; e < E; e += kThreads) s_used[e] = 0;
   __syncthreads();
-  // logits: one warp per expert row
-  const uint32_t warp = tid >> 5, lane = tid & 31;
+  // logits: one warp per expert row, 8 weights per lane per step
   for (uint32_t e = warp; e < E; e += kThreads / 32) {
     const uint16_t* we = wr + size_t(e) * H;
     float acc = 0.f;
-    for (uint32_t i = lane; i < H; i += 32) acc += bf2f(ht[i]) * bf2f(we[i]);
+    for (uint32_t i = lane * 8; i < H; i += 256) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(we + i));
+      acc = fmaf(bf2f(w.x & 0xFFFFu), s_h[i], acc);
+      acc = fmaf(__uint_as_float(w.x & 0xFFFF0000u), s_h[i + 1], acc);
+      acc = fmaf(bf2f(w.y & 0xFFFFu), s_h[i + 2], acc);
+      acc = fmaf(__uint_as_float(w.y & 0xFFFF0000u), s_h[i + 3], acc);
+      acc = fmaf(bf2f(w.z & 0xFFFFu), s_h[i + 4], acc);
+      acc = fmaf(__uint_as_float(w.z & 0xFFFF0000u), s_h[i + 5], acc);
+      acc = fmaf(bf2f(w.w & 0xFFFFu), s_h[i + 6], acc);
+      acc = fmaf(__uint_as_float(w.w & 0xFFFF0000u), s_h[i + 7], acc);
+    }
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
     if (lane == 0) s_p[e] = rbf(acc) + (bias ? bias[e] : 0.f);
   }
   __syncthreads();
+  // softmax (fp32): block max, then block sum of exp
+  float mx = -INFINITY;
+  for (uint32_t e = tid; e < E; e += kThreads) mx = fmaxf(mx, s_p[e]);
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  if (lane == 0) s_redf[warp] = mx;
+  __syncthreads();
   if (tid == 0) {
-    float mx = -INFINITY;
-    for (uint32_t e = 0; e < E; e++) mx = fmaxf(mx, s_p[e]);
-    float sum = 0.f;
-    for (uint32_t e = 0; e < E; e++) {
-      s_p[e] = __expf(s_p[e] - mx);
-      sum += s_p[e];
+    float m = -INFINITY;
+    for (int w = 0; w < kThreads / 32; w++) m = fmaxf(m, s_redf[w]);
+    s_max = m;
+  }
+  __syncthreads();
+  float sm = 0.f;
+  for (uint32_t e = tid; e < E; e += kThreads) {
+    const float p = __expf(s_p[e] - s_max);
+    s_p[e] = p;
+    sm += p;
+  }
+  for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
+  __syncthreads();
+  if (lane == 0) s_redf[warp] = sm;
+  __syncthreads();
+  if (tid == 0) {
+    float a = 0.f;
+    for (int w = 0; w < kThreads / 32; w++) a += s_redf[w];
+    s_sum = a;
+  }
+  // top-k: k rounds of block arg-max over the unused experts.  Probabilities
+  // are >= 0; a NaN (non-finite activations) ranks below every number, so
+  // each round still picks a valid unused expert.
+  for (uint32_t j = 0; j < k; j++) {
+    float bv = -3.f;
+    int bi = 0x7FFFFFFF;
+    for (uint32_t e = tid; e < E; e += kThreads) {
+      const float v = s_p[e];
+      if (!s_used[e]) argmax_pair(bv, bi, v == v ? v : -2.f, int(e));
     }
+    for (int o = 16; o; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      argmax_pair(bv, bi, v2, i2);
+    }
+    __syncthreads();
+    if (lane == 0) {
+      s_redf[warp] = bv;
+      s_redi[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kThreads / 32; w++) argmax_pair(bv, bi, s_redf[w], s_redi[w]);
+      s_pick[j] = bi;
+      s_used[bi] = 1;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
     float sel = 0.f;
-    uint32_t chosen[64];
-    float pw[64];
+    for (uint32_t j = 0; j < k; j++) sel += s_p[s_pick[j]] / s_sum;
     for (uint32_t j = 0; j < k; j++) {
-      float best = -1.f;
-      uint32_t bi = 0;
-      for (uint32_t e = 0; e < E; e++) {
-        bool used = false;
-        for (uint32_t q = 0; q < j; q++) used |= (chosen[q] == e);
-        if (!used && s_p[e] > best) { best = s_p[e]; bi = e; }
-      }
-      chosen[j] = bi;
-      pw[j] = best / sum;
-      sel += pw[j];
-    }
-    for (uint32_t j = 0; j < k; j++) {
-      routes->idx[t * k + j] = chosen[j];
-      routes->w[t * k + j] = norm_topk ? pw[j] / sel : pw[j];
+      const float pw = s_p[s_pick[j]] / s_sum;
+      routes->idx[t * k + j] = uint32_t(s_pick[j]);
+      routes->w[t * k + j] = norm_topk ? pw / sel : pw;
     }
   }
 }
@@ -198,6 +258,7 @@ struct GemvShared {
 };
 
 // 8 BF16 weights (one uint4) times 8 activations at column k of each token.
+template <int NT>
 __device__ __forceinline__ void dot8(const uint4 w, const uint16_t* __restrict__ act, uint32_t ld,
                                      const uint32_t* tok, uint32_t ntk, uint32_t k, float* acc) {
   const float w0 = bf2f(w.x & 0xFFFFu), w1 = __uint_as_float(w.x & 0xFFFF0000u);
@@ -205,7 +266,7 @@ __device__ __forceinline__ void dot8(const uint4 w, const uint16_t* __restrict__
   const float w4 = bf2f(w.z & 0xFFFFu), w5 = __uint_as_float(w.z & 0xFFFF0000u);
   const float w6 = bf2f(w.w & 0xFFFFu), w7 = __uint_as_float(w.w & 0xFFFF0000u);
 #pragma unroll
-  for (int j = 0; j < kTok; j++) {
+  for (int j = 0; j < NT; j++) {
     if (j < int(ntk)) {
       const uint4 a = __ldg(reinterpret_cast<const uint4*>(act + size_t(tok[j]) * ld + k));
       float s = acc[j];
@@ -225,6 +286,7 @@ __device__ __forceinline__ void dot8(const uint4 w, const uint16_t* __restrict__
 // Decodes tile `t` of one projection for the CTA's tokens and adds every
 // row's dot products into sh.acc[slot].  Rows of `cols` elements; each lane
 // pair owns one `every`-element segment.  Returns nothing; errors -> sh.status.
+template <int NT>
 __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t, int slot,
                           const uint16_t* __restrict__ act, uint32_t ld, uint32_t ntk) {
   const voom_rans_tile tl = P.tiles[t];
@@ -237,9 +299,9 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
     build_lut(sh.lut[0], sh.cum[0], sh.red, &sh.degenerate[0], P.src + tl.low_freq);
     build_lut(sh.lut[1], sh.cum[1], sh.red, &sh.degenerate[1], P.src + tl.high_freq);
   }
-  float acc[kTok];
+  float acc[NT];
 #pragma unroll
-  for (int j = 0; j < kTok; j++) acc[j] = 0.f;
+  for (int j = 0; j < NT; j++) acc[j] = 0.f;
   uint32_t row_local = 0;
   if (p < nseg) {
     row_local = p / spr;
@@ -253,7 +315,7 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
           v[q] = uint32_t(wsrc[2 * (c + 2 * q)]) | (uint32_t(wsrc[2 * (c + 2 * q) + 1]) << 8) |
                  (uint32_t(wsrc[2 * (c + 2 * q) + 2]) << 16) | (uint32_t(wsrc[2 * (c + 2 * q) + 3]) << 24);
         w = make_uint4(v[0], v[1], v[2], v[3]);
-        dot8(w, act, ld, sh.tok, ntk, k0 + c, acc);
+        dot8<NT>(w, act, ld, sh.tok, ntk, k0 + c, acc);
       }
     } else {
       const uint32_t* ck = P.ckpt + P.ckpt_base[t];
@@ -268,20 +330,24 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
       const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
       const unsigned mask = 0x3u << (tid & 30u);
       uint32_t done = 0;
-      for (; done < every; done += 16) {
-        const bool ok = (r.len - r.cur >= 40u) && (r.x >= kRansL);
-        if (!__all_sync(mask, ok)) break;
-        uint32_t a[4];
+      if (every >= 16 && __all_sync(mask, (r.len - r.cur >= kWinGuard) && (r.x >= kRansL))) {
+        Window W;
+        win_open(W, r);
+        for (;;) {
+          uint32_t a[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const uint32_t s0 = rans_step_fast(lut_s, r);
-          const uint32_t s1 = rans_step_fast(lut_s, r);
-          const uint32_t s2 = rans_step_fast(lut_s, r);
-          const uint32_t s3 = rans_step_fast(lut_s, r);
-          a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+          for (int j = 0; j < 4; j++) {
+            const uint32_t s0 = rans_step_win(lut_s, r, W);
+            const uint32_t s1 = rans_step_win(lut_s, r, W);
+            const uint32_t s2 = rans_step_win(lut_s, r, W);
+            const uint32_t s3 = rans_step_win(lut_s, r, W);
+            a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
+          }
+          const uint4 w = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
+          dot8<NT>(w, act, ld, sh.tok, ntk, k0 + done + 8 * lane, acc);
+          done += 16;
+          if (done + 16 > every || !__all_sync(mask, r.len - r.cur >= kWinGuard)) break;
         }
-        const uint4 w = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
-        dot8(w, act, ld, sh.tok, ntk, k0 + done + 8 * lane, acc);
       }
       // exact tail in lockstep: both planes have the same count left
       for (; done < every; done++) {
@@ -289,7 +355,9 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
         const uint32_t o = __shfl_xor_sync(mask, s, 1);
         if (lane == 0) {
           const float w = bf2f(s | (o << 8));
-          for (uint32_t j = 0; j < ntk; j++) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
+#pragma unroll
+          for (int j = 0; j < NT; j++)
+            if (j < int(ntk)) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
         }
       }
       const bool last = (p + 1 == nseg);
@@ -300,26 +368,37 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
   }
   // pair reduce, then rows meet in shared memory
 #pragma unroll
-  for (int j = 0; j < kTok; j++) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 1);
-  if (p < nseg && lane == 0)
-    for (uint32_t j = 0; j < ntk; j++) atomicAdd(&sh.acc[slot][row_local][j], acc[j]);
+  for (int j = 0; j < NT; j++) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 1);
+  if (p < nseg && lane == 0) {
+#pragma unroll
+    for (int j = 0; j < NT; j++)
+      if (j < int(ntk)) atomicAdd(&sh.acc[slot][row_local][j], acc[j]);
+  }
   __syncthreads();
 }
 
+// Bit 2 of the status word: an expert has more route rows than the grid's
+// token groups cover (more tokens than T for one expert).
+constexpr uint32_t kStatusRoutes = 2u;
+
+template <int NT>
 __device__ __forceinline__ bool setup_tokens(GemvShared& sh, const Routes* R, uint32_t u, uint32_t grp,
-                                             uint32_t* ntk_out) {
+                                             uint32_t* ntk_out, uint32_t* status) {
   if (u >= R->n_unique) return false;
   const uint32_t n = R->ntok[u];
-  if (grp * kTok >= n) return false;
-  const uint32_t ntk = min(uint32_t(kTok), n - grp * kTok);
-  if (threadIdx.x < kTok)
-    sh.tok[threadIdx.x] = threadIdx.x < ntk ? R->upair[R->uoff[u] + grp * kTok + threadIdx.x] : 0;
+  if (threadIdx.x == 0 && blockIdx.x == 0 && grp == 0 && n > gridDim.z * NT) atomicOr(status, kStatusRoutes);
+  if (grp * NT >= n) return false;
+  const uint32_t ntk = min(uint32_t(NT), n - grp * NT);
+  if (threadIdx.x < NT)
+    sh.tok[threadIdx.x] = threadIdx.x < ntk ? R->upair[R->uoff[u] + grp * NT + threadIdx.x] : 0;
   *ntk_out = ntk;
   return true;
 }
 
 // gate + up tiles of one routed expert -> activation rows (BF16) per token.
-__global__ void __launch_bounds__(kThreads, 1) moe_gate_up(const voom_expert_pages* __restrict__ pages,
+// NT = tokens per CTA (1, 2, 4 or 8): registers scale with it.
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 4) moe_gate_up(const voom_expert_pages* __restrict__ pages,
                                                            const Routes* __restrict__ R,
                                                            const uint16_t* __restrict__ h, uint32_t H, uint32_t I,
                                                            uint16_t* __restrict__ act_out, uint32_t* status) {
@@ -327,14 +406,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up(const voom_expert_pag
   GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
   const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
   uint32_t ntk;
-  if (!setup_tokens(sh, R, u, grp, &ntk)) return;
+  if (!setup_tokens<NT>(sh, R, u, grp, &ntk, status)) return;
   const voom_expert_pages& E = pages[R->expert[u]];
   if (t >= E.gate.n_tiles) return;
   for (int i = threadIdx.x; i < 2 * 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
   if (threadIdx.x == 0) sh.status = 0;
   __syncthreads();
-  gemv_tile(sh, E.gate, t, 0, h, H, ntk);
-  gemv_tile(sh, E.up, t, 1, h, H, ntk);
+  gemv_tile<NT>(sh, E.gate, t, 0, h, H, ntk);
+  gemv_tile<NT>(sh, E.up, t, 1, h, H, ntk);
   const voom_rans_tile tl = E.gate.tiles[t];
   const uint32_t rows = tl.raw_len / (2u * H), row0 = uint32_t(tl.dst / (2u * H));
   for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
@@ -342,13 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_gate_up(const voom_expert_pag
     const float g = rbf(sh.acc[0][row][j]), up = rbf(sh.acc[1][row][j]);
     const float s = rbf(1.f / (1.f + __expf(-g)));
     const float a = rbf(rbf(s * g) * up);
-    act_out[size_t(R->uoff[u] + grp * kTok + j) * I + row0 + row] = uint16_t(f2bf(a));
+    act_out[size_t(R->uoff[u] + grp * NT + j) * I + row0 + row] = uint16_t(f2bf(a));
   }
   if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
 }
 
 // down tile of one routed expert -> y rows (BF16) per token.
-__global__ void __launch_bounds__(kThreads, 1) moe_down(const voom_expert_pages* __restrict__ pages,
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 4) moe_down(const voom_expert_pages* __restrict__ pages,
                                                         const Routes* __restrict__ R,
                                                         const uint16_t* __restrict__ act, uint32_t H, uint32_t I,
                                                         uint16_t* __restrict__ y_out, uint32_t* status) {
@@ -356,20 +436,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down(const voom_expert_pages*
   GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
   const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
   uint32_t ntk;
-  if (!setup_tokens(sh, R, u, grp, &ntk)) return;
+  if (!setup_tokens<NT>(sh, R, u, grp, &ntk, status)) return;
   const voom_expert_pages& E = pages[R->expert[u]];
   if (t >= E.down.n_tiles) return;
   // the down projection reads this expert's activation rows
-  if (threadIdx.x < kTok) sh.tok[threadIdx.x] = R->uoff[u] + grp * kTok + threadIdx.x;
+  if (threadIdx.x < NT) sh.tok[threadIdx.x] = R->uoff[u] + grp * NT + threadIdx.x;
   for (int i = threadIdx.x; i < 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
   if (threadIdx.x == 0) sh.status = 0;
   __syncthreads();
-  gemv_tile(sh, E.down, t, 0, act, I, ntk);
+  gemv_tile<NT>(sh, E.down, t, 0, act, I, ntk);
   const voom_rans_tile tl = E.down.tiles[t];
   const uint32_t rows = tl.raw_len / (2u * I), row0 = uint32_t(tl.dst / (2u * I));
   for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
     const uint32_t row = q / ntk, j = q % ntk;
-    y_out[size_t(R->uoff[u] + grp * kTok + j) * H + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
+    y_out[size_t(R->uoff[u] + grp * NT + j) * H + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
   }
   if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
 }
@@ -408,6 +488,33 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   return s;
 }
 
+
+template <int NT>
+int launch_gemv_nt(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
+                   uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t gate_tiles,
+                   uint32_t down_tiles, uint32_t* d_status, cudaStream_t st) {
+  const uint32_t groups = (T + NT - 1) / NT;
+  const size_t smem = sizeof(GemvShared);
+  if (cudaFuncSetAttribute(moe_gate_up<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(moe_down<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return VOOM_E_CUDA;
+  moe_gate_up<NT><<<dim3(gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
+  moe_down<NT><<<dim3(down_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
+  return VOOM_OK;
+}
+
+// gate/up then down for every routed expert; tokens per CTA chosen from T
+// (an expert sees at most T tokens).
+int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act, uint16_t* y,
+                uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t gate_tiles, uint32_t down_tiles,
+                uint32_t* d_status, cudaStream_t st) {
+  if (T == 1) return launch_gemv_nt<1>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+  if (T == 2) return launch_gemv_nt<2>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+  if (T <= 4) return launch_gemv_nt<4>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+  return launch_gemv_nt<8>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+}
+
 }  // namespace
 
 VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k) {
@@ -421,7 +528,7 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
                             uint32_t* d_status, void* stream) {
   if (!d_pages || !d_router_w || !d_x || !d_x_out || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
   if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
-      top_k > n_experts || H % 8 || I % 8)
+      top_k > n_experts || H % 8 || I % 8 || H > kMaxH)
     return VOOM_E_INVALID_ARG;
   const ScratchLayout L = layout(T, H, I, top_k);
   if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
@@ -435,13 +542,8 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
                                       R);
   moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
-  const uint32_t groups = (T + kTok - 1) / kTok;
-  const size_t smem = sizeof(GemvShared);
-  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
-      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return VOOM_E_CUDA;
-  moe_gate_up<<<dim3(gate_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
-  moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
+  const int rc = launch_gemv(d_pages, R, h, act, y, T, H, I, max_unique, gate_tiles, down_tiles, d_status, st);
+  if (rc != VOOM_OK) return rc;
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
@@ -467,7 +569,7 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
                               uint32_t* d_status, void* stream) {
   if (!d_pages || !d_router_w || !d_x || !d_y || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
   if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
-      top_k > n_experts || H % 8 || I % 8)
+      top_k > n_experts || H % 8 || I % 8 || H > kMaxH)
     return VOOM_E_INVALID_ARG;
   const ScratchLayout L = layout(T, H, I, top_k);
   if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
@@ -481,13 +583,8 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
                                       h, R);
   moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
-  const uint32_t groups = (T + kTok - 1) / kTok;
-  const size_t smem = sizeof(GemvShared);
-  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
-      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return VOOM_E_CUDA;
-  moe_gate_up<<<dim3(gate_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
-  moe_down<<<dim3(down_tiles, max_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, d_y, d_status);
+  const int rc = launch_gemv(d_pages, R, h, act, d_y, T, H, I, max_unique, gate_tiles, down_tiles, d_status, st);
+  if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
 
@@ -572,12 +669,7 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
       cudaMemcpyAsync(&R->upair[0], d_upair, 4ull * n_rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return VOOM_E_CUDA;
   moe_route_offsets<<<1, 32, 0, st>>>(R, n_unique, T);
-  const uint32_t groups = (T + kTok - 1) / kTok;
-  const size_t smem = sizeof(GemvShared);
-  if (cudaFuncSetAttribute(moe_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
-      cudaFuncSetAttribute(moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-    return VOOM_E_CUDA;
-  moe_gate_up<<<dim3(gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, d_h, H, I, act, d_status);
-  moe_down<<<dim3(down_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, d_y, d_status);
+  const int rc = launch_gemv(d_pages, R, d_h, act, d_y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+  if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

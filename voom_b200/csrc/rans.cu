@@ -92,29 +92,33 @@ __device__ __forceinline__ void decode_generic(uint32_t lut_s, bool degenerate, 
 
 // Lockstep pair decode of up to `nchunks` x 16 symbols (low plane on the even
 // lane, high plane on the odd lane, both non-degenerate, `out` 16-byte
-// aligned).  A chunk runs on the branch-free step only when both lanes have
-// >= 40 payload bytes left and a normal state; otherwise the pair stops and
-// the caller finishes each plane with decode_generic.  Returns chunks done.
+// aligned).  A chunk runs on the windowed branch-free step only when both
+// lanes have >= kWinGuard payload bytes left and a normal state; otherwise the
+// pair stops and the caller finishes each plane with decode_generic.  Returns
+// chunks done.
 __device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r, uint32_t nchunks,
                                                      uint32_t first, uint8_t* out, uint32_t lane,
                                                      uint32_t* ckpt, uint32_t every,
                                                      uint32_t limit_k, unsigned mask) {
   uint32_t c = 0;
-  for (; c < nchunks; c++) {
-    const bool ok = (r.len - r.cur >= 40u) && (r.x >= kRansL);
-    if (!__all_sync(mask, ok)) break;
-    asm volatile("prefetch.global.L1 [%0];" ::"l"(r.payload + r.cur + 256));
+  if (nchunks == 0 || !__all_sync(mask, (r.len - r.cur >= kWinGuard) && (r.x >= kRansL))) return 0;
+  Window W;
+  win_open(W, r);
+  for (;;) {
+    if ((c & 3u) == 0) asm volatile("prefetch.global.L1 [%0];" ::"l"(r.payload + r.cur + 256));
     uint32_t a[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const uint32_t s0 = rans_step_fast(lut_s, r);
-      const uint32_t s1 = rans_step_fast(lut_s, r);
-      const uint32_t s2 = rans_step_fast(lut_s, r);
-      const uint32_t s3 = rans_step_fast(lut_s, r);
+      const uint32_t s0 = rans_step_win(lut_s, r, W);
+      const uint32_t s1 = rans_step_win(lut_s, r, W);
+      const uint32_t s2 = rans_step_win(lut_s, r, W);
+      const uint32_t s3 = rans_step_win(lut_s, r, W);
       a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
     }
     *reinterpret_cast<uint4*>(out + 32u * c + 16u * lane) = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
-    if (ckpt) record_ckpt(ckpt, first + 16u * (c + 1), every, limit_k, lane, r);
+    c++;
+    if (ckpt) record_ckpt(ckpt, first + 16u * c, every, limit_k, lane, r);
+    if (c == nchunks || !__all_sync(mask, r.len - r.cur >= kWinGuard)) break;
   }
   return c;
 }

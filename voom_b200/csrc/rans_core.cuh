@@ -70,6 +70,57 @@ __device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, PlaneRun& r) 
   return e & 0xFFu;
 }
 
+// Renormalisation bytes of a fast run held in registers: a 64-bit window of
+// the stream's next bytes (left-aligned, first byte most significant) plus one
+// preloaded aligned word.  A step shifts k bytes out of the window; the window
+// takes the preloaded word once 4 or fewer bytes remain, and only then is a
+// new word loaded.  Per step about a third of a warp's lanes issue a load,
+// against two unaligned loads per lane for load4_be, and the load result is
+// not needed before the following refill.  Reads reach at most cur + 11.
+struct Window {
+  const uint32_t* words;  // next word to load
+  uint64_t w;             // bytes [cur, cur + n) left-aligned
+  uint32_t n;             // valid bytes in w: 5..8 before each step
+  uint32_t nxt;           // big-endian word holding bytes [cur + n, cur + n + 4)
+};
+
+__device__ __forceinline__ uint32_t ldg_be32(const uint32_t* p) { return __byte_perm(__ldg(p), 0, 0x0123); }
+
+// Opens a window at r.cur.  Payload bytes [cur - 3, cur + 12) must be readable.
+__device__ __forceinline__ void win_open(Window& W, const PlaneRun& r) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(r.payload) + r.cur;
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  const uint32_t s = uint32_t(a & 3u);
+  const uint64_t v = (uint64_t(ldg_be32(p)) << 32) | ldg_be32(p + 1);
+  W.w = v << (8u * s);
+  W.n = 8u - s;
+  W.nxt = ldg_be32(p + 2);
+  W.words = p + 3;
+}
+
+// Same arithmetic as rans_step_fast with the bytes taken from the window.
+__device__ __forceinline__ uint32_t rans_step_win(uint32_t lut_s, PlaneRun& r, Window& W) {
+  const uint32_t e = lds32(lut_s + 4u * (r.x & 4095u));
+  const uint32_t xs = r.x >> 12;
+  const uint32_t x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
+  const uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
+  r.x = __funnelshift_l(uint32_t(W.w >> 32), x, 8u * k);
+  W.w <<= 8u * k;
+  W.n -= k;
+  r.cur += k;
+  if (W.n <= 4u) {
+    W.w |= uint64_t(W.nxt) << (32u - 8u * W.n);
+    W.n += 4u;
+    W.nxt = ldg_be32(W.words);
+    W.words++;
+  }
+  return e & 0xFFu;
+}
+
+// Bytes a fast 16-symbol chunk needs left in the stream: 32 consumed at most,
+// plus the window's 12-byte reach.
+constexpr uint32_t kWinGuard = 48;
+
 // Builds the decode table of one plane from its 256 x u16 frequency table
 // into lut[4096] (cum[257] and red[8] are shared scratch).  All 256 threads of
 // the block participate.  *degenerate = 1 when every frequency is zero.
@@ -93,16 +144,42 @@ __device__ __forceinline__ void build_lut(uint32_t* lut, uint32_t* cum, uint32_t
   const uint32_t total = cum[256];
   if (tid == 0) *degenerate = (total == 0);
   if (total == 4096u) {
-    for (int slot = tid; slot < 4096; slot += 256) {
-      // last symbol s with cum[s] <= slot (zero-frequency symbols are skipped)
-      int lo = 0, hi = 256;
-      while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (cum[mid] <= uint32_t(slot)) lo = mid; else hi = mid - 1;
-      }
-      uint32_t c = cum[lo];
-      uint32_t fs = cum[lo + 1] - c;
-      lut[slot] = uint32_t(lo) | ((fs - 1u) << 8) | ((uint32_t(slot) - c) << 20);
+    // slot -> symbol without searching: mark each symbol's first slot, then a
+    // block-wide running maximum over the 4096 slots (16 per thread).
+    uint32_t* mark = lut;  // reused as the marker array, overwritten below
+    const uint32_t base_slot = uint32_t(tid) * 16u;
+#pragma unroll
+    for (int j = 0; j < 16; j++) mark[base_slot + j] = 0;
+    __syncthreads();
+    if (f) mark[cum[tid]] = uint32_t(tid) + 1u;
+    __syncthreads();
+    uint32_t m[16];
+    uint32_t run = 0;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      run = max(run, mark[base_slot + j]);
+      m[j] = run;
+    }
+    // exclusive prefix maximum of the per-thread maxima
+    uint32_t incl = run;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl = max(incl, n);
+    }
+    __syncthreads();
+    if (lane == 31) red[warp] = incl;
+    __syncthreads();
+    uint32_t before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+    if (lane == 0) before = 0;
+    for (int w = 0; w < warp; w++) before = max(before, red[w]);
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+      const uint32_t s1 = max(before, m[j]);  // symbol + 1 owning this slot
+      const uint32_t sym = s1 - 1u;
+      const uint32_t c = cum[sym];
+      const uint32_t fs = cum[sym + 1] - c;
+      const uint32_t slot = base_slot + uint32_t(j);
+      lut[slot] = sym | ((fs - 1u) << 8) | ((slot - c) << 20);
     }
   }
   __syncthreads();

@@ -95,41 +95,52 @@ __device__ __forceinline__ uint64_t load8(const uint8_t* p) {
   return sh ? (lo >> sh) | (hi << (64u - sh)) : lo;
 }
 
-// Backward bit reader (RFC 8878 4.1): the stream is read from its last byte
-// towards its first, skipping the final byte's leading zeros and its 1 marker.
-// `pos` counts unread bits; a 64-bit window holds bits [wlo, wlo+64).
-struct BRead {
+// Backward bit reader (RFC 8878 4.1: a stream is read from its last byte
+// towards its first, after the final byte's leading zeros and 1 marker): the next unread bits are left-aligned in a 64-bit
+// window (stream bit pos-1 at bit 63); `vb` valid bits; refilled 32 bits at a
+// time.  Reading n <= 32 bits is a shift of the window's high word.
+struct BitIn {
   const uint8_t* p;
-  int64_t pos, wlo;
+  int32_t pos;  // unread bits left in the stream
+  int32_t vb;   // valid bits at the top of w (vb <= pos + 32 near the start)
   uint64_t w;
 
+  __device__ __forceinline__ uint32_t bits32_at(int32_t q) const {  // stream bits [q, q+32), zeros below 0
+    if (q >= 0) return uint32_t(load8(p + (q >> 3)) >> (q & 7));
+    if (q <= -32) return 0u;
+    return uint32_t(load8(p) << (-q));
+  }
   __device__ __forceinline__ bool init(const uint8_t* s, uint32_t len) {
     p = s;
     if (len == 0) return false;
     const uint32_t last = __ldg(s + len - 1);
     if (!last) return false;
-    pos = int64_t(8) * (len - 1) + (31 - __clz(last));
+    pos = int32_t(8 * (len - 1) + (31 - __clz(last)));
+    w = 0;
+    vb = 0;
+    refill();
     refill();
     return true;
   }
-  __device__ __forceinline__ void refill() {
-    int64_t lo = pos - 57;
-    if (lo < 0) lo = 0;
-    wlo = lo & ~int64_t(7);
-    w = load8(p + (wlo >> 3));
+  __device__ __forceinline__ void refill() {  // requires vb <= 32
+    w |= uint64_t(bits32_at(pos - vb - 32)) << (32 - vb);
+    vb += 32;
   }
-  __device__ __forceinline__ void ensure(int nb) {
-    if (pos - wlo < nb && wlo > 0) refill();
+  __device__ __forceinline__ void ensure(int n) {
+    if (vb < n) refill();
   }
-  __device__ __forceinline__ uint32_t peek(int nb) const {
-    const int64_t q = pos - nb - wlo;
-    const uint64_t v = q >= 0 ? (w >> q) : (w << (-q));
-    return uint32_t(v & ((1ull << nb) - 1));
+  __device__ __forceinline__ uint32_t top(int n) const {  // 1 <= n <= 32
+    return uint32_t(w >> 32) >> (32 - n);
   }
-  __device__ __forceinline__ uint32_t read(int nb) {
-    if (nb == 0) return 0;
-    const uint32_t v = peek(nb);
-    pos -= nb;
+  __device__ __forceinline__ void skip(int n) {
+    w <<= n;
+    vb -= n;
+    pos -= n;
+  }
+  __device__ __forceinline__ uint32_t read(int n) {  // 0 <= n <= 32
+    if (n == 0) return 0;
+    const uint32_t v = top(n);
+    skip(n);
     return v;
   }
 };
@@ -171,6 +182,7 @@ __device__ void fse_build_dev(const ZFse& f, uint32_t* t, uint16_t* next, int* a
 }
 
 struct K1Shared {
+  uint32_t huf3[2048];  // up to 3 symbols per lookup: s0|s1<<8|s2<<16|bits<<24|count<<28
   uint16_t huf[2048];
   uint16_t sstart[256];
   uint32_t ll[512], of[256], ml[512];
@@ -219,6 +231,25 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     for (uint32_t i = 0; i < len; i++) sh.huf[st + i] = e;
   }
   __syncwarp();
+  // multi-symbol entries: greedily chain codes while they fit in maxbits
+  const uint32_t tsize = 1u << maxbits, mask = tsize - 1;
+  for (uint32_t i = lane; i < tsize; i += 32) {
+    uint32_t e0 = sh.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
+    const uint32_t e1 = sh.huf[(i << l0) & mask], l1 = e1 >> 8;
+    if (bits + l1 <= uint32_t(maxbits)) {
+      syms |= (e1 & 0xFFu) << 8;
+      bits += l1;
+      cnt = 2;
+      const uint32_t e2 = sh.huf[(i << bits) & mask], l2 = e2 >> 8;
+      if (bits + l2 <= uint32_t(maxbits)) {
+        syms |= (e2 & 0xFFu) << 16;
+        bits += l2;
+        cnt = 3;
+      }
+    }
+    sh.huf3[i] = syms | (bits << 24) | (cnt << 28);
+  }
+  __syncwarp();
   const int streams = int(b.lit_streams);
   if (lane < streams) {
     const uint32_t seg = streams == 1 ? b.lit_regen : (b.lit_regen + 3) / 4;
@@ -226,15 +257,26 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     uint64_t off = b.src;
     for (int k = 0; k < lane; k++) off += b.lit_len[k];
     uint8_t* out = lit + uint32_t(lane) * seg;
-    BRead r;
+    BitIn r;
     bool ok = r.init(src + off, b.lit_len[lane]);
     if (ok) {
-      for (uint32_t i = 0; i < count; i++) {
+      uint32_t i = 0;
+      while (i + 3 <= count) {
         r.ensure(maxbits);
-        const uint32_t e = sh.huf[r.peek(maxbits)];
+        const uint32_t e = sh.huf3[r.top(maxbits)];
+        const uint32_t c = e >> 28;
         out[i] = uint8_t(e);
-        r.pos -= int64_t(e >> 8);
-        if (r.pos < 0) break;
+        if (c > 1) out[i + 1] = uint8_t(e >> 8);
+        if (c > 2) out[i + 2] = uint8_t(e >> 16);
+        i += c;
+        r.skip(int((e >> 24) & 15u));
+        if (r.pos < -32) break;
+      }
+      for (; i < count && r.pos >= -32; i++) {
+        r.ensure(maxbits);
+        const uint32_t e = sh.huf[r.top(maxbits)];
+        out[i] = uint8_t(e);
+        r.skip(int(e >> 8));
       }
       ok = (r.pos == 0);
     }
@@ -250,7 +292,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
   if (lane != 0) return;
   uint32_t rk[3] = {0, 1, 2}, rv[3] = {0, 0, 0};
   uint32_t sum_ml = 0, sum_ll = 0, st = 0;
-  BRead r;
+  BitIn r;
   if (!r.init(src + b.seq_src, b.seq_len)) {
     st = VOOM_ZSTD_ST_SEQUENCES;
   } else {
@@ -311,7 +353,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
         sml = (eML >> 16) + r.read(int((eML >> 8) & 0xFFu));
         sof = (eOF >> 16) + r.read(int((eOF >> 8) & 0xFFu));
       }
-      if (r.pos < 0) break;
+      if (r.pos < -32) break;
     }
     if (r.pos != 0) st = VOOM_ZSTD_ST_SEQUENCES;
   }
