@@ -20,8 +20,8 @@
 // segment must land exactly on its successor checkpoint (integrity of the
 // compressed page; the tile CRC-32 was verified when the index was built).
 // Partial row sums meet in shared memory; the CTA applies the reference's
-// BF16 rounding points.  Kernels: router, route plan, gate/up+activation,
-// down, ordered combine.
+// BF16 rounding points.  Kernels: router, route plan, gate/up (one projection
+// tile per CTA), activation, down, ordered combine.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -198,42 +198,89 @@ __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restric
   }
 }
 
-// One thread: unique experts in first-appearance order (positions, then
-// slots), tokens per expert, and each token's contributions ordered by that
-// expert order (the order the reference accumulates them in).
-__global__ void moe_route_plan(Routes* r, uint32_t T, uint32_t k) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  r->T = T;
-  r->k = k;
-  uint32_t nu = 0;
-  for (uint32_t p = 0; p < T * k; p++) {
-    const uint32_t e = r->idx[p];
-    uint32_t u = 0;
-    while (u < nu && r->expert[u] != e) u++;
-    if (u == nu) {
-      r->expert[nu] = e;
-      r->ntok[nu] = 0;
-      nu++;
-    }
-    r->ntok[u]++;
+// Route plan, one CTA of kMaxTK threads (thread p = route position t*k + j):
+// unique experts in first-appearance order (positions, then slots), tokens per
+// expert, route rows grouped by expert in position order, and each token's
+// contributions ordered by that expert order (the order the reference
+// accumulates them in).
+__global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, uint32_t k) {
+  __shared__ uint32_t s_first[kMaxE];  // first position of each expert
+  __shared__ uint32_t s_cnt[kMaxE];    // routes per expert
+  __shared__ uint32_t s_idx[kMaxTK];
+  __shared__ uint32_t s_u[kMaxTK];     // unique index of position p's expert
+  __shared__ uint32_t s_scan[kMaxTK];
+  __shared__ uint32_t s_ntok[kMaxTK];  // routes of unique expert u
+  __shared__ uint32_t s_warp[kMaxTK / 32];
+  __shared__ uint32_t s_nu;
+  const uint32_t p = threadIdx.x, n = T * k, lane = p & 31, warp = p >> 5;
+  for (uint32_t e = p; e < kMaxE; e += blockDim.x) {
+    s_first[e] = 0xFFFFFFFFu;
+    s_cnt[e] = 0;
   }
-  r->n_unique = nu;
-  r->uoff[0] = 0;
-  for (uint32_t u = 0; u < nu; u++) r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
-  uint32_t fill[kMaxTK];
-  for (uint32_t u = 0; u < nu; u++) fill[u] = 0;
-  for (uint32_t p = 0; p < T * k; p++) {
-    uint32_t u = 0;
-    while (r->expert[u] != r->idx[p]) u++;
-    const uint32_t q = r->uoff[u] + fill[u]++;
-    r->upair[q] = p / k;
-    r->w_bf16[q] = uint16_t(f2bf(r->w[p]));
+  __syncthreads();
+  const uint32_t e = p < n ? r->idx[p] : 0u;
+  if (p < n) {
+    s_idx[p] = e;
+    atomicMin(&s_first[e], p);
+    atomicAdd(&s_cnt[e], 1u);
   }
-  for (uint32_t t = 0; t < T; t++) {
-    uint32_t n = 0;
-    for (uint32_t u = 0; u < nu; u++)
-      for (uint32_t q = r->uoff[u]; q < r->uoff[u + 1]; q++)
-        if (r->upair[q] == t) r->tok_order[t * k + n++] = q;
+  __syncthreads();
+  // exclusive scan of "p is its expert's first position" -> unique index
+  const uint32_t flag = (p < n && s_first[e] == p) ? 1u : 0u;
+  uint32_t v = flag;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, v, o);
+    if (lane >= o) v += t;
+  }
+  if (lane == 31) s_warp[warp] = v;
+  __syncthreads();
+  uint32_t before = 0;
+  for (uint32_t w = 0; w < warp; w++) before += s_warp[w];
+  s_scan[p] = before + v - flag;
+  __syncthreads();
+  const uint32_t u = p < n ? s_scan[s_first[e]] : 0u;
+  if (p < n) s_u[p] = u;
+  if (flag) {
+    r->expert[u] = e;
+    r->ntok[u] = s_cnt[e];
+    s_ntok[u] = s_cnt[e];
+  }
+  if (p == blockDim.x - 1) {
+    s_nu = before + v;
+    r->n_unique = before + v;
+    r->T = T;
+    r->k = k;
+  }
+  __syncthreads();
+  // uoff: exclusive scan of ntok in unique order (thread u holds ntok[u])
+  const uint32_t nu = s_nu;
+  const uint32_t cnt_u = p < nu ? s_ntok[p] : 0u;
+  uint32_t c = cnt_u;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, c, o);
+    if (lane >= o) c += t;
+  }
+  __syncthreads();
+  if (lane == 31) s_warp[warp] = c;
+  __syncthreads();
+  uint32_t base = 0;
+  for (uint32_t w = 0; w < warp; w++) base += s_warp[w];
+  if (p < nu) s_scan[p] = base + c - cnt_u;
+  if (p == 0) r->uoff[0] = 0;
+  if (p < nu) r->uoff[p + 1] = base + c;
+  __syncthreads();
+  if (p < n) {
+    // route row: uoff[u] + earlier positions with the same expert
+    uint32_t rank = 0;
+    for (uint32_t q = 0; q < p; q++) rank += (s_idx[q] == e) ? 1u : 0u;
+    const uint32_t row = s_scan[u] + rank;
+    r->upair[row] = p / k;
+    r->w_bf16[row] = uint16_t(f2bf(r->w[p]));
+    // this token's routes ordered by unique index (experts of a token are distinct)
+    const uint32_t t = p / k, t0 = t * k;
+    uint32_t pos = 0;
+    for (uint32_t j = 0; j < k; j++) pos += (s_u[t0 + j] < u) ? 1u : 0u;
+    r->tok_order[t0 + pos] = row;
   }
 }
 
@@ -252,7 +299,7 @@ struct GemvShared {
   uint32_t cum[2][257];
   uint32_t red[8];
   uint32_t degenerate[2];
-  float acc[2][128][kTok];  // [projection][row in tile][token]
+  float acc[1][128][kTok];  // [0][row in tile][token]
   uint32_t tok[kTok];
   uint32_t status;
 };
@@ -329,41 +376,49 @@ __device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t,
       }
       const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
       const unsigned mask = 0x3u << (tid & 30u);
-      uint32_t done = 0;
-      if (every >= 16 && __all_sync(mask, (r.len - r.cur >= kWinGuard) && (r.x >= kRansL))) {
+      const bool degenerate = sh.degenerate[lane] != 0;
+      const bool last = (p + 1 == nseg);
+      const uint32_t x0 = r.x, c0 = r.cur;
+      auto landed = [&]() {
+        return last ? (r.cur == r.len) : (r.x == ck[p * 4 + lane * 2] && r.cur == ck[p * 4 + lane * 2 + 1]);
+      };
+      // Whole segment on the clamped window; a pair that does not land where
+      // the exact decoder did (a stream that runs out of bytes) redoes the
+      // segment on the exact path.
+      bool exact = (every & 15u) || !__all_sync(mask, !degenerate && win_can_open(r));
+      if (!exact) {
         Window W;
         win_open(W, r);
-        for (;;) {
+        uint32_t x = r.x;
+        for (uint32_t done = 0; done < every; done += 16) {
           uint32_t a[4];
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            const uint32_t s0 = rans_step_win(lut_s, r, W);
-            const uint32_t s1 = rans_step_win(lut_s, r, W);
-            const uint32_t s2 = rans_step_win(lut_s, r, W);
-            const uint32_t s3 = rans_step_win(lut_s, r, W);
-            a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
-          }
+          win_decode16(lut_s, x, W, a);
           const uint4 w = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
           dot8<NT>(w, act, ld, sh.tok, ntk, k0 + done + 8 * lane, acc);
-          done += 16;
-          if (done + 16 > every || !__all_sync(mask, r.len - r.cur >= kWinGuard)) break;
         }
-      }
-      // exact tail in lockstep: both planes have the same count left
-      for (; done < every; done++) {
-        const uint32_t s = rans_step_exact(lut_s, false, r);
-        const uint32_t o = __shfl_xor_sync(mask, s, 1);
-        if (lane == 0) {
-          const float w = bf2f(s | (o << 8));
+        r.x = x;
+        r.cur = win_cur(W);
+        if (__any_sync(mask, !landed())) {
+          exact = true;
+          r.x = x0;
+          r.cur = c0;
 #pragma unroll
-          for (int j = 0; j < NT; j++)
-            if (j < int(ntk)) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
+          for (int j = 0; j < NT; j++) acc[j] = 0.f;
         }
       }
-      const bool last = (p + 1 == nseg);
-      const bool landed = last ? (r.cur == r.len)
-                               : (r.x == ck[p * 4 + lane * 2] && r.cur == ck[p * 4 + lane * 2 + 1]);
-      if (!landed) atomicOr(&sh.status, 1u);
+      if (exact) {  // lockstep pair: both planes decode `every` symbols
+        for (uint32_t done = 0; done < every; done++) {
+          const uint32_t s = rans_step_exact(lut_s, degenerate, r);
+          const uint32_t o = __shfl_xor_sync(mask, s, 1);
+          if (lane == 0) {
+            const float w = bf2f(s | (o << 8));
+#pragma unroll
+            for (int j = 0; j < NT; j++)
+              if (j < int(ntk)) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
+          }
+        }
+        if (!landed()) atomicOr(&sh.status, 1u);
+      }
     }
   }
   // pair reduce, then rows meet in shared memory
@@ -395,35 +450,62 @@ __device__ __forceinline__ bool setup_tokens(GemvShared& sh, const Routes* R, ui
   return true;
 }
 
-// gate + up tiles of one routed expert -> activation rows (BF16) per token.
-// NT = tokens per CTA (1, 2, 4 or 8): registers scale with it.
+// One gate or up tile of one routed expert (blockIdx.x = 2 * tile + proj) ->
+// BF16 rows g (gate) or u (up) per token; moe_act combines them.  NT = tokens
+// per CTA (1, 2, 4 or 8): registers scale with it.
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 4) moe_gate_up(const voom_expert_pages* __restrict__ pages,
                                                            const Routes* __restrict__ R,
                                                            const uint16_t* __restrict__ h, uint32_t H, uint32_t I,
-                                                           uint16_t* __restrict__ act_out, uint32_t* status) {
+                                                           uint16_t* __restrict__ g_out,
+                                                           uint16_t* __restrict__ u_out, uint32_t* status) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
-  const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
+  const uint32_t t = blockIdx.x >> 1, proj = blockIdx.x & 1u, u = blockIdx.y, grp = blockIdx.z;
   uint32_t ntk;
   if (!setup_tokens<NT>(sh, R, u, grp, &ntk, status)) return;
   const voom_expert_pages& E = pages[R->expert[u]];
-  if (t >= E.gate.n_tiles) return;
-  for (int i = threadIdx.x; i < 2 * 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
+  const voom_expert_proj& P = proj ? E.up : E.gate;
+  if (t >= P.n_tiles) return;
+  for (int i = threadIdx.x; i < 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
   if (threadIdx.x == 0) sh.status = 0;
   __syncthreads();
-  gemv_tile<NT>(sh, E.gate, t, 0, h, H, ntk);
-  gemv_tile<NT>(sh, E.up, t, 1, h, H, ntk);
-  const voom_rans_tile tl = E.gate.tiles[t];
+  gemv_tile<NT>(sh, P, t, 0, h, H, ntk);
+  const voom_rans_tile tl = P.tiles[t];
   const uint32_t rows = tl.raw_len / (2u * H), row0 = uint32_t(tl.dst / (2u * H));
+  uint16_t* out = proj ? u_out : g_out;
   for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
     const uint32_t row = q / ntk, j = q % ntk;
-    const float g = rbf(sh.acc[0][row][j]), up = rbf(sh.acc[1][row][j]);
-    const float s = rbf(1.f / (1.f + __expf(-g)));
-    const float a = rbf(rbf(s * g) * up);
-    act_out[size_t(R->uoff[u] + grp * NT + j) * I + row0 + row] = uint16_t(f2bf(a));
+    out[size_t(R->uoff[u] + grp * NT + j) * I + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
   }
   if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
+}
+
+// SwiGLU of the route rows, in place over g: a = bf16(bf16(bf16(sigmoid(g)) * g) * u)
+// (layer_runner.py _swiglu :185-190).  8 columns per thread.
+__global__ void moe_act(const Routes* __restrict__ R, uint16_t* __restrict__ g, const uint16_t* __restrict__ up,
+                        uint32_t I) {
+  const uint32_t row = blockIdx.y;
+  if (row >= R->uoff[R->n_unique]) return;
+  const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 8u;
+  if (c >= I) return;
+  uint4* gp = reinterpret_cast<uint4*>(g + size_t(row) * I + c);
+  const uint4 gv = *gp;
+  const uint4 uv = *reinterpret_cast<const uint4*>(up + size_t(row) * I + c);
+  const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int hlf = 0; hlf < 2; hlf++) {
+      const float gf = bf2f((gw[q] >> (16 * hlf)) & 0xFFFFu), uf = bf2f((uw[q] >> (16 * hlf)) & 0xFFFFu);
+      const float sg = rbf(1.f / (1.f + __expf(-gf)));
+      r |= f2bf(rbf(rbf(sg * gf) * uf)) << (16 * hlf);
+    }
+    o[q] = r;
+  }
+  *gp = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // down tile of one routed expert -> y rows (BF16) per token.
@@ -483,7 +565,7 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   s.routes = o; o = align256(o + sizeof(Routes));
   s.h = o; o = align256(o + uint64_t(T) * H * 2 + 16);
   s.act = o; o = align256(o + uint64_t(T) * k * I * 2 + 16);
-  s.y = o; o = align256(o + uint64_t(T) * k * H * 2 + 16);
+  s.y = o; o = align256(o + uint64_t(T) * k * (H > I ? H : I) * 2 + 16);  // u rows, then y rows
   s.total = o;
   return s;
 }
@@ -491,28 +573,35 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
 
 template <int NT>
 int launch_gemv_nt(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
-                   uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t gate_tiles,
-                   uint32_t down_tiles, uint32_t* d_status, cudaStream_t st) {
+                   uint16_t* ubuf, uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique,
+                   uint32_t max_rows, uint32_t gate_tiles, uint32_t down_tiles, uint32_t* d_status,
+                   cudaStream_t st) {
   const uint32_t groups = (T + NT - 1) / NT;
   const size_t smem = sizeof(GemvShared);
   if (cudaFuncSetAttribute(moe_gate_up<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
           cudaSuccess ||
       cudaFuncSetAttribute(moe_down<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return VOOM_E_CUDA;
-  moe_gate_up<NT><<<dim3(gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, d_status);
+  moe_gate_up<NT><<<dim3(2 * gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, ubuf,
+                                                                                   d_status);
+  moe_act<<<dim3((I / 8 + 127) / 128, max_rows), 128, 0, st>>>(R, act, ubuf, I);
   moe_down<NT><<<dim3(down_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
   return VOOM_OK;
 }
 
-// gate/up then down for every routed expert; tokens per CTA chosen from T
-// (an expert sees at most T tokens).
-int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act, uint16_t* y,
-                uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t gate_tiles, uint32_t down_tiles,
-                uint32_t* d_status, cudaStream_t st) {
-  if (T == 1) return launch_gemv_nt<1>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
-  if (T == 2) return launch_gemv_nt<2>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
-  if (T <= 4) return launch_gemv_nt<4>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
-  return launch_gemv_nt<8>(d_pages, R, h, act, y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+// gate/up, activation, then down for every routed expert; tokens per CTA
+// chosen from T (an expert sees at most T tokens).  ubuf holds max_rows x I.
+int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
+                uint16_t* ubuf, uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique,
+                uint32_t max_rows, uint32_t gate_tiles, uint32_t down_tiles, uint32_t* d_status, cudaStream_t st) {
+#define VOOM_GEMV(NT)                                                                                         \
+  launch_gemv_nt<NT>(d_pages, R, h, act, ubuf, y, T, H, I, n_unique, max_rows, gate_tiles, down_tiles, d_status, \
+                     st)
+  if (T == 1) return VOOM_GEMV(1);
+  if (T == 2) return VOOM_GEMV(2);
+  if (T <= 4) return VOOM_GEMV(4);
+  return VOOM_GEMV(8);
+#undef VOOM_GEMV
 }
 
 }  // namespace
@@ -540,9 +629,10 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, top_k, norm_topk, h,
                                       R);
-  moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
+  moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
-  const int rc = launch_gemv(d_pages, R, h, act, y, T, H, I, max_unique, gate_tiles, down_tiles, d_status, st);
+  const int rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
+                             d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
@@ -581,9 +671,11 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
   if (cudaMemsetAsync(d_y, 0, size_t(T) * top_k * H * 2, st) != cudaSuccess) return VOOM_E_CUDA;
   moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, top_k, norm_topk,
                                       h, R);
-  moe_route_plan<<<1, 32, 0, st>>>(R, T, top_k);
+  moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
-  const int rc = launch_gemv(d_pages, R, h, act, d_y, T, H, I, max_unique, gate_tiles, down_tiles, d_status, st);
+  uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
+  const int rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
+                             d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
@@ -657,11 +749,12 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
     return VOOM_E_INVALID_ARG;
   if (T == 0 || n_unique == 0 || n_rows == 0 || n_rows > kMaxTK || n_unique > n_rows || H % 8 || I % 8)
     return VOOM_E_INVALID_ARG;
-  const uint64_t need = align256(sizeof(Routes)) + align256(uint64_t(n_rows) * I * 2 + 16);
-  if (scratch_bytes < need) return VOOM_E_CAPACITY;
+  const ScratchLayout L = layout(n_rows, H, I, 1);
+  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
   uint8_t* s = static_cast<uint8_t*>(d_scratch);
-  Routes* R = reinterpret_cast<Routes*>(s);
-  uint16_t* act = reinterpret_cast<uint16_t*>(s + align256(sizeof(Routes)));
+  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
+  uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // the route header lives in scratch: fill n_unique, T, expert, ntok, upair
   if (cudaMemcpyAsync(&R->expert[0], d_expert_ids, 4ull * n_unique, cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
@@ -669,7 +762,8 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
       cudaMemcpyAsync(&R->upair[0], d_upair, 4ull * n_rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return VOOM_E_CUDA;
   moe_route_offsets<<<1, 32, 0, st>>>(R, n_unique, T);
-  const int rc = launch_gemv(d_pages, R, d_h, act, d_y, T, H, I, n_unique, gate_tiles, down_tiles, d_status, st);
+  const int rc = launch_gemv(d_pages, R, d_h, act, ubuf, d_y, T, H, I, n_unique, n_rows, gate_tiles, down_tiles,
+                             d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

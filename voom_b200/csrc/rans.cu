@@ -92,35 +92,52 @@ __device__ __forceinline__ void decode_generic(uint32_t lut_s, bool degenerate, 
 
 // Lockstep pair decode of up to `nchunks` x 16 symbols (low plane on the even
 // lane, high plane on the odd lane, both non-degenerate, `out` 16-byte
-// aligned).  A chunk runs on the windowed branch-free step only when both
-// lanes have >= kWinGuard payload bytes left and a normal state; otherwise the
-// pair stops and the caller finishes each plane with decode_generic.  Returns
-// chunks done.
+// aligned) on the windowed step.  The pair starts only when both lanes can
+// (win_can_start) and continues while both windows have room for 16 more
+// steps; the caller finishes each plane with decode_generic.  Returns chunks
+// done, with r.x / r.cur advanced past them.
 __device__ __forceinline__ uint32_t decode_pair_fast(uint32_t lut_s, PlaneRun& r, uint32_t nchunks,
                                                      uint32_t first, uint8_t* out, uint32_t lane,
                                                      uint32_t* ckpt, uint32_t every,
                                                      uint32_t limit_k, unsigned mask) {
   uint32_t c = 0;
-  if (nchunks == 0 || !__all_sync(mask, (r.len - r.cur >= kWinGuard) && (r.x >= kRansL))) return 0;
+  if (nchunks == 0 || !__all_sync(mask, win_can_start(r))) return 0;
   Window W;
   win_open(W, r);
+  uint32_t x = r.x;
   for (;;) {
-    if ((c & 3u) == 0) asm volatile("prefetch.global.L1 [%0];" ::"l"(r.payload + r.cur + 256));
+    if ((c & 3u) == 0) asm volatile("prefetch.global.L1 [%0];" ::"l"(W.words + W.j + 64));
     uint32_t a[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const uint32_t s0 = rans_step_win(lut_s, r, W);
-      const uint32_t s1 = rans_step_win(lut_s, r, W);
-      const uint32_t s2 = rans_step_win(lut_s, r, W);
-      const uint32_t s3 = rans_step_win(lut_s, r, W);
-      a[j] = s0 | (s1 << 8) | (s2 << 16) | (s3 << 24);
-    }
+    win_decode16(lut_s, x, W, a);
     *reinterpret_cast<uint4*>(out + 32u * c + 16u * lane) = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
     c++;
-    if (ckpt) record_ckpt(ckpt, first + 16u * c, every, limit_k, lane, r);
-    if (c == nchunks || !__all_sync(mask, r.len - r.cur >= kWinGuard)) break;
+    if (ckpt) {
+      r.x = x;
+      r.cur = win_cur(W);
+      record_ckpt(ckpt, first + 16u * c, every, limit_k, lane, r);
+    }
+    if (c == nchunks || !__all_sync(mask, win_room(W, r.len))) break;
   }
+  r.x = x;
+  r.cur = win_cur(W);
   return c;
+}
+
+// One full segment (`every` symbols, a multiple of 16) of a lane pair on the
+// clamped window (win_can_open holds for both lanes; `out` 16-byte aligned).
+// r.x / r.cur end where the window stopped; the caller checks the landing.
+__device__ __forceinline__ void decode_pair_seg(uint32_t lut_s, PlaneRun& r, uint32_t every, uint8_t* out,
+                                                uint32_t lane, unsigned mask) {
+  Window W;
+  win_open(W, r);
+  uint32_t x = r.x;
+  for (uint32_t c = 0; c < every / 16u; c++) {
+    uint32_t a[4];
+    win_decode16(lut_s, x, W, a);
+    *reinterpret_cast<uint4*>(out + 32u * c + 16u * lane) = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
+  }
+  r.x = x;
+  r.cur = win_cur(W);
 }
 
 __device__ __forceinline__ void load_crc_tables(SharedPlanes& sh) {
@@ -248,17 +265,28 @@ __global__ void __launch_bounds__(kThreads, 2) rans_indexed_kernel(
       plane_start(r, src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload, x0,
                   c0, seg != 0);
     }
-    // The pair runs the fast path together only when both planes have a full
-    // segment; otherwise each lane finishes on the exact path.
+    // The pair decodes a full segment on the clamped window when both planes
+    // have one; a pair that does not land where the exact decoder did (a
+    // stream that runs out of bytes) redoes it, like every partial segment,
+    // on the exact path.
     const uint32_t cnt_high = first < n_high ? min(every, n_high - first) : 0u;
+    const bool last = (seg + 1 > nb) || ((seg + 1) * every > n);
     uint32_t done = 0;
-    if (fast_ok && cnt_high == every)
-      done = 16u * decode_pair_fast(lut_s, r, every / 16, first, out + tl.dst + 2u * first, lane, nullptr,
-                                    every, 0, mask);
+    if (fast_ok && cnt_high == every && (every & 15u) == 0 && __all_sync(mask, win_can_open(r))) {
+      const uint32_t x0 = r.x, c0 = r.cur;
+      decode_pair_seg(lut_s, r, every, out + tl.dst + 2u * first, lane, mask);
+      const bool landed = last ? (r.cur == r.len)
+                               : (r.x == ck[seg * 4 + lane * 2] && r.cur == ck[seg * 4 + lane * 2 + 1]);
+      if (__any_sync(mask, !landed)) {
+        r.x = x0;
+        r.cur = c0;
+      } else {
+        done = every;
+      }
+    }
     if (active) {
       decode_generic(lut_s, sh.degenerate[lane], r, cnt - done, first + done,
                      out + tl.dst + lane + 2u * (first + done), nullptr, every, 0, lane);
-      const bool last = (seg + 1 > nb) || ((seg + 1) * every > n);
       if (last) {
         if (r.cur != r.len) bad |= lane ? VOOM_RANS_ST_HIGH_TRAILING : VOOM_RANS_ST_LOW_TRAILING;
       } else if (r.x != ck[seg * 4 + lane * 2] || r.cur != ck[seg * 4 + lane * 2 + 1]) {

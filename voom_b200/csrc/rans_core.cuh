@@ -22,15 +22,6 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   return v;
 }
 
-// The 4 bytes at p as a big-endian word (first byte most significant), from
-// two aligned L1-cached loads.  p[0..7] must be readable.
-__device__ __forceinline__ uint32_t load4_be(const uint8_t* p) {
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-  const uint32_t v = __funnelshift_r(__ldg(w), __ldg(w + 1), uint32_t(a & 3u) * 8u);
-  return __byte_perm(v, 0, 0x0123);
-}
-
 struct PlaneRun {
   const uint8_t* payload;  // plane payload: u32 initial state, renorm bytes
   uint32_t x, cur, len;
@@ -55,71 +46,114 @@ __device__ __forceinline__ uint32_t rans_step_exact(uint32_t lut_s, bool degener
   return sym;
 }
 
-// Branch-free symbol step for the bulk of a stream.  Preconditions: x >= L,
-// non-degenerate table, at least 8 payload bytes left.  From x >= 2^23 and
-// freq >= 1 the new state is >= 2^11, so at most two renormalisation bytes
-// are needed: k = (x < 2^23) + (x < 2^15).
-__device__ __forceinline__ uint32_t rans_step_fast(uint32_t lut_s, PlaneRun& r) {
-  const uint32_t be = load4_be(r.payload + r.cur);
-  const uint32_t e = lds32(lut_s + 4u * (r.x & 4095u));
-  const uint32_t xs = r.x >> 12;
-  uint32_t x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
-  const uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
-  r.x = __funnelshift_l(be, x, 8u * k);
-  r.cur += k;
-  return e & 0xFFu;
-}
-
-// Renormalisation bytes of a fast run held in registers: a 64-bit window of
-// the stream's next bytes (left-aligned, first byte most significant) plus one
-// preloaded aligned word.  A step shifts k bytes out of the window; the window
-// takes the preloaded word once 4 or fewer bytes remain, and only then is a
-// new word loaded.  Per step about a third of a warp's lanes issue a load,
-// against two unaligned loads per lane for load4_be, and the load result is
-// not needed before the following refill.  Reads reach at most cur + 11.
+// Renormalisation bytes of a fast run held in registers: a 64-bit window
+// (hi:lo) of the stream's next bytes, left-aligned, with nb valid bits, plus
+// one preloaded aligned word (nxt).  A step shifts 8k bits out of the window;
+// every second step the window takes nxt if 32 or fewer bits remain, and only
+// then is the next word loaded.  Two steps use at most 32 bits, so the window
+// never runs dry.  About a third of a warp's lanes load on a refill step, the
+// load has two steps to land, and the bookkeeping is a few register ops.
 struct Window {
-  const uint32_t* words;  // next word to load
-  uint64_t w;             // bytes [cur, cur + n) left-aligned
-  uint32_t n;             // valid bytes in w: 5..8 before each step
-  uint32_t nxt;           // big-endian word holding bytes [cur + n, cur + n + 4)
+  const uint32_t* words;  // aligned words of the stream; words[j] is loaded next
+  uint32_t j;
+  uint32_t jlast;         // last word holding a payload byte: loads clamp to it
+  uint32_t hi, lo;        // window bits, first byte at the top of hi
+  uint32_t nb;            // valid bits in (hi:lo), a multiple of 8
+  uint32_t nxt;           // big-endian words[j - 1]: the bytes after the window
+  uint32_t base;          // payload offset of words[0]
 };
 
 __device__ __forceinline__ uint32_t ldg_be32(const uint32_t* p) { return __byte_perm(__ldg(p), 0, 0x0123); }
 
-// Opens a window at r.cur.  Payload bytes [cur - 3, cur + 12) must be readable.
+// Opens a window at r.cur (requires 4 <= cur < len).  Loads never go past the
+// aligned word that holds the payload's last byte, and an aligned word that
+// holds a byte of a buffer lies inside that buffer's allocation, so every
+// load is in bounds whatever the stream holds.  Bytes past the payload end
+// enter the window only when a stream asks for more bytes than it has; the
+// reference encoder's streams never do (they end at state L with every byte
+// consumed), and callers detect it by the landing check (cursor past len).
 __device__ __forceinline__ void win_open(Window& W, const PlaneRun& r) {
   const uintptr_t a = reinterpret_cast<uintptr_t>(r.payload) + r.cur;
-  const uint32_t* p = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
   const uint32_t s = uint32_t(a & 3u);
-  const uint64_t v = (uint64_t(ldg_be32(p)) << 32) | ldg_be32(p + 1);
-  W.w = v << (8u * s);
-  W.n = 8u - s;
-  W.nxt = ldg_be32(p + 2);
-  W.words = p + 3;
+  W.words = reinterpret_cast<const uint32_t*>(a - s);
+  W.base = r.cur - s;
+  W.jlast = (r.len - 1u - W.base) >> 2;
+  const uint32_t w0 = ldg_be32(W.words), w1 = ldg_be32(W.words + min(1u, W.jlast));
+  W.hi = __funnelshift_l(w1, w0, 8u * s);
+  W.lo = w1 << (8u * s);
+  W.nb = 64u - 8u * s;
+  W.nxt = ldg_be32(W.words + min(2u, W.jlast));
+  W.j = 3;
 }
 
-// Same arithmetic as rans_step_fast with the bytes taken from the window.
-__device__ __forceinline__ uint32_t rans_step_win(uint32_t lut_s, PlaneRun& r, Window& W) {
-  const uint32_t e = lds32(lut_s + 4u * (r.x & 4095u));
-  const uint32_t xs = r.x >> 12;
-  const uint32_t x = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
-  const uint32_t k = uint32_t(x < kRansL) + uint32_t(x < (kRansL >> 8));
-  r.x = __funnelshift_l(uint32_t(W.w >> 32), x, 8u * k);
-  W.w <<= 8u * k;
-  W.n -= k;
-  r.cur += k;
-  if (W.n <= 4u) {
-    W.w |= uint64_t(W.nxt) << (32u - 8u * W.n);
-    W.n += 4u;
-    W.nxt = ldg_be32(W.words);
-    W.words++;
+// Stream position of the window's first byte.
+__device__ __forceinline__ uint32_t win_cur(const Window& W) { return W.base + 4u * (W.j - 1u) - (W.nb >> 3); }
+
+// True when the next 16 steps (8 refills) stay inside a payload of `len` bytes.
+__device__ __forceinline__ bool win_room(const Window& W, uint32_t len) {
+  return W.base + 4u * (W.j + 8u) <= len;
+}
+
+__device__ __forceinline__ void win_refill(Window& W) {
+  const bool use = W.nb <= 32u;
+  const uint32_t m = use ? 0xFFFFFFFFu : 0u;
+  W.hi |= __funnelshift_rc(W.nxt, 0u, W.nb) & m;        // nxt >> nb
+  W.lo |= __funnelshift_lc(0u, W.nxt, 32u - W.nb) & m;  // nxt << (32 - nb)
+  W.nb += m & 32u;
+  // predicated load (no branch): lanes that keep their window skip the access
+  uint32_t raw = 0;
+  asm(
+      "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p ld.global.nc.u32 %0, [%1];\n\t}"
+      : "+r"(raw)
+      : "l"(W.words + min(W.j, W.jlast)), "r"(m));
+  W.nxt = use ? __byte_perm(raw, 0, 0x0123) : W.nxt;
+  W.j += m & 1u;
+}
+
+// One symbol; returns the table entry (symbol in its low byte).  Requires
+// L <= x < 2^31, which then holds after the step as well: the decoded state
+// y lies in [2^11, 2^31) and 8k = (clz(y) - 1) & ~7 brings it back to
+// [2^23, 2^31) -- the reference's byte-wise loop, k in {0, 1, 2}.
+__device__ __forceinline__ uint32_t rans_step_win(uint32_t lut_s, uint32_t& x, Window& W) {
+  const uint32_t e = lds32(lut_s + 4u * (x & 4095u));
+  const uint32_t xs = x >> 12;
+  const uint32_t y = ((e >> 8) & 4095u) * xs + xs + (e >> 20);
+  const uint32_t sh = (uint32_t(__clz(y)) - 1u) & ~7u;
+  x = __funnelshift_l(W.hi, y, sh);
+  W.hi = __funnelshift_l(W.lo, W.hi, sh);
+  W.lo <<= sh;
+  W.nb -= sh;
+  return e;
+}
+
+// Bytes 0 of four table entries, packed low to high.
+__device__ __forceinline__ uint32_t pack4(uint32_t e0, uint32_t e1, uint32_t e2, uint32_t e3) {
+  return __byte_perm(__byte_perm(e0, e1, 0x0040), __byte_perm(e2, e3, 0x0040), 0x5410);
+}
+
+// 16 symbols of one lane (4 words of 4 bytes), refilling every second step.
+__device__ __forceinline__ void win_decode16(uint32_t lut_s, uint32_t& x, Window& W, uint32_t a[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    win_refill(W);
+    const uint32_t e0 = rans_step_win(lut_s, x, W);
+    const uint32_t e1 = rans_step_win(lut_s, x, W);
+    win_refill(W);
+    const uint32_t e2 = rans_step_win(lut_s, x, W);
+    const uint32_t e3 = rans_step_win(lut_s, x, W);
+    a[q] = pack4(e0, e1, e2, e3);
   }
-  return e & 0xFFu;
 }
 
-// Bytes a fast 16-symbol chunk needs left in the stream: 32 consumed at most,
-// plus the window's 12-byte reach.
-constexpr uint32_t kWinGuard = 48;
+// Entry condition of a guarded windowed run (win_room checked per 16 steps).
+__device__ __forceinline__ bool win_can_start(const PlaneRun& r) {
+  return r.len >= r.cur + 48u && r.x >= kRansL && r.x < 0x80000000u;
+}
+
+// Entry condition of a clamped windowed run over a whole segment.
+__device__ __forceinline__ bool win_can_open(const PlaneRun& r) {
+  return r.cur >= 4u && r.len >= r.cur + 16u && r.x >= kRansL && r.x < 0x80000000u;
+}
 
 // Builds the decode table of one plane from its 256 x u16 frequency table
 // into lut[4096] (cum[257] and red[8] are shared scratch).  All 256 threads of
@@ -144,42 +178,13 @@ __device__ __forceinline__ void build_lut(uint32_t* lut, uint32_t* cum, uint32_t
   const uint32_t total = cum[256];
   if (tid == 0) *degenerate = (total == 0);
   if (total == 4096u) {
-    // slot -> symbol without searching: mark each symbol's first slot, then a
-    // block-wide running maximum over the 4096 slots (16 per thread).
-    uint32_t* mark = lut;  // reused as the marker array, overwritten below
-    const uint32_t base_slot = uint32_t(tid) * 16u;
-#pragma unroll
-    for (int j = 0; j < 16; j++) mark[base_slot + j] = 0;
-    __syncthreads();
-    if (f) mark[cum[tid]] = uint32_t(tid) + 1u;
-    __syncthreads();
-    uint32_t m[16];
-    uint32_t run = 0;
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-      run = max(run, mark[base_slot + j]);
-      m[j] = run;
-    }
-    // exclusive prefix maximum of the per-thread maxima
-    uint32_t incl = run;
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl = max(incl, n);
-    }
-    __syncthreads();
-    if (lane == 31) red[warp] = incl;
-    __syncthreads();
-    uint32_t before = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-    if (lane == 0) before = 0;
-    for (int w = 0; w < warp; w++) before = max(before, red[w]);
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-      const uint32_t s1 = max(before, m[j]);  // symbol + 1 owning this slot
-      const uint32_t sym = s1 - 1u;
-      const uint32_t c = cum[sym];
-      const uint32_t fs = cum[sym + 1] - c;
-      const uint32_t slot = base_slot + uint32_t(j);
-      lut[slot] = sym | ((fs - 1u) << 8) | ((slot - c) << 20);
+    // each warp fills the slots of every 8th symbol, 32 consecutive slots
+    // per store (conflict-free); symbols are interleaved so the few large
+    // ones land on different warps.
+    for (int sym = warp; sym < 256; sym += 8) {
+      const uint32_t c = cum[sym], fs = cum[sym + 1] - c;
+      const uint32_t hdr = uint32_t(sym) | ((fs - 1u) << 8);
+      for (uint32_t i = lane; i < fs; i += 32) lut[c + i] = hdr | (i << 20);
     }
   }
   __syncthreads();
