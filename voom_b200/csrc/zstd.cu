@@ -95,53 +95,65 @@ __device__ __forceinline__ uint64_t load8(const uint8_t* p) {
   return sh ? (lo >> sh) | (hi << (64u - sh)) : lo;
 }
 
-// Backward bit reader (RFC 8878 4.1: a stream is read from its last byte
-// towards its first, after the final byte's leading zeros and 1 marker): the next unread bits are left-aligned in a 64-bit
-// window (stream bit pos-1 at bit 63); `vb` valid bits; refilled 32 bits at a
-// time.  Reading n <= 32 bits is a shift of the window's high word.
-struct BitIn {
-  const uint8_t* p;
-  int32_t pos;  // unread bits left in the stream
-  int32_t vb;   // valid bits at the top of w (vb <= pos + 32 near the start)
-  uint64_t w;
+__device__ __forceinline__ uint32_t bfe32(uint32_t v, uint32_t pos, uint32_t len) {
+  uint32_t r;
+  asm("bfe.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(pos), "r"(len));
+  return r;
+}
 
-  __device__ __forceinline__ uint32_t bits32_at(int32_t q) const {  // stream bits [q, q+32), zeros below 0
-    if (q >= 0) return uint32_t(load8(p + (q >> 3)) >> (q & 7));
-    if (q <= -32) return 0u;
-    return uint32_t(load8(p) << (-q));
+// Register window over a backward bitstream for one lane: the unread bits
+// just below position P, left-aligned in (hi:lo) with vb of them valid,
+// refilled 32 bits at a time from aligned words that are loaded two refills
+// ahead (q0, q1), so a lane's loads are in flight long before they are needed
+// and do not depend on L1 keeping the line.  Words below the stream start
+// read as zero, as do the bits of word 0 below the stream's first byte.
+struct DownWin {
+  const uint32_t* w;
+  uint32_t mask0;  // keeps the stream's bits of word 0
+  uint32_t hi, lo, vb;
+  uint32_t q0, q1;
+  int32_t nidx;    // next word to load
+  int32_t P;       // unread stream bits
+
+  __device__ __forceinline__ uint32_t word(int32_t i) const {
+    const uint32_t v = __ldg(w + max(i, 0));
+    return i < 0 ? 0u : (i == 0 ? v & mask0 : v);
   }
-  __device__ __forceinline__ bool init(const uint8_t* s, uint32_t len) {
-    p = s;
-    if (len == 0) return false;
-    const uint32_t last = __ldg(s + len - 1);
-    if (!last) return false;
-    pos = int32_t(8 * (len - 1) + (31 - __clz(last)));
-    w = 0;
-    vb = 0;
-    refill();
-    refill();
-    return true;
+  __device__ __forceinline__ void init(const uint8_t* s, int32_t P0) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(s);
+    w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t boff = uint32_t(a & 3u) * 8u;
+    mask0 = ~((1u << boff) - 1u);
+    P = P0;
+    const int32_t A = P0 + int32_t(boff);  // aligned bit position, >= 1
+    const int32_t m = (A - 1) >> 5;
+    const uint32_t sh = uint32_t(32 * (m + 1) - A);  // 0..31
+    const uint32_t wm = word(m), wm1 = word(m - 1);
+    hi = __funnelshift_l(wm1, wm, sh);
+    lo = wm1 << sh;
+    vb = 64u - sh;
+    q0 = word(m - 2);
+    q1 = word(m - 3);
+    nidx = m - 4;
   }
-  __device__ __forceinline__ void refill() {  // requires vb <= 32
-    w |= uint64_t(bits32_at(pos - vb - 32)) << (32 - vb);
-    vb += 32;
-  }
-  __device__ __forceinline__ void ensure(int n) {
-    if (vb < n) refill();
-  }
-  __device__ __forceinline__ uint32_t top(int n) const {  // 1 <= n <= 32
-    return uint32_t(w >> 32) >> (32 - n);
-  }
-  __device__ __forceinline__ void skip(int n) {
-    w <<= n;
+  __device__ __forceinline__ void consume(uint32_t n) {  // n <= 31
+    hi = __funnelshift_l(lo, hi, n);
+    lo <<= n;
     vb -= n;
-    pos -= n;
+    P -= int32_t(n);
   }
-  __device__ __forceinline__ uint32_t read(int n) {  // 0 <= n <= 32
-    if (n == 0) return 0;
-    const uint32_t v = top(n);
-    skip(n);
-    return v;
+  // afterwards at least 32 bits are valid
+  __device__ __forceinline__ void refill() {
+    const bool use = vb <= 32u;
+    const uint32_t m = use ? 0xFFFFFFFFu : 0u;
+    hi |= __funnelshift_rc(q0, 0u, vb) & m;
+    lo |= __funnelshift_lc(0u, q0, 32u - vb) & m;
+    vb += m & 32u;
+    if (use) {
+      q0 = q1;
+      q1 = word(nidx);
+      nidx--;
+    }
   }
 };
 
@@ -186,6 +198,10 @@ struct K1Shared {
   uint16_t huf[2048];
   uint16_t sstart[256];
   uint32_t ll[512], of[256], ml[512];
+  // sequence decode cells: low word = state base | nbBits << 16 | extra bits << 24,
+  // high word = the code's baseline value (RFC 8878 3.1.1.3.2.1.1)
+  uint2 ll2[512], ml2[512];
+  uint4 sring[128];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 127
   uint16_t next[3][64];
   int al[3];
   uint32_t st;
@@ -193,21 +209,128 @@ struct K1Shared {
   uint32_t rep_kind[3], rep_val[3];
 };
 
-__device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh,
-                                uint8_t* lit) {
-  const int lane = threadIdx.x & 31;
+constexpr int kLitWarps = 4;                 // one warp per Huffman stream
+constexpr int kK1Threads = 32 * (kLitWarps + 1);  // + the sequence warp
+
+// Named barrier over the literal warps only (the sequence warp runs on).
+__device__ __forceinline__ void lit_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kLitWarps)); }
+
+// Write-combining byte output of one lane: bytes gather in a 64-bit register
+// and leave as aligned 8-byte stores; the partial first and last words go out
+// byte by byte, so a lane never writes outside its own range.  (A warp's lanes
+// write far-apart ranges, so byte stores would cost one L1 wavefront per lane
+// per byte.)
+struct ByteSink {
+  uint64_t* wp;   // aligned word being filled
+  uint64_t acc;
+  uint32_t k;     // bytes of the word filled (from its aligned start)
+  uint32_t k0;    // first byte of ours in the first word; 0 after it
+  __device__ __forceinline__ void init(uint8_t* dst) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(dst);
+    wp = reinterpret_cast<uint64_t*>(a & ~uintptr_t(7));
+    k = k0 = uint32_t(a & 7u);
+    acc = 0;
+  }
+  __device__ __forceinline__ void flush_bytes(uint32_t from, uint32_t to) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(wp);
+    for (uint32_t j = from; j < to; j++) b[j] = uint8_t(acc >> (8 * j));
+  }
+  // append the c (1..3) bytes of `syms` (low first)
+  __device__ __forceinline__ void put(uint32_t syms, uint32_t c) {
+    const uint64_t v = uint64_t(syms & (0xFFFFFFu >> (8 * (3 - c))));
+    acc |= v << (8 * k);
+    const uint64_t spill = k ? v >> (64 - 8 * k) : 0ull;  // bytes past the word
+    k += c;
+    if (k >= 8) {
+      if (k0) {
+        flush_bytes(k0, 8);
+        k0 = 0;
+      } else {
+        *wp = acc;
+      }
+      wp++;
+      acc = spill;
+      k -= 8;
+    }
+  }
+  __device__ __forceinline__ void finish() { flush_bytes(k0, k); }
+};
+
+// Huffman decode of one backward stream by one lane, from W.P down to the
+// first codeword boundary at or below `stop` (want < 0; out may be null to
+// count only), or of exactly `want` symbols.  Multi-symbol lookups never
+// cross `stop` (one lookup spans at most maxbits bits), so the exit is the
+// first true boundary at or below it whatever the grouping; in counted mode
+// they run while >= 3 symbols remain, like the serial decoder.  Returns the
+// symbols decoded.
+__device__ __forceinline__ uint32_t huf_run(const K1Shared& sh, DownWin& W, int32_t stop, uint32_t maxbits,
+                                            uint8_t* out, int32_t want) {
+  const uint32_t shift = 32u - maxbits;
+  uint32_t n = 0;
+  ByteSink bs;
+  if (out) bs.init(out);
+  if (want < 0) {  // every code is >= 1 bit (the planner checks the weights), so P falls
+    while (W.P - int32_t(maxbits) > stop) {
+      W.refill();
+      const uint32_t e = sh.huf3[W.hi >> shift];
+      const uint32_t c = e >> 28;
+      if (out) bs.put(e, c);
+      n += c;
+      W.consume(max(1u, (e >> 24) & 15u));
+    }
+    while (W.P > stop) {
+      W.refill();
+      const uint32_t e = sh.huf[W.hi >> shift];
+      if (out) bs.put(e, 1);
+      n++;
+      W.consume(max(1u, e >> 8));
+    }
+    if (out) bs.finish();
+    return n;
+  }
+  const uint32_t w = uint32_t(want);
+  while (n + 3 <= w && W.P >= -32) {
+    W.refill();
+    const uint32_t e = sh.huf3[W.hi >> shift];
+    const uint32_t c = e >> 28;
+    bs.put(e, c);
+    n += c;
+    W.consume(max(1u, (e >> 24) & 15u));
+  }
+  for (; n < w && W.P >= -32; n++) {
+    W.refill();
+    const uint32_t e = sh.huf[W.hi >> shift];
+    bs.put(e, 1);
+    W.consume(max(1u, e >> 8));
+  }
+  bs.finish();
+  return n;
+}
+
+// Literals section (RFC 8878 3.1.1.3.1) by the literal warps: raw / RLE by
+// all of them; Huffman streams one warp each.  A stream of B bits is cut into
+// 32 spans; lane j starts at the top of span j and decodes to the first
+// codeword boundary at or below the span's end (its exit).  Lane j+1 then
+// restarts at lane j's exit, and the pass repeats until no start moves: lane
+// 0 starts on the true first codeword, so after pass k lanes 0..k-1 are
+// exact, and Huffman codes resynchronise within a few codewords, so two
+// passes usually settle every lane.  A last pass writes each lane's symbols at
+// its prefix offset; the last lane decodes exactly the remaining count and
+// must end on bit 0 (the serial decoder's check).
+__device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh, uint8_t* lit) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (b.lit_type == 0) {
-    for (uint32_t i = lane; i < b.lit_regen; i += 32) lit[i] = __ldg(src + b.src + i);
+    for (uint32_t i = tid; i < b.lit_regen; i += 32 * kLitWarps) lit[i] = __ldg(src + b.src + i);
     return;
   }
   if (b.lit_type == 1) {
     const uint8_t c = __ldg(src + b.src);
-    for (uint32_t i = lane; i < b.lit_regen; i += 32) lit[i] = c;
+    for (uint32_t i = tid; i < b.lit_regen; i += 32 * kLitWarps) lit[i] = c;
     return;
   }
   const ZHuf& H = v.huf[b.huf];
   const int maxbits = H.maxbits, nsym = H.nsym;
-  if (lane == 0) {
+  if (tid == 0) {
     uint32_t count[13] = {0}, start[13];
     for (int s = 0; s < nsym; s++) count[H.w[s]]++;
     uint32_t pos = 0;
@@ -222,18 +345,18 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       start[w] += 1u << (w - 1);
     }
   }
-  __syncwarp();
-  for (int s = lane; s < nsym; s += 32) {
+  lit_sync();
+  for (int s = tid; s < nsym; s += 32 * kLitWarps) {
     const int w = H.w[s];
     if (!w) continue;
     const uint16_t e = uint16_t(s | ((maxbits + 1 - w) << 8));
     const uint32_t st = sh.sstart[s], len = 1u << (w - 1);
     for (uint32_t i = 0; i < len; i++) sh.huf[st + i] = e;
   }
-  __syncwarp();
+  lit_sync();
   // multi-symbol entries: greedily chain codes while they fit in maxbits
   const uint32_t tsize = 1u << maxbits, mask = tsize - 1;
-  for (uint32_t i = lane; i < tsize; i += 32) {
+  for (uint32_t i = tid; i < tsize; i += 32 * kLitWarps) {
     uint32_t e0 = sh.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
     const uint32_t e1 = sh.huf[(i << l0) & mask], l1 = e1 >> 8;
     if (bits + l1 <= uint32_t(maxbits)) {
@@ -249,125 +372,354 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     }
     sh.huf3[i] = syms | (bits << 24) | (cnt << 28);
   }
-  __syncwarp();
+  lit_sync();
   const int streams = int(b.lit_streams);
-  if (lane < streams) {
-    const uint32_t seg = streams == 1 ? b.lit_regen : (b.lit_regen + 3) / 4;
-    const uint32_t count = (streams == 1 || lane < 3) ? seg : b.lit_regen - 3 * seg;
-    uint64_t off = b.src;
-    for (int k = 0; k < lane; k++) off += b.lit_len[k];
-    uint8_t* out = lit + uint32_t(lane) * seg;
-    BitIn r;
-    bool ok = r.init(src + off, b.lit_len[lane]);
-    if (ok) {
-      uint32_t i = 0;
-      while (i + 3 <= count) {
-        r.ensure(maxbits);
-        const uint32_t e = sh.huf3[r.top(maxbits)];
-        const uint32_t c = e >> 28;
-        out[i] = uint8_t(e);
-        if (c > 1) out[i + 1] = uint8_t(e >> 8);
-        if (c > 2) out[i + 2] = uint8_t(e >> 16);
-        i += c;
-        r.skip(int((e >> 24) & 15u));
-        if (r.pos < -32) break;
+  if (warp >= streams) return;
+  const uint32_t seg = streams == 1 ? b.lit_regen : (b.lit_regen + 3) / 4;
+  const uint32_t count = (streams == 1 || warp < 3) ? seg : b.lit_regen - 3 * seg;
+  uint64_t off = b.src;
+  for (int k = 0; k < warp; k++) off += b.lit_len[k];
+  uint8_t* out = lit + uint32_t(warp) * seg;
+  const uint8_t* sp = src + off;
+  const uint32_t slen = b.lit_len[warp];
+  const uint32_t lastb = slen ? __ldg(sp + slen - 1) : 0u;
+  bool ok = lastb != 0;
+  if (ok) {
+    const int32_t B = int32_t(8 * (slen - 1) + (31 - __clz(lastb)));
+    // spans: one lane for short streams, else 32
+    const int nl = B >= 32 * 256 ? 32 : 1;
+    const int32_t span = (B + nl - 1) / nl;
+    const bool active = lane < nl;
+    const bool last = lane == nl - 1;
+    const int32_t stop = last ? 0 : B - (lane + 1) * span;
+    int32_t start = active ? B - lane * span : 0;
+    uint32_t n = 0;
+    for (int pass = 0; pass <= nl; pass++) {
+      int32_t exitp = start;
+      n = 0;
+      if (active && !last) {
+        DownWin W;
+        W.init(sp, start);
+        n = huf_run(sh, W, stop, uint32_t(maxbits), nullptr, -1);
+        exitp = W.P;
       }
-      for (; i < count && r.pos >= -32; i++) {
-        r.ensure(maxbits);
-        const uint32_t e = sh.huf[r.top(maxbits)];
-        out[i] = uint8_t(e);
-        r.skip(int(e >> 8));
-      }
-      ok = (r.pos == 0);
+      int32_t next = __shfl_up_sync(0xFFFFFFFFu, exitp, 1);
+      if (lane == 0 || !active) next = start;
+      if (!__any_sync(0xFFFFFFFFu, next != start)) break;
+      start = next;
     }
-    if (!ok) atomicOr(&sh.st, VOOM_ZSTD_ST_LITERALS);
+    // offsets: exclusive prefix of the non-last lanes' counts
+    uint32_t incl = (active && !last) ? n : 0u;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t excl = incl - ((active && !last) ? n : 0u);
+    bool lane_ok = true;
+    if (active) {
+      DownWin W;
+      W.init(sp, start);
+      if (!last) {
+        lane_ok = excl + n <= count;  // a damaged stream may decode more symbols than it holds
+        if (lane_ok) huf_run(sh, W, stop, uint32_t(maxbits), out + excl, -1);
+      } else if (excl <= count) {
+        const uint32_t got = huf_run(sh, W, 0, uint32_t(maxbits), out + excl, int32_t(count - excl));
+        lane_ok = (got == count - excl) && W.P == 0;
+      } else {
+        lane_ok = false;
+      }
+    }
+    ok = __all_sync(0xFFFFFFFFu, lane_ok);
   }
+  if (!ok && lane == 0) atomicOr(&sh.st, VOOM_ZSTD_ST_LITERALS);
 }
 
+// Symbolic repeat-offset slot: kind 0..2 = the block's input slot minus d,
+// kind 3 = the constant d.
+struct RepSlots {
+  uint32_t k[3], d[3];
+};
+
+__device__ __forceinline__ void rep_sub(uint32_t& k, uint32_t& d, uint32_t kk, uint32_t dd, uint32_t delta) {
+  k = kk;
+  d = kk == 3 ? dd - delta : dd + delta;
+}
+
+// One sequence's repeat-offset rule (RFC 8878 3.1.2.5) applied to symbolic
+// slots; returns the offset it uses.
+__device__ __forceinline__ void rep_step(RepSlots& r, uint32_t ofv, uint32_t ll, uint32_t& ok, uint32_t& ov) {
+  if (ofv > 3) {
+    ok = 3;
+    ov = ofv - 3;
+  } else {
+    const uint32_t idx = ofv - 1 + (ll == 0);
+    if (idx == 0) {
+      ok = r.k[0]; ov = r.d[0];
+      return;
+    }
+    if (idx == 1) {
+      ok = r.k[1]; ov = r.d[1];
+      r.k[1] = r.k[0]; r.d[1] = r.d[0];
+      r.k[0] = ok; r.d[0] = ov;
+      return;
+    }
+    if (idx == 2) {
+      ok = r.k[2]; ov = r.d[2];
+    } else {
+      rep_sub(ok, ov, r.k[0], r.d[0], 1);
+    }
+  }
+  r.k[2] = r.k[1]; r.d[2] = r.d[1];
+  r.k[1] = r.k[0]; r.d[1] = r.d[0];
+  r.k[0] = ok; r.d[0] = ov;
+}
+
+// Slots after transform t applied to slots s (t is symbolic in its own input).
+__device__ __forceinline__ RepSlots rep_compose(const RepSlots& s, const RepSlots& t) {
+  RepSlots o;
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    if (t.k[q] == 3) {
+      o.k[q] = 3;
+      o.d[q] = t.d[q];
+    } else {
+      const uint32_t src = t.k[q];
+      const uint32_t sk = src == 0 ? s.k[0] : (src == 1 ? s.k[1] : s.k[2]);
+      const uint32_t sd = src == 0 ? s.d[0] : (src == 1 ? s.d[1] : s.d[2]);
+      rep_sub(o.k[q], o.d[q], sk, sd, t.d[q]);
+    }
+  }
+  return o;
+}
+
+// Scan of one group of up to 32 decoded sequences (lane L holds sequence
+// i0 + L when `valid`): repeat-offset slots and output positions from the
+// group's carry-in (slots C, output position dst, literal position lit),
+// written as 32 consecutive ZSeq records; returns the carry-out.
+__device__ __forceinline__ void seq_group(ZSeq* out, uint32_t i0, bool valid, uint32_t ll, uint32_t ml, uint32_t ofv,
+                                          RepSlots& C, uint32_t& dst, uint32_t& lit) {
+  const int lane = threadIdx.x & 31;
+  RepSlots t;
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    t.k[q] = uint32_t(q);
+    t.d[q] = 0;
+  }
+  uint32_t uk = 0, ud = 0;
+  if (valid) rep_step(t, ofv, ll, uk, ud);
+  RepSlots incl = t;
+  uint32_t sdst = valid ? ll + ml : 0u, slit = valid ? ll : 0u;
+  for (int o = 1; o < 32; o <<= 1) {
+    RepSlots prev;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      prev.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], o);
+      prev.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], o);
+    }
+    const uint32_t pd = __shfl_up_sync(0xFFFFFFFFu, sdst, o), pl = __shfl_up_sync(0xFFFFFFFFu, slit, o);
+    if (lane >= o) {
+      incl = rep_compose(prev, incl);
+      sdst += pd;
+      slit += pl;
+    }
+  }
+  RepSlots ex;
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    ex.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], 1);
+    ex.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], 1);
+    if (lane == 0) {
+      ex.k[q] = uint32_t(q);
+      ex.d[q] = 0;
+    }
+  }
+  const RepSlots before = rep_compose(C, ex);
+  uint32_t ok, ov;
+  if (uk == 3) {
+    ok = 3;
+    ov = ud;
+  } else {
+    const uint32_t bk = uk == 0 ? before.k[0] : (uk == 1 ? before.k[1] : before.k[2]);
+    const uint32_t bd = uk == 0 ? before.d[0] : (uk == 1 ? before.d[1] : before.d[2]);
+    rep_sub(ok, ov, bk, bd, ud);
+  }
+  if (valid) {
+    ZSeq z;
+    z.ll = ll;
+    z.ml = ml;
+    z.oval = ov;
+    z.okind = ok;
+    z.dst = dst + sdst - (ll + ml);
+    z.lit = lit + slit - ll;
+    out[i0 + lane] = z;
+  }
+  RepSlots all;
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    all.k[q] = __shfl_sync(0xFFFFFFFFu, incl.k[q], 31);
+    all.d[q] = __shfl_sync(0xFFFFFFFFu, incl.d[q], 31);
+  }
+  C = rep_compose(C, all);
+  dst += __shfl_sync(0xFFFFFFFFu, sdst, 31);
+  lit += __shfl_sync(0xFFFFFFFFu, slit, 31);
+}
+
+// Sequences section (RFC 8878 3.1.1.3.2.2) by the sequence warp.  All 32
+// lanes run the FSE walk in lockstep (same values; shared-memory reads are
+// broadcasts).  Each sequence reads its fields from fixed positions below the
+// current bit position P -- offset extra bits, match-length extra, literal-
+// length extra, then the LL, ML and OF state bits -- so the six positions
+// come from the three table cells and every field from three independent
+// 32-bit reads of a shared-memory ring of the bitstream that the warp refills
+// with coalesced loads.  Lane L keeps sequence i when i % 32 == L; every 32
+// sequences one warp scan resolves their repeat offsets and output positions
+// (seq_group) and writes 32 records.
 __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh) {
   const int lane = threadIdx.x & 31;
   if (lane < 3) fse_build_dev(v.fse[b.fse[lane]], lane == 0 ? sh.ll : (lane == 1 ? sh.of : sh.ml), sh.next[lane],
                               &sh.al[lane]);
   __syncwarp();
-  if (lane != 0) return;
-  uint32_t rk[3] = {0, 1, 2}, rv[3] = {0, 0, 0};
-  uint32_t sum_ml = 0, sum_ll = 0, st = 0;
-  BitIn r;
-  if (!r.init(src + b.seq_src, b.seq_len)) {
+  {
+    const uint32_t nll = 1u << sh.al[0], nof = 1u << sh.al[1], nml = 1u << sh.al[2];
+    for (uint32_t u = lane; u < nll; u += 32) {
+      const uint32_t t = sh.ll[u], c = min(t & 0xFFu, 35u);
+      sh.ll2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ll_bits[c]) << 24), c_ll_base[c]);
+    }
+    for (uint32_t u = lane; u < nml; u += 32) {
+      const uint32_t t = sh.ml[u], c = min(t & 0xFFu, 52u);
+      sh.ml2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ml_bits[c]) << 24), c_ml_base[c]);
+    }
+    for (uint32_t u = lane; u < nof; u += 32) {
+      const uint32_t t = sh.of[u];
+      sh.of[u] = (t >> 16) | (((t >> 8) & 0xFFu) << 16) | (min(t & 0xFFu, 31u) << 24);
+    }
+  }
+  __syncwarp();
+  ZSeq* out = v.seq + b.seq_off;
+  RepSlots C;
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    C.k[q] = uint32_t(q);
+    C.d[q] = 0;
+  }
+  uint32_t dst = 0, lit = 0, st = 0;
+  const uint8_t* p = src + b.seq_src;
+  const uint32_t len = b.seq_len;
+  const uint32_t lastb = len ? __ldg(p + len - 1) : 0u;
+  if (!lastb) {
     st = VOOM_ZSTD_ST_SEQUENCES;
   } else {
-    r.ensure(26);
-    uint32_t sll = r.read(sh.al[0]), sof = r.read(sh.al[1]), sml = r.read(sh.al[2]);
-    ZSeq* out = v.seq + b.seq_off;
-    uint32_t dst = 0;
-    for (uint32_t i = 0; i < b.nseq; i++) {
-      const uint32_t eLL = sh.ll[sll], eOF = sh.of[sof], eML = sh.ml[sml];
-      const uint32_t ofc = eOF & 0xFFu, mlc = eML & 0xFFu, llc = eLL & 0xFFu;
-      r.ensure(31);
-      const uint32_t ofv = (1u << ofc) + r.read(int(ofc));
-      r.ensure(32);
-      const uint32_t ml = c_ml_base[mlc] + r.read(c_ml_bits[mlc]);
-      const uint32_t ll = c_ll_base[llc] + r.read(c_ll_bits[llc]);
-      // repeat-offset rules (RFC 8878 3.1.2.5) on symbolic slots
-      uint32_t ok, ov;
-      if (ofv > 3) {
-        ok = 3;
-        ov = ofv - 3;
-        rk[2] = rk[1]; rv[2] = rv[1];
-        rk[1] = rk[0]; rv[1] = rv[0];
-        rk[0] = ok; rv[0] = ov;
-      } else {
-        const uint32_t idx = ofv - 1 + (ll == 0);
-        if (idx == 0) {
-          ok = rk[0]; ov = rv[0];
-        } else if (idx == 1) {
-          ok = rk[1]; ov = rv[1];
-          rk[1] = rk[0]; rv[1] = rv[0];
-          rk[0] = ok; rv[0] = ov;
-        } else if (idx == 2) {
-          ok = rk[2]; ov = rv[2];
-          rk[2] = rk[1]; rv[2] = rv[1];
-          rk[1] = rk[0]; rv[1] = rv[0];
-          rk[0] = ok; rv[0] = ov;
-        } else {
-          ok = rk[0]; ov = rk[0] == 3 ? rv[0] - 1 : rv[0] + 1;
-          rk[2] = rk[1]; rv[2] = rv[1];
-          rk[1] = rk[0]; rv[1] = rv[0];
-          rk[0] = ok; rv[0] = ov;
-        }
+    // Aligned words of the stream: word k holds aligned bits [32k, 32k+32);
+    // stream bit q is aligned bit q + boff.  Ring entry i holds words i..i+3
+    // (128 bits from word i), so any 64-bit window is one 16-byte read.
+    const uintptr_t pa = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* wbase = reinterpret_cast<const uint32_t*>(pa & ~uintptr_t(3));
+    const int32_t boff = int32_t(pa & 3u) * 8;
+    auto gword = [&](int32_t k) -> uint32_t { return k >= 0 ? __ldg(wbase + k) : 0u; };
+    // entries [e0, e0 + 32) from words e0 .. e0 + 34 (the top three words of
+    // the batch come from `above`, the words just over it)
+    auto fill32 = [&](int32_t e0, uint32_t w_l, uint3 above) {
+      const uint32_t n1 = __shfl_down_sync(0xFFFFFFFFu, w_l, 1), n2 = __shfl_down_sync(0xFFFFFFFFu, w_l, 2),
+                     n3 = __shfl_down_sync(0xFFFFFFFFu, w_l, 3);
+      const uint32_t w1 = lane < 31 ? n1 : above.x;
+      const uint32_t w2 = lane < 30 ? n2 : (lane == 30 ? above.x : above.y);
+      const uint32_t w3 = lane < 29 ? n3 : (lane == 29 ? above.x : (lane == 30 ? above.y : above.z));
+      sh.sring[(e0 + lane) & 127] = make_uint4(w_l, w1, w2, w3);
+    };
+    const int32_t Pa0 = int32_t(8 * (len - 1) + (31 - __clz(lastb))) + boff;  // aligned position
+    int32_t Pa = Pa0;
+    // ring covers entries [lo_w, lo_w + 128); reads touch entries at or below (Pa-1)>>5
+    int32_t lo_w = ((Pa0 - 1) >> 5) + 1 - 128;
+    {
+      const int32_t topw = lo_w + 128;
+      uint3 above = make_uint3(gword(topw), gword(topw + 1), gword(topw + 2));
+      for (int j = 3; j >= 0; j--) {
+        const int32_t e0 = lo_w + 32 * j;
+        const uint32_t w_l = gword(e0 + lane);
+        fill32(e0, w_l, above);
+        above = make_uint3(__shfl_sync(0xFFFFFFFFu, w_l, 0), __shfl_sync(0xFFFFFFFFu, w_l, 1),
+                           __shfl_sync(0xFFFFFFFFu, w_l, 2));
       }
-      ZSeq s;
-      s.ll = ll;
-      s.ml = ml;
-      s.oval = ov;
-      s.okind = ok;
-      s.dst = dst;
-      s.lit = sum_ll;
-      out[i] = s;
-      dst += ll + ml;
-      sum_ml += ml;
-      sum_ll += ll;
-      if (i + 1 < b.nseq) {
-        r.ensure(26);
-        sll = (eLL >> 16) + r.read(int((eLL >> 8) & 0xFFu));
-        sml = (eML >> 16) + r.read(int((eML >> 8) & 0xFFu));
-        sof = (eOF >> 16) + r.read(int((eOF >> 8) & 0xFFu));
-      }
-      if (r.pos < -32) break;
     }
-    if (r.pos != 0) st = VOOM_ZSTD_ST_SEQUENCES;
+    uint32_t pre = gword(lo_w - 32 + lane);  // next batch, loaded one refill ahead
+    __syncwarp();
+    // stream bits [q, q + 32) at aligned position a
+    auto at = [&](int32_t a) -> uint32_t {
+      const uint4 e = sh.sring[(a >> 5) & 127];
+      return __funnelshift_r(e.x, e.y, uint32_t(a) & 31u);
+    };
+    const uint32_t a0 = sh.al[0], a1 = sh.al[1], a2 = sh.al[2];
+    uint32_t sll = 0, sof = 0, sml = 0;
+    if (Pa - boff < int32_t(a0 + a1 + a2)) {
+      st = VOOM_ZSTD_ST_SEQUENCES;
+    } else {
+      const uint32_t init = at(Pa - int32_t(a0 + a1 + a2));
+      sml = bfe32(init, 0, a2);
+      sof = bfe32(init, a2, a1);
+      sll = bfe32(init, a1 + a2, a0);
+      Pa -= int32_t(a0 + a1 + a2);
+    }
+    const uint32_t nseq = b.nseq;
+    uint32_t my_ll = 0, my_ml = 0, my_of = 0, i = 0;
+    for (; i < nseq && !st; i++) {
+      // keep >= 4 entries of ring below the lowest word this sequence reads (<= 89 bits)
+      if (((Pa - 96) >> 5) < lo_w) {
+        const uint4 e = sh.sring[lo_w & 127];
+        fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
+        lo_w -= 32;
+        pre = gword(lo_w - 32 + lane);
+        __syncwarp();
+      }
+      // the 32 bits below Pa, read alongside the table cells
+      const uint32_t w1 = at(Pa - 32);
+      const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
+      const uint32_t eOF = sh.of[sof];
+      const uint32_t ofc = eOF >> 24, mlb = eML.x >> 24, llb = eLL.x >> 24;
+      const bool more = i + 1 < nseq;
+      const uint32_t nLL = more ? bfe32(eLL.x, 16, 8) : 0u, nML = more ? bfe32(eML.x, 16, 8) : 0u,
+                     nOF = more ? bfe32(eOF, 16, 8) : 0u;
+      const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
+      const uint32_t ns = nLL + nML;
+      const uint32_t total = ox + ns + nOF;
+      if (Pa - boff < int32_t(total)) {
+        st = VOOM_ZSTD_ST_SEQUENCES;
+        break;
+      }
+      // fields top-down: offset extra (<= 31 bits) from w1, ML and LL extras
+      // (<= 32 bits together) from the word below it, states (<= 26 bits)
+      // from the word below the extras
+      const uint32_t w2 = at(Pa - int32_t(ofc) - 32), w3 = at(Pa - int32_t(ox) - 32);
+      const uint32_t ofv = (1u << ofc) + bfe32(w1, 32u - ofc, ofc);
+      const uint32_t ml = eML.y + bfe32(w2, 32u - mlb, mlb);
+      const uint32_t ll = eLL.y + bfe32(w2, 32u - mlb - llb, llb);
+      sll = (eLL.x & 0xFFFFu) + bfe32(w3, 32u - nLL, nLL);
+      sml = (eML.x & 0xFFFFu) + bfe32(w3, 32u - ns, nML);
+      sof = (eOF & 0xFFFFu) + bfe32(w3, 32u - ns - nOF, nOF);
+      Pa -= int32_t(total);
+      if ((i & 31u) == uint32_t(lane)) {
+        my_ll = ll;
+        my_ml = ml;
+        my_of = ofv;
+      }
+      if ((i & 31u) == 31u) seq_group(out, i - 31, true, my_ll, my_ml, my_of, C, dst, lit);
+    }
+    if (i & 31u) seq_group(out, i & ~31u, uint32_t(lane) < (i & 31u), my_ll, my_ml, my_of, C, dst, lit);
+    if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;
   }
-  if (sum_ll > b.lit_regen) st |= VOOM_ZSTD_ST_SEQUENCES;
-  if (st) atomicOr(&sh.st, st);
-  sh.out_size = b.lit_regen + sum_ml;
-  for (int k = 0; k < 3; k++) {
-    sh.rep_kind[k] = rk[k];
-    sh.rep_val[k] = rv[k];
+  if (lane == 0) {
+    // lit = sum of literal lengths, dst - lit = sum of match lengths
+    if (lit > b.lit_regen) st |= VOOM_ZSTD_ST_SEQUENCES;
+    if (st) atomicOr(&sh.st, st);
+    sh.out_size = b.lit_regen + (dst - lit);
+    for (int k = 0; k < 3; k++) {
+      sh.rep_kind[k] = C.k[k];
+      sh.rep_val[k] = C.d[k];
+    }
   }
 }
 
-__global__ void __launch_bounds__(64) zstd_block_decode(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                        uint8_t* scratch) {
+__global__ void __launch_bounds__(kK1Threads) zstd_block_decode(const uint8_t* __restrict__ src,
+                                                                const uint8_t* img, uint8_t* scratch) {
   __shared__ K1Shared sh;
   const View v = make_view(img, scratch);
   const ZBlock b = v.blocks[blockIdx.x];
@@ -392,7 +744,7 @@ __global__ void __launch_bounds__(64) zstd_block_decode(const uint8_t* __restric
     }
   }
   __syncthreads();
-  if (threadIdx.x < 32) decode_literals(src, v, b, sh, v.lit + b.lit_off);
+  if (threadIdx.x < 32 * kLitWarps) decode_literals(src, v, b, sh, v.lit + b.lit_off);
   else if (b.nseq) decode_sequences(src, v, b, sh);
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -653,7 +1005,7 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   const uint8_t* img = static_cast<const uint8_t*>(d_plan);
   uint8_t* scr = static_cast<uint8_t*>(d_scratch);
   if (h.n_blocks) {
-    zstd_block_decode<<<h.n_blocks, 64, 0, s>>>(d_src, img, scr);
+    zstd_block_decode<<<h.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr);
     zstd_job_scan<<<(h.n_jobs + 127) / 128, 128, 0, s>>>(img, scr, d_status);
     zstd_block_execute<<<h.n_blocks, 128, 0, s>>>(d_src, img, scr, d_status);
   }
