@@ -288,7 +288,7 @@ class C2Vpack:
         return True
 
     def step_e2e(self):
-        out, spans = self.packed.decode_bodies(self.heads, self.pinned.numpy(), self.offs, self.lens,
+        out, spans = self.packed.decode_bodies(self.heads, self.pinned, self.offs, self.lens,
                                                device=self.dev, src_dev=None)
         return self.archive.size, 4 * len(self.heads)
 

@@ -3,6 +3,8 @@ host<->device staging.  torch supplies device memory and streams only."""
 
 from __future__ import annotations
 
+import threading
+
 import numpy as np
 import torch
 
@@ -42,11 +44,29 @@ def pinned_empty(n: int) -> torch.Tensor:
     return torch.empty(int(n), dtype=torch.uint8, pin_memory=True)
 
 
+_STAGE_CHUNK = 8 << 20  # bytes per staging half
+_stage: dict = {}         # device index -> (pinned staging tensor, [event, event], lock)
+_stage_lock = threading.Lock()
+
+
+def _staging(device: torch.device):
+    """A reusable pinned staging buffer of two halves per device (allocating
+    pinned memory per call costs milliseconds per hundred MB)."""
+    with _stage_lock:
+        st = _stage.get(device.index)
+        if st is None:
+            buf = pinned_empty(2 * _STAGE_CHUNK)
+            st = (buf, [None, None], threading.Lock())
+            _stage[device.index] = st
+    return st
+
+
 def upload(host, device: torch.device, *, pad: int = PAD, stream: torch.cuda.Stream | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """Copy a host buffer into a new (or given) device uint8 tensor with `pad`
-    zero bytes after it.  Pinned CPU tensors are copied asynchronously; other
-    buffers are staged through a pinned buffer first."""
+    zero bytes after it.  Pinned CPU tensors are copied asynchronously in one
+    DMA; pageable buffers go through a cached two-half pinned staging buffer,
+    the memcpy of one half overlapping the DMA of the other."""
     if isinstance(host, torch.Tensor) and host.device.type == "cuda":
         src = host.reshape(-1).view(torch.uint8)
         n = src.numel()
@@ -55,27 +75,36 @@ def upload(host, device: torch.device, *, pad: int = PAD, stream: torch.cuda.Str
         if pad:
             dev[n:n + pad].zero_()
         return dev
+    s = stream if stream is not None else torch.cuda.current_stream(device)
     if isinstance(host, torch.Tensor) and host.is_pinned():
         src = host.reshape(-1).view(torch.uint8)
-    else:
-        arr = as_u8(host)
-        src = pinned_empty(arr.size)
-        src.numpy()[:] = arr
-    n = src.numel()
+        n = src.numel()
+        dev = out if out is not None else torch.empty(n + pad, dtype=torch.uint8, device=device)
+        with torch.cuda.stream(s):
+            dev[:n].copy_(src, non_blocking=True)
+            if pad:
+                dev[n:n + pad].zero_()
+        return dev
+    arr = as_u8(host)
+    n = arr.size
     dev = out if out is not None else torch.empty(n + pad, dtype=torch.uint8, device=device)
-    with torch.cuda.stream(stream) if stream is not None else _null():
-        dev[:n].copy_(src, non_blocking=True)
+    buf, events, lock = _staging(device)
+    stage = buf.numpy()
+    with lock, torch.cuda.stream(s):
+        for i, off in enumerate(range(0, n, _STAGE_CHUNK)):
+            half = i & 1
+            if events[half] is not None:
+                events[half].synchronize()  # that half's previous DMA is done
+            m = min(_STAGE_CHUNK, n - off)
+            base = half * _STAGE_CHUNK
+            stage[base:base + m] = arr[off:off + m]
+            dev[off:off + m].copy_(buf[base:base + m], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s)
+            events[half] = ev
         if pad:
             dev[n:n + pad].zero_()
     return dev
-
-
-class _null:
-    def __enter__(self):
-        return None
-
-    def __exit__(self, *a):
-        return False
 
 
 def tensor_from_numpy(arr: np.ndarray, device: torch.device) -> torch.Tensor:

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <new>
+#include <atomic>
 #include <thread>
 #include <vector>
 
@@ -225,8 +226,19 @@ struct JobPlan {
   bool bad = false;
 };
 
-bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZBlock& b, uint32_t& last_huf,
-                     uint32_t last_fse[3]) {
+// Tables a compressed block declares: its own Huffman description or none
+// (treeless literals reuse the frame's previous table), and per sequence
+// code either the predefined table (0), its own RLE / compressed table (1)
+// or the previous block's (2, repeat mode).  Filled in parallel; the
+// references are resolved per frame afterwards (resolve_job).
+struct BlockTables {
+  bool huf_own = false, treeless = false;
+  ZHuf huf;
+  int fse_kind[3] = {0, 0, 0};
+  ZFse fse[3];
+};
+
+bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, ZBlock& b, BlockTables& T) {
   const uint8_t* p = base + at;
   if (n < 1) return false;
   // literals section header (RFC 8878 3.1.1.3.1.1)
@@ -260,20 +272,17 @@ bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZB
     if (regen > kBlockMax || size_t(hsz) + csize > n) return false;
     size_t q = size_t(hsz), avail = csize;
     if (type == 2) {
-      ZHuf h;
       size_t wu;
-      if (!read_huffman(p + q, avail, &h, &wu)) return false;
-      last_huf = uint32_t(jp.huf.size());
-      jp.huf.push_back(h);
+      if (!read_huffman(p + q, avail, &T.huf, &wu)) return false;
+      T.huf_own = true;
       q += wu;
       avail -= wu;
-    } else if (last_huf == kNone) {
-      return false;  // treeless literals without a previous table
+    } else {
+      T.treeless = true;  // needs the frame's previous table
     }
     b.lit_type = 2;
     b.lit_regen = uint32_t(regen);
     b.lit_streams = uint32_t(streams);
-    b.huf = last_huf;
     if (streams == 1) {
       if (avail == 0) return false;
       b.src = at + q;
@@ -321,17 +330,16 @@ bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZB
   const int mode[3] = {modes >> 6, (modes >> 4) & 3, (modes >> 2) & 3};  // LL, OF, ML
   for (int k = 0; k < 3; k++) {
     if (mode[k] == 0) {
-      b.fse[k] = kPredef | uint32_t(k);
+      T.fse_kind[k] = 0;
     } else if (mode[k] == 1) {
       if (hsz >= n || p[hsz] > kMaxSym[k]) return false;
-      ZFse f;
+      ZFse& f = T.fse[k];
       memset(&f, 0, sizeof f);
       f.rle = 1;
       f.rle_sym = p[hsz++];
-      b.fse[k] = uint32_t(jp.fse.size());
-      jp.fse.push_back(f);
+      T.fse_kind[k] = 1;
     } else if (mode[k] == 2) {
-      ZFse f;
+      ZFse& f = T.fse[k];
       memset(&f, 0, sizeof f);
       int al;
       size_t u;
@@ -341,15 +349,12 @@ bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZB
       if (!fse_build(f.norm, ns, al, tmp)) return false;
       f.nsym = uint16_t(ns);
       f.al = uint8_t(al);
-      b.fse[k] = uint32_t(jp.fse.size());
-      jp.fse.push_back(f);
+      T.fse_kind[k] = 1;
       hsz += u;
     } else {
-      if (last_fse[k] == kNone) return false;
-      b.fse[k] = last_fse[k];
+      T.fse_kind[k] = 2;
     }
   }
-  for (int k = 0; k < 3; k++) last_fse[k] = b.fse[k];
   if (hsz >= n || p[n - 1] == 0) return false;
   b.nseq = uint32_t(nseq);
   b.seq_src = at + hsz;
@@ -357,7 +362,9 @@ bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, JobPlan& jp, ZB
   return true;
 }
 
-void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
+// Frame and block walk of one job (sequential: block headers chain); the
+// compressed blocks' sections are parsed later in parallel.
+void walk_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
   uint64_t pos = job.src;
   const uint64_t end = job.src + job.src_len;
   if (job.src_len == 0) { jp.bad = true; return; }
@@ -398,7 +405,6 @@ void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
     const uint64_t block_max = std::min<uint64_t>(wsize, kBlockMax);
     fr.block_first = uint32_t(jp.blocks.size());
     const uint32_t frame_index = uint32_t(jp.frames.size());
-    uint32_t last_huf = kNone, last_fse[3] = {kNone, kNone, kNone};
     for (;;) {
       if (pos + 3 > end) { jp.bad = true; return; }
       const uint32_t bh = uint32_t(le(base + pos, 3));
@@ -425,7 +431,8 @@ void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
         pos += 1;
       } else {
         if (pos + bs > end) { jp.bad = true; return; }
-        if (!plan_compressed(base, pos, size_t(bs), jp, b, last_huf, last_fse)) { jp.bad = true; return; }
+        b.src = pos;
+        b.size = uint32_t(bs);  // compressed size until parsed
         pos += bs;
       }
       jp.blocks.push_back(b);
@@ -439,6 +446,45 @@ void plan_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
       pos += 4;
     }
     jp.frames.push_back(fr);
+  }
+}
+
+// Table references of one job's compressed blocks, frame by frame: own
+// tables are appended, treeless / repeat blocks take the previous ones
+// (RFC 8878 3.1.1.3.1.1, 3.1.1.3.2.1.1).
+void resolve_job(JobPlan& jp, const std::vector<BlockTables>& tabs, const std::vector<uint8_t>& ok) {
+  for (const ZFrame& fr : jp.frames) {
+    uint32_t last_huf = kNone, last_fse[3] = {kNone, kNone, kNone};
+    for (uint32_t i = fr.block_first; i < fr.block_first + fr.n_blocks; i++) {
+      ZBlock& b = jp.blocks[i];
+      if (b.type != 2) continue;
+      if (!ok[i]) { jp.bad = true; return; }
+      const BlockTables& T = tabs[i];
+      if (b.lit_type == 2) {
+        if (T.huf_own) {
+          last_huf = uint32_t(jp.huf.size());
+          jp.huf.push_back(T.huf);
+        } else if (last_huf == kNone) {
+          jp.bad = true;  // treeless literals without a previous table
+          return;
+        }
+        b.huf = last_huf;
+      }
+      if (b.nseq) {
+        for (int k = 0; k < 3; k++) {
+          if (T.fse_kind[k] == 0) {
+            b.fse[k] = kPredef | uint32_t(k);
+          } else if (T.fse_kind[k] == 1) {
+            b.fse[k] = uint32_t(jp.fse.size());
+            jp.fse.push_back(T.fse[k]);
+          } else {
+            if (last_fse[k] == kNone) { jp.bad = true; return; }
+            b.fse[k] = last_fse[k];
+          }
+          last_fse[k] = b.fse[k];
+        }
+      }
+    }
   }
 }
 
@@ -473,18 +519,48 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   Plan* P = new (std::nothrow) Plan();
   if (!P) return nullptr;
   std::vector<JobPlan> jp(n_jobs);
-  int nt = threads > 0 ? threads : int(std::max(1u, std::thread::hardware_concurrency()));
-  nt = std::max(1, std::min<int>(nt, int(n_jobs)));
-  auto work = [&](int w) {
-    for (uint32_t j = uint32_t(w); j < n_jobs; j += uint32_t(nt)) {
-      if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; continue; }
-      plan_job(h_src, jobs[j], jp[j]);
-    }
+  const int nt_all = threads > 0 ? threads : int(std::max(1u, std::thread::hardware_concurrency()));
+  // runs f(i) for i in [0, n) on up to nt_all threads (dynamic assignment)
+  auto parallel = [&](uint64_t n, auto&& f) {
+    const int nt = int(std::max<uint64_t>(1, std::min<uint64_t>(uint64_t(nt_all), n)));
+    std::atomic<uint64_t> next{0};
+    auto run = [&]() {
+      for (uint64_t i = next.fetch_add(1); i < n; i = next.fetch_add(1)) f(i);
+    };
+    std::vector<std::thread> pool;
+    for (int w = 1; w < nt; w++) pool.emplace_back(run);
+    run();
+    for (auto& t : pool) t.join();
   };
-  std::vector<std::thread> pool;
-  for (int w = 1; w < nt; w++) pool.emplace_back(work, w);
-  if (n_jobs) work(0);
-  for (auto& t : pool) t.join();
+  // 1. frame / block walk per job
+  parallel(n_jobs, [&](uint64_t j) {
+    if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; return; }
+    walk_job(h_src, jobs[j], jp[j]);
+  });
+  // 2. every compressed block's sections, in parallel over all jobs
+  std::vector<std::pair<uint32_t, uint32_t>> todo;  // (job, block)
+  std::vector<std::vector<BlockTables>> tabs(n_jobs);
+  std::vector<std::vector<uint8_t>> okb(n_jobs);
+  for (uint32_t j = 0; j < n_jobs; j++) {
+    if (jp[j].bad) continue;
+    tabs[j].resize(jp[j].blocks.size());
+    okb[j].assign(jp[j].blocks.size(), 1);
+    for (uint32_t i = 0; i < jp[j].blocks.size(); i++)
+      if (jp[j].blocks[i].type == 2) todo.emplace_back(j, i);
+  }
+  parallel(todo.size(), [&](uint64_t t) {
+    const uint32_t j = todo[t].first, i = todo[t].second;
+    ZBlock& b = jp[j].blocks[i];
+    const uint64_t at = b.src;
+    const size_t bs = b.size;
+    b.src = 0;
+    b.size = 0;
+    okb[j][i] = plan_compressed(h_src, at, bs, b, tabs[j][i]) ? 1 : 0;
+  });
+  // 3. table references, frame by frame
+  parallel(n_jobs, [&](uint64_t j) {
+    if (!jp[j].bad) resolve_job(jp[j], tabs[j], okb[j]);
+  });
 
   // predefined sequence tables occupy fse[0..2]
   for (int k = 0; k < 3; k++) {

@@ -142,12 +142,15 @@ def body_job(head: dict, body_off: int, body_len: int, dst: int) -> tuple[np.nda
 def decode_bodies(heads: list[dict], host_buf: np.ndarray, offsets: list[int], lengths: list[int], *,
                   device=None, src_dev: torch.Tensor | None = None, align: int = 256,
                   stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, list[tuple[int, int]]]:
-    """Decode many vpack bodies that sit in one host buffer (and optionally
-    already in `src_dev`) with one batched GPU decode.  Returns the device
-    output buffer and each body's (offset, length) in it."""
+    """Decode many vpack bodies that sit in one host buffer (numpy, bytes or a
+    CPU tensor; a pinned tensor is copied in one asynchronous DMA) and
+    optionally already in `src_dev`, with one batched GPU decode.  Returns the
+    device output buffer and each body's (offset, length) in it."""
     from .. import _device
 
     dev = _device.require_cuda(device)
+    upload_src = host_buf
+    host_buf = _device.as_u8(host_buf)
     jobs, spans, raw_copies = [], [], []
     dst = 0
     for head, off, ln in zip(heads, offsets, lengths):
@@ -164,7 +167,7 @@ def decode_bodies(heads: list[dict], host_buf: np.ndarray, offsets: list[int], l
         dst += (n + align - 1) // align * align
     with torch.cuda.device(dev):
         if src_dev is None:
-            src_dev = _device.upload(host_buf, dev, stream=stream)
+            src_dev = _device.upload(upload_src, dev, stream=stream)
         out = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
         for off, d, n in raw_copies:
             out[d:d + n].copy_(src_dev[off:off + n])
