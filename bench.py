@@ -374,7 +374,7 @@ class C3Moe:
         self.routed = None
         self.per_expert_bytes = per_expert
         self.algo_bytes = None  # set after a routing pass (distinct experts per layer)
-        self.launches_per_step = 6 * layers  # router, plan, gate/up, act, down, combine
+        self.launches_per_step = 7 * layers  # router logits, top-k, plan, gate/up, act, down, combine
         self.experts_raw = experts
 
     def _run(self, x, stream):
@@ -518,7 +518,7 @@ class C4MoeEP:
         self.scaling = "strong"
         self.L = layers
         self.algo_bytes = 1  # replaced after the first step (routed local pages)
-        self.launches_per_step = 6 * layers  # router, plan, gate/up, act, down, combine (+ NCCL)
+        self.launches_per_step = 7 * layers  # router logits, top-k, plan, gate/up, act, down, combine (+ NCCL)
 
     def _run(self, x):
         cur = x

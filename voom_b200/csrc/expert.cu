@@ -63,11 +63,15 @@ __device__ __forceinline__ uint32_t f2bf(float f) {  // round to nearest even
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 
 // ------------------------------------------------------------------ router
-// One CTA per token: RMSNorm (optional), logits = h @ Wr.T rounded to BF16
-// (+ optional bias), fp32 softmax, top-k (largest first; ties -> lower expert
-// id) by k rounds of block arg-max, optional renormalisation.  Writes h (BF16)
-// for the expert kernels.
+// Two kernels.  moe_router_logits: grid (ceil(E / 16), T); each CTA applies
+// the RMSNorm (optional) to its token and computes 16 experts' logits =
+// h @ Wr.T rounded to BF16 (+ optional bias), one warp per two experts, 8
+// weights per lane per step; CTA 0 of a token also writes h (BF16) for the
+// expert kernels.  moe_router_topk: one CTA per token, fp32 softmax, top-k
+// (largest first; ties -> lower expert id) by k rounds of block arg-max,
+// optional renormalisation.
 constexpr int kMaxH = 8192;
+constexpr int kRouterExperts = 16;  // experts per logits CTA
 
 __device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) {
@@ -76,45 +80,43 @@ __device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) 
   }
 }
 
-__global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restrict__ x,
-                                                       const uint16_t* __restrict__ norm_w, float eps,
-                                                       const uint16_t* __restrict__ wr,
-                                                       const float* __restrict__ bias, uint32_t E, uint32_t H,
-                                                       uint32_t k, uint32_t norm_topk, uint16_t* __restrict__ h,
-                                                       Routes* routes) {
+__global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __restrict__ x,
+                                                              const uint16_t* __restrict__ norm_w, float eps,
+                                                              const uint16_t* __restrict__ wr,
+                                                              const float* __restrict__ bias, uint32_t E,
+                                                              uint32_t H, uint16_t* __restrict__ h,
+                                                              float* __restrict__ logits) {
   __shared__ float s_h[kMaxH];
-  __shared__ float s_p[kMaxE];
-  __shared__ float s_redf[kThreads / 32];
-  __shared__ int s_redi[kThreads / 32];
-  __shared__ float s_scale, s_max, s_sum;
-  __shared__ uint8_t s_used[kMaxE];
-  __shared__ int s_pick[64];
-  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float s_red[kThreads / 32];
+  __shared__ float s_scale;
+  const uint32_t t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint16_t* xt = x + size_t(t) * H;
+  if (norm_w) {
+    float ss = 0.f;
+    for (uint32_t i = tid; i < H; i += kThreads) {
+      const float v = bf2f(xt[i]);
+      ss += v * v;
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int w = 0; w < kThreads / 32; w++) tot += s_red[w];
+      s_scale = rsqrtf(tot / float(H) + eps);
+    }
+    __syncthreads();
+  }
+  const bool write_h = blockIdx.x == 0;
   uint16_t* ht = h + size_t(t) * H;
-  float ss = 0.f;
-  for (uint32_t i = tid; i < H; i += kThreads) {
-    const float v = bf2f(xt[i]);
-    ss += v * v;
-  }
-  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-  if (lane == 0) s_redf[warp] = ss;
-  __syncthreads();
-  if (tid == 0) {
-    float tot = 0.f;
-    for (int w = 0; w < kThreads / 32; w++) tot += s_redf[w];
-    s_scale = rsqrtf(tot / float(H) + eps);
-  }
-  __syncthreads();
   for (uint32_t i = tid; i < H; i += kThreads) {
     const uint32_t hb = norm_w ? f2bf(bf2f(xt[i]) * s_scale * bf2f(norm_w[i])) : xt[i];
-    ht[i] = uint16_t(hb);
+    if (write_h) ht[i] = uint16_t(hb);
     s_h[i] = bf2f(hb);
   }
-  for (uint32_t e = tid; e < E; e += kThreads) s_used[e] = 0;
   __syncthreads();
-  // logits: one warp per expert row, 8 weights per lane per step
-  for (uint32_t e = warp; e < E; e += kThreads / 32) {
+  const uint32_t e_end = min(E, (blockIdx.x + 1) * kRouterExperts);
+  for (uint32_t e = blockIdx.x * kRouterExperts + warp; e < e_end; e += kThreads / 32) {
     const uint16_t* we = wr + size_t(e) * H;
     float acc = 0.f;
     for (uint32_t i = lane * 8; i < H; i += 256) {
@@ -129,7 +131,22 @@ __global__ void __launch_bounds__(kThreads) moe_router(const uint16_t* __restric
       acc = fmaf(__uint_as_float(w.w & 0xFFFF0000u), s_h[i + 7], acc);
     }
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) s_p[e] = rbf(acc) + (bias ? bias[e] : 0.f);
+    if (lane == 0) logits[size_t(t) * E + e] = rbf(acc) + (bias ? bias[e] : 0.f);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) moe_router_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
+                                                            uint32_t norm_topk, Routes* routes) {
+  __shared__ float s_p[kMaxE];
+  __shared__ float s_redf[kThreads / 32];
+  __shared__ int s_redi[kThreads / 32];
+  __shared__ float s_max, s_sum;
+  __shared__ uint8_t s_used[kMaxE];
+  __shared__ int s_pick[64];
+  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (uint32_t e = tid; e < E; e += kThreads) {
+    s_p[e] = logits[size_t(t) * E + e];
+    s_used[e] = 0;
   }
   __syncthreads();
   // softmax (fp32): block max, then block sum of exp
@@ -556,7 +573,7 @@ __global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __rest
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
 struct ScratchLayout {
-  uint64_t routes, h, act, y, total;
+  uint64_t routes, h, logits, act, y, total;
 };
 
 ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
@@ -564,6 +581,7 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   uint64_t o = 0;
   s.routes = o; o = align256(o + sizeof(Routes));
   s.h = o; o = align256(o + uint64_t(T) * H * 2 + 16);
+  s.logits = o; o = align256(o + uint64_t(T) * kMaxE * 4);
   s.act = o; o = align256(o + uint64_t(T) * k * I * 2 + 16);
   s.y = o; o = align256(o + uint64_t(T) * k * (H > I ? H : I) * 2 + 16);  // u rows, then y rows
   s.total = o;
@@ -627,8 +645,10 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
   uint16_t* y = reinterpret_cast<uint16_t*>(s + L.y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, top_k, norm_topk, h,
-                                      R);
+  float* logits = reinterpret_cast<float*>(s + L.logits);
+  moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
+      d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, h, logits);
+  moe_router_topk<<<T, kThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   const int rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
@@ -669,8 +689,10 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
   uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(d_y, 0, size_t(T) * top_k * H * 2, st) != cudaSuccess) return VOOM_E_CUDA;
-  moe_router<<<T, kThreads, 0, st>>>(d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, top_k, norm_topk,
-                                      h, R);
+  float* logits = reinterpret_cast<float*>(s + L.logits);
+  moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
+      d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, h, logits);
+  moe_router_topk<<<T, kThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
@@ -697,6 +719,7 @@ constexpr uint32_t kNoAllocMaxT = 64, kNoAllocMaxRoutes = 256, kNoAllocMaxH = 81
 constexpr uint64_t kNoAllocBytes =
     ((sizeof(Routes) + 255) & ~uint64_t(255)) +
     ((uint64_t(kNoAllocMaxT) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255)) +
+    uint64_t(kNoAllocMaxT) * kMaxE * 4 +
     ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxI * 2 + 16 + 255) & ~uint64_t(255)) +
     ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255));
 
