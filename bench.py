@@ -21,6 +21,8 @@ from __future__ import annotations
 
 import argparse
 import json
+import glob
+import re
 import os
 import statistics
 import subprocess
@@ -35,6 +37,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per step of `workload` from the committed ncu summaries
+    (a `traffic_bytes_per_step <workload>: N` line under profiles/), or None."""
+    pat = re.compile(r"^traffic_bytes_per_step (\S+): (\d+)\s*$")
+    for f in sorted(glob.glob(os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "*.md"))):
+        with open(f) as fh:
+            for line in fh:
+                m = pat.match(line)
+                if m and m.group(1) == workload:
+                    return int(m.group(2)), os.path.join("profiles", os.path.basename(f))
+    return None
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -273,7 +288,7 @@ class C2Vpack:
         self.units_per_step = self.raw_bytes
         self.algo_bytes = self.archive.size + self.raw_bytes
         self.n_blocks = int(self.plan.info.n_blocks)
-        self.launches_per_step = 10  # K1 K2 K3 6xK4 K5 (+K6 only for checksummed frames)
+        self.launches_per_step = 11  # K1 K2 K3 6xK4 K5 K6
 
     def step_device(self, stream_ptr: int):
         self.batch.run(self.src, self.out, self.torch.cuda.current_stream(self.dev))
@@ -710,8 +725,12 @@ def main():
     if w.unit != "GB/s":
         value = w.units_per_step * mult / (ms * 1e-3)
         e2e_value = w.units_per_step * mult / (e2e_ms * 1e-3)
+    prof = profiled_traffic(w.config()["workload"])
     roof = {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": getattr(w, "traffic", None),
+            "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": prof[0] if prof else None,
+            "traffic_unit": "DRAM bytes per step (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+            "traffic_source": prof[1] if prof else None,
+            "algorithmic_bytes_per_step": int(w.algo_bytes),
             "peak_kind": f"{peaks_kind} (hbm_gbs)"}
     cpu = None
     if rank == 0 and world == 1:
