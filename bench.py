@@ -288,7 +288,7 @@ class C2Vpack:
         self.units_per_step = self.raw_bytes
         self.algo_bytes = self.archive.size + self.raw_bytes
         self.n_blocks = int(self.plan.info.n_blocks)
-        self.launches_per_step = 11  # K1 K2 K3 6xK4 K5 K6
+        self.launches_per_step = 12  # K1 K1b K2 K3 6xK4 K5 K6
 
     def step_device(self, stream_ptr: int):
         self.batch.run(self.src, self.out, self.torch.cuda.current_stream(self.dev))

@@ -135,54 +135,36 @@ __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __
   }
 }
 
-__global__ void __launch_bounds__(kThreads) moe_router_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
-                                                            uint32_t norm_topk, Routes* routes) {
+// One warp per token: softmax and k rounds of warp arg-max over the logits
+// (each lane owns experts lane, lane + 32, ...).
+__global__ void __launch_bounds__(32) moe_router_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
+                                                      uint32_t norm_topk, Routes* routes) {
   __shared__ float s_p[kMaxE];
-  __shared__ float s_redf[kThreads / 32];
-  __shared__ int s_redi[kThreads / 32];
-  __shared__ float s_max, s_sum;
   __shared__ uint8_t s_used[kMaxE];
   __shared__ int s_pick[64];
-  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (uint32_t e = tid; e < E; e += kThreads) {
-    s_p[e] = logits[size_t(t) * E + e];
-    s_used[e] = 0;
-  }
-  __syncthreads();
-  // softmax (fp32): block max, then block sum of exp
+  const uint32_t t = blockIdx.x, lane = threadIdx.x;
   float mx = -INFINITY;
-  for (uint32_t e = tid; e < E; e += kThreads) mx = fmaxf(mx, s_p[e]);
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-  if (lane == 0) s_redf[warp] = mx;
-  __syncthreads();
-  if (tid == 0) {
-    float m = -INFINITY;
-    for (int w = 0; w < kThreads / 32; w++) m = fmaxf(m, s_redf[w]);
-    s_max = m;
+  for (uint32_t e = lane; e < E; e += 32) {
+    const float v = logits[size_t(t) * E + e];
+    s_p[e] = v;
+    s_used[e] = 0;
+    mx = fmaxf(mx, v);
   }
-  __syncthreads();
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
   float sm = 0.f;
-  for (uint32_t e = tid; e < E; e += kThreads) {
-    const float p = __expf(s_p[e] - s_max);
+  for (uint32_t e = lane; e < E; e += 32) {
+    const float p = __expf(s_p[e] - mx);
     s_p[e] = p;
     sm += p;
   }
   for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
-  __syncthreads();
-  if (lane == 0) s_redf[warp] = sm;
-  __syncthreads();
-  if (tid == 0) {
-    float a = 0.f;
-    for (int w = 0; w < kThreads / 32; w++) a += s_redf[w];
-    s_sum = a;
-  }
-  // top-k: k rounds of block arg-max over the unused experts.  Probabilities
-  // are >= 0; a NaN (non-finite activations) ranks below every number, so
-  // each round still picks a valid unused expert.
+  __syncwarp();
+  // top-k: probabilities are >= 0; a NaN (non-finite activations) ranks below
+  // every number, so each round still picks a valid unused expert
   for (uint32_t j = 0; j < k; j++) {
     float bv = -3.f;
     int bi = 0x7FFFFFFF;
-    for (uint32_t e = tid; e < E; e += kThreads) {
+    for (uint32_t e = lane; e < E; e += 32) {
       const float v = s_p[e];
       if (!s_used[e]) argmax_pair(bv, bi, v == v ? v : -2.f, int(e));
     }
@@ -191,24 +173,17 @@ __global__ void __launch_bounds__(kThreads) moe_router_topk(const float* __restr
       const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
       argmax_pair(bv, bi, v2, i2);
     }
-    __syncthreads();
     if (lane == 0) {
-      s_redf[warp] = bv;
-      s_redi[warp] = bi;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < kThreads / 32; w++) argmax_pair(bv, bi, s_redf[w], s_redi[w]);
       s_pick[j] = bi;
       s_used[bi] = 1;
     }
-    __syncthreads();
+    __syncwarp();
   }
-  if (tid == 0) {
+  if (lane == 0) {
     float sel = 0.f;
-    for (uint32_t j = 0; j < k; j++) sel += s_p[s_pick[j]] / s_sum;
+    for (uint32_t j = 0; j < k; j++) sel += s_p[s_pick[j]] / sm;
     for (uint32_t j = 0; j < k; j++) {
-      const float pw = s_p[s_pick[j]] / s_sum;
+      const float pw = s_p[s_pick[j]] / sm;
       routes->idx[t * k + j] = uint32_t(s_pick[j]);
       routes->w[t * k + j] = norm_topk ? pw / sel : pw;
     }
@@ -648,7 +623,7 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   float* logits = reinterpret_cast<float*>(s + L.logits);
   moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
       d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, h, logits);
-  moe_router_topk<<<T, kThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
+  moe_router_topk<<<T, 32, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   const int rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
@@ -692,7 +667,7 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
   float* logits = reinterpret_cast<float*>(s + L.logits);
   moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
       d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, h, logits);
-  moe_router_topk<<<T, kThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
+  moe_router_topk<<<T, 32, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);

@@ -1,21 +1,24 @@
 // GPU Zstandard (RFC 8878) decoder for vpack hi planes and kv_paged pages.
 //
 // Pipeline over a planned batch of jobs (host plan: zstd_plan.cpp):
-//   K1 block decode  - one CTA per block.  Warp 0 builds the Huffman table in
-//                      shared memory and decodes the (1 or 4) literal streams,
-//                      one lane per stream; warp 1 builds the LL/OF/ML FSE
-//                      tables (one lane each) and lane 0 decodes the sequence
-//                      bitstream, recording (literal length, match length,
-//                      offset value) and the block's repeat-offset transform
-//                      (each of the 3 repeat slots as "input slot minus d" or
-//                      a constant) so blocks need no serial pass.
+//   K1 block decode  - one CTA per block.  Four warps build the Huffman table
+//                      and decode the literal streams (one warp per stream,
+//                      32 lanes on spans that settle on codeword boundaries);
+//                      the fifth warp builds the LL/OF/ML FSE tables and walks
+//                      the sequence bitstream, storing each sequence's literal
+//                      length, match length and offset value.
+//   K1b seq scan     - one CTA per block: repeat-offset rules on symbolic slots
+//                      (each of the 3 repeat slots as "block-start slot minus
+//                      d" or a constant) and output / literal positions by a
+//                      block scan over sequence chunks; the block's output size
+//                      and repeat transform, so blocks need no serial pass.
 //   K2 job scan      - one thread per job: block output positions (prefix sum
 //                      of block sizes) and the repeat offsets every block starts
 //                      with (composition of the transforms); size checks.
-//   K3 block execute - one CTA per block: concrete offsets (serial replay of
-//                      the repeat-offset rules from the block's start state),
-//                      then every output byte is written as either a resolved
-//                      literal (bit 31 set | byte) or the position it copies.
+//   K3 block execute - one CTA per block: concrete offsets from the block's
+//                      start state, then every output byte is written as either
+//                      a resolved literal (bit 31 set | byte) or the position it
+//                      copies.
 //   K4 resolve       - pointer jumping over the decoded space: each pass
 //                      follows up to 16 copy links per byte with path
 //                      compression, so chains of any length resolve in
@@ -66,6 +69,7 @@ struct View {
   ZSeq* seq;
   ZBlockRt* rt;
   uint32_t* dirty;
+  uint2* list;  // two resolve worklists of (Z position, tile)
 };
 
 __device__ __forceinline__ View make_view(const uint8_t* img, uint8_t* scratch) {
@@ -82,6 +86,7 @@ __device__ __forceinline__ View make_view(const uint8_t* img, uint8_t* scratch) 
   v.seq = reinterpret_cast<ZSeq*>(scratch + v.h->s_seq);
   v.rt = reinterpret_cast<ZBlockRt*>(scratch + v.h->s_blk);
   v.dirty = reinterpret_cast<uint32_t*>(scratch + v.h->s_ctr);
+  v.list = reinterpret_cast<uint2*>(scratch + v.h->s_list);
   return v;
 }
 
@@ -492,78 +497,6 @@ __device__ __forceinline__ RepSlots rep_compose(const RepSlots& s, const RepSlot
   return o;
 }
 
-// Scan of one group of up to 32 decoded sequences (lane L holds sequence
-// i0 + L when `valid`): repeat-offset slots and output positions from the
-// group's carry-in (slots C, output position dst, literal position lit),
-// written as 32 consecutive ZSeq records; returns the carry-out.
-__device__ __forceinline__ void seq_group(ZSeq* out, uint32_t i0, bool valid, uint32_t ll, uint32_t ml, uint32_t ofv,
-                                          RepSlots& C, uint32_t& dst, uint32_t& lit) {
-  const int lane = threadIdx.x & 31;
-  RepSlots t;
-#pragma unroll
-  for (int q = 0; q < 3; q++) {
-    t.k[q] = uint32_t(q);
-    t.d[q] = 0;
-  }
-  uint32_t uk = 0, ud = 0;
-  if (valid) rep_step(t, ofv, ll, uk, ud);
-  RepSlots incl = t;
-  uint32_t sdst = valid ? ll + ml : 0u, slit = valid ? ll : 0u;
-  for (int o = 1; o < 32; o <<= 1) {
-    RepSlots prev;
-#pragma unroll
-    for (int q = 0; q < 3; q++) {
-      prev.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], o);
-      prev.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], o);
-    }
-    const uint32_t pd = __shfl_up_sync(0xFFFFFFFFu, sdst, o), pl = __shfl_up_sync(0xFFFFFFFFu, slit, o);
-    if (lane >= o) {
-      incl = rep_compose(prev, incl);
-      sdst += pd;
-      slit += pl;
-    }
-  }
-  RepSlots ex;
-#pragma unroll
-  for (int q = 0; q < 3; q++) {
-    ex.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], 1);
-    ex.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], 1);
-    if (lane == 0) {
-      ex.k[q] = uint32_t(q);
-      ex.d[q] = 0;
-    }
-  }
-  const RepSlots before = rep_compose(C, ex);
-  uint32_t ok, ov;
-  if (uk == 3) {
-    ok = 3;
-    ov = ud;
-  } else {
-    const uint32_t bk = uk == 0 ? before.k[0] : (uk == 1 ? before.k[1] : before.k[2]);
-    const uint32_t bd = uk == 0 ? before.d[0] : (uk == 1 ? before.d[1] : before.d[2]);
-    rep_sub(ok, ov, bk, bd, ud);
-  }
-  if (valid) {
-    ZSeq z;
-    z.ll = ll;
-    z.ml = ml;
-    z.oval = ov;
-    z.okind = ok;
-    z.dst = dst + sdst - (ll + ml);
-    z.lit = lit + slit - ll;
-    out[i0 + lane] = z;
-  }
-  RepSlots all;
-#pragma unroll
-  for (int q = 0; q < 3; q++) {
-    all.k[q] = __shfl_sync(0xFFFFFFFFu, incl.k[q], 31);
-    all.d[q] = __shfl_sync(0xFFFFFFFFu, incl.d[q], 31);
-  }
-  C = rep_compose(C, all);
-  dst += __shfl_sync(0xFFFFFFFFu, sdst, 31);
-  lit += __shfl_sync(0xFFFFFFFFu, slit, 31);
-}
-
 // Sequences section (RFC 8878 3.1.1.3.2.2) by the sequence warp.  All 32
 // lanes run the FSE walk in lockstep (same values; shared-memory reads are
 // broadcasts).  Each sequence reads its fields from fixed positions below the
@@ -571,9 +504,9 @@ __device__ __forceinline__ void seq_group(ZSeq* out, uint32_t i0, bool valid, ui
 // length extra, then the LL, ML and OF state bits -- so the six positions
 // come from the three table cells and every field from three independent
 // 32-bit reads of a shared-memory ring of the bitstream that the warp refills
-// with coalesced loads.  Lane L keeps sequence i when i % 32 == L; every 32
-// sequences one warp scan resolves their repeat offsets and output positions
-// (seq_group) and writes 32 records.
+// with coalesced loads.  It stores each sequence's literal length, match
+// length and offset value; zstd_seq_scan resolves repeat offsets and output
+// positions in parallel afterwards.
 __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh) {
   const int lane = threadIdx.x & 31;
   if (lane < 3) fse_build_dev(v.fse[b.fse[lane]], lane == 0 ? sh.ll : (lane == 1 ? sh.of : sh.ml), sh.next[lane],
@@ -596,13 +529,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
   }
   __syncwarp();
   ZSeq* out = v.seq + b.seq_off;
-  RepSlots C;
-#pragma unroll
-  for (int q = 0; q < 3; q++) {
-    C.k[q] = uint32_t(q);
-    C.d[q] = 0;
-  }
-  uint32_t dst = 0, lit = 0, st = 0;
+  uint32_t st = 0;
   const uint8_t* p = src + b.seq_src;
   const uint32_t len = b.seq_len;
   const uint32_t lastb = len ? __ldg(p + len - 1) : 0u;
@@ -660,8 +587,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       Pa -= int32_t(a0 + a1 + a2);
     }
     const uint32_t nseq = b.nseq;
-    uint32_t my_ll = 0, my_ml = 0, my_of = 0, i = 0;
-    for (; i < nseq && !st; i++) {
+    for (uint32_t i = 0; i < nseq && !st; i++) {
       // keep >= 4 entries of ring below the lowest word this sequence reads (<= 89 bits)
       if (((Pa - 96) >> 5) < lo_w) {
         const uint4 e = sh.sring[lo_w & 127];
@@ -696,26 +622,14 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       sml = (eML.x & 0xFFFFu) + bfe32(w3, 32u - ns, nML);
       sof = (eOF & 0xFFFFu) + bfe32(w3, 32u - ns - nOF, nOF);
       Pa -= int32_t(total);
-      if ((i & 31u) == uint32_t(lane)) {
-        my_ll = ll;
-        my_ml = ml;
-        my_of = ofv;
+      if (lane == 0) {  // raw record; zstd_seq_scan fills offsets and positions
+        *reinterpret_cast<uint2*>(&out[i].ll) = make_uint2(ll, ml);
+        out[i].oval = ofv;
       }
-      if ((i & 31u) == 31u) seq_group(out, i - 31, true, my_ll, my_ml, my_of, C, dst, lit);
     }
-    if (i & 31u) seq_group(out, i & ~31u, uint32_t(lane) < (i & 31u), my_ll, my_ml, my_of, C, dst, lit);
     if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;
   }
-  if (lane == 0) {
-    // lit = sum of literal lengths, dst - lit = sum of match lengths
-    if (lit > b.lit_regen) st |= VOOM_ZSTD_ST_SEQUENCES;
-    if (st) atomicOr(&sh.st, st);
-    sh.out_size = b.lit_regen + (dst - lit);
-    for (int k = 0; k < 3; k++) {
-      sh.rep_kind[k] = C.k[k];
-      sh.rep_val[k] = C.d[k];
-    }
-  }
+  if (lane == 0 && st) atomicOr(&sh.st, st);
 }
 
 __global__ void __launch_bounds__(kK1Threads) zstd_block_decode(const uint8_t* __restrict__ src,
@@ -748,13 +662,152 @@ __global__ void __launch_bounds__(kK1Threads) zstd_block_decode(const uint8_t* _
   else if (b.nseq) decode_sequences(src, v, b, sh);
   __syncthreads();
   if (threadIdx.x == 0) {
+    // blocks with sequences get out_size and the repeat transform from zstd_seq_scan
     uint32_t st = sh.st;
-    if (sh.out_size > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
+    if (!b.nseq && sh.out_size > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
     rt->out_size = sh.out_size;
     rt->status = st;
     for (int k = 0; k < 3; k++) {
-      rt->rep_kind[k] = sh.rep_kind[k];
-      rt->rep_val[k] = sh.rep_val[k];
+      rt->rep_kind[k] = uint32_t(k);
+      rt->rep_val[k] = 0;
+    }
+  }
+}
+
+// Per compressed block with sequences, after zstd_block_decode: the repeat-
+// offset rules and output / literal positions of every sequence (RFC 8878
+// 3.1.2.5).  Rounds of 256 consecutive records (coalesced loads and stores):
+// each thread takes one record's symbolic slot transform (slot = block-start
+// slot minus d, or a constant) and lengths, warps scan them, the 8 warp totals
+// are scanned in shared memory, and the round's carry-in (all earlier rounds
+// composed) gives every record its slots, offset and positions.  Also the
+// block's output size, its repeat transform for the job scan, and the
+// literal-count check.
+constexpr int kSeqScanThreads = 256;
+
+__global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch) {
+  __shared__ uint32_t s_k[kSeqScanThreads / 32][3], s_d[kSeqScanThreads / 32][3];
+  __shared__ uint32_t s_ll[kSeqScanThreads / 32], s_ml[kSeqScanThreads / 32];
+  const View v = make_view(img, scratch);
+  const ZBlock b = v.blocks[blockIdx.x];
+  if (b.type != 2 || b.nseq == 0) return;
+  ZBlockRt* rt = v.rt + blockIdx.x;
+  if (rt->status) return;  // the block failed in K1; its job is reported bad
+  ZSeq* seq = v.seq + b.seq_off;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, n = b.nseq;
+  RepSlots C;  // slots at the start of the round (relative to the block start)
+#pragma unroll
+  for (int q = 0; q < 3; q++) {
+    C.k[q] = uint32_t(q);
+    C.d[q] = 0;
+  }
+  uint32_t cll = 0, cml = 0;  // literal and match bytes before the round
+  for (uint32_t base = 0; base < n; base += kSeqScanThreads) {
+    const uint32_t i = base + tid;
+    const bool valid = i < n;
+    uint32_t ll = 0, ml = 0, ofv = 4;
+    if (valid) {
+      const uint2 lm = *reinterpret_cast<const uint2*>(&seq[i].ll);
+      ll = lm.x;
+      ml = lm.y;
+      ofv = seq[i].oval;
+    }
+    RepSlots t;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      t.k[q] = uint32_t(q);
+      t.d[q] = 0;
+    }
+    uint32_t uk = 0, ud = 0;
+    if (valid) rep_step(t, ofv, ll, uk, ud);
+    RepSlots incl = t;
+    uint32_t ill = ll, iml = ml;
+    for (int o = 1; o < 32; o <<= 1) {
+      RepSlots prev;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        prev.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], o);
+        prev.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], o);
+      }
+      const uint32_t pl = __shfl_up_sync(0xFFFFFFFFu, ill, o), pm = __shfl_up_sync(0xFFFFFFFFu, iml, o);
+      if (lane >= o) {
+        incl = rep_compose(prev, incl);
+        ill += pl;
+        iml += pm;
+      }
+    }
+    if (lane == 31) {
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        s_k[warp][q] = incl.k[q];
+        s_d[warp][q] = incl.d[q];
+      }
+      s_ll[warp] = ill;
+      s_ml[warp] = iml;
+    }
+    __syncthreads();
+    // this warp's carry-in within the round, then all warps' total
+    RepSlots cw = C, all = C;
+    uint32_t wll = cll, wml = cml, tll = cll, tml = cml;
+    for (uint32_t w = 0; w < kSeqScanThreads / 32; w++) {
+      RepSlots ww;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        ww.k[q] = s_k[w][q];
+        ww.d[q] = s_d[w][q];
+      }
+      if (w < warp) {
+        cw = rep_compose(cw, ww);
+        wll += s_ll[w];
+        wml += s_ml[w];
+      }
+      all = rep_compose(all, ww);
+      tll += s_ll[w];
+      tml += s_ml[w];
+    }
+    __syncthreads();  // s_k / s_d are rewritten next round
+    RepSlots ex;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      ex.k[q] = __shfl_up_sync(0xFFFFFFFFu, incl.k[q], 1);
+      ex.d[q] = __shfl_up_sync(0xFFFFFFFFu, incl.d[q], 1);
+      if (lane == 0) {
+        ex.k[q] = uint32_t(q);
+        ex.d[q] = 0;
+      }
+    }
+    uint32_t ell = __shfl_up_sync(0xFFFFFFFFu, ill, 1), eml = __shfl_up_sync(0xFFFFFFFFu, iml, 1);
+    if (lane == 0) ell = eml = 0;
+    if (valid) {
+      const RepSlots before = rep_compose(cw, ex);
+      uint32_t ok, ov;
+      if (uk == 3) {
+        ok = 3;
+        ov = ud;
+      } else {
+        const uint32_t bk = uk == 0 ? before.k[0] : (uk == 1 ? before.k[1] : before.k[2]);
+        const uint32_t bd = uk == 0 ? before.d[0] : (uk == 1 ? before.d[1] : before.d[2]);
+        rep_sub(ok, ov, bk, bd, ud);
+      }
+      const uint32_t lit = wll + ell, dst = lit + wml + eml;
+      // records are 24 bytes: (oval, okind) and (dst, lit) are 8-byte aligned pairs
+      *reinterpret_cast<uint2*>(&seq[i].oval) = make_uint2(ov, ok);
+      *reinterpret_cast<uint2*>(&seq[i].dst) = make_uint2(dst, lit);
+    }
+    C = all;
+    cll = tll;
+    cml = tml;
+  }
+  if (tid == 0) {
+    uint32_t st = 0;
+    if (cll > b.lit_regen) st |= VOOM_ZSTD_ST_SEQUENCES;
+    const uint32_t out_size = b.lit_regen + cml;
+    if (out_size > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
+    rt->out_size = out_size;
+    rt->status = st;
+    for (int k = 0; k < 3; k++) {
+      rt->rep_kind[k] = C.k[k];
+      rt->rep_val[k] = C.d[k];
     }
   }
 }
@@ -788,9 +841,16 @@ __global__ void zstd_job_scan(const uint8_t* img, uint8_t* scratch, uint32_t* st
   if (st) atomicOr(status + j, st);
 }
 
-__global__ void __launch_bounds__(128) zstd_block_execute(const uint8_t* __restrict__ src, const uint8_t* img,
+// Output chunk of K3: its entries are built in shared memory, then written out
+// with coalesced stores (a sequence's bytes are contiguous, but a warp's
+// sequences are not).
+constexpr uint32_t kExecChunk = 4096;
+constexpr uint32_t kExecMaxChunks = (128 * 1024) / kExecChunk + 1;
+
+__global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restrict__ src, const uint8_t* img,
                                                           uint8_t* scratch, uint32_t* status) {
-  __shared__ uint32_t s_end[2];
+  __shared__ uint32_t s_out[kExecChunk];
+  __shared__ uint32_t s_first[kExecMaxChunks];
   const View v = make_view(img, scratch);
   const ZBlock b = v.blocks[blockIdx.x];
   if (v.jobs[b.job].bad) return;
@@ -805,59 +865,135 @@ __global__ void __launch_bounds__(128) zstd_block_execute(const uint8_t* __restr
     for (uint32_t i = threadIdx.x; i < b.size; i += blockDim.x) res[i] = c;
     return;
   }
-  if (rt.status) return;  // the job already failed in K1
+  if (rt.status) return;  // the job already failed in K1 / K1b
   const ZSeq* seq = v.seq + b.seq_off;
   const uint8_t* lit = v.lit + b.lit_off;
   const uint64_t before = rt.zstart - rt.frame_zstart;
-  uint32_t bad = 0;
-  for (uint32_t i = threadIdx.x; i < b.nseq; i += blockDim.x) {
-    const ZSeq s = seq[i];
-    const uint32_t off = s.okind == 3 ? s.oval : rt.init_rep[s.okind] - s.oval;
-    const bool ok = off != 0 && uint64_t(off) <= before + s.dst + s.ll;
-    bad |= !ok;
-    for (uint32_t k = 0; k < s.ll; k++) res[s.dst + k] = kResolved | lit[s.lit + k];
-    const uint64_t m = rt.zstart + s.dst + s.ll;
-    for (uint32_t k = 0; k < s.ml; k++) res[s.dst + s.ll + k] = ok ? uint32_t(m + k - off) : kResolved;
-    if (i + 1 == b.nseq && threadIdx.x == (b.nseq - 1) % blockDim.x) {
-      s_end[0] = s.dst + s.ll + s.ml;
-      s_end[1] = s.lit + s.ll;
-    }
+  const uint32_t n = b.nseq, out_size = rt.out_size;
+  if (out_size > b.max_out) return;  // reported by K1b
+  const uint32_t nchunks = (out_size + kExecChunk - 1) / kExecChunk;
+  // the literal tail after the last sequence is record n
+  uint32_t tail_dst = 0, tail_lit = 0;
+  if (n) {
+    const ZSeq last = seq[n - 1];
+    tail_dst = last.dst + last.ll + last.ml;
+    tail_lit = last.lit + last.ll;
   }
-  if (threadIdx.x == 0 && b.nseq == 0) {
-    s_end[0] = 0;
-    s_end[1] = 0;
+  // s_first[c] = the record holding chunk c's first byte
+  for (uint32_t c = threadIdx.x; c < nchunks; c += blockDim.x) s_first[c] = n;
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const ZSeq s = seq[i];
+    const uint32_t len = s.ll + s.ml;
+    for (uint32_t c = (s.dst + kExecChunk - 1) / kExecChunk; c * kExecChunk < s.dst + len && c < nchunks; c++)
+      s_first[c] = i;
+  }
+  __syncthreads();
+  uint32_t bad = 0;
+  for (uint32_t c = 0; c < nchunks; c++) {
+    const uint32_t c0 = c * kExecChunk, c1 = min(out_size, c0 + kExecChunk);
+    for (uint32_t i = s_first[c] + threadIdx.x; i <= n; i += blockDim.x) {
+      uint32_t dst, ll, ml, lp, off = 0;
+      bool ok = true;
+      if (i < n) {
+        const ZSeq s = seq[i];
+        dst = s.dst;
+        ll = s.ll;
+        ml = s.ml;
+        lp = s.lit;
+        const uint32_t rep = s.okind == 0 ? rt.init_rep[0] : (s.okind == 1 ? rt.init_rep[1] : rt.init_rep[2]);
+        off = s.okind == 3 ? s.oval : rep - s.oval;
+        ok = off != 0 && uint64_t(off) <= before + dst + ll;
+      } else {
+        dst = tail_dst;
+        ll = b.lit_regen - tail_lit;
+        ml = 0;
+        lp = tail_lit;
+      }
+      if (dst >= c1) break;  // records are in output order
+      bad |= !ok;
+      const uint32_t a0 = max(dst, c0), a1 = min(dst + ll, c1);
+      for (uint32_t p = a0; p < a1; p++) s_out[p - c0] = kResolved | lit[lp + (p - dst)];
+      const uint64_t m = rt.zstart + dst + ll;
+      const uint32_t b0 = max(dst + ll, c0), b1 = min(dst + ll + ml, c1);
+      for (uint32_t p = b0; p < b1; p++) s_out[p - c0] = ok ? uint32_t(m + (p - dst - ll) - off) : kResolved;
+    }
+    __syncthreads();
+    for (uint32_t p = c0 + threadIdx.x; p < c1; p += blockDim.x) res[p] = s_out[p - c0];
+    __syncthreads();
   }
   if (bad) atomicOr(status + b.job, VOOM_ZSTD_ST_OFFSET);
-  __syncthreads();
-  const uint32_t pos = s_end[0], litp = s_end[1];
-  for (uint32_t k = threadIdx.x; k < b.lit_regen - litp; k += blockDim.x) res[pos + k] = kResolved | lit[litp + k];
 }
 
+// Counters after the tile flags: [0] worklist overflow, [1 + p] entries pass
+// p left unresolved.
+static_assert(kResolvePasses > 2, "the first list pass clears the tile flags, the last one sets them");
+
+__device__ __forceinline__ void list_push(const View& v, uint32_t* ctr, int pass, uint32_t z, uint32_t tile) {
+  const uint32_t i = atomicAdd(&ctr[1 + pass], 1u);
+  uint2* out = v.list + uint64_t(pass & 1) * v.h->list_cap;
+  if (i < v.h->list_cap) out[i] = make_uint2(z, tile);
+  else atomicOr(&ctr[0], 1u);
+}
+
+// Follows up to kHops copy links from u; returns the last value reached.
+__device__ __forceinline__ uint32_t chase(const View& v, uint32_t u, uint64_t zmax) {
+  for (int h = 0; h < kHops && !(u & kResolved); h++) {
+    if (u >= zmax) return kResolved;  // out-of-range link (only from a damaged stream)
+    u = v.res[u];
+  }
+  return u;
+}
+
+// Pass 0 scans every output tile: each unresolved byte follows up to 16 links
+// (path compression: the byte keeps the last link reached) and, if still
+// unresolved, goes on a worklist.  Later passes work the worklist only (one
+// thread per entry, the next list receives what is left); if the list
+// overflowed they rescan the tiles that still had unresolved bytes instead.
+// The tile flags K5 checks are cleared by the first list pass and set again by
+// the last one for entries left over.
 __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, uint32_t* status,
-                                                    int first_pass) {
+                                                    int pass) {
   __shared__ uint32_t s_unres;
   const View v = make_view(img, scratch);
+  uint32_t* ctr = v.dirty + v.h->n_tiles;
+  const uint64_t zmax = v.h->zbytes;
+  const bool list_mode = pass > 0 && !*reinterpret_cast<volatile uint32_t*>(&ctr[0]);
+  if (list_mode) {
+    if (pass == 1 && threadIdx.x == 0) v.dirty[blockIdx.x] = 0;
+    const uint64_t left = ctr[pass], cap = v.h->list_cap;  // left by pass - 1
+    const uint64_t n_in = left < cap ? left : cap;
+    const uint2* in = v.list + uint64_t((pass - 1) & 1) * v.h->list_cap;
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < n_in;
+         e += uint64_t(gridDim.x) * blockDim.x) {
+      const uint2 ent = in[e];
+      if (ent.x >= zmax || ent.y >= v.h->n_tiles) continue;
+      const uint32_t u = chase(v, v.res[ent.x], zmax);
+      v.res[ent.x] = u;
+      if (!(u & kResolved)) {
+        if (pass == kResolvePasses - 1) v.dirty[ent.y] = 1;
+        else list_push(v, ctr, pass, ent.x, ent.y);
+      }
+    }
+    return;
+  }
   const ZOutTile t = v.tiles[blockIdx.x];
-  if (!first_pass && !v.dirty[blockIdx.x]) return;
+  if (pass > 0 && !v.dirty[blockIdx.x]) return;
   const ZJob job = v.jobs[t.job];
   if (job.bad) return;
   if (threadIdx.x == 0) s_unres = 0;
   __syncthreads();
-  const uint64_t zmax = v.h->zbytes;
   uint32_t unres = 0;
   for (uint64_t k = t.begin + threadIdx.x; k < t.begin + t.len; k += blockDim.x) {
     const uint64_t z = job.zoff + k;
     uint32_t u = v.res[z];
     if (u & kResolved) continue;
-    for (int h = 0; h < kHops && !(u & kResolved); h++) {
-      if (u >= zmax) {
-        u = kResolved;
-        break;
-      }
-      u = v.res[u];
-    }
+    u = chase(v, u, zmax);
     v.res[z] = u;
-    unres += !(u & kResolved);
+    if (!(u & kResolved)) {
+      unres++;
+      if (pass == 0) list_push(v, ctr, 0, uint32_t(z), blockIdx.x);
+    }
   }
   if (unres) atomicAdd(&s_unres, unres);
   __syncthreads();
@@ -1004,14 +1140,17 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* img = static_cast<const uint8_t*>(d_plan);
   uint8_t* scr = static_cast<uint8_t*>(d_scratch);
+  // resolve worklist counters (after the tile flags)
+  if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
   if (h.n_blocks) {
     zstd_block_decode<<<h.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr);
+    zstd_seq_scan<<<h.n_blocks, kSeqScanThreads, 0, s>>>(img, scr);
     zstd_job_scan<<<(h.n_jobs + 127) / 128, 128, 0, s>>>(img, scr, d_status);
-    zstd_block_execute<<<h.n_blocks, 128, 0, s>>>(d_src, img, scr, d_status);
+    zstd_block_execute<<<h.n_blocks, 256, 0, s>>>(d_src, img, scr, d_status);
   }
   if (h.n_tiles) {
     for (int p = 0; p < kResolvePasses; p++)
-      zstd_resolve<<<h.n_tiles, 256, 0, s>>>(img, scr, d_status, p == 0);
+      zstd_resolve<<<h.n_tiles, 256, 0, s>>>(img, scr, d_status, p);
     zstd_output<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status);
   }
   if (h.n_frames) zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_status);

@@ -76,7 +76,8 @@ struct ZPlanHeader {
   uint64_t off_jobs, off_frames, off_blocks, off_huf, off_fse, off_tiles;
   uint64_t lit_bytes, n_seq, zbytes;
   // scratch layout (byte offsets into d_scratch)
-  uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_total;
+  uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_list, s_total;
+  uint64_t list_cap;  // entries per resolve worklist
 };
 
 // Per-sequence record in scratch.  The offset is stored symbolically, as
