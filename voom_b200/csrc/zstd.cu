@@ -163,6 +163,8 @@ struct DownWin {
 };
 
 // FSE decode table (RFC 8878 4.1.1): cell = symbol | nbBits << 8 | base << 16.
+// S = stride of the table in u32 words (2 when it is the x word of a uint2 cell array).
+template <int S>
 __device__ void fse_build_dev(const ZFse& f, uint32_t* t, uint16_t* next, int* al_out) {
   if (f.rle) {
     t[0] = f.rle_sym;
@@ -174,7 +176,7 @@ __device__ void fse_build_dev(const ZFse& f, uint32_t* t, uint16_t* next, int* a
   for (int s = 0; s < nsym; s++) {
     const int c = f.norm[s];
     if (c == -1) {
-      t[high--] = uint32_t(s);
+      t[S * high--] = uint32_t(s);
       next[s] = 1;
     } else {
       next[s] = uint16_t(c > 0 ? c : 0);
@@ -185,15 +187,15 @@ __device__ void fse_build_dev(const ZFse& f, uint32_t* t, uint16_t* next, int* a
   for (int s = 0; s < nsym; s++) {
     const int c = f.norm[s];
     for (int i = 0; i < c; i++) {
-      t[pos] = uint32_t(s);
+      t[S * pos] = uint32_t(s);
       do pos = (pos + step) & mask; while (pos > high);
     }
   }
   for (int u = 0; u < size; u++) {
-    const uint32_t s = t[u] & 0xFFu;
+    const uint32_t s = t[S * u] & 0xFFu;
     const uint32_t x = next[s]++;
     const uint32_t nb = uint32_t(al - (31 - __clz(x)));
-    t[u] = s | (nb << 8) | (((x << nb) - uint32_t(size)) << 16);
+    t[S * u] = s | (nb << 8) | (((x << nb) - uint32_t(size)) << 16);
   }
   *al_out = al;
 }
@@ -202,7 +204,7 @@ struct K1Shared {
   uint32_t huf3[2048];  // up to 3 symbols per lookup: s0|s1<<8|s2<<16|bits<<24|count<<28
   uint16_t huf[2048];
   uint16_t sstart[256];
-  uint32_t ll[512], of[256], ml[512];
+  uint32_t of[256];
   // sequence decode cells: low word = state base | nbBits << 16 | extra bits << 24,
   // high word = the code's baseline value (RFC 8878 3.1.1.3.2.1.1)
   uint2 ll2[512], ml2[512];
@@ -509,17 +511,19 @@ __device__ __forceinline__ RepSlots rep_compose(const RepSlots& s, const RepSlot
 // positions in parallel afterwards.
 __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh) {
   const int lane = threadIdx.x & 31;
-  if (lane < 3) fse_build_dev(v.fse[b.fse[lane]], lane == 0 ? sh.ll : (lane == 1 ? sh.of : sh.ml), sh.next[lane],
-                              &sh.al[lane]);
+  if (lane == 1) fse_build_dev<1>(v.fse[b.fse[1]], sh.of, sh.next[1], &sh.al[1]);
+  else if (lane == 0 || lane == 2)  // LL / ML tables built in the x words of their cell arrays
+    fse_build_dev<2>(v.fse[b.fse[lane]], reinterpret_cast<uint32_t*>(lane == 0 ? sh.ll2 : sh.ml2), sh.next[lane],
+                     &sh.al[lane]);
   __syncwarp();
   {
     const uint32_t nll = 1u << sh.al[0], nof = 1u << sh.al[1], nml = 1u << sh.al[2];
     for (uint32_t u = lane; u < nll; u += 32) {
-      const uint32_t t = sh.ll[u], c = min(t & 0xFFu, 35u);
+      const uint32_t t = sh.ll2[u].x, c = min(t & 0xFFu, 35u);
       sh.ll2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ll_bits[c]) << 24), c_ll_base[c]);
     }
     for (uint32_t u = lane; u < nml; u += 32) {
-      const uint32_t t = sh.ml[u], c = min(t & 0xFFu, 52u);
+      const uint32_t t = sh.ml2[u].x, c = min(t & 0xFFu, 52u);
       sh.ml2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ml_bits[c]) << 24), c_ml_base[c]);
     }
     for (uint32_t u = lane; u < nof; u += 32) {
@@ -632,7 +636,7 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
   if (lane == 0 && st) atomicOr(&sh.st, st);
 }
 
-__global__ void __launch_bounds__(kK1Threads) zstd_block_decode(const uint8_t* __restrict__ src,
+__global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t* __restrict__ src,
                                                                 const uint8_t* img, uint8_t* scratch) {
   __shared__ K1Shared sh;
   const View v = make_view(img, scratch);
