@@ -138,3 +138,39 @@ def test_expert_parallel_split_matches_full_layer(built_lib):
     check(load().voom_moe_combine(scratch.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, 1,
                                   _device.stream_ptr(x.device)), "voom_moe_combine")
     assert torch.equal(out, want)
+
+
+def test_expert_batches_producer_consumer(small):
+    """The engine's batch producer feeding consume_expert_batches with the fused
+    grouped SwiGLU: every routed expert computed once, in batch order, and each
+    expert's rows match the reference math."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from voom_b200.runtime import moe
+    from voom_b200.runtime.expert_batching import consume_expert_batches, iter_expert_batches
+
+    store, ex, _, _ = small
+    g = torch.Generator().manual_seed(11)
+    h = torch.randn((6, 512), generator=g).to(torch.bfloat16)
+    positions = {3: [0, 2], 0: [1], 7: [0, 3, 5], 11: [4], 5: [2, 5]}
+    ids = list(positions)
+    hd = h.cuda()
+    done = []
+
+    def fetch(batch):  # page mapping of a storage batch (pages stay compressed in HBM)
+        return {e: store.pages[e] for e in batch}
+
+    def consume(batch_ids, pages):
+        assert set(batch_ids) <= set(pages)
+        y = moe.swiglu_grouped(store, batch_ids, [positions[e] for e in batch_ids], hd).cpu()
+        row = 0
+        for e in batch_ids:
+            tl = positions[e]
+            assert om.rel_l2(y[row:row + len(tl)], om.swiglu(h[tl], *ex[e])) < TOL
+            row += len(tl)
+            done.append(e)
+
+    with ThreadPoolExecutor(max_workers=1) as pool:
+        consume_expert_batches(iter_expert_batches(ids, fetch, fetch_batch=2, compute_batch=1, executor=pool),
+                               consume)
+    assert done == ids

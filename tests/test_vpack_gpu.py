@@ -111,3 +111,23 @@ def test_smollm2_scaled_archive(built_lib):
     got = out.cpu().numpy()
     for (d, n), r in zip(spans, raws):
         assert np.array_equal(got[d:d + n], r)
+
+
+def test_packed_weight_store_through_weight_cache(archive_dir, decoded):
+    """WeightStore leg over the reference's archive: canonical -> stored name
+    translation at the archive boundary, pages materialised through WeightCache."""
+    from voom_b200.runtime.weight_cache import WeightCache
+    from voom_b200.runtime.weight_store import PackedWeightStore
+
+    index = json.loads((archive_dir / "weights.vpack2.index.json").read_text())
+    stored = sorted(index)
+    real = {f"model.{n}": n for n in stored}
+    store = PackedWeightStore(archive_dir, real_name=real, require_hashes=True)
+    cache = WeightCache(store, max_bytes=1 << 30)
+    logical = [f"model.{n}" for n in stored]
+    pages = cache.get_many([(f"page{i}", [name]) for i, name in enumerate(logical)])
+    for i, name in enumerate(logical):
+        t = pages[f"page{i}"][name]
+        assert t.is_cuda
+        assert sha(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()) == decoded[real[name]], name
+    assert cache.stats.misses == len(logical) and store.archive_bytes > 0
