@@ -604,10 +604,13 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       const uint32_t w1 = at(Pa - 32);
       const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
       const uint32_t eOF = sh.of[sof];
-      const uint32_t ofc = eOF >> 24, mlb = eML.x >> 24, llb = eLL.x >> 24;
+      // cell bytes: [0,1] next-state base, [2] state bits, [3] extra bits
+      const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
+                     llb = __byte_perm(eLL.x, 0, 0x4443);
       const bool more = i + 1 < nseq;
-      const uint32_t nLL = more ? bfe32(eLL.x, 16, 8) : 0u, nML = more ? bfe32(eML.x, 16, 8) : 0u,
-                     nOF = more ? bfe32(eOF, 16, 8) : 0u;
+      const uint32_t nLL = more ? __byte_perm(eLL.x, 0, 0x4442) : 0u,
+                     nML = more ? __byte_perm(eML.x, 0, 0x4442) : 0u,
+                     nOF = more ? __byte_perm(eOF, 0, 0x4442) : 0u;
       const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
       const uint32_t ns = nLL + nML;
       const uint32_t total = ox + ns + nOF;
@@ -615,16 +618,18 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
         st = VOOM_ZSTD_ST_SEQUENCES;
         break;
       }
-      // fields top-down: offset extra (<= 31 bits) from w1, ML and LL extras
-      // (<= 32 bits together) from the word below it, states (<= 26 bits)
-      // from the word below the extras
+      // Fields top-down, each the top n bits of a 32-bit window (n = 0 reads
+      // nothing: the clamped funnel shift by 32 gives 0): offset extra (<= 31
+      // bits) at the top of w1, ML then LL extras (<= 32 bits together) at the
+      // top of the word below it, the LL, ML, OF state bits (<= 26) at the top
+      // of the word below the extras.
       const uint32_t w2 = at(Pa - int32_t(ofc) - 32), w3 = at(Pa - int32_t(ox) - 32);
-      const uint32_t ofv = (1u << ofc) + bfe32(w1, 32u - ofc, ofc);
-      const uint32_t ml = eML.y + bfe32(w2, 32u - mlb, mlb);
-      const uint32_t ll = eLL.y + bfe32(w2, 32u - mlb - llb, llb);
-      sll = (eLL.x & 0xFFFFu) + bfe32(w3, 32u - nLL, nLL);
-      sml = (eML.x & 0xFFFFu) + bfe32(w3, 32u - ns, nML);
-      sof = (eOF & 0xFFFFu) + bfe32(w3, 32u - ns - nOF, nOF);
+      const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
+      const uint32_t ml = eML.y + __funnelshift_rc(w2, 0u, 32u - mlb);
+      const uint32_t ll = eLL.y + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
+      sll = (eLL.x & 0xFFFFu) + __funnelshift_rc(w3, 0u, 32u - nLL);
+      sml = (eML.x & 0xFFFFu) + __funnelshift_rc(w3 << nLL, 0u, 32u - nML);
+      sof = (eOF & 0xFFFFu) + __funnelshift_rc(w3 << ns, 0u, 32u - nOF);
       Pa -= int32_t(total);
       if (lane == 0) {  // raw record; zstd_seq_scan fills offsets and positions
         *reinterpret_cast<uint2*>(&out[i].ll) = make_uint2(ll, ml);

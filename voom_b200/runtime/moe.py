@@ -32,7 +32,20 @@ PAGES_DTYPE = np.dtype([("gate", PROJ_DTYPE), ("up", PROJ_DTYPE), ("down", PROJ_
 assert PAGES_DTYPE.itemsize == 144
 
 
-def tile_bytes_for(cols: int, every: int = EVERY, max_tile: int = 1 << 16) -> int:
+def every_for(cols: int, longest: int = 512) -> int:
+    """Checkpoint interval for rows of `cols` elements: the longest power of
+    two <= `longest` (and >= 64) dividing the row, so each lane pair of the
+    fused kernels decodes one whole row segment.  Longer segments mean fewer
+    decode lanes and fewer decode-table builds per projection."""
+    e = longest
+    while e > 64 and cols % e:
+        e //= 2
+    if cols % e:
+        raise ValueError(f"row length {cols} is not a multiple of 64")
+    return e
+
+
+def tile_bytes_for(cols: int, every: int = EVERY, max_tile: int = 1 << 17) -> int:
     """Tile size for a projection with rows of `cols` BF16: whole rows, at most
     128 checkpoint segments and at most `max_tile` bytes per tile."""
     if cols % every:
@@ -68,15 +81,17 @@ class ExpertStore:
     kernels skip it).  `alias` maps an expert id to another expert whose pages it
     shares (synthetic workloads that reuse one page set)."""
 
-    def __init__(self, experts: list, device, every: int = EVERY, alias: dict[int, int] | None = None):
+    def __init__(self, experts: list, device, every: int | None = None, alias: dict[int, int] | None = None):
         self.device = _device.require_cuda(device)
         alias = alias or {}
         self.pages: list = [None] * len(experts)
         for e, ws in enumerate(experts):
             if ws is not None and e not in alias:
                 g, u, d = ws
-                self.pages[e] = (ProjPage(g, self.device, every), ProjPage(u, self.device, every),
-                                 ProjPage(d, self.device, every))
+                eg = every or every_for(g.shape[1])
+                ed = every or every_for(d.shape[1])
+                self.pages[e] = (ProjPage(g, self.device, eg), ProjPage(u, self.device, eg),
+                                 ProjPage(d, self.device, ed))
         for e, src in alias.items():
             self.pages[e] = self.pages[src]
         first = next(ws for ws in experts if ws is not None)
