@@ -697,6 +697,9 @@ constexpr int kSeqScanThreads = 256;
 __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch) {
   __shared__ uint32_t s_k[kSeqScanThreads / 32][3], s_d[kSeqScanThreads / 32][3];
   __shared__ uint32_t s_ll[kSeqScanThreads / 32], s_ml[kSeqScanThreads / 32];
+  // per warp: carry-in slots and length sums; entry [8] = the round total
+  __shared__ uint32_t s_ck[kSeqScanThreads / 32 + 1][3], s_cd[kSeqScanThreads / 32 + 1][3];
+  __shared__ uint32_t s_cl[kSeqScanThreads / 32 + 1], s_cm[kSeqScanThreads / 32 + 1];
   const View v = make_view(img, scratch);
   const ZBlock b = v.blocks[blockIdx.x];
   if (b.type != 2 || b.nseq == 0) return;
@@ -755,26 +758,81 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
       s_ml[warp] = iml;
     }
     __syncthreads();
-    // this warp's carry-in within the round, then all warps' total
-    RepSlots cw = C, all = C;
-    uint32_t wll = cll, wml = cml, tll = cll, tml = cml;
-    for (uint32_t w = 0; w < kSeqScanThreads / 32; w++) {
-      RepSlots ww;
+    // warp 0 scans the 8 warp totals (lane w holds warp w's), starting from
+    // the round's carry-in C, and publishes each warp's carry-in and the total
+    if (warp == 0) {
+      constexpr int kW = kSeqScanThreads / 32;
+      RepSlots x;
+      uint32_t xl = 0, xm = 0;
 #pragma unroll
       for (int q = 0; q < 3; q++) {
-        ww.k[q] = s_k[w][q];
-        ww.d[q] = s_d[w][q];
+        x.k[q] = lane < kW ? s_k[lane][q] : uint32_t(q);
+        x.d[q] = lane < kW ? s_d[lane][q] : 0u;
       }
-      if (w < warp) {
-        cw = rep_compose(cw, ww);
-        wll += s_ll[w];
-        wml += s_ml[w];
+      if (lane < kW) {
+        xl = s_ll[lane];
+        xm = s_ml[lane];
       }
-      all = rep_compose(all, ww);
-      tll += s_ll[w];
-      tml += s_ml[w];
+      for (int o = 1; o < kW; o <<= 1) {
+        RepSlots prev;
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+          prev.k[q] = __shfl_up_sync(0xFFFFFFFFu, x.k[q], o);
+          prev.d[q] = __shfl_up_sync(0xFFFFFFFFu, x.d[q], o);
+        }
+        const uint32_t pl = __shfl_up_sync(0xFFFFFFFFu, xl, o), pm = __shfl_up_sync(0xFFFFFFFFu, xm, o);
+        if (lane >= o) {
+          x = rep_compose(prev, x);
+          xl += pl;
+          xm += pm;
+        }
+      }
+      // exclusive: carry-in of warp `lane` = C composed with warps 0..lane-1
+      RepSlots e;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        e.k[q] = __shfl_up_sync(0xFFFFFFFFu, x.k[q], 1);
+        e.d[q] = __shfl_up_sync(0xFFFFFFFFu, x.d[q], 1);
+        if (lane == 0) {
+          e.k[q] = uint32_t(q);
+          e.d[q] = 0;
+        }
+      }
+      uint32_t el = __shfl_up_sync(0xFFFFFFFFu, xl, 1), em = __shfl_up_sync(0xFFFFFFFFu, xm, 1);
+      if (lane == 0) el = em = 0;
+      const RepSlots cin = rep_compose(C, e);
+      if (lane < kW) {
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+          s_ck[lane][q] = cin.k[q];
+          s_cd[lane][q] = cin.d[q];
+        }
+        s_cl[lane] = cll + el;
+        s_cm[lane] = cml + em;
+      }
+      if (lane == kW - 1) {
+        const RepSlots tot = rep_compose(C, x);
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+          s_ck[kW][q] = tot.k[q];
+          s_cd[kW][q] = tot.d[q];
+        }
+        s_cl[kW] = cll + xl;
+        s_cm[kW] = cml + xm;
+      }
     }
-    __syncthreads();  // s_k / s_d are rewritten next round
+    __syncthreads();
+    RepSlots cw, all;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      cw.k[q] = s_ck[warp][q];
+      cw.d[q] = s_cd[warp][q];
+      all.k[q] = s_ck[kSeqScanThreads / 32][q];
+      all.d[q] = s_cd[kSeqScanThreads / 32][q];
+    }
+    const uint32_t wll = s_cl[warp], wml = s_cm[warp];
+    const uint32_t tll = s_cl[kSeqScanThreads / 32], tml = s_cm[kSeqScanThreads / 32];
+    __syncthreads();  // the shared totals are rewritten next round
     RepSlots ex;
 #pragma unroll
     for (int q = 0; q < 3; q++) {
