@@ -591,52 +591,77 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       Pa -= int32_t(a0 + a1 + a2);
     }
     const uint32_t nseq = b.nseq;
-    for (uint32_t i = 0; i < nseq && !st; i++) {
-      // keep >= 4 entries of ring below the lowest word this sequence reads (<= 89 bits)
-      if (((Pa - 96) >> 5) < lo_w) {
-        const uint4 e = sh.sring[lo_w & 127];
-        fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
-        lo_w -= 32;
-        pre = gword(lo_w - 32 + lane);
-        __syncwarp();
+    // Lane j keeps the bit position and table cells of sequence 32m + j; after
+    // every 32 sequences the lanes extract their sequences' fields together and
+    // store the 32 records, so the walk itself carries only the state chain.
+    // The 32 positions of a batch stay inside the ring: a sequence spans at
+    // most 89 bits and the ring is refilled 32 entries at a time.
+    int32_t myPa = 0;
+    uint32_t mll = 0, mml = 0, mof = 0;
+    auto flush = [&](uint32_t first, uint32_t count) {
+      if (uint32_t(lane) < count) {
+        const uint2 eLL = sh.ll2[mll], eML = sh.ml2[mml];
+        const uint32_t eOF = sh.of[mof];
+        const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
+                       llb = __byte_perm(eLL.x, 0, 0x4443);
+        // offset extra (<= 31 bits) at the top of the word below the
+        // position, ML then LL extras (<= 32 bits together) under it; a field
+        // of n bits is the top n bits of its window (n = 0: the clamped
+        // funnel shift by 32 gives 0)
+        const uint32_t w1 = at(myPa - 32), w2 = at(myPa - int32_t(ofc) - 32);
+        const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
+        const uint32_t ml = eML.y + __funnelshift_rc(w2, 0u, 32u - mlb);
+        const uint32_t ll = eLL.y + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
+        ZSeq* r = out + first + lane;  // raw record; zstd_seq_scan fills offsets and positions
+        *reinterpret_cast<uint2*>(&r->ll) = make_uint2(ll, ml);
+        r->oval = ofv;
       }
-      // the 32 bits below Pa, read alongside the table cells
-      const uint32_t w1 = at(Pa - 32);
-      const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
-      const uint32_t eOF = sh.of[sof];
-      // cell bytes: [0,1] next-state base, [2] state bits, [3] extra bits
-      const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
-                     llb = __byte_perm(eLL.x, 0, 0x4443);
-      const bool more = i + 1 < nseq;
-      const uint32_t nLL = more ? __byte_perm(eLL.x, 0, 0x4442) : 0u,
-                     nML = more ? __byte_perm(eML.x, 0, 0x4442) : 0u,
-                     nOF = more ? __byte_perm(eOF, 0, 0x4442) : 0u;
-      const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
-      const uint32_t ns = nLL + nML;
-      const uint32_t total = ox + ns + nOF;
-      if (Pa - boff < int32_t(total)) {
-        st = VOOM_ZSTD_ST_SEQUENCES;
-        break;
+    };
+    if (!st) {
+      uint32_t j = 0, first = 0;
+      for (uint32_t i = 0; i < nseq; i++) {
+        // keep >= 4 entries of ring below the lowest word this sequence reads (<= 89 bits)
+        if (((Pa - 96) >> 5) < lo_w) {
+          const uint4 e = sh.sring[lo_w & 127];
+          fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
+          lo_w -= 32;
+          pre = gword(lo_w - 32 + lane);
+          __syncwarp();
+        }
+        const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
+        const uint32_t eOF = sh.of[sof];
+        if (uint32_t(lane) == j) {
+          myPa = Pa;
+          mll = sll;
+          mml = sml;
+          mof = sof;
+        }
+        // cell bytes: [0,1] next-state base, [2] state bits, [3] extra bits
+        const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
+                       llb = __byte_perm(eLL.x, 0, 0x4443);
+        const bool more = i + 1 < nseq;
+        const uint32_t nLL = more ? __byte_perm(eLL.x, 0, 0x4442) : 0u,
+                       nML = more ? __byte_perm(eML.x, 0, 0x4442) : 0u,
+                       nOF = more ? __byte_perm(eOF, 0, 0x4442) : 0u;
+        const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
+        const uint32_t ns = nLL + nML;
+        // LL, ML, OF state bits (<= 26) at the top of the word below the extras
+        const uint32_t w3 = at(Pa - int32_t(ox) - 32);
+        sll = (eLL.x & 0xFFFFu) + __funnelshift_rc(w3, 0u, 32u - nLL);
+        sml = (eML.x & 0xFFFFu) + __funnelshift_rc(w3 << nLL, 0u, 32u - nML);
+        sof = (eOF & 0xFFFFu) + __funnelshift_rc(w3 << ns, 0u, 32u - nOF);
+        // A stream that runs out reads zero words below its start (never
+        // memory outside it) and ends with Pa below boff: checked once below.
+        Pa -= int32_t(ox + ns + nOF);
+        if (++j == 32) {
+          flush(first, 32);
+          first += 32;
+          j = 0;
+        }
       }
-      // Fields top-down, each the top n bits of a 32-bit window (n = 0 reads
-      // nothing: the clamped funnel shift by 32 gives 0): offset extra (<= 31
-      // bits) at the top of w1, ML then LL extras (<= 32 bits together) at the
-      // top of the word below it, the LL, ML, OF state bits (<= 26) at the top
-      // of the word below the extras.
-      const uint32_t w2 = at(Pa - int32_t(ofc) - 32), w3 = at(Pa - int32_t(ox) - 32);
-      const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
-      const uint32_t ml = eML.y + __funnelshift_rc(w2, 0u, 32u - mlb);
-      const uint32_t ll = eLL.y + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
-      sll = (eLL.x & 0xFFFFu) + __funnelshift_rc(w3, 0u, 32u - nLL);
-      sml = (eML.x & 0xFFFFu) + __funnelshift_rc(w3 << nLL, 0u, 32u - nML);
-      sof = (eOF & 0xFFFFu) + __funnelshift_rc(w3 << ns, 0u, 32u - nOF);
-      Pa -= int32_t(total);
-      if (lane == 0) {  // raw record; zstd_seq_scan fills offsets and positions
-        *reinterpret_cast<uint2*>(&out[i].ll) = make_uint2(ll, ml);
-        out[i].oval = ofv;
-      }
+      flush(first, j);
     }
-    if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;
+    if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;  // overrun (Pa < boff) or bits left over
   }
   if (lane == 0 && st) atomicOr(&sh.st, st);
 }
@@ -992,14 +1017,33 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
   if (bad) atomicOr(status + b.job, VOOM_ZSTD_ST_OFFSET);
 }
 
-// Counters after the tile flags: [0] worklist overflow, [1 + p] entries pass
-// p left unresolved.
-static_assert(kResolvePasses > 2, "the first list pass clears the tile flags, the last one sets them");
+// Match links left by block execution are resolved in three steps.
+//  zstd_output (one CTA per output tile) streams the tile's link words, follows
+//    each unresolved byte's links up to kHops times (the links of 8
+//    neighbouring bytes in lockstep, so their loads are in flight together),
+//    stores what it reached back (path compression: chains through the byte
+//    stop there) and writes every resolved byte to the output, interleaved
+//    with the lo plane.  A byte still unresolved goes on worklist 0; its
+//    output byte is written later.
+//  zstd_resolve passes 1 .. kResolvePasses-1 follow the links of the worklist
+//    entries (list p-1 in, list p out; lists 1 and 2 alternate).
+//  zstd_patch writes the output byte of every worklist-0 entry, or flags the
+//    job when its chain is still unresolved.
+// If worklist 0 overflows, the passes rescan the tiles that had unresolved
+// bytes and zstd_patch rewrites those tiles whole.  Later lists cannot
+// overflow: a pass pushes at most one entry per entry it reads.
+// Counters after the tile flags: [0] worklist-0 overflow, [1 + p] entries
+// pushed by pass p.  A tile flag holds kPatch | unresolved count.
+static_assert(kResolvePasses > 1, "at least one list pass");
+constexpr uint32_t kPatch = 0x80000000u;
+
+__device__ __forceinline__ uint2* list_at(const View& v, int pass) {
+  return v.list + uint64_t(pass == 0 ? 0 : 1 + ((pass - 1) & 1)) * v.h->list_cap;
+}
 
 __device__ __forceinline__ void list_push(const View& v, uint32_t* ctr, int pass, uint32_t z, uint32_t tile) {
   const uint32_t i = atomicAdd(&ctr[1 + pass], 1u);
-  uint2* out = v.list + uint64_t(pass & 1) * v.h->list_cap;
-  if (i < v.h->list_cap) out[i] = make_uint2(z, tile);
+  if (i < v.h->list_cap) list_at(v, pass)[i] = make_uint2(z, tile);
   else atomicOr(&ctr[0], 1u);
 }
 
@@ -1012,42 +1056,151 @@ __device__ __forceinline__ uint32_t chase(const View& v, uint32_t u, uint64_t zm
   return u;
 }
 
-// Pass 0 scans every output tile: each unresolved byte follows up to 16 links
-// (path compression: the byte keeps the last link reached) and, if still
-// unresolved, goes on a worklist.  Later passes work the worklist only (one
-// thread per entry, the next list receives what is left); if the list
-// overflowed they rescan the tiles that still had unresolved bytes instead.
-// The tile flags K5 checks are cleared by the first list pass and set again by
-// the last one for entries left over.
-__global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, uint32_t* status,
-                                                    int pass) {
+// chase() of 8 links in lockstep rounds: the loads of one round are
+// independent, so up to 8 are in flight per thread.
+__device__ __forceinline__ void chase8(const View& v, uint32_t (&u)[8], uint64_t zmax) {
+  for (int h = 0; h < kHops; h++) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (!(u[i] & kResolved)) u[i] = u[i] < zmax ? v.res[u[i]] : kResolved;
+    if (u[0] & u[1] & u[2] & u[3] & u[4] & u[5] & u[6] & u[7] & kResolved) return;
+  }
+}
+
+// Output bytes of job bytes k .. k+7 (hi0 = bytes 0-3, hi1 = bytes 4-7):
+// interleaved with the body's lo plane (vpack) or stored as they are.
+__device__ __forceinline__ void emit8(const ZJob& job, const uint8_t* __restrict__ src, uint8_t* __restrict__ out,
+                                      uint64_t k, uint32_t hi0, uint32_t hi1) {
+  if (job.flags & VOOM_ZSTD_INTERLEAVE) {
+    const uint64_t lo = load8(src + job.lo_src + k);
+    const uint32_t lo0 = uint32_t(lo), lo1 = uint32_t(lo >> 32);
+    uint4 o;
+    o.x = __byte_perm(lo0, hi0, 0x5140);
+    o.y = __byte_perm(lo0, hi0, 0x7362);
+    o.z = __byte_perm(lo1, hi1, 0x5140);
+    o.w = __byte_perm(lo1, hi1, 0x7362);
+    uint8_t* d = out + job.dst + 2 * k;
+    if ((job.dst & 15u) == 0) {
+      *reinterpret_cast<uint4*>(d) = o;
+    } else {
+      const uint32_t wv[4] = {o.x, o.y, o.z, o.w};
+      for (int i = 0; i < 16; i++) d[i] = uint8_t(wv[i >> 2] >> (8 * (i & 3)));
+    }
+  } else {
+    uint8_t* d = out + job.dst + k;
+    if ((reinterpret_cast<uintptr_t>(d) & 7u) == 0) {
+      *reinterpret_cast<uint2*>(d) = make_uint2(hi0, hi1);
+    } else {
+      for (int i = 0; i < 8; i++) d[i] = uint8_t((i < 4 ? hi0 : hi1) >> (8 * (i & 3)));
+    }
+  }
+}
+
+__device__ __forceinline__ void emit1(const ZJob& job, const uint8_t* __restrict__ src, uint8_t* __restrict__ out,
+                                      uint64_t k, uint8_t hb, bool lo_too) {
+  if (job.flags & VOOM_ZSTD_INTERLEAVE) {
+    if (lo_too) out[job.dst + 2 * k] = __ldg(src + job.lo_src + k);
+    out[job.dst + 2 * k + 1] = hb;
+  } else {
+    out[job.dst + k] = hb;
+  }
+}
+
+__device__ __forceinline__ uint32_t low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+__global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ src, const uint8_t* img,
+                                                   uint8_t* scratch, uint8_t* __restrict__ out) {
+  __shared__ uint32_t s_unres;
+  const View v = make_view(img, scratch);
+  const ZOutTile t = v.tiles[blockIdx.x];
+  const ZJob job = v.jobs[t.job];
+  if (job.bad) return;
+  if (threadIdx.x == 0) s_unres = 0;
+  __syncthreads();
+  uint32_t* ctr = v.dirty + v.h->n_tiles;
+  const uint64_t zmax = v.h->zbytes;
+  const uint64_t end = t.begin + t.len;
+  uint32_t unres = 0;
+  // The tile is walked in block-wide steps of 8 bytes per thread with a
+  // barrier after each, so chains into earlier steps of the tile end at the
+  // value stored there (match offsets are mostly longer than one step).  Each
+  // thread loads its next link words before chasing the current ones; only
+  // the owning thread ever writes a position here, so the early load is exact.
+  const uint32_t step = 8u * blockDim.x;
+  uint4 n0 = make_uint4(0, 0, 0, 0), n1 = n0;
+  if (t.begin + 8u * threadIdx.x + 8 <= end) {
+    n0 = *reinterpret_cast<const uint4*>(v.res + job.zoff + t.begin + 8u * threadIdx.x);
+    n1 = *reinterpret_cast<const uint4*>(v.res + job.zoff + t.begin + 8u * threadIdx.x + 4);
+  }
+  for (uint64_t base = t.begin; base < end; base += step) {
+    const uint64_t k = base + 8u * threadIdx.x;
+    const uint64_t z = job.zoff + k;
+    const uint4 r0 = n0, r1 = n1;
+    if (k + step + 8 <= end) {
+      n0 = *reinterpret_cast<const uint4*>(v.res + z + step);
+      n1 = *reinterpret_cast<const uint4*>(v.res + z + step + 4);
+    }
+    if (k + 8 <= end) {
+      uint32_t u[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+      if (!(u[0] & u[1] & u[2] & u[3] & u[4] & u[5] & u[6] & u[7] & kResolved)) {
+        chase8(v, u, zmax);
+        // path compression: later chains through these bytes stop here
+        *reinterpret_cast<uint4*>(v.res + z) = make_uint4(u[0], u[1], u[2], u[3]);
+        *reinterpret_cast<uint4*>(v.res + z + 4) = make_uint4(u[4], u[5], u[6], u[7]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (!(u[i] & kResolved)) {
+            unres++;
+            list_push(v, ctr, 0, uint32_t(z + i), blockIdx.x);
+          }
+        }
+      }
+      emit8(job, src, out, k, low_bytes(u[0], u[1], u[2], u[3]), low_bytes(u[4], u[5], u[6], u[7]));
+    } else if (k < end) {
+      for (uint32_t i = 0; i < uint32_t(end - k); i++) {
+        uint32_t u = v.res[z + i];
+        if (!(u & kResolved)) {
+          u = chase(v, u, zmax);
+          v.res[z + i] = u;
+          if (!(u & kResolved)) {
+            unres++;
+            list_push(v, ctr, 0, uint32_t(z + i), blockIdx.x);
+          }
+        }
+        emit1(job, src, out, k + i, uint8_t(u), true);
+      }
+    }
+    __syncthreads();
+  }
+  if (unres) atomicAdd(&s_unres, unres);
+  __syncthreads();
+  if (threadIdx.x == 0) v.dirty[blockIdx.x] = s_unres ? (kPatch | s_unres) : 0u;
+}
+
+__global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, int pass) {
   __shared__ uint32_t s_unres;
   const View v = make_view(img, scratch);
   uint32_t* ctr = v.dirty + v.h->n_tiles;
   const uint64_t zmax = v.h->zbytes;
-  const bool list_mode = pass > 0 && !*reinterpret_cast<volatile uint32_t*>(&ctr[0]);
-  if (list_mode) {
-    if (pass == 1 && threadIdx.x == 0) v.dirty[blockIdx.x] = 0;
-    const uint64_t left = ctr[pass], cap = v.h->list_cap;  // left by pass - 1
+  if (!*reinterpret_cast<volatile uint32_t*>(&ctr[0])) {
+    const uint64_t left = ctr[pass], cap = v.h->list_cap;  // pushed by pass - 1
     const uint64_t n_in = left < cap ? left : cap;
-    const uint2* in = v.list + uint64_t((pass - 1) & 1) * v.h->list_cap;
+    const uint2* in = list_at(v, pass - 1);
     for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < n_in;
          e += uint64_t(gridDim.x) * blockDim.x) {
       const uint2 ent = in[e];
       if (ent.x >= zmax || ent.y >= v.h->n_tiles) continue;
       const uint32_t u = chase(v, v.res[ent.x], zmax);
       v.res[ent.x] = u;
-      if (!(u & kResolved)) {
-        if (pass == kResolvePasses - 1) v.dirty[ent.y] = 1;
-        else list_push(v, ctr, pass, ent.x, ent.y);
-      }
+      if (!(u & kResolved) && pass + 1 < kResolvePasses) list_push(v, ctr, pass, ent.x, ent.y);
     }
     return;
   }
   const ZOutTile t = v.tiles[blockIdx.x];
-  if (pass > 0 && !v.dirty[blockIdx.x]) return;
   const ZJob job = v.jobs[t.job];
-  if (job.bad) return;
+  if (job.bad || !(v.dirty[blockIdx.x] & ~kPatch)) return;
   if (threadIdx.x == 0) s_unres = 0;
   __syncthreads();
   uint32_t unres = 0;
@@ -1057,28 +1210,44 @@ __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t*
     if (u & kResolved) continue;
     u = chase(v, u, zmax);
     v.res[z] = u;
-    if (!(u & kResolved)) {
-      unres++;
-      if (pass == 0) list_push(v, ctr, 0, uint32_t(z), blockIdx.x);
-    }
+    unres += !(u & kResolved);
   }
   if (unres) atomicAdd(&s_unres, unres);
   __syncthreads();
-  if (threadIdx.x == 0) v.dirty[blockIdx.x] = s_unres;
+  if (threadIdx.x == 0) v.dirty[blockIdx.x] = kPatch | s_unres;
 }
 
-__global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                   uint8_t* scratch, uint8_t* __restrict__ out, uint32_t* status) {
+__global__ void __launch_bounds__(256) zstd_patch(const uint8_t* __restrict__ src, const uint8_t* img,
+                                                  uint8_t* scratch, uint8_t* __restrict__ out, uint32_t* status) {
   const View v = make_view(img, scratch);
+  uint32_t* ctr = v.dirty + v.h->n_tiles;
+  const uint64_t zmax = v.h->zbytes;
+  if (!*reinterpret_cast<volatile uint32_t*>(&ctr[0])) {
+    const uint64_t left = ctr[1], cap = v.h->list_cap;
+    const uint64_t n_in = left < cap ? left : cap;
+    const uint2* in = list_at(v, 0);
+    for (uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; e < n_in;
+         e += uint64_t(gridDim.x) * blockDim.x) {
+      const uint2 ent = in[e];
+      if (ent.x >= zmax || ent.y >= v.h->n_tiles) continue;
+      const uint32_t j = v.tiles[ent.y].job;
+      const uint32_t u = v.res[ent.x];
+      if (!(u & kResolved)) {
+        atomicOr(status + j, VOOM_ZSTD_ST_UNRESOLVED);
+        continue;
+      }
+      const ZJob& job = v.jobs[j];
+      emit1(job, src, out, ent.x - job.zoff, uint8_t(u), false);
+    }
+    return;
+  }
   const ZOutTile t = v.tiles[blockIdx.x];
   const ZJob job = v.jobs[t.job];
-  if (job.bad) return;
-  if (v.dirty[blockIdx.x]) {
+  if (job.bad || !(v.dirty[blockIdx.x] & kPatch)) return;
+  if (v.dirty[blockIdx.x] & ~kPatch) {
     if (threadIdx.x == 0) atomicOr(status + t.job, VOOM_ZSTD_ST_UNRESOLVED);
     return;
   }
-  const bool inter = job.flags & VOOM_ZSTD_INTERLEAVE;
-  const bool vec = ((job.dst & 15u) == 0);
   const uint64_t end = t.begin + t.len;
   for (uint64_t k = t.begin + 8u * threadIdx.x; k < end; k += 8u * blockDim.x) {
     const uint64_t z = job.zoff + k;
@@ -1086,41 +1255,9 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
     if (cnt == 8) {
       const uint4 r0 = *reinterpret_cast<const uint4*>(v.res + z);
       const uint4 r1 = *reinterpret_cast<const uint4*>(v.res + z + 4);
-      const uint32_t hi0 = __byte_perm(__byte_perm(r0.x, r0.y, 0x0040), __byte_perm(r0.z, r0.w, 0x0040), 0x5410);
-      const uint32_t hi1 = __byte_perm(__byte_perm(r1.x, r1.y, 0x0040), __byte_perm(r1.z, r1.w, 0x0040), 0x5410);
-      if (inter) {
-        const uint64_t lo = load8(src + job.lo_src + k);
-        const uint32_t lo0 = uint32_t(lo), lo1 = uint32_t(lo >> 32);
-        uint4 o;
-        o.x = __byte_perm(lo0, hi0, 0x5140);
-        o.y = __byte_perm(lo0, hi0, 0x7362);
-        o.z = __byte_perm(lo1, hi1, 0x5140);
-        o.w = __byte_perm(lo1, hi1, 0x7362);
-        uint8_t* d = out + job.dst + 2 * k;
-        if (vec) {
-          *reinterpret_cast<uint4*>(d) = o;
-        } else {
-          const uint32_t wv[4] = {o.x, o.y, o.z, o.w};
-          for (int i = 0; i < 16; i++) d[i] = uint8_t(wv[i >> 2] >> (8 * (i & 3)));
-        }
-      } else {
-        uint8_t* d = out + job.dst + k;
-        if ((reinterpret_cast<uintptr_t>(d) & 7u) == 0) {
-          *reinterpret_cast<uint2*>(d) = make_uint2(hi0, hi1);
-        } else {
-          for (int i = 0; i < 8; i++) d[i] = uint8_t((i < 4 ? hi0 : hi1) >> (8 * (i & 3)));
-        }
-      }
+      emit8(job, src, out, k, low_bytes(r0.x, r0.y, r0.z, r0.w), low_bytes(r1.x, r1.y, r1.z, r1.w));
     } else {
-      for (uint32_t i = 0; i < cnt; i++) {
-        const uint8_t hb = uint8_t(v.res[z + i]);
-        if (inter) {
-          out[job.dst + 2 * (k + i)] = __ldg(src + job.lo_src + k + i);
-          out[job.dst + 2 * (k + i) + 1] = hb;
-        } else {
-          out[job.dst + k + i] = hb;
-        }
-      }
+      for (uint32_t i = 0; i < cnt; i++) emit1(job, src, out, k + i, uint8_t(v.res[z + i]), true);
     }
   }
 }
@@ -1128,12 +1265,15 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
 // XXH64 (xxHash specification) of a frame's decoded bytes, one thread per frame.
 __device__ __forceinline__ uint64_t rotl64(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
 
-__global__ void zstd_checksum(const uint8_t* img, uint8_t* scratch, uint32_t* status) {
+// The bytes are read back from the output (hi bytes of an interleaved body).
+__global__ void zstd_checksum(const uint8_t* img, uint8_t* scratch, const uint8_t* __restrict__ out,
+                              uint32_t* status) {
   const View v = make_view(img, scratch);
   const uint32_t f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= v.h->n_frames) return;
   const ZFrame fr = v.frames[f];
-  if (!fr.csum_flag || v.jobs[fr.job].bad || status[fr.job]) return;
+  const ZJob& job = v.jobs[fr.job];
+  if (!fr.csum_flag || job.bad || status[fr.job]) return;
   const uint64_t P1 = 0x9E3779B185EBCA87ull, P2 = 0xC2B2AE3D27D4EB4Full, P3 = 0x165667B19E3779F9ull,
                  P4 = 0x85EBCA77C2B2AE63ull, P5 = 0x27D4EB2F165667C5ull;
   uint64_t z0 = 0, n = 0;
@@ -1143,8 +1283,10 @@ __global__ void zstd_checksum(const uint8_t* img, uint8_t* scratch, uint32_t* st
     z0 = a.zstart;
     n = l.zstart + l.out_size - z0;
   }
-  const uint32_t* r = v.res + z0;
-  auto byte = [&](uint64_t i) { return uint64_t(r[i] & 0xFFu); };
+  const bool inter = job.flags & VOOM_ZSTD_INTERLEAVE;
+  const uint8_t* r = out + job.dst + (inter ? 2 * (z0 - job.zoff) + 1 : z0 - job.zoff);
+  const uint32_t stride = inter ? 2u : 1u;
+  auto byte = [&](uint64_t i) { return uint64_t(r[stride * i]); };
   auto rd = [&](uint64_t i, int nb) {
     uint64_t x = 0;
     for (int k = 0; k < nb; k++) x |= byte(i + k) << (8 * k);
@@ -1216,10 +1358,10 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
     zstd_block_execute<<<h.n_blocks, 256, 0, s>>>(d_src, img, scr, d_status);
   }
   if (h.n_tiles) {
-    for (int p = 0; p < kResolvePasses; p++)
-      zstd_resolve<<<h.n_tiles, 256, 0, s>>>(img, scr, d_status, p);
-    zstd_output<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status);
+    zstd_output<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out);
+    for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<h.n_tiles, 256, 0, s>>>(img, scr, p);
+    zstd_patch<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status);
   }
-  if (h.n_frames) zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_status);
+  if (h.n_frames) zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_out, d_status);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

@@ -657,9 +657,11 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   h.s_seq = s; s = align_up(s + sizeof(ZSeq) * nseq, 256);
   h.s_blk = s; s = align_up(s + sizeof(ZBlockRt) * P->blocks.size(), 256);
   h.s_ctr = s; s = align_up(s + 4 * P->tiles.size() + 256, 256);
-  // two worklists of Z positions still unresolved after a resolve pass
+  // three worklists of Z positions still unresolved: list 0 from the output
+  // pass (kept for the patch pass), lists 1 and 2 alternating between the
+  // resolve passes
   h.list_cap = std::max<uint64_t>(65536, zoff / 64);
-  h.s_list = s; s = align_up(s + 2 * 8 * h.list_cap, 256);
+  h.s_list = s; s = align_up(s + 3 * 8 * h.list_cap, 256);
   h.s_total = s;
   return P;
 }

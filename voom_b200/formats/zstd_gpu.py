@@ -166,6 +166,44 @@ def decompress_device(data, size: int | None = None, *, device=None,
     return out[:size]
 
 
+def decompress_many(frames: list, sizes: list[int] | None = None, *, device=None, align: int = 256,
+                    stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, list[tuple[int, int]]]:
+    """Many independent zstd frames in ONE batched GPU decode: returns the
+    device buffer and each frame's (offset, length) in it (offsets aligned to
+    `align` bytes).  Raises ZstdError naming the first failing frame's fault."""
+    dev = _device.require_cuda(device)
+    arrs = [_device.as_u8(f) for f in frames]
+    if sizes is None:
+        sizes = []
+        for a in arrs:
+            n = frame_content_size(a)
+            if n is None:
+                raise ZstdError("frame content size unknown; pass sizes=")
+            sizes.append(n)
+    if len(sizes) != len(arrs):
+        raise ValueError("one size per frame")
+    jobs = np.zeros(len(arrs), dtype=JOB_DTYPE)
+    spans, src, dst = [], 0, 0
+    for i, (a, n) in enumerate(zip(arrs, sizes)):
+        jobs[i] = (src, a.size, dst, n, 0, 0, 0)
+        spans.append((dst, int(n)))
+        src += a.size
+        dst += (int(n) + align - 1) // align * align
+    host = np.concatenate(arrs) if arrs else np.zeros(0, np.uint8)
+    with torch.cuda.device(dev):
+        out = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
+        if not arrs:
+            return out, spans
+        plan = ZstdPlan(host, jobs)
+        d_src = _device.upload(host, dev, stream=stream)
+        batch = ZstdBatch(plan, dev)
+        batch.run(d_src, out, stream)
+        st = batch.job_status()
+    if st.any():
+        raise ZstdError(describe(int(st[np.nonzero(st)[0][0]])))
+    return out, spans
+
+
 def decompress(data, size: int | None = None) -> bytes:
     """Drop-in for compression.zstd.decompress(data) (bytes in, bytes out)."""
     return decompress_device(data, size).cpu().numpy().tobytes()
