@@ -209,6 +209,7 @@ struct K1Shared {
   // high word = the code's baseline value (RFC 8878 3.1.1.3.2.1.1)
   uint2 ll2[512], ml2[512];
   uint4 sring[128];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 127
+  uint4 skeep[32];   // per sequence of the current batch: bit position, LL, ML, OF states
   uint16_t next[3][64];
   int al[3];
   uint32_t st;
@@ -591,17 +592,19 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       Pa -= int32_t(a0 + a1 + a2);
     }
     const uint32_t nseq = b.nseq;
-    // Lane j keeps the bit position and table cells of sequence 32m + j; after
-    // every 32 sequences the lanes extract their sequences' fields together and
-    // store the 32 records, so the walk itself carries only the state chain.
-    // The 32 positions of a batch stay inside the ring: a sequence spans at
-    // most 89 bits and the ring is refilled 32 entries at a time.
-    int32_t myPa = 0;
-    uint32_t mll = 0, mml = 0, mof = 0;
+    // The walk records each sequence's bit position and states in skeep;
+    // after every 32 sequences lane j extracts the fields of the batch's
+    // sequence j and stores its record, so the walk itself carries only the
+    // state chain.  The 32 positions of a batch stay inside the ring: a
+    // sequence spans at most 89 bits and the ring is refilled 32 entries at a
+    // time.
     auto flush = [&](uint32_t first, uint32_t count) {
+      __syncwarp();
       if (uint32_t(lane) < count) {
-        const uint2 eLL = sh.ll2[mll], eML = sh.ml2[mml];
-        const uint32_t eOF = sh.of[mof];
+        const uint4 k = sh.skeep[lane];
+        const int32_t myPa = int32_t(k.x);
+        const uint2 eLL = sh.ll2[k.y], eML = sh.ml2[k.z];
+        const uint32_t eOF = sh.of[k.w];
         const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
                        llb = __byte_perm(eLL.x, 0, 0x4443);
         // offset extra (<= 31 bits) at the top of the word below the
@@ -616,33 +619,32 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
         *reinterpret_cast<uint2*>(&r->ll) = make_uint2(ll, ml);
         r->oval = ofv;
       }
+      __syncwarp();
     };
     if (!st) {
-      uint32_t j = 0, first = 0;
-      for (uint32_t i = 0; i < nseq; i++) {
-        // keep >= 4 entries of ring below the lowest word this sequence reads (<= 89 bits)
-        if (((Pa - 96) >> 5) < lo_w) {
+      // refill when Pa - 96 drops below the ring's lowest word
+      int32_t refill_at = 32 * lo_w + 96;
+      auto refill = [&]() {
+        if (Pa < refill_at) {
           const uint4 e = sh.sring[lo_w & 127];
           fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
           lo_w -= 32;
+          refill_at -= 32 * 32;
           pre = gword(lo_w - 32 + lane);
           __syncwarp();
         }
+      };
+      // one sequence that reads state bits (every sequence but the last)
+      auto step = [&](uint4* keep) {
+        refill();
         const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
         const uint32_t eOF = sh.of[sof];
-        if (uint32_t(lane) == j) {
-          myPa = Pa;
-          mll = sll;
-          mml = sml;
-          mof = sof;
-        }
+        *keep = make_uint4(uint32_t(Pa), sll, sml, sof);  // same value from every lane
         // cell bytes: [0,1] next-state base, [2] state bits, [3] extra bits
         const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
                        llb = __byte_perm(eLL.x, 0, 0x4443);
-        const bool more = i + 1 < nseq;
-        const uint32_t nLL = more ? __byte_perm(eLL.x, 0, 0x4442) : 0u,
-                       nML = more ? __byte_perm(eML.x, 0, 0x4442) : 0u,
-                       nOF = more ? __byte_perm(eOF, 0, 0x4442) : 0u;
+        const uint32_t nLL = __byte_perm(eLL.x, 0, 0x4442), nML = __byte_perm(eML.x, 0, 0x4442),
+                       nOF = __byte_perm(eOF, 0, 0x4442);
         const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
         const uint32_t ns = nLL + nML;
         // LL, ML, OF state bits (<= 26) at the top of the word below the extras
@@ -653,13 +655,27 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
         // A stream that runs out reads zero words below its start (never
         // memory outside it) and ends with Pa below boff: checked once below.
         Pa -= int32_t(ox + ns + nOF);
-        if (++j == 32) {
-          flush(first, 32);
-          first += 32;
-          j = 0;
+      };
+      for (uint32_t first = 0; first + 1 < nseq; first += 32) {
+        const uint32_t cnt = min(32u, nseq - 1 - first);
+        if (cnt == 32) {
+          for (uint32_t g = 0; g < 32; g += 8) {
+#pragma unroll
+            for (uint32_t jj = 0; jj < 8; jj++) step(sh.skeep + g + jj);
+          }
+        } else {
+          for (uint32_t jj = 0; jj < cnt; jj++) step(sh.skeep + jj);
         }
+        flush(first, cnt);
       }
-      flush(first, j);
+      if (nseq) {  // the last sequence: extra bits only
+        refill();
+        sh.skeep[0] = make_uint4(uint32_t(Pa), sll, sml, sof);
+        const uint32_t ofc = __byte_perm(sh.of[sof], 0, 0x4443), mlb = __byte_perm(sh.ml2[sml].x, 0, 0x4443),
+                       llb = __byte_perm(sh.ll2[sll].x, 0, 0x4443);
+        Pa -= int32_t(ofc + mlb + llb);
+        flush(nseq - 1, 1);
+      }
     }
     if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;  // overrun (Pa < boff) or bits left over
   }
