@@ -218,6 +218,7 @@ struct K1Shared {
 };
 
 constexpr int kLitWarps = 4;                 // one warp per Huffman stream
+constexpr int32_t kLitMargin = 128;          // bits decoded to synchronise a span's entry
 constexpr int kK1Threads = 32 * (kLitWarps + 1);  // + the sequence warp
 
 // Named barrier over the literal warps only (the sequence warp runs on).
@@ -401,6 +402,16 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     const bool last = lane == nl - 1;
     const int32_t stop = last ? 0 : B - (lane + 1) * span;
     int32_t start = active ? B - lane * span : 0;
+    if (active && lane > 0) {
+      // Enter the span synchronised: decode from kLitMargin bits above its
+      // top down to the first boundary at or below it.  Huffman codes
+      // resynchronise within a few codewords, so this is usually the previous
+      // lane's exit and the first counting pass is already exact.
+      DownWin W;
+      W.init(sp, min(B, start + kLitMargin));
+      huf_run(sh, W, start, uint32_t(maxbits), nullptr, -1);
+      start = W.P;
+    }
     uint32_t n = 0;
     for (int pass = 0; pass <= nl; pass++) {
       int32_t exitp = start;
@@ -577,8 +588,10 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
     __syncwarp();
     // stream bits [q, q + 32) at aligned position a
     auto at = [&](int32_t a) -> uint32_t {
-      const uint4 e = sh.sring[(a >> 5) & 127];
-      return __funnelshift_r(e.x, e.y, uint32_t(a) & 31u);
+      // entry (a >> 5) & 127 at byte offset ((a >> 5) & 127) * 16
+      const uint4 e = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(sh.sring) +
+                                                      ((uint32_t(a) >> 1) & 0x7F0u));
+      return __funnelshift_r(e.x, e.y, uint32_t(a));  // shifts by a & 31
     };
     const uint32_t a0 = sh.al[0], a1 = sh.al[1], a2 = sh.al[2];
     uint32_t sll = 0, sof = 0, sml = 0;
