@@ -162,42 +162,92 @@ struct DownWin {
   }
 };
 
-// FSE decode table (RFC 8878 4.1.1): cell = symbol | nbBits << 8 | base << 16.
-// S = stride of the table in u32 words (2 when it is the x word of a uint2 cell array).
+// FSE decode table (RFC 8878 4.1.1): cell = symbol | nbBits << 8 | base << 16,
+// built by one warp.  S = stride of the table in u32 words (2 when it is the x
+// word of a uint2 cell array); `next` and `start` are 64-entry scratch.
+//  - "less than 1" symbols (count -1) take the top cells in symbol order;
+//  - the other symbols' occurrences, in symbol order, go to the cells the
+//    spread walk pos_k = (k * step) & mask visits, skipping cells above
+//    `high`: lane l walks its own range of k, a warp scan of the valid counts
+//    gives each lane its first occurrence index, and a binary search of the
+//    symbols' first occurrence indices gives each occurrence's symbol;
+//  - a cell's state counter x is the symbol's count plus the number of its
+//    cells below it: cells are taken 32 at a time in increasing order and
+//    lanes holding the same symbol rank themselves with match_any.
 template <int S>
-__device__ void fse_build_dev(const ZFse& f, uint32_t* t, uint16_t* next, int* al_out) {
+__device__ void fse_build_warp(const ZFse& f, uint32_t* t, uint16_t* next, uint16_t* start, int* al_out) {
+  const int lane = threadIdx.x & 31;
   if (f.rle) {
-    t[0] = f.rle_sym;
-    *al_out = 0;
+    if (lane == 0) {
+      t[0] = f.rle_sym;
+      *al_out = 0;
+    }
+    __syncwarp();
     return;
   }
   const int al = f.al, size = 1 << al, nsym = f.nsym;
-  int high = size - 1;
-  for (int s = 0; s < nsym; s++) {
-    const int c = f.norm[s];
-    if (c == -1) {
-      t[S * high--] = uint32_t(s);
-      next[s] = 1;
-    } else {
-      next[s] = uint16_t(c > 0 ? c : 0);
+  const uint32_t lt = (1u << lane) - 1u;
+  const int c0 = lane < nsym ? f.norm[lane] : 0, c1 = lane + 32 < nsym ? f.norm[lane + 32] : 0;
+  const uint32_t lp0 = __ballot_sync(0xFFFFFFFFu, c0 == -1), lp1 = __ballot_sync(0xFFFFFFFFu, c1 == -1);
+  const int n_lp = __popc(lp0) + __popc(lp1);
+  const int high = size - 1 - n_lp;
+  if (c0 == -1) t[S * (size - 1 - __popc(lp0 & lt))] = uint32_t(lane);
+  if (c1 == -1) t[S * (size - 1 - __popc(lp0) - __popc(lp1 & lt))] = uint32_t(lane + 32);
+  // first occurrence index of every symbol (prefix sums of the positive counts)
+  const int p0 = c0 > 0 ? c0 : 0, p1 = c1 > 0 ? c1 : 0;
+  int i0 = p0, i1 = p1;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a0 = __shfl_up_sync(0xFFFFFFFFu, i0, o), a1 = __shfl_up_sync(0xFFFFFFFFu, i1, o);
+    if (lane >= o) {
+      i0 += a0;
+      i1 += a1;
     }
   }
-  const int step = (size >> 1) + (size >> 3) + 3, mask = size - 1;
-  int pos = 0;
-  for (int s = 0; s < nsym; s++) {
-    const int c = f.norm[s];
-    for (int i = 0; i < c; i++) {
-      t[S * pos] = uint32_t(s);
-      do pos = (pos + step) & mask; while (pos > high);
-    }
+  const int tot0 = __shfl_sync(0xFFFFFFFFu, i0, 31);
+  start[lane] = uint16_t(i0 - p0);
+  start[lane + 32] = uint16_t(tot0 + i1 - p1);
+  next[lane] = uint16_t(c0 == -1 ? 1 : p0);
+  next[lane + 32] = uint16_t(c1 == -1 ? 1 : p1);
+  __syncwarp();
+  // spread: lane l takes k in [l * per, (l + 1) * per)
+  const int per = size >> 5, step = (size >> 1) + (size >> 3) + 3, mask = size - 1;
+  const int k0 = lane * per;
+  int valid = 0;
+  for (int k = k0; k < k0 + per; k++) valid += ((k * step) & mask) <= high;
+  int before = valid;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xFFFFFFFFu, before, o);
+    if (lane >= o) before += a;
   }
-  for (int u = 0; u < size; u++) {
-    const uint32_t s = t[S * u] & 0xFFu;
-    const uint32_t x = next[s]++;
+  int j = before - valid;
+  const int ns = nsym < 64 ? nsym : 64;
+  for (int k = k0; k < k0 + per; k++) {
+    const int pos = (k * step) & mask;
+    if (pos > high) continue;
+    // last symbol whose first occurrence index is <= j
+    int lo = 0, hi = ns - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (int(start[mid]) <= j) lo = mid;
+      else hi = mid - 1;
+    }
+    t[S * pos] = uint32_t(lo);
+    j++;
+  }
+  __syncwarp();
+  for (int base = 0; base < size; base += 32) {
+    const int u = base + lane;
+    const uint32_t sym = t[S * u] & 0xFFu;
+    const uint32_t m = __match_any_sync(0xFFFFFFFFu, sym);
+    const uint32_t x = uint32_t(next[sym]) + uint32_t(__popc(m & lt));
+    __syncwarp();
+    if ((m & lt) == 0) next[sym] = uint16_t(next[sym] + __popc(m));
     const uint32_t nb = uint32_t(al - (31 - __clz(x)));
-    t[S * u] = s | (nb << 8) | (((x << nb) - uint32_t(size)) << 16);
+    t[S * u] = sym | (nb << 8) | (((x << nb) - uint32_t(size)) << 16);
+    __syncwarp();
   }
-  *al_out = al;
+  if (lane == 0) *al_out = al;
+  __syncwarp();
 }
 
 struct K1Shared {
@@ -211,6 +261,7 @@ struct K1Shared {
   uint4 sring[128];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 127
   uint4 skeep[32];   // per sequence of the current batch: bit position, LL, ML, OF states
   uint16_t next[3][64];
+  uint16_t fse_start[64];
   int al[3];
   uint32_t st;
   uint32_t out_size;
@@ -523,11 +574,10 @@ __device__ __forceinline__ RepSlots rep_compose(const RepSlots& s, const RepSlot
 // positions in parallel afterwards.
 __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh) {
   const int lane = threadIdx.x & 31;
-  if (lane == 1) fse_build_dev<1>(v.fse[b.fse[1]], sh.of, sh.next[1], &sh.al[1]);
-  else if (lane == 0 || lane == 2)  // LL / ML tables built in the x words of their cell arrays
-    fse_build_dev<2>(v.fse[b.fse[lane]], reinterpret_cast<uint32_t*>(lane == 0 ? sh.ll2 : sh.ml2), sh.next[lane],
-                     &sh.al[lane]);
-  __syncwarp();
+  // LL / ML tables are built in the x words of their cell arrays
+  fse_build_warp<2>(v.fse[b.fse[0]], reinterpret_cast<uint32_t*>(sh.ll2), sh.next[0], sh.fse_start, &sh.al[0]);
+  fse_build_warp<1>(v.fse[b.fse[1]], sh.of, sh.next[1], sh.fse_start, &sh.al[1]);
+  fse_build_warp<2>(v.fse[b.fse[2]], reinterpret_cast<uint32_t*>(sh.ml2), sh.next[2], sh.fse_start, &sh.al[2]);
   {
     const uint32_t nll = 1u << sh.al[0], nof = 1u << sh.al[1], nml = 1u << sh.al[2];
     for (uint32_t u = lane; u < nll; u += 32) {
