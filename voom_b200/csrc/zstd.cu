@@ -789,21 +789,24 @@ __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t
 
 // Per compressed block with sequences, after zstd_block_decode: the repeat-
 // offset rules and output / literal positions of every sequence (RFC 8878
-// 3.1.2.5).  Rounds of 256 consecutive records (coalesced loads and stores):
-// each thread takes one record's symbolic slot transform (slot = block-start
-// slot minus d, or a constant) and lengths, warps scan them, the 8 warp totals
-// are scanned in shared memory, and the round's carry-in (all earlier rounds
-// composed) gives every record its slots, offset and positions.  Also the
+// 3.1.2.5).  Rounds of 256 x 4 consecutive records: each thread applies the
+// rules of its 4 records to symbolic slots (slot = block-start slot minus d,
+// or a constant), giving its transform and length sums; warps scan the
+// transforms, the 8 warp totals are scanned by warp 0, and each thread,
+// starting from its carry-in (all earlier records composed), replays its 4
+// records on those slots to get each one's offset and positions.  Also the
 // block's output size, its repeat transform for the job scan, and the
 // literal-count check.
 constexpr int kSeqScanThreads = 256;
+constexpr int kSeqPerThread = 4;
 
 __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch) {
-  __shared__ uint32_t s_k[kSeqScanThreads / 32][3], s_d[kSeqScanThreads / 32][3];
-  __shared__ uint32_t s_ll[kSeqScanThreads / 32], s_ml[kSeqScanThreads / 32];
-  // per warp: carry-in slots and length sums; entry [8] = the round total
-  __shared__ uint32_t s_ck[kSeqScanThreads / 32 + 1][3], s_cd[kSeqScanThreads / 32 + 1][3];
-  __shared__ uint32_t s_cl[kSeqScanThreads / 32 + 1], s_cm[kSeqScanThreads / 32 + 1];
+  constexpr int kW = kSeqScanThreads / 32;
+  __shared__ uint32_t s_k[kW][3], s_d[kW][3];
+  __shared__ uint32_t s_ll[kW], s_ml[kW];
+  // per warp: carry-in slots and length sums; entry [kW] = the round total
+  __shared__ uint32_t s_ck[kW + 1][3], s_cd[kW + 1][3];
+  __shared__ uint32_t s_cl[kW + 1], s_cm[kW + 1];
   const View v = make_view(img, scratch);
   const ZBlock b = v.blocks[blockIdx.x];
   if (b.type != 2 || b.nseq == 0) return;
@@ -818,26 +821,35 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
     C.d[q] = 0;
   }
   uint32_t cll = 0, cml = 0;  // literal and match bytes before the round
-  for (uint32_t base = 0; base < n; base += kSeqScanThreads) {
-    const uint32_t i = base + tid;
-    const bool valid = i < n;
-    uint32_t ll = 0, ml = 0, ofv = 4;
-    if (valid) {
-      const uint2 lm = *reinterpret_cast<const uint2*>(&seq[i].ll);
-      ll = lm.x;
-      ml = lm.y;
-      ofv = seq[i].oval;
+  for (uint32_t base = 0; base < n; base += kSeqScanThreads * kSeqPerThread) {
+    const uint32_t i0 = base + tid * kSeqPerThread;
+    uint32_t ll[kSeqPerThread], ml[kSeqPerThread], ofv[kSeqPerThread];
+#pragma unroll
+    for (int r = 0; r < kSeqPerThread; r++) {
+      ll[r] = ml[r] = 0;
+      ofv[r] = 4;
+      if (i0 + r < n) {
+        const uint2 lm = *reinterpret_cast<const uint2*>(&seq[i0 + r].ll);
+        ll[r] = lm.x;
+        ml[r] = lm.y;
+        ofv[r] = seq[i0 + r].oval;
+      }
     }
-    RepSlots t;
+    // this thread's transform: its records' rules on identity slots
+    RepSlots incl;
 #pragma unroll
     for (int q = 0; q < 3; q++) {
-      t.k[q] = uint32_t(q);
-      t.d[q] = 0;
+      incl.k[q] = uint32_t(q);
+      incl.d[q] = 0;
     }
-    uint32_t uk = 0, ud = 0;
-    if (valid) rep_step(t, ofv, ll, uk, ud);
-    RepSlots incl = t;
-    uint32_t ill = ll, iml = ml;
+    uint32_t ill = 0, iml = 0;
+#pragma unroll
+    for (int r = 0; r < kSeqPerThread; r++) {
+      uint32_t uk, ud;
+      if (i0 + r < n) rep_step(incl, ofv[r], ll[r], uk, ud);
+      ill += ll[r];
+      iml += ml[r];
+    }
     for (int o = 1; o < 32; o <<= 1) {
       RepSlots prev;
 #pragma unroll
@@ -862,10 +874,9 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
       s_ml[warp] = iml;
     }
     __syncthreads();
-    // warp 0 scans the 8 warp totals (lane w holds warp w's), starting from
-    // the round's carry-in C, and publishes each warp's carry-in and the total
+    // warp 0 scans the warp totals (lane w holds warp w's), starting from the
+    // round's carry-in C, and publishes each warp's carry-in and the total
     if (warp == 0) {
-      constexpr int kW = kSeqScanThreads / 32;
       RepSlots x;
       uint32_t xl = 0, xm = 0;
 #pragma unroll
@@ -931,12 +942,13 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
     for (int q = 0; q < 3; q++) {
       cw.k[q] = s_ck[warp][q];
       cw.d[q] = s_cd[warp][q];
-      all.k[q] = s_ck[kSeqScanThreads / 32][q];
-      all.d[q] = s_cd[kSeqScanThreads / 32][q];
+      all.k[q] = s_ck[kW][q];
+      all.d[q] = s_cd[kW][q];
     }
     const uint32_t wll = s_cl[warp], wml = s_cm[warp];
-    const uint32_t tll = s_cl[kSeqScanThreads / 32], tml = s_cm[kSeqScanThreads / 32];
+    const uint32_t tll = s_cl[kW], tml = s_cm[kW];
     __syncthreads();  // the shared totals are rewritten next round
+    // exclusive within the warp: the lanes below this one
     RepSlots ex;
 #pragma unroll
     for (int q = 0; q < 3; q++) {
@@ -949,21 +961,20 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
     }
     uint32_t ell = __shfl_up_sync(0xFFFFFFFFu, ill, 1), eml = __shfl_up_sync(0xFFFFFFFFu, iml, 1);
     if (lane == 0) ell = eml = 0;
-    if (valid) {
-      const RepSlots before = rep_compose(cw, ex);
-      uint32_t ok, ov;
-      if (uk == 3) {
-        ok = 3;
-        ov = ud;
-      } else {
-        const uint32_t bk = uk == 0 ? before.k[0] : (uk == 1 ? before.k[1] : before.k[2]);
-        const uint32_t bd = uk == 0 ? before.d[0] : (uk == 1 ? before.d[1] : before.d[2]);
-        rep_sub(ok, ov, bk, bd, ud);
+    // replay this thread's records on the slots in force before its first
+    RepSlots cur = rep_compose(cw, ex);
+    uint32_t lit = wll + ell, dst = lit + wml + eml;
+#pragma unroll
+    for (int r = 0; r < kSeqPerThread; r++) {
+      if (i0 + r < n) {
+        uint32_t ok, ov;
+        rep_step(cur, ofv[r], ll[r], ok, ov);
+        // records are 24 bytes: (oval, okind) and (dst, lit) are 8-byte aligned pairs
+        *reinterpret_cast<uint2*>(&seq[i0 + r].oval) = make_uint2(ov, ok);
+        *reinterpret_cast<uint2*>(&seq[i0 + r].dst) = make_uint2(dst, lit);
       }
-      const uint32_t lit = wll + ell, dst = lit + wml + eml;
-      // records are 24 bytes: (oval, okind) and (dst, lit) are 8-byte aligned pairs
-      *reinterpret_cast<uint2*>(&seq[i].oval) = make_uint2(ov, ok);
-      *reinterpret_cast<uint2*>(&seq[i].dst) = make_uint2(dst, lit);
+      lit += ll[r];
+      dst += ll[r] + ml[r];
     }
     C = all;
     cll = tll;
