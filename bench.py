@@ -640,6 +640,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--tokens", type=int, default=1, help="c3_moe: tokens per step (1 or 8)")
     ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
+    ap.add_argument("--device-only", action="store_true",
+                    help="parity check, warm-up and timed device steps only: no end-to-end leg, CPU baseline or "
+                         "clock sampler (the run the ncu captures in profiles/ use); prints no bench line")
     args = ap.parse_args()
 
     import torch
@@ -679,8 +682,9 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler = None if args.device_only else ClockSampler(local)
+    if sampler:
+        sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
@@ -689,9 +693,17 @@ def main():
         w.step_device(sptr)
         ends[i].record(stream)
     torch.cuda.synchronize()
-    clocks = sampler.stop()
+    clocks = sampler.stop() if sampler else None
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms = sum(step_ms) / len(step_ms)
+    if args.device_only:
+        if rank == 0:
+            print(json.dumps({"device_only": True, "workload": w.config()["workload"], "steps": args.steps,
+                              "ms_per_step": round(ms, 5)}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
