@@ -82,7 +82,10 @@ def test_streamed_variant(built_lib):
     assert np.array_equal(ov.decode_body(head, body), raw.reshape(-1))
 
 
-def test_corrupt_body_hash_caught_before_decode(archive_dir):
+def test_corrupt_body_hash_mismatch_refused(archive_dir):
+    """The hashes run alongside the GPU decode; a mismatch is still the error
+    raised (before any tensor is returned), also when the damaged body no
+    longer decodes."""
     from voom_b200.formats.packed2 import Vpack2Reader
 
     data = bytearray((archive_dir / "weights.vpack2").read_bytes())
@@ -91,6 +94,21 @@ def test_corrupt_body_hash_caught_before_decode(archive_dir):
     r = Vpack2Reader(archive_dir)
     with pytest.raises(IOError, match="hash mismatch"):
         r.fetch(list(r.index))
+    assert r.tensors_read == 0
+
+
+def test_reader_reuses_pinned_buffer(archive_dir, decoded):
+    from voom_b200.formats.packed2 import Vpack2Reader
+
+    r = Vpack2Reader(archive_dir, require_hashes=True)
+    names = sorted(r.index)
+    a, _, _ = r.fetch(names)
+    buf = r._host
+    assert buf is not None and buf.is_pinned()
+    b, _, _ = r.fetch(names[: len(names) // 2], parallel=3)
+    assert r._host is buf
+    for n in b:
+        assert torch.equal(a[n], b[n])
 
 
 def test_smollm2_scaled_archive(built_lib):

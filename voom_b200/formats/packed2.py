@@ -7,7 +7,12 @@ generation pointer.  `Vpack2Reader.fetch` keeps the reference's contract
 (coalesced runs with RUN_GAP, short-read and hash checks, fail-closed index
 validation, immutable-archive check, `(tensors, seconds, bytes_read)`), but
 every body of the request is decoded in ONE batched GPU decode and the
-tensors are returned on the CUDA device.
+tensors are returned on the CUDA device.  Bodies are read into a reused
+pinned buffer and hashed on host threads; the GPU decode runs while the
+hashes finish, and nothing is returned before they all match.  SHA-256 stays
+on the host: it is one serial chain per body, so a GPU thread per body would
+be bounded by the largest body at a small fraction of a host core's SHA
+throughput.
 
 Reference interface replaced: formats/packed2.py:42-60, 63-99, 123-175,
 178-191, 194-255, 258-406.
@@ -21,6 +26,7 @@ import json
 import os
 import re
 import struct
+import threading
 import time
 import warnings
 from pathlib import Path
@@ -194,6 +200,8 @@ class Vpack2Reader:
         self._archive_identity = (st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns)
         self.runs_read = 0
         self.tensors_read = 0
+        self._host = None  # pinned read buffer reused across fetches
+        self._host_lock = threading.Lock()
 
     def _validate_index(self) -> None:
         size = self.archive.stat().st_size
@@ -244,10 +252,27 @@ class Vpack2Reader:
             os.close(fd)
         return entry["head"], self._checked_body(name, entry, body)
 
+    def _host_buffer(self, n: int) -> tuple[torch.Tensor, bool]:
+        """A pinned host buffer of >= n bytes: the reader's cached one (grown
+        as needed) when no other fetch holds it, else a fresh one.  Pinning
+        costs milliseconds per hundred MB, so steady-state fetches reuse it."""
+        if self._host_lock.acquire(blocking=False):
+            if self._host is None or self._host.numel() < n:
+                self._host = None
+                self._host = torch.empty(max(n, 1 << 20), dtype=torch.uint8, pin_memory=True)
+            return self._host, True
+        return torch.empty(max(n, 1), dtype=torch.uint8, pin_memory=True), False
+
     def fetch(self, names: list[str], parallel: int = 4) -> tuple[dict, float, int]:
-        """Coalesce the request into sequential runs, read + hash them on a host
-        thread pool into one pinned buffer, decode every body in one batched
-        GPU decode.  Returns (name -> CUDA tensor, seconds, bytes read)."""
+        """Coalesce the request into sequential runs (RUN_GAP: the bytes
+        between bodies of a run count as read, as in the reference), lay the
+        bodies out in one pinned buffer, and read + hash them on a host thread
+        pool, largest body first (each task preads its body and then takes its
+        SHA-256).  As soon as every body is in the buffer, this thread plans
+        the decode, DMAs the buffer to the GPU and decodes every body in ONE
+        batched decode while the hashes finish.  Tensors are returned only
+        after every hash has matched; a mismatch raises the reference's
+        IOError.  Returns (name -> CUDA tensor, seconds, bytes read)."""
         t0 = time.perf_counter()
         self._assert_archive_immutable()
         entries = sorted(((self.index[n], n) for n in names), key=lambda e: e[0]["off"])
@@ -262,45 +287,62 @@ class Vpack2Reader:
                 j += 1
             runs.append((start, end, entries[i:j]))
             i = j
-        total = sum(e - s for s, e, _ in runs)
-        from .. import _device
-
-        host = _device.pinned_empty(max(total, 1))
-        hv = memoryview(host.numpy())
-        run_base, pos = [], 0
-        for s, e, _ in runs:
-            run_base.append(pos)
-            pos += e - s
-        fd = os.open(self.archive, os.O_RDONLY)
-        try:
-            def read_run(k):
-                s, e, ents = runs[k]
-                view = hv[run_base[k]:run_base[k] + (e - s)]
-                _pread_exact(fd, e - s, s, view)
-                for ent, name in ents:
-                    rel = ent["off"] - s
-                    self._checked_body(name, ent, view[rel:rel + ent["len"]])
-                return e - s
-
-            if len(runs) <= 1 or parallel <= 1:
-                sizes = [read_run(k) for k in range(len(runs))]
-            else:
-                with cf.ThreadPoolExecutor(max_workers=min(parallel, len(runs))) as pool:
-                    sizes = list(pool.map(read_run, range(len(runs))))
-        finally:
-            os.close(fd)
-        heads, offs, lens, order = [], [], [], []
-        for k, (s, _e, ents) in enumerate(runs):
-            for ent, name in ents:
+        nbytes = sum(e - s for s, e, _ in runs)
+        heads, offs, lens, order, ents = [], [], [], [], []
+        total = 0
+        for _s, _e, run in runs:
+            for ent, name in run:
                 heads.append(ent["head"])
-                offs.append(run_base[k] + ent["off"] - s)
-                lens.append(ent["len"])
+                offs.append(total)
+                lens.append(int(ent["len"]))
                 order.append(name)
-        out, spans = decode_bodies(heads, host.numpy(), offs, lens, device=self.device)
+                ents.append(ent)
+                total += (int(ent["len"]) + 15) // 16 * 16
+        host, owned = self._host_buffer(total)
+        try:
+            hv = memoryview(host.numpy())
+            fd = os.open(self.archive, os.O_RDONLY)
+            try:
+                left = [len(order)]
+                cond = threading.Condition()
+
+                def body_task(k):
+                    view = hv[offs[k]:offs[k] + lens[k]]
+                    try:
+                        _pread_exact(fd, lens[k], int(ents[k]["off"]), view)
+                    finally:
+                        with cond:
+                            left[0] -= 1
+                            cond.notify_all()
+                    self._checked_body(order[k], ents[k], view)
+
+                # `parallel` is the reference's read queue depth; hashing is
+                # CPU work, so the pool is at least as wide as the host allows
+                workers = max(1, parallel, min(16, os.cpu_count() or 1))
+                with cf.ThreadPoolExecutor(max_workers=min(workers, max(1, len(order)))) as pool:
+                    futs = {k: pool.submit(body_task, k) for k in sorted(range(len(order)), key=lambda k: -lens[k])}
+                    with cond:
+                        cond.wait_for(lambda: left[0] == 0)
+                    decode_error = None
+                    if not any(f.done() and f.exception() for f in futs.values()):
+                        try:
+                            out, spans = decode_bodies(heads, host[:max(total, 1)], offs, lens, device=self.device)
+                            torch.cuda.current_stream().synchronize()
+                        except Exception as exc:  # a failed read or hash takes precedence, as they come first there
+                            decode_error = exc
+                    cf.wait(list(futs.values()))
+                    for k in range(len(order)):  # the first failing body in archive order
+                        futs[k].result()
+                    if decode_error is not None:
+                        raise decode_error
+            finally:
+                os.close(fd)
+        finally:
+            if owned:
+                self._host_lock.release()
         result = {}
         for name, head, (d, n) in zip(order, heads, spans):
             result[name] = to_torch(head, out[d:d + n])
             self.tensors_read += 1
         self.runs_read += len(runs)
-        torch.cuda.current_stream().synchronize()
-        return result, time.perf_counter() - t0, int(sum(sizes))
+        return result, time.perf_counter() - t0, int(nbytes)
