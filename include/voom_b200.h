@@ -243,6 +243,35 @@ void voom_zstd_plan_destroy(void* plan);
 int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                      uint8_t* d_out, uint32_t* d_status, void* stream);
 
+/* ------------------------------------------------------- BF16 NF12 sidecar */
+/* One NF12 layer stream in device memory (16-byte aligned): header_bytes of
+ * 16-byte block headers, 384 code bytes per block, then the 3-byte patches
+ * (formats/bf16_nf12_sidecar.py:318-420 of the reference).
+ *
+ * voom_nf12_decode: blocks [first_block, first_block + n_blocks) to BF16 bits,
+ * each at its header's output offset minus output_base in d_out (out_values
+ * entries).  A block whose header points outside the stream or the output is
+ * skipped and sets bit 0 of *d_status.
+ * Replaces: runtime/bf16_nf12_sidecar.py:21-98 (voom_bf16_nf12_decode_v1 and
+ * _decode_span), used by decode_layer / decode_names :126-248. */
+int voom_nf12_decode(const uint8_t* d_enc, uint64_t enc_bytes, uint64_t header_bytes, uint32_t first_block,
+                     uint32_t n_blocks, uint64_t output_base, uint16_t* d_out, uint64_t out_values,
+                     uint32_t* d_status, void* stream);
+
+/* Fused NF12 decode + small-M linear: d_out[p, n] = sum_k d_x[p, k] * W[n, k]
+ * (BF16 in and out, fp32 accumulation) for 1 <= M <= 8 activation rows, W the
+ * N x K tensor whose blocks start at first_block (K % 512 == 0, N % 8 == 0:
+ * the reference's direct_linear_eligible shapes).  d_scratch must hold
+ * voom_nf12_linear_scratch_bytes(M, K, N) bytes (0: may be NULL).  A block
+ * that is not full or whose patches leave the stream sets bit 1 of
+ * *d_status.
+ * Replaces: runtime/bf16_nf12_linear.py:19-135 (voom_nf12_small_gemm_k{K}_n{N}_p{P}
+ * and NF12Tensor.matmul). */
+uint64_t voom_nf12_linear_scratch_bytes(uint32_t M, uint32_t K, uint32_t N);
+int voom_nf12_linear(const uint16_t* d_x, uint32_t M, uint32_t K, uint32_t N, const uint8_t* d_enc,
+                     uint64_t enc_bytes, uint64_t header_bytes, uint32_t first_block, void* d_scratch,
+                     uint64_t scratch_bytes, uint16_t* d_out, uint32_t* d_status, void* stream);
+
 /* ---------------------------------------------------- fused MoE experts */
 /* One projection (rows x cols BF16, row-major, HF layout) of one expert kept
  * compressed in HBM as a VRN1 frame with its tile plan and checkpoint index

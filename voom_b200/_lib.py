@@ -93,6 +93,9 @@ SIGNATURES: dict[str, tuple] = {
     "voom_moe_combine": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "voom_moe_layer_noalloc": (_i32, [_vp, _u32, _vp, _vp, ctypes.c_float, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                       _u32, _u32, _u32, _vp, _vp]),
+    "voom_nf12_decode": (_i32, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _u64, _vp, _vp]),
+    "voom_nf12_linear_scratch_bytes": (_u64, [_u32, _u32, _u32]),
+    "voom_nf12_linear": (_i32, [_vp, _u32, _u32, _u32, _vp, _u64, _u64, _u32, _vp, _u64, _vp, _vp, _vp]),
     "voom_expert_swiglu": (_i32, [_vp, _vp, _u32, _vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32, _u32, _vp, _vp,
                                   _u64, _vp, _vp]),
 }
