@@ -578,7 +578,200 @@ class C4MoeEP:
                 "l2": "flushed between steps (512 MiB write)"}
 
 
-WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe, "c4_moe_ep": C4MoeEP}
+class C5Nf12:
+    """BF16 NF12 exact sidecar (the reference's next fused decode -> GEMV
+    format): the seven projections of one Llama-3-8B-shaped decoder layer
+    (q 4096x4096, k/v 1024x4096, o 4096x4096, gate/up 14336x4096, down
+    4096x14336; BF16 N(0, 0.02) with 0.01% outliers that need patches) kept as
+    one NF12 layer stream in HBM.  A step multiplies `--tokens` activation rows
+    by all seven weights through the fused decode + small-M linear; the metric
+    is BF16-equivalent weight bytes streamed per second."""
+
+    data = "synthetic (seeded numpy): BF16 N(0, 0.02), 0.01% outliers N(0, 8)"
+    metric = "NF12 fused decode + linear, BF16-equivalent weight GB/s"
+    unit = "GB/s"
+    dtype = "fp32-acc bf16"
+    SHAPES = (("self_attn.q_proj", 4096, 4096), ("self_attn.k_proj", 1024, 4096), ("self_attn.v_proj", 1024, 4096),
+              ("self_attn.o_proj", 4096, 4096), ("mlp.gate_proj", 14336, 4096), ("mlp.up_proj", 14336, 4096),
+              ("mlp.down_proj", 4096, 14336))
+
+    def __init__(self, device, rank: int, tokens: int = 1):
+        import torch
+
+        from voom_b200 import _device, synthetic
+        from voom_b200.formats import nf12
+
+        self.torch = torch
+        self.nf12 = nf12
+        self.dev = device
+        self.M = tokens
+        self.name = f"c5_nf12_llama8b_layer_M{tokens}"
+        tensors = []
+        for i, (name, n, k) in enumerate(self.SHAPES):
+            bits = synthetic.bf16_normal((n, k), 0.02, 500 + i + 31 * rank).reshape(-1).copy()
+            idx = np.random.default_rng(600 + i).choice(bits.size, bits.size // 10000, replace=False)
+            bits[idx] = synthetic.bf16_normal((idx.size,), 8.0, 700 + i).reshape(-1)
+            tensors.append((f"model.layers.0.{name}.weight", bits, (n, k)))
+        self.payload, self.entry = nf12.build_layer(tensors)
+        self.raw_bytes = sum(b.size * 2 for _, b, _ in tensors)
+        self.enc = _device.upload(np.frombuffer(self.payload, np.uint8), device)
+        self.specs = self.entry["tensors"]
+        lib = self.lib = __import__("voom_b200._lib", fromlist=["load"]).load()
+        g = torch.Generator().manual_seed(77 + rank)
+        self.x = torch.randn((tokens, 4096), generator=g).to(torch.bfloat16).to(device)
+        self.x14 = torch.randn((tokens, 14336), generator=g).to(torch.bfloat16).to(device)
+        self.outs, self.scratch = [], []
+        self.launches_per_step = 0
+        for sp in self.specs:
+            n, k = sp["shape"]
+            need = int(lib.voom_nf12_linear_scratch_bytes(tokens, k, n))
+            self.scratch.append((torch.empty(max(need, 1), dtype=torch.uint8, device=device), need))
+            self.outs.append(torch.empty((tokens, n), dtype=torch.bfloat16, device=device))
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.launches_per_step = 2  # the batched fused linear (+ the reduce of split K ranges)
+        self.units_per_step = self.raw_bytes
+        self.algo_bytes = len(self.payload) + sum(2 * tokens * (sp["shape"][0] + sp["shape"][1]) for sp in self.specs)
+        self.tensors = [nf12.NF12Tensor(self.enc, self.entry, sp) for sp in self.specs]
+        self.x_host = torch.empty((tokens, 4096), dtype=torch.bfloat16).pin_memory()
+        self.x_host.copy_(self.x.cpu())
+        self.x14_host = torch.empty((tokens, 14336), dtype=torch.bfloat16).pin_memory()
+        self.x14_host.copy_(self.x14.cpu())
+        self.out_host = [torch.empty((tokens, sp["shape"][0]), dtype=torch.bfloat16).pin_memory()
+                         for sp in self.specs]
+
+    def _x(self, sp, x, x14):
+        return x14 if sp["shape"][1] == 14336 else x
+
+    def _tasks(self, x, x14, outs):
+        import ctypes
+
+        from voom_b200.formats.nf12 import LinearTask
+
+        arr = (LinearTask * len(self.specs))()
+        for i, (sp, out) in enumerate(zip(self.specs, outs)):
+            n, k = sp["shape"]
+            arr[i] = LinearTask(self._x(sp, x, x14).data_ptr(), out.data_ptr(), k, n, int(sp["block_start"]), 0)
+        need = int(self.lib.voom_nf12_linear_batch_scratch_bytes(ctypes.byref(arr), len(self.specs), self.M))
+        return arr, need
+
+    def step_device(self, stream_ptr: int):
+        """All seven projections in one voom_nf12_linear_batch launch."""
+        import ctypes
+
+        from voom_b200._lib import check
+
+        if getattr(self, "_batch", None) is None or self._batch[0] is not self.outs:
+            arr, need = self._tasks(self.x, self.x14, self.outs)
+            scr = self.torch.empty(max(need, 1), dtype=self.torch.uint8, device=self.dev)
+            self._batch = (self.outs, arr, need, scr)
+        _, arr, need, scr = self._batch
+        check(self.lib.voom_nf12_linear_batch(ctypes.byref(arr), len(self.specs), self.M, self.enc.data_ptr(),
+                                              int(self.entry["file_bytes"]), int(self.entry["header_bytes"]),
+                                              scr.data_ptr(), need, self.status.data_ptr(), stream_ptr),
+              "voom_nf12_linear_batch")
+
+    def verify(self) -> bool:
+        torch = self.torch
+        if int(self.status.item()):
+            return False
+        dense = self.nf12.decode_layer(self.enc, self.entry)
+        for sp, out in zip(self.specs, self.outs):
+            w = dense[sp["name"]].float()
+            ref = self._x(sp, self.x, self.x14).float() @ w.T
+            if float((out.float() - ref).norm() / ref.norm()) > 1e-2:
+                return False
+        return True
+
+    def extra(self, stream, steps: int, flush) -> dict:
+        """Whole-layer decode to BF16 (one voom_nf12_decode launch) and the fused
+        linear at 8 activation rows."""
+        torch = self.torch
+        lib = self.lib
+        out = torch.empty(int(self.entry["output_value_count"]), dtype=torch.int16, device=self.dev)
+        st = torch.zeros(1, dtype=torch.int32, device=self.dev)
+
+        def dec():
+            lib.voom_nf12_decode(self.enc.data_ptr(), int(self.entry["file_bytes"]), int(self.entry["header_bytes"]),
+                                 0, int(self.entry["block_count"]), 0, out.data_ptr(), out.numel(), st.data_ptr(),
+                                 int(stream.cuda_stream))
+
+        def timed(fn):
+            fn()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            for a, b in ev:
+                flush.fill_(5)
+                a.record(stream)
+                fn()
+                b.record(stream)
+            torch.cuda.synchronize()
+            return sum(a.elapsed_time(b) for a, b in ev) / steps
+
+        ms = timed(dec)
+        ok = int(st.item()) == 0
+        res = {"layer_decode": {"value": round(self.raw_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s decoded",
+                                "ms_per_step": round(ms, 5), "hbm_gbs": round((len(self.payload) + self.raw_bytes)
+                                                                              / (ms * 1e-3) / 1e9, 1),
+                                "status_ok": ok}}
+        if self.M != 8:
+            w8 = C5Nf12.__new__(C5Nf12)
+            w8.__dict__.update(self.__dict__)
+            w8.M = 8
+            g = torch.Generator().manual_seed(99)
+            w8.x = torch.randn((8, 4096), generator=g).to(torch.bfloat16).to(self.dev)
+            w8.x14 = torch.randn((8, 14336), generator=g).to(torch.bfloat16).to(self.dev)
+            w8.outs = [torch.empty((8, sp["shape"][0]), dtype=torch.bfloat16, device=self.dev) for sp in self.specs]
+            w8._batch = None
+            ms8 = timed(lambda: w8.step_device(int(stream.cuda_stream)))
+            res["fused_linear_M8"] = {"value": round(self.raw_bytes / (ms8 * 1e-3) / 1e9, 2), "unit": self.unit,
+                                      "ms_per_step": round(ms8, 5), "correct": w8.verify()}
+        return res
+
+    def step_e2e(self):
+        """Public API: activations from pinned host memory, NF12Tensor.matmul for
+        the seven projections, outputs back to pinned host memory."""
+        x = self.x_host.to(self.dev, non_blocking=True)
+        x14 = self.x14_host.to(self.dev, non_blocking=True)
+        for t, sp, oh in zip(self.tensors, self.specs, self.out_host):
+            oh.copy_(t.matmul(self._x(sp, x, x14)), non_blocking=True)
+        return 2 * self.M * (4096 + 14336), sum(2 * self.M * sp["shape"][0] for sp in self.specs)
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        """Oracle (numpy restatement of the block decode) of the q projection
+        plus an fp32 matmul, one projection per thread, until `budget_s`."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import nf12 as onf
+
+        sp = self.specs[0]
+        n, k = sp["shape"]
+        x = self.x.float().cpu().numpy()
+        hb = int(self.entry["header_bytes"])
+
+        def one(_):
+            bits = onf.decode_span(self.payload, hb, int(sp["block_start"]), int(sp["block_count"]),
+                                   int(sp["output_offset"]), n * k)
+            return x @ onf.bf16_bits_to_f32(bits).reshape(n, k).T
+
+        done = 0
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            while time.perf_counter() - t0 < budget_s:
+                list(pool.map(one, range(threads)))
+                done += threads
+        dt = time.perf_counter() - t0
+        return {"value": done * n * k * 2 / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{done} q_proj ({n}x{k}) oracle decodes + fp32 matmuls of {self.M} row(s) on {threads} "
+                          f"thread(s), {dt:.1f} s"}
+
+    def config(self) -> dict:
+        return {"workload": self.name, "matrices": [[n, k] for _, n, k in self.SHAPES], "tokens": self.M,
+                "encoded_bytes": len(self.payload), "bf16_bytes": self.raw_bytes,
+                "ratio": round(self.raw_bytes / len(self.payload), 4),
+                "l2": "flushed between steps (512 MiB write); the 327 MB stream exceeds L2"}
+
+
+WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe, "c4_moe_ep": C4MoeEP, "c5_nf12": C5Nf12}
 DEFAULT_WORKLOAD = "c2_vpack"
 
 
@@ -608,7 +801,7 @@ def run_reference(args, world, rank):
     threads = os.cpu_count() or 1
     wl = WORKLOADS[args.workload]
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    w = wl(dev, 0, tokens=args.tokens) if wl is C3Moe else wl(dev, 0)
+    w = wl(dev, 0, tokens=args.tokens) if wl in (C3Moe, C5Nf12) else wl(dev, 0)
     times = []
     vals = []
     for i in range(args.warmup + args.steps):
@@ -657,7 +850,7 @@ def main():
     torch.cuda.set_device(dev)
     peaks, peaks_kind = load_peaks()
     wl = WORKLOADS[args.workload]
-    if wl is C3Moe:
+    if wl in (C3Moe, C5Nf12):
         w = wl(dev, rank, tokens=args.tokens)
     elif wl is C4MoeEP:
         w = wl(dev, rank, tokens=args.tokens, world=world)

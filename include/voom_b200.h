@@ -272,6 +272,27 @@ int voom_nf12_linear(const uint16_t* d_x, uint32_t M, uint32_t K, uint32_t N, co
                      uint64_t enc_bytes, uint64_t header_bytes, uint32_t first_block, void* d_scratch,
                      uint64_t scratch_bytes, uint16_t* d_out, uint32_t* d_status, void* stream);
 
+/* Several NF12 linears of one layer stream and one M in a single launch (up
+ * to 16, e.g. the q/k/v/o and gate/up/down projections of a decoder layer),
+ * so small matrices share the GPU instead of each filling it alone.  Each
+ * task: d_x (M x K BF16), d_out (M x N BF16), K, N, first_block, with the
+ * same shape rules as voom_nf12_linear.  Same results as one call per task.
+ * Replaces: the per-projection NF12Tensor.matmul calls of one layer
+ * (runtime/bf16_nf12_linear.py:223-244). */
+typedef struct voom_nf12_linear_task {
+  const uint16_t* d_x;
+  uint16_t* d_out;
+  uint32_t K;
+  uint32_t N;
+  uint32_t first_block;
+  uint32_t pad;
+} voom_nf12_linear_task;
+
+uint64_t voom_nf12_linear_batch_scratch_bytes(const voom_nf12_linear_task* tasks, uint32_t n, uint32_t M);
+int voom_nf12_linear_batch(const voom_nf12_linear_task* tasks, uint32_t n, uint32_t M, const uint8_t* d_enc,
+                           uint64_t enc_bytes, uint64_t header_bytes, void* d_scratch, uint64_t scratch_bytes,
+                           uint32_t* d_status, void* stream);
+
 /* ---------------------------------------------------- fused MoE experts */
 /* One projection (rows x cols BF16, row-major, HF layout) of one expert kept
  * compressed in HBM as a VRN1 frame with its tile plan and checkpoint index

@@ -223,3 +223,25 @@ def test_gpu_nf12_tensor_matmul_paths():
         ref = x.float() @ dense.float().T
         assert tuple(got.shape) == (*lead, n)
         assert _rel_l2(got, ref) <= 1e-2
+
+
+@pytest.mark.gpu
+def test_gpu_batched_linear_equals_single_calls():
+    """One launch over a layer's projections (different K and N) gives the
+    same bits as one call per projection."""
+    dev = torch.device("cuda:0")
+    shapes = [("q", 512, 1024), ("k", 128, 1024), ("gate", 1536, 1024), ("down", 1024, 1536)]
+    tensors = [(n, _weights(r, c, 200 + i).reshape(-1), (r, c)) for i, (n, r, c) in enumerate(shapes)]
+    payload, entry = nf12.build_layer(tensors)
+    enc = torch.from_numpy(np.frombuffer(payload, np.uint8).copy()).to(dev)
+    for m in (1, 4, 8):
+        g = torch.Generator().manual_seed(m)
+        xs = {1024: torch.randn((m, 1024), generator=g).to(torch.bfloat16).to(dev),
+              1536: torch.randn((m, 1536), generator=g).to(torch.bfloat16).to(dev)}
+        items = [(xs[sp["shape"][1]], sp) for sp in entry["tensors"]]
+        got = nf12.linear_batch(items, enc, entry)
+        for (x, sp), o in zip(items, got):
+            assert torch.equal(o, nf12.linear(x, enc, entry, sp))
+            w = torch.from_numpy(onf.bf16_bits_to_f32(dict((n, b) for n, b, _ in tensors)[sp["name"]])
+                                 .reshape(sp["shape"]))
+            assert _rel_l2(o.cpu(), x.float().cpu() @ w.T) <= 1e-2

@@ -96,6 +96,8 @@ SIGNATURES: dict[str, tuple] = {
     "voom_nf12_decode": (_i32, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _u64, _vp, _vp]),
     "voom_nf12_linear_scratch_bytes": (_u64, [_u32, _u32, _u32]),
     "voom_nf12_linear": (_i32, [_vp, _u32, _u32, _u32, _vp, _u64, _u64, _u32, _vp, _u64, _vp, _vp, _vp]),
+    "voom_nf12_linear_batch_scratch_bytes": (_u64, [_vp, _u32, _u32]),
+    "voom_nf12_linear_batch": (_i32, [_vp, _u32, _u32, _vp, _u64, _u64, _vp, _u64, _vp, _vp]),
     "voom_expert_swiglu": (_i32, [_vp, _vp, _u32, _vp, _vp, _u32, _u32, _vp, _u32, _u32, _u32, _u32, _vp, _vp,
                                   _u64, _vp, _vp]),
 }

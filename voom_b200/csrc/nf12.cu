@@ -131,81 +131,187 @@ __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 
 
 constexpr int kLinWarps = 8;
 
-// Warp: rows [row0, row0 + R), K blocks [kb0, kb1) of each row.
+// fp32 bits of the weight whose 12-bit code has its low 11 bits at bits
+// 16-26 of t1 and its sign at bit 31 of t2 (the other bits of t1 / t2 are
+// masked off): low bits | sign | modal nibble << 27.
+__device__ __forceinline__ float wf(uint32_t t1, uint32_t t2, uint32_t m27) {
+  return __uint_as_float((t1 & 0x07FF0000u) | (t2 & 0x80000000u) | m27);
+}
+
+// The 8 weights of 96 code bits (a, b, d = three consecutive code words):
+// code j sits at bits 12j .. 12j + 11; each weight is two shifts (or funnel
+// shifts) that place its low bits and its sign, then two masks.
+__device__ __forceinline__ void weights8(uint32_t a, uint32_t b, uint32_t d, uint32_t m27, float (&w)[8]) {
+  w[0] = wf(a << 16, a << 20, m27);
+  w[1] = wf(a << 4, a << 8, m27);
+  w[2] = wf(__funnelshift_r(a, b, 8), __funnelshift_r(a, b, 4), m27);
+  w[3] = wf(b << 12, b << 16, m27);
+  w[4] = wf(b, b << 4, m27);
+  w[5] = wf(__funnelshift_r(b, d, 12), __funnelshift_r(b, d, 8), m27);
+  w[6] = wf(d << 8, d << 12, m27);
+  w[7] = wf(d >> 4, d, m27);
+}
+
+template <int M>
+struct Fix {
+  float v[M];
+};
+
+// Exceptions of one block that fall in [lo, lo + 32): the main loop used
+// the weight decoded with the modal nibble, so each adds x * (exact -
+// decoded) (the first patch of an index wins).  Kept out of line: it runs
+// only for blocks with exceptions.
+template <int M>
+__device__ __noinline__ Fix<M> patch_fix(const uint8_t* __restrict__ enc, uint64_t codes_off, uint32_t poff,
+                                         uint32_t cnt, uint32_t m27, uint32_t lo, const uint16_t* __restrict__ xb,
+                                         uint32_t K) {
+  Fix<M> f;
+#pragma unroll
+  for (int p = 0; p < M; p++) f.v[p] = 0.f;
+  const uint8_t* pp = enc + poff;
+  for (uint32_t i = 0; i < cnt; i++) {
+    const uint32_t local = pp[kPatchBytes * i];
+    if (local < lo || local >= lo + 32) continue;
+    bool first = true;
+    for (uint32_t j = 0; j < i; j++) first &= pp[kPatchBytes * j] != local;
+    if (!first) continue;
+    const uint8_t* cb = enc + codes_off + 3u * (local >> 1);
+    const uint32_t pair = cb[0] | (uint32_t(cb[1]) << 8) | (uint32_t(cb[2]) << 16);
+    const uint32_t code = (local & 1) ? pair >> 12 : pair & 0xFFFu;
+    const float dec = __uint_as_float(((code & 0x7FFu) << 16) | ((code & 0x800u) << 20) | m27);
+    const float ex = __uint_as_float((pp[kPatchBytes * i + 1] | (uint32_t(pp[kPatchBytes * i + 2]) << 8)) << 16);
+#pragma unroll
+    for (int p = 0; p < M; p++) {
+      const float xv = __uint_as_float(uint32_t(xb[uint64_t(p) * K + local]) << 16);
+      f.v[p] = fmaf(xv, ex, fmaf(-xv, dec, f.v[p]));
+    }
+  }
+  return f;
+}
+
+// One weight matrix of a fused linear launch: out = x @ W.T with W the
+// N x K tensor whose blocks start at first_block.  Warps [warp_begin,
+// warp_begin + row_groups * splits) of the launch work on it; with splits > 1
+// each writes fp32 partial sums of its K range to partial[split][M][N].
+struct LinTask {
+  const uint16_t* x;
+  uint16_t* out;
+  float* partial;
+  uint32_t K, N, first_block, splits, row_groups, warp_begin;
+};
+
+constexpr int kMaxTasks = 16;
+
+struct LinTasks {
+  LinTask t[kMaxTasks];
+  uint32_t n;
+};
+
+// Codes of R rows for one group of 4 blocks and, per row, meta = modal
+// nibble << 27 | 1 if the block has exceptions | 2 if it is not a full block.
+template <int R>
+struct Group {
+  uint4 cw[R][3];
+  uint32_t meta[R];
+};
+
+template <int R>
+__device__ __forceinline__ void load_group(Group<R>& G, const uint8_t* __restrict__ enc, uint64_t header_bytes,
+                                           uint32_t first_block, uint32_t row0, uint32_t N, uint32_t kblocks,
+                                           uint32_t kb, bool on, uint32_t s) {
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    const uint32_t row = min(row0 + r, N - 1);
+    const uint32_t blk = first_block + row * kblocks + (on ? kb : 0);
+    const uint4 h = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk) * kHeaderBytes));
+    const uint4* q = reinterpret_cast<const uint4*>(enc + header_bytes + uint64_t(blk) * kCodeBytes + 48u * s);
+    G.cw[r][0] = __ldg(q);
+    G.cw[r][1] = __ldg(q + 1);
+    G.cw[r][2] = __ldg(q + 2);
+    G.meta[r] = ((h.w & 15u) << 27) | (on && (h.z >> 16) ? 1u : 0u) | (on && (h.z & 0xFFFFu) != kBlockValues ? 2u : 0u);
+  }
+}
+
+// Warp of a task: rows [row0, row0 + R), K in groups of 4 blocks (1024
+// values): lane l takes 32 consecutive values of block l / 8 of the group (48
+// code bytes, three 16-byte loads per row), so a warp iteration streams 4
+// blocks of each of its rows; the next group's codes are loaded before the
+// current group is multiplied.
 template <int M, int R>
-__global__ void __launch_bounds__(32 * kLinWarps) nf12_linear(const uint16_t* __restrict__ x, uint32_t K, uint32_t N,
-                                                              const uint8_t* __restrict__ enc, uint64_t enc_bytes,
-                                                              uint64_t header_bytes, uint32_t first_block,
-                                                              uint32_t splits, float* __restrict__ partial,
-                                                              uint16_t* __restrict__ out, uint32_t* status) {
-  const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t warp = blockIdx.x * kLinWarps + (threadIdx.x >> 5);
-  const uint32_t groups = (N + R - 1) / R;
-  if (warp >= groups * splits) return;
-  const uint32_t g = warp % groups, sp = warp / groups;
-  const uint32_t row0 = g * R;
+__device__ __forceinline__ void linear_task(const LinTask& T, uint32_t w, uint32_t lane, const uint8_t* __restrict__ enc,
+                                            uint64_t enc_bytes, uint64_t header_bytes, uint32_t* status) {
+  const uint32_t gn = w % T.row_groups, sp = w / T.row_groups;
+  const uint32_t row0 = gn * R, N = T.N, K = T.K;
   const uint32_t kblocks = K / kBlockValues;
-  const uint32_t per = (kblocks + splits - 1) / splits;
-  const uint32_t kb0 = sp * per, kb1 = min(kblocks, kb0 + per);
+  const uint32_t kgroups = (kblocks + 3) / 4;
+  const uint32_t per = (kgroups + T.splits - 1) / T.splits;
+  const uint32_t g0 = sp * per, g1 = min(kgroups, g0 + per);
+  const uint32_t bsub = lane >> 3, s = lane & 7u;  // block of the group, 32-value slice of the block
+  const uint16_t* __restrict__ x = T.x;
   float acc[M][R];
 #pragma unroll
   for (int p = 0; p < M; p++)
 #pragma unroll
     for (int r = 0; r < R; r++) acc[p][r] = 0.f;
   bool bad = false;
-  for (uint32_t kb = kb0; kb < kb1; kb++) {
-    const uint32_t k0 = kb * kBlockValues + lane * 8u;
-    uint4 xv[M];
+  Group<R> cur;
+  if (g0 < g1) load_group<R>(cur, enc, header_bytes, T.first_block, row0, N, kblocks, g0 * 4 + bsub,
+                             g0 * 4 + bsub < kblocks, s);
+  for (uint32_t g = g0; g < g1; g++) {
+    const uint32_t kb = g * 4 + bsub;
+    const bool on = kb < kblocks;  // the last group of a row may hold 2 blocks
+    Group<R> nxt;
+    const uint32_t kbn = kb + 4;
+    if (g + 1 < g1) load_group<R>(nxt, enc, header_bytes, T.first_block, row0, N, kblocks, kbn, kbn < kblocks, s);
 #pragma unroll
-    for (int p = 0; p < M; p++) xv[p] = __ldg(reinterpret_cast<const uint4*>(x + uint64_t(p) * K + k0));
+    for (int r = 0; r < R; r++) bad |= (cur.meta[r] & 2u) != 0;
+    const uint32_t k0 = kb * kBlockValues + 32u * s;
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-      const uint32_t row = row0 + r;
-      if (row >= N) break;
-      const uint32_t blk = first_block + row * kblocks + kb;
-      const Hdr h = load_hdr(enc, blk);
-      uint32_t c[8];
-      lane_codes(enc + header_bytes + uint64_t(blk) * kCodeBytes, lane, c);
-      const uint32_t m11 = h.mode << 11;
-      uint32_t wb[8];
+    for (int c = 0; c < 4; c++) {  // 8 values per step
+      uint4 xv[M];
 #pragma unroll
-      for (int i = 0; i < 8; i++) wb[i] = restore(c[i], m11);
-      if (h.count) {  // rare: exceptions of this block, first patch of an index wins
-        if (h.valid != kBlockValues || uint64_t(h.patch_off) + uint64_t(h.count) * kPatchBytes > enc_bytes) {
-          bad = true;
-        } else {
-          const uint8_t* pp = enc + h.patch_off;
+      for (int p = 0; p < M; p++)
+        xv[p] = on ? __ldg(reinterpret_cast<const uint4*>(x + uint64_t(p) * K + k0 + 8 * c)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const uint32_t target = lane * 8u + uint32_t(i);
-            for (uint32_t p = 0; p < h.count; p++) {
-              if (pp[kPatchBytes * p] == target) {
-                wb[i] = pp[kPatchBytes * p + 1] | (uint32_t(pp[kPatchBytes * p + 2]) << 8);
-                break;
-              }
-            }
-          }
+      for (int r = 0; r < R; r++) {
+        // code words 3c .. 3c + 2 of the lane's 12
+        const uint32_t wa = c == 0 ? cur.cw[r][0].x : c == 1 ? cur.cw[r][0].w : c == 2 ? cur.cw[r][1].z : cur.cw[r][2].y;
+        const uint32_t wb = c == 0 ? cur.cw[r][0].y : c == 1 ? cur.cw[r][1].x : c == 2 ? cur.cw[r][1].w : cur.cw[r][2].z;
+        const uint32_t wd = c == 0 ? cur.cw[r][0].z : c == 1 ? cur.cw[r][1].y : c == 2 ? cur.cw[r][2].x : cur.cw[r][2].w;
+        float wt[8];
+        weights8(wa, wb, wd, cur.meta[r] & 0x78000000u, wt);
+#pragma unroll
+        for (int p = 0; p < M; p++) {
+          float t = acc[p][r];
+          t = fmaf(bf_lo(xv[p].x), wt[0], t);
+          t = fmaf(bf_hi(xv[p].x), wt[1], t);
+          t = fmaf(bf_lo(xv[p].y), wt[2], t);
+          t = fmaf(bf_hi(xv[p].y), wt[3], t);
+          t = fmaf(bf_lo(xv[p].z), wt[4], t);
+          t = fmaf(bf_hi(xv[p].z), wt[5], t);
+          t = fmaf(bf_lo(xv[p].w), wt[6], t);
+          t = fmaf(bf_hi(xv[p].w), wt[7], t);
+          acc[p][r] = t;
         }
-      } else if (h.valid != kBlockValues) {
-        bad = true;
-      }
-      float w[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++) w[i] = __uint_as_float(wb[i] << 16);
-#pragma unroll
-      for (int p = 0; p < M; p++) {
-        float s = acc[p][r];
-        s = fmaf(bf_lo(xv[p].x), w[0], s);
-        s = fmaf(bf_hi(xv[p].x), w[1], s);
-        s = fmaf(bf_lo(xv[p].y), w[2], s);
-        s = fmaf(bf_hi(xv[p].y), w[3], s);
-        s = fmaf(bf_lo(xv[p].z), w[4], s);
-        s = fmaf(bf_hi(xv[p].z), w[5], s);
-        s = fmaf(bf_lo(xv[p].w), w[6], s);
-        s = fmaf(bf_hi(xv[p].w), w[7], s);
-        acc[p][r] = s;
       }
     }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      if (cur.meta[r] & 1u) {  // rare: the block has exceptions, decoded above with the modal nibble
+        const uint32_t blk = T.first_block + min(row0 + r, N - 1) * kblocks + kb;
+        const uint4 h = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk) * kHeaderBytes));
+        const uint32_t m27 = cur.meta[r] & 0x78000000u, cnt = h.z >> 16;
+        if (m27 == (15u << 27) || uint64_t(h.x) + uint64_t(cnt) * kPatchBytes > enc_bytes) {
+          bad = true;  // patches outside the stream, or a modal nibble of 15 (an exception may decode to Inf)
+        } else {
+          const Fix<M> f = patch_fix<M>(enc, header_bytes + uint64_t(blk) * kCodeBytes, h.x, cnt, m27, 32u * s,
+                                        x + uint64_t(kb) * kBlockValues, K);
+#pragma unroll
+          for (int p = 0; p < M; p++) acc[p][r] += f.v[p];
+        }
+      }
+    }
+    if (g + 1 < g1) cur = nxt;
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(status, 2u);
 #pragma unroll
@@ -221,25 +327,42 @@ __global__ void __launch_bounds__(32 * kLinWarps) nf12_linear(const uint16_t* __
       for (int r = 0; r < R; r++) {
         const uint32_t row = row0 + r;
         if (row >= N) continue;
-        if (splits == 1) {
-          out[uint64_t(p) * N + row] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[p][r]));
+        if (T.splits == 1) {
+          T.out[uint64_t(p) * N + row] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[p][r]));
         } else {
-          partial[(uint64_t(sp) * M + p) * N + row] = acc[p][r];
+          T.partial[(uint64_t(sp) * M + p) * N + row] = acc[p][r];
         }
       }
   }
 }
 
-__global__ void nf12_reduce(const float* __restrict__ partial, uint32_t splits, uint32_t M, uint32_t N,
-                            uint16_t* __restrict__ out) {
-  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= uint64_t(M) * N) return;
-  float s = 0.f;
-  for (uint32_t sp = 0; sp < splits; sp++) s += partial[uint64_t(sp) * M * N + i];
-  out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s));
+template <int M, int R>
+__global__ void __launch_bounds__(32 * kLinWarps, (M > 4 ? 1 : 2))
+    nf12_linear(const LinTasks tasks, uint32_t total_warps, const uint8_t* __restrict__ enc, uint64_t enc_bytes,
+                uint64_t header_bytes, uint32_t* status) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t warp = blockIdx.x * kLinWarps + (threadIdx.x >> 5);
+  if (warp >= total_warps) return;
+  uint32_t i = 0;
+  while (i + 1 < tasks.n && warp >= tasks.t[i + 1].warp_begin) i++;
+  linear_task<M, R>(tasks.t[i], warp - tasks.t[i].warp_begin, lane, enc, enc_bytes, header_bytes, status);
 }
 
-uint32_t rows_per_warp(uint32_t M) { return M <= 2 ? 2u : 4u; }
+// Sums the split partials of every split task in split order.
+__global__ void nf12_reduce(const LinTasks tasks, uint32_t M) {
+  for (uint32_t ti = 0; ti < tasks.n; ti++) {
+    const LinTask& T = tasks.t[ti];
+    if (T.splits < 2) continue;
+    const uint64_t n = uint64_t(M) * T.N;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
+      float s = 0.f;
+      for (uint32_t sp = 0; sp < T.splits; sp++) s += T.partial[uint64_t(sp) * n + i];
+      T.out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s));
+    }
+  }
+}
+
+uint32_t rows_per_warp(uint32_t) { return 2u; }
 
 int g_sms = 0;
 
@@ -253,27 +376,82 @@ int sm_count() {
   return g_sms;
 }
 
-// K-range splits: enough warps to keep every SM busy (about 8 CTAs of 8 warps
-// each), at least 2 blocks of K per split.
-uint32_t pick_splits(uint32_t groups, uint32_t kblocks) {
-  const uint64_t want = uint64_t(sm_count()) * 8 * kLinWarps;
-  if (groups >= want) return 1;
-  uint32_t s = uint32_t((want + groups - 1) / groups);
-  s = s < kblocks / 2 ? s : kblocks / 2;
-  return s < 1 ? 1 : s;
+// Split plan of a launch: when the tasks' row groups are too few to keep
+// about 16 warps resident per SM, every task's K range is split (at least 2
+// groups of 4 blocks per split) and its fp32 partials take their place in the
+// scratch, task after task.  Returns the scratch bytes needed.
+uint64_t plan_tasks(LinTasks& L, uint32_t M) {
+  const uint32_t R = rows_per_warp(M);
+  uint64_t groups = 0;
+  for (uint32_t i = 0; i < L.n; i++) {
+    L.t[i].row_groups = (L.t[i].N + R - 1) / R;
+    groups += L.t[i].row_groups;
+  }
+  const uint64_t want = uint64_t(sm_count()) * 16;
+  const uint32_t f = groups >= want ? 1u : uint32_t((want + groups - 1) / groups);
+  uint64_t scratch = 0;
+  uint32_t warp = 0;
+  for (uint32_t i = 0; i < L.n; i++) {
+    LinTask& T = L.t[i];
+    const uint32_t kgroups = (T.K / kBlockValues + 3) / 4;
+    uint32_t sp = f < kgroups / 2 ? f : kgroups / 2;
+    T.splits = sp < 1 ? 1 : sp;
+    T.warp_begin = warp;
+    warp += T.row_groups * T.splits;
+    if (T.splits > 1) scratch += uint64_t(T.splits) * M * T.N * sizeof(float);
+  }
+  return scratch;
 }
 
 template <int M>
-void launch_linear(uint32_t R, const uint16_t* x, uint32_t K, uint32_t N, const uint8_t* enc, uint64_t enc_bytes,
-                   uint64_t header_bytes, uint32_t first_block, uint32_t splits, float* partial, uint16_t* out,
-                   uint32_t* status, cudaStream_t s) {
-  const uint32_t groups = (N + R - 1) / R;
-  const uint32_t warps = groups * splits;
-  const uint32_t grid = (warps + kLinWarps - 1) / kLinWarps;
-  constexpr int kR = M <= 2 ? 2 : 4;  // rows per warp; matches rows_per_warp()
-  (void)R;
-  nf12_linear<M, kR><<<grid, 32 * kLinWarps, 0, s>>>(x, K, N, enc, enc_bytes, header_bytes, first_block, splits,
-                                                      partial, out, status);
+void launch_tasks(const LinTasks& L, const uint8_t* enc, uint64_t enc_bytes, uint64_t header_bytes, uint32_t* status,
+                  cudaStream_t s) {
+  constexpr int kR = 2;  // rows per warp; matches rows_per_warp()
+  const LinTask& last = L.t[L.n - 1];
+  const uint32_t warps = last.warp_begin + last.row_groups * last.splits;
+  nf12_linear<M, kR><<<(warps + kLinWarps - 1) / kLinWarps, 32 * kLinWarps, 0, s>>>(L, warps, enc, enc_bytes,
+                                                                                    header_bytes, status);
+}
+
+int run_tasks(LinTasks& L, uint32_t M, const uint8_t* enc, uint64_t enc_bytes, uint64_t header_bytes, void* scratch,
+              uint64_t scratch_bytes, uint32_t* status, cudaStream_t s) {
+  const uint64_t need = plan_tasks(L, M);
+  if (need && (!scratch || scratch_bytes < need)) return VOOM_E_CAPACITY;
+  uint64_t off = 0;
+  bool split = false;
+  for (uint32_t i = 0; i < L.n; i++) {
+    LinTask& T = L.t[i];
+    if (T.splits > 1) {
+      T.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + off);
+      off += uint64_t(T.splits) * M * T.N * sizeof(float);
+      split = true;
+    } else {
+      T.partial = nullptr;
+    }
+  }
+  switch (M) {
+    case 1: launch_tasks<1>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 2: launch_tasks<2>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 3: launch_tasks<3>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 4: launch_tasks<4>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 5: launch_tasks<5>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 6: launch_tasks<6>(L, enc, enc_bytes, header_bytes, status, s); break;
+    case 7: launch_tasks<7>(L, enc, enc_bytes, header_bytes, status, s); break;
+    default: launch_tasks<8>(L, enc, enc_bytes, header_bytes, status, s); break;
+  }
+  if (split) nf12_reduce<<<sm_count() * 2, 256, 0, s>>>(L, M);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+// Host checks of one task: shapes the kernel takes and its blocks inside the stream.
+int check_task(const uint16_t* x, const uint16_t* out, uint32_t M, uint32_t K, uint32_t N, uint32_t first_block,
+               uint64_t enc_bytes, uint64_t header_bytes) {
+  if (!x || !out) return VOOM_E_INVALID_ARG;
+  if (!M || M > 8 || !N || !K || K % 512 || N % 8) return VOOM_E_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return VOOM_E_INVALID_ARG;
+  const uint64_t end = uint64_t(first_block) + uint64_t(N) * (K / kBlockValues);
+  if (end * kHeaderBytes > header_bytes || header_bytes + end * kCodeBytes > enc_bytes) return VOOM_E_INVALID_ARG;
+  return VOOM_OK;
 }
 
 }  // namespace
@@ -298,41 +476,62 @@ VOOM_API int voom_nf12_decode(const uint8_t* d_enc, uint64_t enc_bytes, uint64_t
 
 VOOM_API uint64_t voom_nf12_linear_scratch_bytes(uint32_t M, uint32_t K, uint32_t N) {
   if (!M || M > 8 || !N || !K || K % 512) return 0;
-  const uint32_t R = rows_per_warp(M);
-  const uint32_t splits = pick_splits((N + R - 1) / R, K / kBlockValues);
-  return splits > 1 ? uint64_t(splits) * M * N * sizeof(float) : 0;
+  LinTasks L{};
+  L.n = 1;
+  L.t[0].K = K;
+  L.t[0].N = N;
+  return plan_tasks(L, M);
 }
 
 VOOM_API int voom_nf12_linear(const uint16_t* d_x, uint32_t M, uint32_t K, uint32_t N, const uint8_t* d_enc,
                               uint64_t enc_bytes, uint64_t header_bytes, uint32_t first_block, void* d_scratch,
                               uint64_t scratch_bytes, uint16_t* d_out, uint32_t* d_status, void* stream) {
-  if (!d_x || !d_enc || !d_out || !d_status) return VOOM_E_INVALID_ARG;
-  if (!M || M > 8 || !N || !K || K % 512 || N % 8) return VOOM_E_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(d_enc) & 15u) || (reinterpret_cast<uintptr_t>(d_x) & 15u))
+  if (!d_enc || !d_status || (reinterpret_cast<uintptr_t>(d_enc) & 15u) || header_bytes % kHeaderBytes)
     return VOOM_E_INVALID_ARG;
-  if (header_bytes % kHeaderBytes) return VOOM_E_INVALID_ARG;
-  const uint32_t kblocks = K / kBlockValues;
-  const uint64_t end = uint64_t(first_block) + uint64_t(N) * kblocks;
-  if (end * kHeaderBytes > header_bytes || header_bytes + end * kCodeBytes > enc_bytes) return VOOM_E_INVALID_ARG;
-  const uint32_t R = rows_per_warp(M);
-  const uint32_t splits = pick_splits((N + R - 1) / R, kblocks);
-  const uint64_t need = splits > 1 ? uint64_t(splits) * M * N * sizeof(float) : 0;
-  if (need && (!d_scratch || scratch_bytes < need)) return VOOM_E_CAPACITY;
-  float* partial = static_cast<float*>(d_scratch);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (M) {
-    case 1: launch_linear<1>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 2: launch_linear<2>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 3: launch_linear<3>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 4: launch_linear<4>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 5: launch_linear<5>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 6: launch_linear<6>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    case 7: launch_linear<7>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
-    default: launch_linear<8>(R, d_x, K, N, d_enc, enc_bytes, header_bytes, first_block, splits, partial, d_out, d_status, s); break;
+  const int rc = check_task(d_x, d_out, M, K, N, first_block, enc_bytes, header_bytes);
+  if (rc != VOOM_OK) return rc;
+  LinTasks L{};
+  L.n = 1;
+  L.t[0].x = d_x;
+  L.t[0].out = d_out;
+  L.t[0].K = K;
+  L.t[0].N = N;
+  L.t[0].first_block = first_block;
+  return run_tasks(L, M, d_enc, enc_bytes, header_bytes, d_scratch, scratch_bytes, d_status,
+                   static_cast<cudaStream_t>(stream));
+}
+
+VOOM_API uint64_t voom_nf12_linear_batch_scratch_bytes(const voom_nf12_linear_task* tasks, uint32_t n, uint32_t M) {
+  if (!tasks || !n || n > kMaxTasks || !M || M > 8) return 0;
+  LinTasks L{};
+  L.n = n;
+  for (uint32_t i = 0; i < n; i++) {
+    if (!tasks[i].K || tasks[i].K % 512 || !tasks[i].N) return 0;
+    L.t[i].K = tasks[i].K;
+    L.t[i].N = tasks[i].N;
   }
-  if (splits > 1) {
-    const uint64_t n = uint64_t(M) * N;
-    nf12_reduce<<<uint32_t((n + 255) / 256), 256, 0, s>>>(partial, splits, M, N, d_out);
+  return plan_tasks(L, M);
+}
+
+VOOM_API int voom_nf12_linear_batch(const voom_nf12_linear_task* tasks, uint32_t n, uint32_t M, const uint8_t* d_enc,
+                                    uint64_t enc_bytes, uint64_t header_bytes, void* d_scratch,
+                                    uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  if (!tasks || !n || !d_enc || !d_status || (reinterpret_cast<uintptr_t>(d_enc) & 15u) ||
+      header_bytes % kHeaderBytes)
+    return VOOM_E_INVALID_ARG;
+  if (n > kMaxTasks) return VOOM_E_CAPACITY;
+  LinTasks L{};
+  L.n = n;
+  for (uint32_t i = 0; i < n; i++) {
+    const voom_nf12_linear_task& t = tasks[i];
+    const int rc = check_task(t.d_x, t.d_out, M, t.K, t.N, t.first_block, enc_bytes, header_bytes);
+    if (rc != VOOM_OK) return rc;
+    L.t[i].x = t.d_x;
+    L.t[i].out = t.d_out;
+    L.t[i].K = t.K;
+    L.t[i].N = t.N;
+    L.t[i].first_block = t.first_block;
   }
-  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+  return run_tasks(L, M, d_enc, enc_bytes, header_bytes, d_scratch, scratch_bytes, d_status,
+                   static_cast<cudaStream_t>(stream));
 }

@@ -23,6 +23,7 @@ Reference interface replaced: formats/bf16_nf12_sidecar.py:72-206,
 
 from __future__ import annotations
 
+import ctypes
 import json
 import math
 import struct
@@ -41,6 +42,12 @@ BLOCK_HEADER_BYTES = 16
 HEADER_DTYPE = np.dtype([("patch_offset", "<u4"), ("output", "<u4"), ("valid", "<u2"), ("count", "<u2"),
                          ("mode", "u1"), ("flags", "u1"), ("reserved", "<u2")])
 assert HEADER_DTYPE.itemsize == BLOCK_HEADER_BYTES
+
+
+class LinearTask(ctypes.Structure):
+    """voom_nf12_linear_task: one projection of a batched fused linear."""
+    _fields_ = [("d_x", ctypes.c_void_p), ("d_out", ctypes.c_void_p), ("K", ctypes.c_uint32),
+                ("N", ctypes.c_uint32), ("first_block", ctypes.c_uint32), ("pad", ctypes.c_uint32)]
 
 
 class NF12Error(ValueError):
@@ -240,9 +247,13 @@ def direct_linear_eligible(spec: dict) -> bool:
     return len(shape) == 2 and shape[0] % 8 == 0 and shape[1] % 512 == 0 and int(spec["raw_bytes"]) >= 1_000_000
 
 
-def linear(x: torch.Tensor, enc: torch.Tensor, entry: dict, spec: dict) -> torch.Tensor:
+def linear(x: torch.Tensor, enc: torch.Tensor, entry: dict, spec: dict, *,
+           status: torch.Tensor | None = None) -> torch.Tensor:
     """x (M <= 8 rows of K, BF16, CUDA) @ W.T with W decoded on the fly:
-    (M, N) BF16, fp32 accumulation."""
+    (M, N) BF16, fp32 accumulation.  Without `status` the call reads its own
+    status back (one synchronisation) and raises on a damaged operand; with
+    it, failures accumulate into that int32 device flag for the caller to
+    check later (the kernel never reads outside the stream either way)."""
     n_size, k_size = (int(v) for v in spec["shape"])
     m = x.shape[0]
     if x.dtype != torch.bfloat16 or x.shape[1] != k_size or not 1 <= m <= 8:
@@ -255,13 +266,67 @@ def linear(x: torch.Tensor, enc: torch.Tensor, entry: dict, spec: dict) -> torch
     need = int(lib.voom_nf12_linear_scratch_bytes(m, k_size, n_size))
     scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
     out = torch.empty((m, n_size), dtype=torch.bfloat16, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    own = status is None
+    if own:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
     check(lib.voom_nf12_linear(x.data_ptr(), m, k_size, n_size, enc.data_ptr(), int(entry["file_bytes"]),
                                int(entry["header_bytes"]), int(spec["block_start"]), scratch.data_ptr(), need,
                                out.data_ptr(), status.data_ptr(), _device.stream_ptr(dev)), "voom_nf12_linear")
-    if int(status.item()):
+    if own and int(status.item()):
         raise NF12Error("BF16 NF12 linear operand has a partial block or patches outside the stream")
     return out
+
+
+def linear_batch(items: list[tuple[torch.Tensor, dict]], enc: torch.Tensor, entry: dict, *,
+                 status: torch.Tensor | None = None) -> list[torch.Tensor]:
+    """Several fused linears of one layer stream in one launch: items are
+    (x, spec) with the same number of rows M <= 8 (up to 16 items); returns
+    each x @ W.T as voom_nf12_linear would."""
+    if not items or len(items) > 16:
+        raise ValueError("nf12 linear_batch takes 1..16 projections")
+    m = items[0][0].shape[0]
+    dev = enc.device
+    keep, outs = [], []
+    arr = (LinearTask * len(items))()
+    for i, (x, spec) in enumerate(items):
+        n_size, k_size = (int(v) for v in spec["shape"])
+        if x.dtype != torch.bfloat16 or x.shape != (m, k_size) or not 1 <= m <= 8:
+            raise ValueError("nf12 linear_batch takes M x K BF16 rows, the same M for every item")
+        x = x.contiguous()
+        if x.data_ptr() % 16:
+            x = x.clone()
+        out = torch.empty((m, n_size), dtype=torch.bfloat16, device=dev)
+        keep.append(x)
+        outs.append(out)
+        arr[i] = LinearTask(x.data_ptr(), out.data_ptr(), k_size, n_size, int(spec["block_start"]), 0)
+    lib = load()
+    need = int(lib.voom_nf12_linear_batch_scratch_bytes(ctypes.byref(arr), len(items), m))
+    scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    own = status is None
+    if own:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib.voom_nf12_linear_batch(ctypes.byref(arr), len(items), m, enc.data_ptr(), int(entry["file_bytes"]),
+                                     int(entry["header_bytes"]), scratch.data_ptr(), need, status.data_ptr(),
+                                     _device.stream_ptr(dev)), "voom_nf12_linear_batch")
+    if own and int(status.item()):
+        raise NF12Error("BF16 NF12 linear operand has a partial block or patches outside the stream")
+    return outs
+
+
+def check_headers(encoded_host: np.ndarray, entry: dict, spec: dict) -> None:
+    """Host check of one tensor's block headers: every block full (a linear
+    operand), output offsets in order, patches inside the stream."""
+    hb = int(entry["header_bytes"])
+    hdr = np.frombuffer(encoded_host[:hb], dtype=HEADER_DTYPE)
+    b0, nb = int(spec["block_start"]), int(spec["block_count"])
+    h = hdr[b0:b0 + nb]
+    if h.size != nb:
+        raise NF12Error("BF16 NF12 tensor blocks exceed the layer headers")
+    end = h["patch_offset"].astype(np.uint64) + h["count"].astype(np.uint64) * PATCH_BYTES
+    want_out = int(spec["output_offset"]) + np.arange(nb, dtype=np.uint64) * BLOCK_VALUES
+    if (h["valid"] > BLOCK_VALUES).any() or (end > int(entry["file_bytes"])).any() \
+            or not np.array_equal(h["output"].astype(np.uint64), want_out):
+        raise NF12Error("BF16 NF12 block header points outside the stream or output")
 
 
 class NF12Tensor:
@@ -272,6 +337,16 @@ class NF12Tensor:
         self.entry = entry
         self.spec = spec
         self.encoded = _device_stream(encoded, entry, device)
+        hb = int(entry["header_bytes"])
+        host = (encoded[:hb].cpu().numpy() if isinstance(encoded, torch.Tensor) else _device.as_u8(encoded)[:hb])
+        check_headers(np.concatenate([host, np.zeros(0, np.uint8)]), entry, spec)
+        # damaged blocks found by the fused kernel accumulate here (see check())
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.encoded.device)
+
+    def check(self) -> None:
+        """Raise if any fused product so far met a damaged block."""
+        if int(self.status.item()):
+            raise NF12Error("BF16 NF12 linear operand has a partial block or patches outside the stream")
 
     @property
     def nbytes(self) -> int:
@@ -297,11 +372,12 @@ class NF12Tensor:
         n_size, k_size = self.shape
         if positions <= 8 and x.shape[-1] == k_size and direct_linear_eligible(self.spec) \
                 and x.dtype == torch.bfloat16:
-            return linear(x.reshape(positions, k_size), self.encoded, self.entry, self.spec).reshape(*lead, n_size)
+            return linear(x.reshape(positions, k_size), self.encoded, self.entry, self.spec,
+                          status=self.status).reshape(*lead, n_size)
         dense = decode_layer(self.encoded, self.entry)[self.spec["name"]]
         return x @ dense.T
 
 
 __all__ = ["BLOCK_VALUES", "CODE_BYTES_PER_BLOCK", "PATCH_BYTES", "BLOCK_HEADER_BYTES", "NF12Error", "NF12Tensor",
            "pack_tensor", "build_layer", "safetensors_file", "read_layer_file", "decode_layer", "decode_names",
-           "direct_linear_eligible", "linear", "VoomError"]
+           "direct_linear_eligible", "linear", "linear_batch", "check_headers", "LinearTask", "VoomError"]
