@@ -126,52 +126,28 @@ __global__ void __launch_bounds__(32 * kDecodeWarps) nf12_decode(const uint8_t* 
   }
 }
 
-__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
-
 constexpr int kLinWarps = 8;
-
-// fp32 bits of the weight whose 12-bit code has its low 11 bits at bits
-// 16-26 of t1 and its sign at bit 31 of t2 (the other bits of t1 / t2 are
-// masked off): low bits | sign | modal nibble << 27.
-__device__ __forceinline__ float wf(uint32_t t1, uint32_t t2, uint32_t m27) {
-  return __uint_as_float((t1 & 0x07FF0000u) | (t2 & 0x80000000u) | m27);
-}
-
-// The 8 weights of 96 code bits (a, b, d = three consecutive code words):
-// code j sits at bits 12j .. 12j + 11; each weight is two shifts (or funnel
-// shifts) that place its low bits and its sign, then two masks.
-__device__ __forceinline__ void weights8(uint32_t a, uint32_t b, uint32_t d, uint32_t m27, float (&w)[8]) {
-  w[0] = wf(a << 16, a << 20, m27);
-  w[1] = wf(a << 4, a << 8, m27);
-  w[2] = wf(__funnelshift_r(a, b, 8), __funnelshift_r(a, b, 4), m27);
-  w[3] = wf(b << 12, b << 16, m27);
-  w[4] = wf(b, b << 4, m27);
-  w[5] = wf(__funnelshift_r(b, d, 12), __funnelshift_r(b, d, 8), m27);
-  w[6] = wf(d << 8, d << 12, m27);
-  w[7] = wf(d >> 4, d, m27);
-}
 
 template <int M>
 struct Fix {
   float v[M];
 };
 
-// Exceptions of one block that fall in [lo, lo + 32): the main loop used
+// Exceptions of one block that fall in [lo, lo + len): the main loop used
 // the weight decoded with the modal nibble, so each adds x * (exact -
 // decoded) (the first patch of an index wins).  Kept out of line: it runs
 // only for blocks with exceptions.
 template <int M>
 __device__ __noinline__ Fix<M> patch_fix(const uint8_t* __restrict__ enc, uint64_t codes_off, uint32_t poff,
-                                         uint32_t cnt, uint32_t m27, uint32_t lo, const uint16_t* __restrict__ xb,
-                                         uint32_t K) {
+                                         uint32_t cnt, uint32_t m27, uint32_t lo, uint32_t len,
+                                         const uint16_t* __restrict__ xb, uint32_t K) {
   Fix<M> f;
 #pragma unroll
   for (int p = 0; p < M; p++) f.v[p] = 0.f;
   const uint8_t* pp = enc + poff;
   for (uint32_t i = 0; i < cnt; i++) {
     const uint32_t local = pp[kPatchBytes * i];
-    if (local < lo || local >= lo + 32) continue;
+    if (local < lo || local >= lo + len) continue;
     bool first = true;
     for (uint32_t j = 0; j < i; j++) first &= pp[kPatchBytes * j] != local;
     if (!first) continue;
@@ -207,137 +183,161 @@ struct LinTasks {
   uint32_t n;
 };
 
-// Codes of R rows for one group of 4 blocks and, per row, meta = modal
-// nibble << 27 | 1 if the block has exceptions | 2 if it is not a full block.
-template <int R>
-struct Group {
-  uint4 cw[R][3];
-  uint32_t meta[R];
-};
+// Packed BF16 pair (low value in bits 0-15) of the 24-bit code pair at bits
+// 0-23 of y: per value its low 11 code bits, its sign (code bit 11) at bit
+// 15, and the modal nibble (m2 = mode << 11 | mode << 27) in bits 11-14.
+__device__ __forceinline__ uint32_t pair_bf16x2(uint32_t y, uint32_t m2) {
+  return (y & 0x7FFu) | ((y << 4) & 0x07FF8000u) | ((y << 8) & 0x80000000u) | m2;
+}
 
-template <int R>
-__device__ __forceinline__ void load_group(Group<R>& G, const uint8_t* __restrict__ enc, uint64_t header_bytes,
-                                           uint32_t first_block, uint32_t row0, uint32_t N, uint32_t kblocks,
-                                           uint32_t kb, bool on, uint32_t s) {
+// The 32 packed pairs of 96 code bytes (six uint4 = 24 words; every 3 words
+// hold 4 pairs).
+__device__ __forceinline__ void pairs32(const uint4 (&q)[6], uint32_t m2, uint32_t (&pk)[32]) {
+  const uint32_t w[24] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                          q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w,
+                          q[4].x, q[4].y, q[4].z, q[4].w, q[5].x, q[5].y, q[5].z, q[5].w};
 #pragma unroll
-  for (int r = 0; r < R; r++) {
-    const uint32_t row = min(row0 + r, N - 1);
-    const uint32_t blk = first_block + row * kblocks + (on ? kb : 0);
-    const uint4 h = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk) * kHeaderBytes));
-    const uint4* q = reinterpret_cast<const uint4*>(enc + header_bytes + uint64_t(blk) * kCodeBytes + 48u * s);
-    G.cw[r][0] = __ldg(q);
-    G.cw[r][1] = __ldg(q + 1);
-    G.cw[r][2] = __ldg(q + 2);
-    G.meta[r] = ((h.w & 15u) << 27) | (on && (h.z >> 16) ? 1u : 0u) | (on && (h.z & 0xFFFFu) != kBlockValues ? 2u : 0u);
+  for (int i = 0; i < 8; i++) {
+    const uint32_t a = w[3 * i], b = w[3 * i + 1], d = w[3 * i + 2];
+    pk[4 * i] = pair_bf16x2(a, m2);
+    pk[4 * i + 1] = pair_bf16x2(__funnelshift_r(a, b, 24), m2);
+    pk[4 * i + 2] = pair_bf16x2(__funnelshift_r(b, d, 16), m2);
+    pk[4 * i + 3] = pair_bf16x2(d >> 8, m2);
   }
 }
 
-// Warp of a task: rows [row0, row0 + R), K in groups of 4 blocks (1024
-// values): lane l takes 32 consecutive values of block l / 8 of the group (48
-// code bytes, three 16-byte loads per row), so a warp iteration streams 4
-// blocks of each of its rows; the next group's codes are loaded before the
-// current group is multiplied.
-template <int M, int R>
-__device__ __forceinline__ void linear_task(const LinTask& T, uint32_t w, uint32_t lane, const uint8_t* __restrict__ enc,
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Warp of a task: 16 weight rows [row0, row0 + 16) x all tokens, one 256-value
+// block of each row per step, on the tensor cores (mma m16n8k16, BF16 in,
+// fp32 accumulate): weight rows are the MMA's M dimension, the (up to 8)
+// activation rows its N dimension.  Lane (g = lane / 4, t = lane % 4) decodes
+// code pairs [32 t, 32 t + 32) of rows g and g + 8 (96 contiguous code bytes
+// each) straight into A-fragment registers; because the sum over k may run
+// in any order, MMA k-pairs t and t + 4 of slice s are the lane's own pairs
+// 2 s and 2 s + 1, and the activation fragment (token g) is loaded with the
+// same mapping.  Exceptions (decoded with the modal nibble) are corrected
+// out of line.
+template <int M>
+__device__ __forceinline__ void linear_tile(const LinTask& T, uint32_t w, uint32_t lane, const uint8_t* __restrict__ enc,
                                             uint64_t enc_bytes, uint64_t header_bytes, uint32_t* status) {
-  const uint32_t gn = w % T.row_groups, sp = w / T.row_groups;
-  const uint32_t row0 = gn * R, N = T.N, K = T.K;
+  const uint32_t tiles = T.row_groups;
+  const uint32_t tile = w % tiles, sp = w / tiles;
+  const uint32_t N = T.N, K = T.K;
+  const uint32_t g = lane >> 2, t = lane & 3u;
+  const uint32_t r0 = tile * 16 + g, r1 = r0 + 8;
+  const bool v0 = r0 < N, v1 = r1 < N;
   const uint32_t kblocks = K / kBlockValues;
-  const uint32_t kgroups = (kblocks + 3) / 4;
-  const uint32_t per = (kgroups + T.splits - 1) / T.splits;
-  const uint32_t g0 = sp * per, g1 = min(kgroups, g0 + per);
-  const uint32_t bsub = lane >> 3, s = lane & 7u;  // block of the group, 32-value slice of the block
+  const uint32_t per = (kblocks + T.splits - 1) / T.splits;
+  const uint32_t kb0 = sp * per, kb1 = min(kblocks, kb0 + per);
   const uint16_t* __restrict__ x = T.x;
-  float acc[M][R];
+  const bool xon = g < uint32_t(M);
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  float e[4] = {0.f, 0.f, 0.f, 0.f};  // second accumulator: halves the MMA dependency chain
+  float corr[2][M];
 #pragma unroll
-  for (int p = 0; p < M; p++)
+  for (int h = 0; h < 2; h++)
 #pragma unroll
-    for (int r = 0; r < R; r++) acc[p][r] = 0.f;
+    for (int p = 0; p < M; p++) corr[h][p] = 0.f;
   bool bad = false;
-  Group<R> cur;
-  if (g0 < g1) load_group<R>(cur, enc, header_bytes, T.first_block, row0, N, kblocks, g0 * 4 + bsub,
-                             g0 * 4 + bsub < kblocks, s);
-  for (uint32_t g = g0; g < g1; g++) {
-    const uint32_t kb = g * 4 + bsub;
-    const bool on = kb < kblocks;  // the last group of a row may hold 2 blocks
-    Group<R> nxt;
-    const uint32_t kbn = kb + 4;
-    if (g + 1 < g1) load_group<R>(nxt, enc, header_bytes, T.first_block, row0, N, kblocks, kbn, kbn < kblocks, s);
+  for (uint32_t kb = kb0; kb < kb1; kb++) {
+    const uint32_t blk0 = T.first_block + (v0 ? r0 : 0) * kblocks + kb;
+    const uint32_t blk1 = T.first_block + (v1 ? r1 : 0) * kblocks + kb;
+    const uint4 h0 = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk0) * kHeaderBytes));
+    const uint4 h1 = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk1) * kHeaderBytes));
+    uint4 q0[6], q1[6];
+    const uint4* c0 = reinterpret_cast<const uint4*>(enc + header_bytes + uint64_t(blk0) * kCodeBytes + 96u * t);
+    const uint4* c1 = reinterpret_cast<const uint4*>(enc + header_bytes + uint64_t(blk1) * kCodeBytes + 96u * t);
 #pragma unroll
-    for (int r = 0; r < R; r++) bad |= (cur.meta[r] & 2u) != 0;
-    const uint32_t k0 = kb * kBlockValues + 32u * s;
-#pragma unroll
-    for (int c = 0; c < 4; c++) {  // 8 values per step
-      uint4 xv[M];
-#pragma unroll
-      for (int p = 0; p < M; p++)
-        xv[p] = on ? __ldg(reinterpret_cast<const uint4*>(x + uint64_t(p) * K + k0 + 8 * c)) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        // code words 3c .. 3c + 2 of the lane's 12
-        const uint32_t wa = c == 0 ? cur.cw[r][0].x : c == 1 ? cur.cw[r][0].w : c == 2 ? cur.cw[r][1].z : cur.cw[r][2].y;
-        const uint32_t wb = c == 0 ? cur.cw[r][0].y : c == 1 ? cur.cw[r][1].x : c == 2 ? cur.cw[r][1].w : cur.cw[r][2].z;
-        const uint32_t wd = c == 0 ? cur.cw[r][0].z : c == 1 ? cur.cw[r][1].y : c == 2 ? cur.cw[r][2].x : cur.cw[r][2].w;
-        float wt[8];
-        weights8(wa, wb, wd, cur.meta[r] & 0x78000000u, wt);
-#pragma unroll
-        for (int p = 0; p < M; p++) {
-          float t = acc[p][r];
-          t = fmaf(bf_lo(xv[p].x), wt[0], t);
-          t = fmaf(bf_hi(xv[p].x), wt[1], t);
-          t = fmaf(bf_lo(xv[p].y), wt[2], t);
-          t = fmaf(bf_hi(xv[p].y), wt[3], t);
-          t = fmaf(bf_lo(xv[p].z), wt[4], t);
-          t = fmaf(bf_hi(xv[p].z), wt[5], t);
-          t = fmaf(bf_lo(xv[p].w), wt[6], t);
-          t = fmaf(bf_hi(xv[p].w), wt[7], t);
-          acc[p][r] = t;
-        }
-      }
+    for (int i = 0; i < 6; i++) {
+      q0[i] = __ldg(c0 + i);
+      q1[i] = __ldg(c1 + i);
     }
+    // activations of token g for k = kb * 256 + 64 t .. + 64
+    uint4 xv[8];
+    const uint4* xp = reinterpret_cast<const uint4*>(x + uint64_t(xon ? g : 0) * K + uint64_t(kb) * kBlockValues + 64u * t);
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-      if (cur.meta[r] & 1u) {  // rare: the block has exceptions, decoded above with the modal nibble
-        const uint32_t blk = T.first_block + min(row0 + r, N - 1) * kblocks + kb;
-        const uint4 h = __ldg(reinterpret_cast<const uint4*>(enc + uint64_t(blk) * kHeaderBytes));
-        const uint32_t m27 = cur.meta[r] & 0x78000000u, cnt = h.z >> 16;
-        if (m27 == (15u << 27) || uint64_t(h.x) + uint64_t(cnt) * kPatchBytes > enc_bytes) {
+    for (int i = 0; i < 8; i++) xv[i] = xon ? __ldg(xp + i) : make_uint4(0, 0, 0, 0);
+    const uint32_t mode0 = h0.w & 15u, mode1 = h1.w & 15u;
+    bad |= (v0 && (h0.z & 0xFFFFu) != kBlockValues) || (v1 && (h1.z & 0xFFFFu) != kBlockValues);
+    uint32_t a[32], b[32];
+    pairs32(q0, (mode0 << 11) | (mode0 << 27), a);
+    pairs32(q1, (mode1 << 11) | (mode1 << 27), b);
+    const uint32_t xw[32] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w,
+                             xv[2].x, xv[2].y, xv[2].z, xv[2].w, xv[3].x, xv[3].y, xv[3].z, xv[3].w,
+                             xv[4].x, xv[4].y, xv[4].z, xv[4].w, xv[5].x, xv[5].y, xv[5].z, xv[5].w,
+                             xv[6].x, xv[6].y, xv[6].z, xv[6].w, xv[7].x, xv[7].y, xv[7].z, xv[7].w};
+#pragma unroll
+    for (int s = 0; s < 16; s += 2) {
+      mma_bf16_16816(d, a[2 * s], b[2 * s], a[2 * s + 1], b[2 * s + 1], xw[2 * s], xw[2 * s + 1]);
+      mma_bf16_16816(e, a[2 * s + 2], b[2 * s + 2], a[2 * s + 3], b[2 * s + 3], xw[2 * s + 2], xw[2 * s + 3]);
+    }
+    // rare: exceptions of rows g / g + 8 in this lane's 64 values
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+      const uint4 hd = hh ? h1 : h0;
+      const bool vv = hh ? v1 : v0;
+      const uint32_t cnt = hd.z >> 16;
+      if (vv && cnt) {
+        const uint32_t m27 = (hd.w & 15u) << 27;
+        if (m27 == (15u << 27) || uint64_t(hd.x) + uint64_t(cnt) * kPatchBytes > enc_bytes) {
           bad = true;  // patches outside the stream, or a modal nibble of 15 (an exception may decode to Inf)
         } else {
-          const Fix<M> f = patch_fix<M>(enc, header_bytes + uint64_t(blk) * kCodeBytes, h.x, cnt, m27, 32u * s,
-                                        x + uint64_t(kb) * kBlockValues, K);
+          const uint32_t blk = hh ? blk1 : blk0;
+          const Fix<M> f = patch_fix<M>(enc, header_bytes + uint64_t(blk) * kCodeBytes, hd.x, cnt, m27, 64u * t,
+                                        64u, x + uint64_t(kb) * kBlockValues, K);
 #pragma unroll
-          for (int p = 0; p < M; p++) acc[p][r] += f.v[p];
+          for (int p = 0; p < M; p++) corr[hh][p] += f.v[p];
         }
       }
     }
-    if (g + 1 < g1) cur = nxt;
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(status, 2u);
 #pragma unroll
-  for (int p = 0; p < M; p++)
+  for (int i = 0; i < 4; i++) d[i] += e[i];
+  // corrections: sum over the 4 lanes of the row group, then each lane adds
+  // those of its two tokens 2t, 2t + 1
 #pragma unroll
-    for (int r = 0; r < R; r++)
+  for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[p][r] += __shfl_xor_sync(0xFFFFFFFFu, acc[p][r], o);
-  if (lane == 0) {
+    for (int p = 0; p < M; p++) {
+      corr[hh][p] += __shfl_xor_sync(0xFFFFFFFFu, corr[hh][p], 1);
+      corr[hh][p] += __shfl_xor_sync(0xFFFFFFFFu, corr[hh][p], 2);
+    }
 #pragma unroll
-    for (int p = 0; p < M; p++)
+  for (int p = 0; p < M; p++) {
+    if (uint32_t(p) == 2 * t) {
+      d[0] += corr[0][p];
+      d[2] += corr[1][p];
+    }
+    if (uint32_t(p) == 2 * t + 1) {
+      d[1] += corr[0][p];
+      d[3] += corr[1][p];
+    }
+  }
+  // D fragment: d0, d1 = rows r0, tokens 2t, 2t+1; d2, d3 = row r1
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        const uint32_t row = row0 + r;
-        if (row >= N) continue;
-        if (T.splits == 1) {
-          T.out[uint64_t(p) * N + row] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[p][r]));
-        } else {
-          T.partial[(uint64_t(sp) * M + p) * N + row] = acc[p][r];
-        }
-      }
+  for (int i = 0; i < 4; i++) {
+    const uint32_t p = 2 * t + (i & 1);
+    const uint32_t row = i < 2 ? r0 : r1;
+    if (p >= uint32_t(M) || row >= N) continue;
+    if (T.splits == 1) {
+      T.out[uint64_t(p) * N + row] = __bfloat16_as_ushort(__float2bfloat16_rn(d[i]));
+    } else {
+      T.partial[(uint64_t(sp) * M + p) * N + row] = d[i];
+    }
   }
 }
 
-template <int M, int R>
-__global__ void __launch_bounds__(32 * kLinWarps, (M > 4 ? 1 : 2))
+template <int M>
+__global__ void __launch_bounds__(32 * kLinWarps)
     nf12_linear(const LinTasks tasks, uint32_t total_warps, const uint8_t* __restrict__ enc, uint64_t enc_bytes,
                 uint64_t header_bytes, uint32_t* status) {
   const uint32_t lane = threadIdx.x & 31u;
@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(32 * kLinWarps, (M > 4 ? 1 : 2))
   if (warp >= total_warps) return;
   uint32_t i = 0;
   while (i + 1 < tasks.n && warp >= tasks.t[i + 1].warp_begin) i++;
-  linear_task<M, R>(tasks.t[i], warp - tasks.t[i].warp_begin, lane, enc, enc_bytes, header_bytes, status);
+  linear_tile<M>(tasks.t[i], warp - tasks.t[i].warp_begin, lane, enc, enc_bytes, header_bytes, status);
 }
 
 // Sums the split partials of every split task in split order.
@@ -361,8 +361,6 @@ __global__ void nf12_reduce(const LinTasks tasks, uint32_t M) {
     }
   }
 }
-
-uint32_t rows_per_warp(uint32_t) { return 2u; }
 
 int g_sms = 0;
 
@@ -381,20 +379,24 @@ int sm_count() {
 // groups of 4 blocks per split) and its fp32 partials take their place in the
 // scratch, task after task.  Returns the scratch bytes needed.
 uint64_t plan_tasks(LinTasks& L, uint32_t M) {
-  const uint32_t R = rows_per_warp(M);
-  uint64_t groups = 0;
+  uint64_t tiles = 0;
   for (uint32_t i = 0; i < L.n; i++) {
-    L.t[i].row_groups = (L.t[i].N + R - 1) / R;
-    groups += L.t[i].row_groups;
+    L.t[i].row_groups = (L.t[i].N + 15) / 16;
+    tiles += L.t[i].row_groups;
   }
   const uint64_t want = uint64_t(sm_count()) * 16;
-  const uint32_t f = groups >= want ? 1u : uint32_t((want + groups - 1) / groups);
+  const uint32_t f = tiles >= want ? 1u : uint32_t((want + tiles - 1) / tiles);
   uint64_t scratch = 0;
   uint32_t warp = 0;
   for (uint32_t i = 0; i < L.n; i++) {
     LinTask& T = L.t[i];
-    const uint32_t kgroups = (T.K / kBlockValues + 3) / 4;
-    uint32_t sp = f < kgroups / 2 ? f : kgroups / 2;
+    const uint32_t kblocks = T.K / kBlockValues;
+    // at most 16 blocks of K per warp (long rows would otherwise set the
+    // launch's tail), more splits while the launch has too few warps, at
+    // least 4 blocks per split
+    uint32_t sp = (kblocks + 15) / 16;
+    sp = sp > f ? sp : f;
+    sp = sp < kblocks / 4 ? sp : kblocks / 4;
     T.splits = sp < 1 ? 1 : sp;
     T.warp_begin = warp;
     warp += T.row_groups * T.splits;
@@ -406,11 +408,10 @@ uint64_t plan_tasks(LinTasks& L, uint32_t M) {
 template <int M>
 void launch_tasks(const LinTasks& L, const uint8_t* enc, uint64_t enc_bytes, uint64_t header_bytes, uint32_t* status,
                   cudaStream_t s) {
-  constexpr int kR = 2;  // rows per warp; matches rows_per_warp()
   const LinTask& last = L.t[L.n - 1];
   const uint32_t warps = last.warp_begin + last.row_groups * last.splits;
-  nf12_linear<M, kR><<<(warps + kLinWarps - 1) / kLinWarps, 32 * kLinWarps, 0, s>>>(L, warps, enc, enc_bytes,
-                                                                                    header_bytes, status);
+  nf12_linear<M><<<(warps + kLinWarps - 1) / kLinWarps, 32 * kLinWarps, 0, s>>>(L, warps, enc, enc_bytes,
+                                                                                header_bytes, status);
 }
 
 int run_tasks(LinTasks& L, uint32_t M, const uint8_t* enc, uint64_t enc_bytes, uint64_t header_bytes, void* scratch,
