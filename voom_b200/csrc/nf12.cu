@@ -190,14 +190,13 @@ __device__ __forceinline__ uint32_t pair_bf16x2(uint32_t y, uint32_t m2) {
   return (y & 0x7FFu) | ((y << 4) & 0x07FF8000u) | ((y << 8) & 0x80000000u) | m2;
 }
 
-// The 32 packed pairs of 96 code bytes (six uint4 = 24 words; every 3 words
-// hold 4 pairs).
-__device__ __forceinline__ void pairs32(const uint4 (&q)[6], uint32_t m2, uint32_t (&pk)[32]) {
-  const uint32_t w[24] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
-                          q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w,
-                          q[4].x, q[4].y, q[4].z, q[4].w, q[5].x, q[5].y, q[5].z, q[5].w};
+// The 16 packed pairs of 48 code bytes (three uint4 = 12 words; every 3
+// words hold 4 pairs).
+__device__ __forceinline__ void pairs16(const uint4 (&q)[3], uint32_t m2, uint32_t (&pk)[16]) {
+  const uint32_t w[12] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                          q[2].x, q[2].y, q[2].z, q[2].w};
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+  for (int i = 0; i < 4; i++) {
     const uint32_t a = w[3 * i], b = w[3 * i + 1], d = w[3 * i + 2];
     pk[4 * i] = pair_bf16x2(a, m2);
     pk[4 * i + 1] = pair_bf16x2(__funnelshift_r(a, b, 24), m2);
@@ -260,24 +259,28 @@ __device__ __forceinline__ void linear_tile(const LinTask& T, uint32_t w, uint32
       q0[i] = __ldg(c0 + i);
       q1[i] = __ldg(c1 + i);
     }
-    // activations of token g for k = kb * 256 + 64 t .. + 64
-    uint4 xv[8];
-    const uint4* xp = reinterpret_cast<const uint4*>(x + uint64_t(xon ? g : 0) * K + uint64_t(kb) * kBlockValues + 64u * t);
-#pragma unroll
-    for (int i = 0; i < 8; i++) xv[i] = xon ? __ldg(xp + i) : make_uint4(0, 0, 0, 0);
     const uint32_t mode0 = h0.w & 15u, mode1 = h1.w & 15u;
     bad |= (v0 && (h0.z & 0xFFFFu) != kBlockValues) || (v1 && (h1.z & 0xFFFFu) != kBlockValues);
-    uint32_t a[32], b[32];
-    pairs32(q0, (mode0 << 11) | (mode0 << 27), a);
-    pairs32(q1, (mode1 << 11) | (mode1 << 27), b);
-    const uint32_t xw[32] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w,
-                             xv[2].x, xv[2].y, xv[2].z, xv[2].w, xv[3].x, xv[3].y, xv[3].z, xv[3].w,
-                             xv[4].x, xv[4].y, xv[4].z, xv[4].w, xv[5].x, xv[5].y, xv[5].z, xv[5].w,
-                             xv[6].x, xv[6].y, xv[6].z, xv[6].w, xv[7].x, xv[7].y, xv[7].z, xv[7].w};
+    const uint32_t m20 = (mode0 << 11) | (mode0 << 27), m21 = (mode1 << 11) | (mode1 << 27);
+    // activations of token g for k = kb * 256 + 64 t .. + 64, in two halves
+    const uint4* xp = reinterpret_cast<const uint4*>(x + uint64_t(xon ? g : 0) * K + uint64_t(kb) * kBlockValues + 64u * t);
 #pragma unroll
-    for (int s = 0; s < 16; s += 2) {
-      mma_bf16_16816(d, a[2 * s], b[2 * s], a[2 * s + 1], b[2 * s + 1], xw[2 * s], xw[2 * s + 1]);
-      mma_bf16_16816(e, a[2 * s + 2], b[2 * s + 2], a[2 * s + 3], b[2 * s + 3], xw[2 * s + 2], xw[2 * s + 3]);
+    for (int half = 0; half < 2; half++) {
+      uint4 xv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) xv[i] = xon ? __ldg(xp + 4 * half + i) : make_uint4(0, 0, 0, 0);
+      const uint4 qa[3] = {q0[3 * half], q0[3 * half + 1], q0[3 * half + 2]};
+      const uint4 qb[3] = {q1[3 * half], q1[3 * half + 1], q1[3 * half + 2]};
+      uint32_t a[16], b[16];
+      pairs16(qa, m20, a);
+      pairs16(qb, m21, b);
+      const uint32_t xw[16] = {xv[0].x, xv[0].y, xv[0].z, xv[0].w, xv[1].x, xv[1].y, xv[1].z, xv[1].w,
+                               xv[2].x, xv[2].y, xv[2].z, xv[2].w, xv[3].x, xv[3].y, xv[3].z, xv[3].w};
+#pragma unroll
+      for (int s = 0; s < 8; s += 2) {
+        mma_bf16_16816(d, a[2 * s], b[2 * s], a[2 * s + 1], b[2 * s + 1], xw[2 * s], xw[2 * s + 1]);
+        mma_bf16_16816(e, a[2 * s + 2], b[2 * s + 2], a[2 * s + 3], b[2 * s + 3], xw[2 * s + 2], xw[2 * s + 3]);
+      }
     }
     // rare: exceptions of rows g / g + 8 in this lane's 64 values
 #pragma unroll
