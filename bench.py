@@ -728,12 +728,15 @@ class C5Nf12:
         return res
 
     def step_e2e(self):
-        """Public API: activations from pinned host memory, NF12Tensor.matmul for
-        the seven projections, outputs back to pinned host memory."""
+        """Public API: activations from pinned host memory, the layer's seven
+        projections through nf12.linear_batch (one launch), outputs back to
+        pinned host memory."""
         x = self.x_host.to(self.dev, non_blocking=True)
         x14 = self.x14_host.to(self.dev, non_blocking=True)
-        for t, sp, oh in zip(self.tensors, self.specs, self.out_host):
-            oh.copy_(t.matmul(self._x(sp, x, x14)), non_blocking=True)
+        outs = self.nf12.linear_batch([(self._x(sp, x, x14), sp) for sp in self.specs], self.enc, self.entry,
+                                      status=self.status)
+        for o, oh in zip(outs, self.out_host):
+            oh.copy_(o, non_blocking=True)
         return 2 * self.M * (4096 + 14336), sum(2 * self.M * sp["shape"][0] for sp in self.specs)
 
     def cpu_sample(self, threads: int, budget_s: float) -> dict:
