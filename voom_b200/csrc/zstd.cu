@@ -1095,7 +1095,18 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
       if (dst >= c1) break;  // records are in output order
       bad |= !ok;
       const uint32_t a0 = max(dst, c0), a1 = min(dst + ll, c1);
-      for (uint32_t p = a0; p < a1; p++) s_out[p - c0] = kResolved | lit[lp + (p - dst)];
+      {  // literal bytes, 8 loads in flight at a time (read-only global loads)
+        uint32_t p = a0;
+        for (; p + 8 <= a1; p += 8) {
+          const uint8_t* q = lit + lp + (p - dst);
+          uint32_t bv[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) bv[k] = __ldg(q + k);
+#pragma unroll
+          for (int k = 0; k < 8; k++) s_out[p - c0 + k] = kResolved | bv[k];
+        }
+        for (; p < a1; p++) s_out[p - c0] = kResolved | __ldg(lit + lp + (p - dst));
+      }
       const uint64_t m = rt.zstart + dst + ll;
       const uint32_t b0 = max(dst + ll, c0), b1 = min(dst + ll + ml, c1);
       for (uint32_t p = b0; p < b1; p++) s_out[p - c0] = ok ? uint32_t(m + (p - dst - ll) - off) : kResolved;
