@@ -174,3 +174,27 @@ def test_expert_batches_producer_consumer(small):
         consume_expert_batches(iter_expert_batches(ids, fetch, fetch_batch=2, compute_batch=1, executor=pool),
                                consume)
     assert done == ids
+
+
+@pytest.mark.gpu
+def test_moe_step_graph_replays_the_eager_stack():
+    """MoeStepGraph (the layer stack captured in one CUDA graph) gives the
+    same bits as calling the layers one by one, for new inputs too."""
+    from voom_b200.runtime import moe
+
+    torch.manual_seed(5)
+    dev = torch.device("cuda:0")
+    E, H, I = 16, 256, 128
+    experts = [tuple((torch.randn(sh) * 0.05).to(torch.bfloat16).contiguous().view(torch.int16).numpy()
+                     .view(np.uint16) for sh in ((I, H), (I, H), (H, I))) for _ in range(E)]
+    store = moe.ExpertStore(experts, dev)
+    layers = [moe.MoeLayer(store, torch.randn((E, H)).to(torch.bfloat16).to(dev),
+                           (1 + 0.05 * torch.randn(H)).to(torch.bfloat16).to(dev), top_k=4) for _ in range(3)]
+    for T in (1, 5):
+        g = moe.MoeStepGraph(layers, T, H, dev)
+        for trial in range(2):
+            x = torch.randn((T, H)).to(torch.bfloat16).to(dev)
+            cur = x
+            for layer in layers:
+                cur = layer(cur)
+            assert torch.equal(g.step(x), cur)

@@ -71,7 +71,7 @@ __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 // (largest first; ties -> lower expert id) by k rounds of block arg-max,
 // optional renormalisation.
 constexpr int kMaxH = 8192;
-constexpr int kRouterExperts = 16;  // experts per logits CTA
+constexpr int kRouterExperts = 4;  // experts per logits CTA: two warps per expert, one half of H each
 
 __device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) {
@@ -115,11 +115,13 @@ __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __
     s_h[i] = bf2f(hb);
   }
   __syncthreads();
-  const uint32_t e_end = min(E, (blockIdx.x + 1) * kRouterExperts);
-  for (uint32_t e = blockIdx.x * kRouterExperts + warp; e < e_end; e += kThreads / 32) {
+  const uint32_t e = blockIdx.x * kRouterExperts + (warp & 3u), half = warp >> 2;
+  const uint32_t hmid = (H / 16) * 8;  // split point, a multiple of 8
+  __shared__ float s_part[kThreads / 32];
+  if (e < E) {
     const uint16_t* we = wr + size_t(e) * H;
     float acc = 0.f;
-    for (uint32_t i = lane * 8; i < H; i += 256) {
+    for (uint32_t i = (half ? hmid : 0u) + lane * 8; i < (half ? H : hmid); i += 256) {
       const uint4 w = __ldg(reinterpret_cast<const uint4*>(we + i));
       acc = fmaf(bf2f(w.x & 0xFFFFu), s_h[i], acc);
       acc = fmaf(__uint_as_float(w.x & 0xFFFF0000u), s_h[i + 1], acc);
@@ -131,55 +133,60 @@ __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __
       acc = fmaf(__uint_as_float(w.w & 0xFFFF0000u), s_h[i + 7], acc);
     }
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) logits[size_t(t) * E + e] = rbf(acc) + (bias ? bias[e] : 0.f);
+    if (lane == 0) s_part[warp] = acc;
   }
+  __syncthreads();
+  if (e < E && half == 0 && lane == 0)
+    logits[size_t(t) * E + e] = rbf(s_part[warp] + s_part[warp + 4]) + (bias ? bias[e] : 0.f);
 }
 
-// One warp per token: softmax and k rounds of warp arg-max over the logits
-// (each lane owns experts lane, lane + 32, ...).
-__global__ void __launch_bounds__(32) moe_router_topk(const float* __restrict__ logits, uint32_t E, uint32_t k,
-                                                      uint32_t norm_topk, Routes* routes) {
+// One CTA per token: fp32 softmax (max and sum as one warp over lanes
+// e % 32), then every expert's rank in (probability desc, id asc) order --
+// each thread compares its experts against all others -- and the k first
+// become the routes.  A NaN probability ranks below every number.
+constexpr int kTopkThreads = 256;
+
+__global__ void __launch_bounds__(kTopkThreads) moe_router_topk(const float* __restrict__ logits, uint32_t E,
+                                                                uint32_t k, uint32_t norm_topk, Routes* routes) {
   __shared__ float s_p[kMaxE];
-  __shared__ uint8_t s_used[kMaxE];
+  __shared__ float s_key[kMaxE];
   __shared__ int s_pick[64];
-  const uint32_t t = blockIdx.x, lane = threadIdx.x;
-  float mx = -INFINITY;
-  for (uint32_t e = lane; e < E; e += 32) {
-    const float v = logits[size_t(t) * E + e];
-    s_p[e] = v;
-    s_used[e] = 0;
-    mx = fmaxf(mx, v);
+  __shared__ float s_mx, s_sm;
+  const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  for (uint32_t e = tid; e < E; e += kTopkThreads) s_p[e] = logits[size_t(t) * E + e];
+  __syncthreads();
+  if (tid < 32) {
+    float mx = -INFINITY;
+    for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, s_p[e]);
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) s_mx = mx;
   }
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-  float sm = 0.f;
-  for (uint32_t e = lane; e < E; e += 32) {
+  __syncthreads();
+  const float mx = s_mx;
+  for (uint32_t e = tid; e < E; e += kTopkThreads) {
     const float p = __expf(s_p[e] - mx);
     s_p[e] = p;
-    sm += p;
+    s_key[e] = p == p ? p : -2.f;
   }
-  for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
-  __syncwarp();
-  // top-k: probabilities are >= 0; a NaN (non-finite activations) ranks below
-  // every number, so each round still picks a valid unused expert
-  for (uint32_t j = 0; j < k; j++) {
-    float bv = -3.f;
-    int bi = 0x7FFFFFFF;
-    for (uint32_t e = lane; e < E; e += 32) {
-      const float v = s_p[e];
-      if (!s_used[e]) argmax_pair(bv, bi, v == v ? v : -2.f, int(e));
-    }
-    for (int o = 16; o; o >>= 1) {
-      const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-      const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-      argmax_pair(bv, bi, v2, i2);
-    }
-    if (lane == 0) {
-      s_pick[j] = bi;
-      s_used[bi] = 1;
-    }
-    __syncwarp();
+  __syncthreads();
+  if (tid < 32) {
+    float sm = 0.f;
+    for (uint32_t e = lane; e < E; e += 32) sm += s_p[e];
+    for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
+    if (lane == 0) s_sm = sm;
   }
-  if (lane == 0) {
+  for (uint32_t e = tid; e < E; e += kTopkThreads) {
+    const float v = s_key[e];
+    uint32_t rank = 0;
+    for (uint32_t q = 0; q < E; q++) {
+      const float w = s_key[q];
+      rank += (w > v || (w == v && q < e)) ? 1u : 0u;
+    }
+    if (rank < k) s_pick[rank] = int(e);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const float sm = s_sm;
     float sel = 0.f;
     for (uint32_t j = 0; j < k; j++) sel += s_p[s_pick[j]] / sm;
     for (uint32_t j = 0; j < k; j++) {
@@ -623,7 +630,7 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   float* logits = reinterpret_cast<float*>(s + L.logits);
   moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
       d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, h, logits);
-  moe_router_topk<<<T, 32, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
+  moe_router_topk<<<T, kTopkThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   const int rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
@@ -667,7 +674,7 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
   float* logits = reinterpret_cast<float*>(s + L.logits);
   moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
       d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, h, logits);
-  moe_router_topk<<<T, 32, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
+  moe_router_topk<<<T, kTopkThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
   moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
   const uint32_t max_unique = min(n_experts, T * top_k);
   uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);

@@ -153,6 +153,49 @@ class MoeLayer:
     __call__ = forward
 
 
+class MoeStepGraph:
+    """A fixed stack of MoE layers for T tokens, captured once in a CUDA graph
+    and replayed per decode step: one graph launch instead of about eight
+    kernel launches per layer, with results bit-identical to calling the
+    layers one by one.  `step(x)` copies x into the graph's input buffer,
+    replays, and returns the graph's output buffer (overwritten by the next
+    step).  Every layer's scratch is allocated before the capture, so the
+    replay allocates nothing."""
+
+    def __init__(self, layers: list, T: int, H: int, device, *, residual: bool = True):
+        self.layers = list(layers)
+        self.T, self.H = int(T), int(H)
+        self.device = torch.device(device)
+        self.x = torch.zeros((self.T, self.H), dtype=torch.bfloat16, device=self.device)
+        self.bufs = [torch.empty_like(self.x) for _ in range(2)]
+        for layer in self.layers:
+            layer.scratch(self.T)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._run(residual)  # warm-up outside the capture
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self._run(residual)
+
+    def _run(self, residual: bool) -> torch.Tensor:
+        cur = self.x
+        for i, layer in enumerate(self.layers):
+            nxt = self.bufs[i % 2]
+            layer(cur, out=nxt, residual=residual)
+            cur = nxt
+        return cur
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+    def step(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x)
+        return self.replay()
+
+
 def route_rows(idx: np.ndarray):
     """Host mirror of the device route plan: unique experts in first-appearance
     order over (position, slot), tokens per expert, route-row offsets, the token
