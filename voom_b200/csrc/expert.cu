@@ -73,13 +73,6 @@ __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 constexpr int kMaxH = 8192;
 constexpr int kRouterExperts = 4;  // experts per logits CTA: two warps per expert, one half of H each
 
-__device__ __forceinline__ void argmax_pair(float& v, int& i, float v2, int i2) {
-  if (v2 > v || (v2 == v && i2 < i)) {
-    v = v2;
-    i = i2;
-  }
-}
-
 __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __restrict__ x,
                                                               const uint16_t* __restrict__ norm_w, float eps,
                                                               const uint16_t* __restrict__ wr,

@@ -1109,7 +1109,28 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
       }
       const uint64_t m = rt.zstart + dst + ll;
       const uint32_t b0 = max(dst + ll, c0), b1 = min(dst + ll + ml, c1);
-      for (uint32_t p = b0; p < b1; p++) s_out[p - c0] = ok ? uint32_t(m + (p - dst - ll) - off) : kResolved;
+      {  // match bytes: a link to the source, or -- when the source lies in an
+         // earlier chunk of this block, whose words this CTA wrote before the
+         // last barrier -- that word itself (its byte, or its own link: one hop
+         // of the output pass's chase done here); 8 loads in flight at a time
+        uint32_t p = b0;
+        for (; p + 8 <= b1; p += 8) {
+          uint32_t vv[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint32_t q = p + k;
+            vv[k] = ok ? uint32_t(m + (q - dst - ll) - off) : kResolved;
+            if (ok && off <= q && q - off < c0) vv[k] = res[q - off];
+          }
+#pragma unroll
+          for (int k = 0; k < 8; k++) s_out[p - c0 + k] = vv[k];
+        }
+        for (; p < b1; p++) {
+          uint32_t val = ok ? uint32_t(m + (p - dst - ll) - off) : kResolved;
+          if (ok && off <= p && p - off < c0) val = res[p - off];
+          s_out[p - c0] = val;
+        }
+      }
     }
     __syncthreads();
     for (uint32_t p = c0 + threadIdx.x; p < c1; p += blockDim.x) res[p] = s_out[p - c0];
