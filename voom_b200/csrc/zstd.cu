@@ -1245,11 +1245,11 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
   const uint64_t zmax = v.h->zbytes;
   const uint64_t end = t.begin + t.len;
   uint32_t unres = 0;
-  // The tile is walked in block-wide steps of 8 bytes per thread with a
-  // barrier after each, so chains into earlier steps of the tile end at the
-  // value stored there (match offsets are mostly longer than one step).  Each
-  // thread loads its next link words before chasing the current ones; only
-  // the owning thread ever writes a position here, so the early load is exact.
+  // The tile is walked in block-wide steps of 8 bytes per thread (no barrier
+  // between steps: links into the block's own earlier chunks were already
+  // followed once by the block execute pass).  Each thread loads its next
+  // link words before chasing the current ones; only the owning thread ever
+  // writes a position here, so the early load is exact.
   const uint32_t step = 8u * blockDim.x;
   uint4 n0 = make_uint4(0, 0, 0, 0), n1 = n0;
   if (t.begin + 8u * threadIdx.x + 8 <= end) {
@@ -1294,7 +1294,6 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
         emit1(job, src, out, k + i, uint8_t(u), true);
       }
     }
-    __syncthreads();
   }
   if (unres) atomicAdd(&s_unres, unres);
   __syncthreads();
