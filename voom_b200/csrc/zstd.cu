@@ -994,9 +994,23 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
   }
 }
 
-__global__ void zstd_job_scan(const uint8_t* img, uint8_t* scratch, uint32_t* status) {
+// K2, one warp per job: the blocks of each frame 32 at a time -- a warp scan
+// of their output sizes gives every block's Z position, and a scan of their
+// symbolic repeat-offset transforms (composed in block order) applied to the
+// repeat offsets at the start of the chunk gives every block's initial repeat
+// offsets; the chunk's totals carry into the next 32.
+constexpr int kJobScanWarps = 4;
+
+__device__ __forceinline__ uint32_t rep_apply(const RepSlots& t, const uint32_t (&in)[3], int q) {
+  const uint32_t src = t.k[q] == 0 ? in[0] : (t.k[q] == 1 ? in[1] : in[2]);
+  return t.k[q] == 3 ? t.d[q] : src - t.d[q];
+}
+
+__global__ void __launch_bounds__(32 * kJobScanWarps) zstd_job_scan(const uint8_t* img, uint8_t* scratch,
+                                                                     uint32_t* status) {
   const View v = make_view(img, scratch);
-  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t j = blockIdx.x * kJobScanWarps + (threadIdx.x >> 5);
   if (j >= v.h->n_jobs) return;
   const ZJob job = v.jobs[j];
   if (job.bad) return;
@@ -1006,21 +1020,79 @@ __global__ void zstd_job_scan(const uint8_t* img, uint8_t* scratch, uint32_t* st
     const ZFrame fr = v.frames[f];
     uint32_t rep[3] = {1, 4, 8};
     const uint64_t fz = z;
-    for (uint32_t bi = fr.block_first; bi < fr.block_first + fr.n_blocks; bi++) {
-      ZBlockRt* rt = v.rt + bi;
-      rt->zstart = z;
-      rt->frame_zstart = fz;
-      for (int k = 0; k < 3; k++) rt->init_rep[k] = rep[k];
-      st |= rt->status;
-      z += rt->out_size;
+    for (uint32_t c = 0; c < fr.n_blocks; c += 32) {
+      const uint32_t bi = fr.block_first + c + lane;
+      const bool on = c + lane < fr.n_blocks;
+      uint32_t size = 0;
+      RepSlots T;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        T.k[q] = uint32_t(q);
+        T.d[q] = 0;
+      }
+      if (on) {
+        const ZBlockRt& rt = v.rt[bi];
+        size = rt.out_size;
+        st |= rt.status;
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+          T.k[q] = rt.rep_kind[q];
+          T.d[q] = rt.rep_val[q];
+        }
+      }
+      // inclusive scans of sizes and transforms over the lanes
+      uint64_t incl = size;
+      RepSlots X = T;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t ps = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        RepSlots prev;
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+          prev.k[q] = __shfl_up_sync(0xFFFFFFFFu, X.k[q], o);
+          prev.d[q] = __shfl_up_sync(0xFFFFFFFFu, X.d[q], o);
+        }
+        if (lane >= uint32_t(o)) {
+          incl += ps;
+          X = rep_compose(prev, X);
+        }
+      }
+      // exclusive: the transform of the lanes below this one
+      RepSlots E;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        E.k[q] = __shfl_up_sync(0xFFFFFFFFu, X.k[q], 1);
+        E.d[q] = __shfl_up_sync(0xFFFFFFFFu, X.d[q], 1);
+        if (lane == 0) {
+          E.k[q] = uint32_t(q);
+          E.d[q] = 0;
+        }
+      }
+      if (on) {
+        ZBlockRt* rt = v.rt + bi;
+        rt->zstart = z + incl - size;
+        rt->frame_zstart = fz;
+#pragma unroll
+        for (int q = 0; q < 3; q++) rt->init_rep[q] = rep_apply(E, rep, q);
+      }
+      // carry: the chunk's total size and composed transform (lane 31)
+      z += __shfl_sync(0xFFFFFFFFu, incl, 31);
+      RepSlots A;
+#pragma unroll
+      for (int q = 0; q < 3; q++) {
+        A.k[q] = __shfl_sync(0xFFFFFFFFu, X.k[q], 31);
+        A.d[q] = __shfl_sync(0xFFFFFFFFu, X.d[q], 31);
+      }
       uint32_t nr[3];
-      for (int k = 0; k < 3; k++) nr[k] = rt->rep_kind[k] == 3 ? rt->rep_val[k] : rep[rt->rep_kind[k]] - rt->rep_val[k];
-      for (int k = 0; k < 3; k++) rep[k] = nr[k];
+#pragma unroll
+      for (int q = 0; q < 3; q++) nr[q] = rep_apply(A, rep, q);
+#pragma unroll
+      for (int q = 0; q < 3; q++) rep[q] = nr[q];
     }
     if (fr.fcs != ~0ull && z - fz != fr.fcs) st |= VOOM_ZSTD_ST_SIZE;
   }
+  for (int o = 16; o; o >>= 1) st |= __shfl_xor_sync(0xFFFFFFFFu, st, o);
   if (z - job.zoff != job.dst_len) st |= VOOM_ZSTD_ST_SIZE;
-  if (st) atomicOr(status + j, st);
+  if (st && lane == 0) atomicOr(status + j, st);
 }
 
 // Output chunk of K3: its entries are built in shared memory, then written out
@@ -1475,7 +1547,8 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   if (h.n_blocks) {
     zstd_block_decode<<<h.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr);
     zstd_seq_scan<<<h.n_blocks, kSeqScanThreads, 0, s>>>(img, scr);
-    zstd_job_scan<<<(h.n_jobs + 127) / 128, 128, 0, s>>>(img, scr, d_status);
+    zstd_job_scan<<<(h.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(img, scr,
+                                                                                                 d_status);
     zstd_block_execute<<<h.n_blocks, 256, 0, s>>>(d_src, img, scr, d_status);
   }
   if (h.n_tiles) {
