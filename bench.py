@@ -24,6 +24,7 @@ import json
 import glob
 import re
 import os
+import pickle
 import statistics
 import subprocess
 import sys
@@ -780,7 +781,121 @@ class C5Nf12:
                 "l2": "flushed between steps (512 MiB write); the 327 MB stream exceeds L2"}
 
 
-WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe, "c4_moe_ep": C4MoeEP, "c5_nf12": C5Nf12}
+class C6KvPaged:
+    """Config 5: the PagedKVCache spill/reload codec.  `pages` KV pages of 16
+    positions x 8 KV heads x 128 head_dim BF16 (K and V N(0, 1) x a per-page,
+    per-head scale U(0.5, 4)), spilled in the reference's compressed format
+    (`.kvz`: pickle of {"shape", "k": zstd level 1 of K, "v": zstd level 1 of
+    V}, runtime/kv_paged.py:77-91) on host threads.  A step reloads every
+    page: all 2 x `pages` frames in one batched GPU decode.  Metric: decoded
+    KV bytes per second."""
+
+    metric = "BF16 weight-page decode GB/s (bit-exact)"
+    unit = "GB/s"
+    dtype = "u8"
+    data = ("synthetic (seeded torch, generated on the device): K and V BF16 N(0, 1) x per-page per-head "
+            "U(0.5, 4)")
+
+    def __init__(self, device, rank: int, pages: int = 65536):
+        import torch
+
+        from voom_b200.formats import zstd_gpu
+        from voom_b200.runtime import kv_paged
+
+        self.torch = torch
+        self.dev = device
+        self.kv = kv_paged
+        self.n_pages = pages
+        self.name = f"c6_kv_paged_{pages}"
+        H, P, D = 8, 16, 128
+        g = torch.Generator(device=device).manual_seed(2026 + 7919 * rank)
+        self.raw = torch.empty((pages, 2, 1, H, P, D), dtype=torch.bfloat16, device=device)
+        chunk = 4096
+        for a in range(0, pages, chunk):
+            n = min(chunk, pages - a)
+            x = torch.randn((n, 2, 1, H, P, D), generator=g, device=device)
+            s = torch.rand((n, 2, 1, H, 1, 1), generator=g, device=device) * 3.5 + 0.5
+            self.raw[a:a + n] = (x * s).to(torch.bfloat16)
+        host = self.raw.view(torch.int16).cpu().numpy().view(np.uint16)
+        self.blobs = kv_paged.spill_pages_compressed(host[:, 0], host[:, 1], threads=os.cpu_count() or 8)
+        del host
+        self.page_bytes = 2 * H * P * D
+        frames = []
+        for b in self.blobs:
+            d = pickle.loads(b)
+            frames += [d["k"], d["v"]]
+        jobs = np.zeros(len(frames), dtype=zstd_gpu.JOB_DTYPE)
+        src = 0
+        for i, f in enumerate(frames):
+            jobs[i] = (src, len(f), i * self.page_bytes, self.page_bytes, 0, 0, 0)
+            src += len(f)
+        self.comp = np.frombuffer(b"".join(frames), np.uint8)
+        self.plan = zstd_gpu.ZstdPlan(self.comp, jobs)
+        self.batch = zstd_gpu.ZstdBatch(self.plan, device)
+        self.src = _dev_upload(self.comp, device)
+        self.out = torch.empty(len(frames) * self.page_bytes, dtype=torch.uint8, device=device)
+        self.raw_bytes = self.out.numel()
+        self.units_per_step = self.raw_bytes
+        self.algo_bytes = self.comp.size + self.raw_bytes
+        self.n_blocks = int(self.plan.info.n_blocks)
+        self.n_seq = int(self.plan.info.n_seq)
+        self.launches_per_step = 12
+
+    def step_device(self, stream_ptr: int):
+        self.batch.run(self.src, self.out, self.torch.cuda.current_stream(self.dev))
+
+    def verify(self) -> bool:
+        if self.batch.job_status().any():
+            return False
+        return bool(self.torch.equal(self.out, self.raw.view(-1).view(self.torch.uint8)))
+
+    def step_e2e(self):
+        """Public API: kv_paged.reload_blobs over the host-resident .kvz pages
+        (parse, plan, one upload, one batched decode, status read back)."""
+        self.kv.reload_blobs(self.blobs, self.dev)
+        return int(self.comp.size), 4 * 2 * self.n_pages
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        """The reference reload (`_Page.load`: unpickle + zstd.decompress of K
+        and V, kv_paged.py:98-113), pages spread over `threads` host threads,
+        until `budget_s` of wall time."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import vpack as ov
+
+        k, v = ov.kv_load(self.blobs[0])
+        ref = self.raw[0].view(self.torch.int16).cpu().numpy().view(np.uint16)
+        assert np.array_equal(k, ref[0]) and np.array_equal(v, ref[1])
+        step = 1024
+        done, i = 0, 0
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            while time.perf_counter() - t0 < budget_s:
+                sl = [self.blobs[(i + j) % self.n_pages] for j in range(step)]
+                i += step
+                for kk, _ in pool.map(ov.kv_load, sl):
+                    done += 2 * kk.nbytes
+        dt = time.perf_counter() - t0
+        return {"value": done / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{done // self.page_bytes // 2} page reloads (.kvz unpickle + libzstd decompress of K "
+                          f"and V) on {threads} thread(s), {dt:.1f} s"}
+
+    def config(self) -> dict:
+        return {"workload": self.name, "pages": self.n_pages, "page_shape": [1, 8, 16, 128], "tensors_per_page": 2,
+                "frames": 2 * self.n_pages, "zstd_blocks": self.n_blocks, "sequences": self.n_seq,
+                "compressed_bytes": int(self.comp.size), "raw_bytes": int(self.raw_bytes),
+                "ratio": round(self.raw_bytes / self.comp.size, 4), "zstd_level": 1,
+                "l2": "flushed between steps (512 MiB write); inputs and output exceed L2"}
+
+
+def _dev_upload(arr, device):
+    from voom_b200 import _device
+
+    return _device.upload(arr, device)
+
+
+WORKLOADS = {"c1_rans": C1Rans, "c2_vpack": C2Vpack, "c3_moe": C3Moe, "c4_moe_ep": C4MoeEP, "c5_nf12": C5Nf12,
+             "c6_kv_paged": C6KvPaged}
 DEFAULT_WORKLOAD = "c2_vpack"
 
 
@@ -810,7 +925,12 @@ def run_reference(args, world, rank):
     threads = os.cpu_count() or 1
     wl = WORKLOADS[args.workload]
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    w = wl(dev, 0, tokens=args.tokens) if wl in (C3Moe, C5Nf12) else wl(dev, 0)
+    if wl in (C3Moe, C5Nf12):
+        w = wl(dev, 0, tokens=args.tokens)
+    elif wl is C6KvPaged:
+        w = wl(dev, 0, pages=args.kv_pages)
+    else:
+        w = wl(dev, 0)
     times = []
     vals = []
     for i in range(args.warmup + args.steps):
@@ -842,6 +962,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--tokens", type=int, default=1, help="c3_moe: tokens per step (1 or 8)")
     ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
+    ap.add_argument("--kv-pages", type=int, default=65536, help="c6_kv_paged: KV pages (65536 = config 5)")
     ap.add_argument("--device-only", action="store_true",
                     help="parity check, warm-up and timed device steps only: no end-to-end leg, CPU baseline or "
                          "clock sampler (the run the ncu captures in profiles/ use); prints no bench line")
@@ -865,6 +986,8 @@ def main():
         w = wl(dev, rank, tokens=args.tokens, world=world)
     elif wl is C2Vpack:
         w = wl(dev, rank, layers=args.c2_layers)
+    elif wl is C6KvPaged:
+        w = wl(dev, rank, pages=args.kv_pages)
     else:
         w = wl(dev, rank)
     stream = torch.cuda.current_stream(dev)

@@ -236,12 +236,33 @@ void voom_zstd_plan_destroy(void* plan);
  * readable padding after the end), d_plan = the plan image in device memory,
  * d_scratch = info.scratch_bytes of device memory (contents ignored),
  * d_out = output, d_status = n_jobs u32 status words (VOOM_ZSTD_ST_* bits,
- * accumulated: clear before the call).  Enqueues on `stream`; the match
- * resolution loop synchronises with `stream` between passes.
+ * accumulated: clear before the call).  Enqueues every pass on `stream`
+ * without host synchronisation (the resolve passes read their worklist
+ * counts on the device).
  * Replaces: compression.zstd.decompress + the lo/hi interleave of
  * formats/packed2.py:178-191 (decode_body) and runtime/kv_paged.py:98-113. */
 int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                      uint8_t* d_out, uint32_t* d_status, void* stream);
+
+/* ------------------------------------------------- KV spill pages (.kvz) */
+/* One compressed KV page as runtime/kv_paged.py:86-88 writes it: the pickle
+ * of {"shape": tuple, "k": zstd(K bits, 1), "v": zstd(V bits, 1)}. */
+typedef struct voom_kvz_page {
+  uint64_t k_off, k_len; /* the K frame: offset in the gather buffer, bytes */
+  uint64_t v_off, v_len; /* the V frame                                     */
+  int64_t shape[8];      /* the "shape" tuple                               */
+  uint32_t ndim;
+  uint32_t status;       /* 0 = parsed; 1 = not a pickle this walker reads
+                            (the caller unpickles that page itself)          */
+} voom_kvz_page;
+
+/* Copies n pages (h_src_addrs[j], lens[j] bytes; h_src_addrs NULL = the pages
+ * are already at h_dst + dst_offs[j]) into h_dst at dst_offs[j] on `threads`
+ * host threads (<= 0: all cores) and walks each page's pickle in place,
+ * filling pages[j] with the offsets of its two zstd frames in h_dst.
+ * Replaces: the pickle.load of runtime/kv_paged.py:104-105. */
+int voom_kvz_gather(const uint64_t* h_src_addrs, const uint64_t* lens, const uint64_t* dst_offs, uint32_t n,
+                    uint8_t* h_dst, voom_kvz_page* pages, int threads);
 
 /* ------------------------------------------------------- BF16 NF12 sidecar */
 /* One NF12 layer stream in device memory (16-byte aligned): header_bytes of

@@ -44,6 +44,22 @@ def pinned_empty(n: int) -> torch.Tensor:
     return torch.empty(int(n), dtype=torch.uint8, pin_memory=True)
 
 
+class PinnedArena:
+    """A growing pinned host buffer reused across calls (pinning memory costs
+    milliseconds per hundred MB).  Hold `lock` from `get` until every copy
+    out of the buffer has completed."""
+
+    def __init__(self):
+        self._buf: torch.Tensor | None = None
+        self.lock = threading.Lock()
+
+    def get(self, n: int) -> torch.Tensor:
+        if self._buf is None or self._buf.numel() < n:
+            self._buf = None
+            self._buf = pinned_empty(max(int(n), 1) * 5 // 4 + 4096)
+        return self._buf
+
+
 _STAGE_CHUNK = 8 << 20  # bytes per staging half
 _stage: dict = {}         # device index -> (pinned staging tensor, [event, event], lock)
 _stage_lock = threading.Lock()

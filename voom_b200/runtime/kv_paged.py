@@ -20,9 +20,12 @@ Reference interface replaced: runtime/kv_paged.py:35-240.
 
 from __future__ import annotations
 
+import ctypes
 import json
 import pickle
+import platform
 import struct
+import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
@@ -32,6 +35,7 @@ import numpy as np
 import torch
 
 from .. import _device
+from .._lib import check, load
 from ..formats import zstd_host
 from ..formats.zstd_gpu import JOB_DTYPE, ZstdBatch, ZstdError, ZstdPlan, describe
 
@@ -127,6 +131,120 @@ class _Page:
         return load_pages([self])[0]
 
 
+KVZ_PAGE_DTYPE = np.dtype([("k_off", "<u8"), ("k_len", "<u8"), ("v_off", "<u8"), ("v_len", "<u8"),
+                           ("shape", "<i8", (8,)), ("ndim", "<u4"), ("status", "<u4")])
+assert KVZ_PAGE_DTYPE.itemsize == 104
+
+# CPython keeps a bytes object's data inline after a fixed header; the data
+# address is id(obj) + this offset (checked once against ctypes below).
+_BYTES_DATA = bytes.__basicsize__ - 1
+_arenas: dict = {}
+_arenas_lock = threading.Lock()
+
+
+def _inline_bytes_ok() -> bool:
+    if platform.python_implementation() != "CPython":
+        return False
+    probe = bytes(range(97, 123)) * 3
+    return ctypes.string_at(id(probe) + _BYTES_DATA, len(probe)) == probe
+
+
+_INLINE_BYTES = _inline_bytes_ok()
+
+
+def _addresses(blobs: list) -> np.ndarray:
+    """Host addresses of the blobs' bytes (the objects stay alive in `blobs`)."""
+    if _INLINE_BYTES and all(type(b) is bytes for b in blobs):
+        return np.fromiter(map(id, blobs), np.uint64, len(blobs)) + np.uint64(_BYTES_DATA)
+    keep = [b if type(b) is bytes else bytes(b) for b in blobs]
+    blobs[:] = keep
+    return np.array([ctypes.cast(ctypes.c_char_p(b), ctypes.c_void_p).value for b in keep], np.uint64)
+
+
+def _arena(device: torch.device) -> _device.PinnedArena:
+    with _arenas_lock:
+        a = _arenas.get(device.index)
+        if a is None:
+            a = _arenas[device.index] = _device.PinnedArena()
+        return a
+
+
+def _reload(blobs: list, dev: torch.device, same_shape: bool):
+    """Gather the .kvz pages into the device's pinned arena, walk their
+    pickles (pages the native walker does not read are unpickled here), plan
+    every K and V frame, upload once and decode in one batch.  Returns the
+    output buffer, each page's (shape, K offset, V offset, bytes)."""
+    n = len(blobs)
+    blobs = list(blobs)
+    lens = np.fromiter(map(len, blobs), np.uint64, n)
+    offs = np.zeros(n, np.uint64)
+    if n > 1:
+        np.cumsum(lens[:-1], out=offs[1:])
+    total = int(lens.sum())
+    addrs = _addresses(blobs)
+    pages = np.zeros(n, KVZ_PAGE_DTYPE)
+    arena = _arena(dev)
+    with arena.lock:
+        buf = arena.get(total + _device.PAD)
+        host = buf.numpy()
+        check(load().voom_kvz_gather(addrs.ctypes.data, lens.ctypes.data, offs.ctypes.data, n, buf.data_ptr(),
+                                     pages.ctypes.data, 0), "voom_kvz_gather")
+        bad = np.nonzero(pages["status"])[0]
+        if bad.size:
+            extra = []
+            for i in bad:
+                d = pickle.loads(blobs[i])
+                shape = tuple(int(x) for x in d["shape"])
+                extra.append((int(i), shape, bytes(d["k"]), bytes(d["v"])))
+            need = total + sum(len(k) + len(v) for _, _, k, v in extra) + _device.PAD
+            if need > buf.numel():
+                old = host[:total].copy()
+                buf = arena.get(need)
+                host = buf.numpy()
+                host[:total] = old
+            pos = total
+            for i, shape, k, v in extra:
+                pg = pages[i]
+                pg["ndim"] = len(shape)
+                pg["shape"][:len(shape)] = shape
+                for key, fr in (("k", k), ("v", v)):
+                    host[pos:pos + len(fr)] = np.frombuffer(fr, np.uint8)
+                    pg[key + "_off"], pg[key + "_len"] = pos, len(fr)
+                    pos += len(fr)
+            total = pos
+        ndim = pages["ndim"].astype(np.int64)
+        shp = pages["shape"]
+        dims = np.where(np.arange(8)[None, :] < ndim[:, None], shp, 1)
+        nbytes = dims.prod(axis=1) * 2
+        if (shp < 0).any() or (ndim > 8).any():
+            raise ValueError("negative dimensions in a .kvz page shape")
+        shapes = [tuple(int(x) for x in shp[i, :ndim[i]]) for i in range(n)] if not same_shape else None
+        if same_shape:
+            if n and (ndim != ndim[0]).any() or n and (shp != shp[0]).any():
+                raise ValueError("reload_blobs needs pages of one shape")
+            shapes = [tuple(int(x) for x in shp[0, :ndim[0]])] * n if n else []
+        span = (nbytes + 255) // 256 * 256
+        dst = np.zeros(n, np.int64)
+        if n > 1:
+            np.cumsum(2 * span[:-1], out=dst[1:])
+        jobs = np.zeros(2 * n, dtype=JOB_DTYPE)
+        jobs["src"][0::2], jobs["src_len"][0::2] = pages["k_off"], pages["k_len"]
+        jobs["src"][1::2], jobs["src_len"][1::2] = pages["v_off"], pages["v_len"]
+        jobs["dst"][0::2], jobs["dst"][1::2] = dst, dst + span
+        jobs["dst_len"][0::2] = jobs["dst_len"][1::2] = nbytes
+        out_bytes = int(dst[-1] + 2 * span[-1]) if n else 0
+        with torch.cuda.device(dev):
+            d_src = _device.upload(buf[:total], dev)  # one async DMA from pinned memory
+            plan = ZstdPlan(host[:total], jobs)       # host plan overlaps the DMA
+            out = torch.empty(max(out_bytes, 1), dtype=torch.uint8, device=dev)
+            batch = ZstdBatch(plan, dev)
+            batch.run(d_src, out)
+            st = batch.job_status()                    # waits for the decode (and the DMA)
+    if st.any():
+        raise ZstdError(describe(int(st[np.nonzero(st)[0][0]])))
+    return out, [(shapes[i], int(dst[i]), int(dst[i] + span[i]), int(nbytes[i])) for i in range(n)]
+
+
 def load_pages(pages: list[_Page]) -> list[tuple[torch.Tensor, torch.Tensor]]:
     """Reload spilled pages: every zstd frame of every compressed page in one
     batched GPU decode; uncompressed pages through safetensors."""
@@ -141,37 +259,14 @@ def load_pages(pages: list[_Page]) -> list[tuple[torch.Tensor, torch.Tensor]]:
     if not comp:
         return out
     dev = comp[0][1].device
-    blobs, jobs, shapes = [], [], []
-    src = dst = 0
+    blobs = []
     for _, p in comp:
         with open(p.path, "rb") as f:
-            d = pickle.load(f)
-        shape = tuple(d["shape"])
-        n = int(np.prod(shape)) * 2
-        for key in ("k", "v"):
-            b = d[key]
-            blobs.append(b)
-            jobs.append((src, len(b), dst, n, 0, 0, 0))
-            src += len(b)
-            dst += (n + 255) // 256 * 256
-        shapes.append((shape, n))
-    host = np.frombuffer(b"".join(blobs), np.uint8)
-    jarr = np.array(jobs, dtype=JOB_DTYPE)
-    plan = ZstdPlan(host, jarr)
-    with torch.cuda.device(dev):
-        d_src = _device.upload(host, dev)
-        buf = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
-        batch = ZstdBatch(plan, dev)
-        batch.run(d_src, buf)
-        st = batch.job_status()
-    if st.any():
-        raise ZstdError(describe(int(st[np.nonzero(st)[0][0]])))
-    for q, (i, _p) in enumerate(comp):
-        shape, n = shapes[q]
-        kd, vd = int(jarr[2 * q]["dst"]), int(jarr[2 * q + 1]["dst"])
-        k = buf[kd:kd + n].view(torch.bfloat16).reshape(shape)
-        v = buf[vd:vd + n].view(torch.bfloat16).reshape(shape)
-        out[i] = (k, v)
+            blobs.append(f.read())
+    buf, spans = _reload(blobs, dev, same_shape=False)
+    for (i, _p), (shape, kd, vd, n) in zip(comp, spans):
+        out[i] = (buf[kd:kd + n].view(torch.bfloat16).reshape(shape),
+                  buf[vd:vd + n].view(torch.bfloat16).reshape(shape))
     return out
 
 
@@ -291,29 +386,17 @@ def spill_pages_compressed(pages_k: np.ndarray, pages_v: np.ndarray, threads: in
 
 
 def reload_blobs(blobs: list[bytes], device=None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Decode many .kvz pages in one batched GPU decode -> (K, V) stacked on
-    a leading page axis."""
+    """Decode many .kvz pages (all of one shape) in one batched GPU decode ->
+    (K, V) stacked on a leading page axis (views of one device buffer)."""
     dev = _device.require_cuda(device)
-    frames, jobs, shape = [], [], None
-    src = dst = 0
-    for blob in blobs:
-        d = pickle.loads(blob)
-        shape = tuple(d["shape"])
-        n = int(np.prod(shape)) * 2
-        for key in ("k", "v"):
-            frames.append(d[key])
-            jobs.append((src, len(d[key]), dst, n, 0, 0, 0))
-            src += len(d[key])
-            dst += n
-    host = np.frombuffer(b"".join(frames), np.uint8)
-    plan = ZstdPlan(host, np.array(jobs, dtype=JOB_DTYPE))
-    with torch.cuda.device(dev):
-        d_src = _device.upload(host, dev)
-        buf = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
-        batch = ZstdBatch(plan, dev)
-        batch.run(d_src, buf)
-        st = batch.job_status()
-    if st.any():
-        raise ZstdError(describe(int(st[np.nonzero(st)[0][0]])))
-    kv = buf.view(torch.bfloat16).reshape(len(blobs), 2, *shape)
+    if not blobs:
+        raise ValueError("reload_blobs needs at least one page")
+    buf, spans = _reload(blobs, dev, same_shape=True)
+    shape, _, _, n = spans[0]
+    span = (n + 255) // 256 * 256
+    if span == n:
+        kv = buf[:2 * n * len(blobs)].view(torch.bfloat16).reshape(len(blobs), 2, *shape)
+        return kv[:, 0], kv[:, 1]
+    rows = buf[:2 * span * len(blobs)].view(len(blobs), 2, span)[:, :, :n]
+    kv = rows.contiguous().view(torch.bfloat16).reshape(len(blobs), 2, *shape)
     return kv[:, 0], kv[:, 1]
