@@ -201,7 +201,9 @@ enum {
   VOOM_ZSTD_ST_OFFSET = 8u,    /* match reaches before the frame start / zero   */
   VOOM_ZSTD_ST_SIZE = 16u,     /* content size / block size / job length mismatch */
   VOOM_ZSTD_ST_CHECKSUM = 32u, /* XXH64 content checksum mismatch */
-  VOOM_ZSTD_ST_UNRESOLVED = 64u /* match chains not resolved (internal limit) */
+  VOOM_ZSTD_ST_UNRESOLVED = 64u, /* match chains not resolved (internal limit) */
+  VOOM_ZSTD_ST_TOO_LARGE = 128u  /* a job with matches decoding to more than
+                                    2 GiB - 1 MiB (split it into several jobs) */
 };
 
 typedef struct voom_zstd_plan_info {
@@ -212,6 +214,10 @@ typedef struct voom_zstd_plan_info {
   uint64_t decoded_bytes;   /* sum of dst_len over planned jobs              */
   uint64_t scratch_bytes;   /* device scratch voom_zstd_decode needs         */
   uint64_t plan_bytes;      /* bytes of the device plan image                */
+  uint32_t n_segments;      /* decode passes (each at most 1 GiB of jobs that
+                               need match resolution)                         */
+  uint32_t n_direct_jobs;   /* jobs without sequences, decoded straight to the
+                               output                                         */
 } voom_zstd_plan_info;
 
 /* Host plan of a batch of jobs whose bytes are in host memory h_src: walks
@@ -232,8 +238,8 @@ int voom_zstd_plan_image(const void* plan, void* h_image, uint64_t cap);
 int voom_zstd_plan_job_status(const void* plan, uint32_t* h_status);
 void voom_zstd_plan_destroy(void* plan);
 
-/* GPU decode of a planned batch: d_src = the same bytes as h_src (16 bytes of
- * readable padding after the end), d_plan = the plan image in device memory,
+/* GPU decode of a planned batch: d_src = the same bytes as h_src, 16-byte
+ * aligned, with 16 bytes of readable padding after the end; d_plan = the plan image in device memory,
  * d_scratch = info.scratch_bytes of device memory (contents ignored),
  * d_out = output, d_status = n_jobs u32 status words (VOOM_ZSTD_ST_* bits,
  * accumulated: clear before the call).  Enqueues every pass on `stream`

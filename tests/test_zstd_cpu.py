@@ -91,3 +91,40 @@ def test_frame_content_size(frames):
             assert fcs is None
         else:
             assert fcs == len(raw), name
+
+
+def test_planner_direct_jobs_and_segments(built_lib):
+    """Jobs without sequences (and not interleaved) are planned direct, with
+    no link-word scratch; jobs with matches are cut into segments of at most
+    1 GiB of decoded bytes; one job above 2 GiB - 1 MiB is refused."""
+    from voom_b200 import synthetic
+    from voom_b200.formats import zstd_gpu as Z
+    from voom_b200.formats import zstd_host as zh
+
+    k, _ = synthetic.kv_pages(8, seed=3)
+    lit_frames = [zh.compress(k[i].tobytes(), 1) for i in range(8)]
+    rep = (np.arange(1 << 20, dtype=np.uint32) % 977).astype(np.uint8).tobytes()
+    seq_frame = zh.compress(rep, 1)
+    src = b"".join(lit_frames) + seq_frame
+    n_rep = 2600  # 2600 MiB of matched output -> 3 segments
+    jobs = np.zeros(8 + n_rep + 2, dtype=Z.JOB_DTYPE)
+    off = 0
+    for i, f in enumerate(lit_frames):
+        jobs[i] = (off, len(f), i * 32768, 32768, 0, 0, 0)
+        off += len(f)
+    for i in range(n_rep):
+        jobs[8 + i] = (off, len(seq_frame), (8 + i) << 20, 1 << 20, 0, 0, 0)
+    jobs[8 + n_rep] = (0, len(lit_frames[0]), 0, 32768, 0, Z.INTERLEAVE, 0)  # interleaved: not direct
+    jobs[9 + n_rep] = (off, len(seq_frame), 0, 3 << 30, 0, 0, 0)  # claims 3 GiB with matches
+    plan = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs)
+    info = plan.info
+    assert info.n_direct_jobs == 8
+    assert info.n_segments == 3
+    assert plan.plan_status[9 + n_rep] == Z.ST_TOO_LARGE
+    assert not plan.plan_status[:9 + n_rep].any()
+    assert "too large" in Z.describe(Z.ST_TOO_LARGE)
+    # the link words of the largest segment (1 GiB) bound the scratch
+    assert 4 << 30 <= info.scratch_bytes < (4 << 30) + (1 << 30)
+
+    only_direct = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs[:8])
+    assert only_direct.info.n_direct_jobs == 8 and only_direct.info.scratch_bytes < (2 << 20)  # worklists only

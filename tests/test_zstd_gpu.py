@@ -117,3 +117,85 @@ def test_large_hi_plane_multi_block(Z):
     hi = synthetic.bf16_normal((8 << 20,), 0.02, 5).view(np.uint8)[1::2].tobytes()  # 8 MiB, 64 blocks
     fr = zh.compress(hi, 1)
     assert Z.decompress(fr) == hi
+
+
+def test_direct_and_segmented_batch_bit_exact(Z):
+    """One batch of literal-only KV frames (decoded straight to the output,
+    one lane per Huffman stream) and 1.25 GiB of matched jobs (two Z-space
+    segments), bit-exact."""
+    from voom_b200 import _device, synthetic
+    from voom_b200.formats import zstd_host as zh
+
+    k, v = synthetic.kv_pages(64, seed=6)
+    pages = [k[i].tobytes() for i in range(64)] + [v[i].tobytes() for i in range(64)]
+    lit_frames = [zh.compress(p, 1) for p in pages]
+    rep = (np.arange(1 << 22, dtype=np.uint32) % 1021).astype(np.uint8)
+    rep[::4093] ^= 0x5A
+    seq_frame = zh.compress(rep.tobytes(), 1)
+    n_rep = 320  # 1.25 GiB of matched output
+    src = b"".join(lit_frames) + seq_frame
+    jobs = np.zeros(len(pages) + n_rep, dtype=Z.JOB_DTYPE)
+    off = dst = 0
+    for i, f in enumerate(lit_frames):
+        jobs[i] = (off, len(f), dst, 32768, 0, 0, 0)
+        off += len(f)
+        dst += 32768
+    for i in range(n_rep):
+        jobs[len(pages) + i] = (off, len(seq_frame), dst, rep.size, 0, 0, 0)
+        dst += rep.size
+    plan = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs)
+    assert plan.info.n_segments == 2 and plan.info.n_direct_jobs == len(pages)
+    dev = torch.device("cuda", 0)
+    d_src = _device.upload(np.frombuffer(src, np.uint8), dev)
+    out = torch.empty(dst, dtype=torch.uint8, device=dev)
+    batch = Z.ZstdBatch(plan, dev)
+    batch.run(d_src, out)
+    assert not batch.job_status().any()
+    lit_out = out[:len(pages) * 32768].cpu().numpy()
+    assert lit_out.tobytes() == b"".join(pages)
+    reps = out[len(pages) * 32768:].view(n_rep, rep.size)
+    assert torch.equal(reps, torch.from_numpy(rep).to(dev).expand(n_rep, -1))
+
+
+def test_direct_literals_unaligned_outputs_and_damage(Z):
+    """Direct jobs at odd output offsets (byte head / tail around the 32-bit
+    stores), single-stream literals, and a truncated literal stream that must
+    be reported, never accepted."""
+    from voom_b200 import _device, synthetic
+    from voom_b200.formats import zstd_host as zh
+
+    rng = np.random.default_rng(12)
+    k, _ = synthetic.kv_pages(6, seed=2)
+    raws = [k[i].tobytes()[:n] for i, n in enumerate([32768, 32767, 1500, 200, 9001, 32766])]
+    frames = [zh.compress(r, 1) for r in raws]
+    src = b"".join(frames)
+    jobs = np.zeros(len(raws), dtype=Z.JOB_DTYPE)
+    off, dst = 0, 3
+    for i, (f, r) in enumerate(zip(frames, raws)):
+        jobs[i] = (off, len(f), dst, len(r), 0, 0, 0)
+        off += len(f)
+        dst += len(r) + int(rng.integers(1, 7))
+    plan = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs)
+    assert plan.info.n_direct_jobs == len(raws)
+    dev = torch.device("cuda", 0)
+    out = torch.zeros(dst + 16, dtype=torch.uint8, device=dev)
+    batch = Z.ZstdBatch(plan, dev)
+    batch.run(_device.upload(np.frombuffer(src, np.uint8), dev), out)
+    assert not batch.job_status().any()
+    got = out.cpu().numpy()
+    for j, r in zip(jobs, raws):
+        assert got[int(j["dst"]):int(j["dst"]) + len(r)].tobytes() == r
+    # a frame whose last literal stream lost bytes: rejected like the oracle
+    f = bytearray(frames[0])
+    bad = bytes(f[:-30]) + bytes(30)
+    assert oz_reject(bad, len(raws[0]))
+    with pytest.raises(Z.ZstdError):
+        Z.decompress(bad, size=len(raws[0]))
+
+
+def oz_reject(frame: bytes, n: int) -> bool:
+    try:
+        oz.decompress(frame, capacity=n + 64)
+    except oz.ZstdError:
+        return True
+    return False

@@ -31,6 +31,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "common.cuh"
 #include "zstd_plan.h"
 
@@ -154,6 +156,98 @@ struct DownWin {
     hi |= __funnelshift_rc(q0, 0u, vb) & m;
     lo |= __funnelshift_lc(0u, q0, 32u - vb) & m;
     vb += m & 32u;
+    if (use) {
+      q0 = q1;
+      q1 = word(nidx);
+      nidx--;
+    }
+  }
+};
+
+// Asynchronous 16-byte global -> shared copies (cp.async, per thread groups).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// DownWin for one lane reading its own stream through a ring of 32 words (4
+// quarters of 8) in shared memory, filled by cp.async.  Async-copy groups are
+// tracked per warp, so a lane waiting for its own copy would wait for every
+// lane's: the decode therefore runs in warp-uniform rounds (at most 8 ring
+// words, one quarter, per lane per round), and at each round start every
+// lane commits one group (possibly empty) and waits only for the groups of
+// earlier rounds.  A lane keeps the three quarters below the one it reads
+// from issued (the whole ring at the start), so every quarter it reads in a
+// round was issued at least two rounds earlier.  Words are counted from the
+// 16-byte boundary at or below the stream start; bits below the stream start
+// read as whatever precedes it, which cannot change a decode that ends
+// exactly on the stream's first bit (and one that does not is rejected either
+// way).
+constexpr int kRingStride = 36;  // words per lane row (16-byte aligned rows)
+constexpr int kRingRound = 8;    // ring words a lane may read per round
+
+struct RingWin {
+  const uint8_t* g;
+  uint32_t* ring;
+  uint32_t nchunk;  // 16-byte chunks from g that hold stream bytes (0: lane idle)
+  uint32_t hi, lo, vb;
+  uint32_t q0, q1;
+  int32_t nidx;
+  int32_t P;
+  int32_t nextq;  // next quarter to issue
+
+  __device__ __forceinline__ uint32_t word(int32_t i) const { return i < 0 ? 0u : ring[i & 31]; }
+  __device__ __forceinline__ void fetch(int32_t h) {  // words [8h, 8h + 8) into their ring slots
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const uint32_t c = 2u * uint32_t(h) + uint32_t(k);
+      if (h >= 0 && c < nchunk) cp_async16(ring + ((8 * h + 4 * k) & 31), g + 16ull * c);
+    }
+  }
+  // every lane of the warp calls this (an idle lane passes slen = 0)
+  __device__ __forceinline__ void init(const uint8_t* s, uint32_t slen, int32_t P0, uint32_t* lane_ring) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(s);
+    g = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(15));
+    const uint32_t off = uint32_t(a & 15u);
+    ring = lane_ring;
+    nchunk = slen ? (off + slen + 15) / 16 : 0u;
+    P = P0;
+    const int32_t A = slen ? P0 + int32_t(8 * off) : 1;
+    const int32_t m = (A - 1) >> 5;
+    for (int k = 0; k < 4; k++) fetch((m >> 3) - k);  // the whole ring
+    nextq = (m >> 3) - 4;
+    cp_async_commit();
+    cp_async_wait_all();
+    const uint32_t sh = uint32_t(32 * (m + 1) - A);
+    const uint32_t wm = word(m), wm1 = word(m - 1);
+    hi = __funnelshift_l(wm1, wm, sh);
+    lo = wm1 << sh;
+    vb = 64u - sh;
+    q0 = word(m - 2);
+    q1 = word(m - 3);
+    nidx = m - 4;
+  }
+  // round start (after the warp's wait): issue the quarters down to three
+  // below the one the next read falls in
+  __device__ __forceinline__ void top_up() {
+    const int32_t target = (nidx >> 3) - 3;
+    while (nextq >= target && nextq >= 0) fetch(nextq--);
+  }
+  __device__ __forceinline__ void consume(uint32_t n) {
+    hi = __funnelshift_l(lo, hi, n);
+    lo <<= n;
+    vb -= n;
+    P -= int32_t(n);
+  }
+  __device__ __forceinline__ void refill() {
+    const bool use = vb <= 32u;
+    const uint32_t mk = use ? 0xFFFFFFFFu : 0u;
+    hi |= __funnelshift_rc(q0, 0u, vb) & mk;
+    lo |= __funnelshift_lc(0u, q0, 32u - vb) & mk;
+    vb += mk & 32u;
     if (use) {
       q0 = q1;
       q1 = word(nidx);
@@ -504,6 +598,159 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
   if (!ok && lane == 0) atomicOr(&sh.st, VOOM_ZSTD_ST_LITERALS);
 }
 
+// Huffman literals of direct jobs' blocks (no sequences: the literals are the
+// output), one lane per stream.  Spans of one stream decoded in parallel enter
+// their span speculatively and need another pass for every lane whose entry
+// did not resynchronise; literals close to uniform (the low bytes of BF16
+// activations) resynchronise slowly, so here every stream is decoded once,
+// serially, and the parallelism comes from the number of streams: a warp
+// takes 8 blocks, lanes 4g..4g+3 the (up to) 4 streams of block g, with the
+// block's single-symbol decode table (2^maxbits u16 entries) in shared memory.
+constexpr int kDlBlocksPerWarp = 8;
+constexpr uint32_t kHufTab = 1u << 11;  // RFC 8878 caps Huffman codes at 11 bits
+
+__global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __restrict__ src, const uint8_t* img,
+                                                           uint8_t* scratch, uint8_t* __restrict__ out,
+                                                           uint32_t* status) {
+  __shared__ uint16_t s_tab[kDlBlocksPerWarp][kHufTab];
+  __shared__ __align__(16) uint32_t s_ring[32][kRingStride];
+  const View v = make_view(img, scratch);
+  const uint32_t* dlit = reinterpret_cast<const uint32_t*>(img + v.h->off_dlit);
+  const uint32_t lane = threadIdx.x, g = lane >> 2, q = lane & 3u;
+  const uint32_t slot = blockIdx.x * kDlBlocksPerWarp + g;
+  const bool on = slot < v.h->n_dlit;
+  ZBlock b;
+  uint32_t maxbits = 1, nsym = 0;
+  const ZHuf* H = nullptr;
+  if (on) {
+    b = v.blocks[dlit[slot]];
+    H = v.huf + b.huf;
+    maxbits = H->maxbits;
+    nsym = H->nsym;
+  }
+  // table build: lane q of the group places symbols [64q, 64q + 64); codes are
+  // canonical (weight ascending, then symbol order), so every weight's first
+  // position is the sum over lighter weights and a lane's offset within a
+  // weight is the count of that weight in the lanes before it
+  uint32_t cnt[12];
+#pragma unroll
+  for (int k = 0; k < 12; k++) cnt[k] = 0;
+  const uint32_t s0 = 64 * q, s1 = min(nsym, s0 + 64);
+  for (uint32_t sy = s0; sy < s1; sy++) {
+    const uint32_t w = H->w[sy];
+#pragma unroll
+    for (int k = 1; k < 12; k++) cnt[k] += (w == uint32_t(k));
+  }
+  uint32_t pos[12];
+  uint32_t start = 0;
+#pragma unroll
+  for (int k = 1; k < 12; k++) {
+    uint32_t incl = cnt[k];
+    uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, 1, 4);
+    if (q >= 1) incl += t;
+    t = __shfl_up_sync(0xFFFFFFFFu, incl, 2, 4);
+    if (q >= 2) incl += t;
+    const uint32_t total = __shfl_sync(0xFFFFFFFFu, incl, 3, 4);
+    pos[k] = start + ((incl - cnt[k]) << (k - 1));
+    start += total << (k - 1);
+  }
+  // a complete code fills the table exactly (the same for the group's lanes)
+  bool ok = start == (1u << maxbits);
+  uint16_t* tab = s_tab[g];
+  for (uint32_t sy = s0; sy < s1 && ok; sy++) {
+    const uint32_t w = H->w[sy];
+    if (!w) continue;
+    uint32_t p = 0;
+#pragma unroll
+    for (int k = 1; k < 12; k++)
+      if (w == uint32_t(k)) {
+        p = pos[k];
+        pos[k] += 1u << (k - 1);
+      }
+    const uint16_t e = uint16_t(sy | ((maxbits + 1 - w) << 8));
+    const uint32_t len = 1u << (w - 1);
+    for (uint32_t i = 0; i < len; i++)
+      if (p + i < kHufTab) tab[p + i] = e;
+  }
+  __syncwarp();
+  // From here every lane stays to the end: the rounds below are warp-uniform.
+  const int streams = on ? int(b.lit_streams) : 0;
+  const bool act = on && int(q) < streams;
+  uint32_t seg = 0, count = 0, slen = 0;
+  const uint8_t* sp = src;
+  uint8_t* dst = out;
+  int32_t B = 0;
+  if (act) {
+    const ZJob& job = v.jobs[b.job];
+    seg = streams == 1 ? b.lit_regen : (b.lit_regen + 3) / 4;
+    count = (streams == 1 || q < 3) ? seg : b.lit_regen - 3 * seg;
+    uint64_t off = b.src;
+    slen = b.lit_len[0];
+#pragma unroll
+    for (uint32_t k = 1; k < 4; k++)
+      if (k <= q) {
+        off += slen;
+        slen = b.lit_len[k];
+      }
+    sp = src + off;
+    const uint32_t lastb = slen ? __ldg(sp + slen - 1) : 0u;
+    ok = ok && lastb != 0 && seg * uint64_t(q) <= b.lit_regen;
+    if (ok) B = int32_t(8 * (slen - 1) + (31 - __clz(lastb)));
+    dst = out + job.dst + b.out_off + uint64_t(q) * seg;
+  }
+  ok = act && ok;
+  RingWin W;
+  W.init(sp, ok ? slen : 0u, B, s_ring[lane]);
+  const uint32_t shift = 32u - maxbits;
+  uint32_t n = 0;
+  // one symbol: a refill leaves >= 32 valid bits, a code is <= 11
+  auto one = [&]() -> uint32_t {
+    W.refill();
+    const uint32_t e = tab[W.hi >> shift];
+    W.consume(e >> 8);
+    return e;
+  };
+  // head: single symbols up to a 4-byte boundary of the output (within the
+  // ring's initial four quarters: at most 3 refills)
+  if (ok) {
+    const uint32_t head = min(count, uint32_t(4u - (reinterpret_cast<uintptr_t>(dst) & 3u)) & 3u);
+    for (; n < head && W.P >= -32; n++) dst[n] = uint8_t(one());
+  }
+  uint32_t* d32 = reinterpret_cast<uint32_t*>(dst + n);
+  bool live = ok && n + 4 <= count && W.P >= -32;
+  while (__any_sync(0xFFFFFFFFu, live)) {
+    cp_async_wait_prev();
+    if (live) W.top_up();
+    cp_async_commit();
+    // 4 symbols (two refills, at most 2 ring words) and one 32-bit store per step
+#pragma unroll 2
+    for (int r = 0; r < kRingRound / 2; r++) {
+      if (live) {
+        W.refill();
+        const uint32_t e0 = tab[W.hi >> shift];
+        W.consume(e0 >> 8);
+        const uint32_t e1 = tab[W.hi >> shift];
+        W.consume(e1 >> 8);
+        W.refill();
+        const uint32_t e2 = tab[W.hi >> shift];
+        W.consume(e2 >> 8);
+        const uint32_t e3 = tab[W.hi >> shift];
+        W.consume(e3 >> 8);
+        *d32++ = __byte_perm(__byte_perm(e0, e1, 0x0040), __byte_perm(e2, e3, 0x0040), 0x5410);
+        n += 4;
+        live = n + 4 <= count && W.P >= -32;
+      }
+    }
+  }
+  // every copy complete: the tail below may read from the quarter issued last,
+  // and no copy may still target shared memory when the CTA exits
+  cp_async_wait_all();
+  if (ok)  // tail: fewer than 4 symbols (at most 3 more ring words)
+    for (; n < count && W.P >= -32; n++) dst[n] = uint8_t(one());
+  ok = ok && n == count && W.P == 0;
+  if (act && !ok) atomicOr(status + b.job, VOOM_ZSTD_ST_LITERALS);
+}
+
 // Symbolic repeat-offset slot: kind 0..2 = the block's input slot minus d,
 // kind 3 = the constant d.
 struct RepSlots {
@@ -746,11 +993,13 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
 }
 
 __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t* __restrict__ src,
-                                                                const uint8_t* img, uint8_t* scratch) {
+                                                                const uint8_t* img, uint8_t* scratch,
+                                                                uint8_t* out, uint32_t block0) {
   __shared__ K1Shared sh;
   const View v = make_view(img, scratch);
-  const ZBlock b = v.blocks[blockIdx.x];
-  ZBlockRt* rt = v.rt + blockIdx.x;
+  const uint32_t bi = block0 + blockIdx.x;
+  const ZBlock b = v.blocks[bi];
+  ZBlockRt* rt = v.rt + bi;
   if (b.type != 2) {
     if (threadIdx.x == 0) {
       rt->out_size = b.size;
@@ -771,7 +1020,12 @@ __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t
     }
   }
   __syncthreads();
-  if (threadIdx.x < 32 * kLitWarps) decode_literals(src, v, b, sh, v.lit + b.lit_off);
+  if (threadIdx.x < 32 * kLitWarps) {
+    // a direct job's literals are its output bytes
+    const ZJob& job = v.jobs[b.job];
+    if (!(job.direct && b.lit_type == 2))  // those are zstd_direct_literals' work
+      decode_literals(src, v, b, sh, job.direct ? out + job.dst + b.out_off : v.lit + b.lit_off);
+  }
   else if (b.nseq) decode_sequences(src, v, b, sh);
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -800,7 +1054,8 @@ __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t
 constexpr int kSeqScanThreads = 256;
 constexpr int kSeqPerThread = 4;
 
-__global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch) {
+__global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch,
+                                                                 uint32_t block0) {
   constexpr int kW = kSeqScanThreads / 32;
   __shared__ uint32_t s_k[kW][3], s_d[kW][3];
   __shared__ uint32_t s_ll[kW], s_ml[kW];
@@ -808,9 +1063,9 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
   __shared__ uint32_t s_ck[kW + 1][3], s_cd[kW + 1][3];
   __shared__ uint32_t s_cl[kW + 1], s_cm[kW + 1];
   const View v = make_view(img, scratch);
-  const ZBlock b = v.blocks[blockIdx.x];
+  const ZBlock b = v.blocks[block0 + blockIdx.x];
   if (b.type != 2 || b.nseq == 0) return;
-  ZBlockRt* rt = v.rt + blockIdx.x;
+  ZBlockRt* rt = v.rt + block0 + blockIdx.x;
   if (rt->status) return;  // the block failed in K1; its job is reported bad
   ZSeq* seq = v.seq + b.seq_off;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, n = b.nseq;
@@ -1007,11 +1262,13 @@ __device__ __forceinline__ uint32_t rep_apply(const RepSlots& t, const uint32_t 
 }
 
 __global__ void __launch_bounds__(32 * kJobScanWarps) zstd_job_scan(const uint8_t* img, uint8_t* scratch,
-                                                                     uint32_t* status) {
+                                                                     uint32_t* status, uint32_t job0,
+                                                                     uint32_t n_jobs) {
   const View v = make_view(img, scratch);
   const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t j = blockIdx.x * kJobScanWarps + (threadIdx.x >> 5);
-  if (j >= v.h->n_jobs) return;
+  const uint32_t jr = blockIdx.x * kJobScanWarps + (threadIdx.x >> 5);
+  if (jr >= n_jobs) return;
+  const uint32_t j = job0 + jr;
   const ZJob job = v.jobs[j];
   if (job.bad) return;
   uint64_t z = job.zoff;
@@ -1101,14 +1358,31 @@ __global__ void __launch_bounds__(32 * kJobScanWarps) zstd_job_scan(const uint8_
 constexpr uint32_t kExecChunk = 4096;
 constexpr uint32_t kExecMaxChunks = (128 * 1024) / kExecChunk + 1;
 
+constexpr uint32_t kLongLit = 64;  // literal runs longer than this are copied by the whole CTA
+
 __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                          uint8_t* scratch, uint32_t* status) {
+                                                          uint8_t* scratch, uint8_t* __restrict__ out,
+                                                          uint32_t* status, uint32_t block0) {
   __shared__ uint32_t s_out[kExecChunk];
   __shared__ uint32_t s_first[kExecMaxChunks];
+  __shared__ uint3 s_long[kExecChunk / (kLongLit + 1) + 1];  // (first, end, literal position) per long run
+  __shared__ uint32_t s_nlong;
   const View v = make_view(img, scratch);
-  const ZBlock b = v.blocks[blockIdx.x];
-  if (v.jobs[b.job].bad) return;
-  const ZBlockRt rt = v.rt[blockIdx.x];
+  const uint32_t bi = block0 + blockIdx.x;
+  const ZBlock b = v.blocks[bi];
+  const ZJob& job = v.jobs[b.job];
+  if (job.bad) return;
+  if (job.direct) {  // raw / RLE bytes straight to the output; literals were written by K1
+    uint8_t* d = out + job.dst + b.out_off;
+    if (b.type == 0) {
+      for (uint32_t i = threadIdx.x; i < b.size; i += blockDim.x) d[i] = __ldg(src + b.src + i);
+    } else if (b.type == 1) {
+      const uint8_t c = __ldg(src + b.src);
+      for (uint32_t i = threadIdx.x; i < b.size; i += blockDim.x) d[i] = c;
+    }
+    return;
+  }
+  const ZBlockRt rt = v.rt[bi];
   uint32_t* res = v.res + rt.zstart;
   if (b.type == 0) {
     for (uint32_t i = threadIdx.x; i < b.size; i += blockDim.x) res[i] = kResolved | __ldg(src + b.src + i);
@@ -1135,6 +1409,7 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
   }
   // s_first[c] = the record holding chunk c's first byte
   for (uint32_t c = threadIdx.x; c < nchunks; c += blockDim.x) s_first[c] = n;
+  if (threadIdx.x == 0) s_nlong = 0;
   __syncthreads();
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
     const ZSeq s = seq[i];
@@ -1167,7 +1442,9 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
       if (dst >= c1) break;  // records are in output order
       bad |= !ok;
       const uint32_t a0 = max(dst, c0), a1 = min(dst + ll, c1);
-      {  // literal bytes, 8 loads in flight at a time (read-only global loads)
+      if (a1 > a0 + kLongLit) {  // a long run: queued for the CTA-wide copy below
+        s_long[atomicAdd(&s_nlong, 1u)] = make_uint3(a0, a1, lp + (a0 - dst));
+      } else {  // literal bytes, 8 loads in flight at a time (read-only global loads)
         uint32_t p = a0;
         for (; p + 8 <= a1; p += 8) {
           const uint8_t* q = lit + lp + (p - dst);
@@ -1205,6 +1482,14 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
       }
     }
     __syncthreads();
+    const uint32_t nlong = s_nlong;
+    for (uint32_t r = 0; r < nlong; r++) {  // long literal runs, coalesced over the CTA
+      const uint3 L = s_long[r];
+      for (uint32_t p = L.x + threadIdx.x; p < L.y; p += blockDim.x)
+        s_out[p - c0] = kResolved | __ldg(lit + L.z + (p - L.x));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_nlong = 0;
     for (uint32_t p = c0 + threadIdx.x; p < c1; p += blockDim.x) res[p] = s_out[p - c0];
     __syncthreads();
   }
@@ -1305,10 +1590,11 @@ __device__ __forceinline__ uint32_t low_bytes(uint32_t a, uint32_t b, uint32_t c
 }
 
 __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                   uint8_t* scratch, uint8_t* __restrict__ out) {
+                                                   uint8_t* scratch, uint8_t* __restrict__ out, uint32_t tile0) {
   __shared__ uint32_t s_unres;
   const View v = make_view(img, scratch);
-  const ZOutTile t = v.tiles[blockIdx.x];
+  const uint32_t ti = tile0 + blockIdx.x;
+  const ZOutTile t = v.tiles[ti];
   const ZJob job = v.jobs[t.job];
   if (job.bad) return;
   if (threadIdx.x == 0) s_unres = 0;
@@ -1347,7 +1633,7 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
         for (int i = 0; i < 8; i++) {
           if (!(u[i] & kResolved)) {
             unres++;
-            list_push(v, ctr, 0, uint32_t(z + i), blockIdx.x);
+            list_push(v, ctr, 0, uint32_t(z + i), ti);
           }
         }
       }
@@ -1360,7 +1646,7 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
           v.res[z + i] = u;
           if (!(u & kResolved)) {
             unres++;
-            list_push(v, ctr, 0, uint32_t(z + i), blockIdx.x);
+            list_push(v, ctr, 0, uint32_t(z + i), ti);
           }
         }
         emit1(job, src, out, k + i, uint8_t(u), true);
@@ -1369,10 +1655,11 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
   }
   if (unres) atomicAdd(&s_unres, unres);
   __syncthreads();
-  if (threadIdx.x == 0) v.dirty[blockIdx.x] = s_unres ? (kPatch | s_unres) : 0u;
+  if (threadIdx.x == 0) v.dirty[ti] = s_unres ? (kPatch | s_unres) : 0u;
 }
 
-__global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, int pass) {
+__global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, int pass,
+                                                    uint32_t tile0) {
   __shared__ uint32_t s_unres;
   const View v = make_view(img, scratch);
   uint32_t* ctr = v.dirty + v.h->n_tiles;
@@ -1391,9 +1678,10 @@ __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t*
     }
     return;
   }
-  const ZOutTile t = v.tiles[blockIdx.x];
+  const uint32_t ti = tile0 + blockIdx.x;
+  const ZOutTile t = v.tiles[ti];
   const ZJob job = v.jobs[t.job];
-  if (job.bad || !(v.dirty[blockIdx.x] & ~kPatch)) return;
+  if (job.bad || !(v.dirty[ti] & ~kPatch)) return;
   if (threadIdx.x == 0) s_unres = 0;
   __syncthreads();
   uint32_t unres = 0;
@@ -1407,11 +1695,12 @@ __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t*
   }
   if (unres) atomicAdd(&s_unres, unres);
   __syncthreads();
-  if (threadIdx.x == 0) v.dirty[blockIdx.x] = kPatch | s_unres;
+  if (threadIdx.x == 0) v.dirty[ti] = kPatch | s_unres;
 }
 
 __global__ void __launch_bounds__(256) zstd_patch(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                  uint8_t* scratch, uint8_t* __restrict__ out, uint32_t* status) {
+                                                  uint8_t* scratch, uint8_t* __restrict__ out, uint32_t* status,
+                                                  uint32_t tile0) {
   const View v = make_view(img, scratch);
   uint32_t* ctr = v.dirty + v.h->n_tiles;
   const uint64_t zmax = v.h->zbytes;
@@ -1434,10 +1723,11 @@ __global__ void __launch_bounds__(256) zstd_patch(const uint8_t* __restrict__ sr
     }
     return;
   }
-  const ZOutTile t = v.tiles[blockIdx.x];
+  const uint32_t ti = tile0 + blockIdx.x;
+  const ZOutTile t = v.tiles[ti];
   const ZJob job = v.jobs[t.job];
-  if (job.bad || !(v.dirty[blockIdx.x] & kPatch)) return;
-  if (v.dirty[blockIdx.x] & ~kPatch) {
+  if (job.bad || !(v.dirty[ti] & kPatch)) return;
+  if (v.dirty[ti] & ~kPatch) {
     if (threadIdx.x == 0) atomicOr(status + t.job, VOOM_ZSTD_ST_UNRESOLVED);
     return;
   }
@@ -1530,31 +1820,46 @@ __global__ void zstd_checksum(const uint8_t* img, uint8_t* scratch, const uint8_
 // Host side: counts come from the host plan handle (zstd_plan.cpp).
 namespace voom {
 namespace zstd {
-bool plan_counts(const void* plan, ZPlanHeader* out);
+bool plan_counts(const void* plan, ZPlanHeader* out, std::vector<ZSegment>* segs);
 }
 }  // namespace voom
 
 VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                               uint8_t* d_out, uint32_t* d_status, void* stream) {
   if (!d_src || !d_plan || !h_plan || !d_scratch || !d_out || !d_status) return VOOM_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(d_src) & 15u) return VOOM_E_INVALID_ARG;  // streams are read in 16-byte chunks
   ZPlanHeader h;
-  if (!voom::zstd::plan_counts(h_plan, &h)) return VOOM_E_INVALID_ARG;
+  std::vector<ZSegment> segs;
+  if (!voom::zstd::plan_counts(h_plan, &h, &segs)) return VOOM_E_INVALID_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* img = static_cast<const uint8_t*>(d_plan);
   uint8_t* scr = static_cast<uint8_t*>(d_scratch);
-  // resolve worklist counters (after the tile flags)
-  if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
-  if (h.n_blocks) {
-    zstd_block_decode<<<h.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr);
-    zstd_seq_scan<<<h.n_blocks, kSeqScanThreads, 0, s>>>(img, scr);
-    zstd_job_scan<<<(h.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(img, scr,
-                                                                                                 d_status);
-    zstd_block_execute<<<h.n_blocks, 256, 0, s>>>(d_src, img, scr, d_status);
+  static bool attrs_set = false;  // per process: ask for the largest shared-memory carveout
+  if (!attrs_set) {
+    cudaFuncSetAttribute(zstd_direct_literals, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attrs_set = true;
   }
-  if (h.n_tiles) {
-    zstd_output<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out);
-    for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<h.n_tiles, 256, 0, s>>>(img, scr, p);
-    zstd_patch<<<h.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status);
+  if (h.n_dlit)
+    zstd_direct_literals<<<(h.n_dlit + kDlBlocksPerWarp - 1) / kDlBlocksPerWarp, 32, 0, s>>>(d_src, img, scr,
+                                                                                            d_out, d_status);
+  // One pass of the pipeline per Z-space segment; the link-word scratch and
+  // the resolve worklists are reused, everything else is indexed globally.
+  for (const ZSegment& g : segs) {
+    // resolve worklist counters (after the tile flags)
+    if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
+    if (g.n_blocks) {
+      zstd_block_decode<<<g.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr, d_out, g.block0);
+      zstd_seq_scan<<<g.n_blocks, kSeqScanThreads, 0, s>>>(img, scr, g.block0);
+      zstd_job_scan<<<(g.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(
+          img, scr, d_status, g.job0, g.n_jobs);
+      zstd_block_execute<<<g.n_blocks, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.block0);
+    }
+    if (g.n_tiles) {
+      zstd_output<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, g.tile0);
+      for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<g.n_tiles, 256, 0, s>>>(img, scr, p, g.tile0);
+      zstd_patch<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.tile0);
+    }
   }
   if (h.n_frames) zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_out, d_status);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;

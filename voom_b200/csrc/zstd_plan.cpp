@@ -449,6 +449,35 @@ void walk_job(const uint8_t* base, const voom_zstd_job& job, JobPlan& jp) {
   }
 }
 
+// A job is direct when it is not interleaved and none of its blocks has
+// sequences: every block's decoded size is then known here (raw / RLE size,
+// or the literals' regenerated size), so each block's output offset is too.
+// The sizes must add up to the job length and match every recorded frame
+// content size; otherwise the job takes the general path, which reports the
+// mismatch.
+bool make_direct(JobPlan& jp, const voom_zstd_job& job) {
+  if (jp.bad || (job.flags & VOOM_ZSTD_INTERLEAVE)) return false;
+  uint64_t off = 0;
+  for (const ZFrame& fr : jp.frames) {
+    const uint64_t f0 = off;
+    for (uint32_t i = fr.block_first; i < fr.block_first + fr.n_blocks; i++) {
+      const ZBlock& b = jp.blocks[i];
+      if (b.type == 2 && b.nseq) return false;
+      const uint64_t sz = b.type == 2 ? b.lit_regen : b.size;
+      if (sz > b.max_out) return false;
+      off += sz;
+    }
+    if (fr.fcs != ~0ull && off - f0 != fr.fcs) return false;
+  }
+  if (off != job.dst_len) return false;
+  off = 0;
+  for (ZBlock& b : jp.blocks) {
+    b.out_off = off;
+    off += b.type == 2 ? b.lit_regen : b.size;
+  }
+  return true;
+}
+
 // Table references of one job's compressed blocks, frame by frame: own
 // tables are appended, treeless / repeat blocks take the previous ones
 // (RFC 8878 3.1.1.3.1.1, 3.1.1.3.2.1.1).
@@ -489,12 +518,14 @@ void resolve_job(JobPlan& jp, const std::vector<BlockTables>& tabs, const std::v
 }
 
 struct Plan {
+  std::vector<ZSegment> segs;
   std::vector<ZJob> jobs;
   std::vector<ZFrame> frames;
   std::vector<ZBlock> blocks;
   std::vector<ZHuf> huf;
   std::vector<ZFse> fse;
   std::vector<ZOutTile> tiles;
+  std::vector<uint32_t> dlit;
   std::vector<uint32_t> status;
   ZPlanHeader hdr;
   uint64_t image_bytes = 0;
@@ -557,9 +588,11 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     b.size = 0;
     okb[j][i] = plan_compressed(h_src, at, bs, b, tabs[j][i]) ? 1 : 0;
   });
-  // 3. table references, frame by frame
+  // 3. table references, frame by frame; direct jobs
+  std::vector<uint8_t> direct(n_jobs, 0);
   parallel(n_jobs, [&](uint64_t j) {
     if (!jp[j].bad) resolve_job(jp[j], tabs[j], okb[j]);
+    direct[j] = make_direct(jp[j], jobs[j]) ? 1 : 0;
   });
 
   // predefined sequence tables occupy fse[0..2]
@@ -573,8 +606,24 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     f.al = uint8_t(k == 1 ? 5 : 6);
     P->fse.push_back(f);
   }
-  uint64_t zoff = 0, lit = 0, nseq = 0;
+  uint64_t zoff = 0, zmax = 0, lit = 0, nseq = 0;
   P->status.assign(n_jobs, 0);
+  ZSegment seg;
+  memset(&seg, 0, sizeof seg);
+  auto close_segment = [&](uint32_t j_end) {
+    seg.n_jobs = j_end - seg.job0;
+    seg.n_frames = uint32_t(P->frames.size()) - seg.frame0;
+    seg.n_blocks = uint32_t(P->blocks.size()) - seg.block0;
+    seg.n_tiles = uint32_t(P->tiles.size()) - seg.tile0;
+    seg.zbytes = zoff;
+    zmax = std::max(zmax, zoff);
+    if (seg.n_jobs) P->segs.push_back(seg);
+    seg.job0 = j_end;
+    seg.frame0 = uint32_t(P->frames.size());
+    seg.block0 = uint32_t(P->blocks.size());
+    seg.tile0 = uint32_t(P->tiles.size());
+    zoff = 0;
+  };
   for (uint32_t j = 0; j < n_jobs; j++) {
     ZJob zj;
     memset(&zj, 0, sizeof zj);
@@ -584,9 +633,20 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     zj.dst_len = jobs[j].dst_len;
     zj.lo_src = jobs[j].lo_src;
     zj.flags = jobs[j].flags;
-    zj.zoff = zoff;
-    zoff += align_up(jobs[j].dst_len, 16);
     JobPlan& q = jp[j];
+    const uint64_t zneed = (q.bad || direct[j]) ? 0 : align_up(jobs[j].dst_len, 16);
+    if (zneed > kZJobMax) {
+      zj.bad = 1;
+      zj.zoff = zoff;
+      P->status[j] = VOOM_ZSTD_ST_TOO_LARGE;
+      P->n_bad++;
+      P->jobs.push_back(zj);
+      continue;
+    }
+    if (zneed && zoff + zneed > kZSeg && j > seg.job0) close_segment(j);
+    zj.zoff = zoff;
+    zoff += zneed;
+    zj.direct = direct[j];
     if (q.bad) {
       zj.bad = 1;
       P->status[j] = VOOM_ZSTD_ST_FORMAT;
@@ -611,10 +671,10 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
         if (b.fse[k] == kNone) continue;
         b.fse[k] = (b.fse[k] & kPredef) ? (b.fse[k] & 3u) : b.fse[k] + sbase;
       }
-      b.src += 0;
       b.lit_off = lit;
       b.seq_off = nseq;
-      if (b.type == 2) {
+      if (b.type == 2 && zj.direct && b.lit_type == 2) P->dlit.push_back(uint32_t(P->blocks.size()));
+      if (b.type == 2 && !zj.direct) {
         lit += align_up(b.lit_regen, 16);
         nseq += b.nseq;
       }
@@ -622,7 +682,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     }
     P->huf.insert(P->huf.end(), q.huf.begin(), q.huf.end());
     P->fse.insert(P->fse.end(), q.fse.begin(), q.fse.end());
-    for (uint64_t s = 0; s < jobs[j].dst_len; s += kOutTile) {
+    for (uint64_t s = 0; !zj.direct && s < jobs[j].dst_len; s += kOutTile) {
       ZOutTile t;
       memset(&t, 0, sizeof t);
       t.job = j;
@@ -632,6 +692,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     }
     P->jobs.push_back(zj);
   }
+  close_segment(n_jobs);
   ZPlanHeader& h = P->hdr;
   memset(&h, 0, sizeof h);
   h.n_jobs = n_jobs;
@@ -647,12 +708,14 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   h.off_huf = o; o = align_up(o + sizeof(ZHuf) * P->huf.size(), 256);
   h.off_fse = o; o = align_up(o + sizeof(ZFse) * P->fse.size(), 256);
   h.off_tiles = o; o = align_up(o + sizeof(ZOutTile) * P->tiles.size(), 256);
+  h.n_dlit = uint32_t(P->dlit.size());
+  h.off_dlit = o; o = align_up(o + sizeof(uint32_t) * P->dlit.size(), 256);
   P->image_bytes = o;
   h.lit_bytes = lit;
   h.n_seq = nseq;
-  h.zbytes = zoff;
+  h.zbytes = zmax;  // the largest segment: the link-word scratch is reused by every segment
   uint64_t s = 0;
-  h.s_res = s; s = align_up(s + 4 * zoff, 256);
+  h.s_res = s; s = align_up(s + 4 * zmax, 256);
   h.s_lit = s; s = align_up(s + lit + 64, 256);
   h.s_seq = s; s = align_up(s + sizeof(ZSeq) * nseq, 256);
   h.s_blk = s; s = align_up(s + sizeof(ZBlockRt) * P->blocks.size(), 256);
@@ -660,7 +723,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   // three worklists of Z positions still unresolved: list 0 from the output
   // pass (kept for the patch pass), lists 1 and 2 alternating between the
   // resolve passes
-  h.list_cap = std::max<uint64_t>(65536, zoff / 64);
+  h.list_cap = std::max<uint64_t>(65536, zmax / 64);
   h.s_list = s; s = align_up(s + 3 * 8 * h.list_cap, 256);
   h.s_total = s;
   return P;
@@ -678,9 +741,16 @@ VOOM_API int voom_zstd_plan_info_get(const void* plan, voom_zstd_plan_info* info
   info->n_bad_jobs = P->n_bad;
   info->lit_bytes = P->hdr.lit_bytes;
   info->n_seq = P->hdr.n_seq;
-  info->decoded_bytes = P->hdr.zbytes;
+  uint64_t decoded = 0;
+  for (size_t j = 0; j < P->jobs.size(); j++)
+    if (!P->jobs[j].bad) decoded += P->jobs[j].dst_len;
+  info->decoded_bytes = decoded;
   info->scratch_bytes = P->hdr.s_total;
   info->plan_bytes = P->image_bytes;
+  info->n_segments = uint32_t(P->segs.size());
+  uint32_t nd = 0;
+  for (const ZJob& j : P->jobs) nd += (j.direct && !j.bad) ? 1u : 0u;
+  info->n_direct_jobs = nd;
   return VOOM_OK;
 }
 
@@ -698,6 +768,7 @@ VOOM_API int voom_zstd_plan_image(const void* plan, void* h_image, uint64_t cap)
   if (!P->huf.empty()) memcpy(img + h.off_huf, P->huf.data(), sizeof(ZHuf) * P->huf.size());
   if (!P->fse.empty()) memcpy(img + h.off_fse, P->fse.data(), sizeof(ZFse) * P->fse.size());
   if (!P->tiles.empty()) memcpy(img + h.off_tiles, P->tiles.data(), sizeof(ZOutTile) * P->tiles.size());
+  if (!P->dlit.empty()) memcpy(img + h.off_dlit, P->dlit.data(), sizeof(uint32_t) * P->dlit.size());
   return VOOM_OK;
 }
 
@@ -713,9 +784,10 @@ VOOM_API void voom_zstd_plan_destroy(void* plan) { delete static_cast<Plan*>(pla
 namespace voom {
 namespace zstd {
 // Launch sizes for voom_zstd_decode, read from the host plan handle.
-bool plan_counts(const void* plan, ZPlanHeader* out) {
+bool plan_counts(const void* plan, ZPlanHeader* out, std::vector<ZSegment>* segs) {
   if (!plan) return false;
   *out = static_cast<const Plan*>(plan)->hdr;
+  *segs = static_cast<const Plan*>(plan)->segs;
   return true;
 }
 }  // namespace zstd

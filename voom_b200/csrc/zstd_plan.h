@@ -13,10 +13,15 @@ constexpr uint32_t kOutTile = 64 * 1024;  // Z-space bytes per output-pass work 
 
 struct ZJob {
   uint64_t src, src_len, dst, dst_len, lo_src;
-  uint64_t zoff;  // first byte of this job in the concatenated decoded space (Z-space)
+  uint64_t zoff;  // first byte of this job in its segment's decoded space (Z-space)
   uint32_t flags;
   uint32_t frame_first, n_frames;
   uint32_t bad;  // structural error found by the planner: not decoded
+  // 1: no block of the job has sequences and it is not interleaved, so the
+  // planner knows every block's output offset: literals and raw / RLE bytes
+  // are written straight to the output (no Z-space, no link words)
+  uint32_t direct;
+  uint32_t pad;
 };
 
 struct ZFrame {
@@ -32,6 +37,7 @@ struct ZBlock {
   uint64_t seq_src;  // compressed: sequence bitstream
   uint64_t lit_off;  // literal scratch offset of this block
   uint64_t seq_off;  // first sequence record of this block
+  uint64_t out_off;  // direct jobs: output offset of the block within the job
   uint32_t type;     // 0 raw, 1 rle, 2 compressed
   uint32_t size;     // raw/rle: decoded bytes
   uint32_t frame;    // global frame index
@@ -70,10 +76,27 @@ struct ZOutTile {
   uint64_t len;
 };
 
+// Z positions are 31-bit (bit 31 of a link word flags a resolved byte), so the
+// jobs that need match resolution are decoded in segments of at most kZSeg
+// Z-space bytes; a job is never split, and one whose own Z size exceeds
+// kZJobMax is refused.
+constexpr uint64_t kZSeg = 1ull << 30;
+constexpr uint64_t kZJobMax = (1ull << 31) - (1ull << 20);
+
+// Contiguous job / frame / block / tile ranges of one segment (host only).
+struct ZSegment {
+  uint32_t job0, n_jobs, frame0, n_frames, block0, n_blocks, tile0, n_tiles;
+  uint64_t zbytes;
+};
+
 // Plan image: this header followed by the arrays at the given byte offsets.
 struct ZPlanHeader {
   uint32_t n_jobs, n_frames, n_blocks, n_huf, n_fse, n_tiles;
   uint64_t off_jobs, off_frames, off_blocks, off_huf, off_fse, off_tiles;
+  // direct jobs' blocks with Huffman literals (global block indices): their
+  // streams are decoded one lane each by zstd_direct_literals
+  uint32_t n_dlit, pad_dlit;
+  uint64_t off_dlit;
   uint64_t lit_bytes, n_seq, zbytes;
   // scratch layout (byte offsets into d_scratch)
   uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_list, s_total;

@@ -25,9 +25,11 @@ assert JOB_DTYPE.itemsize == 48
 
 INTERLEAVE = 1
 ST_FORMAT, ST_LITERALS, ST_SEQUENCES, ST_OFFSET, ST_SIZE, ST_CHECKSUM, ST_UNRESOLVED = 1, 2, 4, 8, 16, 32, 64
+ST_TOO_LARGE = 128
 _ST_NAMES = {ST_FORMAT: "malformed frame", ST_LITERALS: "corrupt literals", ST_SEQUENCES: "corrupt sequences",
              ST_OFFSET: "offset out of range", ST_SIZE: "content size mismatch",
-             ST_CHECKSUM: "content checksum mismatch", ST_UNRESOLVED: "unresolved match chain"}
+             ST_CHECKSUM: "content checksum mismatch", ST_UNRESOLVED: "unresolved match chain",
+             ST_TOO_LARGE: "job too large for one decode (more than 2 GiB - 1 MiB with matches)"}
 
 
 class ZstdError(Exception):
@@ -42,7 +44,8 @@ class PlanInfo(ctypes.Structure):
     _fields_ = [("n_jobs", ctypes.c_uint32), ("n_frames", ctypes.c_uint32), ("n_blocks", ctypes.c_uint32),
                 ("n_huf", ctypes.c_uint32), ("n_fse", ctypes.c_uint32), ("n_bad_jobs", ctypes.c_uint32),
                 ("lit_bytes", ctypes.c_uint64), ("n_seq", ctypes.c_uint64), ("decoded_bytes", ctypes.c_uint64),
-                ("scratch_bytes", ctypes.c_uint64), ("plan_bytes", ctypes.c_uint64)]
+                ("scratch_bytes", ctypes.c_uint64), ("plan_bytes", ctypes.c_uint64),
+                ("n_segments", ctypes.c_uint32), ("n_direct_jobs", ctypes.c_uint32)]
 
 
 def frame_content_size(data) -> int | None:
