@@ -994,10 +994,10 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
 
 __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t* __restrict__ src,
                                                                 const uint8_t* img, uint8_t* scratch,
-                                                                uint8_t* out, uint32_t block0) {
+                                                                uint8_t* out, uint32_t bl0) {
   __shared__ K1Shared sh;
   const View v = make_view(img, scratch);
-  const uint32_t bi = block0 + blockIdx.x;
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
   const ZBlock b = v.blocks[bi];
   ZBlockRt* rt = v.rt + bi;
   if (b.type != 2) {
@@ -1055,7 +1055,7 @@ constexpr int kSeqScanThreads = 256;
 constexpr int kSeqPerThread = 4;
 
 __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch,
-                                                                 uint32_t block0) {
+                                                                 uint32_t bl0) {
   constexpr int kW = kSeqScanThreads / 32;
   __shared__ uint32_t s_k[kW][3], s_d[kW][3];
   __shared__ uint32_t s_ll[kW], s_ml[kW];
@@ -1063,9 +1063,10 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
   __shared__ uint32_t s_ck[kW + 1][3], s_cd[kW + 1][3];
   __shared__ uint32_t s_cl[kW + 1], s_cm[kW + 1];
   const View v = make_view(img, scratch);
-  const ZBlock b = v.blocks[block0 + blockIdx.x];
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
+  const ZBlock b = v.blocks[bi];
   if (b.type != 2 || b.nseq == 0) return;
-  ZBlockRt* rt = v.rt + block0 + blockIdx.x;
+  ZBlockRt* rt = v.rt + bi;
   if (rt->status) return;  // the block failed in K1; its job is reported bad
   ZSeq* seq = v.seq + b.seq_off;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, n = b.nseq;
@@ -1270,7 +1271,9 @@ __global__ void __launch_bounds__(32 * kJobScanWarps) zstd_job_scan(const uint8_
   if (jr >= n_jobs) return;
   const uint32_t j = job0 + jr;
   const ZJob job = v.jobs[j];
-  if (job.bad) return;
+  // direct jobs: sizes were checked by the planner, literal faults are
+  // reported by the literal decoders themselves
+  if (job.bad || job.direct) return;
   uint64_t z = job.zoff;
   uint32_t st = 0;
   for (uint32_t f = job.frame_first; f < job.frame_first + job.n_frames; f++) {
@@ -1362,13 +1365,13 @@ constexpr uint32_t kLongLit = 64;  // literal runs longer than this are copied b
 
 __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restrict__ src, const uint8_t* img,
                                                           uint8_t* scratch, uint8_t* __restrict__ out,
-                                                          uint32_t* status, uint32_t block0) {
+                                                          uint32_t* status, uint32_t bl0) {
   __shared__ uint32_t s_out[kExecChunk];
   __shared__ uint32_t s_first[kExecMaxChunks];
   __shared__ uint3 s_long[kExecChunk / (kLongLit + 1) + 1];  // (first, end, literal position) per long run
   __shared__ uint32_t s_nlong;
   const View v = make_view(img, scratch);
-  const uint32_t bi = block0 + blockIdx.x;
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
   const ZBlock b = v.blocks[bi];
   const ZJob& job = v.jobs[b.job];
   if (job.bad) return;
@@ -1848,12 +1851,12 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   for (const ZSegment& g : segs) {
     // resolve worklist counters (after the tile flags)
     if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
-    if (g.n_blocks) {
-      zstd_block_decode<<<g.n_blocks, kK1Threads, 0, s>>>(d_src, img, scr, d_out, g.block0);
-      zstd_seq_scan<<<g.n_blocks, kSeqScanThreads, 0, s>>>(img, scr, g.block0);
+    if (g.n_bl) {
+      zstd_block_decode<<<g.n_bl, kK1Threads, 0, s>>>(d_src, img, scr, d_out, g.bl0);
+      zstd_seq_scan<<<g.n_bl, kSeqScanThreads, 0, s>>>(img, scr, g.bl0);
       zstd_job_scan<<<(g.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(
           img, scr, d_status, g.job0, g.n_jobs);
-      zstd_block_execute<<<g.n_blocks, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.block0);
+      zstd_block_execute<<<g.n_bl, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.bl0);
     }
     if (g.n_tiles) {
       zstd_output<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, g.tile0);

@@ -11,6 +11,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <memory>
 #include <new>
 #include <atomic>
 #include <thread>
@@ -481,7 +482,7 @@ bool make_direct(JobPlan& jp, const voom_zstd_job& job) {
 // Table references of one job's compressed blocks, frame by frame: own
 // tables are appended, treeless / repeat blocks take the previous ones
 // (RFC 8878 3.1.1.3.1.1, 3.1.1.3.2.1.1).
-void resolve_job(JobPlan& jp, const std::vector<BlockTables>& tabs, const std::vector<uint8_t>& ok) {
+void resolve_job(JobPlan& jp, const BlockTables* tabs, const uint8_t* ok) {
   for (const ZFrame& fr : jp.frames) {
     uint32_t last_huf = kNone, last_fse[3] = {kNone, kNone, kNone};
     for (uint32_t i = fr.block_first; i < fr.block_first + fr.n_blocks; i++) {
@@ -517,19 +518,26 @@ void resolve_job(JobPlan& jp, const std::vector<BlockTables>& tabs, const std::v
   }
 }
 
+// Per-job counts (filled in parallel) and first indices in the plan arrays
+// (a serial prefix pass): the arrays are then filled in parallel, straight
+// into the image.
+struct JobSpan {
+  uint32_t nf, nb, nh, ns, nt, ndl, nbl;
+  uint64_t lit, nseq;
+};
+struct JobBase {
+  uint32_t f, b, h, s, t, dl, bl;
+  uint64_t lit, seq;
+};
+
 struct Plan {
   std::vector<ZSegment> segs;
-  std::vector<ZJob> jobs;
-  std::vector<ZFrame> frames;
-  std::vector<ZBlock> blocks;
-  std::vector<ZHuf> huf;
-  std::vector<ZFse> fse;
-  std::vector<ZOutTile> tiles;
-  std::vector<uint32_t> dlit;
   std::vector<uint32_t> status;
+  std::unique_ptr<uint8_t[]> image;  // header + arrays, ready to copy to the device
   ZPlanHeader hdr;
   uint64_t image_bytes = 0;
-  uint32_t n_bad = 0;
+  uint64_t decoded = 0;
+  uint32_t n_bad = 0, n_direct = 0;
 };
 
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
@@ -568,34 +576,176 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; return; }
     walk_job(h_src, jobs[j], jp[j]);
   });
-  // 2. every compressed block's sections, in parallel over all jobs
-  std::vector<std::pair<uint32_t, uint32_t>> todo;  // (job, block)
-  std::vector<std::vector<BlockTables>> tabs(n_jobs);
-  std::vector<std::vector<uint8_t>> okb(n_jobs);
-  for (uint32_t j = 0; j < n_jobs; j++) {
-    if (jp[j].bad) continue;
-    tabs[j].resize(jp[j].blocks.size());
-    okb[j].assign(jp[j].blocks.size(), 1);
-    for (uint32_t i = 0; i < jp[j].blocks.size(); i++)
-      if (jp[j].blocks[i].type == 2) todo.emplace_back(j, i);
-  }
-  parallel(todo.size(), [&](uint64_t t) {
-    const uint32_t j = todo[t].first, i = todo[t].second;
-    ZBlock& b = jp[j].blocks[i];
-    const uint64_t at = b.src;
-    const size_t bs = b.size;
-    b.src = 0;
-    b.size = 0;
-    okb[j][i] = plan_compressed(h_src, at, bs, b, tabs[j][i]) ? 1 : 0;
-  });
-  // 3. table references, frame by frame; direct jobs
+  // 2. per job: every compressed block's sections, table references, the
+  // direct check and the job's counts
+  std::vector<uint64_t> bstart(n_jobs + 1, 0);
+  for (uint32_t j = 0; j < n_jobs; j++) bstart[j + 1] = bstart[j] + (jp[j].bad ? 0 : jp[j].blocks.size());
+  std::unique_ptr<BlockTables[]> tabs(new BlockTables[std::max<uint64_t>(1, bstart[n_jobs])]);
+  std::unique_ptr<uint8_t[]> okb(new uint8_t[std::max<uint64_t>(1, bstart[n_jobs])]);
   std::vector<uint8_t> direct(n_jobs, 0);
+  std::vector<JobSpan> span(n_jobs);
   parallel(n_jobs, [&](uint64_t j) {
-    if (!jp[j].bad) resolve_job(jp[j], tabs[j], okb[j]);
-    direct[j] = make_direct(jp[j], jobs[j]) ? 1 : 0;
+    JobPlan& q = jp[j];
+    JobSpan& c = span[j];
+    memset(&c, 0, sizeof c);
+    if (q.bad) return;
+    BlockTables* T = tabs.get() + bstart[j];
+    uint8_t* ok = okb.get() + bstart[j];
+    for (size_t i = 0; i < q.blocks.size(); i++) {
+      ZBlock& b = q.blocks[i];
+      ok[i] = 1;
+      if (b.type != 2) continue;
+      const uint64_t at = b.src;
+      const size_t bs = b.size;
+      b.src = 0;
+      b.size = 0;
+      ok[i] = plan_compressed(h_src, at, bs, b, T[i]) ? 1 : 0;
+    }
+    resolve_job(q, T, ok);
+    direct[j] = make_direct(q, jobs[j]) ? 1 : 0;
+    if (q.bad) return;
+    c.nf = uint32_t(q.frames.size());
+    c.nb = uint32_t(q.blocks.size());
+    c.nh = uint32_t(q.huf.size());
+    c.ns = uint32_t(q.fse.size());
+    c.nt = direct[j] ? 0u : uint32_t((jobs[j].dst_len + kOutTile - 1) / kOutTile);
+    for (const ZBlock& b : q.blocks) {
+      if (b.type == 2 && direct[j] && b.lit_type == 2) c.ndl++;
+      else c.nbl++;
+      if (b.type == 2 && !direct[j]) {
+        c.lit += align_up(b.lit_regen, 16);
+        c.nseq += b.nseq;
+      }
+    }
   });
+  tabs.reset();
+  okb.reset();
 
-  // predefined sequence tables occupy fse[0..2]
+  // 3. serial prefix: Z-space offsets, segments, statuses, array bases
+  std::vector<JobBase> base(n_jobs);
+  std::vector<uint64_t> zoffs(n_jobs, 0);
+  std::vector<uint8_t> bad(n_jobs, 0);
+  JobBase run;
+  memset(&run, 0, sizeof run);
+  run.s = 3;  // predefined sequence tables occupy fse[0..2]
+  uint64_t zoff = 0, zmax = 0;
+  P->status.assign(n_jobs, 0);
+  ZSegment seg;
+  memset(&seg, 0, sizeof seg);
+  auto close_segment = [&](uint32_t j_end) {
+    seg.n_jobs = j_end - seg.job0;
+    seg.n_frames = run.f - seg.frame0;
+    seg.n_blocks = run.b - seg.block0;
+    seg.n_tiles = run.t - seg.tile0;
+    seg.n_bl = run.bl - seg.bl0;
+    seg.zbytes = zoff;
+    zmax = std::max(zmax, zoff);
+    if (seg.n_jobs) P->segs.push_back(seg);
+    seg.job0 = j_end;
+    seg.frame0 = run.f;
+    seg.block0 = run.b;
+    seg.tile0 = run.t;
+    seg.bl0 = run.bl;
+    zoff = 0;
+  };
+  for (uint32_t j = 0; j < n_jobs; j++) {
+    const bool qbad = jp[j].bad;
+    const uint64_t zneed = (qbad || direct[j]) ? 0 : align_up(jobs[j].dst_len, 16);
+    if (zneed > kZJobMax) {
+      bad[j] = 1;
+      zoffs[j] = zoff;
+      P->status[j] = VOOM_ZSTD_ST_TOO_LARGE;
+      P->n_bad++;
+      continue;
+    }
+    if (zneed && zoff + zneed > kZSeg && j > seg.job0) close_segment(j);
+    zoffs[j] = zoff;
+    zoff += zneed;
+    if (qbad) {
+      bad[j] = 1;
+      P->status[j] = VOOM_ZSTD_ST_FORMAT;
+      P->n_bad++;
+      continue;
+    }
+    base[j] = run;
+    const JobSpan& c = span[j];
+    run.f += c.nf;
+    run.b += c.nb;
+    run.h += c.nh;
+    run.s += c.ns;
+    run.t += c.nt;
+    run.dl += c.ndl;
+    run.bl += c.nbl;
+    run.lit += c.lit;
+    run.seq += c.nseq;
+    P->decoded += jobs[j].dst_len;
+    P->n_direct += direct[j];
+  }
+  close_segment(n_jobs);
+
+  // 4. image layout, then every job's entries written in parallel
+  ZPlanHeader& h = P->hdr;
+  memset(&h, 0, sizeof h);
+  h.n_jobs = n_jobs;
+  h.n_frames = run.f;
+  h.n_blocks = run.b;
+  h.n_huf = run.h;
+  h.n_fse = run.s;
+  h.n_tiles = run.t;
+  h.n_dlit = run.dl;
+  h.n_blist = run.bl;
+  uint64_t o = align_up(sizeof(ZPlanHeader), 256);
+  h.off_jobs = o; o = align_up(o + sizeof(ZJob) * uint64_t(n_jobs), 256);
+  h.off_frames = o; o = align_up(o + sizeof(ZFrame) * uint64_t(run.f), 256);
+  h.off_blocks = o; o = align_up(o + sizeof(ZBlock) * uint64_t(run.b), 256);
+  h.off_huf = o; o = align_up(o + sizeof(ZHuf) * uint64_t(run.h), 256);
+  h.off_fse = o; o = align_up(o + sizeof(ZFse) * uint64_t(run.s), 256);
+  h.off_tiles = o; o = align_up(o + sizeof(ZOutTile) * uint64_t(run.t), 256);
+  h.off_dlit = o; o = align_up(o + sizeof(uint32_t) * uint64_t(run.dl), 256);
+  h.off_blist = o; o = align_up(o + sizeof(uint32_t) * uint64_t(run.bl), 256);
+  P->image_bytes = o;
+  h.lit_bytes = run.lit;
+  h.n_seq = run.seq;
+  h.zbytes = zmax;  // the largest segment: the link-word scratch is reused by every segment
+  uint64_t s = 0;
+  h.s_res = s; s = align_up(s + 4 * zmax, 256);
+  h.s_lit = s; s = align_up(s + run.lit + 64, 256);
+  h.s_seq = s; s = align_up(s + sizeof(ZSeq) * run.seq, 256);
+  h.s_blk = s; s = align_up(s + sizeof(ZBlockRt) * uint64_t(run.b), 256);
+  h.s_ctr = s; s = align_up(s + 4 * uint64_t(run.t) + 256, 256);
+  // three worklists of Z positions still unresolved: list 0 from the output
+  // pass (kept for the patch pass), lists 1 and 2 alternating between the
+  // resolve passes
+  h.list_cap = std::max<uint64_t>(65536, zmax / 64);
+  h.s_list = s; s = align_up(s + 3 * 8 * h.list_cap, 256);
+  h.s_total = s;
+
+  P->image.reset(new (std::nothrow) uint8_t[P->image_bytes]);
+  if (!P->image) {
+    delete P;
+    return nullptr;
+  }
+  uint8_t* img = P->image.get();
+  // the alignment gaps between the arrays are zero
+  const uint64_t ends[9][2] = {{sizeof(ZPlanHeader), h.off_jobs},
+                               {h.off_jobs + sizeof(ZJob) * uint64_t(n_jobs), h.off_frames},
+                               {h.off_frames + sizeof(ZFrame) * uint64_t(run.f), h.off_blocks},
+                               {h.off_blocks + sizeof(ZBlock) * uint64_t(run.b), h.off_huf},
+                               {h.off_huf + sizeof(ZHuf) * uint64_t(run.h), h.off_fse},
+                               {h.off_fse + sizeof(ZFse) * uint64_t(run.s), h.off_tiles},
+                               {h.off_tiles + sizeof(ZOutTile) * uint64_t(run.t), h.off_dlit},
+                               {h.off_dlit + sizeof(uint32_t) * uint64_t(run.dl), h.off_blist},
+                               {h.off_blist + sizeof(uint32_t) * uint64_t(run.bl), P->image_bytes}};
+  for (const auto& g : ends) memset(img + g[0], 0, g[1] - g[0]);
+  memcpy(img, &h, sizeof h);
+  ZJob* J = reinterpret_cast<ZJob*>(img + h.off_jobs);
+  ZFrame* F = reinterpret_cast<ZFrame*>(img + h.off_frames);
+  ZBlock* B = reinterpret_cast<ZBlock*>(img + h.off_blocks);
+  ZHuf* H = reinterpret_cast<ZHuf*>(img + h.off_huf);
+  ZFse* S = reinterpret_cast<ZFse*>(img + h.off_fse);
+  ZOutTile* TL = reinterpret_cast<ZOutTile*>(img + h.off_tiles);
+  uint32_t* DL = reinterpret_cast<uint32_t*>(img + h.off_dlit);
+  uint32_t* BL = reinterpret_cast<uint32_t*>(img + h.off_blist);
   for (int k = 0; k < 3; k++) {
     ZFse f;
     memset(&f, 0, sizeof f);
@@ -604,27 +754,10 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     for (int i = 0; i < n; i++) f.norm[i] = d[i];
     f.nsym = uint16_t(n);
     f.al = uint8_t(k == 1 ? 5 : 6);
-    P->fse.push_back(f);
+    S[k] = f;
   }
-  uint64_t zoff = 0, zmax = 0, lit = 0, nseq = 0;
-  P->status.assign(n_jobs, 0);
-  ZSegment seg;
-  memset(&seg, 0, sizeof seg);
-  auto close_segment = [&](uint32_t j_end) {
-    seg.n_jobs = j_end - seg.job0;
-    seg.n_frames = uint32_t(P->frames.size()) - seg.frame0;
-    seg.n_blocks = uint32_t(P->blocks.size()) - seg.block0;
-    seg.n_tiles = uint32_t(P->tiles.size()) - seg.tile0;
-    seg.zbytes = zoff;
-    zmax = std::max(zmax, zoff);
-    if (seg.n_jobs) P->segs.push_back(seg);
-    seg.job0 = j_end;
-    seg.frame0 = uint32_t(P->frames.size());
-    seg.block0 = uint32_t(P->blocks.size());
-    seg.tile0 = uint32_t(P->tiles.size());
-    zoff = 0;
-  };
-  for (uint32_t j = 0; j < n_jobs; j++) {
+  parallel(n_jobs, [&](uint64_t jj) {
+    const uint32_t j = uint32_t(jj);
     ZJob zj;
     memset(&zj, 0, sizeof zj);
     zj.src = jobs[j].src;
@@ -633,99 +766,61 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     zj.dst_len = jobs[j].dst_len;
     zj.lo_src = jobs[j].lo_src;
     zj.flags = jobs[j].flags;
-    JobPlan& q = jp[j];
-    const uint64_t zneed = (q.bad || direct[j]) ? 0 : align_up(jobs[j].dst_len, 16);
-    if (zneed > kZJobMax) {
+    zj.zoff = zoffs[j];
+    if (bad[j]) {
       zj.bad = 1;
-      zj.zoff = zoff;
-      P->status[j] = VOOM_ZSTD_ST_TOO_LARGE;
-      P->n_bad++;
-      P->jobs.push_back(zj);
-      continue;
+      zj.direct = (P->status[j] == VOOM_ZSTD_ST_TOO_LARGE) ? 0u : direct[j];
+      J[j] = zj;
+      return;
     }
-    if (zneed && zoff + zneed > kZSeg && j > seg.job0) close_segment(j);
-    zj.zoff = zoff;
-    zoff += zneed;
     zj.direct = direct[j];
-    if (q.bad) {
-      zj.bad = 1;
-      P->status[j] = VOOM_ZSTD_ST_FORMAT;
-      P->n_bad++;
-      P->jobs.push_back(zj);
-      continue;
-    }
-    const uint32_t fbase = uint32_t(P->frames.size()), bbase = uint32_t(P->blocks.size());
-    const uint32_t hbase = uint32_t(P->huf.size()), sbase = uint32_t(P->fse.size());
-    zj.frame_first = fbase;
+    const JobPlan& q = jp[j];
+    const JobBase& bs = base[j];
+    zj.frame_first = bs.f;
     zj.n_frames = uint32_t(q.frames.size());
-    for (auto f : q.frames) {
-      f.block_first += bbase;
+    for (size_t k = 0; k < q.frames.size(); k++) {
+      ZFrame f = q.frames[k];
+      f.block_first += bs.b;
       f.job = j;
-      P->frames.push_back(f);
+      F[bs.f + k] = f;
     }
-    for (auto b : q.blocks) {
-      b.frame += fbase;
+    uint64_t lit = bs.lit, nseq = bs.seq;
+    uint32_t ndl = 0, nbl = 0;
+    for (size_t i = 0; i < q.blocks.size(); i++) {
+      ZBlock b = q.blocks[i];
+      b.frame += bs.f;
       b.job = j;
-      if (b.huf != kNone) b.huf += hbase;
+      if (b.huf != kNone) b.huf += bs.h;
       for (int k = 0; k < 3; k++) {
         if (b.fse[k] == kNone) continue;
-        b.fse[k] = (b.fse[k] & kPredef) ? (b.fse[k] & 3u) : b.fse[k] + sbase;
+        b.fse[k] = (b.fse[k] & kPredef) ? (b.fse[k] & 3u) : b.fse[k] + bs.s;
       }
       b.lit_off = lit;
       b.seq_off = nseq;
-      if (b.type == 2 && zj.direct && b.lit_type == 2) P->dlit.push_back(uint32_t(P->blocks.size()));
+      const uint32_t gi = bs.b + uint32_t(i);
+      if (b.type == 2 && zj.direct && b.lit_type == 2)
+        DL[bs.dl + ndl++] = gi;
+      else
+        BL[bs.bl + nbl++] = gi;
       if (b.type == 2 && !zj.direct) {
         lit += align_up(b.lit_regen, 16);
         nseq += b.nseq;
       }
-      P->blocks.push_back(b);
+      B[gi] = b;
     }
-    P->huf.insert(P->huf.end(), q.huf.begin(), q.huf.end());
-    P->fse.insert(P->fse.end(), q.fse.begin(), q.fse.end());
-    for (uint64_t s = 0; !zj.direct && s < jobs[j].dst_len; s += kOutTile) {
+    for (size_t k = 0; k < q.huf.size(); k++) H[bs.h + k] = q.huf[k];
+    for (size_t k = 0; k < q.fse.size(); k++) S[bs.s + k] = q.fse[k];
+    uint32_t nt = 0;
+    for (uint64_t s0 = 0; !zj.direct && s0 < jobs[j].dst_len; s0 += kOutTile) {
       ZOutTile t;
       memset(&t, 0, sizeof t);
       t.job = j;
-      t.begin = s;
-      t.len = std::min<uint64_t>(kOutTile, jobs[j].dst_len - s);
-      P->tiles.push_back(t);
+      t.begin = s0;
+      t.len = std::min<uint64_t>(kOutTile, jobs[j].dst_len - s0);
+      TL[bs.t + nt++] = t;
     }
-    P->jobs.push_back(zj);
-  }
-  close_segment(n_jobs);
-  ZPlanHeader& h = P->hdr;
-  memset(&h, 0, sizeof h);
-  h.n_jobs = n_jobs;
-  h.n_frames = uint32_t(P->frames.size());
-  h.n_blocks = uint32_t(P->blocks.size());
-  h.n_huf = uint32_t(P->huf.size());
-  h.n_fse = uint32_t(P->fse.size());
-  h.n_tiles = uint32_t(P->tiles.size());
-  uint64_t o = align_up(sizeof(ZPlanHeader), 256);
-  h.off_jobs = o; o = align_up(o + sizeof(ZJob) * P->jobs.size(), 256);
-  h.off_frames = o; o = align_up(o + sizeof(ZFrame) * P->frames.size(), 256);
-  h.off_blocks = o; o = align_up(o + sizeof(ZBlock) * P->blocks.size(), 256);
-  h.off_huf = o; o = align_up(o + sizeof(ZHuf) * P->huf.size(), 256);
-  h.off_fse = o; o = align_up(o + sizeof(ZFse) * P->fse.size(), 256);
-  h.off_tiles = o; o = align_up(o + sizeof(ZOutTile) * P->tiles.size(), 256);
-  h.n_dlit = uint32_t(P->dlit.size());
-  h.off_dlit = o; o = align_up(o + sizeof(uint32_t) * P->dlit.size(), 256);
-  P->image_bytes = o;
-  h.lit_bytes = lit;
-  h.n_seq = nseq;
-  h.zbytes = zmax;  // the largest segment: the link-word scratch is reused by every segment
-  uint64_t s = 0;
-  h.s_res = s; s = align_up(s + 4 * zmax, 256);
-  h.s_lit = s; s = align_up(s + lit + 64, 256);
-  h.s_seq = s; s = align_up(s + sizeof(ZSeq) * nseq, 256);
-  h.s_blk = s; s = align_up(s + sizeof(ZBlockRt) * P->blocks.size(), 256);
-  h.s_ctr = s; s = align_up(s + 4 * P->tiles.size() + 256, 256);
-  // three worklists of Z positions still unresolved: list 0 from the output
-  // pass (kept for the patch pass), lists 1 and 2 alternating between the
-  // resolve passes
-  h.list_cap = std::max<uint64_t>(65536, zmax / 64);
-  h.s_list = s; s = align_up(s + 3 * 8 * h.list_cap, 256);
-  h.s_total = s;
+    J[j] = zj;
+  });
   return P;
 }
 
@@ -741,16 +836,11 @@ VOOM_API int voom_zstd_plan_info_get(const void* plan, voom_zstd_plan_info* info
   info->n_bad_jobs = P->n_bad;
   info->lit_bytes = P->hdr.lit_bytes;
   info->n_seq = P->hdr.n_seq;
-  uint64_t decoded = 0;
-  for (size_t j = 0; j < P->jobs.size(); j++)
-    if (!P->jobs[j].bad) decoded += P->jobs[j].dst_len;
-  info->decoded_bytes = decoded;
+  info->decoded_bytes = P->decoded;
   info->scratch_bytes = P->hdr.s_total;
   info->plan_bytes = P->image_bytes;
   info->n_segments = uint32_t(P->segs.size());
-  uint32_t nd = 0;
-  for (const ZJob& j : P->jobs) nd += (j.direct && !j.bad) ? 1u : 0u;
-  info->n_direct_jobs = nd;
+  info->n_direct_jobs = P->n_direct;
   return VOOM_OK;
 }
 
@@ -758,17 +848,7 @@ VOOM_API int voom_zstd_plan_image(const void* plan, void* h_image, uint64_t cap)
   if (!plan || !h_image) return VOOM_E_INVALID_ARG;
   const Plan* P = static_cast<const Plan*>(plan);
   if (cap < P->image_bytes) return VOOM_E_CAPACITY;
-  uint8_t* img = static_cast<uint8_t*>(h_image);
-  memset(img, 0, P->image_bytes);
-  const ZPlanHeader& h = P->hdr;
-  memcpy(img, &h, sizeof h);
-  if (!P->jobs.empty()) memcpy(img + h.off_jobs, P->jobs.data(), sizeof(ZJob) * P->jobs.size());
-  if (!P->frames.empty()) memcpy(img + h.off_frames, P->frames.data(), sizeof(ZFrame) * P->frames.size());
-  if (!P->blocks.empty()) memcpy(img + h.off_blocks, P->blocks.data(), sizeof(ZBlock) * P->blocks.size());
-  if (!P->huf.empty()) memcpy(img + h.off_huf, P->huf.data(), sizeof(ZHuf) * P->huf.size());
-  if (!P->fse.empty()) memcpy(img + h.off_fse, P->fse.data(), sizeof(ZFse) * P->fse.size());
-  if (!P->tiles.empty()) memcpy(img + h.off_tiles, P->tiles.data(), sizeof(ZOutTile) * P->tiles.size());
-  if (!P->dlit.empty()) memcpy(img + h.off_dlit, P->dlit.data(), sizeof(uint32_t) * P->dlit.size());
+  memcpy(h_image, P->image.get(), P->image_bytes);
   return VOOM_OK;
 }
 

@@ -86,6 +86,7 @@ constexpr uint64_t kZJobMax = (1ull << 31) - (1ull << 20);
 // Contiguous job / frame / block / tile ranges of one segment (host only).
 struct ZSegment {
   uint32_t job0, n_jobs, frame0, n_frames, block0, n_blocks, tile0, n_tiles;
+  uint32_t bl0, n_bl;  // range of the block list (the blocks zstd_block_decode etc. run on)
   uint64_t zbytes;
 };
 
@@ -97,6 +98,10 @@ struct ZPlanHeader {
   // streams are decoded one lane each by zstd_direct_literals
   uint32_t n_dlit, pad_dlit;
   uint64_t off_dlit;
+  // every other block (global indices, job order): the block decode, sequence
+  // scan and block execute kernels run on this list, segment by segment
+  uint32_t n_blist, pad_blist;
+  uint64_t off_blist;
   uint64_t lit_bytes, n_seq, zbytes;
   // scratch layout (byte offsets into d_scratch)
   uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_list, s_total;

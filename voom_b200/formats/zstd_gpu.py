@@ -104,7 +104,7 @@ class ZstdPlan:
             raise VoomError("voom_zstd_plan_create failed")
         self.info = PlanInfo()
         check(self._lib.voom_zstd_plan_info_get(self.handle, ctypes.byref(self.info)), "voom_zstd_plan_info_get")
-        self.image = np.zeros(max(self.info.plan_bytes, 1), dtype=np.uint8)
+        self.image = np.empty(max(self.info.plan_bytes, 1), dtype=np.uint8)  # every byte is written below
         check(self._lib.voom_zstd_plan_image(self.handle, self.image.ctypes.data, self.image.size),
               "voom_zstd_plan_image")
         self.plan_status = np.zeros(max(self.jobs.size, 1), dtype=np.uint32)
