@@ -900,6 +900,38 @@ DEFAULT_WORKLOAD = "c2_vpack"
 
 
 # ------------------------------------------------------------------- main
+ZSTD_KERNELS = {1: "zstd_direct_literals", 2: "zstd_block_decode", 3: "zstd_seq_scan", 4: "zstd_job_scan",
+                5: "zstd_block_execute", 6: "zstd_output", 7: "zstd_resolve (all passes)", 8: "zstd_patch",
+                9: "zstd_checksum"}
+
+
+def zstd_kernel_times(w, steps: int, flush, stream) -> dict | None:
+    """Mean ms per step of every zstd kernel (CUDA events recorded by the
+    library after each launch, voom_zstd_set_timing), outside the timed loop."""
+    import ctypes
+
+    import torch
+    from voom_b200._lib import load
+
+    if not hasattr(w, "batch"):
+        return None
+    lib = load()
+    lib.voom_zstd_set_timing(1)
+    ms = np.zeros(512, np.float32)
+    ids = np.zeros(512, np.uint32)
+    tot: dict = {}
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        w.step_device(int(stream.cuda_stream))
+        n = lib.voom_zstd_kernel_times(ms.ctypes.data_as(ctypes.c_void_p), ids.ctypes.data_as(ctypes.c_void_p), 512)
+        for k in range(max(n, 0)):
+            name = ZSTD_KERNELS.get(int(ids[k]), str(int(ids[k])))
+            tot[name] = tot.get(name, 0.0) + float(ms[k])
+    torch.cuda.synchronize()
+    lib.voom_zstd_set_timing(0)
+    return {k: round(v / steps, 4) for k, v in tot.items()}
+
+
 def dist_init():
     import torch
     import torch.distributed as dist
@@ -963,6 +995,9 @@ def main():
     ap.add_argument("--tokens", type=int, default=1, help="c3_moe: tokens per step (1 or 8)")
     ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
     ap.add_argument("--kv-pages", type=int, default=65536, help="c6_kv_paged: KV pages (65536 = config 5)")
+    ap.add_argument("--kernel-times", action="store_true",
+                    help="zstd workloads: after the timed steps, time `--steps` more steps with a CUDA event after "
+                         "every kernel launch and report the mean ms per kernel per step ('kernel_ms')")
     ap.add_argument("--device-only", action="store_true",
                     help="parity check, warm-up and timed device steps only: no end-to-end leg, CPU baseline or "
                          "clock sampler (the run the ncu captures in profiles/ use); prints no bench line")
@@ -1021,10 +1056,14 @@ def main():
     clocks = sampler.stop() if sampler else None
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms = sum(step_ms) / len(step_ms)
+    kernel_ms = zstd_kernel_times(w, args.steps, flush, stream) if args.kernel_times else None
     if args.device_only:
         if rank == 0:
-            print(json.dumps({"device_only": True, "workload": w.config()["workload"], "steps": args.steps,
-                              "ms_per_step": round(ms, 5)}), flush=True)
+            line = {"device_only": True, "workload": w.config()["workload"], "steps": args.steps,
+                    "ms_per_step": round(ms, 5)}
+            if kernel_ms is not None:
+                line["kernel_ms"] = kernel_ms
+            print(json.dumps(line), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -1085,6 +1124,7 @@ def main():
                     "d2h_bytes_per_step": bo},
             "gpu_launches": args.steps * getattr(w, "launches_per_step", 1), "clocks": clocks,
             "step_ms_min": round(min(step_ms), 5), "step_ms_max": round(max(step_ms), 5),
+            **({"kernel_ms": kernel_ms} if kernel_ms is not None else {}),
             **extra,
         }
         print(json.dumps(line), flush=True)

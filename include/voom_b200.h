@@ -250,6 +250,21 @@ void voom_zstd_plan_destroy(void* plan);
 int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                      uint8_t* d_out, uint32_t* d_status, void* stream);
 
+/* Per-kernel timing of voom_zstd_decode (diagnostics; no counterpart in the
+ * reference).  voom_zstd_set_timing(1) makes every later voom_zstd_decode
+ * record a CUDA event after each of its launches (on the device current when
+ * timing was switched on); voom_zstd_kernel_times(ms, ids, cap) waits for the
+ * last decode and returns how many (interval ms, kernel id) pairs it wrote, in
+ * launch order.  Kernel ids: */
+enum {
+  VOOM_ZSTD_K_DIRECT_LITERALS = 1, VOOM_ZSTD_K_BLOCK_DECODE = 2, VOOM_ZSTD_K_SEQ_SCAN = 3,
+  VOOM_ZSTD_K_JOB_SCAN = 4, VOOM_ZSTD_K_BLOCK_EXECUTE = 5, VOOM_ZSTD_K_OUTPUT = 6,
+  VOOM_ZSTD_K_RESOLVE = 7, /* all resolve passes of one segment */
+  VOOM_ZSTD_K_PATCH = 8, VOOM_ZSTD_K_CHECKSUM = 9
+};
+int voom_zstd_set_timing(int on);
+int voom_zstd_kernel_times(float* ms, uint32_t* ids, int cap);
+
 /* ------------------------------------------------- KV spill pages (.kvz) */
 /* One compressed KV page as runtime/kv_paged.py:86-88 writes it: the pickle
  * of {"shape": tuple, "k": zstd(K bits, 1), "v": zstd(V bits, 1)}. */

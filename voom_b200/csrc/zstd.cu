@@ -1827,6 +1827,47 @@ bool plan_counts(const void* plan, ZPlanHeader* out, std::vector<ZSegment>* segs
 }
 }  // namespace voom
 
+// Optional per-kernel timing of voom_zstd_decode (diagnostics): when on, an
+// event is recorded on the launch stream after every launch, with the id of
+// the kernel it closes; voom_zstd_kernel_times returns the intervals of the
+// last decode.  Events belong to the device current when timing was enabled.
+namespace {
+constexpr int kMaxTimed = 96;
+bool g_time_on = false;
+cudaEvent_t g_tev[kMaxTimed + 1];
+uint32_t g_tid[kMaxTimed];
+int g_ntev = 0;
+void tmark(cudaStream_t s, uint32_t id) {
+  if (!g_time_on || g_ntev > kMaxTimed) return;
+  if (g_ntev > 0) g_tid[g_ntev - 1] = id;
+  cudaEventRecord(g_tev[g_ntev++], s);
+}
+}  // namespace
+
+VOOM_API int voom_zstd_set_timing(int on) {
+  if (on && !g_time_on) {
+    for (int i = 0; i <= kMaxTimed; i++)
+      if (cudaEventCreate(&g_tev[i]) != cudaSuccess) return VOOM_E_CUDA;
+  } else if (!on && g_time_on) {
+    cudaDeviceSynchronize();
+    for (int i = 0; i <= kMaxTimed; i++) cudaEventDestroy(g_tev[i]);
+  }
+  g_time_on = on != 0;
+  g_ntev = 0;
+  return VOOM_OK;
+}
+
+VOOM_API int voom_zstd_kernel_times(float* ms, uint32_t* ids, int cap) {
+  if (!g_time_on || g_ntev < 2) return 0;
+  if (cudaEventSynchronize(g_tev[g_ntev - 1]) != cudaSuccess) return VOOM_E_CUDA;
+  int n = 0;
+  for (int i = 1; i < g_ntev && n < cap; i++, n++) {
+    if (cudaEventElapsedTime(&ms[n], g_tev[i - 1], g_tev[i]) != cudaSuccess) return VOOM_E_CUDA;
+    ids[n] = g_tid[i - 1];
+  }
+  return n;
+}
+
 VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                               uint8_t* d_out, uint32_t* d_status, void* stream) {
   if (!d_src || !d_plan || !h_plan || !d_scratch || !d_out || !d_status) return VOOM_E_INVALID_ARG;
@@ -1843,9 +1884,13 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
                          cudaSharedmemCarveoutMaxShared);
     attrs_set = true;
   }
-  if (h.n_dlit)
+  g_ntev = 0;
+  tmark(s, 0);
+  if (h.n_dlit) {
     zstd_direct_literals<<<(h.n_dlit + kDlBlocksPerWarp - 1) / kDlBlocksPerWarp, 32, 0, s>>>(d_src, img, scr,
                                                                                             d_out, d_status);
+    tmark(s, VOOM_ZSTD_K_DIRECT_LITERALS);
+  }
   // One pass of the pipeline per Z-space segment; the link-word scratch and
   // the resolve worklists are reused, everything else is indexed globally.
   for (const ZSegment& g : segs) {
@@ -1853,17 +1898,27 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
     if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
     if (g.n_bl) {
       zstd_block_decode<<<g.n_bl, kK1Threads, 0, s>>>(d_src, img, scr, d_out, g.bl0);
+      tmark(s, VOOM_ZSTD_K_BLOCK_DECODE);
       zstd_seq_scan<<<g.n_bl, kSeqScanThreads, 0, s>>>(img, scr, g.bl0);
+      tmark(s, VOOM_ZSTD_K_SEQ_SCAN);
       zstd_job_scan<<<(g.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(
           img, scr, d_status, g.job0, g.n_jobs);
+      tmark(s, VOOM_ZSTD_K_JOB_SCAN);
       zstd_block_execute<<<g.n_bl, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.bl0);
+      tmark(s, VOOM_ZSTD_K_BLOCK_EXECUTE);
     }
     if (g.n_tiles) {
       zstd_output<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, g.tile0);
+      tmark(s, VOOM_ZSTD_K_OUTPUT);
       for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<g.n_tiles, 256, 0, s>>>(img, scr, p, g.tile0);
+      tmark(s, VOOM_ZSTD_K_RESOLVE);
       zstd_patch<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.tile0);
+      tmark(s, VOOM_ZSTD_K_PATCH);
     }
   }
-  if (h.n_frames) zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_out, d_status);
+  if (h.n_frames) {
+    zstd_checksum<<<(h.n_frames + 63) / 64, 64, 0, s>>>(img, scr, d_out, d_status);
+    tmark(s, VOOM_ZSTD_K_CHECKSUM);
+  }
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
