@@ -236,9 +236,12 @@ struct RingWin {
     const int32_t target = (nidx >> 3) - 3;
     while (nextq >= target && nextq >= 0) fetch(nextq--);
   }
-  __device__ __forceinline__ void consume(uint32_t n) {
-    hi = __funnelshift_l(lo, hi, n);
-    lo <<= n;
+  // e = a table entry whose low 5 bits are the code length (1..11): the
+  // funnel shifts use the amount modulo 32 and the counters mask it
+  __device__ __forceinline__ void consume_entry(uint32_t e) {
+    hi = __funnelshift_l(lo, hi, e);
+    lo = __funnelshift_l(0u, lo, e);
+    const uint32_t n = e & 31u;
     vb -= n;
     P -= int32_t(n);
   }
@@ -632,15 +635,28 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
   // canonical (weight ascending, then symbol order), so every weight's first
   // position is the sum over lighter weights and a lane's offset within a
   // weight is the count of that weight in the lanes before it
+  // this lane's 64 weights as 16 independent 4-byte loads (ZHuf rows are
+  // 4-byte aligned); weights past nsym read as 0
+  const uint32_t s0 = 64 * q, s1 = min(nsym, s0 + 64);
+  uint32_t wv[16];
+#pragma unroll
+  for (int k = 0; k < 16; k++) {
+    const uint32_t sy = s0 + 4u * uint32_t(k);
+    uint32_t x = sy < s1 ? __ldg(reinterpret_cast<const uint32_t*>(H->w + sy)) : 0u;
+    if (sy + 4 > s1 && sy < s1) x &= 0xFFFFFFFFu >> (8 * (sy + 4 - s1));
+    wv[k] = x;
+  }
   uint32_t cnt[12];
 #pragma unroll
   for (int k = 0; k < 12; k++) cnt[k] = 0;
-  const uint32_t s0 = 64 * q, s1 = min(nsym, s0 + 64);
-  for (uint32_t sy = s0; sy < s1; sy++) {
-    const uint32_t w = H->w[sy];
 #pragma unroll
-    for (int k = 1; k < 12; k++) cnt[k] += (w == uint32_t(k));
-  }
+  for (int k = 0; k < 16; k++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const uint32_t w = (wv[k] >> (8 * c)) & 0xFFu;
+#pragma unroll
+      for (int t = 1; t < 12; t++) cnt[t] += (w == uint32_t(t));
+    }
   uint32_t pos[12];
   uint32_t start = 0;
 #pragma unroll
@@ -656,21 +672,27 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
   }
   // a complete code fills the table exactly (the same for the group's lanes)
   bool ok = start == (1u << maxbits);
+  // entry = code length | symbol << 8: the funnel shift that consumes a code
+  // takes its amount from the low 5 bits, so no extraction sits in the chain
   uint16_t* tab = s_tab[g];
-  for (uint32_t sy = s0; sy < s1 && ok; sy++) {
-    const uint32_t w = H->w[sy];
-    if (!w) continue;
-    uint32_t p = 0;
+  if (ok) {
 #pragma unroll
-    for (int k = 1; k < 12; k++)
-      if (w == uint32_t(k)) {
-        p = pos[k];
-        pos[k] += 1u << (k - 1);
+    for (int k4 = 0; k4 < 64; k4++) {  // unrolled: wv stays in registers
+      const uint32_t w = (wv[k4 >> 2] >> (8 * (k4 & 3))) & 0xFFu;
+      if (w) {
+        uint32_t p = 0;
+#pragma unroll
+        for (int k = 1; k < 12; k++)
+          if (w == uint32_t(k)) {
+            p = pos[k];
+            pos[k] += 1u << (k - 1);
+          }
+        const uint16_t e = uint16_t((maxbits + 1 - w) | ((s0 + uint32_t(k4)) << 8));
+        const uint32_t len = 1u << (w - 1);
+        for (uint32_t i = 0; i < len; i++)
+          if (p + i < kHufTab) tab[p + i] = e;
       }
-    const uint16_t e = uint16_t(sy | ((maxbits + 1 - w) << 8));
-    const uint32_t len = 1u << (w - 1);
-    for (uint32_t i = 0; i < len; i++)
-      if (p + i < kHufTab) tab[p + i] = e;
+    }
   }
   __syncwarp();
   // From here every lane stays to the end: the rounds below are warp-uniform.
@@ -707,8 +729,8 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
   auto one = [&]() -> uint32_t {
     W.refill();
     const uint32_t e = tab[W.hi >> shift];
-    W.consume(e >> 8);
-    return e;
+    W.consume_entry(e);
+    return e >> 8;
   };
   // head: single symbols up to a 4-byte boundary of the output (within the
   // ring's initial four quarters: at most 3 refills)
@@ -728,15 +750,16 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
       if (live) {
         W.refill();
         const uint32_t e0 = tab[W.hi >> shift];
-        W.consume(e0 >> 8);
+        W.consume_entry(e0);
         const uint32_t e1 = tab[W.hi >> shift];
-        W.consume(e1 >> 8);
+        W.consume_entry(e1);
         W.refill();
         const uint32_t e2 = tab[W.hi >> shift];
-        W.consume(e2 >> 8);
+        W.consume_entry(e2);
         const uint32_t e3 = tab[W.hi >> shift];
-        W.consume(e3 >> 8);
-        *d32++ = __byte_perm(__byte_perm(e0, e1, 0x0040), __byte_perm(e2, e3, 0x0040), 0x5410);
+        W.consume_entry(e3);
+        // symbols are byte 1 of each entry
+        *d32++ = __byte_perm(__byte_perm(e0, e1, 0x0051), __byte_perm(e2, e3, 0x0051), 0x5410);
         n += 4;
         live = n + 4 <= count && W.P >= -32;
       }
@@ -1878,12 +1901,6 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* img = static_cast<const uint8_t*>(d_plan);
   uint8_t* scr = static_cast<uint8_t*>(d_scratch);
-  static bool attrs_set = false;  // per process: ask for the largest shared-memory carveout
-  if (!attrs_set) {
-    cudaFuncSetAttribute(zstd_direct_literals, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attrs_set = true;
-  }
   g_ntev = 0;
   tmark(s, 0);
   if (h.n_dlit) {
