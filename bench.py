@@ -186,9 +186,40 @@ class C1Rans:
             b.record(stream)
         torch.cuda.synchronize()
         ms = sum(a.elapsed_time(b) for a, b in ev) / steps
-        return {"indexed_decode": {"value": round(len(self.raw) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
-                                   "ms_per_step": round(ms, 5), "bit_exact": ok, "ckpt_every": 256,
-                                   "index_bytes": int(page.ckpt.numel() * 4)}}
+        res = {"indexed_decode": {"value": round(len(self.raw) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                                  "ms_per_step": round(ms, 5), "bit_exact": ok, "ckpt_every": 256,
+                                  "index_bytes": int(page.ckpt.numel() * 4)}}
+        # the same tensor framed with smaller tiles (more independent streams), cold decode
+        from voom_b200 import _device
+        from voom_b200._lib import check, load
+
+        for tb, label in ((1 << 16, "tile_64KiB"), (1 << 14, "tile_16KiB")):
+            frame, _ = self.R.encode(self.raw, tile_bytes=tb)
+            plan = self.R.plan(frame)
+            src = _device.upload(frame, self.dev)
+            tiles = _device.tensor_from_numpy(plan.tiles, self.dev)
+            nt = int(plan.info.n_tiles)
+            st = torch.zeros(nt, dtype=torch.int32, device=self.dev)
+
+            def run():
+                check(load().voom_rans_decode(src.data_ptr(), tiles.data_ptr(), nt, out.data_ptr(), st.data_ptr(),
+                                              None, None, 0, int(stream.cuda_stream)), "voom_rans_decode")
+
+            run()
+            torch.cuda.synchronize()
+            ok = bool((st.cpu().numpy() == 0).all()) and out.cpu().numpy().tobytes() == self.raw
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            for a, b in ev:
+                flush.fill_(4)
+                a.record(stream)
+                run()
+                b.record(stream)
+            torch.cuda.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+            res[label] = {"value": round(len(self.raw) / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                          "ms_per_step": round(ms, 5), "bit_exact": ok, "tiles": nt,
+                          "frame_bytes": len(frame), "ratio": round(len(self.raw) / len(frame), 4)}
+        return res
 
     def step_e2e(self):
         out = self.R.decode_device(self.pinned_frame, device=self.dev)
@@ -817,7 +848,10 @@ class C6KvPaged:
             s = torch.rand((n, 2, 1, H, 1, 1), generator=g, device=device) * 3.5 + 0.5
             self.raw[a:a + n] = (x * s).to(torch.bfloat16)
         host = self.raw.view(torch.int16).cpu().numpy().view(np.uint16)
-        self.blobs = kv_paged.spill_pages_compressed(host[:, 0], host[:, 1], threads=os.cpu_count() or 8)
+        self.spill_threads = os.cpu_count() or 8
+        t0 = time.perf_counter()
+        self.blobs = kv_paged.spill_pages_compressed(host[:, 0], host[:, 1], threads=self.spill_threads)
+        self.spill_s = time.perf_counter() - t0
         del host
         self.page_bytes = 2 * H * P * D
         frames = []
@@ -848,6 +882,14 @@ class C6KvPaged:
         if self.batch.job_status().any():
             return False
         return bool(self.torch.equal(self.out, self.raw.view(-1).view(self.torch.uint8)))
+
+    def extra(self, stream, steps: int, flush) -> dict:
+        """The spill leg of the same pages, timed once at set-up: host libzstd
+        level 1 (the reference's own codec call, so the .kvz bytes are
+        identical) on a thread pool, raw K/V bytes per second."""
+        return {"spill": {"value": round(self.raw_bytes / self.spill_s / 1e9, 3), "unit": "GB/s",
+                          "seconds": round(self.spill_s, 3), "threads": self.spill_threads,
+                          "how": "kv_paged.spill_pages_compressed: zstd level 1 of K and V + pickle per page"}}
 
     def step_e2e(self):
         """Public API: kv_paged.reload_blobs over the host-resident .kvz pages
