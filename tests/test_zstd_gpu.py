@@ -199,3 +199,34 @@ def oz_reject(frame: bytes, n: int) -> bool:
     except oz.ZstdError:
         return True
     return False
+
+
+def test_direct_literals_short_codes(Z):
+    """Literal-only frames whose Huffman codes are shorter than 11 bits (small,
+    skewed alphabets) next to 11-bit ones (KV bytes), decoded in one batch."""
+    from voom_b200 import _device, synthetic
+    from voom_b200.formats import zstd_host as zh
+
+    rng = np.random.default_rng(21)
+    raws = []
+    for alpha, n in ((3, 5000), (12, 20000), (40, 30000), (90, 7777), (200, 32768)):
+        p = rng.dirichlet(np.ones(alpha) * 0.7)
+        raws.append(rng.choice(alpha, size=n, p=p).astype(np.uint8).tobytes())
+    k, _ = synthetic.kv_pages(2, seed=9)
+    raws += [k[0].tobytes(), k[1].tobytes()[:20001]]
+    frames = [zh.compress(r, 1) for r in raws]
+    jobs = np.zeros(len(raws), dtype=Z.JOB_DTYPE)
+    off = dst = 0
+    for i, (f, r) in enumerate(zip(frames, raws)):
+        jobs[i] = (off, len(f), dst, len(r), 0, 0, 0)
+        off += len(f)
+        dst += len(r)
+    src = b"".join(frames)
+    plan = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs)
+    assert plan.info.n_direct_jobs >= 3
+    dev = torch.device("cuda", 0)
+    out = torch.empty(dst, dtype=torch.uint8, device=dev)
+    batch = Z.ZstdBatch(plan, dev)
+    batch.run(_device.upload(np.frombuffer(src, np.uint8), dev), out)
+    assert not batch.job_status().any()
+    assert out.cpu().numpy().tobytes() == b"".join(raws)
