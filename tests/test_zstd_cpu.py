@@ -128,3 +128,23 @@ def test_planner_direct_jobs_and_segments(built_lib):
 
     only_direct = Z.ZstdPlan(np.frombuffer(src, np.uint8), jobs[:8])
     assert only_direct.info.n_direct_jobs == 8 and only_direct.info.scratch_bytes < (2 << 20)  # worklists only
+
+
+def test_cabi_example_frames(built_lib, tmp_path):
+    """The C-ABI example's frame files: jobs cover the source back to back,
+    the planner takes them as direct jobs, and libzstd decodes each frame to
+    its slice of raw.bin."""
+    from voom_b200.cabi_example import make_kv_frames
+    from voom_b200.formats import zstd_gpu as Z
+
+    make_kv_frames.main(str(tmp_path), 6)
+    src = np.fromfile(tmp_path / "src.bin", np.uint8)
+    jobs = np.fromfile(tmp_path / "jobs.bin", Z.JOB_DTYPE)
+    raw = np.fromfile(tmp_path / "raw.bin", np.uint8)
+    assert jobs.size == 12 and int(jobs["src"][-1] + jobs["src_len"][-1]) == src.size
+    assert int(jobs["dst"][-1] + jobs["dst_len"][-1]) == raw.size
+    for j in jobs:
+        fr = src[int(j["src"]):int(j["src"] + j["src_len"])].tobytes()
+        assert oz.libzstd_decompress(fr, int(j["dst_len"])) == raw[int(j["dst"]):int(j["dst"] + j["dst_len"])].tobytes()
+    plan = Z.ZstdPlan(src, jobs)
+    assert plan.info.n_direct_jobs + plan.info.n_bad_jobs <= 12 and not plan.plan_status.any()
