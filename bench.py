@@ -1,7 +1,12 @@
 """Benchmark of the voom_b200 weight-page decode path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1_rans]
+                    [--workload c1_rans|c2_vpack|c3_moe|c4_moe_ep|c5_nf12|c6_kv_paged]
+                    [--tokens T] [--kernel-times] [--device-only]
+
+Workloads: c1_rans (config 1), c2_vpack (config 2, the
+default), c3_moe (config 3), c4_moe_ep (config 4, expert parallel), c6_kv_paged
+(config 5, 65,536 KV pages), c5_nf12 (the NF12 sidecar, a next row).
 
 A step is one pass of the hot path over one batch of synthetic input with
 the shape of a BASELINE config (see `--workload`).  `value` is device
