@@ -196,7 +196,7 @@ struct RingWin {
   uint32_t hi, lo, vb;
   uint32_t q0, q1;
   int32_t nidx;
-  int32_t P;
+  int32_t pc;     // unread stream bits = vb + pc + 32 * nidx (kept out of the per-symbol chain)
   int32_t nextq;  // next quarter to issue
 
   __device__ __forceinline__ uint32_t word(int32_t i) const { return i < 0 ? 0u : ring[i & 31]; }
@@ -214,7 +214,6 @@ struct RingWin {
     const uint32_t off = uint32_t(a & 15u);
     ring = lane_ring;
     nchunk = slen ? (off + slen + 15) / 16 : 0u;
-    P = P0;
     const int32_t A = slen ? P0 + int32_t(8 * off) : 1;
     const int32_t m = (A - 1) >> 5;
     for (int k = 0; k < 4; k++) fetch((m >> 3) - k);  // the whole ring
@@ -229,7 +228,10 @@ struct RingWin {
     q0 = word(m - 2);
     q1 = word(m - 3);
     nidx = m - 4;
+    pc = P0 - int32_t(vb) - 32 * nidx;
   }
+  // unread stream bits (negative after an overrun)
+  __device__ __forceinline__ int32_t pos() const { return int32_t(vb) + pc + 32 * nidx; }
   // round start (after the warp's wait): issue the quarters down to three
   // below the one the next read falls in
   __device__ __forceinline__ void top_up() {
@@ -237,13 +239,11 @@ struct RingWin {
     while (nextq >= target && nextq >= 0) fetch(nextq--);
   }
   // e = a table entry whose low 5 bits are the code length (1..11): the
-  // funnel shifts use the amount modulo 32 and the counters mask it
+  // funnel shifts use the amount modulo 32 and the counter masks it
   __device__ __forceinline__ void consume_entry(uint32_t e) {
     hi = __funnelshift_l(lo, hi, e);
     lo = __funnelshift_l(0u, lo, e);
-    const uint32_t n = e & 31u;
-    vb -= n;
-    P -= int32_t(n);
+    vb -= e & 31u;
   }
   __device__ __forceinline__ void refill() {
     const bool use = vb <= 32u;
@@ -736,10 +736,12 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
   // ring's initial four quarters: at most 3 refills)
   if (ok) {
     const uint32_t head = min(count, uint32_t(4u - (reinterpret_cast<uintptr_t>(dst) & 3u)) & 3u);
-    for (; n < head && W.P >= -32; n++) dst[n] = uint8_t(one());
+    for (; n < head; n++) dst[n] = uint8_t(one());
   }
   uint32_t* d32 = reinterpret_cast<uint32_t*>(dst + n);
-  bool live = ok && n + 4 <= count && W.P >= -32;
+  // the count bounds every loop; a damaged stream that runs past its start reads
+  // zero words and is rejected by the final position check
+  bool live = ok && n + 4 <= count;
   while (__any_sync(0xFFFFFFFFu, live)) {
     cp_async_wait_prev();
     if (live) W.top_up();
@@ -761,7 +763,7 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
         // symbols are byte 1 of each entry
         *d32++ = __byte_perm(__byte_perm(e0, e1, 0x0051), __byte_perm(e2, e3, 0x0051), 0x5410);
         n += 4;
-        live = n + 4 <= count && W.P >= -32;
+        live = n + 4 <= count;
       }
     }
   }
@@ -769,8 +771,8 @@ __global__ void __launch_bounds__(32) zstd_direct_literals(const uint8_t* __rest
   // and no copy may still target shared memory when the CTA exits
   cp_async_wait_all();
   if (ok)  // tail: fewer than 4 symbols (at most 3 more ring words)
-    for (; n < count && W.P >= -32; n++) dst[n] = uint8_t(one());
-  ok = ok && n == count && W.P == 0;
+    for (; n < count; n++) dst[n] = uint8_t(one());
+  ok = ok && n == count && W.pos() == 0;
   if (act && !ok) atomicOr(status + b.job, VOOM_ZSTD_ST_LITERALS);
 }
 
