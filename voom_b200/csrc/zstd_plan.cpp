@@ -37,20 +37,26 @@ inline uint64_t le(const uint8_t* p, int n) {
 }
 
 // ------------------------------------------------ table-description readers
+// little-endian bit field [q, q + nb) of p[0..n) (zero past n), nb <= 32
+inline uint32_t bitfield(const uint8_t* p, size_t n, uint64_t q, int nb) {
+  if (nb <= 0) return 0;
+  const uint64_t byte = q >> 3;
+  uint64_t v = 0;
+  if (byte + 8 <= n) {
+    memcpy(&v, p + byte, 8);
+  } else {
+    for (uint64_t k = 0; k < 8 && byte + k < n; k++) v |= uint64_t(p[byte + k]) << (8 * k);
+  }
+  v >>= (q & 7);
+  return uint32_t(v & ((uint64_t(1) << nb) - 1));
+}
 struct FwdBits {
   const uint8_t* p;
   size_t n;
   uint64_t pos = 0;
-  uint32_t peek(int nb) const {
-    uint32_t v = 0;
-    for (int i = 0; i < nb; i++) {
-      const uint64_t q = pos + uint64_t(i);
-      v |= (q / 8 < n ? (uint32_t(p[q / 8]) >> (q % 8)) & 1u : 0u) << i;
-    }
-    return v;
-  }
+  uint32_t peek(int nb) const { return bitfield(p, n, pos, nb); }
   uint32_t get(int nb) {
-    uint32_t v = peek(nb);
+    const uint32_t v = peek(nb);
     pos += uint64_t(nb);
     return v;
   }
@@ -152,17 +158,19 @@ struct BwdBits {
     pos = int64_t(8 * (len - 1)) + hb32(b[len - 1]);
     return true;
   }
+  // the nb bits below pos (bits below the stream start read as 0)
   uint32_t read(int nb) {
+    const int64_t q = pos - nb;
     uint32_t v = 0;
-    for (int i = nb - 1; i >= 0; i--) {
-      const int64_t q = pos - nb + i;
-      const uint32_t bit = q >= 0 ? (uint32_t(p[q / 8]) >> (q % 8)) & 1u : 0u;
-      v |= bit << i;
-    }
+    if (q >= 0)
+      v = bitfield(p, n, uint64_t(q), nb);
+    else if (pos > 0)
+      v = bitfield(p, n, 0, int(pos)) << int(-q);
     pos -= nb;
     return v;
   }
 };
+
 
 // Huffman tree description (RFC 8878 4.2.1) -> weights of every symbol.
 bool read_huffman(const uint8_t* p, size_t n, ZHuf* h, size_t* used) {
