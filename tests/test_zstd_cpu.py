@@ -148,3 +148,26 @@ def test_cabi_example_frames(built_lib, tmp_path):
         assert oz.libzstd_decompress(fr, int(j["dst_len"])) == raw[int(j["dst"]):int(j["dst"] + j["dst_len"])].tobytes()
     plan = Z.ZstdPlan(src, jobs)
     assert plan.info.n_direct_jobs + plan.info.n_bad_jobs <= 12 and not plan.plan_status.any()
+
+
+def test_planner_direct_decision_edges(built_lib):
+    """Direct (straight-to-output) planning only when every block size is
+    known and adds up: raw blocks and multi-frame jobs qualify; a job length
+    one byte off the frames' content, an interleaved job, or a block with
+    sequences does not (those take the general path, which reports the
+    mismatch)."""
+    from voom_b200.formats import zstd_gpu as Z
+    from voom_b200.formats import zstd_host as zh
+
+    rng = np.random.default_rng(0)
+    rand = rng.integers(0, 256, 200000, dtype=np.uint8).tobytes()
+    cases = {"raw": (zh.compress(rand, 1), len(rand), True),
+             "two_frames": (zh.compress(rand[:5000], 1) + zh.compress(rand[5000:9000], 1), 9000, True),
+             "sequences": (zh.compress(bytes(150000), 1), 150000, False)}
+    for name, (frame, n, direct) in cases.items():
+        for extra, flags, want in ((0, 0, direct), (1, 0, False), (0, Z.INTERLEAVE, False)):
+            job = np.zeros(1, Z.JOB_DTYPE)
+            job[0] = (0, len(frame), 0, n + extra, len(frame) if flags else 0, flags, 0)
+            plan = Z.ZstdPlan(np.frombuffer(frame + bytes(n + extra), np.uint8), job)
+            assert plan.info.n_direct_jobs == int(want), (name, extra, flags)
+            assert plan.plan_status[0] == 0
