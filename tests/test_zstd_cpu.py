@@ -171,3 +171,26 @@ def test_planner_direct_decision_edges(built_lib):
             plan = Z.ZstdPlan(np.frombuffer(frame + bytes(n + extra), np.uint8), job)
             assert plan.info.n_direct_jobs == int(want), (name, extra, flags)
             assert plan.plan_status[0] == 0
+
+
+def test_cabi_example_vpack_bodies(built_lib, tmp_path):
+    """The C-ABI example's vpack files (config-2 bodies, two layers): one
+    interleaved job per body, outputs back to back, and the oracle's
+    decode_body of every body equals its slice of raw.bin."""
+    from oracle import vpack as ov
+    from voom_b200.cabi_example import make_vpack_bodies
+    from voom_b200.formats import zstd_gpu as Z
+
+    make_vpack_bodies.main(str(tmp_path), 2)
+    src = np.fromfile(tmp_path / "src.bin", np.uint8)
+    jobs = np.fromfile(tmp_path / "jobs.bin", Z.JOB_DTYPE)
+    raw = np.fromfile(tmp_path / "raw.bin", np.uint8)
+    assert (jobs["flags"] & Z.INTERLEAVE).all()
+    assert int(jobs["dst"][-1] + 2 * jobs["dst_len"][-1]) == raw.size
+    for j in jobs[:6]:
+        head = {"hi_z": int(j["src_len"]), "lo": int(j["dst_len"])}
+        body = src[int(j["src"]):int(j["src"] + j["src_len"] + j["dst_len"])]
+        got = ov.decode_body(head, body)
+        assert got.tobytes() == raw[int(j["dst"]):int(j["dst"] + 2 * j["dst_len"])].tobytes()
+    plan = Z.ZstdPlan(src, jobs)
+    assert plan.info.n_jobs == jobs.size and not plan.plan_status.any()
