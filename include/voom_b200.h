@@ -255,7 +255,8 @@ int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_pla
  * record a CUDA event after each of its launches (on the device current when
  * timing was switched on); voom_zstd_kernel_times(ms, ids, cap) waits for the
  * last decode and returns how many (interval ms, kernel id) pairs it wrote, in
- * launch order.  Kernel ids: */
+ * launch order.  A profiling aid: one process-wide event set, so time one
+ * decode at a time (not thread-safe).  Kernel ids: */
 enum {
   VOOM_ZSTD_K_DIRECT_LITERALS = 1, VOOM_ZSTD_K_BLOCK_DECODE = 2, VOOM_ZSTD_K_SEQ_SCAN = 3,
   VOOM_ZSTD_K_JOB_SCAN = 4, VOOM_ZSTD_K_BLOCK_EXECUTE = 5, VOOM_ZSTD_K_OUTPUT = 6,
