@@ -198,3 +198,29 @@ def test_moe_step_graph_replays_the_eager_stack():
             for layer in layers:
                 cur = layer(cur)
             assert torch.equal(g.step(x), cur)
+
+
+def test_damaged_expert_page_raises(built_lib):
+    """A routed expert whose compressed page is damaged must not give a silent
+    wrong answer: the layer's status carries the fault and check_status()
+    raises (the reference raises while decoding a damaged frame), then the
+    word is clear again for the next step."""
+    from voom_b200.runtime import moe
+
+    E, H, I = 4, 512, 256
+    ex, wr, nw = make(E, H, I, 0.02, 9)
+    store = moe.ExpertStore([tuple(bits(w) for w in e) for e in ex], "cuda:0")
+    layer = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=E, norm_topk=True)  # every expert routed
+    x = torch.randn((2, H), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    layer(x)
+    layer.check_status()  # intact pages: no error
+    page = store.pages[1][0].page  # gate projection of expert 1
+    mid = page.src.numel() // 2
+    page.src[mid] ^= 0x5A
+    layer(x)
+    with pytest.raises(ValueError, match="checkpoint verification"):
+        layer.check_status()
+    assert int(layer.status.item()) == 0
+    page.src[mid] ^= 0x5A  # repaired: clean again
+    layer(x)
+    layer.check_status()

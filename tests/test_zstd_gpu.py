@@ -230,3 +230,49 @@ def test_direct_literals_short_codes(Z):
     batch.run(_device.upload(np.frombuffer(src, np.uint8), dev), out)
     assert not batch.job_status().any()
     assert out.cpu().numpy().tobytes() == b"".join(raws)
+
+
+def _text(n: int, seed: int) -> bytes:
+    """Bytes with many short matches (level 1 emits sequences for them)."""
+    rng = np.random.default_rng(seed)
+    words = [bytes(rng.integers(97, 123, rng.integers(2, 9), dtype=np.uint8)) for _ in range(200)]
+    out = bytearray()
+    while len(out) < n:
+        out += words[int(rng.integers(0, len(words)))] + b" "
+    return bytes(out[:n])
+
+
+@pytest.mark.parametrize("first_len", [70_000, 300_000])
+def test_frame_longer_than_its_job_leaves_the_next_job_intact(Z, first_len):
+    """A frame without a content size whose decoded bytes exceed its job's
+    dst_len must be rejected without writing past that job's share of the
+    decode scratch: the next job of the same batch stays bit-exact."""
+    from voom_b200 import _device
+    from voom_b200.formats import zstd_host
+
+    long_raw = _text(first_len, 1)
+    c = zstd_host.ZstdCompressor(level=1)
+    long_fr = c.compress(long_raw) + c.flush()  # streamed: no frame content size
+    assert Z.frame_content_size(long_fr) is None
+    ok_raw = _text(90_000, 2)
+    ok_fr = zstd_host.compress(ok_raw, 1)
+    short = first_len // 3  # the caller's (wrong) output size for the first job
+    src = long_fr + ok_fr
+    jobs = np.zeros(2, dtype=Z.JOB_DTYPE)
+    d1 = (short + 255) // 256 * 256
+    jobs[0] = (0, len(long_fr), 0, short, 0, 0, 0)
+    jobs[1] = (len(long_fr), len(ok_fr), d1, len(ok_raw), 0, 0, 0)
+    host = np.frombuffer(src, np.uint8)
+    plan = Z.ZstdPlan(host, jobs)
+    dev = torch.device("cuda", 0)
+    d_src = _device.upload(host, dev)
+    out = torch.full((d1 + len(ok_raw) + 4096,), 0xA5, dtype=torch.uint8, device=dev)
+    batch = Z.ZstdBatch(plan, dev)
+    for _ in range(2):
+        batch.run(d_src, out)
+        st = batch.job_status()
+        assert st[0] & Z.ST_SIZE, Z.describe(int(st[0]))
+        assert st[1] == 0, Z.describe(int(st[1]))
+        got = out.cpu().numpy()
+        assert got[d1:d1 + len(ok_raw)].tobytes() == ok_raw
+        assert (got[d1 + len(ok_raw):] == 0xA5).all()  # nothing written past the last job

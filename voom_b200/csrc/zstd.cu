@@ -1411,6 +1411,13 @@ __global__ void __launch_bounds__(256) zstd_block_execute(const uint8_t* __restr
     return;
   }
   const ZBlockRt rt = v.rt[bi];
+  // A job's Z-space holds exactly dst_len words.  Blocks whose decoded sizes
+  // add up to more (no content size, a damaged stream, a wrong dst_len) were
+  // flagged by the job scan; none of their bytes may be written, or they
+  // would land in the next job's words or past the scratch.
+  if ((status[b.job] & VOOM_ZSTD_ST_SIZE) || rt.zstart < job.zoff ||
+      rt.zstart + rt.out_size > job.zoff + job.dst_len)
+    return;
   uint32_t* res = v.res + rt.zstart;
   if (b.type == 0) {
     for (uint32_t i = threadIdx.x; i < b.size; i += blockDim.x) res[i] = kResolved | __ldg(src + b.src + i);
@@ -1794,6 +1801,10 @@ __global__ void zstd_checksum(const uint8_t* img, uint8_t* scratch, const uint8_
     z0 = a.zstart;
     n = l.zstart + l.out_size - z0;
   }
+  if (z0 < job.zoff || z0 + n > job.zoff + job.dst_len) {  // never read past the job's output
+    atomicOr(status + fr.job, VOOM_ZSTD_ST_SIZE);
+    return;
+  }
   const bool inter = job.flags & VOOM_ZSTD_INTERLEAVE;
   const uint8_t* r = out + job.dst + (inter ? 2 * (z0 - job.zoff) + 1 : z0 - job.zoff);
   const uint32_t stride = inter ? 2u : 1u;
@@ -1859,11 +1870,19 @@ bool plan_counts(const void* plan, ZPlanHeader* out, std::vector<ZSegment>* segs
 namespace {
 constexpr int kMaxTimed = 96;
 bool g_time_on = false;
+int g_time_dev = -1;  // device the events were created on
 cudaEvent_t g_tev[kMaxTimed + 1];
 uint32_t g_tid[kMaxTimed];
 int g_ntev = 0;
+// Timing applies to decodes on the device the events belong to; a decode on
+// any other device records nothing.
+bool timing_here() {
+  if (!g_time_on) return false;
+  int dev = -1;
+  return cudaGetDevice(&dev) == cudaSuccess && dev == g_time_dev;
+}
 void tmark(cudaStream_t s, uint32_t id) {
-  if (!g_time_on || g_ntev > kMaxTimed) return;
+  if (g_ntev > kMaxTimed || !timing_here()) return;
   if (g_ntev > 0) g_tid[g_ntev - 1] = id;
   cudaEventRecord(g_tev[g_ntev++], s);
 }
@@ -1871,11 +1890,23 @@ void tmark(cudaStream_t s, uint32_t id) {
 
 VOOM_API int voom_zstd_set_timing(int on) {
   if (on && !g_time_on) {
-    for (int i = 0; i <= kMaxTimed; i++)
-      if (cudaEventCreate(&g_tev[i]) != cudaSuccess) return VOOM_E_CUDA;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return VOOM_E_CUDA;
+    for (int i = 0; i <= kMaxTimed; i++) {
+      if (cudaEventCreate(&g_tev[i]) != cudaSuccess) {
+        for (int q = 0; q < i; q++) cudaEventDestroy(g_tev[q]);  // nothing stays half made
+        return VOOM_E_CUDA;
+      }
+    }
+    g_time_dev = dev;
   } else if (!on && g_time_on) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(g_time_dev);
     cudaDeviceSynchronize();
     for (int i = 0; i <= kMaxTimed; i++) cudaEventDestroy(g_tev[i]);
+    if (cur >= 0) cudaSetDevice(cur);
+    g_time_dev = -1;
   }
   g_time_on = on != 0;
   g_ntev = 0;
@@ -1884,6 +1915,8 @@ VOOM_API int voom_zstd_set_timing(int on) {
 
 VOOM_API int voom_zstd_kernel_times(float* ms, uint32_t* ids, int cap) {
   if (!g_time_on || g_ntev < 2) return 0;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != g_time_dev) return 0;
   if (cudaEventSynchronize(g_tev[g_ntev - 1]) != cudaSuccess) return VOOM_E_CUDA;
   int n = 0;
   for (int i = 1; i < g_ntev && n < cap; i++, n++) {
@@ -1903,7 +1936,7 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint8_t* img = static_cast<const uint8_t*>(d_plan);
   uint8_t* scr = static_cast<uint8_t*>(d_scratch);
-  g_ntev = 0;
+  if (timing_here()) g_ntev = 0;
   tmark(s, 0);
   if (h.n_dlit) {
     zstd_direct_literals<<<(h.n_dlit + kDlBlocksPerWarp - 1) / kDlBlocksPerWarp, 32, 0, s>>>(d_src, img, scr,

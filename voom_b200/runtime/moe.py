@@ -32,6 +32,27 @@ PAGES_DTYPE = np.dtype([("gate", PROJ_DTYPE), ("up", PROJ_DTYPE), ("down", PROJ_
 assert PAGES_DTYPE.itemsize == 144
 
 
+# Status word bits written by the fused kernels (one u32 per layer).
+STATUS_PAGE = 1    # a compressed expert page failed its checkpoint verification
+STATUS_ROUTES = 2  # an expert got more route rows than the launch covered
+
+
+def raise_on_status(status: torch.Tensor, what: str) -> None:
+    """Reads a layer's device status word (synchronises its stream), clears it,
+    and raises ValueError when a kernel reported a fault.  The reference
+    raises while decoding a damaged page (formats/bf16_rans.py:216-221); the
+    fused kernels cannot raise, so the fault is carried to the next check."""
+    v = int(status.item())
+    if v:
+        status.zero_()
+        parts = []
+        if v & STATUS_PAGE:
+            parts.append("a compressed expert page failed its checkpoint verification")
+        if v & STATUS_ROUTES:
+            parts.append("an expert had more routed tokens than the launch covered")
+        raise ValueError(f"{what}: " + "; ".join(parts or [f"status 0x{v:x}"]))
+
+
 def every_for(cols: int, longest: int = 512) -> int:
     """Checkpoint interval for rows of `cols` elements: the longest power of
     two <= `longest` (and >= 64) dividing the row, so each lane pair of the
@@ -152,6 +173,13 @@ class MoeLayer:
 
     __call__ = forward
 
+    def check_status(self) -> None:
+        """Raises ValueError if any forward since the last check met a damaged
+        expert page (or a routing overflow); clears the status word.  Forward
+        itself never synchronises, so callers check once per step, where they
+        read results anyway."""
+        raise_on_status(self.status, "MoE layer")
+
 
 class MoeStepGraph:
     """A fixed stack of MoE layers for T tokens, captured once in a CUDA graph
@@ -194,6 +222,11 @@ class MoeStepGraph:
     def step(self, x: torch.Tensor) -> torch.Tensor:
         self.x.copy_(x)
         return self.replay()
+
+    def check_status(self) -> None:
+        """check_status() of every layer of the stack (one synchronisation)."""
+        for i, layer in enumerate(self.layers):
+            raise_on_status(layer.status, f"MoE layer {i}")
 
 
 def route_rows(idx: np.ndarray):
@@ -289,6 +322,10 @@ class ExpertParallelMoeLayer:
 
     __call__ = forward
 
+    def check_status(self) -> None:
+        """As MoeLayer.check_status (this rank's experts only)."""
+        raise_on_status(self.status, "expert-parallel MoE layer")
+
 
 def swiglu_grouped(store: ExpertStore, expert_ids: list[int], token_lists: list[list[int]], h: torch.Tensor,
                    stream: torch.cuda.Stream | None = None) -> torch.Tensor:
@@ -311,6 +348,5 @@ def swiglu_grouped(store: ExpertStore, expert_ids: list[int], token_lists: list[
                                     d_upair.data_ptr(), n_rows, T, h.contiguous().data_ptr(), store.H, store.I,
                                     store.gate_tiles, store.down_tiles, y.data_ptr(), scratch.data_ptr(), need,
                                     status.data_ptr(), _device.stream_ptr(dev, stream)), "voom_expert_swiglu")
-    if int(status.item()):
-        raise ValueError("compressed expert page failed its checkpoint verification")
+    raise_on_status(status, "voom_expert_swiglu")
     return y
