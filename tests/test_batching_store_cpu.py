@@ -10,7 +10,7 @@ from concurrent.futures import ThreadPoolExecutor
 
 import pytest
 
-from voom_b200.runtime.expert_batching import BatchStats, consume_expert_batches, iter_expert_batches
+from voom_b200.runtime.expert_batching import BatchStats, iter_expert_batches
 
 
 def test_batches_and_compute_chunks():
@@ -78,8 +78,10 @@ def test_pipelined_one_fetch_in_flight_and_order():
     st = BatchStats()
     seen = []
     with ThreadPoolExecutor(max_workers=2) as ex:
-        consume_expert_batches(iter_expert_batches(list(range(10)), fetch, fetch_batch=3, executor=ex, stats=st),
-                               lambda ids, pages: seen.append((ids, sorted(pages))))
+        gen = iter_expert_batches(list(range(10)), fetch, fetch_batch=3, executor=ex, stats=st)
+        for ids, pages in gen:
+            seen.append((ids, sorted(pages)))
+            del pages
     assert [ids for ids, _ in seen] == [[0, 1, 2], [3, 4, 5], [6, 7, 8], [9]]
     assert order == [[0, 1, 2], [3, 4, 5], [6, 7, 8], [9]]
     assert peak[0] == 1 and st.prefetch_submitted == 4
@@ -103,24 +105,6 @@ def test_pipelined_close_cancels_pending_fetch():
         gen.close()
         release.set()
     assert [0, 1] in started and [4, 5] not in started
-
-
-def test_consumer_error_closes_producer():
-    closed = []
-
-    def gen():
-        try:
-            yield [1], {1: 1}
-            yield [2], {2: 2}
-        finally:
-            closed.append(True)
-
-    def boom(ids, pages):
-        raise ValueError("compute failed")
-
-    with pytest.raises(ValueError):
-        consume_expert_batches(gen(), boom)
-    assert closed == [True]
 
 
 class FakeReader:

@@ -127,3 +127,61 @@ def test_access_order_matches_reference_layout(golden):
     _, index, _ = golden
     by_off = [n for n, _ in sorted(index.items(), key=lambda kv: kv[1]["off"])]
     assert access_order(list(index)) == by_off
+
+
+def test_run_coalescing_matches_the_sequential_rule():
+    """Vpack2Reader.fetch's vectorised run split against a direct restatement
+    of formats/packed2.py:361-372 (extend the run while the next body starts
+    within RUN_GAP of the furthest end so far)."""
+    import random
+
+    from voom_b200.formats.packed2 import _coalesce
+
+    def runs(ext, gap):
+        out, i = [], 0
+        while i < len(ext):
+            start, end, j = ext[i][0], ext[i][0] + ext[i][1], i + 1
+            while j < len(ext) and ext[j][0] - end <= gap:
+                end = max(end, ext[j][0] + ext[j][1])
+                j += 1
+            out.append((start, end, j - i))
+            i = j
+        return out
+
+    rnd = random.Random(7)
+    for _ in range(2000):
+        ext = sorted((rnd.randint(0, 100), rnd.randint(0, 30)) for _ in range(rnd.randint(1, 12)))
+        gap = rnd.randint(0, 20)
+        run, covered = _coalesce(np.array([a for a, _ in ext]), np.array([b for _, b in ext]), gap)
+        want = runs(ext, gap)
+        assert int(run[-1]) + 1 == len(want)
+        assert covered == sum(e - s for s, e, _ in want)
+        assert [int((run == k).sum()) for k in range(len(want))] == [c for *_, c in want]
+
+
+def test_verify_generation_extents_and_hashes(tmp_path):
+    """The audit without decoding (CPU): a clean archive, then a damaged body
+    and a truncated file, with the reference's report messages."""
+    import json
+    import shutil
+
+    from tests.conftest import GOLDEN
+    from voom_b200.formats.packed2 import verify_generation
+
+    shutil.copy(GOLDEN / "vpack2_tiny.bin", tmp_path / "weights.vpack2")
+    shutil.copy(GOLDEN / "vpack2_tiny.index.json", tmp_path / "weights.vpack2.index.json")
+    index = json.loads((tmp_path / "weights.vpack2.index.json").read_text())
+    rep = verify_generation(tmp_path, decode=False)
+    assert rep["errors"] == [] and rep["tensors"] == len(index) == rep["hashed"]
+    name = sorted(index, key=lambda n: index[n]["off"])[3]
+    blob = bytearray((tmp_path / "weights.vpack2").read_bytes())
+    blob[index[name]["off"] + 1] ^= 0xFF
+    (tmp_path / "weights.vpack2").write_bytes(bytes(blob))
+    rep = verify_generation(tmp_path, decode=False)
+    assert rep["errors"] == [f"hash mismatch at {name}"]
+    last = max(index, key=lambda n: index[n]["off"])
+    (tmp_path / "weights.vpack2").write_bytes(bytes(blob[:-5]))
+    rep = verify_generation(tmp_path, decode=False)
+    end = index[last]["off"] + index[last]["len"]
+    assert rep["errors"] == [f"archive size {end - 5} != indexed extent end {end}",
+                             f"hash mismatch at {name}", f"short read at {last}"]

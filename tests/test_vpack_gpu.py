@@ -131,21 +131,43 @@ def test_smollm2_scaled_archive(built_lib):
         assert np.array_equal(got[d:d + n], r)
 
 
-def test_packed_weight_store_through_weight_cache(archive_dir, decoded):
+def test_packed_weight_store_fetch(archive_dir, decoded):
     """WeightStore leg over the reference's archive: canonical -> stored name
-    translation at the archive boundary, pages materialised through WeightCache."""
-    from voom_b200.runtime.weight_cache import WeightCache
+    translation at the archive boundary, duplicates fetched once, every page
+    decoded on the device in one batched call (the reference's WeightCache
+    calls exactly this fetch, runtime/weight_cache.py:116-122)."""
     from voom_b200.runtime.weight_store import PackedWeightStore
 
     index = json.loads((archive_dir / "weights.vpack2.index.json").read_text())
     stored = sorted(index)
     real = {f"model.{n}": n for n in stored}
     store = PackedWeightStore(archive_dir, real_name=real, require_hashes=True)
-    cache = WeightCache(store, max_bytes=1 << 30)
     logical = [f"model.{n}" for n in stored]
-    pages = cache.get_many([(f"page{i}", [name]) for i, name in enumerate(logical)])
-    for i, name in enumerate(logical):
-        t = pages[f"page{i}"][name]
+    tensors, secs, nbytes = store.fetch(logical + logical[:3])
+    assert sorted(tensors) == sorted(logical) and secs >= 0
+    for name in logical:
+        t = tensors[name]
         assert t.is_cuda
         assert sha(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()) == decoded[real[name]], name
-    assert cache.stats.misses == len(logical) and store.archive_bytes > 0
+    assert nbytes == store.archive_bytes > 0
+
+def test_verify_generation_decodes_every_body(archive_dir):
+    """The full audit: every body hashed and decoded in one batched GPU decode;
+    a body whose stream is damaged but whose digest was rewritten to match is
+    named by the per-body attribution pass."""
+    from voom_b200.formats.packed2 import verify_generation
+
+    index = json.loads((archive_dir / "weights.vpack2.index.json").read_text())
+    rep = verify_generation(archive_dir)
+    assert rep["errors"] == [] and rep["decoded"] == rep["tensors"] == len(index)
+    name = next(n for n in sorted(index, key=lambda n: index[n]["off"])
+                if "raw" not in index[n]["head"] and index[n]["len"] > 4096)
+    e = index[name]
+    blob = bytearray((archive_dir / "weights.vpack2").read_bytes())
+    blob[e["off"] + 6] ^= 0xFF  # the zstd frame header of the hi plane
+    e["sha"] = sha(blob[e["off"]:e["off"] + e["len"]])[:32]
+    (archive_dir / "weights.vpack2").write_bytes(bytes(blob))
+    (archive_dir / "weights.vpack2.index.json").write_text(json.dumps(index))
+    rep = verify_generation(archive_dir)
+    assert len(rep["errors"]) == 1 and rep["errors"][0].startswith(f"decode failure at {name}: ")
+    assert rep["decoded"] == len(index) - 1

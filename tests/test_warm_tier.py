@@ -28,7 +28,7 @@ def test_admit_frames_are_libzstd_level1_of_raw_bytes():
     page = _bf16_page(1)
     tier.admit("p", page)
     assert tier.admits == 1 and "p" in tier
-    comp = tier._store["p"]
+    comp = tier._held["p"].frames
     assert [(n, k, s) for n, k, s, _ in comp] == [("w", "bf16", (64, 256)), ("b", "bf16", (256,))]
     for (name, _, _, frame) in comp:
         raw = _raw(page[name])
@@ -57,7 +57,7 @@ def test_budget_drops_oldest_admissions_and_duplicates_are_ignored():
     for i in range(4):
         tier.admit(f"p{i}", _bf16_page(i))
     tier.admit("p3", _bf16_page(99))  # already held: ignored
-    assert list(tier._store) == ["p2", "p3"]
+    assert tier.keys() == ["p2", "p3"]
     assert tier.admits == 4 and tier.resident_bytes <= tier.max_bytes
     assert "warm tier: 0 hits, 4 admits, 0 rejects" in tier.summary()
 
@@ -86,30 +86,3 @@ def test_take_round_trip_bit_exact_and_batched():
             assert t.dtype == ref.dtype and t.shape == ref.shape
             assert torch.equal(t.view(torch.uint8), ref.view(torch.uint8))
     assert tier.hits == 4 and tier.resident_bytes == 0
-
-
-@pytest.mark.gpu
-def test_weight_cache_miss_is_served_from_warm_tier():
-    from voom_b200.runtime.weight_cache import WeightCache
-
-    dev = torch.device("cuda:0")
-    src = {f"l{i}.w": (torch.randn((256, 256)) * 0.02).to(torch.bfloat16).to(dev) for i in range(3)}
-
-    class Store:
-        def __init__(self):
-            self.calls = 0
-
-        def fetch(self, names):
-            self.calls += 1
-            t = {n: src[n].clone() for n in names}
-            return t, 0.0, sum(x.numel() * 2 for x in t.values())
-
-    store = Store()
-    tier = WarmTier(1 << 30, device=dev)
-    cache = WeightCache(store, max_bytes=256 * 256 * 2, warm=tier)
-    cache.get("l0", ["l0.w"])
-    cache.get("l1", ["l1.w"])  # evicts l0 into the warm tier
-    assert tier.admits == 1 and "l0" in tier
-    got = cache.get("l0", ["l0.w"])
-    assert store.calls == 2 and tier.hits == 1
-    assert torch.equal(got["l0.w"].view(torch.int16), src["l0.w"].view(torch.int16))

@@ -48,8 +48,28 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+def build_hostbuf(verbose: bool = False, force: bool = False) -> Path:
+    """The small CPython extension of pyext/hostbuf.c (buffer addresses for
+    the KV page gather), built with the host C compiler next to this file."""
+    import sysconfig
+
+    src = PKG / "pyext" / "hostbuf.c"
+    out = PKG / ("_hostbuf" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if force or _stale(out, [src]):
+        cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+        cmd = [cc, "-O2", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], str(src), "-o", str(out)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"building _hostbuf failed:\n{res.stdout}\n{res.stderr}")
+    return out
+
+
 def build(verbose: bool = False, force: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile every source under csrc/ and link libvoom_b200.so; return its path."""
+    """Compile every source under csrc/ and link libvoom_b200.so (and the
+    _hostbuf extension); return the library's path."""
+    build_hostbuf(verbose, force)
     nvcc = _nvcc()
     BUILD_DIR.mkdir(exist_ok=True)
     srcs = _sources()

@@ -137,8 +137,28 @@ def resolve_generation(model_dir: Path) -> tuple[Path, Path]:
     return model_dir / "weights.vpack2", model_dir / "weights.vpack2.index.json"
 
 
+def _extent_problems(names: list[str], offs: np.ndarray, lens: np.ndarray, size: int) -> list[str]:
+    """Extent audit of an index sorted by offset: each body must start where the
+    previous one ended, and the last must end at the archive size.  Messages
+    are the reference's (formats/packed2.py:194-243)."""
+    expect = np.zeros_like(offs)
+    if offs.size > 1:
+        expect[1:] = offs[:-1] + lens[:-1]
+    out = [f"extent gap/overlap at {names[k]}: off {int(offs[k])} != {int(expect[k])}"
+           for k in np.nonzero(offs != expect)[0]]
+    end = int(offs[-1] + lens[-1]) if offs.size else 0
+    if end != size:
+        out.append(f"archive size {size} != indexed extent end {end}")
+    return out
+
+
 def verify_generation(model_dir: str | Path, decode: bool = True, paths: tuple[Path, Path] | None = None) -> dict:
-    """Full extent + hash (+ GPU decode) audit of the active generation."""
+    """Audit of the active generation: extents, every body's hash, and (with
+    `decode`) every body's decode.  The archive is read once into host memory,
+    bodies are hashed on host threads and all hash-clean bodies are decoded in
+    one batched GPU decode; only when that batch reports a failure are the
+    bodies decoded one by one to name the failing ones.  Returns
+    {"tensors", "hashed", "decoded", "errors"} like formats/packed2.py:194-243."""
     model_dir = Path(model_dir)
     report = {"tensors": 0, "hashed": 0, "decoded": 0, "errors": []}
     try:
@@ -150,36 +170,74 @@ def verify_generation(model_dir: str | Path, decode: bool = True, paths: tuple[P
     if not archive.exists():
         report["errors"].append(f"archive missing: {archive.name}")
         return report
-    size = archive.stat().st_size
-    entries = sorted(index.items(), key=lambda kv: kv[1]["off"])
-    report["tensors"] = len(entries)
-    pos = 0
-    for name, e in entries:
-        if e["off"] != pos:
-            report["errors"].append(f"extent gap/overlap at {name}: off {e['off']} != {pos}")
-            pos = e["off"]
-        pos += e["len"]
-    if pos != size:
-        report["errors"].append(f"archive size {size} != indexed extent end {pos}")
-    with open(archive, "rb") as f:
-        for name, e in entries:
-            f.seek(e["off"])
-            body = f.read(e["len"])
-            if len(body) != e["len"]:
-                report["errors"].append(f"short read at {name}")
-                continue
-            if e.get("sha"):
-                report["hashed"] += 1
-                if hashlib.sha256(body).hexdigest()[:32] != e["sha"]:
-                    report["errors"].append(f"hash mismatch at {name}")
-                    continue
-            if decode:
+    names = sorted(index, key=lambda n: index[n]["off"])
+    offs = np.array([index[n]["off"] for n in names], np.int64)
+    lens = np.array([index[n]["len"] for n in names], np.int64)
+    report["tensors"] = len(names)
+    blob = np.fromfile(archive, np.uint8)
+    report["errors"] += _extent_problems(names, offs, lens, blob.size)
+
+    def audit(k: int) -> str | None:
+        o, n = int(offs[k]), int(lens[k])
+        if o < 0 or o + n > blob.size:
+            return f"short read at {names[k]}"
+        want = index[names[k]].get("sha")
+        if want and hashlib.sha256(blob[o:o + n]).hexdigest()[:32] != want:
+            return f"hash mismatch at {names[k]}"
+        return None
+
+    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+        problems = list(pool.map(audit, range(len(names))))
+    report["hashed"] = sum(1 for k, pr in enumerate(problems)
+                           if index[names[k]].get("sha") and (pr is None or pr.startswith("hash")))
+    clean = [k for k, pr in enumerate(problems) if pr is None]
+    if decode and clean:
+        heads = [index[names[k]]["head"] for k in clean]
+        try:
+            decode_bodies(heads, blob, [int(offs[k]) for k in clean], [int(lens[k]) for k in clean])
+            report["decoded"] = len(clean)
+        except Exception:
+            for k in clean:  # attribute the failure body by body
                 try:
-                    decode_body(e["head"], body)
+                    decode_body(index[names[k]]["head"], blob[int(offs[k]):int(offs[k] + lens[k])])
                     report["decoded"] += 1
                 except Exception as exc:
-                    report["errors"].append(f"decode failure at {name}: {exc}")
+                    problems[k] = f"decode failure at {names[k]}: {exc}"
+    report["errors"] += [pr for pr in problems if pr is not None]
     return report
+
+
+def _verify_digest(name: str, expected: str | None, body, require: bool):
+    """The vpack2 body integrity rule (formats/packed2.py:322-331): a body with
+    a recorded digest must match it (first 32 hex digits of SHA-256); an
+    unhashed body passes only when hashes are not required.  Raises the
+    reference's IOError messages; returns the body."""
+    if expected is not None:
+        got = hashlib.sha256(body).hexdigest()[:32]
+        if got == expected:
+            return body
+        raise IOError(f"vpack2 body hash mismatch for {name}: {got} != {expected}")
+    if require:
+        raise IOError(f"unhashed vpack2 body refused: {name}")
+    return body
+
+
+def _coalesce(offs: np.ndarray, lens: np.ndarray, gap: int = RUN_GAP) -> tuple[np.ndarray, int]:
+    """Run ids of extents sorted by offset: an extent joins the current run when
+    it starts at most `gap` bytes after the furthest end seen so far
+    (formats/packed2.py:361-372).  With offsets sorted, the furthest end within
+    a run is the running maximum over all earlier extents (an extent that
+    opens a run starts, and so ends, beyond every earlier one), so the split
+    is one vectorised test.  Returns (run id per extent, bytes the runs cover
+    -- gaps inside a run are read, as in the reference)."""
+    if offs.size == 0:
+        return np.zeros(0, np.int64), 0
+    reach = np.maximum.accumulate(offs + lens)
+    run = np.zeros(offs.size, np.int64)
+    np.cumsum(offs[1:] - reach[:-1] > gap, out=run[1:])
+    first = np.r_[0, np.nonzero(np.diff(run))[0] + 1]
+    last = np.r_[first[1:], offs.size] - 1
+    return run, int((reach[last] - offs[first]).sum())
 
 
 class Vpack2Reader:
@@ -228,16 +286,8 @@ class Vpack2Reader:
         if (st.st_dev, st.st_ino, st.st_size, st.st_mtime_ns) != self._archive_identity:
             raise IOError("vpack2 archive changed after reader initialization")
 
-    def _checked_body(self, name: str, entry: dict, body) -> bytes:
-        expected = entry.get("sha")
-        if expected is None:
-            if self.require_hashes:
-                raise IOError(f"unhashed vpack2 body refused: {name}")
-            return body
-        actual = hashlib.sha256(body).hexdigest()[:32]
-        if actual != expected:
-            raise IOError(f"vpack2 body hash mismatch for {name}: {actual} != {expected}")
-        return body
+    def _checked_body(self, name: str, entry: dict, body):
+        return _verify_digest(name, entry.get("sha"), body, self.require_hashes)
 
     def has(self, name: str) -> bool:
         return name in self.index
@@ -275,29 +325,17 @@ class Vpack2Reader:
         IOError.  Returns (name -> CUDA tensor, seconds, bytes read)."""
         t0 = time.perf_counter()
         self._assert_archive_immutable()
-        entries = sorted(((self.index[n], n) for n in names), key=lambda e: e[0]["off"])
-        runs: list[tuple[int, int, list]] = []
-        i = 0
-        while i < len(entries):
-            start = entries[i][0]["off"]
-            end = start + entries[i][0]["len"]
-            j = i + 1
-            while j < len(entries) and entries[j][0]["off"] - end <= RUN_GAP:
-                end = max(end, entries[j][0]["off"] + entries[j][0]["len"])
-                j += 1
-            runs.append((start, end, entries[i:j]))
-            i = j
-        nbytes = sum(e - s for s, e, _ in runs)
-        heads, offs, lens, order, ents = [], [], [], [], []
-        total = 0
-        for _s, _e, run in runs:
-            for ent, name in run:
-                heads.append(ent["head"])
-                offs.append(total)
-                lens.append(int(ent["len"]))
-                order.append(name)
-                ents.append(ent)
-                total += (int(ent["len"]) + 15) // 16 * 16
+        order = sorted(dict.fromkeys(names), key=lambda n: self.index[n]["off"])
+        ents = [self.index[n] for n in order]
+        offs_a = np.array([int(e["off"]) for e in ents], np.int64)
+        lens_a = np.array([int(e["len"]) for e in ents], np.int64)
+        run_id, nbytes = _coalesce(offs_a, lens_a)
+        n_runs = int(run_id[-1]) + 1 if run_id.size else 0
+        heads = [e["head"] for e in ents]
+        lens = [int(x) for x in lens_a]
+        slots = (lens_a + 15) // 16 * 16  # bodies 16-byte aligned in the pinned buffer
+        offs = np.r_[0, np.cumsum(slots)[:-1]].astype(np.int64).tolist() if ents else []
+        total = int(slots.sum())
         host, owned = self._host_buffer(total)
         try:
             hv = memoryview(host.numpy())
@@ -344,5 +382,5 @@ class Vpack2Reader:
         for name, head, (d, n) in zip(order, heads, spans):
             result[name] = to_torch(head, out[d:d + n])
             self.tensors_read += 1
-        self.runs_read += len(runs)
+        self.runs_read += n_runs
         return result, time.perf_counter() - t0, int(nbytes)

@@ -20,10 +20,9 @@ Reference interface replaced: runtime/kv_paged.py:35-240.
 
 from __future__ import annotations
 
-import ctypes
+import itertools
 import json
 import pickle
-import platform
 import struct
 import threading
 import time
@@ -63,11 +62,12 @@ def _bf16_to_raw(t: torch.Tensor) -> bytes:
     return t.detach().contiguous().view(torch.int16).cpu().numpy().tobytes()
 
 
-def _write_safetensors(path: Path, tensors: dict[str, torch.Tensor]) -> None:
+def _write_safetensors_raw(path: Path, tensors: dict[str, tuple[tuple, np.ndarray]]) -> None:
+    """safetensors file of BF16 tensors given as (shape, int16 bit array)."""
     header, blobs, off = {}, [], 0
-    for name, t in tensors.items():
-        raw = _bf16_to_raw(t)
-        header[name] = {"dtype": "BF16", "shape": list(t.shape), "data_offsets": [off, off + len(raw)]}
+    for name, (shape, bits) in tensors.items():
+        raw = np.ascontiguousarray(bits).tobytes()
+        header[name] = {"dtype": "BF16", "shape": list(shape), "data_offsets": [off, off + len(raw)]}
         blobs.append(raw)
         off += len(raw)
     hj = json.dumps(header).encode()
@@ -75,6 +75,11 @@ def _write_safetensors(path: Path, tensors: dict[str, torch.Tensor]) -> None:
         f.write(struct.pack("<Q", len(hj)) + hj)
         for b in blobs:
             f.write(b)
+
+
+def _write_safetensors(path: Path, tensors: dict[str, torch.Tensor]) -> None:
+    _write_safetensors_raw(path, {n: (tuple(t.shape), t.detach().contiguous().view(torch.int16).cpu().numpy())
+                                  for n, t in tensors.items()})
 
 
 def _read_safetensors(path: Path, device) -> dict[str, torch.Tensor]:
@@ -108,22 +113,9 @@ class _Page:
         return self.k is not None
 
     def spill(self, path: Path, compress: bool = False) -> int | None:
-        """Returns the compressed byte count if compress=True, else None."""
-        if compress:
-            k_c = zstd_host.compress(_bf16_to_raw(self.k), 1)
-            v_c = zstd_host.compress(_bf16_to_raw(self.v), 1)
-            path = path.with_suffix(".kvz")
-            with open(path, "wb") as f:
-                pickle.dump({"shape": self.shape, "k": k_c, "v": v_c}, f)
-            self._compressed = True
-            self.path = path
-            self.k = self.v = None
-            return len(k_c) + len(v_c)
-        _write_safetensors(path, {"k": self.k, "v": self.v})
-        self._compressed = False
-        self.path = path
-        self.k = self.v = None
-        return None
+        """Writes this page out (spill_batch of one page); returns the
+        compressed byte count if compress=True, else None."""
+        return spill_batch([self], [path], compress, None)
 
     def load(self) -> tuple[torch.Tensor, torch.Tensor]:
         if self.resident:
@@ -135,30 +127,18 @@ KVZ_PAGE_DTYPE = np.dtype([("k_off", "<u8"), ("k_len", "<u8"), ("v_off", "<u8"),
                            ("shape", "<i8", (8,)), ("ndim", "<u4"), ("status", "<u4")])
 assert KVZ_PAGE_DTYPE.itemsize == 104
 
-# CPython keeps a bytes object's data inline after a fixed header; the data
-# address is id(obj) + this offset (checked once against ctypes below).
-_BYTES_DATA = bytes.__basicsize__ - 1
 _arenas: dict = {}
 _arenas_lock = threading.Lock()
 
 
-def _inline_bytes_ok() -> bool:
-    if platform.python_implementation() != "CPython":
-        return False
-    probe = bytes(range(97, 123)) * 3
-    return ctypes.string_at(id(probe) + _BYTES_DATA, len(probe)) == probe
-
-
-_INLINE_BYTES = _inline_bytes_ok()
-
-
 def _addresses(blobs: list) -> np.ndarray:
-    """Host addresses of the blobs' bytes (the objects stay alive in `blobs`)."""
-    if _INLINE_BYTES and all(type(b) is bytes for b in blobs):
-        return np.fromiter(map(id, blobs), np.uint64, len(blobs)) + np.uint64(_BYTES_DATA)
-    keep = [b if type(b) is bytes else bytes(b) for b in blobs]
-    blobs[:] = keep
-    return np.array([ctypes.cast(ctypes.c_char_p(b), ctypes.c_void_p).value for b in keep], np.uint64)
+    """Host addresses of the blobs' bytes, read through the buffer protocol
+    (the blobs stay referenced by the caller while the addresses are used)."""
+    from .. import _hostbuf
+
+    out = np.empty(len(blobs), np.uint64)
+    _hostbuf.addresses(blobs, out)
+    return out
 
 
 def _arena(device: torch.device) -> _device.PinnedArena:
@@ -282,10 +262,10 @@ class PagedKVCache:
         self.compress_spill = compress_spill
         self.spill_dir = Path(spill_dir)
         self.spill_dir.mkdir(parents=True, exist_ok=True)
-        self._pages: list[list[_Page]] = [[] for _ in range(num_layers)]
-        self._tail_k: list[torch.Tensor | None] = [None] * num_layers
-        self._tail_v: list[torch.Tensor | None] = [None] * num_layers
-        self._offset = 0
+        self._pages: list[list[_Page]] = []
+        self._tail_k: list[torch.Tensor | None] = []
+        self._tail_v: list[torch.Tensor | None] = []
+        self._reset()
         self.stats = KVStats()
         self._pool = ThreadPoolExecutor(max_workers=max(1, spill_threads))
 
@@ -337,39 +317,89 @@ class PagedKVCache:
         return total
 
     def release(self) -> None:
-        paths = {page.path for pages in self._pages for page in pages if page.path is not None}
+        """Drops every page and tail and deletes the spill files this cache
+        wrote -- and only those (runtime/kv_paged.py:196-212)."""
+        files = {pg.path for pg in itertools.chain.from_iterable(self._pages) if pg.path is not None}
+        self._reset()
+        for f in files:
+            f.unlink(missing_ok=True)
+
+    def _reset(self) -> None:
         self._pages = [[] for _ in range(self.num_layers)]
         self._tail_k = [None] * self.num_layers
         self._tail_v = [None] * self.num_layers
         self._offset = 0
-        for path in paths:
-            try:
-                path.unlink()
-            except FileNotFoundError:
-                pass
 
-    def _enforce_budget(self):
-        if self.nbytes() <= self.max_bytes:
+    def _spill_victims(self) -> list[tuple[int, int]]:
+        """(page index, layer) of the pages that must leave HBM for nbytes() to
+        fit max_bytes.  Candidates are the resident closed pages outside each
+        layer's newest `resident_pages`, taken oldest page index first and in
+        layer order within an index (the reference's round-robin,
+        runtime/kv_paged.py:216-240); the victims are the shortest prefix whose
+        bytes cover the excess, the pages the reference spills one by one."""
+        excess = self.nbytes() - self.max_bytes
+        if excess <= 0:
+            return []
+        cands = sorted((i, layer) for layer, pages in enumerate(self._pages)
+                       for i in range(len(pages) - self.resident_pages) if pages[i].resident)
+        victims = []
+        for i, layer in cands:
+            if excess <= 0:
+                break
+            victims.append((i, layer))
+            excess -= self._pages[layer][i].nbytes
+        return victims
+
+    def _enforce_budget(self) -> None:
+        victims = self._spill_victims()
+        if not victims:
             return
-        for page_idx in range(max(len(p) for p in self._pages)):
-            for layer in range(self.num_layers):
-                pages = self._pages[layer]
-                if page_idx >= len(pages) - self.resident_pages:
-                    continue
-                page = pages[page_idx]
-                if not page.resident:
-                    continue
-                raw_bytes = page.nbytes
-                t0 = time.perf_counter()
-                comp = page.spill(self.spill_dir / f"kv_l{layer}_p{page_idx}.safetensors",
-                                  compress=self.compress_spill)
-                self.stats.spills += 1
-                self.stats.spill_s += time.perf_counter() - t0
-                if comp is not None:
-                    self.stats.spill_bytes_raw += raw_bytes
-                    self.stats.spill_bytes_compressed += comp
-                if self.nbytes() <= self.max_bytes:
-                    return
+        t0 = time.perf_counter()
+        pages = [self._pages[layer][i] for i, layer in victims]
+        paths = [self.spill_dir / f"kv_l{layer}_p{i}.safetensors" for i, layer in victims]
+        comp = spill_batch(pages, paths, self.compress_spill, self._pool)
+        self.stats.spills += len(pages)
+        self.stats.spill_s += time.perf_counter() - t0
+        if comp is not None:
+            self.stats.spill_bytes_raw += sum(pg.nbytes for pg in pages)
+            self.stats.spill_bytes_compressed += comp
+
+
+def spill_batch(pages: list[_Page], paths: list[Path], compress: bool,
+                pool: ThreadPoolExecutor | None) -> int | None:
+    """Spills resident pages together: their K and V leave the device in one
+    copy, each page's file is written on `pool`, and every page drops its
+    device tensors.  Compressed spills write the reference's `.kvz` (a pickle
+    of {"shape", "k": zstd(raw K, 1), "v": zstd(raw V, 1)}, kv_paged.py:77-91)
+    and return the compressed byte total; uncompressed spills write
+    safetensors with tensors "k" and "v" and return None.  Without a pool the
+    files are written on the calling thread."""
+    if not pages:
+        return 0 if compress else None
+    flat = torch.cat([t.detach().reshape(-1) for pg in pages for t in (pg.k, pg.v)])
+    host = flat.view(torch.int16).cpu().numpy()
+    pos, slices = 0, []
+    for pg in pages:
+        n = pg.k.numel()
+        slices.append((host[pos:pos + n], host[pos + n:pos + 2 * n]))
+        pos += 2 * n
+
+    def write(j: int) -> int:
+        pg, (k, v) = pages[j], slices[j]
+        if compress:
+            kc, vc = zstd_host.compress(k.tobytes(), 1), zstd_host.compress(v.tobytes(), 1)
+            with open(paths[j].with_suffix(".kvz"), "wb") as f:
+                pickle.dump({"shape": pg.shape, "k": kc, "v": vc}, f)
+            return len(kc) + len(vc)
+        _write_safetensors_raw(paths[j], {"k": (pg.shape, k), "v": (pg.shape, v)})
+        return 0
+
+    sizes = list((pool.map if pool is not None else map)(write, range(len(pages))))
+    for pg, path in zip(pages, paths):
+        pg.path = path.with_suffix(".kvz") if compress else path
+        pg._compressed = compress
+        pg.k = pg.v = None
+    return sum(sizes) if compress else None
 
 
 def spill_pages_compressed(pages_k: np.ndarray, pages_v: np.ndarray, threads: int = 8) -> list[bytes]:

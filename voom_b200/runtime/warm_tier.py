@@ -20,8 +20,8 @@ decodes several pages in one batch.
 from __future__ import annotations
 
 import threading
-from collections import OrderedDict
 from concurrent.futures import ThreadPoolExecutor
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -46,6 +46,13 @@ def _page_to_blobs(tensors: dict) -> list[tuple[str, str, tuple, np.ndarray]] | 
     return out
 
 
+class _Held(NamedTuple):
+    """One admitted page: its (name, kind, shape, zstd frame) entries and the
+    compressed bytes they hold."""
+    frames: list
+    nbytes: int
+
+
 class WarmTier:
     MIN_RATIO = 1.15  # pages that barely compress are not admitted
 
@@ -53,8 +60,8 @@ class WarmTier:
         self.max_bytes = max_bytes
         self.device = device
         self.threads = max(1, int(threads))
-        self._store: OrderedDict[str, list] = OrderedDict()  # key -> [(name, kind, shape, frame)]
-        self._bytes = 0
+        self._held: dict[str, _Held] = {}  # insertion order is admission order
+        self._held_bytes = 0
         self._lock = threading.Lock()
         self.hits = 0
         self.admits = 0
@@ -67,38 +74,52 @@ class WarmTier:
             return list(pool.map(lambda r: zstd_host.compress(r, 1), raws))
 
     def admit(self, key: str, tensors: dict) -> None:
+        """Compress a page evicted from the device cache and hold it.  The page is
+        refused (counted in `rejects`) when a tensor has a type the tier does not
+        hold or the page shrinks by less than MIN_RATIO; a key already held is
+        left as it is."""
         blobs = _page_to_blobs(tensors)
         if blobs is None:
             self.rejects += 1
             return
         if self.device is None:
-            for t in tensors.values():
-                if t.is_cuda:
-                    self.device = t.device
-                    break
+            self.device = next((t.device for t in tensors.values() if t.is_cuda), None)
         frames = self._compress([raw for *_, raw in blobs])
-        raw_total = sum(raw.size for *_, raw in blobs)
-        comp_total = sum(len(c) for c in frames)
-        if raw_total / max(comp_total, 1) < self.MIN_RATIO:
+        held = _Held([(name, kind, shape, f) for (name, kind, shape, _), f in zip(blobs, frames)],
+                     sum(len(f) for f in frames))
+        raw_bytes = sum(raw.size for *_, raw in blobs)
+        if raw_bytes < self.MIN_RATIO * max(held.nbytes, 1):
             self.rejects += 1
             return
-        comp = [(name, kind, shape, c) for (name, kind, shape, _), c in zip(blobs, frames)]
         with self._lock:
-            if key in self._store:
-                return
-            self._store[key] = comp
-            self._bytes += comp_total
-            self.admits += 1
-            while self._bytes > self.max_bytes and self._store:
-                _, old = self._store.popitem(last=False)
-                self._bytes -= sum(len(c) for *_, c in old)
+            if key not in self._held:
+                self._held[key] = held
+                self._held_bytes += held.nbytes
+                self.admits += 1
+                self._trim_locked()
+
+    def _trim_locked(self) -> None:
+        """Drops the oldest admissions until the held bytes fit `max_bytes`
+        (the page just admitted too, when it alone does not fit)."""
+        excess = self._held_bytes - self.max_bytes
+        if excess <= 0:
+            return
+        victims = []
+        for k, h in self._held.items():
+            if excess <= 0:
+                break
+            victims.append(k)
+            excess -= h.nbytes
+        for k in victims:
+            self._held_bytes -= self._held.pop(k).nbytes
 
     def _pop(self, key: str) -> list | None:
         with self._lock:
-            comp = self._store.pop(key, None)
-            if comp is not None:
-                self._bytes -= sum(len(c) for *_, c in comp)
-        return comp
+            held = self._held.pop(key, None)
+            if held is None:
+                return None
+            self._held_bytes -= held.nbytes
+        return held.frames
 
     def take(self, key: str) -> dict | None:
         return self.take_many([key])[key]
@@ -129,12 +150,17 @@ class WarmTier:
 
     def __contains__(self, key: str) -> bool:
         with self._lock:
-            return key in self._store
+            return key in self._held
+
+    def keys(self) -> list[str]:
+        """Held page keys, oldest admission first."""
+        with self._lock:
+            return list(self._held)
 
     @property
     def resident_bytes(self) -> int:
-        return self._bytes
+        return self._held_bytes
 
     def summary(self) -> str:
         return (f"warm tier: {self.hits} hits, {self.admits} admits, {self.rejects} rejects, "
-                f"{self._bytes / 1e6:.0f}MB resident")
+                f"{self._held_bytes / 1e6:.0f}MB resident")
