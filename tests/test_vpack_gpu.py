@@ -164,7 +164,7 @@ def test_verify_generation_decodes_every_body(archive_dir):
                 if "raw" not in index[n]["head"] and index[n]["len"] > 4096)
     e = index[name]
     blob = bytearray((archive_dir / "weights.vpack2").read_bytes())
-    blob[e["off"] + 6] ^= 0xFF  # the zstd frame header of the hi plane
+    blob[e["off"] + 1] ^= 0xFF  # the zstd magic number of the hi plane
     e["sha"] = sha(blob[e["off"]:e["off"] + e["len"]])[:32]
     (archive_dir / "weights.vpack2").write_bytes(bytes(blob))
     (archive_dir / "weights.vpack2.index.json").write_text(json.dumps(index))
