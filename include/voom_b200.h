@@ -362,6 +362,39 @@ typedef struct voom_expert_pages {
 /* Scratch bytes voom_moe_layer needs. */
 uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k);
 
+/* MoE families: which reference layer the routing and accumulation follow.
+ *   VOOM_MOE_GENERIC  runtime/layer_runner.py:347-394 (run_moe_mlp): BF16
+ *                     logits, fp32 softmax, top-k, optional renormalisation,
+ *                     BF16 route weights, experts accumulated in first-
+ *                     appearance order over (position, slot).
+ *   VOOM_MOE_QWEN35   runtime/qwen35.py:584-638 (_route_experts, _moe): as
+ *                     generic but always renormalised (norm_topk must be 1),
+ *                     ascending expert order, zero-centred RMSNorm weight
+ *                     (1 + w, qwen35.py:133-150), and a shared expert gated
+ *                     by bf16(sigmoid(bf16(h . shared_gate_w))).
+ *   VOOM_MOE_GLM      runtime/glm.py:364-392, 429-486: fp32 router logits,
+ *                     sigmoid scores, choice by score + d_router_bias (the
+ *                     e_score_correction_bias, fp32), weights = the chosen
+ *                     scores (/ (sum + 1e-20) when norm_topk) x routed_scale,
+ *                     kept in fp32, ascending expert order, then + the
+ *                     shared expert. */
+#define VOOM_MOE_GENERIC 0u
+#define VOOM_MOE_QWEN35 1u
+#define VOOM_MOE_GLM 2u
+
+typedef struct voom_moe_variant {
+  uint32_t family;                 /* VOOM_MOE_* */
+  uint32_t norm_topk;              /* renormalise the chosen route weights */
+  float routed_scale;              /* GLM routed_scaling_factor (1 for the others) */
+  int32_t shared_expert;           /* page-table index of the shared expert (>= n_experts), or -1 */
+  const uint16_t* d_shared_gate_w; /* qwen35 shared_expert_gate weight, H BF16; NULL otherwise */
+  const float* d_router_bias;      /* GLM: correction bias (E fp32); generic: added to the logits; or NULL */
+} voom_moe_variant;
+
+/* Scratch bytes voom_moe_layer_v / voom_moe_experts_v need (a shared expert
+ * adds one route row per token). */
+uint64_t voom_moe_scratch_bytes_v(const voom_moe_variant* v, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k);
+
 /* One MoE layer for T tokens, entirely on the device: RMSNorm (d_norm_w may
  * be NULL), router GEMV, fp32 softmax, top-k, optional renormalisation,
  * fused rANS-decode + SwiGLU GEMV of every routed expert straight from its
@@ -398,6 +431,25 @@ int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_experts, const
                      uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream);
 int voom_moe_combine(const void* d_scratch, const uint16_t* d_y, const uint16_t* d_x, uint16_t* d_x_out,
                      uint32_t T, uint32_t H, uint32_t residual, void* stream);
+
+/* voom_moe_layer / voom_moe_experts for any family (voom_moe_variant).  The
+ * page table holds the n_experts routed experts and, at index
+ * v->shared_expert, the shared expert (same intermediate size I), which every
+ * token uses.  voom_moe_experts_v's d_y has T * (top_k + 1) rows with a shared
+ * expert (its rows last, in token order), else T * top_k; in expert-parallel
+ * use the shared expert's pages are present on one rank only.
+ * voom_moe_combine applies the family's accumulation (the routes carry it).
+ * Replaces: runtime/layer_runner.py:347-394, runtime/qwen35.py:584-638 and
+ * runtime/glm.py:364-406, 429-486 over pages fetched by WeightCache. */
+int voom_moe_layer_v(const voom_moe_variant* v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                     const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                     uint16_t* d_x_out, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t gate_tiles,
+                     uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
+                     uint32_t* d_status, void* stream);
+int voom_moe_experts_v(const voom_moe_variant* v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                       const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                       uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t gate_tiles, uint32_t down_tiles,
+                       uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream);
 
 /* voom_moe_layer without any device allocation, for callers that cannot
  * allocate device memory themselves: runtimes that own every byte of the GPU

@@ -224,3 +224,93 @@ def test_damaged_expert_page_raises(built_lib):
     page.src[mid] ^= 0x5A  # repaired: clean again
     layer(x)
     layer.check_status()
+
+
+def _family_case(family, E, H, I, n_pages, seed):
+    """Router experts 0..E-1 over `n_pages` distinct page sets (expert e uses
+    set e % n_pages: the routing covers all E experts, the decode work is real
+    for every routed page), plus a shared expert at index E for qwen35 / glm."""
+    from voom_b200.runtime import moe
+
+    g = torch.Generator().manual_seed(seed)
+    sets = [tuple((torch.randn(s, generator=g) * 0.02).to(torch.bfloat16) for s in ((I, H), (I, H), (H, I)))
+            for _ in range(n_pages + 1)]
+    shared = sets.pop()
+    ex = [sets[e % n_pages] for e in range(E)]
+    wr = (torch.randn((E, H), generator=g) * (0.3 if family == "glm" else 1.0)).to(torch.bfloat16)
+    nw = (0.1 * torch.randn(H, generator=g)).to(torch.bfloat16) if family == "qwen35" else \
+        (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    extra = dict(family=family)
+    ref = dict(family=family)
+    bits_list = [tuple(bits(w) for w in s) for s in sets]
+    table = [bits_list[e % n_pages] for e in range(E)]
+    alias = {e: e % n_pages for e in range(n_pages, E)}
+    if family != "generic":
+        table.append(tuple(bits(w) for w in shared))
+        extra["shared"] = E
+        ref["shared"] = shared
+    if family == "qwen35":
+        sgw = (torch.randn(H, generator=g) * 0.05).to(torch.bfloat16)
+        extra["shared_gate_w"] = sgw.cuda()
+        ref["shared_gate_w"] = sgw
+    if family == "glm":
+        bias = torch.randn(E, generator=g) * 0.5
+        extra.update(router_bias=bias.cuda(), routed_scale=2.5)
+        ref.update(bias=bias, routed_scale=2.5)
+    store = moe.ExpertStore(table, "cuda:0", alias=alias)
+    return store, ex, wr, nw, extra, ref
+
+
+@pytest.mark.parametrize("family", ["generic", "qwen35", "glm"])
+@pytest.mark.parametrize("shape", ["c3", "c4"])
+def test_families_match_pinned_oracle(built_lib, family, shape):
+    """Every family's layer through the C ABI against the HF-pinned oracle at
+    config-3 shapes (H 2048, E 128, I 768, top-8) and config-4 shapes (H 6144,
+    E 160, I 2048, top-8) for T = 1, 8 and 64 tokens, rel-L2 <= 1e-2."""
+    from voom_b200.runtime import moe
+
+    E, H, I, n_pages = (128, 2048, 768, 16) if shape == "c3" else (160, 6144, 2048, 8)
+    store, ex, wr, nw, extra, ref = _family_case(family, E, H, I, n_pages, 11 + len(family))
+    layer = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=8, norm_topk=True, **extra)
+    for T in (1, 8, 64):
+        g = torch.Generator().manual_seed(1000 + T)
+        x = torch.randn((T, H), generator=g).to(torch.bfloat16)
+        got = layer(x.cuda()).cpu()
+        layer.check_status()
+        want = om.moe_layer(x, wr, nw, ex, 8, True, **ref)
+        err = om.rel_l2(got, want)
+        assert err < TOL, (family, shape, T, err)
+        # the routed part alone (the residual dominates the norm above)
+        got_r = layer(x.cuda(), residual=False).cpu()
+        want_r = om.moe_layer(x, wr, nw, ex, 8, True, residual=False, **ref)
+        err_r = om.rel_l2(got_r, want_r)
+        assert err_r < TOL, (family, shape, T, err_r)
+
+
+@pytest.mark.parametrize("family", ["qwen35", "glm"])
+def test_family_expert_parallel_split_is_exact(built_lib, family):
+    """The expert-parallel phases on one GPU with the experts split in two
+    stores (one holding the shared expert): the summed route rows and the
+    combine reproduce the single layer bit for bit."""
+    from voom_b200.runtime import moe
+
+    E, H, I = 32, 512, 256
+    store, ex, wr, nw, extra, ref = _family_case(family, E, H, I, 32, 5)
+    full = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=4, **extra)
+    table = [tuple(bits(w) for w in e) for e in ex]
+    shared = tuple(bits(w) for w in ref["shared"])
+    halves = []
+    for r in range(2):
+        mine = [t if i % 2 == r else None for i, t in enumerate(table)]
+        mine.append(shared if r == 0 else None)  # the shared expert's pages live on rank 0
+        halves.append(moe.ExpertParallelMoeLayer(moe.ExpertStore(mine, "cuda:0"), wr.cuda(), nw.cuda(), top_k=4,
+                                                 **extra))
+    x = torch.randn((8, H), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+    want = full(x)
+    ys = [hl.experts(x) for hl in halves]
+    y = ys[0] + ys[1]  # exactly one nonzero contributor per row
+    out = torch.empty_like(x)
+    halves[0].combine(x, y, out)
+    assert torch.equal(out, want)
+    for hl in halves:
+        hl.check_status()

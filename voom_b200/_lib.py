@@ -49,6 +49,21 @@ assert RANS_TILE_DTYPE.itemsize == 56
 RANS_CHUNK_DTYPE = np.dtype([("tile", "<u4"), ("seg_begin", "<u4"), ("seg_end", "<u4"), ("n_in_tile", "<u4")])
 
 
+# MoE families (VOOM_MOE_*) and voom_moe_variant
+MOE_FAMILIES = {"generic": 0, "qwen35": 1, "glm": 2}
+
+
+class MoeVariant(ctypes.Structure):
+    _fields_ = [
+        ("family", ctypes.c_uint32),
+        ("norm_topk", ctypes.c_uint32),
+        ("routed_scale", ctypes.c_float),
+        ("shared_expert", ctypes.c_int32),
+        ("d_shared_gate_w", ctypes.c_void_p),
+        ("d_router_bias", ctypes.c_void_p),
+    ]
+
+
 class RansPlanInfo(ctypes.Structure):
     _fields_ = [
         ("raw_size", ctypes.c_uint64),
@@ -94,6 +109,11 @@ SIGNATURES: dict[str, tuple] = {
     "voom_moe_experts": (_i32, [_vp, _u32, _vp, _vp, _vp, ctypes.c_float, _vp, _u32, _u32, _u32, _u32, _u32, _u32,
                                 _u32, _vp, _vp, _u64, _vp, _vp]),
     "voom_moe_combine": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "voom_moe_scratch_bytes_v": (_u64, [_vp, _u32, _u32, _u32, _u32]),
+    "voom_moe_layer_v": (_i32, [_vp, _vp, _u32, _vp, _vp, ctypes.c_float, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
+                                _u32, _u32, _vp, _u64, _vp, _vp]),
+    "voom_moe_experts_v": (_i32, [_vp, _vp, _u32, _vp, _vp, ctypes.c_float, _vp, _u32, _u32, _u32, _u32, _u32,
+                                  _u32, _vp, _vp, _u64, _vp, _vp]),
     "voom_moe_layer_noalloc": (_i32, [_vp, _u32, _vp, _vp, ctypes.c_float, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                       _u32, _u32, _u32, _vp, _vp]),
     "voom_nf12_decode": (_i32, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _u64, _vp, _vp]),

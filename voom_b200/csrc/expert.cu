@@ -39,19 +39,28 @@ constexpr int kThreads = 256;
 constexpr int kTok = 8;          // tokens per expert pass
 constexpr int kMaxTK = 512;      // T * top_k
 constexpr int kMaxE = 1024;      // experts
+constexpr int kMaxU = kMaxTK + 1;     // unique experts: the routed ones + the shared expert
+constexpr int kMaxRows = 2 * kMaxTK;  // route rows: T * top_k routed + T shared (T <= kMaxTK)
+
+// Families (which reference layer the math follows): VOOM_MOE_GENERIC,
+// VOOM_MOE_QWEN35, VOOM_MOE_GLM (include/voom_b200.h).
+constexpr uint32_t kNoShared = 0xFFFFFFFFu;
 
 struct Routes {
-  uint32_t n_unique;
-  uint32_t T, k, pad;
-  uint32_t expert[kMaxTK];      // unique experts in first-appearance order
-  uint32_t ntok[kMaxTK];        // tokens routed to unique expert u
-  uint32_t uoff[kMaxTK + 1];    // first route row of unique expert u
-  uint32_t upair[kMaxTK];       // [uoff[u] + i] -> token of the i-th route of u
+  uint32_t n_unique;            // unique experts, the shared expert (if any) last
+  uint32_t T, k, family;
+  uint32_t expert[kMaxU];       // unique experts: first-appearance (generic) or ascending id order
+  uint32_t ntok[kMaxU];         // tokens routed to unique expert u
+  uint32_t uoff[kMaxU + 1];     // first route row of unique expert u
+  uint32_t upair[kMaxRows];     // [uoff[u] + i] -> token of the i-th route of u
   uint32_t tok_order[kMaxTK];   // [t*k + j] -> route row, sorted by u per token
-  uint16_t w_bf16[kMaxTK];      // [route row] route weight in BF16
-  uint16_t pad2[kMaxTK];
+  uint16_t w_bf16[kMaxRows];    // [route row] route weight in BF16 (generic, qwen35)
+  float w_row[kMaxRows];        // [route row] route weight in fp32 (glm)
   uint32_t idx[kMaxTK];         // [t*k + j] expert
   float w[kMaxTK];              // [t*k + j] route weight (fp32)
+  uint16_t sgate[kMaxTK];       // qwen35: bf16(sigmoid(bf16(h_t . Wsg))) per token
+  uint32_t shared_u;            // unique index of the shared expert, or kNoShared
+  uint32_t n_rows;              // route rows in use
 };
 
 __device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }
@@ -73,12 +82,20 @@ __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 constexpr int kMaxH = 8192;
 constexpr int kRouterExperts = 4;  // experts per logits CTA: two warps per expert, one half of H each
 
+// Family differences: the qwen35 RMSNorm is zero-centred (weight 1 + w in
+// fp32, qwen35.py:133-150); the GLM router computes fp32 logits from h and W
+// cast to fp32 with no BF16 rounding and takes its bias in the top-k
+// (glm.py:364-392); the generic / qwen35 logits are BF16 (quant.matmul)
+// plus an optional fp32 bias.  Expert row E, when sg_w is given, is the
+// qwen35 shared-expert gate: its BF16 logit goes through a sigmoid rounded
+// to BF16 into R->sgate[t] (qwen35.py:637-638).
 __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __restrict__ x,
                                                               const uint16_t* __restrict__ norm_w, float eps,
                                                               const uint16_t* __restrict__ wr,
                                                               const float* __restrict__ bias, uint32_t E,
                                                               uint32_t H, uint16_t* __restrict__ h,
-                                                              float* __restrict__ logits) {
+                                                              float* __restrict__ logits, uint32_t family,
+                                                              const uint16_t* __restrict__ sg_w, Routes* R) {
   __shared__ float s_h[kMaxH];
   __shared__ float s_red[kThreads / 32];
   __shared__ float s_scale;
@@ -102,17 +119,19 @@ __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __
   }
   const bool write_h = blockIdx.x == 0;
   uint16_t* ht = h + size_t(t) * H;
+  const float w_shift = family == VOOM_MOE_QWEN35 ? 1.f : 0.f;
   for (uint32_t i = tid; i < H; i += kThreads) {
-    const uint32_t hb = norm_w ? f2bf(bf2f(xt[i]) * s_scale * bf2f(norm_w[i])) : xt[i];
+    const uint32_t hb = norm_w ? f2bf(bf2f(xt[i]) * s_scale * (bf2f(norm_w[i]) + w_shift)) : xt[i];
     if (write_h) ht[i] = uint16_t(hb);
     s_h[i] = bf2f(hb);
   }
   __syncthreads();
   const uint32_t e = blockIdx.x * kRouterExperts + (warp & 3u), half = warp >> 2;
   const uint32_t hmid = (H / 16) * 8;  // split point, a multiple of 8
+  const uint32_t rows = E + (sg_w ? 1u : 0u);
   __shared__ float s_part[kThreads / 32];
-  if (e < E) {
-    const uint16_t* we = wr + size_t(e) * H;
+  if (e < rows) {
+    const uint16_t* we = e < E ? wr + size_t(e) * H : sg_w;
     float acc = 0.f;
     for (uint32_t i = (half ? hmid : 0u) + lane * 8; i < (half ? H : hmid); i += 256) {
       const uint4 w = __ldg(reinterpret_cast<const uint4*>(we + i));
@@ -129,45 +148,73 @@ __global__ void __launch_bounds__(kThreads) moe_router_logits(const uint16_t* __
     if (lane == 0) s_part[warp] = acc;
   }
   __syncthreads();
-  if (e < E && half == 0 && lane == 0)
-    logits[size_t(t) * E + e] = rbf(s_part[warp] + s_part[warp + 4]) + (bias ? bias[e] : 0.f);
+  if (e < rows && half == 0 && lane == 0) {
+    const float acc = s_part[warp] + s_part[warp + 4];
+    if (e == E) {
+      R->sgate[t] = uint16_t(f2bf(1.f / (1.f + expf(-rbf(acc)))));
+    } else if (family == VOOM_MOE_GLM) {
+      logits[size_t(t) * E + e] = acc;  // fp32 logits; the bias applies to the sigmoid scores
+    } else {
+      logits[size_t(t) * E + e] = rbf(acc) + (bias ? bias[e] : 0.f);
+    }
+  }
 }
 
-// One CTA per token: fp32 softmax (max and sum as one warp over lanes
-// e % 32), then every expert's rank in (probability desc, id asc) order --
-// each thread compares its experts against all others -- and the k first
-// become the routes.  A NaN probability ranks below every number.
+// One CTA per token.  generic / qwen35 (layer_runner.py:359-368,
+// qwen35.py:584-593): fp32 softmax of the logits (max and sum as one warp
+// over lanes e % 32), keys = probabilities, weights = the chosen
+// probabilities, renormalised over the k chosen when norm_topk.  glm
+// (glm.py:364-392): scores = sigmoid(fp32 logit), keys = scores + bias (the
+// correction bias only decides the choice), weights = the chosen scores,
+// divided by (their sum + 1e-20) when norm_topk, times routed_scale.  Every
+// expert's rank in (key desc, id asc) order is counted by one thread against
+// all others -- ties to the lower id, a NaN key ranks lowest -- and the k
+// first become the routes.
 constexpr int kTopkThreads = 256;
 
 __global__ void __launch_bounds__(kTopkThreads) moe_router_topk(const float* __restrict__ logits, uint32_t E,
-                                                                uint32_t k, uint32_t norm_topk, Routes* routes) {
+                                                                uint32_t k, uint32_t norm_topk, Routes* routes,
+                                                                uint32_t family, const float* __restrict__ bias,
+                                                                float routed_scale) {
   __shared__ float s_p[kMaxE];
   __shared__ float s_key[kMaxE];
   __shared__ int s_pick[64];
   __shared__ float s_mx, s_sm;
   const uint32_t t = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const bool glm = family == VOOM_MOE_GLM;
   for (uint32_t e = tid; e < E; e += kTopkThreads) s_p[e] = logits[size_t(t) * E + e];
   __syncthreads();
-  if (tid < 32) {
-    float mx = -INFINITY;
-    for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, s_p[e]);
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
-    if (lane == 0) s_mx = mx;
+  if (glm) {
+    for (uint32_t e = tid; e < E; e += kTopkThreads) {
+      const float sc = 1.f / (1.f + expf(-s_p[e]));
+      s_p[e] = sc;
+      const float key = bias ? sc + bias[e] : sc;
+      s_key[e] = key == key ? key : -INFINITY;
+    }
+    if (tid == 0) s_sm = 1.f;
+  } else {
+    if (tid < 32) {
+      float mx = -INFINITY;
+      for (uint32_t e = lane; e < E; e += 32) mx = fmaxf(mx, s_p[e]);
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      if (lane == 0) s_mx = mx;
+    }
+    __syncthreads();
+    const float mx = s_mx;
+    for (uint32_t e = tid; e < E; e += kTopkThreads) {
+      const float p = expf(s_p[e] - mx);
+      s_p[e] = p;
+      s_key[e] = p == p ? p : -2.f;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      float sm = 0.f;
+      for (uint32_t e = lane; e < E; e += 32) sm += s_p[e];
+      for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
+      if (lane == 0) s_sm = sm;
+    }
   }
   __syncthreads();
-  const float mx = s_mx;
-  for (uint32_t e = tid; e < E; e += kTopkThreads) {
-    const float p = __expf(s_p[e] - mx);
-    s_p[e] = p;
-    s_key[e] = p == p ? p : -2.f;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    float sm = 0.f;
-    for (uint32_t e = lane; e < E; e += 32) sm += s_p[e];
-    for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
-    if (lane == 0) s_sm = sm;
-  }
   for (uint32_t e = tid; e < E; e += kTopkThreads) {
     const float v = s_key[e];
     uint32_t rank = 0;
@@ -182,29 +229,56 @@ __global__ void __launch_bounds__(kTopkThreads) moe_router_topk(const float* __r
     const float sm = s_sm;
     float sel = 0.f;
     for (uint32_t j = 0; j < k; j++) sel += s_p[s_pick[j]] / sm;
+    const float den = glm ? sel + 1e-20f : sel;
     for (uint32_t j = 0; j < k; j++) {
       const float pw = s_p[s_pick[j]] / sm;
+      float w = norm_topk ? pw / den : pw;
+      if (glm) w *= routed_scale;
       routes->idx[t * k + j] = uint32_t(s_pick[j]);
-      routes->w[t * k + j] = norm_topk ? pw / sel : pw;
+      routes->w[t * k + j] = w;
     }
   }
 }
 
-// Route plan, one CTA of kMaxTK threads (thread p = route position t*k + j):
-// unique experts in first-appearance order (positions, then slots), tokens per
-// expert, route rows grouped by expert in position order, and each token's
-// contributions ordered by that expert order (the order the reference
-// accumulates them in).
-__global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, uint32_t k) {
+// Route plan, one CTA of kMaxTK threads (thread p = route position t*k + j).
+// Unique experts are numbered in the order the family accumulates them:
+// first appearance over (position, slot) for generic (layer_runner.py:
+// 378-394), ascending id for qwen35 and glm (qwen35.py:617-633, glm.py:
+// 455-480).  Then tokens per expert, route rows grouped by expert in
+// position order, and each token's routes ordered by that expert order.
+// With a shared expert (page-table index `shared`, kNoShared if none), it is
+// appended as the last unique expert with one row per token (rows
+// T*k .. T*k + T - 1, token order); the combine adds it after the routed sum.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  uint32_t incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= uint32_t(o)) incl += t;
+  }
+  __syncthreads();
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  uint32_t before = 0, all = 0;
+  for (uint32_t w = 0; w < blockDim.x / 32; w++) {
+    before += w < warp ? s_warp[w] : 0u;
+    all += s_warp[w];
+  }
+  *total = all;
+  return before + incl - v;
+}
+
+__global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, uint32_t k, uint32_t family,
+                                                          uint32_t shared) {
   __shared__ uint32_t s_first[kMaxE];  // first position of each expert
   __shared__ uint32_t s_cnt[kMaxE];    // routes per expert
+  __shared__ uint32_t s_uid[kMaxE];    // unique index of each expert (ascending order)
   __shared__ uint32_t s_idx[kMaxTK];
   __shared__ uint32_t s_u[kMaxTK];     // unique index of position p's expert
   __shared__ uint32_t s_scan[kMaxTK];
-  __shared__ uint32_t s_ntok[kMaxTK];  // routes of unique expert u
+  __shared__ uint32_t s_ntok[kMaxU];   // routes of unique expert u
   __shared__ uint32_t s_warp[kMaxTK / 32];
-  __shared__ uint32_t s_nu;
-  const uint32_t p = threadIdx.x, n = T * k, lane = p & 31, warp = p >> 5;
+  const uint32_t p = threadIdx.x, n = T * k;
   for (uint32_t e = p; e < kMaxE; e += blockDim.x) {
     s_first[e] = 0xFFFFFFFFu;
     s_cnt[e] = 0;
@@ -217,49 +291,53 @@ __global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, 
     atomicAdd(&s_cnt[e], 1u);
   }
   __syncthreads();
-  // exclusive scan of "p is its expert's first position" -> unique index
-  const uint32_t flag = (p < n && s_first[e] == p) ? 1u : 0u;
-  uint32_t v = flag;
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, v, o);
-    if (lane >= o) v += t;
+  uint32_t nu = 0, u = 0;
+  if (family == VOOM_MOE_GENERIC) {
+    // exclusive scan of "p is its expert's first position" -> unique index
+    const uint32_t flag = (p < n && s_first[e] == p) ? 1u : 0u;
+    s_scan[p] = block_excl_scan(flag, s_warp, &nu);
+    __syncthreads();
+    u = p < n ? s_scan[s_first[e]] : 0u;
+  } else {
+    // exclusive scan of "expert is routed" over ids (two ids per thread)
+    const uint32_t e0 = 2 * p, e1 = 2 * p + 1;
+    const uint32_t f0 = s_first[e0] != 0xFFFFFFFFu, f1 = s_first[e1] != 0xFFFFFFFFu;
+    const uint32_t b = block_excl_scan(f0 + f1, s_warp, &nu);
+    s_uid[e0] = b;
+    s_uid[e1] = b + f0;
+    __syncthreads();
+    u = p < n ? s_uid[e] : 0u;
   }
-  if (lane == 31) s_warp[warp] = v;
-  __syncthreads();
-  uint32_t before = 0;
-  for (uint32_t w = 0; w < warp; w++) before += s_warp[w];
-  s_scan[p] = before + v - flag;
-  __syncthreads();
-  const uint32_t u = p < n ? s_scan[s_first[e]] : 0u;
-  if (p < n) s_u[p] = u;
-  if (flag) {
-    r->expert[u] = e;
-    r->ntok[u] = s_cnt[e];
-    s_ntok[u] = s_cnt[e];
+  if (p < n) {
+    s_u[p] = u;
+    if (s_first[e] == p) {
+      r->expert[u] = e;
+      r->ntok[u] = s_cnt[e];
+      s_ntok[u] = s_cnt[e];
+    }
   }
-  if (p == blockDim.x - 1) {
-    s_nu = before + v;
-    r->n_unique = before + v;
+  const bool has_shared = shared != kNoShared;
+  if (p == 0) {
+    r->n_unique = nu + (has_shared ? 1u : 0u);
     r->T = T;
     r->k = k;
+    r->family = family;
+    r->shared_u = has_shared ? nu : kNoShared;
+    r->n_rows = n + (has_shared ? T : 0u);
+    if (has_shared) {
+      r->expert[nu] = shared;
+      r->ntok[nu] = T;
+    }
   }
   __syncthreads();
   // uoff: exclusive scan of ntok in unique order (thread u holds ntok[u])
-  const uint32_t nu = s_nu;
+  uint32_t routed_rows = 0;
   const uint32_t cnt_u = p < nu ? s_ntok[p] : 0u;
-  uint32_t c = cnt_u;
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, c, o);
-    if (lane >= o) c += t;
-  }
-  __syncthreads();
-  if (lane == 31) s_warp[warp] = c;
-  __syncthreads();
-  uint32_t base = 0;
-  for (uint32_t w = 0; w < warp; w++) base += s_warp[w];
-  if (p < nu) s_scan[p] = base + c - cnt_u;
+  const uint32_t base = block_excl_scan(cnt_u, s_warp, &routed_rows);
+  if (p < nu) s_scan[p] = base;
   if (p == 0) r->uoff[0] = 0;
-  if (p < nu) r->uoff[p + 1] = base + c;
+  if (p < nu) r->uoff[p + 1] = base + cnt_u;
+  if (has_shared && p == 0) r->uoff[nu + 1] = n + T;
   __syncthreads();
   if (p < n) {
     // route row: uoff[u] + earlier positions with the same expert
@@ -268,11 +346,19 @@ __global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, 
     const uint32_t row = s_scan[u] + rank;
     r->upair[row] = p / k;
     r->w_bf16[row] = uint16_t(f2bf(r->w[p]));
+    r->w_row[row] = r->w[p];
     // this token's routes ordered by unique index (experts of a token are distinct)
     const uint32_t t = p / k, t0 = t * k;
     uint32_t pos = 0;
     for (uint32_t j = 0; j < k; j++) pos += (s_u[t0 + j] < u) ? 1u : 0u;
     r->tok_order[t0 + pos] = row;
+  }
+  if (has_shared) {
+    for (uint32_t t = p; t < T; t += blockDim.x) {
+      r->upair[n + t] = t;
+      r->w_bf16[n + t] = 0x3F80u;  // 1.0
+      r->w_row[n + t] = 1.f;
+    }
   }
 }
 
@@ -281,8 +367,11 @@ __global__ void moe_route_offsets(Routes* r, uint32_t n_unique, uint32_t T) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   r->n_unique = n_unique;
   r->T = T;
+  r->family = VOOM_MOE_GENERIC;
+  r->shared_u = kNoShared;
   r->uoff[0] = 0;
   for (uint32_t u = 0; u < n_unique; u++) r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
+  r->n_rows = r->uoff[n_unique];
 }
 
 // -------------------------------------------------------- fused decode-GEMV
@@ -528,7 +617,11 @@ __global__ void __launch_bounds__(kThreads, 4) moe_down(const voom_expert_pages*
   if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
 }
 
-// out[t] = ordered BF16 sum of bf16(y * w); x_out = bf16(x + out).
+// out[t] = ordered BF16 sum over the token's routes of the contribution
+// bf16(y * w) -- w the BF16 route weight (generic, qwen35) or the fp32 one
+// (glm, glm.py:469-473) -- in the route plan's expert order; then the shared
+// expert's row: qwen35 adds bf16(sgate[t] * y_shared) (qwen35.py:636-638),
+// glm adds y_shared (glm.py:484); x_out = bf16(x + out) with the residual.
 __global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __restrict__ y,
                             const uint16_t* __restrict__ x, uint16_t* __restrict__ x_out, uint32_t H,
                             uint32_t residual) {
@@ -536,10 +629,18 @@ __global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __rest
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= H) return;
   const uint32_t k = R->k;
+  const bool fp32_w = R->family == VOOM_MOE_GLM;
   float o = 0.f;
   for (uint32_t j = 0; j < k; j++) {
     const uint32_t q = R->tok_order[t * k + j];
-    o = rbf(o + rbf(bf2f(y[size_t(q) * H + c]) * bf2f(R->w_bf16[q])));
+    const float w = fp32_w ? R->w_row[q] : bf2f(R->w_bf16[q]);
+    o = rbf(o + rbf(bf2f(y[size_t(q) * H + c]) * w));
+  }
+  const uint32_t su = R->shared_u;
+  if (su != kNoShared) {
+    float ys = bf2f(y[size_t(R->uoff[su] + t) * H + c]);
+    if (R->family == VOOM_MOE_QWEN35) ys = rbf(bf2f(R->sgate[t]) * ys);
+    o = rbf(o + ys);
   }
   const float base = residual ? bf2f(x[size_t(t) * H + c]) : 0.f;
   x_out[size_t(t) * H + c] = uint16_t(f2bf(base + o));
@@ -597,22 +698,64 @@ int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_
 #undef VOOM_GEMV
 }
 
-}  // namespace
-
-VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k) {
-  return layout(T, H, I, top_k).total;
+// The generic family with no shared expert: what the variant-less entry
+// points run.
+voom_moe_variant generic_variant(uint32_t norm_topk, const float* bias) {
+  voom_moe_variant v;
+  v.family = VOOM_MOE_GENERIC;
+  v.norm_topk = norm_topk;
+  v.routed_scale = 1.f;
+  v.shared_expert = -1;
+  v.d_shared_gate_w = nullptr;
+  v.d_router_bias = bias;
+  return v;
 }
 
-static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
-                            const uint16_t* d_norm_w, float eps, const uint16_t* d_x, uint16_t* d_x_out, uint32_t T,
-                            uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
-                            uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
-                            uint32_t* d_status, void* stream) {
-  if (!d_pages || !d_router_w || !d_x || !d_x_out || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+uint32_t rows_per_token(const voom_moe_variant& v, uint32_t top_k) {
+  return top_k + (v.shared_expert >= 0 ? 1u : 0u);
+}
+
+int check_variant(const voom_moe_variant* v, uint32_t n_experts) {
+  if (!v || v->family > VOOM_MOE_GLM) return VOOM_E_INVALID_ARG;
+  if (v->family == VOOM_MOE_QWEN35 && v->norm_topk != 1) return VOOM_E_INVALID_ARG;  // always renormalised
+  if (v->shared_expert >= 0 && uint32_t(v->shared_expert) < n_experts) return VOOM_E_INVALID_ARG;
+  if (v->d_shared_gate_w && (v->family != VOOM_MOE_QWEN35 || v->shared_expert < 0)) return VOOM_E_INVALID_ARG;
+  return VOOM_OK;
+}
+
+// Router, top-k and route plan for T tokens: R, h and the logits in scratch.
+int launch_front(const voom_moe_variant& v, const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps,
+                 const uint16_t* d_x, uint32_t n_experts, uint32_t T, uint32_t H, uint32_t top_k, Routes* R,
+                 uint16_t* h, float* logits, cudaStream_t st) {
+  const uint32_t rows = n_experts + (v.d_shared_gate_w ? 1u : 0u);
+  const float* logit_bias = v.family == VOOM_MOE_GLM ? nullptr : v.d_router_bias;
+  moe_router_logits<<<dim3((rows + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
+      d_x, d_norm_w, eps, d_router_w, logit_bias, n_experts, H, h, logits, v.family, v.d_shared_gate_w, R);
+  moe_router_topk<<<T, kTopkThreads, 0, st>>>(logits, n_experts, top_k, v.norm_topk, R, v.family,
+                                              v.family == VOOM_MOE_GLM ? v.d_router_bias : nullptr,
+                                              v.routed_scale);
+  moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k, v.family,
+                                       v.shared_expert >= 0 ? uint32_t(v.shared_expert) : kNoShared);
+  return VOOM_OK;
+}
+
+int check_shape(uint32_t n_experts, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k) {
   if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
       top_k > n_experts || H % 8 || I % 8 || H > kMaxH)
     return VOOM_E_INVALID_ARG;
-  const ScratchLayout L = layout(T, H, I, top_k);
+  return VOOM_OK;
+}
+
+int moe_layer_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                   const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                   uint16_t* d_x_out, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t gate_tiles,
+                   uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
+                   uint32_t* d_status, void* stream) {
+  if (!d_pages || !d_router_w || !d_x || !d_x_out || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+  int rc = check_shape(n_experts, T, H, I, top_k);
+  if (rc != VOOM_OK) return rc;
+  const uint32_t rpt = rows_per_token(v, top_k);
+  const ScratchLayout L = layout(T, H, I, rpt);
   if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
   uint8_t* s = static_cast<uint8_t*>(d_scratch);
   Routes* R = reinterpret_cast<Routes*>(s + L.routes);
@@ -621,16 +764,50 @@ static int moe_layer_impl(const voom_expert_pages* d_pages, uint32_t n_experts, 
   uint16_t* y = reinterpret_cast<uint16_t*>(s + L.y);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* logits = reinterpret_cast<float*>(s + L.logits);
-  moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
-      d_x, d_norm_w, eps, d_router_w, nullptr, n_experts, H, h, logits);
-  moe_router_topk<<<T, kTopkThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
-  moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
-  const uint32_t max_unique = min(n_experts, T * top_k);
-  const int rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
-                             d_status, st);
+  launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
+  const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
+  rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * rpt, gate_tiles, down_tiles, d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+int moe_experts_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                     const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                     uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t gate_tiles, uint32_t down_tiles,
+                     uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  if (!d_pages || !d_router_w || !d_x || !d_y || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+  int rc = check_shape(n_experts, T, H, I, top_k);
+  if (rc != VOOM_OK) return rc;
+  const uint32_t rpt = rows_per_token(v, top_k);
+  const ScratchLayout L = layout(T, H, I, rpt);
+  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
+  uint8_t* s = static_cast<uint8_t*>(d_scratch);
+  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
+  uint16_t* h = reinterpret_cast<uint16_t*>(s + L.h);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(d_y, 0, size_t(T) * rpt * H * 2, st) != cudaSuccess) return VOOM_E_CUDA;
+  float* logits = reinterpret_cast<float*>(s + L.logits);
+  launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
+  const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
+  uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
+  rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, T, H, I, max_unique, T * rpt, gate_tiles, down_tiles, d_status,
+                   st);
+  if (rc != VOOM_OK) return rc;
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+}  // namespace
+
+VOOM_API uint64_t voom_moe_scratch_bytes(uint32_t T, uint32_t H, uint32_t I, uint32_t top_k) {
+  return layout(T, H, I, top_k).total;
+}
+
+VOOM_API uint64_t voom_moe_scratch_bytes_v(const voom_moe_variant* v, uint32_t T, uint32_t H, uint32_t I,
+                                           uint32_t top_k) {
+  if (!v) return 0;
+  return layout(T, H, I, rows_per_token(*v, top_k)).total;
 }
 
 VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
@@ -638,12 +815,24 @@ VOOM_API int voom_moe_layer(const voom_expert_pages* d_pages, uint32_t n_experts
                             uint32_t H, uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
                             uint32_t down_tiles, uint32_t residual, void* d_scratch, uint64_t scratch_bytes,
                             uint32_t* d_status, void* stream) {
-  return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
+  return moe_layer_impl(generic_variant(norm_topk, nullptr), d_pages, n_experts, d_router_w, d_norm_w, eps, d_x,
+                        d_x_out, T, H, I, top_k, gate_tiles, down_tiles, residual, d_scratch, scratch_bytes,
+                        d_status, stream);
+}
+
+VOOM_API int voom_moe_layer_v(const voom_moe_variant* v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                              const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps, const uint16_t* d_x,
+                              uint16_t* d_x_out, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k,
+                              uint32_t gate_tiles, uint32_t down_tiles, uint32_t residual, void* d_scratch,
+                              uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  const int rc = check_variant(v, n_experts);
+  if (rc != VOOM_OK) return rc;
+  return moe_layer_impl(*v, d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k,
                         gate_tiles, down_tiles, residual, d_scratch, scratch_bytes, d_status, stream);
 }
 
 // Expert-parallel split of the layer: phase 1 leaves the unweighted expert
-// outputs in d_y (T*top_k rows of H, route-row order; rows of experts whose
+// outputs in d_y (route rows of H, route-row order; rows of experts whose
 // pages have no tiles on this rank stay zero) and the routes in d_scratch;
 // the caller sums d_y over ranks; phase 2 combines.
 VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_experts, const uint16_t* d_router_w,
@@ -652,29 +841,20 @@ VOOM_API int voom_moe_experts(const voom_expert_pages* d_pages, uint32_t n_exper
                               uint32_t I, uint32_t top_k, uint32_t norm_topk, uint32_t gate_tiles,
                               uint32_t down_tiles, uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes,
                               uint32_t* d_status, void* stream) {
-  if (!d_pages || !d_router_w || !d_x || !d_y || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
-  if (T == 0 || top_k == 0 || top_k > 64 || uint64_t(T) * top_k > kMaxTK || n_experts > kMaxE ||
-      top_k > n_experts || H % 8 || I % 8 || H > kMaxH)
-    return VOOM_E_INVALID_ARG;
-  const ScratchLayout L = layout(T, H, I, top_k);
-  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
-  uint8_t* s = static_cast<uint8_t*>(d_scratch);
-  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
-  uint16_t* h = reinterpret_cast<uint16_t*>(s + L.h);
-  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(d_y, 0, size_t(T) * top_k * H * 2, st) != cudaSuccess) return VOOM_E_CUDA;
-  float* logits = reinterpret_cast<float*>(s + L.logits);
-  moe_router_logits<<<dim3((n_experts + kRouterExperts - 1) / kRouterExperts, T), kThreads, 0, st>>>(
-      d_x, d_norm_w, eps, d_router_w, d_router_bias, n_experts, H, h, logits);
-  moe_router_topk<<<T, kTopkThreads, 0, st>>>(logits, n_experts, top_k, norm_topk, R);
-  moe_route_plan<<<1, kMaxTK, 0, st>>>(R, T, top_k);
-  const uint32_t max_unique = min(n_experts, T * top_k);
-  uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
-  const int rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, T, H, I, max_unique, T * top_k, gate_tiles, down_tiles,
-                             d_status, st);
+  return moe_experts_impl(generic_variant(norm_topk, d_router_bias), d_pages, n_experts, d_router_w, d_norm_w, eps,
+                          d_x, T, H, I, top_k, gate_tiles, down_tiles, d_y, d_scratch, scratch_bytes, d_status,
+                          stream);
+}
+
+VOOM_API int voom_moe_experts_v(const voom_moe_variant* v, const voom_expert_pages* d_pages, uint32_t n_experts,
+                                const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps,
+                                const uint16_t* d_x, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k,
+                                uint32_t gate_tiles, uint32_t down_tiles, uint16_t* d_y, void* d_scratch,
+                                uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  const int rc = check_variant(v, n_experts);
   if (rc != VOOM_OK) return rc;
-  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+  return moe_experts_impl(*v, d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, T, H, I, top_k, gate_tiles,
+                          down_tiles, d_y, d_scratch, scratch_bytes, d_status, stream);
 }
 
 VOOM_API int voom_moe_combine(const void* d_scratch, const uint16_t* d_y, const uint16_t* d_x, uint16_t* d_x_out,
@@ -730,8 +910,9 @@ VOOM_API int voom_moe_layer_noalloc(const voom_expert_pages* d_pages, uint32_t n
   void* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != VOOM_OK) return rc;
-  return moe_layer_impl(d_pages, n_experts, d_router_w, d_norm_w, eps, d_x, d_x_out, T, H, I, top_k, norm_topk,
-                        gate_tiles, down_tiles, residual, scratch, kNoAllocBytes, d_status, stream);
+  return moe_layer_impl(generic_variant(norm_topk, nullptr), d_pages, n_experts, d_router_w, d_norm_w, eps, d_x,
+                        d_x_out, T, H, I, top_k, gate_tiles, down_tiles, residual, scratch, kNoAllocBytes,
+                        d_status, stream);
 }
 
 // Experts given by the host (routing already grouped, e.g. by

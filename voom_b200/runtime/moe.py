@@ -135,23 +135,55 @@ class ExpertStore:
         return len(self.pages)
 
 
+def _variant(family: str, norm_topk: bool, routed_scale: float, shared: int | None,
+             shared_gate_w: torch.Tensor | None, router_bias: torch.Tensor | None):
+    from .._lib import MOE_FAMILIES, MoeVariant
+
+    if family not in MOE_FAMILIES:
+        raise ValueError(f"unknown MoE family {family!r} (one of {sorted(MOE_FAMILIES)})")
+    if family == "qwen35":
+        norm_topk = True  # qwen35.py:592 always renormalises
+    return MoeVariant(MOE_FAMILIES[family], int(norm_topk), float(routed_scale), -1 if shared is None else int(shared),
+                      None if shared_gate_w is None else shared_gate_w.data_ptr(),
+                      None if router_bias is None else router_bias.data_ptr())
+
+
 class MoeLayer:
-    """Device-side MoE layer (routing on the GPU, no host synchronisation)."""
+    """Device-side MoE layer (routing on the GPU, no host synchronisation).
+
+    `family` picks the reference layer the math follows: "generic"
+    (runtime/layer_runner.py run_moe_mlp), "qwen35" (runtime/qwen35.py _moe:
+    zero-centred norm weight, ascending expert order, shared expert gated by
+    `shared_gate_w`) or "glm" (runtime/glm.py: fp32 sigmoid router with the
+    correction bias `router_bias`, `routed_scale`, fp32 route weights, shared
+    expert).  `shared` is the store index of the shared expert (after the
+    router's experts), or None."""
 
     def __init__(self, store: ExpertStore, router_w: torch.Tensor, norm_w: torch.Tensor | None, *,
-                 top_k: int, norm_topk: bool = True, eps: float = 1e-6):
+                 top_k: int, norm_topk: bool = True, eps: float = 1e-6, family: str = "generic",
+                 shared: int | None = None, shared_gate_w: torch.Tensor | None = None,
+                 router_bias: torch.Tensor | None = None, routed_scale: float = 1.0):
         self.store = store
         self.router_w = router_w.contiguous()
+        self.n_experts = int(self.router_w.shape[0])
         self.norm_w = None if norm_w is None else norm_w.contiguous()
         self.top_k = int(top_k)
-        self.norm_topk = bool(norm_topk)
+        self.norm_topk = bool(norm_topk) or family == "qwen35"
         self.eps = float(eps)
+        self.family = family
+        self.shared = shared
+        self.shared_gate_w = None if shared_gate_w is None else shared_gate_w.contiguous()
+        self.router_bias = None if router_bias is None else router_bias.float().contiguous()
+        self.routed_scale = float(routed_scale)
+        self.variant = _variant(family, self.norm_topk, self.routed_scale, shared, self.shared_gate_w,
+                                self.router_bias)
         self._scratch: dict[int, torch.Tensor] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=store.device)
 
     def scratch(self, T: int) -> torch.Tensor:
         if T not in self._scratch:
-            n = load().voom_moe_scratch_bytes(T, self.store.H, self.store.I, self.top_k)
+            n = load().voom_moe_scratch_bytes_v(ctypes.byref(self.variant), T, self.store.H, self.store.I,
+                                                self.top_k)
             self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=self.store.device)
         return self._scratch[T]
 
@@ -163,12 +195,13 @@ class MoeLayer:
         out = torch.empty_like(x) if out is None else out
         s = self.scratch(T)
         st = self.store
-        check(load().voom_moe_layer(st.table.data_ptr(), len(st), self.router_w.data_ptr(),
-                                    None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
-                                    x.data_ptr(), out.data_ptr(), T, H, st.I, self.top_k, int(self.norm_topk),
-                                    st.gate_tiles, st.down_tiles, int(residual), s.data_ptr(), s.numel(),
-                                    self.status.data_ptr(),
-                                    _device.stream_ptr(st.device, stream)), "voom_moe_layer")
+        check(load().voom_moe_layer_v(ctypes.byref(self.variant), st.table.data_ptr(), self.n_experts,
+                                      self.router_w.data_ptr(),
+                                      None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                      x.data_ptr(), out.data_ptr(), T, H, st.I, self.top_k, st.gate_tiles,
+                                      st.down_tiles, int(residual), s.data_ptr(), s.numel(),
+                                      self.status.data_ptr(), _device.stream_ptr(st.device, stream)),
+              "voom_moe_layer_v")
         return out
 
     __call__ = forward
@@ -277,47 +310,72 @@ class ExpertParallelMoeLayer:
     """MoE layer with experts spread over the ranks of a process group (NCCL).
 
     Every rank routes all tokens (replicated router), runs the fused decode +
-    SwiGLU for its own experts only, the route rows are summed over ranks
-    with one all-reduce (each row has exactly one nonzero contributor, so the
-    sum is exact), and every rank applies the same ordered combine."""
+    SwiGLU for its own experts only (and the shared expert, on the rank that
+    holds its pages), the route rows are summed over ranks with one
+    all-reduce (each row has exactly one nonzero contributor, so the sum is
+    exact), and every rank applies the same ordered combine.  Same family
+    options as MoeLayer."""
 
     def __init__(self, store: ExpertStore, router_w: torch.Tensor, norm_w: torch.Tensor | None, *, top_k: int,
-                 norm_topk: bool = True, eps: float = 1e-6, group=None, router_bias: torch.Tensor | None = None):
+                 norm_topk: bool = True, eps: float = 1e-6, group=None, router_bias: torch.Tensor | None = None,
+                 family: str = "generic", shared: int | None = None, shared_gate_w: torch.Tensor | None = None,
+                 routed_scale: float = 1.0):
         self.store = store
         self.router_w = router_w.contiguous()
+        self.n_experts = int(self.router_w.shape[0])
         self.router_bias = None if router_bias is None else router_bias.float().contiguous()
         self.norm_w = None if norm_w is None else norm_w.contiguous()
         self.top_k = int(top_k)
-        self.norm_topk = bool(norm_topk)
+        self.norm_topk = bool(norm_topk) or family == "qwen35"
         self.eps = float(eps)
         self.group = group
+        self.shared = shared
+        self.shared_gate_w = None if shared_gate_w is None else shared_gate_w.contiguous()
+        self.variant = _variant(family, self.norm_topk, routed_scale, shared, self.shared_gate_w, self.router_bias)
+        self.rows_per_token = self.top_k + (0 if shared is None else 1)
         self._scratch: dict[int, torch.Tensor] = {}
         self._y: dict[int, torch.Tensor] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=store.device)
+        self.last_collective_bytes = 0
+
+    def buffers(self, T: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """(scratch, route-row buffer) for T tokens, allocated once."""
+        st = self.store
+        if T not in self._scratch:
+            n = load().voom_moe_scratch_bytes_v(ctypes.byref(self.variant), T, st.H, st.I, self.top_k)
+            self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=st.device)
+            self._y[T] = torch.empty((T * self.rows_per_token, st.H), dtype=torch.bfloat16, device=st.device)
+        return self._scratch[T], self._y[T]
+
+    def experts(self, x: torch.Tensor) -> torch.Tensor:
+        """Phase 1 on this rank: routes + this rank's expert rows (others zero)."""
+        T, H = x.shape
+        st = self.store
+        s, y = self.buffers(T)
+        check(load().voom_moe_experts_v(ctypes.byref(self.variant), st.table.data_ptr(), self.n_experts,
+                                        self.router_w.data_ptr(),
+                                        None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                        x.data_ptr(), T, H, st.I, self.top_k, st.gate_tiles, st.down_tiles,
+                                        y.data_ptr(), s.data_ptr(), s.numel(), self.status.data_ptr(),
+                                        _device.stream_ptr(st.device, None)), "voom_moe_experts_v")
+        return y
+
+    def combine(self, x: torch.Tensor, y: torch.Tensor, out: torch.Tensor, residual: bool = True) -> None:
+        T, H = x.shape
+        s, _ = self.buffers(T)
+        check(load().voom_moe_combine(s.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, int(residual),
+                                      _device.stream_ptr(self.store.device, None)), "voom_moe_combine")
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, residual: bool = True) -> torch.Tensor:
         import torch.distributed as dist
 
-        T, H = x.shape
-        st = self.store
-        if T not in self._scratch:
-            n = load().voom_moe_scratch_bytes(T, H, st.I, self.top_k)
-            self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=st.device)
-            self._y[T] = torch.empty((T * self.top_k, H), dtype=torch.bfloat16, device=st.device)
-        s, y = self._scratch[T], self._y[T]
         x = x.contiguous()
         out = torch.empty_like(x) if out is None else out
-        sp = _device.stream_ptr(st.device, None)
-        check(load().voom_moe_experts(st.table.data_ptr(), len(st), self.router_w.data_ptr(),
-                                      None if self.router_bias is None else self.router_bias.data_ptr(),
-                                      None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
-                                      x.data_ptr(), T, H, st.I, self.top_k, int(self.norm_topk), st.gate_tiles,
-                                      st.down_tiles, y.data_ptr(), s.data_ptr(), s.numel(), self.status.data_ptr(),
-                                      sp), "voom_moe_experts")
+        y = self.experts(x)
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
-        check(load().voom_moe_combine(s.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, int(residual),
-                                      sp), "voom_moe_combine")
+            self.last_collective_bytes = y.numel() * y.element_size()
+        self.combine(x, y, out, residual)
         return out
 
     __call__ = forward
