@@ -141,13 +141,16 @@ def test_expert_parallel_split_matches_full_layer(built_lib):
 
 
 def test_expert_batches_producer_consumer(small):
-    """The engine's batch producer feeding consume_expert_batches with the fused
-    grouped SwiGLU: every routed expert computed once, in batch order, and each
-    expert's rows match the reference math."""
+    """The engine's batch producer feeding the fused grouped SwiGLU the way the
+    reference's consume_expert_batches drives it (each batch released before
+    the next is requested; that consumer itself stays the reference's and is
+    run over this producer in tests/test_reference_seam.py): every routed
+    expert computed once, in batch order, and each expert's rows match the
+    reference math."""
     from concurrent.futures import ThreadPoolExecutor
 
     from voom_b200.runtime import moe
-    from voom_b200.runtime.expert_batching import consume_expert_batches, iter_expert_batches
+    from voom_b200.runtime.expert_batching import iter_expert_batches
 
     store, ex, _, _ = small
     g = torch.Generator().manual_seed(11)
@@ -171,8 +174,14 @@ def test_expert_batches_producer_consumer(small):
             done.append(e)
 
     with ThreadPoolExecutor(max_workers=1) as pool:
-        consume_expert_batches(iter_expert_batches(ids, fetch, fetch_batch=2, compute_batch=1, executor=pool),
-                               consume)
+        batches = iter_expert_batches(ids, fetch, fetch_batch=2, compute_batch=1, executor=pool)
+        while True:
+            try:
+                batch_ids, pages = next(batches)
+            except StopIteration:
+                break
+            consume(batch_ids, pages)
+            del batch_ids, pages
     assert done == ids
 
 
