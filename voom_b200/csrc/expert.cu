@@ -29,47 +29,15 @@
 
 #include "common.cuh"
 #include "rans_core.cuh"
+#include "moe_common.cuh"
+#include "moe_proj.cuh"
 
 using namespace voom;
 using namespace voom::rans;
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kTok = 8;          // tokens per expert pass
-constexpr int kMaxTK = 512;      // T * top_k
-constexpr int kMaxE = 1024;      // experts
-constexpr int kMaxU = kMaxTK + 1;     // unique experts: the routed ones + the shared expert
-constexpr int kMaxRows = 2 * kMaxTK;  // route rows: T * top_k routed + T shared (T <= kMaxTK)
-
-// Families (which reference layer the math follows): VOOM_MOE_GENERIC,
-// VOOM_MOE_QWEN35, VOOM_MOE_GLM (include/voom_b200.h).
-constexpr uint32_t kNoShared = 0xFFFFFFFFu;
-
-struct Routes {
-  uint32_t n_unique;            // unique experts, the shared expert (if any) last
-  uint32_t T, k, family;
-  uint32_t expert[kMaxU];       // unique experts: first-appearance (generic) or ascending id order
-  uint32_t ntok[kMaxU];         // tokens routed to unique expert u
-  uint32_t uoff[kMaxU + 1];     // first route row of unique expert u
-  uint32_t upair[kMaxRows];     // [uoff[u] + i] -> token of the i-th route of u
-  uint32_t tok_order[kMaxTK];   // [t*k + j] -> route row, sorted by u per token
-  uint16_t w_bf16[kMaxRows];    // [route row] route weight in BF16 (generic, qwen35)
-  float w_row[kMaxRows];        // [route row] route weight in fp32 (glm)
-  uint32_t idx[kMaxTK];         // [t*k + j] expert
-  float w[kMaxTK];              // [t*k + j] route weight (fp32)
-  uint16_t sgate[kMaxTK];       // qwen35: bf16(sigmoid(bf16(h_t . Wsg))) per token
-  uint32_t shared_u;            // unique index of the shared expert, or kNoShared
-  uint32_t n_rows;              // route rows in use
-};
-
-__device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }
-__device__ __forceinline__ uint32_t f2bf(float f) {  // round to nearest even
-  uint32_t u = __float_as_uint(f);
-  if ((u & 0x7F800000u) == 0x7F800000u) return (u >> 16) | ((u & 0xFFFFu) ? 0x40u : 0u);
-  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
-}
-__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+using namespace voom::moe;
 
 // ------------------------------------------------------------------ router
 // Two kernels.  moe_router_logits: grid (ceil(E / 16), T); each CTA applies
@@ -374,194 +342,6 @@ __global__ void moe_route_offsets(Routes* r, uint32_t n_unique, uint32_t T) {
   r->n_rows = r->uoff[n_unique];
 }
 
-// -------------------------------------------------------- fused decode-GEMV
-struct GemvShared {
-  uint32_t lut[2][4096];
-  uint32_t cum[2][257];
-  uint32_t red[8];
-  uint32_t degenerate[2];
-  float acc[1][128][kTok];  // [0][row in tile][token]
-  uint32_t tok[kTok];
-  uint32_t status;
-};
-
-// 8 BF16 weights (one uint4) times 8 activations at column k of each token.
-template <int NT>
-__device__ __forceinline__ void dot8(const uint4 w, const uint16_t* __restrict__ act, uint32_t ld,
-                                     const uint32_t* tok, uint32_t ntk, uint32_t k, float* acc) {
-  const float w0 = bf2f(w.x & 0xFFFFu), w1 = __uint_as_float(w.x & 0xFFFF0000u);
-  const float w2 = bf2f(w.y & 0xFFFFu), w3 = __uint_as_float(w.y & 0xFFFF0000u);
-  const float w4 = bf2f(w.z & 0xFFFFu), w5 = __uint_as_float(w.z & 0xFFFF0000u);
-  const float w6 = bf2f(w.w & 0xFFFFu), w7 = __uint_as_float(w.w & 0xFFFF0000u);
-#pragma unroll
-  for (int j = 0; j < NT; j++) {
-    if (j < int(ntk)) {
-      const uint4 a = __ldg(reinterpret_cast<const uint4*>(act + size_t(tok[j]) * ld + k));
-      float s = acc[j];
-      s = fmaf(w0, bf2f(a.x & 0xFFFFu), s);
-      s = fmaf(w1, __uint_as_float(a.x & 0xFFFF0000u), s);
-      s = fmaf(w2, bf2f(a.y & 0xFFFFu), s);
-      s = fmaf(w3, __uint_as_float(a.y & 0xFFFF0000u), s);
-      s = fmaf(w4, bf2f(a.z & 0xFFFFu), s);
-      s = fmaf(w5, __uint_as_float(a.z & 0xFFFF0000u), s);
-      s = fmaf(w6, bf2f(a.w & 0xFFFFu), s);
-      s = fmaf(w7, __uint_as_float(a.w & 0xFFFF0000u), s);
-      acc[j] = s;
-    }
-  }
-}
-
-// Decodes tile `t` of one projection for the CTA's tokens and adds every
-// row's dot products into sh.acc[slot].  Rows of `cols` elements; each lane
-// pair owns one `every`-element segment.  Returns nothing; errors -> sh.status.
-template <int NT>
-__device__ void gemv_tile(GemvShared& sh, const voom_expert_proj& P, uint32_t t, int slot,
-                          const uint16_t* __restrict__ act, uint32_t ld, uint32_t ntk) {
-  const voom_rans_tile tl = P.tiles[t];
-  const uint32_t row_bytes = 2u * P.cols, every = P.every;
-  const uint32_t rows = tl.raw_len / row_bytes;
-  const uint32_t spr = P.cols / every;  // segments per row
-  const uint32_t nseg = rows * spr;
-  const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1;
-  if (tl.mode == 1) {
-    build_lut(sh.lut[0], sh.cum[0], sh.red, &sh.degenerate[0], P.src + tl.low_freq);
-    build_lut(sh.lut[1], sh.cum[1], sh.red, &sh.degenerate[1], P.src + tl.high_freq);
-  }
-  float acc[NT];
-#pragma unroll
-  for (int j = 0; j < NT; j++) acc[j] = 0.f;
-  uint32_t row_local = 0;
-  if (p < nseg) {
-    row_local = p / spr;
-    const uint32_t k0 = (p % spr) * every;
-    if (tl.mode == 0) {  // stored tile: weights read directly
-      const uint8_t* wsrc = P.src + tl.src + size_t(p) * every * 2;
-      for (uint32_t c = lane * 8; c < every; c += 16) {
-        uint4 w;
-        uint32_t v[4];
-        for (int q = 0; q < 4; q++)
-          v[q] = uint32_t(wsrc[2 * (c + 2 * q)]) | (uint32_t(wsrc[2 * (c + 2 * q) + 1]) << 8) |
-                 (uint32_t(wsrc[2 * (c + 2 * q) + 2]) << 16) | (uint32_t(wsrc[2 * (c + 2 * q) + 3]) << 24);
-        w = make_uint4(v[0], v[1], v[2], v[3]);
-        dot8<NT>(w, act, ld, sh.tok, ntk, k0 + c, acc);
-      }
-    } else {
-      const uint32_t* ck = P.ckpt + P.ckpt_base[t];
-      PlaneRun r;
-      if (p == 0) {
-        plane_start(r, P.src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload, 0, 0,
-                    false);
-      } else {
-        plane_start(r, P.src, lane ? tl.high_freq : tl.low_freq, lane ? tl.high_payload : tl.low_payload,
-                    ck[(p - 1) * 4 + lane * 2], ck[(p - 1) * 4 + lane * 2 + 1], true);
-      }
-      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
-      const unsigned mask = 0x3u << (tid & 30u);
-      const bool degenerate = sh.degenerate[lane] != 0;
-      const bool last = (p + 1 == nseg);
-      const uint32_t x0 = r.x, c0 = r.cur;
-      auto landed = [&]() {
-        return last ? (r.cur == r.len) : (r.x == ck[p * 4 + lane * 2] && r.cur == ck[p * 4 + lane * 2 + 1]);
-      };
-      // Whole segment on the clamped window; a pair that does not land where
-      // the exact decoder did (a stream that runs out of bytes) redoes the
-      // segment on the exact path.
-      bool exact = (every & 15u) || !__all_sync(mask, !degenerate && win_can_open(r));
-      if (!exact) {
-        Window W;
-        win_open(W, r);
-        uint32_t x = r.x;
-        for (uint32_t done = 0; done < every; done += 16) {
-          uint32_t a[4];
-          win_decode16(lut_s, x, W, a);
-          const uint4 w = exchange_pair16(lane, a[0], a[1], a[2], a[3], mask);
-          dot8<NT>(w, act, ld, sh.tok, ntk, k0 + done + 8 * lane, acc);
-        }
-        r.x = x;
-        r.cur = win_cur(W);
-        if (__any_sync(mask, !landed())) {
-          exact = true;
-          r.x = x0;
-          r.cur = c0;
-#pragma unroll
-          for (int j = 0; j < NT; j++) acc[j] = 0.f;
-        }
-      }
-      if (exact) {  // lockstep pair: both planes decode `every` symbols
-        for (uint32_t done = 0; done < every; done++) {
-          const uint32_t s = rans_step_exact(lut_s, degenerate, r);
-          const uint32_t o = __shfl_xor_sync(mask, s, 1);
-          if (lane == 0) {
-            const float w = bf2f(s | (o << 8));
-#pragma unroll
-            for (int j = 0; j < NT; j++)
-              if (j < int(ntk)) acc[j] = fmaf(w, bf2f(act[size_t(sh.tok[j]) * ld + k0 + done]), acc[j]);
-          }
-        }
-        if (!landed()) atomicOr(&sh.status, 1u);
-      }
-    }
-  }
-  // pair reduce, then rows meet in shared memory
-#pragma unroll
-  for (int j = 0; j < NT; j++) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 1);
-  if (p < nseg && lane == 0) {
-#pragma unroll
-    for (int j = 0; j < NT; j++)
-      if (j < int(ntk)) atomicAdd(&sh.acc[slot][row_local][j], acc[j]);
-  }
-  __syncthreads();
-}
-
-// Bit 2 of the status word: an expert has more route rows than the grid's
-// token groups cover (more tokens than T for one expert).
-constexpr uint32_t kStatusRoutes = 2u;
-
-template <int NT>
-__device__ __forceinline__ bool setup_tokens(GemvShared& sh, const Routes* R, uint32_t u, uint32_t grp,
-                                             uint32_t* ntk_out, uint32_t* status) {
-  if (u >= R->n_unique) return false;
-  const uint32_t n = R->ntok[u];
-  if (threadIdx.x == 0 && blockIdx.x == 0 && grp == 0 && n > gridDim.z * NT) atomicOr(status, kStatusRoutes);
-  if (grp * NT >= n) return false;
-  const uint32_t ntk = min(uint32_t(NT), n - grp * NT);
-  if (threadIdx.x < NT)
-    sh.tok[threadIdx.x] = threadIdx.x < ntk ? R->upair[R->uoff[u] + grp * NT + threadIdx.x] : 0;
-  *ntk_out = ntk;
-  return true;
-}
-
-// One gate or up tile of one routed expert (blockIdx.x = 2 * tile + proj) ->
-// BF16 rows g (gate) or u (up) per token; moe_act combines them.  NT = tokens
-// per CTA (1, 2, 4 or 8): registers scale with it.
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 4) moe_gate_up(const voom_expert_pages* __restrict__ pages,
-                                                           const Routes* __restrict__ R,
-                                                           const uint16_t* __restrict__ h, uint32_t H, uint32_t I,
-                                                           uint16_t* __restrict__ g_out,
-                                                           uint16_t* __restrict__ u_out, uint32_t* status) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
-  const uint32_t t = blockIdx.x >> 1, proj = blockIdx.x & 1u, u = blockIdx.y, grp = blockIdx.z;
-  uint32_t ntk;
-  if (!setup_tokens<NT>(sh, R, u, grp, &ntk, status)) return;
-  const voom_expert_pages& E = pages[R->expert[u]];
-  const voom_expert_proj& P = proj ? E.up : E.gate;
-  if (t >= P.n_tiles) return;
-  for (int i = threadIdx.x; i < 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
-  if (threadIdx.x == 0) sh.status = 0;
-  __syncthreads();
-  gemv_tile<NT>(sh, P, t, 0, h, H, ntk);
-  const voom_rans_tile tl = P.tiles[t];
-  const uint32_t rows = tl.raw_len / (2u * H), row0 = uint32_t(tl.dst / (2u * H));
-  uint16_t* out = proj ? u_out : g_out;
-  for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
-    const uint32_t row = q / ntk, j = q % ntk;
-    out[size_t(R->uoff[u] + grp * NT + j) * I + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
-  }
-  if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
-}
-
 // SwiGLU of the route rows, in place over g: a = bf16(bf16(bf16(sigmoid(g)) * g) * u)
 // (layer_runner.py _swiglu :185-190).  8 columns per thread.
 __global__ void moe_act(const Routes* __restrict__ R, uint16_t* __restrict__ g, const uint16_t* __restrict__ up,
@@ -587,34 +367,6 @@ __global__ void moe_act(const Routes* __restrict__ R, uint16_t* __restrict__ g, 
     o[q] = r;
   }
   *gp = make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// down tile of one routed expert -> y rows (BF16) per token.
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 4) moe_down(const voom_expert_pages* __restrict__ pages,
-                                                        const Routes* __restrict__ R,
-                                                        const uint16_t* __restrict__ act, uint32_t H, uint32_t I,
-                                                        uint16_t* __restrict__ y_out, uint32_t* status) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  GemvShared& sh = *reinterpret_cast<GemvShared*>(smem_raw);
-  const uint32_t t = blockIdx.x, u = blockIdx.y, grp = blockIdx.z;
-  uint32_t ntk;
-  if (!setup_tokens<NT>(sh, R, u, grp, &ntk, status)) return;
-  const voom_expert_pages& E = pages[R->expert[u]];
-  if (t >= E.down.n_tiles) return;
-  // the down projection reads this expert's activation rows
-  if (threadIdx.x < NT) sh.tok[threadIdx.x] = R->uoff[u] + grp * NT + threadIdx.x;
-  for (int i = threadIdx.x; i < 128 * kTok; i += kThreads) (&sh.acc[0][0][0])[i] = 0.f;
-  if (threadIdx.x == 0) sh.status = 0;
-  __syncthreads();
-  gemv_tile<NT>(sh, E.down, t, 0, act, I, ntk);
-  const voom_rans_tile tl = E.down.tiles[t];
-  const uint32_t rows = tl.raw_len / (2u * I), row0 = uint32_t(tl.dst / (2u * I));
-  for (uint32_t q = threadIdx.x; q < rows * ntk; q += kThreads) {
-    const uint32_t row = q / ntk, j = q % ntk;
-    y_out[size_t(R->uoff[u] + grp * NT + j) * H + row0 + row] = uint16_t(f2bf(sh.acc[0][row][j]));
-  }
-  if (threadIdx.x == 0 && sh.status) atomicOr(status, 1u);
 }
 
 // out[t] = ordered BF16 sum over the token's routes of the contribution
@@ -665,37 +417,60 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
 }
 
 
+// gate/up, activation, then down for every routed expert.  Experts with at
+// most kTok tokens run on moe_proj_cc (NT picked from max_tok, the most
+// tokens one expert can have); when max_tok > kTok the experts with more
+// tokens run on moe_proj_mma (tensor cores), each page block decoded once.
+// ubuf holds max_rows x I.
 template <int NT>
-int launch_gemv_nt(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
-                   uint16_t* ubuf, uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique,
-                   uint32_t max_rows, uint32_t gate_tiles, uint32_t down_tiles, uint32_t* d_status,
-                   cudaStream_t st) {
-  const uint32_t groups = (T + NT - 1) / NT;
-  const size_t smem = sizeof(GemvShared);
-  if (cudaFuncSetAttribute(moe_gate_up<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
-          cudaSuccess ||
-      cudaFuncSetAttribute(moe_down<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+int launch_cc(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in, uint32_t ld_in,
+              uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t nbpp, uint32_t nblocks, uint32_t n_unique,
+              uint32_t mma_on, uint32_t* d_status, cudaStream_t st) {
+  const size_t smem = sizeof(CcShared);
+  if (cudaFuncSetAttribute(moe_proj_cc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return VOOM_E_CUDA;
-  moe_gate_up<NT><<<dim3(2 * gate_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, h, H, I, act, ubuf,
-                                                                                   d_status);
-  moe_act<<<dim3((I / 8 + 127) / 128, max_rows), 128, 0, st>>>(R, act, ubuf, I);
-  moe_down<NT><<<dim3(down_tiles, n_unique, groups), kThreads, smem, st>>>(d_pages, R, act, H, I, y, d_status);
+  moe_proj_cc<NT><<<dim3(nblocks, n_unique, 1), kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1,
+                                                                       ld_out, nbpp, mma_on, d_status);
   return VOOM_OK;
 }
 
-// gate/up, activation, then down for every routed expert; tokens per CTA
-// chosen from T (an expert sees at most T tokens).  ubuf holds max_rows x I.
+int launch_proj(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in,
+                uint32_t ld_in, uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t rows, uint32_t cols,
+                uint32_t n_proj, uint32_t n_unique, uint32_t max_tok, uint32_t* d_status, cudaStream_t st) {
+  const uint32_t mma_on = max_tok > uint32_t(kTok) ? 1u : 0u;
+  const uint32_t nbpp = (rows + cc_rows(cols) - 1) / cc_rows(cols);
+  int rc;
+  if (max_tok <= 1)
+    rc = launch_cc<1>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+                      d_status, st);
+  else if (max_tok <= 2)
+    rc = launch_cc<2>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+                      d_status, st);
+  else if (max_tok <= 4)
+    rc = launch_cc<4>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+                      d_status, st);
+  else
+    rc = launch_cc<8>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+                      d_status, st);
+  if (rc != VOOM_OK || !mma_on) return rc;
+  const uint32_t ncap = (min(max_tok, kMmaMaxN) + 15u) & ~15u;
+  const uint32_t zc = (max_tok + kMmaMaxN - 1) / kMmaMaxN;
+  const uint32_t smem = mma_smem_bytes(ncap);
+  if (cudaFuncSetAttribute(moe_proj_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return VOOM_E_CUDA;
+  const uint32_t nbm = (rows + kMmaRows - 1) / kMmaRows;
+  moe_proj_mma<<<dim3(n_proj * nbm, n_unique, zc), kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1,
+                                                                          ld_out, nbm, ncap, d_status);
+  return VOOM_OK;
+}
+
 int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
-                uint16_t* ubuf, uint16_t* y, uint32_t T, uint32_t H, uint32_t I, uint32_t n_unique,
-                uint32_t max_rows, uint32_t gate_tiles, uint32_t down_tiles, uint32_t* d_status, cudaStream_t st) {
-#define VOOM_GEMV(NT)                                                                                         \
-  launch_gemv_nt<NT>(d_pages, R, h, act, ubuf, y, T, H, I, n_unique, max_rows, gate_tiles, down_tiles, d_status, \
-                     st)
-  if (T == 1) return VOOM_GEMV(1);
-  if (T == 2) return VOOM_GEMV(2);
-  if (T <= 4) return VOOM_GEMV(4);
-  return VOOM_GEMV(8);
-#undef VOOM_GEMV
+                uint16_t* ubuf, uint16_t* y, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t max_rows,
+                uint32_t max_tok, uint32_t* d_status, cudaStream_t st) {
+  int rc = launch_proj(d_pages, R, 0, h, H, act, ubuf, I, I, H, 2, n_unique, max_tok, d_status, st);
+  if (rc != VOOM_OK) return rc;
+  moe_act<<<dim3((I / 8 + 127) / 128, max_rows), 128, 0, st>>>(R, act, ubuf, I);
+  return launch_proj(d_pages, R, 1, act, I, y, y, H, H, I, 1, n_unique, max_tok, d_status, st);
 }
 
 // The generic family with no shared expert: what the variant-less entry
@@ -766,7 +541,7 @@ int moe_layer_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages, 
   float* logits = reinterpret_cast<float*>(s + L.logits);
   launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
   const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
-  rc = launch_gemv(d_pages, R, h, act, y, y, T, H, I, max_unique, T * rpt, gate_tiles, down_tiles, d_status, st);
+  rc = launch_gemv(d_pages, R, h, act, y, y, H, I, max_unique, T * rpt, T, d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
@@ -792,8 +567,7 @@ int moe_experts_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages
   launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
   const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
   uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
-  rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, T, H, I, max_unique, T * rpt, gate_tiles, down_tiles, d_status,
-                   st);
+  rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, H, I, max_unique, T * rpt, T, d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
@@ -928,6 +702,7 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
     return VOOM_E_INVALID_ARG;
   if (T == 0 || n_unique == 0 || n_rows == 0 || n_rows > kMaxTK || n_unique > n_rows || H % 8 || I % 8)
     return VOOM_E_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(d_h) & 15u) return VOOM_E_INVALID_ARG;  // rows are read 16 bytes at a time
   const ScratchLayout L = layout(n_rows, H, I, 1);
   if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
   uint8_t* s = static_cast<uint8_t*>(d_scratch);
@@ -941,8 +716,7 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
       cudaMemcpyAsync(&R->upair[0], d_upair, 4ull * n_rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return VOOM_E_CUDA;
   moe_route_offsets<<<1, 32, 0, st>>>(R, n_unique, T);
-  const int rc = launch_gemv(d_pages, R, d_h, act, ubuf, d_y, T, H, I, n_unique, n_rows, gate_tiles, down_tiles,
-                             d_status, st);
+  const int rc = launch_gemv(d_pages, R, d_h, act, ubuf, d_y, H, I, n_unique, n_rows, min(T, n_rows), d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

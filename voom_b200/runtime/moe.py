@@ -25,7 +25,6 @@ from .. import _device
 from .._lib import check, load
 from ..formats import bf16_rans
 
-EVERY = 256
 PROJ_DTYPE = np.dtype([("src", "<u8"), ("tiles", "<u8"), ("ckpt", "<u8"), ("ckpt_base", "<u8"),
                        ("n_tiles", "<u4"), ("every", "<u4"), ("rows", "<u4"), ("cols", "<u4")])
 PAGES_DTYPE = np.dtype([("gate", PROJ_DTYPE), ("up", PROJ_DTYPE), ("down", PROJ_DTYPE)])
@@ -55,9 +54,9 @@ def raise_on_status(status: torch.Tensor, what: str) -> None:
 
 def every_for(cols: int, longest: int = 512) -> int:
     """Checkpoint interval for rows of `cols` elements: the longest power of
-    two <= `longest` (and >= 64) dividing the row, so each lane pair of the
-    fused kernels decodes one whole row segment.  Longer segments mean fewer
-    decode lanes and fewer decode-table builds per projection."""
+    two <= `longest` (and >= 64) dividing the row, so a lane pair of the
+    fused kernels decodes whole row segments.  The fused kernels size their
+    row blocks from this rule (every_rule in csrc/moe_proj.cuh)."""
     e = longest
     while e > 64 and cols % e:
         e //= 2
@@ -66,25 +65,29 @@ def every_for(cols: int, longest: int = 512) -> int:
     return e
 
 
-def tile_bytes_for(cols: int, every: int = EVERY, max_tile: int = 1 << 17) -> int:
-    """Tile size for a projection with rows of `cols` BF16: whole rows, at most
-    128 checkpoint segments and at most `max_tile` bytes per tile."""
-    if cols % every:
-        raise ValueError(f"row length {cols} is not a multiple of the checkpoint interval {every}")
-    row_bytes = 2 * cols
-    rows = max(1, min(128 // (cols // every), max_tile // row_bytes))
-    return rows * row_bytes
+def tile_bytes_for(cols: int, min_tile: int = 1 << 20) -> int:
+    """Tile size of a projection's VRN1 frame: the reference's default 1 MiB
+    (formats/bf16_rans.py:148), or the next power of two holding 128 rows when
+    rows are longer (2 MiB for rows of 6144, config 4's pages), so that a
+    block of 128 rows -- the tensor-core kernel's M -- spans at most two tiles."""
+    need = 128 * 2 * cols
+    t = min_tile
+    while t < need:
+        t *= 2
+    return t
 
 
 class ProjPage:
     """One expert projection as a resident compressed page."""
 
-    def __init__(self, w_bits: np.ndarray, device, every: int = EVERY, frame: bytes | None = None):
+    def __init__(self, w_bits: np.ndarray, device, every: int | None = None, frame: bytes | None = None,
+                 tile_bytes: int | None = None):
         rows, cols = w_bits.shape
         self.rows, self.cols = int(rows), int(cols)
+        every = every or every_for(self.cols)
         if frame is None:
             frame, _ = bf16_rans.encode(np.ascontiguousarray(w_bits).view(np.uint8),
-                                        tile_bytes=tile_bytes_for(cols, every))
+                                        tile_bytes=tile_bytes or tile_bytes_for(cols))
         self.page = bf16_rans.RansPage(frame, device=device, every=every)
         self.frame_bytes = len(frame)
 
@@ -100,19 +103,18 @@ class ExpertStore:
     `experts[e]` is (Wg, Wu, Wd) as BF16 bit arrays, or None for an expert whose
     pages live on another GPU (its table entry has zero tiles, so the fused
     kernels skip it).  `alias` maps an expert id to another expert whose pages it
-    shares (synthetic workloads that reuse one page set)."""
+    shares (tests that route many experts over a few page sets).  Every
+    projection is one VRN1 frame with tiles of `tile_bytes` (default
+    tile_bytes_for(cols)) and a checkpoint every every_for(cols) symbols."""
 
-    def __init__(self, experts: list, device, every: int | None = None, alias: dict[int, int] | None = None):
+    def __init__(self, experts: list, device, alias: dict[int, int] | None = None, tile_bytes: int | None = None):
         self.device = _device.require_cuda(device)
         alias = alias or {}
         self.pages: list = [None] * len(experts)
         for e, ws in enumerate(experts):
             if ws is not None and e not in alias:
                 g, u, d = ws
-                eg = every or every_for(g.shape[1])
-                ed = every or every_for(d.shape[1])
-                self.pages[e] = (ProjPage(g, self.device, eg), ProjPage(u, self.device, eg),
-                                 ProjPage(d, self.device, ed))
+                self.pages[e] = tuple(ProjPage(w, self.device, tile_bytes=tile_bytes) for w in (g, u, d))
         for e, src in alias.items():
             self.pages[e] = self.pages[src]
         first = next(ws for ws in experts if ws is not None)
