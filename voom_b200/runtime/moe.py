@@ -17,6 +17,7 @@ runtime/qwen35.py:584-638 (route + consume); runtime/quant.py:431-444.
 from __future__ import annotations
 
 import ctypes
+import threading
 
 import numpy as np
 import torch
@@ -81,14 +82,14 @@ class ProjPage:
     """One expert projection as a resident compressed page."""
 
     def __init__(self, w_bits: np.ndarray, device, every: int | None = None, frame: bytes | None = None,
-                 tile_bytes: int | None = None):
+                 tile_bytes: int | None = None, stream: torch.cuda.Stream | None = None):
         rows, cols = w_bits.shape
         self.rows, self.cols = int(rows), int(cols)
         every = every or every_for(self.cols)
         if frame is None:
             frame, _ = bf16_rans.encode(np.ascontiguousarray(w_bits).view(np.uint8),
                                         tile_bytes=tile_bytes or tile_bytes_for(cols))
-        self.page = bf16_rans.RansPage(frame, device=device, every=every)
+        self.page = bf16_rans.RansPage(frame, device=device, every=every, stream=stream)
         self.frame_bytes = len(frame)
 
     def record(self) -> tuple:
@@ -105,20 +106,47 @@ class ExpertStore:
     kernels skip it).  `alias` maps an expert id to another expert whose pages it
     shares (tests that route many experts over a few page sets).  Every
     projection is one VRN1 frame with tiles of `tile_bytes` (default
-    tile_bytes_for(cols)) and a checkpoint every every_for(cols) symbols."""
+    tile_bytes_for(cols)) and a checkpoint every every_for(cols) symbols.  A
+    weight may also be a callable returning the bit array (generated when its
+    page is built); `threads` > 1 builds pages concurrently."""
 
-    def __init__(self, experts: list, device, alias: dict[int, int] | None = None, tile_bytes: int | None = None):
+    def __init__(self, experts: list, device, alias: dict[int, int] | None = None, tile_bytes: int | None = None,
+                 threads: int = 1):
         self.device = _device.require_cuda(device)
         alias = alias or {}
         self.pages: list = [None] * len(experts)
+        todo = [(e, j, w) for e, ws in enumerate(experts) if ws is not None and e not in alias
+                for j, w in enumerate(ws)]
+        built: dict = {}
+        if threads > 1 and len(todo) > 1:
+            # encode + index many projections at once: a host thread and a
+            # stream each (a page's index build is a small cold decode)
+            from concurrent.futures import ThreadPoolExecutor
+
+            local = threading.local()
+
+            def one(item):
+                e, j, w = item
+                if not hasattr(local, "stream"):
+                    local.stream = torch.cuda.Stream(self.device)
+                with torch.cuda.stream(local.stream):  # the page's status read-back follows its decode
+                    pg = ProjPage(w() if callable(w) else w, self.device, tile_bytes=tile_bytes,
+                                  stream=local.stream)
+                local.stream.synchronize()
+                return (e, j), pg
+
+            with ThreadPoolExecutor(max_workers=threads) as pool:
+                built = dict(pool.map(one, todo))
+        else:
+            for e, j, w in todo:
+                built[(e, j)] = ProjPage(w() if callable(w) else w, self.device, tile_bytes=tile_bytes)
         for e, ws in enumerate(experts):
             if ws is not None and e not in alias:
-                g, u, d = ws
-                self.pages[e] = tuple(ProjPage(w, self.device, tile_bytes=tile_bytes) for w in (g, u, d))
+                self.pages[e] = tuple(built[(e, j)] for j in range(3))
         for e, src in alias.items():
             self.pages[e] = self.pages[src]
-        first = next(ws for ws in experts if ws is not None)
-        self.I, self.H = first[0].shape
+        first = next(t for t in self.pages if t is not None)
+        self.I, self.H = first[0].rows, first[0].cols
         tab = np.zeros(len(self.pages), dtype=PAGES_DTYPE)
         for i, trip in enumerate(self.pages):
             if trip is not None:
