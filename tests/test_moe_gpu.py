@@ -75,8 +75,8 @@ def test_corrupted_page_is_detected(small):
 
     store, ex, wr, nw = small
     gate = store.pages[5][0].page
-    t1 = gate.plan.tiles[1]
-    pos = int(t1["high_freq"]) + 512 + 4 + 200
+    t0 = gate.plan.tiles[-1]  # a byte in the middle of the high plane's payload
+    pos = int(t0["high_freq"]) + 512 + 4 + int(t0["high_payload"]) // 2
     gate.src[pos] ^= 0x5A
     try:
         with pytest.raises(ValueError):
