@@ -45,6 +45,20 @@ sys.path.insert(0, str(ROOT))
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo) and its logical cores."""
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{name}, {os.cpu_count()} logical cores"
+
+
 def profiled_traffic(workload: str):
     """DRAM bytes per step of `workload` from the committed ncu summaries
     (a `traffic_bytes_per_step <workload>: N` line under profiles/), or None."""
@@ -257,13 +271,27 @@ class C1Rans:
                 "l2": "flushed between steps (512 MiB write)"}
 
 
+def lpt_partition(sizes, world: int) -> list[list[int]]:
+    """Longest-processing-time split of items over `world` bins by size:
+    items by descending size (ties by index), each to the least-filled bin."""
+    bins = [[] for _ in range(world)]
+    fill = [0] * world
+    for k in sorted(range(len(sizes)), key=lambda k: (-sizes[k], k)):
+        r = min(range(world), key=lambda b: (fill[b], b))
+        bins[r].append(k)
+        fill[r] += sizes[k]
+    return [sorted(b) for b in bins]
+
+
 class C2Vpack:
     """Config 2: the vpack2 archive of a random-init SmolLM2-135M-shaped
     checkpoint (30 layers, hidden 576, intermediate 1536, 9/3 heads x 64,
     vocab 49152, every tensor BF16 N(0, 0.02)), packed as the reference packs
     it (hi plane zstd level 1 + raw lo plane per tensor, access order).  A step
-    decodes every body of the archive back to BF16 bytes in one batched GPU
-    decode."""
+    decodes every body of the archive back to BF16 bytes.  With N ranks the
+    bodies are split by compressed bytes (LPT); each rank decodes its share in
+    one batched GPU decode and an NCCL all-gather leaves the whole decoded
+    archive on every rank (the replicated-weights case)."""
 
     name = "c2_vpack2_smollm2_135m"
     data = "synthetic (seeded numpy): random-init SmolLM2-135M shapes, every tensor BF16 N(0, 0.02)"
@@ -271,7 +299,7 @@ class C2Vpack:
     unit = "GB/s"
     dtype = "u8"
 
-    def __init__(self, device, rank: int, layers: int = 30):
+    def __init__(self, device, rank: int, layers: int = 30, world: int = 1):
         import torch
         from concurrent.futures import ThreadPoolExecutor
 
@@ -281,6 +309,7 @@ class C2Vpack:
         self.torch = torch
         self.dev = device
         self.packed = packed
+        self.rank, self.world = rank, world
         specs = synthetic.smollm2_tensors(dict(synthetic.SMOLLM2_135M, layers=layers))
         if layers != 30:
             self.name = f"c2_vpack2_smollm2_135m_{layers}layers"
@@ -288,19 +317,24 @@ class C2Vpack:
 
         def make(spec):
             name, shape = spec
-            seed = zlib.crc32(name.encode()) ^ (rank * 7919)
-            bits = synthetic.bf16_normal(shape, 0.02, seed)
+            bits = synthetic.bf16_normal(shape, 0.02, zlib.crc32(name.encode()))
             head, body = packed.body_for("BF16", bits.view(np.uint8))
             return name, {"dtype": "BF16", "shape": list(shape), **head}, body, bits
 
-        with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as pool:
+        threads = max(2, (os.cpu_count() or 8) // max(1, world))
+        with ThreadPoolExecutor(max_workers=threads) as pool:
             items = list(pool.map(make, specs))
         order = packed2.access_order([n for n, _, _, _ in items])
         by = {n: (h, b, r) for n, h, b, r in items}
-        self.names = order
-        self.heads = [by[n][0] for n in order]
-        bodies = [by[n][1] for n in order]
+        self.all_names = order
         self.raws = {n: by[n][2] for n in order}
+        self.raw_bytes = sum(r.nbytes for r in self.raws.values())
+        self.archive_bytes = sum(len(by[n][1]) for n in order)
+        self.parts = lpt_partition([len(by[n][1]) for n in order], world)
+        mine = [order[k] for k in self.parts[rank]]
+        self.names = mine
+        self.heads = [by[n][0] for n in mine]
+        bodies = [by[n][1] for n in mine]
         self.offs, self.lens = [], []
         pos = 0
         for b in bodies:
@@ -311,42 +345,73 @@ class C2Vpack:
         self.pinned = _device.pinned_empty(self.archive.size)
         self.pinned.numpy()[:] = self.archive
         self.src = _device.upload(self.archive, device)
-        self.raw_bytes = sum(r.nbytes for r in self.raws.values())
-        # plan + output layout of the batched decode (built once: the archive index)
-        jobs, self.spans, dst = [], [], 0
-        for h, o, ln in zip(self.heads, self.offs, self.lens):
-            job, n = packed.body_job(h, o, ln, dst)
+        # each rank's decoded share in a slot of `cap` bytes of the gathered buffer
+        self.layout = {}
+        cap = 0
+        for r, part in enumerate(self.parts):
+            dst = 0
+            for k in part:
+                n = self.raws[order[k]].nbytes
+                self.layout[order[k]] = (r, dst, n)
+                dst += (n + 255) // 256 * 256
+            cap = max(cap, dst)
+        self.cap = cap
+        jobs, self.spans = [], []
+        for h, o, ln, name in zip(self.heads, self.offs, self.lens, mine):
+            _, d, _ = self.layout[name]
+            job, n = packed.body_job(h, o, ln, d)
             jobs.append(job)
-            self.spans.append((dst, n))
-            dst += (n + 255) // 256 * 256
+            self.spans.append((d, n))
         self.plan = zstd_gpu.ZstdPlan(self.archive, np.concatenate(jobs))
         self.batch = zstd_gpu.ZstdBatch(self.plan, device)
-        self.out = torch.empty(dst, dtype=torch.uint8, device=device)
-        self.units_per_step = self.raw_bytes
-        self.algo_bytes = self.archive.size + self.raw_bytes
+        self.out = torch.zeros(cap, dtype=torch.uint8, device=device)
+        self.full = torch.zeros(cap * world, dtype=torch.uint8, device=device) if world > 1 else self.out
+        self.units_per_step = self.raw_bytes  # the whole archive decoded (and replicated) per step
+        self.local_raw = sum(self.raws[n].nbytes for n in mine)
+        self.algo_bytes = self.archive.size + self.local_raw  # this rank's decode
+        self.gather_bytes = cap * (world - 1) if world > 1 else 0
         self.n_blocks = int(self.plan.info.n_blocks)
-        self.launches_per_step = 12  # K1 K1b K2 K3 6xK4 K5 K6
+        self.launches_per_step = 12  # K1 K1b K2 K3 6xK4 K5 K6 (+ the NCCL all-gather with N > 1)
+        self.scaling = "strong" if world > 1 else "weak"
+        self.replicated_units = True  # value = the one archive's bytes, not x N
+
+    def _gather(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.full, self.out)
 
     def step_device(self, stream_ptr: int):
         self.batch.run(self.src, self.out, self.torch.cuda.current_stream(self.dev))
+        self._mark = self.torch.cuda.Event(enable_timing=True)
+        self._mark.record()
+        self._gather()
 
     def verify(self) -> bool:
         if self.batch.job_status().any():
             return False
-        got = self.out.cpu().numpy()
-        for n, (d, ln) in zip(self.names, self.spans):
-            if not np.array_equal(got[d:d + ln], self.raws[n].reshape(-1).view(np.uint8)):
+        got = self.full.cpu().numpy()
+        for n, (r, d, ln) in self.layout.items():
+            o = r * self.cap + d if self.world > 1 else d
+            if not np.array_equal(got[o:o + ln], self.raws[n].reshape(-1).view(np.uint8)):
                 return False
         return True
 
     def step_e2e(self):
         out, spans = self.packed.decode_bodies(self.heads, self.pinned, self.offs, self.lens,
                                                device=self.dev, src_dev=None)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            part = self.out
+            for (d, n), (d2, _) in zip(spans, self.spans):
+                part[d2:d2 + n].copy_(out[d:d + n])
+            dist.all_gather_into_tensor(self.full, part)
         return self.archive.size, 4 * len(self.heads)
 
     def cpu_sample(self, threads: int, budget_s: float) -> dict:
         """The reference decode leg (decode_body: libzstd + numpy interleave per
-        body) over the archive, bodies spread over `threads` host threads,
+        body) over this rank's bodies, spread over `threads` host threads,
         repeated until `budget_s` of wall time."""
         from concurrent.futures import ThreadPoolExecutor
 
@@ -364,14 +429,18 @@ class C2Vpack:
                     done += r
         dt = time.perf_counter() - t0
         return {"value": done / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-                "sample": f"{done / self.raw_bytes:.2f} passes over the {len(items)}-body archive "
-                          f"({self.raw_bytes} B decoded per pass) with decode_body restated (libzstd + numpy) "
+                "cpu_model": cpu_model(),
+                "sample": f"{done / self.local_raw:.2f} passes over the {len(items)}-body archive "
+                          f"({self.local_raw} B decoded per pass) with decode_body restated (libzstd + numpy) "
                           f"on {threads} thread(s), {dt:.1f} s"}
 
     def config(self) -> dict:
-        return {"workload": self.name, "tensors": len(self.names), "zstd_blocks": self.n_blocks,
-                "archive_bytes": int(self.archive.size), "raw_bytes": int(self.raw_bytes),
-                "ratio": round(self.raw_bytes / self.archive.size, 4), "zstd_level": 1,
+        return {"workload": self.name, "tensors": len(self.all_names), "zstd_blocks_this_rank": self.n_blocks,
+                "archive_bytes": int(self.archive_bytes), "raw_bytes": int(self.raw_bytes),
+                "ratio": round(self.raw_bytes / self.archive_bytes, 4), "zstd_level": 1,
+                "parallelism": (f"partition x{self.world}: bodies split by compressed bytes (LPT), NCCL "
+                                f"all-gather of the decoded bodies inside the step" if self.world > 1 else "single"),
+                "bodies_this_rank": len(self.names), "archive_bytes_this_rank": int(self.archive.size),
                 "l2": "flushed between steps (512 MiB write); inputs 184 MB + output 269 MB exceed L2"}
 
 
@@ -390,9 +459,10 @@ class C3Moe:
     unit = "tok/s"
     dtype = "bf16"
 
-    def __init__(self, device, rank: int, tokens: int = 1, layers: int = 48):
+    def __init__(self, device, rank: int, tokens: int = 1, layers: int = 48, store=None):
         import torch
 
+        from voom_b200 import synthetic
         from voom_b200.runtime import moe
 
         self.torch = torch
@@ -401,16 +471,16 @@ class C3Moe:
         self.L = layers
         self.name = f"c3_moe_h2048_e128_i768_top8_T{tokens}_L{layers}"
         E, H, I = 128, 2048, 768
-        g = torch.Generator().manual_seed(4242 + rank)
+        g = torch.Generator().manual_seed(4242)
 
-        def bits(t):
-            return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+        def weight(e, j):
+            shape = (I, H) if j < 2 else (H, I)
+            return lambda: synthetic.bf16_normal(shape, 0.02, 90_000 + 3 * e + j)
 
-        experts = []
-        for _ in range(E):
-            experts.append(tuple(bits((torch.randn(sh, generator=g) * 0.02).to(torch.bfloat16))
-                                 for sh in ((I, H), (I, H), (H, I))))
-        self.store = moe.ExpertStore(experts, device)
+        experts = [tuple(weight(e, j) for j in range(3)) for e in range(E)]
+        if store is None:
+            store = moe.ExpertStore(experts, device, threads=max(2, os.cpu_count() or 8))
+        self.store = store
         self.layers = []
         for _ in range(layers):
             wr = torch.randn((E, H), generator=g).to(torch.bfloat16).to(device)
@@ -459,7 +529,13 @@ class C3Moe:
         torch = self.torch
         layer = self.layers[0]
         out = layer(self.x0, residual=False).cpu()
-        ex = [tuple(torch.from_numpy(w.view(np.int16)).view(torch.bfloat16) for w in e) for e in self.experts_raw]
+        raw = self.experts_raw
+
+        class Lazy:  # the oracle reads only the routed experts
+            def __getitem__(self, e):
+                return tuple(torch.from_numpy(w().view(np.int16)).view(torch.bfloat16) for w in raw[e])
+
+        ex = Lazy()
         ref = om.moe_layer(self.x0.cpu(), layer.router_w.cpu(), layer.norm_w.cpu(), ex, 8, True, residual=False)
         ok = om.rel_l2(out, ref) < 1e-2 and all(int(l.status.item()) == 0 for l in self.layers)
         # the replayed graph computes exactly the eager 48-layer stack
@@ -517,108 +593,219 @@ class C3Moe:
 
 
 class C4MoeEP:
-    """Config 4: one large-MoE layer step -- hidden 6144, 160 experts with
-    intermediate 2048 (BF16 N(0, 0.015)) as rANS-coded pages, top-8 routing,
-    expert popularity Zipf(1.1) (seeded permutation) placed over the ranks by
-    LPT, T tokens (`--tokens`), expert outputs combined with one NCCL
-    all-reduce over NVLink.  Each rank encodes `distinct` real page sets and
-    its other experts alias them (identical decode work, smaller setup); the
-    router is biased by log-popularity so routing follows the Zipf law.
-    Metric: tokens per second of the layer step (whole job)."""
+    """Config 4: the large-MoE layer sharded over the ranks -- hidden 6144, 160
+    distinct experts with intermediate 2048 (BF16 N(0, 0.015)), each
+    projection a VRN1 frame of 2 MiB pages (12 per projection) with a
+    checkpoint index, top-8 softmax routing whose expert popularity follows
+    Zipf(1.1) (router logits biased by 4 log p over a seeded permutation of
+    ranks), T tokens per step.  Expert parallel: every rank routes all tokens,
+    runs the fused decode + SwiGLU of its own experts (placed by LPT over the
+    expected decode cost of the T values timed), one NCCL all-reduce sums the
+    route rows, every rank combines.  A step runs `layers` layers (one router
+    each) over the same expert set, the configuration's single layer; the
+    metric is tokens per second through one layer (T x layers / step time)."""
 
     metric = "fused expert GEMV tok/s through one MoE layer (expert parallel)"
     unit = "tok/s"
     dtype = "bf16"
-    data = "synthetic (seeded torch): experts BF16 N(0, 0.015), Zipf(1.1) expert popularity"
+    data = ("synthetic (seeded numpy/torch): 160 distinct experts BF16 N(0, 0.015) in 2 MiB rANS pages, "
+            "router N(0, 0.02) + 4 log Zipf(1.1) popularity bias, tokens N(0, 1)")
+    E, H, I, K = 160, 6144, 2048, 8
+    PAGE = 2 << 20
 
-    def __init__(self, device, rank: int, tokens: int = 8, world: int = 1, layers: int = 8, distinct: int = 8):
+    def __init__(self, device, rank: int, world: int = 1, tokens=(1, 8, 64), layers: int = 4):
         import torch
 
+        from voom_b200 import synthetic
         from voom_b200.runtime import moe
 
         self.torch = torch
         self.dev = device
-        self.T = tokens
-        self.name = f"c4_moe_ep_h6144_e160_i2048_top8_T{tokens}_x{world}"
-        E, H, I = 160, 6144, 2048
-        pop = moe.zipf_popularity(E, 1.1, seed=11)
-        self.owned = moe.place_experts(pop, world)[rank]
-        g = torch.Generator().manual_seed(777 + rank)
-
-        def bits(t):
-            return t.contiguous().view(torch.int16).numpy().view(np.uint16)
-
-        base = [tuple(bits((torch.randn(sh, generator=g) * 0.015).to(torch.bfloat16))
-                      for sh in ((I, H), (I, H), (H, I))) for _ in range(min(distinct, len(self.owned)))]
-        experts: list = [None] * E
-        alias = {}
-        for j, e in enumerate(self.owned):
-            if j < len(base):
-                experts[e] = base[j]
-            else:
-                experts[e] = base[0]
-                alias[e] = self.owned[j % len(base)]
-        self.store = moe.ExpertStore(experts, device, alias=alias)
-        gr = torch.Generator().manual_seed(4242)  # identical router on every rank
-        logp = torch.from_numpy(np.log(pop)).float()
-        self.layers = []
-        for _ in range(layers):
-            wr = (torch.randn((E, H), generator=gr) * 0.02).to(torch.bfloat16).to(device)
-            nw = (1.0 + 0.05 * torch.randn(H, generator=gr)).to(torch.bfloat16).to(device)
-            self.layers.append(moe.ExpertParallelMoeLayer(self.store, wr, nw, top_k=8,
-                                                          router_bias=(4.0 * logp).to(device)))
-        self.x0 = torch.randn((tokens, H), generator=gr).to(torch.bfloat16).to(device)
-        self.bufs = [torch.empty_like(self.x0) for _ in range(2)]
-        self.x_host = self.x0.cpu().pin_memory()
-        self.y_host = torch.empty_like(self.x_host).pin_memory()
-        self.units_per_step = tokens * layers  # token-layers: value = tok/s through one layer
-        self.replicated_units = True  # every rank serves the same tokens: no x world
-        self.scaling = "strong"
+        self.rank, self.world = rank, world
         self.L = layers
-        self.algo_bytes = 1  # replaced after the first step (routed local pages)
-        self.launches_per_step = 7 * layers  # router logits, top-k, plan, gate/up, act, down, combine (+ NCCL)
+        E, H, I = self.E, self.H, self.I
+        self.pop = moe.zipf_popularity(E, 1.1, seed=11)
+        gr = torch.Generator().manual_seed(4242)  # identical routers on every rank
+        logp = torch.from_numpy(np.log(self.pop)).float()
+        self.bias = (4.0 * logp).to(device)
+        self.routers = []
+        for _ in range(layers):
+            wr = (torch.randn((E, H), generator=gr) * 0.02).to(torch.bfloat16)
+            nw = (1.0 + 0.05 * torch.randn(H, generator=gr)).to(torch.bfloat16)
+            self.routers.append((wr, nw))
+        self.cost = self._expected_cost(tokens)
+        self.placement = moe.place_experts(self.cost, world)
+        self.owned = self.placement[rank]
 
-    def _run(self, x):
-        cur = x
-        for i, layer in enumerate(self.layers):
-            out = self.bufs[i % 2]
-            layer(cur, out=out)
-            cur = out
-        return cur
+        def weight(e, j):
+            shape = (I, H) if j < 2 else (H, I)
+            return lambda: synthetic.bf16_normal(shape, 0.015, 50_000 + 3 * e + j)
 
-    def step_device(self, stream_ptr: int):
-        self._run(self.x0)
-        if self.algo_bytes <= 1:
-            torch = self.torch
-            torch.cuda.synchronize()
-            per_expert = self.store.compressed_bytes / max(1, len({id(t) for t in self.store.pages if t}))
-            owned = set(self.owned)
-            n = 0
-            for layer in self.layers:
-                words = layer._scratch[self.T][:16 + 4 * 512].view(torch.int32).cpu().numpy()
-                nu = int(words[0])
-                n += sum(1 for e in words[4:4 + nu] if int(e) in owned)
-            self.local_routed = n
-            self.algo_bytes = int(n * per_expert + 2 * 2 * self.T * 6144 * self.L)
+        table = [None] * E
+        for e in self.owned:
+            table[e] = tuple(weight(e, j) for j in range(3))
+        threads = max(2, (os.cpu_count() or 8) // max(1, world))
+        t0 = time.perf_counter()
+        self.store = moe.ExpertStore(table, device, tile_bytes=self.PAGE, threads=threads)
+        self.setup_s = time.perf_counter() - t0
+        self.expert_bytes = {e: sum(p.frame_bytes for p in self.store.pages[e]) for e in self.owned}
+        self.layers = [moe.ExpertParallelMoeLayer(self.store, wr.to(device), nw.to(device), top_k=self.K,
+                                                  router_bias=self.bias) for wr, nw in self.routers]
 
-    def verify(self) -> bool:
-        return all(int(l.status.item()) == 0 for l in self.layers)
+    def _expected_cost(self, tokens) -> np.ndarray:
+        """Expected page decodes per expert and step, averaged over the timed T
+        values: 1 - (1 - q_e)^T with q_e the probability that a token routes to
+        expert e, estimated with the routers on 2048 random tokens (host)."""
+        torch = self.torch
+        from oracle import moe as om
 
-    def step_e2e(self):
-        x = self.x_host.to(self.dev, non_blocking=True)
-        y = self._run(x)
-        self.y_host.copy_(y, non_blocking=True)
-        return self.T * 6144 * 2, self.T * 6144 * 2
+        g = torch.Generator().manual_seed(99)
+        x = torch.randn((2048, self.H), generator=g).to(torch.bfloat16)
+        q = np.zeros(self.E)
+        for wr, nw in self.routers:
+            h = om.rms_norm(x, nw, 1e-6)
+            idx, _ = om.route(h, wr, self.K, True, bias=self.bias.cpu())
+            q += np.bincount(idx.reshape(-1).numpy(), minlength=self.E) / x.shape[0]
+        q = np.clip(q / len(self.routers), 0.0, 1.0)
+        return np.mean([1.0 - (1.0 - q) ** T for T in tokens], axis=0)
 
-    def cpu_sample(self, threads: int, budget_s: float) -> dict:
-        return {"value": None, "unit": "tok/s", "cores": threads, "kind": "port",
-                "sample": "not sampled for config 4 (see c3_moe for the CPU port of the same layer math)"}
+    def for_tokens(self, T: int) -> "C4Step":
+        return C4Step(self, T)
 
     def config(self) -> dict:
-        return {"workload": self.name, "tokens": self.T, "layers": self.L, "experts": 160, "hidden": 6144,
-                "intermediate": 2048, "top_k": 8, "local_experts": len(self.owned),
-                "popularity": "Zipf(1.1), LPT placement", "combine": "NCCL all-reduce of expert rows",
-                "l2": "flushed between steps (512 MiB write)"}
+        raw = self.store.raw_bytes
+        return {"workload": f"c4_moe_ep_h6144_e160_i2048_top8_x{self.world}", "experts": self.E,
+                "distinct_experts": self.E, "hidden": self.H, "intermediate": self.I, "top_k": self.K,
+                "page_bytes": self.PAGE, "layers_per_step": self.L,
+                "layer_note": "one expert set (config 4's single layer) under `layers_per_step` routers",
+                "local_experts": len(self.owned), "local_page_bytes_compressed": int(self.store.compressed_bytes),
+                "local_page_bytes_raw": int(raw), "ratio": round(raw / max(1, self.store.compressed_bytes), 4),
+                "popularity": "Zipf(1.1) over a seeded permutation, router bias 4 log p",
+                "placement": "LPT over expected page decodes per step (mean over the timed T)",
+                "experts_per_rank": [len(b) for b in self.placement],
+                "combine": "NCCL all-reduce of the BF16 route rows (one nonzero contributor per row), "
+                           "ordered BF16 combine on every rank",
+                "page_build_s": round(self.setup_s, 2),
+                "l2": "flushed between steps (512 MiB write); the page set exceeds L2"}
+
+
+class C4Step:
+    """One T of the config-4 sweep over a built C4MoeEP."""
+
+    unit = "tok/s"
+
+    def __init__(self, c4: C4MoeEP, T: int):
+        torch = c4.torch
+        self.c4, self.T, self.torch = c4, T, torch
+        gx = torch.Generator().manual_seed(7000 + T)  # identical tokens on every rank
+        x = torch.randn((T, c4.H), generator=gx).to(torch.bfloat16)
+        self.x0 = x.to(c4.dev)
+        self.bufs = [torch.empty_like(self.x0) for _ in range(2)]
+        self.x_host = x.pin_memory()
+        self.y_host = torch.empty_like(self.x_host).pin_memory()
+        self.units_per_step = T * c4.L
+        self.algo_bytes = None
+        self.launches_per_step = 9 * c4.L  # router logits, top-k, plan, 2x gate/up, act, 2x down, combine
+        self.nccl_ms = 0.0
+
+    def _run(self, x, timing: bool = False):
+        cur = x
+        ev = []
+        for i, layer in enumerate(self.c4.layers):
+            out = self.bufs[i % 2]
+            if timing and self.c4.world > 1:
+                a, b = self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True)
+                y = layer.experts(cur)
+                a.record()
+                import torch.distributed as dist
+
+                dist.all_reduce(y, op=dist.ReduceOp.SUM)
+                b.record()
+                layer.combine(cur, y, out)
+                ev.append((a, b))
+            else:
+                layer(cur, out=out)
+            cur = out
+        return cur, ev
+
+    def step_device(self, stream_ptr: int):
+        _, ev = self._run(self.x0, timing=True)
+        self._ev = ev
+        if self.algo_bytes is None:
+            self._count_bytes()
+
+    def collective_ms(self) -> float:
+        self.torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in getattr(self, "_ev", []))
+
+    def _count_bytes(self):
+        """Compressed bytes of this rank's routed experts over the step's layers
+        (read from the route tables) + the activations in and out."""
+        torch = self.torch
+        torch.cuda.synchronize()
+        owned = set(self.c4.owned)
+        n_local, byt, distinct = 0, 0, []
+        for layer in self.c4.layers:
+            s, _ = layer.buffers(self.T)
+            words = s[:16 + 4 * 520].view(torch.int32).cpu().numpy()
+            nu = int(words[0])
+            ex = [int(e) for e in words[4:4 + nu]]
+            distinct.append(nu)
+            mine = [e for e in ex if e in owned]
+            n_local += len(mine)
+            byt += sum(self.c4.expert_bytes[e] for e in mine)
+        self.local_routed = n_local
+        self.distinct_per_layer = distinct
+        self.algo_bytes = int(byt + 2 * 2 * self.T * self.c4.H * self.c4.L)
+
+    def verify(self) -> bool:
+        for layer in self.c4.layers:
+            layer.check_status()
+        return True
+
+    def step_e2e(self):
+        x = self.x_host.to(self.c4.dev, non_blocking=True)
+        y, _ = self._run(x)
+        self.y_host.copy_(y, non_blocking=True)
+        return self.T * self.c4.H * 2, self.T * self.c4.H * 2
+
+    def cpu_sample(self, threads: int, budget_s: float) -> dict:
+        """The reference's CPU path for one layer at this T: decode the routed
+        experts' rANS pages with the C oracle (one page per thread) and run the
+        layer math in torch-CPU (the oracle restatement of run_moe_mlp); rank 0
+        of a single-GPU run holds every expert."""
+        torch = self.torch
+        from concurrent.futures import ThreadPoolExecutor
+
+        from oracle import moe as om
+        from oracle import rans as orans
+
+        torch.set_num_threads(threads)
+        wr, nw = self.c4.routers[0]
+        x = self.x0.cpu()
+        bias = self.c4.bias.cpu()
+        pages = self.c4.store.pages
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or done == 0:
+            h = om.rms_norm(x, nw, 1e-6)
+            idx, _ = om.route(h, wr, self.c4.K, True, bias=bias)
+            need = sorted({int(e) for e in idx.flatten()})
+            jobs = [(e, j) for e in need for j in range(3)]
+
+            def dec(item):
+                p = pages[item[0]][item[1]]
+                raw = np.frombuffer(orans.decode(bytes(p.page.src[:p.frame_bytes].cpu().numpy())), np.int16)
+                return item, torch.from_numpy(raw.reshape(p.rows, p.cols).copy()).view(torch.bfloat16)
+
+            with ThreadPoolExecutor(max_workers=threads) as pool:
+                got = dict(pool.map(dec, jobs))
+            ex = {e: tuple(got[(e, j)] for j in range(3)) for e in need}
+            om.moe_layer(x, wr, nw, ex, self.c4.K, True, bias=bias)
+            done += 1
+        dt = time.perf_counter() - t0
+        return {"value": self.T * done / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"{done} layer(s) of T={self.T}: C-oracle rANS decode of the routed experts' pages "
+                          f"({threads} threads) + torch-CPU layer math, {dt:.1f} s"}
 
 
 class C5Nf12:
@@ -995,93 +1182,127 @@ def dist_init():
     return world, rank, local
 
 
+def _ref_archive(layers: int):
+    """Config 2's vpack bodies built with numpy and libzstd only (through the
+    oracle), so the reference arm maps none of this repository's libraries:
+    the same tensors (seeded by name), the reference's body layout (hi plane
+    zstd level 1, then the raw lo plane, formats/packed.py:125-358)."""
+    import zlib
+
+    from oracle import vpack as ov
+
+    h, i, hd, vocab = 576, 1536, 64, 49152
+    q, kv = 9 * hd, 3 * hd
+    specs = [("model.embed_tokens.weight", (vocab, h))]
+    for layer in range(layers):
+        p = f"model.layers.{layer}."
+        specs += [(p + "input_layernorm.weight", (h,)), (p + "self_attn.q_proj.weight", (q, h)),
+                  (p + "self_attn.k_proj.weight", (kv, h)), (p + "self_attn.v_proj.weight", (kv, h)),
+                  (p + "self_attn.o_proj.weight", (h, q)), (p + "post_attention_layernorm.weight", (h,)),
+                  (p + "mlp.gate_proj.weight", (i, h)), (p + "mlp.up_proj.weight", (i, h)),
+                  (p + "mlp.down_proj.weight", (h, i))]
+    specs.append(("model.norm.weight", (h,)))
+
+    def make(spec):
+        name, shape = spec
+        rng = np.random.default_rng(zlib.crc32(name.encode()))
+        x = rng.standard_normal(size=shape, dtype=np.float32) * np.float32(0.02)
+        u = x.view(np.uint32)
+        bits = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+        a = bits.reshape(-1).view(np.uint8)
+        hi_z = ov.zstd_compress(a[1::2].tobytes(), 1)
+        return {"dtype": "BF16", "shape": list(shape), "hi_z": len(hi_z), "lo": a.size // 2}, hi_z + a[0::2].tobytes(), bits
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=os.cpu_count() or 4) as pool:
+        return list(pool.map(make, specs))
+
+
+def _ref_decoder():
+    """The reference's own formats.packed2.decode_body when a reference checkout
+    is present (its compression.zstd import served by the ctypes shim over
+    libzstd kept with the test fixtures), else the oracle's restatement."""
+    sys.path.insert(0, str(ROOT))
+    from tests.reference_checkout import reference_root
+
+    root = reference_root()
+    if root is not None:
+        shim = str(ROOT / "tests" / "golden" / "_shim")
+        for pth in (shim, str(root)):
+            if pth not in sys.path:
+                sys.path.insert(0, pth)
+        import importlib
+
+        mod = importlib.import_module("formats.packed2")
+        return mod.decode_body, "reference", "formats/packed2.py decode_body of the reference checkout"
+    from oracle import vpack as ov
+
+    return ov.decode_body, "port", "oracle/vpack.py decode_body (restatement of formats/packed2.py:178-191)"
+
+
 def run_reference(args, world, rank):
-    """--impl reference: the oracle port of the reference CPU path, rank 0 only."""
+    """--impl reference: the reference's CPU decode of config 2 on all host
+    threads, rank 0 only (other ranks exit without work).  A step is one pass
+    over the whole archive, bodies spread over the threads."""
     if rank != 0:
         return
-    import torch
+    from concurrent.futures import ThreadPoolExecutor
 
     threads = os.cpu_count() or 1
-    wl = WORKLOADS[args.workload]
-    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
-    if wl in (C3Moe, C5Nf12):
-        w = wl(dev, 0, tokens=args.tokens)
-    elif wl is C6KvPaged:
-        w = wl(dev, 0, pages=args.kv_pages)
-    else:
-        w = wl(dev, 0)
+    items = _ref_archive(args.c2_layers)
+    decode, kind, what = _ref_decoder()
+    raw_bytes = sum(b.nbytes for _, _, b in items)
+    arch_bytes = sum(len(body) for _, body, _ in items)
+    for (head, body, bits) in items[:3]:  # the decoder reproduces the tensors
+        assert np.array_equal(np.asarray(decode(head, body), np.uint8).reshape(-1), bits.reshape(-1).view(np.uint8))
     times = []
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = w.cpu_sample(threads, budget_s=args.ref_seconds)
-        if i >= args.warmup:
-            vals.append(r["value"])
-            times.append(w.units_per_step / (r["value"] * 1e9) * 1e3)
-    v = statistics.median(vals)
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        order = sorted(range(len(items)), key=lambda k: -len(items[k][1]))
+        for step in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            n = sum(pool.map(lambda k: np.asarray(decode(items[k][0], items[k][1])).size, order))
+            dt = time.perf_counter() - t0
+            assert n == raw_bytes
+            if step >= args.warmup:
+                times.append(dt)
+    ms = statistics.median(times) * 1e3
+    v = raw_bytes / (ms * 1e-3) / 1e9
+    sample = (f"{args.steps} passes over the {len(items)}-body config-2 archive ({raw_bytes} B decoded per pass) "
+              f"with {what} on {threads} host threads")
     line = {
-        "metric": w.metric, "value": v, "unit": w.unit, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": statistics.median(times), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": w.dtype, "data": w.data,
-        "config": w.config(), "impl": "reference",
-        "cpu_baseline": {"value": v, "unit": w.unit, "cores": threads, "kind": "port",
-                         "sample": r["sample"]},
-        "e2e": {"value": v, "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "metric": C2Vpack.metric, "value": round(v, 4), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": C2Vpack.data,
+        "config": {"workload": C2Vpack.name, "tensors": len(items), "archive_bytes": int(arch_bytes),
+                   "raw_bytes": int(raw_bytes), "ratio": round(raw_bytes / arch_bytes, 4), "zstd_level": 1},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "cpu_model": cpu_model(), "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
-    ap.add_argument("--ref-seconds", type=float, default=4.0)
-    ap.add_argument("--cpu-seconds", type=float, default=6.0)
-    ap.add_argument("--tokens", type=int, default=1, help="c3_moe: tokens per step (1 or 8)")
-    ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
-    ap.add_argument("--kv-pages", type=int, default=65536, help="c6_kv_paged: KV pages (65536 = config 5)")
-    ap.add_argument("--kernel-times", action="store_true",
-                    help="zstd workloads: after the timed steps, time `--steps` more steps with a CUDA event after "
-                         "every kernel launch and report the mean ms per kernel per step ('kernel_ms')")
-    ap.add_argument("--device-only", action="store_true",
-                    help="parity check, warm-up and timed device steps only: no end-to-end leg, CPU baseline or "
-                         "clock sampler (the run the ncu captures in profiles/ use); prints no bench line")
-    args = ap.parse_args()
-
+def measure(w, args, stream, flush, world: int, clocks: bool = True) -> dict:
+    """Bit-exactness check, warm-up, `args.steps` timed device steps (CUDA
+    events on the launching stream, L2 flushed between steps), then the same
+    number of end-to-end steps through the public API.  Every rank takes the
+    same collective steps; times are the max over ranks."""
     import torch
-
-    world, rank, local = dist_init()
-    if args.impl == "reference":
-        run_reference(args, world, rank)
-        return
     import torch.distributed as dist
 
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    peaks, peaks_kind = load_peaks()
-    wl = WORKLOADS[args.workload]
-    if wl in (C3Moe, C5Nf12):
-        w = wl(dev, rank, tokens=args.tokens)
-    elif wl is C4MoeEP:
-        w = wl(dev, rank, tokens=args.tokens, world=world)
-    elif wl is C2Vpack:
-        w = wl(dev, rank, layers=args.c2_layers)
-    elif wl is C6KvPaged:
-        w = wl(dev, rank, pages=args.kv_pages)
-    else:
-        w = wl(dev, rank)
-    stream = torch.cuda.current_stream(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     sptr = int(stream.cuda_stream)
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
-
-    # correctness of the measured path on this input
     w.step_device(sptr)
     torch.cuda.synchronize()
-    if not w.verify():
-        raise SystemExit("bench: device decode is not bit-exact")
-
+    ok = w.verify()
+    if world > 1:
+        t = torch.tensor([1 if ok else 0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = bool(t.item())
+    if not ok:
+        raise SystemExit(f"bench: {type(w).__name__} device result is not exact")
     for _ in range(args.warmup):
         flush.fill_(1)
         w.step_device(sptr)
@@ -1089,39 +1310,38 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler = None if args.device_only else ClockSampler(local)
+    sampler = ClockSampler(torch.cuda.current_device()) if clocks else None
     if sampler:
         sampler.start()
+    marks = []
+    if hasattr(w, "_mark"):
+        del w._mark
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    coll = []
     for i in range(args.steps):
         flush.fill_(i & 0xFF)  # evict the previous step's data from L2
         starts[i].record(stream)
         w.step_device(sptr)
         ends[i].record(stream)
+        if hasattr(w, "_mark"):
+            marks.append(w._mark)
+        if hasattr(w, "collective_ms"):
+            coll.append(getattr(w, "_ev", []))
     torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    clock_rec = sampler.stop() if sampler else None
+    step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
     ms = sum(step_ms) / len(step_ms)
-    kernel_ms = zstd_kernel_times(w, args.steps, flush, stream) if args.kernel_times else None
-    if args.device_only:
-        if rank == 0:
-            line = {"device_only": True, "workload": w.config()["workload"], "steps": args.steps,
-                    "ms_per_step": round(ms, 5)}
-            if kernel_ms is not None:
-                line["kernel_ms"] = kernel_ms
-            print(json.dumps(line), flush=True)
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+    part_ms = sum(a.elapsed_time(m) for a, m in zip(starts, marks)) / len(marks) if marks else None
+    coll_ms = sum(a.elapsed_time(b) for ev in coll for a, b in ev) / len(coll) if any(coll) else None
+    vals = [ms, part_ms or 0.0, coll_ms or 0.0]
+    coll = coll if coll_ms is not None else []
     if world > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    mult = 1 if getattr(w, "replicated_units", False) else world
-    value = w.units_per_step * mult / (ms * 1e-3) / 1e9
-
+        vals = t.tolist()
+    out = {"ms": vals[0], "step_ms": step_ms, "part_ms": vals[1] if marks else None,
+           "coll_ms": vals[2] if coll else None, "clocks": clock_rec}
     # end to end through the public API, pinned host buffers, copies inside
     for _ in range(2):
         w.step_e2e()
@@ -1138,46 +1358,257 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = w.units_per_step * (1 if getattr(w, "replicated_units", False) else world) / (e2e_ms * 1e-3) / 1e9
+    out.update(e2e_ms=e2e_ms, h2d=bi, d2h=bo)
+    return out
 
-    extra = w.extra(stream, args.steps, flush) if hasattr(w, "extra") else {}
-    achieved = w.algo_bytes / (ms * 1e-3) / 1e9
-    if w.unit != "GB/s":
-        value = w.units_per_step * mult / (ms * 1e-3)
-        e2e_value = w.units_per_step * mult / (e2e_ms * 1e-3)
-    prof = profiled_traffic(w.config()["workload"])
-    roof = {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+
+def sum_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(v)], device=torch.device("cuda", torch.cuda.current_device()), dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def roofline(achieved: float, peaks: dict, peaks_kind: str, algo: int, workload: str, note: str) -> dict:
+    prof = profiled_traffic(workload)
+    return {"bound": "hbm", "achieved": round(achieved, 3), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 5), "traffic": prof[0] if prof else None,
             "traffic_unit": "DRAM bytes per step (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
-            "traffic_source": prof[1] if prof else None,
-            "algorithmic_bytes_per_step": int(w.algo_bytes),
-            "peak_kind": f"{peaks_kind} (hbm_gbs)"}
+            "traffic_source": prof[1] if prof else None, "algorithmic_bytes_per_step": int(algo),
+            "achieved_note": note, "peak_kind": f"{peaks_kind} (hbm_gbs)"}
+
+
+def moe_record(w, r: dict, world: int, peaks, peaks_kind, cpu: dict | None, extra: dict) -> dict:
+    """Nested record of one MoE workload (tok/s, roofline, e2e, NCCL share)."""
+    ms = r["ms"]
+    algo = sum_over_ranks(w.algo_bytes, world)
+    rec = {"value": round(w.units_per_step / (ms * 1e-3), 3), "unit": "tok/s", "ms_per_step": round(ms, 5),
+           "roofline": roofline(algo / world / (ms * 1e-3) / 1e9, peaks, peaks_kind, int(algo / world),
+                                extra.get("workload", ""),
+                                "compressed pages of the routed experts on a GPU + activations in and out, per step"
+                                ", mean over ranks / step time"),
+           "e2e": {"value": round(w.units_per_step / (r["e2e_ms"] * 1e-3), 3), "unit": "tok/s",
+                   "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+           "cpu_baseline": cpu, "clocks": r["clocks"],
+           "gpu_launches": getattr(w, "launches_per_step", 1) * 1}
+    if r.get("coll_ms") is not None:
+        rec["collective"] = {"op": "NCCL all-reduce of the route rows", "ms_per_step": round(r["coll_ms"], 5),
+                             "share_of_step": round(r["coll_ms"] / ms, 4)}
+    rec.update(extra)
+    return rec
+
+
+def headline(args, world, rank, local, dev):
+    """The default run: config 2 decode GB/s as the line's value, with nested
+    records for config 4 (expert parallel, T = 1, 8, 64) and, on one GPU,
+    config 3 (T = 1, 8)."""
+    import torch
+    import torch.distributed as dist
+
+    peaks, peaks_kind = load_peaks()
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    host_threads = os.cpu_count() or 1
+
+    w = C2Vpack(dev, rank, layers=args.c2_layers, world=world)
+    r = measure(w, args, stream, flush, world)
+    ms = r["ms"]
+    value = w.units_per_step / (ms * 1e-3) / 1e9
+    e2e_value = w.units_per_step / (r["e2e_ms"] * 1e-3) / 1e9
+    dec_ms = r["part_ms"]
+    algo = sum_over_ranks(w.algo_bytes, world)
+    achieved = algo / world / (dec_ms * 1e-3) / 1e9
+    kernel_ms = zstd_kernel_times(w, args.steps, flush, stream) if args.kernel_times else None
+    cpu = w.cpu_sample(host_threads, budget_s=args.cpu_seconds) if (rank == 0 and world == 1) else None
+    line = {
+        "metric": w.metric, "value": round(value, 4), "unit": w.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
+        "data": w.data, "config": w.config(),
+        "roofline": roofline(achieved, peaks, peaks_kind, int(algo / world), w.config()["workload"],
+                             "per GPU: compressed + decoded bytes of its share / its decode time (the "
+                             "all-gather excluded)"),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 4), "unit": w.unit, "h2d_bytes_per_step": r["h2d"],
+                "d2h_bytes_per_step": r["d2h"]},
+        "gpu_launches": args.steps * w.launches_per_step, "clocks": r["clocks"],
+        "step_ms_min": round(min(r["step_ms"]), 5), "step_ms_max": round(max(r["step_ms"]), 5),
+        "decode_ms_per_step": round(dec_ms, 5),
+        **({"kernel_ms": kernel_ms} if kernel_ms is not None else {}),
+    }
+    if world > 1:
+        line["collective"] = {"op": "NCCL all-gather of the decoded bodies", "bytes_per_rank": int(w.gather_bytes),
+                              "ms_per_step": round(ms - dec_ms, 5), "share_of_step": round(1 - dec_ms / ms, 4)}
+    del w
+    torch.cuda.empty_cache()
+
+    if not args.no_moe:
+        c4 = C4MoeEP(dev, rank, world=world, tokens=tuple(args.c4_tokens), layers=args.c4_layers)
+        recs = {}
+        for T in args.c4_tokens:
+            st = c4.for_tokens(T)
+            rr = measure(st, args, stream, flush, world)
+            cpu4 = None
+            if rank == 0 and world == 1 and T in (1, 8):
+                cpu4 = st.cpu_sample(host_threads, budget_s=args.cpu_seconds / 2)
+                cpu4["cpu_model"] = cpu_model()
+            recs[f"T{T}"] = moe_record(st, rr, world, peaks, peaks_kind, cpu4, {
+                "tokens": T, "workload": f"c4_moe_ep_T{T}",
+                "local_routed_experts_per_step": st.local_routed,
+                "distinct_experts_per_layer": st.distinct_per_layer})
+        line["moe_ep"] = {"metric": c4.metric, "config": c4.config(), "scaling": "strong", "by_tokens": recs}
+        del c4
+        torch.cuda.empty_cache()
+        if world == 1:
+            store = None
+            c3 = {}
+            for T in (1, 8):
+                w3 = C3Moe(dev, 0, tokens=T, store=store)
+                store = w3.store
+                rr = measure(w3, args, stream, flush, world)
+                cpu3 = w3.cpu_sample(host_threads, budget_s=args.cpu_seconds / 2)
+                cpu3["cpu_model"] = cpu_model()
+                c3[f"T{T}"] = moe_record(w3, rr, 1, peaks, peaks_kind, cpu3,
+                                         {"tokens": T, "workload": w3.name,
+                                          "distinct_experts_per_step": getattr(w3, "distinct", None)})
+            line["c3_moe"] = {"metric": C3Moe.metric, "config": w3.config(), "by_tokens": c3}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def single(args, world, rank, local, dev):
+    """--workload X: one workload's line (profiling and development runs)."""
+    import torch
+
+    peaks, peaks_kind = load_peaks()
+    wl = WORKLOADS[args.workload]
+    if wl is C3Moe:
+        w = wl(dev, rank, tokens=args.tokens)
+    elif wl is C5Nf12:
+        w = wl(dev, rank, tokens=args.tokens)
+    elif wl is C4MoeEP:
+        w = wl(dev, rank, world=world, tokens=(args.tokens,), layers=args.c4_layers).for_tokens(args.tokens)
+    elif wl is C2Vpack:
+        w = wl(dev, rank, layers=args.c2_layers, world=world)
+    elif wl is C6KvPaged:
+        w = wl(dev, rank, pages=args.kv_pages)
+    else:
+        w = wl(dev, rank)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    if args.device_only:
+        sptr = int(stream.cuda_stream)
+        w.step_device(sptr)
+        torch.cuda.synchronize()
+        if not w.verify():
+            raise SystemExit("bench: device result is not exact")
+        for _ in range(args.warmup):
+            w.step_device(sptr)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in ev:
+            flush.fill_(2)
+            a.record(stream)
+            w.step_device(sptr)
+            b.record(stream)
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+        kernel_ms = zstd_kernel_times(w, args.steps, flush, stream) if args.kernel_times else None
+        if rank == 0:
+            name = w.config()["workload"] if hasattr(w, "config") else type(w).__name__
+            line = {"device_only": True, "workload": name, "steps": args.steps, "ms_per_step": round(ms, 5)}
+            if kernel_ms is not None:
+                line["kernel_ms"] = kernel_ms
+            print(json.dumps(line), flush=True)
+        return
+    r = measure(w, args, stream, flush, world)
+    ms = r["ms"]
+    mult = 1 if getattr(w, "replicated_units", False) else world
+    if w.unit == "GB/s":
+        value = w.units_per_step * mult / (ms * 1e-3) / 1e9
+        e2e_value = w.units_per_step * mult / (r["e2e_ms"] * 1e-3) / 1e9
+    else:
+        value = w.units_per_step * mult / (ms * 1e-3)
+        e2e_value = w.units_per_step * mult / (r["e2e_ms"] * 1e-3)
+    extra = w.extra(stream, args.steps, flush) if hasattr(w, "extra") else {}
+    algo = sum_over_ranks(w.algo_bytes, world)
+    t_ms = r["part_ms"] or ms
+    cfg = w.config() if hasattr(w, "config") else w.c4.config()
     cpu = None
-    if rank == 0 and world == 1:
-        cpu = w.cpu_sample(1, budget_s=args.cpu_seconds)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = w.cpu_sample(os.cpu_count() or 1, budget_s=args.cpu_seconds)
     if rank == 0:
         line = {
-            "metric": w.metric, "value": round(value, 4), "unit": w.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": getattr(w, "scaling", "weak"), "vs_baseline": None,
-            "dtype": w.dtype,
-            "data": w.data,
-            "config": dict(w.config(), parallelism=f"replicas x{world}" if world > 1 else "single"),
-            "roofline": roof, "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 4), "unit": w.unit, "h2d_bytes_per_step": bi,
-                    "d2h_bytes_per_step": bo},
-            "gpu_launches": args.steps * getattr(w, "launches_per_step", 1), "clocks": clocks,
-            "step_ms_min": round(min(step_ms), 5), "step_ms_max": round(max(step_ms), 5),
-            **({"kernel_ms": kernel_ms} if kernel_ms is not None else {}),
+            "metric": getattr(w, "metric", getattr(getattr(w, "c4", None), "metric", "")), "value": round(value, 4),
+            "unit": w.unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": getattr(w, "scaling", "weak"),
+            "vs_baseline": None, "dtype": getattr(w, "dtype", "bf16"), "data": getattr(w, "data", ""),
+            "config": cfg,
+            "roofline": roofline(algo / world / (t_ms * 1e-3) / 1e9, peaks, peaks_kind, int(algo / world),
+                                 cfg["workload"], "algorithmic bytes per GPU / step time"),
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 4), "unit": w.unit, "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"]},
+            "gpu_launches": args.steps * getattr(w, "launches_per_step", 1), "clocks": r["clocks"],
+            **({"collective_ms_per_step": round(r["coll_ms"], 5)} if r.get("coll_ms") is not None else {}),
             **extra,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help="one workload only (default: config 2 as the line's value with nested config-4 and "
+                         "config-3 records)")
+    ap.add_argument("--ref-seconds", type=float, default=4.0)
+    ap.add_argument("--cpu-seconds", type=float, default=6.0)
+    ap.add_argument("--tokens", type=int, default=1, help="--workload c3_moe / c4_moe_ep / c5_nf12: tokens")
+    ap.add_argument("--c2-layers", type=int, default=30, help="c2_vpack: layers of the archive (30 = config 2)")
+    ap.add_argument("--c4-tokens", type=int, nargs="+", default=[1, 8, 64], help="config-4 token counts")
+    ap.add_argument("--c4-layers", type=int, default=4, help="config-4 routers per step")
+    ap.add_argument("--kv-pages", type=int, default=65536, help="c6_kv_paged: KV pages (65536 = config 5)")
+    ap.add_argument("--no-moe", action="store_true", help="default run: config 2 only")
+    ap.add_argument("--no-cpu", action="store_true", help="--workload runs: skip the CPU baseline leg")
+    ap.add_argument("--kernel-times", action="store_true",
+                    help="zstd workloads: after the timed steps, time `--steps` more steps with a CUDA event after "
+                         "every kernel launch and report the mean ms per kernel per step ('kernel_ms')")
+    ap.add_argument("--device-only", action="store_true",
+                    help="--workload runs: parity check, warm-up and timed device steps only (the run the ncu "
+                         "captures in profiles/ use); prints a short line")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_init()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    try:
+        if args.workload is None:
+            headline(args, world, rank, local, dev)
+        else:
+            single(args, world, rank, local, dev)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":
