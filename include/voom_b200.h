@@ -250,6 +250,40 @@ void voom_zstd_plan_destroy(void* plan);
 int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const void* h_plan, void* d_scratch,
                      uint8_t* d_out, uint32_t* d_status, void* stream);
 
+/* GPU zstd compression into valid RFC 8878 frames, the KV-page spill codec
+ * (and the warm tier's admission): any frame zstd.decompress accepts gives
+ * the page back, so the frames need not be libzstd's.  A frame is split into
+ * blocks of at most voom_zstd_encode_block_bytes() input bytes; each becomes a
+ * Compressed block of Huffman-coded literals (four streams, FSE-compressed or
+ * 4-bit weights, no sequences), RLE literals when one byte value fills it, or
+ * a Raw block when Huffman coding would not shrink it.  Frames are single
+ * segment with the content size and no checksum.  Block b is written into
+ * slot b (voom_zstd_encode_slot_bytes() bytes each) of d_slots; d_sizes[2b] /
+ * d_sizes[2b+1] give the offset and length of its bytes in the slot (the
+ * first block of a frame carries the frame header), so a frame is the
+ * concatenation of its blocks' byte ranges.
+ * Replaces: zstd.compress(raw, level=1) in runtime/kv_paged.py:79-91 and
+ * runtime/warm_tier.py:74-83. */
+typedef struct voom_zenc_block {
+  uint64_t src;       /* offset of the block's first input byte in d_src */
+  uint64_t frame_len; /* content size of the frame the block belongs to */
+  uint32_t len;       /* input bytes of the block (<= voom_zstd_encode_block_bytes()) */
+  uint32_t flags;     /* VOOM_ZENC_FIRST | VOOM_ZENC_LAST */
+} voom_zenc_block;
+
+#define VOOM_ZENC_FIRST 1u /* first block of its frame: the frame header precedes it */
+#define VOOM_ZENC_LAST 2u  /* last block of its frame */
+
+uint64_t voom_zstd_encode_slot_bytes(void);
+uint32_t voom_zstd_encode_block_bytes(void);
+int voom_zstd_encode(const uint8_t* d_src, const voom_zenc_block* d_blocks, uint32_t n_blocks, uint8_t* d_slots,
+                     uint32_t* d_sizes, void* stream);
+/* Packs the encoded blocks into one buffer: block b's bytes (its range in
+ * slot b, from d_sizes) go to d_out + d_dst[b].  No counterpart in the
+ * reference (it writes frames from host memory). */
+int voom_zstd_encode_pack(const uint8_t* d_slots, const uint32_t* d_sizes, const uint64_t* d_dst, uint32_t n_blocks,
+                          uint8_t* d_out, void* stream);
+
 /* Per-kernel timing of voom_zstd_decode (diagnostics; no counterpart in the
  * reference).  voom_zstd_set_timing(1) makes every later voom_zstd_decode
  * record a CUDA event after each of its launches (on the device current when

@@ -102,6 +102,10 @@ SIGNATURES: dict[str, tuple] = {
     "voom_zstd_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "voom_kvz_gather": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp, _i32]),
     "voom_zstd_set_timing": (_i32, [_i32]),
+    "voom_zstd_encode_slot_bytes": (_u64, []),
+    "voom_zstd_encode_block_bytes": (_u32, []),
+    "voom_zstd_encode": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp]),
+    "voom_zstd_encode_pack": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp]),
     "voom_zstd_kernel_times": (_i32, [_vp, _vp, _i32]),
     "voom_moe_scratch_bytes": (_u64, [_u32, _u32, _u32, _u32]),
     "voom_moe_layer": (_i32, [_vp, _u32, _vp, _vp, ctypes.c_float, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32,

@@ -210,3 +210,85 @@ def decompress_many(frames: list, sizes: list[int] | None = None, *, device=None
 def decompress(data, size: int | None = None) -> bytes:
     """Drop-in for compression.zstd.decompress(data) (bytes in, bytes out)."""
     return decompress_device(data, size).cpu().numpy().tobytes()
+
+
+ZENC_BLOCK_DTYPE = np.dtype([("src", "<u8"), ("frame_len", "<u8"), ("len", "<u4"), ("flags", "<u4")])
+assert ZENC_BLOCK_DTYPE.itemsize == 24
+ZENC_FIRST, ZENC_LAST = 1, 2
+
+
+def compress_device(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda.Stream | None = None
+                    ) -> tuple[torch.Tensor, np.ndarray, list[tuple[int, int]]]:
+    """Compress many byte ranges of one device buffer, each into its own zstd
+    frame, in ONE launch of the GPU encoder (voom_zstd_encode).  Returns the
+    device slots, the (slot offset, length) of every block (host array, n x 2)
+    and each frame's (first block, block count).  The frames are valid
+    RFC 8878 frames that zstd.decompress / compression.zstd accept; they are
+    not libzstd's bytes."""
+    lib = load()
+    dev = d_src.device
+    block = int(lib.voom_zstd_encode_block_bytes())
+    slot = int(lib.voom_zstd_encode_slot_bytes())
+    rows, frames = [], []
+    for off, n in zip(offsets, lengths):
+        off, n = int(off), int(n)
+        k0 = len(rows)
+        starts = list(range(0, n, block)) or [0]
+        for k, b0 in enumerate(starts):
+            flags = (ZENC_FIRST if k == 0 else 0) | (ZENC_LAST if k == len(starts) - 1 else 0)
+            rows.append((off + b0, n, min(block, n - b0), flags))
+        frames.append((k0, len(starts)))
+    blocks = np.array(rows, dtype=ZENC_BLOCK_DTYPE) if rows else np.zeros(0, ZENC_BLOCK_DTYPE)
+    n_blocks = len(rows)
+    with torch.cuda.device(dev):
+        d_blocks = _device.tensor_from_numpy(blocks.view(np.uint8), dev) if n_blocks else None
+        slots = torch.empty(max(n_blocks, 1) * slot, dtype=torch.uint8, device=dev)
+        sizes = torch.empty(max(2 * n_blocks, 2), dtype=torch.int32, device=dev)
+        if n_blocks:
+            check(lib.voom_zstd_encode(d_src.data_ptr(), d_blocks.data_ptr(), n_blocks, slots.data_ptr(),
+                                       sizes.data_ptr(), _device.stream_ptr(dev, stream)), "voom_zstd_encode")
+        sz = sizes[:2 * n_blocks].cpu().numpy().view(np.uint32).reshape(-1, 2).astype(np.int64)
+    sz[:, 0] += np.arange(n_blocks, dtype=np.int64) * slot
+    return slots, sz, frames
+
+
+def compress_many(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda.Stream | None = None,
+                  pinned: torch.Tensor | None = None) -> list[bytes]:
+    """compress_device, then every frame as host bytes: the blocks are packed
+    on the device and cross to the host in one copy (into `pinned` when it is
+    a large enough pinned buffer)."""
+    slots, sz, frames = compress_device(d_src, offsets, lengths, stream=stream)
+    n_blocks = sz.shape[0]
+    if n_blocks == 0:
+        return [b"" for _ in frames]
+    dev = d_src.device
+    dst = np.zeros(n_blocks, np.uint64)
+    np.cumsum(sz[:-1, 1], out=dst[1:])
+    total = int(dst[-1] + sz[-1, 1])
+    rel = sz.copy()
+    rel[:, 0] -= np.arange(n_blocks, dtype=np.int64) * int(load().voom_zstd_encode_slot_bytes())
+    d_sizes = _device.tensor_from_numpy(rel.astype(np.uint32), dev)
+    d_dst = _device.tensor_from_numpy(dst, dev)
+    packed = torch.empty(max(total, 1), dtype=torch.uint8, device=dev)
+    check(load().voom_zstd_encode_pack(slots.data_ptr(), d_sizes.data_ptr(), d_dst.data_ptr(), n_blocks,
+                                       packed.data_ptr(), _device.stream_ptr(dev, stream)), "voom_zstd_encode_pack")
+    if pinned is not None and pinned.numel() >= total:
+        pinned[:total].copy_(packed[:total])
+        host = pinned.numpy()
+    else:
+        host = packed[:total].cpu().numpy()
+    out = []
+    for b0, nb in frames:
+        a = int(dst[b0])
+        e = int(dst[b0 + nb - 1] + sz[b0 + nb - 1, 1])
+        out.append(host[a:e].tobytes())
+    return out
+
+
+def compress(data, level: int = 1) -> bytes:
+    """compression.zstd.compress(data) on the GPU (level is accepted for the
+    signature; the encoder has one setting)."""
+    arr = _device.as_u8(data)
+    dev = _device.require_cuda(None)
+    d = _device.upload(arr, dev) if arr.size else torch.zeros(16, dtype=torch.uint8, device=dev)
+    return compress_many(d, [0], [arr.size])[0]

@@ -367,15 +367,32 @@ class PagedKVCache:
 
 def spill_batch(pages: list[_Page], paths: list[Path], compress: bool,
                 pool: ThreadPoolExecutor | None) -> int | None:
-    """Spills resident pages together: their K and V leave the device in one
-    copy, each page's file is written on `pool`, and every page drops its
-    device tensors.  Compressed spills write the reference's `.kvz` (a pickle
-    of {"shape", "k": zstd(raw K, 1), "v": zstd(raw V, 1)}, kv_paged.py:77-91)
-    and return the compressed byte total; uncompressed spills write
-    safetensors with tensors "k" and "v" and return None.  Without a pool the
-    files are written on the calling thread."""
+    """Spills resident pages together and drops their device tensors.
+    Compressed spills write the reference's `.kvz` (a pickle of {"shape", "k":
+    zstd frame of raw K, "v": zstd frame of raw V}, kv_paged.py:77-91) with
+    every frame made by the GPU encoder in one launch (frames the reference's
+    zstd.decompress reads back exactly) and return the compressed byte total;
+    uncompressed spills copy K and V to the host in one copy and write
+    safetensors with tensors "k" and "v", returning None.  Files are written
+    on `pool` (or the calling thread)."""
     if not pages:
         return 0 if compress else None
+    if compress and pages[0].k.is_cuda and all(pg.shape == pages[0].shape for pg in pages):
+        # every K and V frame compressed in one GPU launch; only frames cross to the host
+        blobs = spill_pages_gpu(torch.stack([pg.k for pg in pages]), torch.stack([pg.v for pg in pages]))
+
+        def write_kvz(j: int) -> int:
+            with open(paths[j].with_suffix(".kvz"), "wb") as f:
+                f.write(blobs[j])
+            d = pickle.loads(blobs[j])
+            return len(d["k"]) + len(d["v"])
+
+        sizes = list((pool.map if pool is not None else map)(write_kvz, range(len(pages))))
+        for pg, path in zip(pages, paths):
+            pg.path = path.with_suffix(".kvz")
+            pg._compressed = True
+            pg.k = pg.v = None
+        return sum(sizes)
     flat = torch.cat([t.detach().reshape(-1) for pg in pages for t in (pg.k, pg.v)])
     host = flat.view(torch.int16).cpu().numpy()
     pos, slices = 0, []
@@ -400,6 +417,28 @@ def spill_batch(pages: list[_Page], paths: list[Path], compress: bool,
         pg._compressed = compress
         pg.k = pg.v = None
     return sum(sizes) if compress else None
+
+
+def spill_pages_gpu(k: torch.Tensor, v: torch.Tensor, *, stream: torch.cuda.Stream | None = None,
+                    pinned: torch.Tensor | None = None) -> list[bytes]:
+    """The `.kvz` bytes of many pages at once, compressed on the GPU: k and v
+    are (n, *shape) BF16 device tensors (a page's K is k[i]).  Every K and V
+    becomes one zstd frame in one launch of the GPU encoder
+    (zstd_gpu.compress_many: Huffman-coded literals, valid frames the
+    reference's zstd.decompress reads back exactly), the frames cross to the
+    host in one copy, and each page is pickled as {"shape", "k", "v"}
+    (runtime/kv_paged.py:79-91)."""
+    from ..formats import zstd_gpu
+
+    n = int(k.shape[0])
+    if n == 0:
+        return []
+    shape = tuple(int(x) for x in k.shape[1:])
+    per = int(np.prod(shape)) * 2
+    flat = torch.stack([k.reshape(n, -1), v.reshape(n, -1)], dim=1).contiguous().view(torch.uint8).reshape(-1)
+    offs = np.arange(2 * n, dtype=np.int64) * per
+    frames = zstd_gpu.compress_many(flat, offs, np.full(2 * n, per, np.int64), stream=stream, pinned=pinned)
+    return [pickle.dumps({"shape": shape, "k": frames[2 * i], "v": frames[2 * i + 1]}) for i in range(n)]
 
 
 def spill_pages_compressed(pages_k: np.ndarray, pages_v: np.ndarray, threads: int = 8) -> list[bytes]:
