@@ -597,8 +597,9 @@ class C4MoeEP:
     distinct experts with intermediate 2048 (BF16 N(0, 0.015)), each
     projection a VRN1 frame of 2 MiB pages (12 per projection) with a
     checkpoint index, top-8 softmax routing whose expert popularity follows
-    Zipf(1.1) (router logits biased by 4 log p over a seeded permutation of
-    ranks), T tokens per step.  Expert parallel: every rank routes all tokens,
+    Zipf(1.1) (router logits biased by c log p over a seeded permutation of
+    ranks; top-8 then approximates drawing 8 distinct experts in proportion to
+    the popularity), T tokens per step.  Expert parallel: every rank routes all tokens,
     runs the fused decode + SwiGLU of its own experts (placed by LPT over the
     expected decode cost of the T values timed), one NCCL all-reduce sums the
     route rows, every rank combines.  A step runs `layers` layers (one router
@@ -609,7 +610,7 @@ class C4MoeEP:
     unit = "tok/s"
     dtype = "bf16"
     data = ("synthetic (seeded numpy/torch): 160 distinct experts BF16 N(0, 0.015) in 2 MiB rANS pages, "
-            "router N(0, 0.02) + 4 log Zipf(1.1) popularity bias, tokens N(0, 1)")
+            "router N(0, 0.02) + a log Zipf(1.1) popularity bias, tokens N(0, 1)")
     E, H, I, K = 160, 6144, 2048, 8
     PAGE = 2 << 20
 
@@ -627,7 +628,12 @@ class C4MoeEP:
         self.pop = moe.zipf_popularity(E, 1.1, seed=11)
         gr = torch.Generator().manual_seed(4242)  # identical routers on every rank
         logp = torch.from_numpy(np.log(self.pop)).float()
-        self.bias = (4.0 * logp).to(device)
+        # router logits of unit-variance tokens have noise sigma = 0.02 sqrt(H);
+        # a bias of (sigma / 1.28) log p sets that noise against log p like a
+        # standard Gumbel (std 1.28), so top-8 approximates drawing 8 distinct
+        # experts in proportion to the Zipf popularity (Plackett-Luce)
+        self.bias_scale = 0.02 * float(np.sqrt(H)) / 1.28
+        self.bias = (self.bias_scale * logp).to(device)
         self.routers = []
         for _ in range(layers):
             wr = (torch.randn((E, H), generator=gr) * 0.02).to(torch.bfloat16)
@@ -680,7 +686,8 @@ class C4MoeEP:
                 "layer_note": "one expert set (config 4's single layer) under `layers_per_step` routers",
                 "local_experts": len(self.owned), "local_page_bytes_compressed": int(self.store.compressed_bytes),
                 "local_page_bytes_raw": int(raw), "ratio": round(raw / max(1, self.store.compressed_bytes), 4),
-                "popularity": "Zipf(1.1) over a seeded permutation, router bias 4 log p",
+                "popularity": f"Zipf(1.1) over a seeded permutation, router bias {self.bias_scale:.3f} log p "
+                              "(top-8 ~ 8 distinct draws in proportion to the popularity)",
                 "placement": "LPT over expected page decodes per step (mean over the timed T)",
                 "experts_per_rank": [len(b) for b in self.placement],
                 "combine": "NCCL all-reduce of the BF16 route rows (one nonzero contributor per row), "

@@ -365,3 +365,29 @@ def test_layer_is_deterministic(built_lib):
         for _ in range(3):
             assert torch.equal(layer(x), a)
         layer.check_status()
+
+
+@pytest.mark.parametrize("tile_bytes", [40 * 1024, 3 * 1024 + 512])
+def test_tile_boundaries_inside_rows(built_lib, tile_bytes):
+    """Tiles that cut rows (40 KiB tiles of 3 KiB rows: a seam row every 13
+    rows; 3.5 KiB tiles: every tile ends inside a row): the two partial sums
+    of a seam row meet in a seam cell and give the same result, deterministic,
+    as the reference math."""
+    from voom_b200.runtime import moe
+
+    E, H, I = 6, 1536, 512
+    ex, _, _ = make(E, H, I, 0.02, 41)
+    store = moe.ExpertStore([tuple(bits(w) for w in e) for e in ex], "cuda:0", tile_bytes=tile_bytes)
+    assert store.pages[0][0].page.n_tiles > 10
+    g = torch.Generator().manual_seed(3)
+    h = torch.randn((8, H), generator=g).to(torch.bfloat16)
+    tokens = [[0], [1, 2], [3, 4, 5, 6], list(range(8)), [7], [2, 5]]
+    y = moe.swiglu_grouped(store, list(range(E)), tokens, h.cuda())
+    again = moe.swiglu_grouped(store, list(range(E)), tokens, h.cuda())
+    assert torch.equal(y, again)
+    y = y.cpu()
+    row = 0
+    for e, tl in enumerate(tokens):
+        err = om.rel_l2(y[row:row + len(tl)], om.swiglu(h[tl], *ex[e]))
+        assert err < TOL, (e, err)
+        row += len(tl)

@@ -401,8 +401,11 @@ __global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __rest
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
 struct ScratchLayout {
-  uint64_t routes, h, logits, act, y, total;
+  uint64_t routes, h, logits, act, y, seams, seam_bytes, total;
 };
+
+// Seam cells of the CUDA-core kernel: two projections' worth per unique expert.
+uint64_t seam_bytes(uint32_t max_unique) { return uint64_t(max_unique) * 2 * kSeams * sizeof(SeamCell); }
 
 ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   ScratchLayout s;
@@ -412,6 +415,7 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   s.logits = o; o = align256(o + uint64_t(T) * kMaxE * 4);
   s.act = o; o = align256(o + uint64_t(T) * k * I * 2 + 16);
   s.y = o; o = align256(o + uint64_t(T) * k * (H > I ? H : I) * 2 + 16);  // u rows, then y rows
+  s.seams = o; s.seam_bytes = seam_bytes(min(uint64_t(T) * k, uint64_t(kMaxU))); o = align256(o + s.seam_bytes);
   s.total = o;
   return s;
 }
@@ -424,35 +428,39 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
 // ubuf holds max_rows x I.
 template <int NT>
 int launch_cc(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in, uint32_t ld_in,
-              uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t nbpp, uint32_t nblocks, uint32_t n_unique,
-              uint32_t mma_on, uint32_t* d_status, cudaStream_t st) {
+              uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t nbpp, uint32_t n_proj, uint32_t cpt,
+              uint32_t tiles, uint32_t n_unique, SeamCell* seams, uint32_t* d_status, cudaStream_t st) {
   const size_t smem = sizeof(CcShared);
   if (cudaFuncSetAttribute(moe_proj_cc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return VOOM_E_CUDA;
-  moe_proj_cc<NT><<<dim3(nblocks, n_unique, 1), kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1,
-                                                                       ld_out, nbpp, mma_on, d_status);
+  moe_proj_cc<NT><<<dim3(n_proj * nbpp, n_unique, 1), kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1,
+                                                                             ld_out, nbpp, cpt, tiles, seams, d_status);
   return VOOM_OK;
 }
 
+// One projection kind (gate and up, or down) of every unique expert: rows x
+// cols, `tiles` = the largest tile count of any expert's frame of it.
 int launch_proj(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in,
                 uint32_t ld_in, uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t rows, uint32_t cols,
-                uint32_t n_proj, uint32_t n_unique, uint32_t max_tok, uint32_t* d_status, cudaStream_t st) {
-  const uint32_t mma_on = max_tok > uint32_t(kTok) ? 1u : 0u;
-  const uint32_t nbpp = (rows + cc_rows(cols) - 1) / cc_rows(cols);
+                uint32_t tiles, uint32_t n_proj, uint32_t n_unique, uint32_t max_tok, SeamCell* seams,
+                uint32_t* d_status, cudaStream_t st) {
+  const uint32_t t = max(1u, tiles);
+  const uint32_t cpt = cc_chunks_per_tile(rows, cols, t), nbpp = t * cpt;
+  const uint32_t ntok = min(max_tok, uint32_t(kTok));
   int rc;
-  if (max_tok <= 1)
-    rc = launch_cc<1>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+  if (ntok <= 1)
+    rc = launch_cc<1>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
                       d_status, st);
-  else if (max_tok <= 2)
-    rc = launch_cc<2>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+  else if (ntok <= 2)
+    rc = launch_cc<2>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
                       d_status, st);
-  else if (max_tok <= 4)
-    rc = launch_cc<4>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+  else if (ntok <= 4)
+    rc = launch_cc<4>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
                       d_status, st);
   else
-    rc = launch_cc<8>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj * nbpp, n_unique, mma_on,
+    rc = launch_cc<8>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
                       d_status, st);
-  if (rc != VOOM_OK || !mma_on) return rc;
+  if (rc != VOOM_OK || max_tok <= uint32_t(kTok)) return rc;
   const uint32_t ncap = (min(max_tok, kMmaMaxN) + 15u) & ~15u;
   const uint32_t zc = (max_tok + kMmaMaxN - 1) / kMmaMaxN;
   const uint32_t smem = mma_smem_bytes(ncap);
@@ -464,13 +472,20 @@ int launch_proj(const voom_expert_pages* d_pages, const Routes* R, uint32_t whic
   return VOOM_OK;
 }
 
+// gate/up, activation, then down for every routed expert.  Experts with at
+// most kTok tokens run on moe_proj_cc, the others on moe_proj_mma (tensor
+// cores); either way each page block is decoded once per call.  ubuf holds
+// max_rows x I; seams = seam_bytes(n_unique) of scratch (cleared here).
 int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_t* h, uint16_t* act,
                 uint16_t* ubuf, uint16_t* y, uint32_t H, uint32_t I, uint32_t n_unique, uint32_t max_rows,
-                uint32_t max_tok, uint32_t* d_status, cudaStream_t st) {
-  int rc = launch_proj(d_pages, R, 0, h, H, act, ubuf, I, I, H, 2, n_unique, max_tok, d_status, st);
+                uint32_t max_tok, uint32_t gate_tiles, uint32_t down_tiles, void* seams, uint32_t* d_status,
+                cudaStream_t st) {
+  if (cudaMemsetAsync(seams, 0, seam_bytes(n_unique), st) != cudaSuccess) return VOOM_E_CUDA;
+  SeamCell* sc = static_cast<SeamCell*>(seams);
+  int rc = launch_proj(d_pages, R, 0, h, H, act, ubuf, I, I, H, gate_tiles, 2, n_unique, max_tok, sc, d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_act<<<dim3((I / 8 + 127) / 128, max_rows), 128, 0, st>>>(R, act, ubuf, I);
-  return launch_proj(d_pages, R, 1, act, I, y, y, H, H, I, 1, n_unique, max_tok, d_status, st);
+  return launch_proj(d_pages, R, 1, act, I, y, y, H, H, I, down_tiles, 1, n_unique, max_tok, sc, d_status, st);
 }
 
 // The generic family with no shared expert: what the variant-less entry
@@ -541,7 +556,8 @@ int moe_layer_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages, 
   float* logits = reinterpret_cast<float*>(s + L.logits);
   launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
   const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
-  rc = launch_gemv(d_pages, R, h, act, y, y, H, I, max_unique, T * rpt, T, d_status, st);
+  rc = launch_gemv(d_pages, R, h, act, y, y, H, I, max_unique, T * rpt, T, gate_tiles, down_tiles, s + L.seams,
+                   d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, st>>>(R, y, d_x, d_x_out, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
@@ -567,7 +583,8 @@ int moe_experts_impl(const voom_moe_variant& v, const voom_expert_pages* d_pages
   launch_front(v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
   const uint32_t max_unique = min(n_experts, T * top_k) + (v.shared_expert >= 0 ? 1u : 0u);
   uint16_t* ubuf = reinterpret_cast<uint16_t*>(s + L.y);
-  rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, H, I, max_unique, T * rpt, T, d_status, st);
+  rc = launch_gemv(d_pages, R, h, act, ubuf, d_y, H, I, max_unique, T * rpt, T, gate_tiles, down_tiles, s + L.seams,
+                   d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
@@ -650,7 +667,8 @@ constexpr uint64_t kNoAllocBytes =
     ((uint64_t(kNoAllocMaxT) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255)) +
     uint64_t(kNoAllocMaxT) * kMaxE * 4 +
     ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxI * 2 + 16 + 255) & ~uint64_t(255)) +
-    ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255));
+    ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255)) +
+    ((uint64_t(kNoAllocMaxRoutes) * 2 * kSeams * sizeof(SeamCell) + 255) & ~uint64_t(255));
 
 __device__ __align__(256) uint8_t g_moe_scratch[kNoAllocBytes];
 
@@ -716,7 +734,8 @@ VOOM_API int voom_expert_swiglu(const voom_expert_pages* d_pages, const uint32_t
       cudaMemcpyAsync(&R->upair[0], d_upair, 4ull * n_rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return VOOM_E_CUDA;
   moe_route_offsets<<<1, 32, 0, st>>>(R, n_unique, T);
-  const int rc = launch_gemv(d_pages, R, d_h, act, ubuf, d_y, H, I, n_unique, n_rows, min(T, n_rows), d_status, st);
+  const int rc = launch_gemv(d_pages, R, d_h, act, ubuf, d_y, H, I, n_unique, n_rows, min(T, n_rows), gate_tiles,
+                             down_tiles, s + L.seams, d_status, st);
   if (rc != VOOM_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }

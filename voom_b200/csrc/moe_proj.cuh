@@ -129,81 +129,118 @@ __device__ __forceinline__ const voom_expert_proj& pick_proj(const voom_expert_p
 }
 
 // ------------------------------------------------------------ CUDA-core path
+// A CTA takes a chunk of one tile's segments: whole rows of the tile, at most
+// 128 segments, so it holds one tile's decode tables (about 37 KB of shared
+// memory: four CTAs per SM).  A row that a tile boundary cuts ("seam row")
+// gets partial sums from the two tiles' chunks; each adds its sum into a
+// seam cell in global memory and the second to arrive (an atomic counter,
+// no waiting) writes the BF16 result and clears the cell.  With exactly two
+// fp32 addends the sum does not depend on their order, so results stay
+// deterministic.
+constexpr uint32_t kSeams = 32;  // tile boundaries per projection the seam cells cover (<= 33 tiles)
+
+struct SeamCell {
+  float v[kTok];
+  uint32_t count;
+};
+
+__host__ __device__ inline uint32_t cc_chunks_per_tile(uint32_t rows, uint32_t cols, uint32_t n_tiles) {
+  const uint32_t rb = cc_rows(cols);
+  if (n_tiles <= 1) return (rows + rb - 1) / rb;
+  const uint32_t rows_touch = (rows + n_tiles - 2) / (n_tiles - 1) + 2;  // rows meeting one tile, at most
+  return (rows_touch + rb - 1) / rb;
+}
+
 struct CcShared {
-  uint32_t lut[2][2][4096];  // [tile slot][plane]
+  uint32_t lut[2][4096];     // [plane]
   uint32_t cum[257];
   uint32_t red[8];
-  uint32_t degenerate[2][2];
-  float part[kPairs][kTok];  // [segment of the block][token]
+  uint32_t degenerate[2];
+  float part[kPairs][kTok];  // [segment of the chunk][token]
   uint32_t tok[kTok];
   uint32_t status;
+  uint32_t seam_rows;        // number of seam rows in this chunk (0..2)
+  uint32_t seam_id[2];       // their seam cell indices
+  uint32_t seam_row[2];      // their row numbers
 };
 
 // act: the tokens' input rows (h for gate/up: token index; act for down:
 // route row), ld_in columns; out0/out1: route rows x ld_out (gate / up or y).
-// With mma_on, experts with more than kTok tokens are left to moe_proj_mma;
-// otherwise grid z splits them into groups of NT tokens (each group decodes
-// the block again).
+// Grid: x = chunk slots (n_proj x tiles x chunks per tile), y = unique
+// experts.  Experts with more than kTok tokens are left to moe_proj_mma.
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 3) moe_proj_cc(const voom_expert_pages* __restrict__ pages,
+__global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pages* __restrict__ pages,
                                                            const Routes* __restrict__ R, uint32_t which,
                                                            const uint16_t* __restrict__ act, uint32_t ld_in,
                                                            uint16_t* __restrict__ out0, uint16_t* __restrict__ out1,
-                                                           uint32_t ld_out, uint32_t nbpp, uint32_t mma_on,
+                                                           uint32_t ld_out, uint32_t nbpp, uint32_t cpt,
+                                                           uint32_t tiles_hint, SeamCell* __restrict__ seams,
                                                            uint32_t* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   CcShared& sh = *reinterpret_cast<CcShared*>(smem_raw);
-  const uint32_t u = blockIdx.y, grp = blockIdx.z;
+  const uint32_t u = blockIdx.y;
   if (u >= R->n_unique) return;
   const uint32_t n = R->ntok[u];
-  if (mma_on && n > uint32_t(kTok)) return;  // the tensor-core kernel serves this expert
-  if (threadIdx.x == 0 && blockIdx.x == 0 && grp == 0 && n > gridDim.z * NT) atomicOr(status, kStatusRoutes);
-  if (grp * NT >= n) return;
-  const uint32_t ntk = min(uint32_t(NT), n - grp * NT);
+  if (n > uint32_t(kTok)) return;  // the tensor-core kernel serves this expert
+  if (threadIdx.x == 0 && blockIdx.x == 0 && n > uint32_t(NT)) atomicOr(status, kStatusRoutes);
+  const uint32_t ntk = min(uint32_t(NT), n);
   bool second;
-  uint32_t blk;
-  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, &second, &blk);
+  uint32_t slot_blk;
+  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, &second, &slot_blk);
   if (P.n_tiles == 0) return;  // this expert's pages live on another GPU
-  const uint32_t every = P.every, spr = P.cols / every;
-  const uint32_t rb = cc_rows(P.cols);
-  const uint32_t r0 = blk * rb;
-  if (r0 >= P.rows) return;
-  const uint32_t r1 = min(P.rows, r0 + rb), nseg = (r1 - r0) * spr, g0 = r0 * spr;
-  const uint32_t spt = P.tiles[0].raw_len / (2u * every);
-  const uint32_t t0 = g0 / spt, t1 = (g0 + nseg - 1u) / spt;
   const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1;
-  const bool geometry_ok = every == every_rule(P.cols) && t1 - t0 <= 1u && spt > 0;
-  const uint32_t row_base = R->uoff[u] + grp * NT;
+  const uint32_t every = P.every, spr = P.cols / every, rb = cc_rows(P.cols);
+  const uint32_t spt = P.tiles[0].raw_len / (2u * every);
+  if (P.n_tiles > tiles_hint || P.n_tiles > kSeams + 1 || every != every_rule(P.cols) || spt < spr) {
+    if (tid == 0 && slot_blk == 0) atomicOr(status, kStatusGeometry);
+    return;
+  }
+  const uint32_t t = slot_blk / cpt, c = slot_blk - t * cpt;
+  if (t >= P.n_tiles) return;
+  const voom_rans_tile tl = P.tiles[t];
+  const uint32_t ts0 = t * spt, ts1 = ts0 + tl.raw_len / (2u * every);
+  const uint32_t ra = ts0 / spr;
+  const uint32_t g0 = max(ts0, (ra + c * rb) * spr), g1 = min(ts1, (ra + (c + 1) * rb) * spr);
+  if (g0 >= g1) return;
+  const uint32_t nseg = g1 - g0;
+  const uint32_t row_base = R->uoff[u];
   if (tid < uint32_t(NT)) sh.tok[tid] = tid < ntk ? (which ? row_base + tid : R->upair[row_base + tid]) : 0u;
-  if (tid == 0) sh.status = geometry_ok ? 0u : kStatusGeometry;
-  if (geometry_ok) {
-    for (uint32_t k = 0; k <= t1 - t0; k++) {  // decode tables of the (at most two) tiles of the block
-      const voom_rans_tile& tl = P.tiles[t0 + k];
-      if (tl.mode == 1) {
-        build_lut(sh.lut[k][0], sh.cum, sh.red, &sh.degenerate[k][0], P.src + tl.low_freq);
-        build_lut(sh.lut[k][1], sh.cum, sh.red, &sh.degenerate[k][1], P.src + tl.high_freq);
-      }
+  if (tid == 0) {
+    sh.status = 0;
+    uint32_t ns = 0;
+    const uint32_t cell0 = (u * 2u + (second ? 1u : 0u)) * kSeams;
+    if (g0 == ts0 && ts0 % spr) {  // first row began in the previous tile
+      sh.seam_id[ns] = cell0 + t - 1u;
+      sh.seam_row[ns++] = g0 / spr;
     }
+    if (g1 == ts1 && ts1 % spr) {  // last row continues in the next tile
+      sh.seam_id[ns] = cell0 + t;
+      sh.seam_row[ns++] = (g1 - 1u) / spr;
+    }
+    sh.seam_rows = ns;
+  }
+  if (tl.mode == 1) {
+    build_lut(sh.lut[0], sh.cum, sh.red, &sh.degenerate[0], P.src + tl.low_freq);
+    build_lut(sh.lut[1], sh.cum, sh.red, &sh.degenerate[1], P.src + tl.high_freq);
   }
   __syncthreads();
   float acc[NT];
 #pragma unroll
   for (int j = 0; j < NT; j++) acc[j] = 0.f;
-  if (geometry_ok && p < nseg) {
-    const uint32_t g = g0 + p, t = g / spt, l = g - t * spt, slot = t - t0;
-    const uint32_t k0 = (p % spr) * every;
-    const voom_rans_tile tl = P.tiles[t];
+  if (p < nseg) {
+    const uint32_t g = g0 + p, l = g - ts0;
+    const uint32_t k0 = (g % spr) * every;
     if (tl.mode == 0) {  // stored tile: weights read directly
       const uint8_t* wsrc = P.src + tl.src + size_t(l) * every * 2u;
-      for (uint32_t c = lane * 8u; c < every; c += 16u)
-        dot8<NT>(load_stored8(wsrc + 2u * c), act, ld_in, sh.tok, ntk, k0 + c, acc);
+      for (uint32_t cc = lane * 8u; cc < every; cc += 16u)
+        dot8<NT>(load_stored8(wsrc + 2u * cc), act, ld_in, sh.tok, ntk, k0 + cc, acc);
     } else {
-      const uint32_t nseg_t = tl.raw_len / (2u * every);
+      const uint32_t nseg_t = ts1 - ts0;
       PlaneRun r;
       seg_open(r, P, tl, t, l, lane);
-      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[slot][lane][0]));
+      const uint32_t lut_s = uint32_t(__cvta_generic_to_shared(&sh.lut[lane][0]));
       const unsigned mask = 0x3u << (tid & 30u);
-      const bool degenerate = sh.degenerate[slot][lane] != 0;
+      const bool degenerate = sh.degenerate[lane] != 0;
       const uint32_t x0 = r.x, c0 = r.cur;
       // whole segment on the clamped window; a pair that does not land where
       // the encoder's stream did redoes the segment on the exact path
@@ -245,21 +282,44 @@ __global__ void __launch_bounds__(kThreads, 3) moe_proj_cc(const voom_expert_pag
   }
 #pragma unroll
   for (int j = 0; j < NT; j++) acc[j] += __shfl_xor_sync(0xFFFFFFFFu, acc[j], 1);
-  if (geometry_ok && p < nseg && lane == 0) {
+  if (p < nseg && lane == 0) {
 #pragma unroll
     for (int j = 0; j < NT; j++) sh.part[p][j] = acc[j];
   }
   __syncthreads();
-  if (geometry_ok) {
-    uint16_t* out = second ? out1 : out0;
-    for (uint32_t q = tid; q < (r1 - r0) * ntk; q += kThreads) {
-      const uint32_t row = q / ntk, j = q - row * ntk;
-      float s = 0.f;
-      for (uint32_t c = 0; c < spr; c++) s += sh.part[row * spr + c][j];
-      out[size_t(row_base + j) * ld_out + r0 + row] = uint16_t(f2bf(s));
+  // rows of the chunk: the row's segments summed in order; whole rows are
+  // written, seam rows add into their cell
+  uint16_t* out = second ? out1 : out0;
+  const uint32_t rfirst = g0 / spr, nrows = (g1 - 1u) / spr - rfirst + 1u;
+  bool added = false;
+  for (uint32_t q = tid; q < nrows * ntk; q += kThreads) {
+    const uint32_t ri = q / ntk, j = q - ri * ntk, row = rfirst + ri;
+    const uint32_t a = max(g0, row * spr), b = min(g1, (row + 1u) * spr);
+    float sum = 0.f;
+    for (uint32_t g = a; g < b; g++) sum += sh.part[g - g0][j];
+    if (b - a == spr) {
+      out[size_t(row_base + j) * ld_out + row] = uint16_t(f2bf(sum));
+    } else {
+      const uint32_t k = (sh.seam_rows > 1 && sh.seam_row[1] == row) ? 1u : 0u;
+      atomicAdd(&seams[sh.seam_id[k]].v[j], sum);
+      added = true;
     }
   }
-  if (tid == 0 && sh.status) atomicOr(status, sh.status);
+  if (added) __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    for (uint32_t k = 0; k < sh.seam_rows; k++) {  // the second chunk of a seam row finishes it
+      SeamCell& cell = seams[sh.seam_id[k]];
+      __threadfence();
+      if (atomicAdd(&cell.count, 1u) == 1u) {
+        __threadfence();
+        for (uint32_t j = 0; j < ntk; j++)
+          out[size_t(row_base + j) * ld_out + sh.seam_row[k]] = uint16_t(f2bf(atomicExch(&cell.v[j], 0.f)));
+        atomicExch(&cell.count, 0u);
+      }
+    }
+    if (sh.status) atomicOr(status, sh.status);
+  }
 }
 
 // ------------------------------------------------------- tcgen05 primitives
