@@ -137,7 +137,7 @@ __device__ __forceinline__ const voom_expert_proj& pick_proj(const voom_expert_p
 // no waiting) writes the BF16 result and clears the cell.  With exactly two
 // fp32 addends the sum does not depend on their order, so results stay
 // deterministic.
-constexpr uint32_t kSeams = 32;  // tile boundaries per projection the seam cells cover (<= 33 tiles)
+constexpr uint32_t kSeams = 64;  // tile boundaries per projection the seam cells cover (<= 65 tiles)
 
 struct SeamCell {
   float v[kTok];

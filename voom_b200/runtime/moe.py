@@ -32,9 +32,13 @@ PAGES_DTYPE = np.dtype([("gate", PROJ_DTYPE), ("up", PROJ_DTYPE), ("down", PROJ_
 assert PAGES_DTYPE.itemsize == 144
 
 
+MAX_TILES = 65  # tiles per projection the fused kernels take (kSeams + 1 in csrc/moe_proj.cuh)
+
 # Status word bits written by the fused kernels (one u32 per layer).
 STATUS_PAGE = 1    # a compressed expert page failed its checkpoint verification
 STATUS_ROUTES = 2  # an expert got more route rows than the launch covered
+STATUS_GEOMETRY = 4  # page geometry the kernels do not take (segment length, tile size or count)
+STATUS_TIMEOUT = 8  # a tensor-core completion wait ran out (reported, never observed)
 
 
 def raise_on_status(status: torch.Tensor, what: str) -> None:
@@ -50,6 +54,10 @@ def raise_on_status(status: torch.Tensor, what: str) -> None:
             parts.append("a compressed expert page failed its checkpoint verification")
         if v & STATUS_ROUTES:
             parts.append("an expert had more routed tokens than the launch covered")
+        if v & STATUS_GEOMETRY:
+            parts.append("an expert page has a geometry the fused kernels do not take")
+        if v & STATUS_TIMEOUT:
+            parts.append("a tensor-core completion wait ran out")
         raise ValueError(f"{what}: " + "; ".join(parts or [f"status 0x{v:x}"]))
 
 
@@ -90,6 +98,9 @@ class ProjPage:
             frame, _ = bf16_rans.encode(np.ascontiguousarray(w_bits).view(np.uint8),
                                         tile_bytes=tile_bytes or tile_bytes_for(cols))
         self.page = bf16_rans.RansPage(frame, device=device, every=every, stream=stream)
+        if self.page.n_tiles > MAX_TILES:
+            raise ValueError(f"a {rows}x{cols} projection in {self.page.n_tiles} tiles: the fused kernels take at "
+                             f"most {MAX_TILES} tiles per projection (use larger tiles)")
         self.frame_bytes = len(frame)
 
     def record(self) -> tuple:
