@@ -217,6 +217,51 @@ assert ZENC_BLOCK_DTYPE.itemsize == 24
 ZENC_FIRST, ZENC_LAST = 1, 2
 
 
+class EncodePlan:
+    """The block table of many frames for the GPU encoder, built once (frames
+    of more than voom_zstd_encode_block_bytes() are split into blocks) and
+    resident on `device`; run() encodes the byte ranges of a device buffer."""
+
+    def __init__(self, offsets, lengths, device):
+        lib = load()
+        self.block = int(lib.voom_zstd_encode_block_bytes())
+        self.slot = int(lib.voom_zstd_encode_slot_bytes())
+        offs = np.asarray(offsets, np.int64).reshape(-1)
+        lens = np.asarray(lengths, np.int64).reshape(-1)
+        nb = np.maximum(1, (lens + self.block - 1) // self.block)
+        first = np.zeros(nb.size, np.int64)
+        if nb.size > 1:
+            np.cumsum(nb[:-1], out=first[1:])
+        n_blocks = int(nb.sum())
+        fr = np.repeat(np.arange(nb.size), nb)
+        k = np.arange(n_blocks, dtype=np.int64) - first[fr]
+        blocks = np.zeros(n_blocks, dtype=ZENC_BLOCK_DTYPE)
+        blocks["src"] = offs[fr] + k * self.block
+        blocks["frame_len"] = lens[fr]
+        blocks["len"] = np.minimum(self.block, lens[fr] - k * self.block)
+        blocks["flags"] = np.where(k == 0, ZENC_FIRST, 0) | np.where(k == nb[fr] - 1, ZENC_LAST, 0)
+        self.n_blocks = n_blocks
+        self.frames = list(zip(first.tolist(), nb.tolist()))
+        self.first, self.nb = first, nb
+        self.device = device
+        self.d_blocks = _device.tensor_from_numpy(blocks.view(np.uint8), device) if n_blocks else None
+        self.slots = torch.empty(max(n_blocks, 1) * self.slot, dtype=torch.uint8, device=device)
+        self.sizes = torch.empty(max(2 * n_blocks, 2), dtype=torch.int32, device=device)
+
+    def run(self, d_src: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+        """Enqueue the encode of every block (no host synchronisation)."""
+        if self.n_blocks:
+            check(load().voom_zstd_encode(d_src.data_ptr(), self.d_blocks.data_ptr(), self.n_blocks,
+                                          self.slots.data_ptr(), self.sizes.data_ptr(),
+                                          _device.stream_ptr(self.device, stream)), "voom_zstd_encode")
+
+    def block_sizes(self) -> np.ndarray:
+        """(slot offset within the slot buffer, length) of every block (waits for the encode)."""
+        sz = self.sizes[:2 * self.n_blocks].cpu().numpy().view(np.uint32).reshape(-1, 2).astype(np.int64)
+        sz[:, 0] += np.arange(self.n_blocks, dtype=np.int64) * self.slot
+        return sz
+
+
 def compress_device(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda.Stream | None = None
                     ) -> tuple[torch.Tensor, np.ndarray, list[tuple[int, int]]]:
     """Compress many byte ranges of one device buffer, each into its own zstd
@@ -225,64 +270,47 @@ def compress_device(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda
     and each frame's (first block, block count).  The frames are valid
     RFC 8878 frames that zstd.decompress / compression.zstd accept; they are
     not libzstd's bytes."""
-    lib = load()
-    dev = d_src.device
-    block = int(lib.voom_zstd_encode_block_bytes())
-    slot = int(lib.voom_zstd_encode_slot_bytes())
-    rows, frames = [], []
-    for off, n in zip(offsets, lengths):
-        off, n = int(off), int(n)
-        k0 = len(rows)
-        starts = list(range(0, n, block)) or [0]
-        for k, b0 in enumerate(starts):
-            flags = (ZENC_FIRST if k == 0 else 0) | (ZENC_LAST if k == len(starts) - 1 else 0)
-            rows.append((off + b0, n, min(block, n - b0), flags))
-        frames.append((k0, len(starts)))
-    blocks = np.array(rows, dtype=ZENC_BLOCK_DTYPE) if rows else np.zeros(0, ZENC_BLOCK_DTYPE)
-    n_blocks = len(rows)
-    with torch.cuda.device(dev):
-        d_blocks = _device.tensor_from_numpy(blocks.view(np.uint8), dev) if n_blocks else None
-        slots = torch.empty(max(n_blocks, 1) * slot, dtype=torch.uint8, device=dev)
-        sizes = torch.empty(max(2 * n_blocks, 2), dtype=torch.int32, device=dev)
-        if n_blocks:
-            check(lib.voom_zstd_encode(d_src.data_ptr(), d_blocks.data_ptr(), n_blocks, slots.data_ptr(),
-                                       sizes.data_ptr(), _device.stream_ptr(dev, stream)), "voom_zstd_encode")
-        sz = sizes[:2 * n_blocks].cpu().numpy().view(np.uint32).reshape(-1, 2).astype(np.int64)
-    sz[:, 0] += np.arange(n_blocks, dtype=np.int64) * slot
-    return slots, sz, frames
+    plan = EncodePlan(offsets, lengths, d_src.device)
+    with torch.cuda.device(d_src.device):
+        plan.run(d_src, stream)
+        sz = plan.block_sizes()
+    return plan.slots, sz, plan.frames
 
 
 def compress_many(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda.Stream | None = None,
-                  pinned: torch.Tensor | None = None) -> list[bytes]:
-    """compress_device, then every frame as host bytes: the blocks are packed
-    on the device and cross to the host in one copy (into `pinned` when it is
-    a large enough pinned buffer)."""
-    slots, sz, frames = compress_device(d_src, offsets, lengths, stream=stream)
+                  pinned: torch.Tensor | None = None, plan: EncodePlan | None = None) -> list[bytes]:
+    """Every byte range compressed into a zstd frame on the GPU, returned as
+    host bytes: the blocks are packed on the device and cross to the host in
+    one copy (into `pinned` when it is a large enough pinned buffer).  A plan
+    built once for the same ranges may be passed."""
+    plan = plan or EncodePlan(offsets, lengths, d_src.device)
+    dev = d_src.device
+    with torch.cuda.device(dev):
+        plan.run(d_src, stream)
+        sz = plan.block_sizes()
     n_blocks = sz.shape[0]
     if n_blocks == 0:
-        return [b"" for _ in frames]
-    dev = d_src.device
+        return [b"" for _ in plan.frames]
     dst = np.zeros(n_blocks, np.uint64)
     np.cumsum(sz[:-1, 1], out=dst[1:])
     total = int(dst[-1] + sz[-1, 1])
     rel = sz.copy()
-    rel[:, 0] -= np.arange(n_blocks, dtype=np.int64) * int(load().voom_zstd_encode_slot_bytes())
+    rel[:, 0] -= np.arange(n_blocks, dtype=np.int64) * plan.slot
     d_sizes = _device.tensor_from_numpy(rel.astype(np.uint32), dev)
     d_dst = _device.tensor_from_numpy(dst, dev)
     packed = torch.empty(max(total, 1), dtype=torch.uint8, device=dev)
-    check(load().voom_zstd_encode_pack(slots.data_ptr(), d_sizes.data_ptr(), d_dst.data_ptr(), n_blocks,
+    check(load().voom_zstd_encode_pack(plan.slots.data_ptr(), d_sizes.data_ptr(), d_dst.data_ptr(), n_blocks,
                                        packed.data_ptr(), _device.stream_ptr(dev, stream)), "voom_zstd_encode_pack")
     if pinned is not None and pinned.numel() >= total:
         pinned[:total].copy_(packed[:total])
         host = pinned.numpy()
     else:
         host = packed[:total].cpu().numpy()
-    out = []
-    for b0, nb in frames:
-        a = int(dst[b0])
-        e = int(dst[b0 + nb - 1] + sz[b0 + nb - 1, 1])
-        out.append(host[a:e].tobytes())
-    return out
+    starts = dst[plan.first].astype(np.int64)
+    last = plan.first + plan.nb - 1
+    ends = (dst[last] + sz[last, 1].astype(np.uint64)).astype(np.int64)
+    mv = memoryview(host)
+    return [bytes(mv[a:e]) for a, e in zip(starts.tolist(), ends.tolist())]
 
 
 def compress(data, level: int = 1) -> bytes:
