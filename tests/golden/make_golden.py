@@ -28,7 +28,11 @@ from voom_b200 import synthetic  # noqa: E402
 
 
 def _reference_path() -> Path:
-    p = Path(os.environ.get("VOOM_REFERENCE", "/root/reference"))
+    """The reference checkout named by $VOOM_REFERENCE."""
+    env = os.environ.get("VOOM_REFERENCE")
+    if not env:
+        raise SystemExit("set VOOM_REFERENCE to a checkout of the reference (KyleBoyer/vOOM)")
+    p = Path(env)
     if not (p / "formats" / "bf16_rans.py").exists():
         raise SystemExit(f"reference checkout not found at {p}")
     return p

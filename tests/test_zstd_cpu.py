@@ -130,26 +130,6 @@ def test_planner_direct_jobs_and_segments(built_lib):
     assert only_direct.info.n_direct_jobs == 8 and only_direct.info.scratch_bytes < (2 << 20)  # worklists only
 
 
-def test_cabi_example_frames(built_lib, tmp_path):
-    """The C-ABI example's frame files: jobs cover the source back to back,
-    the planner takes them as direct jobs, and libzstd decodes each frame to
-    its slice of raw.bin."""
-    from voom_b200.cabi_example import make_kv_frames
-    from voom_b200.formats import zstd_gpu as Z
-
-    make_kv_frames.main(str(tmp_path), 6)
-    src = np.fromfile(tmp_path / "src.bin", np.uint8)
-    jobs = np.fromfile(tmp_path / "jobs.bin", Z.JOB_DTYPE)
-    raw = np.fromfile(tmp_path / "raw.bin", np.uint8)
-    assert jobs.size == 12 and int(jobs["src"][-1] + jobs["src_len"][-1]) == src.size
-    assert int(jobs["dst"][-1] + jobs["dst_len"][-1]) == raw.size
-    for j in jobs:
-        fr = src[int(j["src"]):int(j["src"] + j["src_len"])].tobytes()
-        assert oz.libzstd_decompress(fr, int(j["dst_len"])) == raw[int(j["dst"]):int(j["dst"] + j["dst_len"])].tobytes()
-    plan = Z.ZstdPlan(src, jobs)
-    assert plan.info.n_direct_jobs + plan.info.n_bad_jobs <= 12 and not plan.plan_status.any()
-
-
 def test_planner_direct_decision_edges(built_lib):
     """Direct (straight-to-output) planning only when every block size is
     known and adds up: raw blocks and multi-frame jobs qualify; a job length
@@ -171,26 +151,3 @@ def test_planner_direct_decision_edges(built_lib):
             plan = Z.ZstdPlan(np.frombuffer(frame + bytes(n + extra), np.uint8), job)
             assert plan.info.n_direct_jobs == int(want), (name, extra, flags)
             assert plan.plan_status[0] == 0
-
-
-def test_cabi_example_vpack_bodies(built_lib, tmp_path):
-    """The C-ABI example's vpack files (config-2 bodies, two layers): one
-    interleaved job per body, outputs back to back, and the oracle's
-    decode_body of every body equals its slice of raw.bin."""
-    from oracle import vpack as ov
-    from voom_b200.cabi_example import make_vpack_bodies
-    from voom_b200.formats import zstd_gpu as Z
-
-    make_vpack_bodies.main(str(tmp_path), 2)
-    src = np.fromfile(tmp_path / "src.bin", np.uint8)
-    jobs = np.fromfile(tmp_path / "jobs.bin", Z.JOB_DTYPE)
-    raw = np.fromfile(tmp_path / "raw.bin", np.uint8)
-    assert (jobs["flags"] & Z.INTERLEAVE).all()
-    assert int(jobs["dst"][-1] + 2 * jobs["dst_len"][-1]) == raw.size
-    for j in jobs[:6]:
-        head = {"hi_z": int(j["src_len"]), "lo": int(j["dst_len"])}
-        body = src[int(j["src"]):int(j["src"] + j["src_len"] + j["dst_len"])]
-        got = ov.decode_body(head, body)
-        assert got.tobytes() == raw[int(j["dst"]):int(j["dst"] + 2 * j["dst_len"])].tobytes()
-    plan = Z.ZstdPlan(src, jobs)
-    assert plan.info.n_jobs == jobs.size and not plan.plan_status.any()
