@@ -492,7 +492,7 @@ int voom_moe_experts_v(const voom_moe_variant* v, const voom_expert_pages* d_pag
  * that reach this library only through the C ABI and have no CUDA allocator.
  * It has no counterpart in the reference.
  * Same arguments and results as voom_moe_layer minus d_scratch /
- * scratch_bytes: the scratch is one fixed device array (about 7 MiB) per GPU,
+ * scratch_bytes: the scratch is one fixed device array (about 8.5 MiB) per GPU,
  * loaded with the library and held until the process exits.  Limits:
  * T <= 64, T * top_k <= 256, H <= 8192, I <= 4096; larger calls return
  * VOOM_E_CAPACITY without launching anything.  Nothing in the array needs
