@@ -404,8 +404,25 @@ struct ScratchLayout {
   uint64_t routes, h, logits, act, y, seams, seam_bytes, total;
 };
 
-// Seam cells of the CUDA-core kernel: two projections' worth per unique expert.
-uint64_t seam_bytes(uint32_t max_unique) { return uint64_t(max_unique) * 2 * kSeams * sizeof(SeamCell); }
+// Work counters (256 bytes) and seam cells of the CUDA-core kernel: two
+// projections' worth of cells per unique expert.
+constexpr uint64_t kCounterBytes = 256;
+uint64_t seam_bytes(uint32_t max_unique) {
+  return kCounterBytes + uint64_t(max_unique) * 2 * kSeams * sizeof(SeamCell);
+}
+
+// CTAs of the persistent CUDA-core kernel: four per SM of the current device.
+uint32_t cc_grid() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148 * 4;
+  if (!sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  return uint32_t(sms[dev]) * 4u;
+}
 
 ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
   ScratchLayout s;
@@ -429,12 +446,15 @@ ScratchLayout layout(uint32_t T, uint32_t H, uint32_t I, uint32_t k) {
 template <int NT>
 int launch_cc(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in, uint32_t ld_in,
               uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t nbpp, uint32_t n_proj, uint32_t cpt,
-              uint32_t tiles, uint32_t n_unique, SeamCell* seams, uint32_t* d_status, cudaStream_t st) {
+              uint32_t tiles, uint32_t n_unique, SeamCell* seams, uint32_t* counter, uint32_t* d_status,
+              cudaStream_t st) {
   const size_t smem = sizeof(CcShared);
   if (cudaFuncSetAttribute(moe_proj_cc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return VOOM_E_CUDA;
-  moe_proj_cc<NT><<<dim3(n_proj * nbpp, n_unique, 1), kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1,
-                                                                             ld_out, nbpp, cpt, tiles, seams, d_status);
+  const uint32_t items = n_unique * n_proj * nbpp;
+  const uint32_t grid = min(cc_grid(), max(1u, items));
+  moe_proj_cc<NT><<<grid, kThreads, smem, st>>>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt,
+                                                tiles, seams, counter, d_status);
   return VOOM_OK;
 }
 
@@ -443,23 +463,23 @@ int launch_cc(const voom_expert_pages* d_pages, const Routes* R, uint32_t which,
 int launch_proj(const voom_expert_pages* d_pages, const Routes* R, uint32_t which, const uint16_t* in,
                 uint32_t ld_in, uint16_t* out0, uint16_t* out1, uint32_t ld_out, uint32_t rows, uint32_t cols,
                 uint32_t tiles, uint32_t n_proj, uint32_t n_unique, uint32_t max_tok, SeamCell* seams,
-                uint32_t* d_status, cudaStream_t st) {
+                uint32_t* counter, uint32_t* d_status, cudaStream_t st) {
   const uint32_t t = max(1u, tiles);
   const uint32_t cpt = cc_chunks_per_tile(rows, cols, t), nbpp = t * cpt;
   const uint32_t ntok = min(max_tok, uint32_t(kTok));
   int rc;
   if (ntok <= 1)
     rc = launch_cc<1>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
-                      d_status, st);
+                      counter, d_status, st);
   else if (ntok <= 2)
     rc = launch_cc<2>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
-                      d_status, st);
+                      counter, d_status, st);
   else if (ntok <= 4)
     rc = launch_cc<4>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
-                      d_status, st);
+                      counter, d_status, st);
   else
     rc = launch_cc<8>(d_pages, R, which, in, ld_in, out0, out1, ld_out, nbpp, n_proj, cpt, t, n_unique, seams,
-                      d_status, st);
+                      counter, d_status, st);
   if (rc != VOOM_OK || max_tok <= uint32_t(kTok)) return rc;
   const uint32_t ncap = (min(max_tok, kMmaMaxN) + 15u) & ~15u;
   const uint32_t zc = (max_tok + kMmaMaxN - 1) / kMmaMaxN;
@@ -481,11 +501,14 @@ int launch_gemv(const voom_expert_pages* d_pages, const Routes* R, const uint16_
                 uint32_t max_tok, uint32_t gate_tiles, uint32_t down_tiles, void* seams, uint32_t* d_status,
                 cudaStream_t st) {
   if (cudaMemsetAsync(seams, 0, seam_bytes(n_unique), st) != cudaSuccess) return VOOM_E_CUDA;
-  SeamCell* sc = static_cast<SeamCell*>(seams);
-  int rc = launch_proj(d_pages, R, 0, h, H, act, ubuf, I, I, H, gate_tiles, 2, n_unique, max_tok, sc, d_status, st);
+  uint32_t* counters = static_cast<uint32_t*>(seams);
+  SeamCell* sc = reinterpret_cast<SeamCell*>(static_cast<uint8_t*>(seams) + kCounterBytes);
+  int rc = launch_proj(d_pages, R, 0, h, H, act, ubuf, I, I, H, gate_tiles, 2, n_unique, max_tok, sc, counters,
+                       d_status, st);
   if (rc != VOOM_OK) return rc;
   moe_act<<<dim3((I / 8 + 127) / 128, max_rows), 128, 0, st>>>(R, act, ubuf, I);
-  return launch_proj(d_pages, R, 1, act, I, y, y, H, H, I, down_tiles, 1, n_unique, max_tok, sc, d_status, st);
+  return launch_proj(d_pages, R, 1, act, I, y, y, H, H, I, down_tiles, 1, n_unique, max_tok, sc, counters + 1,
+                     d_status, st);
 }
 
 // The generic family with no shared expert: what the variant-less entry
@@ -668,7 +691,7 @@ constexpr uint64_t kNoAllocBytes =
     uint64_t(kNoAllocMaxT) * kMaxE * 4 +
     ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxI * 2 + 16 + 255) & ~uint64_t(255)) +
     ((uint64_t(kNoAllocMaxRoutes) * kNoAllocMaxH * 2 + 16 + 255) & ~uint64_t(255)) +
-    ((uint64_t(kNoAllocMaxRoutes) * 2 * kSeams * sizeof(SeamCell) + 255) & ~uint64_t(255));
+    ((256 + uint64_t(kNoAllocMaxRoutes) * 2 * kSeams * sizeof(SeamCell) + 255) & ~uint64_t(255));
 
 __device__ __align__(256) uint8_t g_moe_scratch[kNoAllocBytes];
 

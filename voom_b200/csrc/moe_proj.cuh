@@ -119,12 +119,13 @@ __device__ __forceinline__ uint4 load_stored8(const uint8_t* p) {
   return make_uint4(v[0], v[1], v[2], v[3]);
 }
 
-// Projection a CTA works on: gate (blockIdx.x < nbpp) or up for which = 0,
-// down for which = 1; *blk = the row block within it.
+// Projection of work slot `bx`: gate (bx < nbpp) or up for which = 0, down
+// for which = 1; *blk = the block within it.
 __device__ __forceinline__ const voom_expert_proj& pick_proj(const voom_expert_pages& E, uint32_t which,
-                                                             uint32_t nbpp, bool* second, uint32_t* blk) {
-  *second = which == 0 && blockIdx.x >= nbpp;
-  *blk = *second ? blockIdx.x - nbpp : blockIdx.x;
+                                                             uint32_t nbpp, uint32_t bx, bool* second,
+                                                             uint32_t* blk) {
+  *second = which == 0 && bx >= nbpp;
+  *blk = *second ? bx - nbpp : bx;
   return which ? E.down : (*second ? E.up : E.gate);
 }
 
@@ -164,29 +165,25 @@ struct CcShared {
   uint32_t seam_row[2];      // their row numbers
 };
 
-// act: the tokens' input rows (h for gate/up: token index; act for down:
-// route row), ld_in columns; out0/out1: route rows x ld_out (gate / up or y).
-// Grid: x = chunk slots (n_proj x tiles x chunks per tile), y = unique
-// experts.  Experts with more than kTok tokens are left to moe_proj_mma.
+// One work item of the CUDA-core kernel: chunk slot `bx` (of n_proj x
+// tiles x chunks per tile) of unique expert u.  act: the tokens' input rows
+// (h for gate/up: token index; act for down: route row), ld_in columns;
+// out0/out1: route rows x ld_out (gate / up or y).  Experts with more than
+// kTok tokens are left to moe_proj_mma.  Ends with a block barrier.
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pages* __restrict__ pages,
-                                                           const Routes* __restrict__ R, uint32_t which,
-                                                           const uint16_t* __restrict__ act, uint32_t ld_in,
-                                                           uint16_t* __restrict__ out0, uint16_t* __restrict__ out1,
-                                                           uint32_t ld_out, uint32_t nbpp, uint32_t cpt,
-                                                           uint32_t tiles_hint, SeamCell* __restrict__ seams,
-                                                           uint32_t* status) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  CcShared& sh = *reinterpret_cast<CcShared*>(smem_raw);
-  const uint32_t u = blockIdx.y;
-  if (u >= R->n_unique) return;
+__device__ __forceinline__ void cc_item(CcShared& sh, const voom_expert_pages* __restrict__ pages,
+                                        const Routes* __restrict__ R, uint32_t which, uint32_t u, uint32_t bx,
+                                        const uint16_t* __restrict__ act, uint32_t ld_in,
+                                        uint16_t* __restrict__ out0, uint16_t* __restrict__ out1, uint32_t ld_out,
+                                        uint32_t nbpp, uint32_t cpt, uint32_t tiles_hint,
+                                        SeamCell* __restrict__ seams, uint32_t* status) {
   const uint32_t n = R->ntok[u];
   if (n > uint32_t(kTok)) return;  // the tensor-core kernel serves this expert
-  if (threadIdx.x == 0 && blockIdx.x == 0 && n > uint32_t(NT)) atomicOr(status, kStatusRoutes);
+  if (threadIdx.x == 0 && bx == 0 && n > uint32_t(NT)) atomicOr(status, kStatusRoutes);
   const uint32_t ntk = min(uint32_t(NT), n);
   bool second;
   uint32_t slot_blk;
-  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, &second, &slot_blk);
+  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, bx, &second, &slot_blk);
   if (P.n_tiles == 0) return;  // this expert's pages live on another GPU
   const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1;
   const uint32_t every = P.every, spr = P.cols / every, rb = cc_rows(P.cols);
@@ -319,6 +316,36 @@ __global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pag
       }
     }
     if (sh.status) atomicOr(status, sh.status);
+  }
+  __syncthreads();  // the next item reuses the shared memory
+}
+
+// Persistent CUDA-core kernel: a grid of a few CTAs per SM pulls items
+// (unique expert, chunk slot) from a global counter until none are left, so
+// the uneven chunks of the routed experts spread evenly over the SMs.
+// counter: zero before the launch.
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pages* __restrict__ pages,
+                                                           const Routes* __restrict__ R, uint32_t which,
+                                                           const uint16_t* __restrict__ act, uint32_t ld_in,
+                                                           uint16_t* __restrict__ out0, uint16_t* __restrict__ out1,
+                                                           uint32_t ld_out, uint32_t nbpp, uint32_t n_proj,
+                                                           uint32_t cpt, uint32_t tiles_hint,
+                                                           SeamCell* __restrict__ seams, uint32_t* counter,
+                                                           uint32_t* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  CcShared& sh = *reinterpret_cast<CcShared*>(smem_raw);
+  __shared__ uint32_t s_item;
+  const uint32_t per_u = n_proj * nbpp, total = R->n_unique * per_u;
+  for (;;) {
+    if (threadIdx.x == 0) s_item = atomicAdd(counter, 1u);
+    __syncthreads();
+    const uint32_t item = s_item;
+    __syncthreads();
+    if (item >= total) break;
+    const uint32_t u = item / per_u;
+    cc_item<NT>(sh, pages, R, which, u, item - u * per_u, act, ld_in, out0, out1, ld_out, nbpp, cpt, tiles_hint,
+                seams, status);
   }
 }
 
@@ -464,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_proj_mma(const voom_expert_pa
   const uint32_t nz = min(n - j0, kMmaMaxN), N = (nz + 15u) & ~15u;
   bool second;
   uint32_t blk;
-  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, &second, &blk);
+  const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, blockIdx.x, &second, &blk);
   if (P.n_tiles == 0) return;
   const uint32_t r0 = blk * kMmaRows;
   if (r0 >= P.rows) return;
