@@ -16,7 +16,7 @@
 //                shared memory and are added in segment order, so results do
 //                not depend on scheduling.
 //  moe_proj_mma  experts with more than 8 tokens (batched decode, prefill).
-//                CTA = 128 rows.  Lane pair p decodes row p in K-steps of 128
+//                CTA = 128 rows.  Lane pair p decodes row p in K-steps of 64
 //                elements into a shared-memory A tile laid out for UMMA
 //                (K-major, no swizzle: 8 x 16-byte core matrices); the
 //                tokens' activations form the B tile; one thread issues
@@ -43,6 +43,10 @@ namespace moe {
 
 using namespace voom::rans;
 
+#ifndef VOOM_EVERY_MAX
+#define VOOM_EVERY_MAX 256
+#endif
+
 constexpr int kPairs = kThreads / 2;   // lane pairs of a CTA: one segment each
 constexpr uint32_t kStatusPage = 1u;      // a segment missed its checkpoint (damaged page)
 constexpr uint32_t kStatusRoutes = 2u;    // an expert has more tokens than the launch covers
@@ -50,7 +54,7 @@ constexpr uint32_t kStatusGeometry = 4u;  // page geometry the kernels do not ta
 constexpr uint32_t kStatusTimeout = 8u;   // a tensor-core completion wait ran out
 
 __host__ __device__ inline uint32_t every_rule(uint32_t cols) {
-  uint32_t e = 512;
+  uint32_t e = VOOM_EVERY_MAX;
   while (e > 64 && cols % e) e >>= 1;
   return cols % e ? 0u : e;
 }
@@ -351,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pag
 
 // ------------------------------------------------------- tcgen05 primitives
 constexpr uint32_t kMmaRows = 128;  // UMMA M: weight rows of a CTA, one per TMEM lane
-constexpr uint32_t kMmaK = 128;     // K elements per shared-memory stage
+constexpr uint32_t kMmaK = 64;      // K elements per shared-memory stage (small: two CTAs per SM)
 constexpr uint32_t kMmaMaxN = 256;  // tokens per CTA (UMMA N <= 256)
 constexpr uint32_t kMbarSpin = 1u << 20;  // bounded completion waits
 
@@ -475,7 +479,7 @@ __device__ __forceinline__ uint32_t tmem_cols(uint32_t n) {
 // multiple of 16, <= 256) the launch sized shared memory for.  Grid: x = row
 // blocks of 128 (gate then up for which = 0), y = unique experts, z = chunks
 // of 256 tokens.
-__global__ void __launch_bounds__(kThreads, 1) moe_proj_mma(const voom_expert_pages* __restrict__ pages,
+__global__ void __launch_bounds__(kThreads, 2) moe_proj_mma(const voom_expert_pages* __restrict__ pages,
                                                             const Routes* __restrict__ R, uint32_t which,
                                                             const uint16_t* __restrict__ act, uint32_t ld_in,
                                                             uint16_t* __restrict__ out0, uint16_t* __restrict__ out1,

@@ -61,7 +61,7 @@ def raise_on_status(status: torch.Tensor, what: str) -> None:
         raise ValueError(f"{what}: " + "; ".join(parts or [f"status 0x{v:x}"]))
 
 
-def every_for(cols: int, longest: int = 512) -> int:
+def every_for(cols: int, longest: int = 256) -> int:
     """Checkpoint interval for rows of `cols` elements: the longest power of
     two <= `longest` (and >= 64) dividing the row, so a lane pair of the
     fused kernels decodes whole row segments.  The fused kernels size their
