@@ -351,12 +351,14 @@ struct K1Shared {
   uint32_t huf3[2048];  // up to 3 symbols per lookup: s0|s1<<8|s2<<16|bits<<24|count<<28
   uint16_t huf[2048];
   uint16_t sstart[256];
+  // sequence decode cells (RFC 8878 3.1.1.3.2.1.1): bytes 0-1 = byte offset of
+  // the next state's first cell, byte 2 = 32 - state bits, byte 3 = extra bits
+  // (OF: the offset code); LL / ML high word = the code's baseline value |
+  // state bits << 24
   uint32_t of[256];
-  // sequence decode cells: low word = state base | nbBits << 16 | extra bits << 24,
-  // high word = the code's baseline value (RFC 8878 3.1.1.3.2.1.1)
   uint2 ll2[512], ml2[512];
   uint4 sring[128];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 127
-  uint4 skeep[32];   // per sequence of the current batch: bit position, LL, ML, OF states
+  uint4 skeep[32];   // per sequence of the current batch: bit position, LL, ML, OF cell offsets
   uint16_t next[3][64];
   uint16_t fse_start[64];
   int al[3];
@@ -851,18 +853,23 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
   fse_build_warp<1>(v.fse[b.fse[1]], sh.of, sh.next[1], sh.fse_start, &sh.al[1]);
   fse_build_warp<2>(v.fse[b.fse[2]], reinterpret_cast<uint32_t*>(sh.ml2), sh.next[2], sh.fse_start, &sh.al[2]);
   {
+    // cells hold the byte offset of the next state's first cell (state base x
+    // cell size) so the next address is one shift-add of the state bits, and
+    // 32 - state bits as the right shift that extracts them
     const uint32_t nll = 1u << sh.al[0], nof = 1u << sh.al[1], nml = 1u << sh.al[2];
     for (uint32_t u = lane; u < nll; u += 32) {
-      const uint32_t t = sh.ll2[u].x, c = min(t & 0xFFu, 35u);
-      sh.ll2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ll_bits[c]) << 24), c_ll_base[c]);
+      const uint32_t t = sh.ll2[u].x, c = min(t & 0xFFu, 35u), nb = (t >> 8) & 0xFFu;
+      sh.ll2[u] = make_uint2(((t >> 16) << 3) | ((32u - nb) << 16) | (uint32_t(c_ll_bits[c]) << 24),
+                             c_ll_base[c] | (nb << 24));
     }
     for (uint32_t u = lane; u < nml; u += 32) {
-      const uint32_t t = sh.ml2[u].x, c = min(t & 0xFFu, 52u);
-      sh.ml2[u] = make_uint2((t >> 16) | (((t >> 8) & 0xFFu) << 16) | (uint32_t(c_ml_bits[c]) << 24), c_ml_base[c]);
+      const uint32_t t = sh.ml2[u].x, c = min(t & 0xFFu, 52u), nb = (t >> 8) & 0xFFu;
+      sh.ml2[u] = make_uint2(((t >> 16) << 3) | ((32u - nb) << 16) | (uint32_t(c_ml_bits[c]) << 24),
+                             c_ml_base[c] | (nb << 24));
     }
     for (uint32_t u = lane; u < nof; u += 32) {
-      const uint32_t t = sh.of[u];
-      sh.of[u] = (t >> 16) | (((t >> 8) & 0xFFu) << 16) | (min(t & 0xFFu, 31u) << 24);
+      const uint32_t t = sh.of[u], nb = (t >> 8) & 0xFFu;
+      sh.of[u] = ((t >> 16) << 2) | ((32u - nb) << 16) | (min(t & 0xFFu, 31u) << 24);
     }
   }
   __syncwarp();
@@ -916,30 +923,35 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       return __funnelshift_r(e.x, e.y, uint32_t(a));  // shifts by a & 31
     };
     const uint32_t a0 = sh.al[0], a1 = sh.al[1], a2 = sh.al[2];
-    uint32_t sll = 0, sof = 0, sml = 0;
+    const char* cll = reinterpret_cast<const char*>(sh.ll2);
+    const char* cml = reinterpret_cast<const char*>(sh.ml2);
+    const char* cof = reinterpret_cast<const char*>(sh.of);
+    // cell byte offsets of the current LL, ML and OF states
+    uint32_t oll = 0, oof = 0, oml = 0;
     if (Pa - boff < int32_t(a0 + a1 + a2)) {
       st = VOOM_ZSTD_ST_SEQUENCES;
     } else {
       const uint32_t init = at(Pa - int32_t(a0 + a1 + a2));
-      sml = bfe32(init, 0, a2);
-      sof = bfe32(init, a2, a1);
-      sll = bfe32(init, a1 + a2, a0);
+      oml = bfe32(init, 0, a2) << 3;
+      oof = bfe32(init, a2, a1) << 2;
+      oll = bfe32(init, a1 + a2, a0) << 3;
       Pa -= int32_t(a0 + a1 + a2);
     }
     const uint32_t nseq = b.nseq;
-    // The walk records each sequence's bit position and states in skeep;
-    // after every 32 sequences lane j extracts the fields of the batch's
-    // sequence j and stores its record, so the walk itself carries only the
-    // state chain.  The 32 positions of a batch stay inside the ring: a
-    // sequence spans at most 89 bits and the ring is refilled 32 entries at a
+    // The walk records each sequence's bit position and cell offsets in
+    // skeep; after every 32 sequences lane j extracts the fields of the
+    // batch's sequence j and stores its record, so the walk itself carries
+    // only the state chain.  The 32 positions of a batch stay inside the ring:
+    // a sequence spans at most 89 bits and the ring is refilled 32 entries at a
     // time.
     auto flush = [&](uint32_t first, uint32_t count) {
       __syncwarp();
       if (uint32_t(lane) < count) {
         const uint4 k = sh.skeep[lane];
         const int32_t myPa = int32_t(k.x);
-        const uint2 eLL = sh.ll2[k.y], eML = sh.ml2[k.z];
-        const uint32_t eOF = sh.of[k.w];
+        const uint2 eLL = *reinterpret_cast<const uint2*>(cll + k.y);
+        const uint2 eML = *reinterpret_cast<const uint2*>(cml + k.z);
+        const uint32_t eOF = *reinterpret_cast<const uint32_t*>(cof + k.w);
         const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
                        llb = __byte_perm(eLL.x, 0, 0x4443);
         // offset extra (<= 31 bits) at the top of the word below the
@@ -948,8 +960,8 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
         // funnel shift by 32 gives 0)
         const uint32_t w1 = at(myPa - 32), w2 = at(myPa - int32_t(ofc) - 32);
         const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
-        const uint32_t ml = eML.y + __funnelshift_rc(w2, 0u, 32u - mlb);
-        const uint32_t ll = eLL.y + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
+        const uint32_t ml = (eML.y & 0xFFFFFFu) + __funnelshift_rc(w2, 0u, 32u - mlb);
+        const uint32_t ll = (eLL.y & 0xFFFFFFu) + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
         ZSeq* r = out + first + lane;  // raw record; zstd_seq_scan fills offsets and positions
         *reinterpret_cast<uint2*>(&r->ll) = make_uint2(ll, ml);
         r->oval = ofv;
@@ -969,27 +981,38 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
           __syncwarp();
         }
       };
-      // one sequence that reads state bits (every sequence but the last)
+      // One sequence that reads state bits (every sequence but the last).
+      // The 96 stream bits under the position come from one ring entry read
+      // beside the three cells (its address depends on the position only),
+      // so the chain from one state to the next holds a single shared-memory
+      // read: cells -> extra-bit count -> the 32 bits under the extras -> the
+      // three state fields -> the next cells' offsets.
       auto step = [&](uint4* keep) {
         refill();
-        const uint2 eLL = sh.ll2[sll], eML = sh.ml2[sml];
-        const uint32_t eOF = sh.of[sof];
-        *keep = make_uint4(uint32_t(Pa), sll, sml, sof);  // same value from every lane
-        // cell bytes: [0,1] next-state base, [2] state bits, [3] extra bits
-        const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
-                       llb = __byte_perm(eLL.x, 0, 0x4443);
-        const uint32_t nLL = __byte_perm(eLL.x, 0, 0x4442), nML = __byte_perm(eML.x, 0, 0x4442),
-                       nOF = __byte_perm(eOF, 0, 0x4442);
-        const uint32_t ox = ofc + mlb + llb;  // extra bits, then the state bits
-        const uint32_t ns = nLL + nML;
-        // LL, ML, OF state bits (<= 26) at the top of the word below the extras
-        const uint32_t w3 = at(Pa - int32_t(ox) - 32);
-        sll = (eLL.x & 0xFFFFu) + __funnelshift_rc(w3, 0u, 32u - nLL);
-        sml = (eML.x & 0xFFFFu) + __funnelshift_rc(w3 << nLL, 0u, 32u - nML);
-        sof = (eOF & 0xFFFFu) + __funnelshift_rc(w3 << ns, 0u, 32u - nOF);
+        const uint2 eLL = *reinterpret_cast<const uint2*>(cll + oll);
+        const uint2 eML = *reinterpret_cast<const uint2*>(cml + oml);
+        const uint32_t eOF = *reinterpret_cast<const uint32_t*>(cof + oof);
+        const uint32_t p96 = uint32_t(Pa - 96);  // >= 32 * lo_w after refill()
+        const uint4 e = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(sh.sring) +
+                                                        ((p96 >> 1) & 0x7F0u));
+        *keep = make_uint4(uint32_t(Pa), oll, oml, oof);  // same value from every lane
+        // stream bits [Pa - 96, Pa) as lo | mid | hi (funnel shifts by p96 & 31)
+        const uint32_t lo = __funnelshift_r(e.x, e.y, p96), mid = __funnelshift_r(e.y, e.z, p96),
+                       hi = __funnelshift_r(e.z, e.w, p96);
+        const uint32_t ox = __byte_perm(eOF, 0, 0x4443) + __byte_perm(eML.x, 0, 0x4443) +
+                            __byte_perm(eLL.x, 0, 0x4443);  // extra bits, <= 63
+        const uint32_t nLL = eLL.y >> 24, nML = eML.y >> 24;
+        const uint32_t nLM = nLL + nML;
+        // the 32 bits under the extras (the LL, ML, OF state bits at the top)
+        const uint32_t w = ox < 32u ? __funnelshift_l(mid, hi, ox) : __funnelshift_l(lo, mid, ox);
+        const uint32_t sLL = __byte_perm(eLL.x, 0, 0x4442), sML = __byte_perm(eML.x, 0, 0x4442),
+                       sOF = __byte_perm(eOF, 0, 0x4442);
+        oll = (eLL.x & 0xFFFFu) + (__funnelshift_rc(w, 0u, sLL) << 3);
+        oml = (eML.x & 0xFFFFu) + (__funnelshift_rc(w << nLL, 0u, sML) << 3);
+        oof = (eOF & 0xFFFFu) + (__funnelshift_rc(w << nLM, 0u, sOF) << 2);
         // A stream that runs out reads zero words below its start (never
         // memory outside it) and ends with Pa below boff: checked once below.
-        Pa -= int32_t(ox + ns + nOF);
+        Pa -= int32_t(ox + nLM + 32u - sOF);
       };
       for (uint32_t first = 0; first + 1 < nseq; first += 32) {
         const uint32_t cnt = min(32u, nseq - 1 - first);
@@ -1005,9 +1028,10 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
       }
       if (nseq) {  // the last sequence: extra bits only
         refill();
-        sh.skeep[0] = make_uint4(uint32_t(Pa), sll, sml, sof);
-        const uint32_t ofc = __byte_perm(sh.of[sof], 0, 0x4443), mlb = __byte_perm(sh.ml2[sml].x, 0, 0x4443),
-                       llb = __byte_perm(sh.ll2[sll].x, 0, 0x4443);
+        sh.skeep[0] = make_uint4(uint32_t(Pa), oll, oml, oof);
+        const uint32_t ofc = __byte_perm(*reinterpret_cast<const uint32_t*>(cof + oof), 0, 0x4443),
+                       mlb = __byte_perm(reinterpret_cast<const uint2*>(cml + oml)->x, 0, 0x4443),
+                       llb = __byte_perm(reinterpret_cast<const uint2*>(cll + oll)->x, 0, 0x4443);
         Pa -= int32_t(ofc + mlb + llb);
         flush(nseq - 1, 1);
       }
