@@ -347,28 +347,37 @@ __device__ void fse_build_warp(const ZFse& f, uint32_t* t, uint16_t* next, uint1
   __syncwarp();
 }
 
-struct K1Shared {
-  uint32_t huf3[2048];  // up to 3 symbols per lookup: s0|s1<<8|s2<<16|bits<<24|count<<28
-  uint16_t huf[2048];
-  uint16_t sstart[256];
-  // sequence decode cells (RFC 8878 3.1.1.3.2.1.1): bytes 0-1 = byte offset of
-  // the next state's first cell, byte 2 = 32 - state bits, byte 3 = extra bits
-  // (OF: the offset code); LL / ML high word = the code's baseline value |
-  // state bits << 24
-  uint32_t of[256];
+// Shared memory of one K1 (zstd_block_decode) CTA: the literal warps' Huffman
+// tables and the sequence warp's FSE tables, bitstream ring and batch
+// positions; eight CTAs fit on an SM.
+constexpr int kSeqRing = 256;  // ring entries (16 B each)
+struct K1Walk {
+  // FSE cells (RFC 8878 3.1.1.3.2.1.1), one per state.  LL / ML: x = extra
+  // bits | state bits << 6 | baseline << 11, y = byte offset of the next
+  // state's first cell.  OF: offset code | state bits << 6 | byte offset of
+  // the next state's first cell << 16.  The low 11 bits of three cells add
+  // without carries between the fields: extra bits <= 63, state bits <= 26.
   uint2 ll2[512], ml2[512];
-  uint4 sring[128];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 127
-  uint4 skeep[32];   // per sequence of the current batch: bit position, LL, ML, OF cell offsets
+  uint32_t of[256];
+  uint4 sring[kSeqRing];  // sequence bitstream: entry i = words i..i+3, ring indexed by i & 255
+  uint4 skeep[32];        // per sequence of the current batch: bit position, LL, ML, OF cell offsets
   uint16_t next[3][64];
   uint16_t fse_start[64];
   int al[3];
+};
+struct K1Lit {
+  uint32_t huf3[2048];  // up to 3 symbols per lookup: s0|s1<<8|s2<<16|bits<<24|count<<28
+  uint16_t huf[2048];
+  uint16_t sstart[256];
+};
+struct K1Shared {
+  K1Lit l;
+  K1Walk w;
   uint32_t st;
-  uint32_t out_size;
-  uint32_t rep_kind[3], rep_val[3];
 };
 
-constexpr int kLitWarps = 4;                 // one warp per Huffman stream
-constexpr int32_t kLitMargin = 128;          // bits decoded to synchronise a span's entry
+constexpr int kLitWarps = 4;                      // one warp per Huffman stream
+constexpr int32_t kLitMargin = 128;               // bits decoded to synchronise a span's entry
 constexpr int kK1Threads = 32 * (kLitWarps + 1);  // + the sequence warp
 
 // Named barrier over the literal warps only (the sequence warp runs on).
@@ -422,7 +431,7 @@ struct ByteSink {
 // first true boundary at or below it whatever the grouping; in counted mode
 // they run while >= 3 symbols remain, like the serial decoder.  Returns the
 // symbols decoded.
-__device__ __forceinline__ uint32_t huf_run(const K1Shared& sh, DownWin& W, int32_t stop, uint32_t maxbits,
+__device__ __forceinline__ uint32_t huf_run(const K1Lit& sh, DownWin& W, int32_t stop, uint32_t maxbits,
                                             uint8_t* out, int32_t want) {
   const uint32_t shift = 32u - maxbits;
   uint32_t n = 0;
@@ -500,7 +509,7 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     for (int s = 0; s < nsym; s++) {
       const int w = H.w[s];
       if (!w) continue;
-      sh.sstart[s] = uint16_t(start[w]);
+      sh.l.sstart[s] = uint16_t(start[w]);
       start[w] += 1u << (w - 1);
     }
   }
@@ -509,27 +518,27 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     const int w = H.w[s];
     if (!w) continue;
     const uint16_t e = uint16_t(s | ((maxbits + 1 - w) << 8));
-    const uint32_t st = sh.sstart[s], len = 1u << (w - 1);
-    for (uint32_t i = 0; i < len; i++) sh.huf[st + i] = e;
+    const uint32_t st = sh.l.sstart[s], len = 1u << (w - 1);
+    for (uint32_t i = 0; i < len; i++) sh.l.huf[st + i] = e;
   }
   lit_sync();
   // multi-symbol entries: greedily chain codes while they fit in maxbits
   const uint32_t tsize = 1u << maxbits, mask = tsize - 1;
   for (uint32_t i = tid; i < tsize; i += 32 * kLitWarps) {
-    uint32_t e0 = sh.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
-    const uint32_t e1 = sh.huf[(i << l0) & mask], l1 = e1 >> 8;
+    uint32_t e0 = sh.l.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
+    const uint32_t e1 = sh.l.huf[(i << l0) & mask], l1 = e1 >> 8;
     if (bits + l1 <= uint32_t(maxbits)) {
       syms |= (e1 & 0xFFu) << 8;
       bits += l1;
       cnt = 2;
-      const uint32_t e2 = sh.huf[(i << bits) & mask], l2 = e2 >> 8;
+      const uint32_t e2 = sh.l.huf[(i << bits) & mask], l2 = e2 >> 8;
       if (bits + l2 <= uint32_t(maxbits)) {
         syms |= (e2 & 0xFFu) << 16;
         bits += l2;
         cnt = 3;
       }
     }
-    sh.huf3[i] = syms | (bits << 24) | (cnt << 28);
+    sh.l.huf3[i] = syms | (bits << 24) | (cnt << 28);
   }
   lit_sync();
   const int streams = int(b.lit_streams);
@@ -559,7 +568,7 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       // lane's exit and the first counting pass is already exact.
       DownWin W;
       W.init(sp, min(B, start + kLitMargin));
-      huf_run(sh, W, start, uint32_t(maxbits), nullptr, -1);
+      huf_run(sh.l, W, start, uint32_t(maxbits), nullptr, -1);
       start = W.P;
     }
     uint32_t n = 0;
@@ -569,7 +578,7 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       if (active && !last) {
         DownWin W;
         W.init(sp, start);
-        n = huf_run(sh, W, stop, uint32_t(maxbits), nullptr, -1);
+        n = huf_run(sh.l, W, stop, uint32_t(maxbits), nullptr, -1);
         exitp = W.P;
       }
       int32_t next = __shfl_up_sync(0xFFFFFFFFu, exitp, 1);
@@ -590,9 +599,9 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       W.init(sp, start);
       if (!last) {
         lane_ok = excl + n <= count;  // a damaged stream may decode more symbols than it holds
-        if (lane_ok) huf_run(sh, W, stop, uint32_t(maxbits), out + excl, -1);
+        if (lane_ok) huf_run(sh.l, W, stop, uint32_t(maxbits), out + excl, -1);
       } else if (excl <= count) {
-        const uint32_t got = huf_run(sh, W, 0, uint32_t(maxbits), out + excl, int32_t(count - excl));
+        const uint32_t got = huf_run(sh.l, W, 0, uint32_t(maxbits), out + excl, int32_t(count - excl));
         lane_ok = (got == count - excl) && W.P == 0;
       } else {
         lane_ok = false;
@@ -836,40 +845,35 @@ __device__ __forceinline__ RepSlots rep_compose(const RepSlots& s, const RepSlot
   return o;
 }
 
-// Sequences section (RFC 8878 3.1.1.3.2.2) by the sequence warp.  All 32
+// Sequences section (RFC 8878 3.1.1.3.2.2) by a K1 walker warp.  All 32
 // lanes run the FSE walk in lockstep (same values; shared-memory reads are
 // broadcasts).  Each sequence reads its fields from fixed positions below the
 // current bit position P -- offset extra bits, match-length extra, literal-
-// length extra, then the LL, ML and OF state bits -- so the six positions
-// come from the three table cells and every field from three independent
-// 32-bit reads of a shared-memory ring of the bitstream that the warp refills
-// with coalesced loads.  It stores each sequence's literal length, match
-// length and offset value; zstd_seq_scan resolves repeat offsets and output
-// positions in parallel afterwards.
-__device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh) {
+// length extra, then the LL, ML and OF state bits.  The walk carries only the
+// state chain and records each sequence's position and cells; every 32
+// sequences lane j extracts the fields of the batch's sequence j and stores
+// its literal length, match length and offset value.  zstd_seq_scan resolves
+// repeat offsets and output positions in parallel afterwards.  Returns the
+// section's status bits.
+__device__ uint32_t decode_sequences(const uint8_t* src, const View& v, const ZBlock& b, K1Walk& sh) {
   const int lane = threadIdx.x & 31;
-  // LL / ML tables are built in the x words of their cell arrays
+  // tables are built in the x words of their cell arrays
   fse_build_warp<2>(v.fse[b.fse[0]], reinterpret_cast<uint32_t*>(sh.ll2), sh.next[0], sh.fse_start, &sh.al[0]);
   fse_build_warp<1>(v.fse[b.fse[1]], sh.of, sh.next[1], sh.fse_start, &sh.al[1]);
   fse_build_warp<2>(v.fse[b.fse[2]], reinterpret_cast<uint32_t*>(sh.ml2), sh.next[2], sh.fse_start, &sh.al[2]);
   {
-    // cells hold the byte offset of the next state's first cell (state base x
-    // cell size) so the next address is one shift-add of the state bits, and
-    // 32 - state bits as the right shift that extracts them
     const uint32_t nll = 1u << sh.al[0], nof = 1u << sh.al[1], nml = 1u << sh.al[2];
     for (uint32_t u = lane; u < nll; u += 32) {
       const uint32_t t = sh.ll2[u].x, c = min(t & 0xFFu, 35u), nb = (t >> 8) & 0xFFu;
-      sh.ll2[u] = make_uint2(((t >> 16) << 3) | ((32u - nb) << 16) | (uint32_t(c_ll_bits[c]) << 24),
-                             c_ll_base[c] | (nb << 24));
+      sh.ll2[u] = make_uint2(uint32_t(c_ll_bits[c]) | (nb << 6) | (c_ll_base[c] << 11), (t >> 16) << 3);
     }
     for (uint32_t u = lane; u < nml; u += 32) {
       const uint32_t t = sh.ml2[u].x, c = min(t & 0xFFu, 52u), nb = (t >> 8) & 0xFFu;
-      sh.ml2[u] = make_uint2(((t >> 16) << 3) | ((32u - nb) << 16) | (uint32_t(c_ml_bits[c]) << 24),
-                             c_ml_base[c] | (nb << 24));
+      sh.ml2[u] = make_uint2(uint32_t(c_ml_bits[c]) | (nb << 6) | (c_ml_base[c] << 11), (t >> 16) << 3);
     }
     for (uint32_t u = lane; u < nof; u += 32) {
       const uint32_t t = sh.of[u], nb = (t >> 8) & 0xFFu;
-      sh.of[u] = ((t >> 16) << 2) | ((32u - nb) << 16) | (min(t & 0xFFu, 31u) << 24);
+      sh.of[u] = min(t & 0xFFu, 31u) | (nb << 6) | (((t >> 16) << 2) << 16);
     }
   }
   __syncwarp();
@@ -878,169 +882,167 @@ __device__ void decode_sequences(const uint8_t* src, const View& v, const ZBlock
   const uint8_t* p = src + b.seq_src;
   const uint32_t len = b.seq_len;
   const uint32_t lastb = len ? __ldg(p + len - 1) : 0u;
-  if (!lastb) {
-    st = VOOM_ZSTD_ST_SEQUENCES;
-  } else {
-    // Aligned words of the stream: word k holds aligned bits [32k, 32k+32);
-    // stream bit q is aligned bit q + boff.  Ring entry i holds words i..i+3
-    // (128 bits from word i), so any 64-bit window is one 16-byte read.
-    const uintptr_t pa = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* wbase = reinterpret_cast<const uint32_t*>(pa & ~uintptr_t(3));
-    const int32_t boff = int32_t(pa & 3u) * 8;
-    auto gword = [&](int32_t k) -> uint32_t { return k >= 0 ? __ldg(wbase + k) : 0u; };
-    // entries [e0, e0 + 32) from words e0 .. e0 + 34 (the top three words of
-    // the batch come from `above`, the words just over it)
-    auto fill32 = [&](int32_t e0, uint32_t w_l, uint3 above) {
-      const uint32_t n1 = __shfl_down_sync(0xFFFFFFFFu, w_l, 1), n2 = __shfl_down_sync(0xFFFFFFFFu, w_l, 2),
-                     n3 = __shfl_down_sync(0xFFFFFFFFu, w_l, 3);
-      const uint32_t w1 = lane < 31 ? n1 : above.x;
-      const uint32_t w2 = lane < 30 ? n2 : (lane == 30 ? above.x : above.y);
-      const uint32_t w3 = lane < 29 ? n3 : (lane == 29 ? above.x : (lane == 30 ? above.y : above.z));
-      sh.sring[(e0 + lane) & 127] = make_uint4(w_l, w1, w2, w3);
-    };
-    const int32_t Pa0 = int32_t(8 * (len - 1) + (31 - __clz(lastb))) + boff;  // aligned position
-    int32_t Pa = Pa0;
-    // ring covers entries [lo_w, lo_w + 128); reads touch entries at or below (Pa-1)>>5
-    int32_t lo_w = ((Pa0 - 1) >> 5) + 1 - 128;
-    {
-      const int32_t topw = lo_w + 128;
-      uint3 above = make_uint3(gword(topw), gword(topw + 1), gword(topw + 2));
-      for (int j = 3; j >= 0; j--) {
-        const int32_t e0 = lo_w + 32 * j;
-        const uint32_t w_l = gword(e0 + lane);
-        fill32(e0, w_l, above);
-        above = make_uint3(__shfl_sync(0xFFFFFFFFu, w_l, 0), __shfl_sync(0xFFFFFFFFu, w_l, 1),
-                           __shfl_sync(0xFFFFFFFFu, w_l, 2));
-      }
+  if (!lastb) return VOOM_ZSTD_ST_SEQUENCES;
+  // Aligned words of the stream: word k holds aligned bits [32k, 32k+32);
+  // stream bit q is aligned bit q + boff.  Ring entry i holds words i..i+3
+  // (128 bits from word i), so any 96-bit window is one 16-byte read.
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* wbase = reinterpret_cast<const uint32_t*>(pa & ~uintptr_t(3));
+  const int32_t boff = int32_t(pa & 3u) * 8;
+  auto gword = [&](int32_t k) -> uint32_t { return k >= 0 ? __ldg(wbase + k) : 0u; };
+  // entries [e0, e0 + 32) from words e0 .. e0 + 34 (the top three words of
+  // the batch come from `above`, the words just over it)
+  auto fill32 = [&](int32_t e0, uint32_t w_l, uint3 above) {
+    const uint32_t n1 = __shfl_down_sync(0xFFFFFFFFu, w_l, 1), n2 = __shfl_down_sync(0xFFFFFFFFu, w_l, 2),
+                   n3 = __shfl_down_sync(0xFFFFFFFFu, w_l, 3);
+    const uint32_t w1 = lane < 31 ? n1 : above.x;
+    const uint32_t w2 = lane < 30 ? n2 : (lane == 30 ? above.x : above.y);
+    const uint32_t w3 = lane < 29 ? n3 : (lane == 29 ? above.x : (lane == 30 ? above.y : above.z));
+    sh.sring[(e0 + lane) & (kSeqRing - 1)] = make_uint4(w_l, w1, w2, w3);
+  };
+  const int32_t Pa0 = int32_t(8 * (len - 1) + (31 - __clz(lastb))) + boff;  // aligned position
+  int32_t Pa = Pa0;
+  // the ring covers entries [lo_w, lo_w + kSeqRing); reads touch entries at or below (Pa - 1) >> 5
+  int32_t lo_w = ((Pa0 - 1) >> 5) + 1 - kSeqRing;
+  {
+    const int32_t topw = lo_w + kSeqRing;
+    uint3 above = make_uint3(gword(topw), gword(topw + 1), gword(topw + 2));
+    for (int j = kSeqRing / 32 - 1; j >= 0; j--) {
+      const int32_t e0 = lo_w + 32 * j;
+      const uint32_t w_l = gword(e0 + lane);
+      fill32(e0, w_l, above);
+      above = make_uint3(__shfl_sync(0xFFFFFFFFu, w_l, 0), __shfl_sync(0xFFFFFFFFu, w_l, 1),
+                         __shfl_sync(0xFFFFFFFFu, w_l, 2));
     }
-    uint32_t pre = gword(lo_w - 32 + lane);  // next batch, loaded one refill ahead
-    __syncwarp();
-    // stream bits [q, q + 32) at aligned position a
-    auto at = [&](int32_t a) -> uint32_t {
-      // entry (a >> 5) & 127 at byte offset ((a >> 5) & 127) * 16
-      const uint4 e = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(sh.sring) +
-                                                      ((uint32_t(a) >> 1) & 0x7F0u));
-      return __funnelshift_r(e.x, e.y, uint32_t(a));  // shifts by a & 31
-    };
-    const uint32_t a0 = sh.al[0], a1 = sh.al[1], a2 = sh.al[2];
-    const char* cll = reinterpret_cast<const char*>(sh.ll2);
-    const char* cml = reinterpret_cast<const char*>(sh.ml2);
-    const char* cof = reinterpret_cast<const char*>(sh.of);
-    // cell byte offsets of the current LL, ML and OF states
-    uint32_t oll = 0, oof = 0, oml = 0;
-    if (Pa - boff < int32_t(a0 + a1 + a2)) {
-      st = VOOM_ZSTD_ST_SEQUENCES;
-    } else {
-      const uint32_t init = at(Pa - int32_t(a0 + a1 + a2));
-      oml = bfe32(init, 0, a2) << 3;
-      oof = bfe32(init, a2, a1) << 2;
-      oll = bfe32(init, a1 + a2, a0) << 3;
-      Pa -= int32_t(a0 + a1 + a2);
-    }
-    const uint32_t nseq = b.nseq;
-    // The walk records each sequence's bit position and cell offsets in
-    // skeep; after every 32 sequences lane j extracts the fields of the
-    // batch's sequence j and stores its record, so the walk itself carries
-    // only the state chain.  The 32 positions of a batch stay inside the ring:
-    // a sequence spans at most 89 bits and the ring is refilled 32 entries at a
-    // time.
-    auto flush = [&](uint32_t first, uint32_t count) {
-      __syncwarp();
-      if (uint32_t(lane) < count) {
-        const uint4 k = sh.skeep[lane];
-        const int32_t myPa = int32_t(k.x);
-        const uint2 eLL = *reinterpret_cast<const uint2*>(cll + k.y);
-        const uint2 eML = *reinterpret_cast<const uint2*>(cml + k.z);
-        const uint32_t eOF = *reinterpret_cast<const uint32_t*>(cof + k.w);
-        const uint32_t ofc = __byte_perm(eOF, 0, 0x4443), mlb = __byte_perm(eML.x, 0, 0x4443),
-                       llb = __byte_perm(eLL.x, 0, 0x4443);
-        // offset extra (<= 31 bits) at the top of the word below the
-        // position, ML then LL extras (<= 32 bits together) under it; a field
-        // of n bits is the top n bits of its window (n = 0: the clamped
-        // funnel shift by 32 gives 0)
-        const uint32_t w1 = at(myPa - 32), w2 = at(myPa - int32_t(ofc) - 32);
-        const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
-        const uint32_t ml = (eML.y & 0xFFFFFFu) + __funnelshift_rc(w2, 0u, 32u - mlb);
-        const uint32_t ll = (eLL.y & 0xFFFFFFu) + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
-        ZSeq* r = out + first + lane;  // raw record; zstd_seq_scan fills offsets and positions
-        *reinterpret_cast<uint2*>(&r->ll) = make_uint2(ll, ml);
-        r->oval = ofv;
-      }
-      __syncwarp();
-    };
-    if (!st) {
-      // refill when Pa - 96 drops below the ring's lowest word
-      int32_t refill_at = 32 * lo_w + 96;
-      auto refill = [&]() {
-        if (Pa < refill_at) {
-          const uint4 e = sh.sring[lo_w & 127];
-          fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
-          lo_w -= 32;
-          refill_at -= 32 * 32;
-          pre = gword(lo_w - 32 + lane);
-          __syncwarp();
-        }
-      };
-      // One sequence that reads state bits (every sequence but the last).
-      // The 96 stream bits under the position come from one ring entry read
-      // beside the three cells (its address depends on the position only),
-      // so the chain from one state to the next holds a single shared-memory
-      // read: cells -> extra-bit count -> the 32 bits under the extras -> the
-      // three state fields -> the next cells' offsets.
-      auto step = [&](uint4* keep) {
-        refill();
-        const uint2 eLL = *reinterpret_cast<const uint2*>(cll + oll);
-        const uint2 eML = *reinterpret_cast<const uint2*>(cml + oml);
-        const uint32_t eOF = *reinterpret_cast<const uint32_t*>(cof + oof);
-        const uint32_t p96 = uint32_t(Pa - 96);  // >= 32 * lo_w after refill()
-        const uint4 e = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(sh.sring) +
-                                                        ((p96 >> 1) & 0x7F0u));
-        *keep = make_uint4(uint32_t(Pa), oll, oml, oof);  // same value from every lane
-        // stream bits [Pa - 96, Pa) as lo | mid | hi (funnel shifts by p96 & 31)
-        const uint32_t lo = __funnelshift_r(e.x, e.y, p96), mid = __funnelshift_r(e.y, e.z, p96),
-                       hi = __funnelshift_r(e.z, e.w, p96);
-        const uint32_t ox = __byte_perm(eOF, 0, 0x4443) + __byte_perm(eML.x, 0, 0x4443) +
-                            __byte_perm(eLL.x, 0, 0x4443);  // extra bits, <= 63
-        const uint32_t nLL = eLL.y >> 24, nML = eML.y >> 24;
-        const uint32_t nLM = nLL + nML;
-        // the 32 bits under the extras (the LL, ML, OF state bits at the top)
-        const uint32_t w = ox < 32u ? __funnelshift_l(mid, hi, ox) : __funnelshift_l(lo, mid, ox);
-        const uint32_t sLL = __byte_perm(eLL.x, 0, 0x4442), sML = __byte_perm(eML.x, 0, 0x4442),
-                       sOF = __byte_perm(eOF, 0, 0x4442);
-        oll = (eLL.x & 0xFFFFu) + (__funnelshift_rc(w, 0u, sLL) << 3);
-        oml = (eML.x & 0xFFFFu) + (__funnelshift_rc(w << nLL, 0u, sML) << 3);
-        oof = (eOF & 0xFFFFu) + (__funnelshift_rc(w << nLM, 0u, sOF) << 2);
-        // A stream that runs out reads zero words below its start (never
-        // memory outside it) and ends with Pa below boff: checked once below.
-        Pa -= int32_t(ox + nLM + 32u - sOF);
-      };
-      for (uint32_t first = 0; first + 1 < nseq; first += 32) {
-        const uint32_t cnt = min(32u, nseq - 1 - first);
-        if (cnt == 32) {
-          for (uint32_t g = 0; g < 32; g += 8) {
-#pragma unroll
-            for (uint32_t jj = 0; jj < 8; jj++) step(sh.skeep + g + jj);
-          }
-        } else {
-          for (uint32_t jj = 0; jj < cnt; jj++) step(sh.skeep + jj);
-        }
-        flush(first, cnt);
-      }
-      if (nseq) {  // the last sequence: extra bits only
-        refill();
-        sh.skeep[0] = make_uint4(uint32_t(Pa), oll, oml, oof);
-        const uint32_t ofc = __byte_perm(*reinterpret_cast<const uint32_t*>(cof + oof), 0, 0x4443),
-                       mlb = __byte_perm(reinterpret_cast<const uint2*>(cml + oml)->x, 0, 0x4443),
-                       llb = __byte_perm(reinterpret_cast<const uint2*>(cll + oll)->x, 0, 0x4443);
-        Pa -= int32_t(ofc + mlb + llb);
-        flush(nseq - 1, 1);
-      }
-    }
-    if (!st && Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;  // overrun (Pa < boff) or bits left over
   }
-  if (lane == 0 && st) atomicOr(&sh.st, st);
+  uint32_t pre = gword(lo_w - 32 + lane);  // next batch, loaded one refill ahead
+  __syncwarp();
+  const char* ring = reinterpret_cast<const char*>(sh.sring);
+  // stream bits [a, a + 32) at aligned position a (entry (a >> 5) & 255 at byte offset 16 x that)
+  auto at = [&](int32_t a) -> uint32_t {
+    const uint4 e = *reinterpret_cast<const uint4*>(ring + ((uint32_t(a) >> 1) & 0xFF0u));
+    return __funnelshift_r(e.x, e.y, uint32_t(a));  // shifts by a & 31
+  };
+  const uint32_t a0 = sh.al[0], a1 = sh.al[1], a2 = sh.al[2];
+  const char* cll = reinterpret_cast<const char*>(sh.ll2);
+  const char* cml = reinterpret_cast<const char*>(sh.ml2);
+  const char* cof = reinterpret_cast<const char*>(sh.of);
+  if (Pa - boff < int32_t(a0 + a1 + a2)) return VOOM_ZSTD_ST_SEQUENCES;
+  // cell byte offsets of the current LL, ML and OF states
+  uint32_t oll, oml, oof;
+  {
+    const uint32_t init = at(Pa - int32_t(a0 + a1 + a2));
+    oml = bfe32(init, 0, a2) << 3;
+    oof = bfe32(init, a2, a1) << 2;
+    oll = bfe32(init, a1 + a2, a0) << 3;
+    Pa -= int32_t(a0 + a1 + a2);
+  }
+  const uint32_t nseq = b.nseq;
+  // after every batch of up to 32 sequences: lane j's record from skeep[j].
+  // The batch's positions stay inside the ring (a sequence spans at most 89
+  // bits; refills move the ring down 32 entries at a time).
+  auto flush = [&](uint32_t first, uint32_t count) {
+    __syncwarp();
+    if (uint32_t(lane) < count) {
+      const uint4 k = sh.skeep[lane];
+      const int32_t myPa = int32_t(k.x);
+      const uint32_t xL = reinterpret_cast<const uint2*>(cll + k.y)->x;
+      const uint32_t xM = reinterpret_cast<const uint2*>(cml + k.z)->x;
+      const uint32_t xO = *reinterpret_cast<const uint32_t*>(cof + k.w);
+      const uint32_t ofc = xO & 63u, mlb = xM & 63u, llb = xL & 63u;
+      // offset extra (<= 31 bits) at the top of the word below the position,
+      // ML then LL extras (<= 32 bits together) under it; a field of n bits is
+      // the top n bits of its window (n = 0: the clamped funnel shift by 32
+      // gives 0)
+      const uint32_t w1 = at(myPa - 32), w2 = at(myPa - int32_t(ofc) - 32);
+      const uint32_t ofv = (1u << ofc) + __funnelshift_rc(w1, 0u, 32u - ofc);
+      const uint32_t ml = (xM >> 11) + __funnelshift_rc(w2, 0u, 32u - mlb);
+      const uint32_t ll = (xL >> 11) + __funnelshift_rc(w2 << mlb, 0u, 32u - llb);
+      ZSeq* r = out + first + lane;  // raw record; zstd_seq_scan fills offsets and positions
+      *reinterpret_cast<uint2*>(&r->ll) = make_uint2(ll, ml);
+      r->oval = ofv;
+    }
+    __syncwarp();
+  };
+  // Checked before every group of up to 8 sequences: refill while Pa - 96 -
+  // 7 x 89 (the lowest window read of the group) would fall under the ring;
+  // one refill of 32 entries (1024 bits) covers a group (<= 712 bits).
+  constexpr int32_t kSlack = 96 + 7 * 89;
+  int32_t refill_at = 32 * lo_w + kSlack;
+  auto refill = [&]() {
+    if (Pa < refill_at) {
+      const uint4 e = sh.sring[lo_w & (kSeqRing - 1)];
+      fill32(lo_w - 32, pre, make_uint3(e.x, e.y, e.z));
+      lo_w -= 32;
+      refill_at -= 32 * 32;
+      pre = gword(lo_w - 32 + lane);
+      __syncwarp();
+    }
+  };
+  // One sequence that reads state bits (every sequence but the last).  The
+  // 96 stream bits under the position come from one ring entry read beside
+  // the three cells (its address depends on the position only), so the chain
+  // from one state to the next holds a single shared-memory read: cells ->
+  // the extra-bit count (one add of the three x words) -> the 32 bits under
+  // the extras -> the three state fields -> the next cells' offsets.
+  auto step = [&](uint4* keep) {
+    const uint2 cL = *reinterpret_cast<const uint2*>(cll + oll);
+    const uint2 cM = *reinterpret_cast<const uint2*>(cml + oml);
+    const uint32_t cO = *reinterpret_cast<const uint32_t*>(cof + oof);
+    const uint32_t p96 = uint32_t(Pa - 96);  // >= 32 * lo_w (refill invariant)
+    const uint4 e = *reinterpret_cast<const uint4*>(ring + ((p96 >> 1) & 0xFF0u));
+    *keep = make_uint4(uint32_t(Pa), oll, oml, oof);  // same value from every lane
+    // stream bits [Pa - 96, Pa) as lo | mid | hi (funnel shifts by p96 & 31)
+    const uint32_t lo = __funnelshift_r(e.x, e.y, p96), mid = __funnelshift_r(e.y, e.z, p96),
+                   hi = __funnelshift_r(e.z, e.w, p96);
+    // bits 0-5: the extra bits (<= 63), bits 6-10: the state bits (<= 26)
+    const uint32_t S = cL.x + cM.x + cO;
+    // the 32 bits under the extras (the LL, ML, OF state bits at the top);
+    // funnel shifts take S modulo 32
+    const uint32_t w = (S & 32u) ? __funnelshift_l(lo, mid, S) : __funnelshift_l(mid, hi, S);
+    // state-bit counts in the low 5 bits (the baselines above are shifted out
+    // modulo 32): top n bits of a word = high word of (0:word) << n
+    const uint32_t nL = cL.x >> 6, nM = cM.x >> 6, nO = cO >> 6;
+    const uint32_t bL = __funnelshift_l(w, 0u, nL);
+    const uint32_t bM = __funnelshift_l(__funnelshift_l(0u, w, nL), 0u, nM);
+    const uint32_t bO = __funnelshift_l(__funnelshift_l(0u, w, nL + nM), 0u, nO);
+    oll = cL.y + (bL << 3);
+    oml = cM.y + (bM << 3);
+    oof = (cO >> 16) + (bO << 2);
+    // A stream that runs out reads zero words below its start (never memory
+    // outside it) and ends with Pa below boff: checked once below.
+    Pa -= int32_t((S & 63u) + ((S >> 6) & 31u));
+  };
+  for (uint32_t first = 0; first + 1 < nseq; first += 32) {
+    const uint32_t cnt = min(32u, nseq - 1 - first);
+    if (cnt == 32) {
+      for (uint32_t g = 0; g < 32; g += 8) {
+        refill();
+#pragma unroll
+        for (uint32_t jj = 0; jj < 8; jj++) step(sh.skeep + g + jj);
+      }
+    } else {
+      for (uint32_t jj = 0; jj < cnt; jj++) {
+        refill();
+        step(sh.skeep + jj);
+      }
+    }
+    flush(first, cnt);
+  }
+  if (nseq) {  // the last sequence: extra bits only
+    refill();
+    sh.skeep[0] = make_uint4(uint32_t(Pa), oll, oml, oof);
+    const uint32_t S = reinterpret_cast<const uint2*>(cll + oll)->x + reinterpret_cast<const uint2*>(cml + oml)->x +
+                       *reinterpret_cast<const uint32_t*>(cof + oof);
+    Pa -= int32_t(S & 63u);
+    flush(nseq - 1, 1);
+  }
+  if (Pa != boff) st = VOOM_ZSTD_ST_SEQUENCES;  // overrun (Pa < boff) or bits left over
+  return st;
 }
 
+// K1: per block of the segment's block list, the literal warps decode the
+// literals section while the sequence warp walks the sequences section.
 __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t* __restrict__ src,
                                                                 const uint8_t* img, uint8_t* scratch,
                                                                 uint8_t* out, uint32_t bl0) {
@@ -1060,28 +1062,23 @@ __global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t
     }
     return;
   }
-  if (threadIdx.x == 0) {
-    sh.st = 0;
-    sh.out_size = b.lit_regen;
-    for (int k = 0; k < 3; k++) {
-      sh.rep_kind[k] = uint32_t(k);
-      sh.rep_val[k] = 0;
-    }
-  }
+  if (threadIdx.x == 0) sh.st = 0;
   __syncthreads();
   if (threadIdx.x < 32 * kLitWarps) {
     // a direct job's literals are its output bytes
     const ZJob& job = v.jobs[b.job];
     if (!(job.direct && b.lit_type == 2))  // those are zstd_direct_literals' work
       decode_literals(src, v, b, sh, job.direct ? out + job.dst + b.out_off : v.lit + b.lit_off);
+  } else if (b.nseq) {
+    const uint32_t st = decode_sequences(src, v, b, sh.w);
+    if ((threadIdx.x & 31) == 0 && st) atomicOr(&sh.st, st);
   }
-  else if (b.nseq) decode_sequences(src, v, b, sh);
   __syncthreads();
   if (threadIdx.x == 0) {
     // blocks with sequences get out_size and the repeat transform from zstd_seq_scan
     uint32_t st = sh.st;
-    if (!b.nseq && sh.out_size > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
-    rt->out_size = sh.out_size;
+    if (!b.nseq && b.lit_regen > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
+    rt->out_size = b.lit_regen;
     rt->status = st;
     for (int k = 0; k < 3; k++) {
       rt->rep_kind[k] = uint32_t(k);
