@@ -1191,7 +1191,7 @@ DEFAULT_WORKLOAD = "c2_vpack"
 # ------------------------------------------------------------------- main
 ZSTD_KERNELS = {1: "zstd_direct_literals", 2: "zstd_block_decode", 3: "zstd_seq_scan", 4: "zstd_job_scan",
                 5: "zstd_block_execute", 6: "zstd_output", 7: "zstd_resolve (all passes)", 8: "zstd_patch",
-                9: "zstd_checksum"}
+                9: "zstd_checksum", 10: "zstd_block_literals"}
 
 
 def zstd_kernel_times(w, steps: int, flush, stream) -> dict | None:

@@ -295,7 +295,7 @@ enum {
   VOOM_ZSTD_K_DIRECT_LITERALS = 1, VOOM_ZSTD_K_BLOCK_DECODE = 2, VOOM_ZSTD_K_SEQ_SCAN = 3,
   VOOM_ZSTD_K_JOB_SCAN = 4, VOOM_ZSTD_K_BLOCK_EXECUTE = 5, VOOM_ZSTD_K_OUTPUT = 6,
   VOOM_ZSTD_K_RESOLVE = 7, /* all resolve passes of one segment */
-  VOOM_ZSTD_K_PATCH = 8, VOOM_ZSTD_K_CHECKSUM = 9
+  VOOM_ZSTD_K_PATCH = 8, VOOM_ZSTD_K_CHECKSUM = 9, VOOM_ZSTD_K_BLOCK_LITERALS = 10
 };
 int voom_zstd_set_timing(int on);
 int voom_zstd_kernel_times(float* ms, uint32_t* ids, int cap);

@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -114,6 +115,8 @@ __device__ __forceinline__ uint32_t bfe32(uint32_t v, uint32_t pos, uint32_t len
 // ahead (q0, q1), so a lane's loads are in flight long before they are needed
 // and do not depend on L1 keeping the line.  Words below the stream start
 // read as zero, as do the bits of word 0 below the stream's first byte.
+// kSmem: the words are in shared memory (a stream staged there), else global.
+template <bool kSmem>
 struct DownWin {
   const uint32_t* w;
   uint32_t mask0;  // keeps the stream's bits of word 0
@@ -123,12 +126,12 @@ struct DownWin {
   int32_t P;       // unread stream bits
 
   __device__ __forceinline__ uint32_t word(int32_t i) const {
-    const uint32_t v = __ldg(w + max(i, 0));
+    const uint32_t v = kSmem ? w[max(i, 0)] : __ldg(w + max(i, 0));
     return i < 0 ? 0u : (i == 0 ? v & mask0 : v);
   }
   __device__ __forceinline__ void init(const uint8_t* s, int32_t P0) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(s);
-    w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    w = reinterpret_cast<const uint32_t*>(s - (a & 3u));
     const uint32_t boff = uint32_t(a & 3u) * 8u;
     mask0 = ~((1u << boff) - 1u);
     P = P0;
@@ -347,9 +350,8 @@ __device__ void fse_build_warp(const ZFse& f, uint32_t* t, uint16_t* next, uint1
   __syncwarp();
 }
 
-// Shared memory of one K1 (zstd_block_decode) CTA: the literal warps' Huffman
-// tables and the sequence warp's FSE tables, bitstream ring and batch
-// positions; eight CTAs fit on an SM.
+// Shared memory of the literal decode (K0: Huffman tables) and of the
+// sequence walk (K1: FSE tables, bitstream ring, batch positions).
 constexpr int kSeqRing = 256;  // ring entries (16 B each)
 struct K1Walk {
   // FSE cells (RFC 8878 3.1.1.3.2.1.1), one per state.  LL / ML: x = extra
@@ -370,18 +372,15 @@ struct K1Lit {
   uint16_t huf[2048];
   uint16_t sstart[256];
 };
-struct K1Shared {
+// K0 (zstd_block_literals): a block's literals section is copied into
+// shared memory first, then decoded from there by one warp per stream.
+constexpr int kLitWarps = 4;               // one warp per Huffman stream
+constexpr uint32_t kLitStage = 34 * 1024;  // bytes of a literals section decoded from shared memory
+struct K0Shared {
   K1Lit l;
-  K1Walk w;
-  uint32_t st;
+  uint4 stage[kLitStage / 16];
 };
-
-constexpr int kLitWarps = 4;                      // one warp per Huffman stream
-constexpr int32_t kLitMargin = 128;               // bits decoded to synchronise a span's entry
-constexpr int kK1Threads = 32 * (kLitWarps + 1);  // + the sequence warp
-
-// Named barrier over the literal warps only (the sequence warp runs on).
-__device__ __forceinline__ void lit_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kLitWarps)); }
+constexpr int32_t kLitMargin = 128;  // bits decoded to synchronise a span's entry
 
 // Write-combining byte output of one lane: bytes gather in a 64-bit register
 // and leave as aligned 8-byte stores; the partial first and last words go out
@@ -431,7 +430,8 @@ struct ByteSink {
 // first true boundary at or below it whatever the grouping; in counted mode
 // they run while >= 3 symbols remain, like the serial decoder.  Returns the
 // symbols decoded.
-__device__ __forceinline__ uint32_t huf_run(const K1Lit& sh, DownWin& W, int32_t stop, uint32_t maxbits,
+template <class Win>
+__device__ __forceinline__ uint32_t huf_run(const K1Lit& sh, Win& W, int32_t stop, uint32_t maxbits,
                                             uint8_t* out, int32_t want) {
   const uint32_t shift = 32u - maxbits;
   uint32_t n = 0;
@@ -485,7 +485,9 @@ __device__ __forceinline__ uint32_t huf_run(const K1Lit& sh, DownWin& W, int32_t
 // passes usually settle every lane.  A last pass writes each lane's symbols at
 // its prefix offset; the last lane decodes exactly the remaining count and
 // must end on bit 0 (the serial decoder's check).
-__device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock& b, K1Shared& sh, uint8_t* lit) {
+template <bool kSmem>
+__device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock& b, K1Lit& sh, uint8_t* lit,
+                                const uint8_t* words, uint64_t words_off, uint32_t* status) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (b.lit_type == 0) {
     for (uint32_t i = tid; i < b.lit_regen; i += 32 * kLitWarps) lit[i] = __ldg(src + b.src + i);
@@ -509,38 +511,38 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     for (int s = 0; s < nsym; s++) {
       const int w = H.w[s];
       if (!w) continue;
-      sh.l.sstart[s] = uint16_t(start[w]);
+      sh.sstart[s] = uint16_t(start[w]);
       start[w] += 1u << (w - 1);
     }
   }
-  lit_sync();
+  __syncthreads();
   for (int s = tid; s < nsym; s += 32 * kLitWarps) {
     const int w = H.w[s];
     if (!w) continue;
     const uint16_t e = uint16_t(s | ((maxbits + 1 - w) << 8));
-    const uint32_t st = sh.l.sstart[s], len = 1u << (w - 1);
-    for (uint32_t i = 0; i < len; i++) sh.l.huf[st + i] = e;
+    const uint32_t st = sh.sstart[s], len = 1u << (w - 1);
+    for (uint32_t i = 0; i < len; i++) sh.huf[st + i] = e;
   }
-  lit_sync();
+  __syncthreads();
   // multi-symbol entries: greedily chain codes while they fit in maxbits
   const uint32_t tsize = 1u << maxbits, mask = tsize - 1;
   for (uint32_t i = tid; i < tsize; i += 32 * kLitWarps) {
-    uint32_t e0 = sh.l.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
-    const uint32_t e1 = sh.l.huf[(i << l0) & mask], l1 = e1 >> 8;
+    uint32_t e0 = sh.huf[i], l0 = e0 >> 8, bits = l0, cnt = 1, syms = e0 & 0xFFu;
+    const uint32_t e1 = sh.huf[(i << l0) & mask], l1 = e1 >> 8;
     if (bits + l1 <= uint32_t(maxbits)) {
       syms |= (e1 & 0xFFu) << 8;
       bits += l1;
       cnt = 2;
-      const uint32_t e2 = sh.l.huf[(i << bits) & mask], l2 = e2 >> 8;
+      const uint32_t e2 = sh.huf[(i << bits) & mask], l2 = e2 >> 8;
       if (bits + l2 <= uint32_t(maxbits)) {
         syms |= (e2 & 0xFFu) << 16;
         bits += l2;
         cnt = 3;
       }
     }
-    sh.l.huf3[i] = syms | (bits << 24) | (cnt << 28);
+    sh.huf3[i] = syms | (bits << 24) | (cnt << 28);
   }
-  lit_sync();
+  __syncthreads();
   const int streams = int(b.lit_streams);
   if (warp >= streams) return;
   const uint32_t seg = streams == 1 ? b.lit_regen : (b.lit_regen + 3) / 4;
@@ -548,9 +550,9 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
   uint64_t off = b.src;
   for (int k = 0; k < warp; k++) off += b.lit_len[k];
   uint8_t* out = lit + uint32_t(warp) * seg;
-  const uint8_t* sp = src + off;
+  const uint8_t* sp = words + (off - words_off);  // the stream, in shared or global memory
   const uint32_t slen = b.lit_len[warp];
-  const uint32_t lastb = slen ? __ldg(sp + slen - 1) : 0u;
+  const uint32_t lastb = slen ? (kSmem ? uint32_t(sp[slen - 1]) : uint32_t(__ldg(sp + slen - 1))) : 0u;
   bool ok = lastb != 0;
   if (ok) {
     const int32_t B = int32_t(8 * (slen - 1) + (31 - __clz(lastb)));
@@ -566,9 +568,9 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       // top down to the first boundary at or below it.  Huffman codes
       // resynchronise within a few codewords, so this is usually the previous
       // lane's exit and the first counting pass is already exact.
-      DownWin W;
+      DownWin<kSmem> W;
       W.init(sp, min(B, start + kLitMargin));
-      huf_run(sh.l, W, start, uint32_t(maxbits), nullptr, -1);
+      huf_run(sh, W, start, uint32_t(maxbits), nullptr, -1);
       start = W.P;
     }
     uint32_t n = 0;
@@ -576,9 +578,9 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       int32_t exitp = start;
       n = 0;
       if (active && !last) {
-        DownWin W;
+        DownWin<kSmem> W;
         W.init(sp, start);
-        n = huf_run(sh.l, W, stop, uint32_t(maxbits), nullptr, -1);
+        n = huf_run(sh, W, stop, uint32_t(maxbits), nullptr, -1);
         exitp = W.P;
       }
       int32_t next = __shfl_up_sync(0xFFFFFFFFu, exitp, 1);
@@ -595,13 +597,13 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     const uint32_t excl = incl - ((active && !last) ? n : 0u);
     bool lane_ok = true;
     if (active) {
-      DownWin W;
+      DownWin<kSmem> W;
       W.init(sp, start);
       if (!last) {
         lane_ok = excl + n <= count;  // a damaged stream may decode more symbols than it holds
-        if (lane_ok) huf_run(sh.l, W, stop, uint32_t(maxbits), out + excl, -1);
+        if (lane_ok) huf_run(sh, W, stop, uint32_t(maxbits), out + excl, -1);
       } else if (excl <= count) {
-        const uint32_t got = huf_run(sh.l, W, 0, uint32_t(maxbits), out + excl, int32_t(count - excl));
+        const uint32_t got = huf_run(sh, W, 0, uint32_t(maxbits), out + excl, int32_t(count - excl));
         lane_ok = (got == count - excl) && W.P == 0;
       } else {
         lane_ok = false;
@@ -609,7 +611,7 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     }
     ok = __all_sync(0xFFFFFFFFu, lane_ok);
   }
-  if (!ok && lane == 0) atomicOr(&sh.st, VOOM_ZSTD_ST_LITERALS);
+  if (!ok && lane == 0) atomicOr(status + b.job, VOOM_ZSTD_ST_LITERALS);
 }
 
 // Huffman literals of direct jobs' blocks (no sequences: the literals are the
@@ -1041,44 +1043,57 @@ __device__ uint32_t decode_sequences(const uint8_t* src, const View& v, const ZB
   return st;
 }
 
-// K1: per block of the segment's block list, the literal warps decode the
-// literals section while the sequence warp walks the sequences section.
-__global__ void __launch_bounds__(kK1Threads, 8) zstd_block_decode(const uint8_t* __restrict__ src,
-                                                                const uint8_t* img, uint8_t* scratch,
-                                                                uint8_t* out, uint32_t bl0) {
-  __shared__ K1Shared sh;
+// K0: the literals section of every block of the segment's block list (one
+// CTA per block, a warp per stream).  The section is first copied into shared
+// memory with coalesced 16-byte loads: the 32 lanes of a stream's warp each
+// decode their own span, and reading the words from global memory made every
+// lookup wait on a load that missed L1.  Sections larger than the stage are
+// decoded from global memory.  Raw and RLE sections are copied; direct jobs'
+// Huffman literals are zstd_direct_literals' work.
+__global__ void __launch_bounds__(32 * kLitWarps) zstd_block_literals(const uint8_t* __restrict__ src,
+                                                                      const uint8_t* img, uint8_t* scratch,
+                                                                      uint8_t* out, uint32_t* status, uint32_t bl0) {
+  __shared__ K0Shared sh;
+  const View v = make_view(img, scratch);
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
+  const ZBlock b = v.blocks[bi];
+  if (b.type != 2) return;
+  const ZJob& job = v.jobs[b.job];
+  if (job.bad || (job.direct && b.lit_type == 2)) return;
+  // a direct job's literals are its output bytes
+  uint8_t* lit = job.direct ? out + job.dst + b.out_off : v.lit + b.lit_off;
+  uint64_t len = 0;
+  if (b.lit_type == 2)
+    for (uint32_t q = 0; q < b.lit_streams; q++) len += b.lit_len[q];
+  const uint64_t base = b.src & ~uint64_t(15);
+  const uint64_t chunks = (b.src + len - base + 15) / 16;  // the source has 16 readable bytes past its end
+  if (b.lit_type == 2 && chunks <= kLitStage / 16) {
+    const uint4* g = reinterpret_cast<const uint4*>(src + base);
+    for (uint32_t i = threadIdx.x; i < chunks; i += blockDim.x) sh.stage[i] = __ldg(g + i);
+    // (the table build in decode_literals synchronises the CTA before any read)
+    decode_literals<true>(src, v, b, sh.l, lit, reinterpret_cast<const uint8_t*>(sh.stage), base, status);
+  } else {
+    decode_literals<false>(src, v, b, sh.l, lit, src, 0, status);
+  }
+}
+
+// K1: the sequences section of every block of the segment's block list, one
+// warp per block (one-warp CTAs spread over the SMs' schedulers two to a
+// scheduler), and every block's runtime record.
+__global__ void __launch_bounds__(32) zstd_block_decode(const uint8_t* __restrict__ src, const uint8_t* img,
+                                                        uint8_t* scratch, uint32_t bl0) {
+  __shared__ K1Walk sh;
   const View v = make_view(img, scratch);
   const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
   const ZBlock b = v.blocks[bi];
   ZBlockRt* rt = v.rt + bi;
-  if (b.type != 2) {
-    if (threadIdx.x == 0) {
-      rt->out_size = b.size;
-      rt->status = 0;
-      for (int k = 0; k < 3; k++) {
-        rt->rep_kind[k] = uint32_t(k);
-        rt->rep_val[k] = 0;
-      }
-    }
-    return;
-  }
-  if (threadIdx.x == 0) sh.st = 0;
-  __syncthreads();
-  if (threadIdx.x < 32 * kLitWarps) {
-    // a direct job's literals are its output bytes
-    const ZJob& job = v.jobs[b.job];
-    if (!(job.direct && b.lit_type == 2))  // those are zstd_direct_literals' work
-      decode_literals(src, v, b, sh, job.direct ? out + job.dst + b.out_off : v.lit + b.lit_off);
-  } else if (b.nseq) {
-    const uint32_t st = decode_sequences(src, v, b, sh.w);
-    if ((threadIdx.x & 31) == 0 && st) atomicOr(&sh.st, st);
-  }
-  __syncthreads();
+  uint32_t st = 0;
+  if (b.type == 2 && b.nseq) st = decode_sequences(src, v, b, sh);
   if (threadIdx.x == 0) {
-    // blocks with sequences get out_size and the repeat transform from zstd_seq_scan
-    uint32_t st = sh.st;
-    if (!b.nseq && b.lit_regen > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
-    rt->out_size = b.lit_regen;
+    // blocks with sequences get out_size and the repeat transform from
+    // zstd_seq_scan; a damaged literals section flags its job in K0
+    if (b.type == 2 && !b.nseq && b.lit_regen > b.max_out) st |= VOOM_ZSTD_ST_SIZE;
+    rt->out_size = b.type == 2 ? b.lit_regen : b.size;
     rt->status = st;
     for (int k = 0; k < 3; k++) {
       rt->rep_kind[k] = uint32_t(k);
@@ -1907,6 +1922,31 @@ void tmark(cudaStream_t s, uint32_t id) {
   if (g_ntev > 0) g_tid[g_ntev - 1] = id;
   cudaEventRecord(g_tev[g_ntev++], s);
 }
+// The literal decode (K0) runs on a side stream beside the sequence walk
+// (K1): the walks are one warp per block and bound by their serial chains, so
+// K0's CTAs use the SMs' spare issue slots instead of adding their time.  One
+// side stream and a fork / join event pair per device, made on first use; the
+// enqueue sequence holds a lock so that concurrent callers' events do not mix.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool tried = false, ok = false;
+};
+SideStream g_side[64];
+std::mutex g_side_mu;
+
+SideStream* side_stream_locked() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  SideStream& ss = g_side[dev];
+  if (!ss.tried) {
+    ss.tried = true;
+    ss.ok = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess &&
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) == cudaSuccess;
+  }
+  return ss.ok ? &ss : nullptr;
+}
 }  // namespace
 
 VOOM_API int voom_zstd_set_timing(int on) {
@@ -1970,8 +2010,22 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
     // resolve worklist counters (after the tile flags)
     if (cudaMemsetAsync(scr + h.s_ctr + 4ull * h.n_tiles, 0, 32, s) != cudaSuccess) return VOOM_E_CUDA;
     if (g.n_bl) {
-      zstd_block_decode<<<g.n_bl, kK1Threads, 0, s>>>(d_src, img, scr, d_out, g.bl0);
-      tmark(s, VOOM_ZSTD_K_BLOCK_DECODE);
+      {
+        std::lock_guard<std::mutex> lock(g_side_mu);
+        SideStream* ss = side_stream_locked();
+        if (ss) {  // K1 on the caller's stream (dispatched first), K0 beside it
+          if (cudaEventRecord(ss->fork, s) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
+            return VOOM_E_CUDA;
+          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0);
+          zstd_block_literals<<<g.n_bl, 32 * kLitWarps, 0, ss->s>>>(d_src, img, scr, d_out, d_status, g.bl0);
+          if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(s, ss->join, 0) != cudaSuccess)
+            return VOOM_E_CUDA;
+        } else {
+          zstd_block_literals<<<g.n_bl, 32 * kLitWarps, 0, s>>>(d_src, img, scr, d_out, d_status, g.bl0);
+          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0);
+        }
+      }
+      tmark(s, VOOM_ZSTD_K_BLOCK_DECODE);  // literals and sequences together
       zstd_seq_scan<<<g.n_bl, kSeqScanThreads, 0, s>>>(img, scr, g.bl0);
       tmark(s, VOOM_ZSTD_K_SEQ_SCAN);
       zstd_job_scan<<<(g.n_jobs + kJobScanWarps - 1) / kJobScanWarps, 32 * kJobScanWarps, 0, s>>>(
