@@ -32,6 +32,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -115,8 +116,6 @@ __device__ __forceinline__ uint32_t bfe32(uint32_t v, uint32_t pos, uint32_t len
 // ahead (q0, q1), so a lane's loads are in flight long before they are needed
 // and do not depend on L1 keeping the line.  Words below the stream start
 // read as zero, as do the bits of word 0 below the stream's first byte.
-// kSmem: the words are in shared memory (a stream staged there), else global.
-template <bool kSmem>
 struct DownWin {
   const uint32_t* w;
   uint32_t mask0;  // keeps the stream's bits of word 0
@@ -126,7 +125,7 @@ struct DownWin {
   int32_t P;       // unread stream bits
 
   __device__ __forceinline__ uint32_t word(int32_t i) const {
-    const uint32_t v = kSmem ? w[max(i, 0)] : __ldg(w + max(i, 0));
+    const uint32_t v = __ldg(w + max(i, 0));
     return i < 0 ? 0u : (i == 0 ? v & mask0 : v);
   }
   __device__ __forceinline__ void init(const uint8_t* s, int32_t P0) {
@@ -165,6 +164,32 @@ struct DownWin {
       nidx--;
     }
   }
+};
+
+// Window over a backward bitstream staged in shared memory, for one lane: the
+// 32 bits just below position P are read afresh for every lookup (two word
+// loads and a funnel shift), so the lane keeps no refill queue and the warp
+// has no divergent refill branch.  Same interface as DownWin for huf_run.
+// The stage has a zero chunk below and above the staged bytes, so the reads
+// near either end of a stream stay inside it (P >= -43 in every decode loop,
+// and the stream starts at least 128 bits above the stage's first bit).
+struct PosWin {
+  const uint32_t* w;  // stage words
+  int32_t boff;       // stage bit of the stream's first bit
+  int32_t P;          // unread stream bits
+  uint32_t hi;        // stream bits [P - 32, P), bit P - 1 at the top
+
+  __device__ __forceinline__ void init(const uint32_t* stage_words, int32_t first_bit, int32_t P0) {
+    w = stage_words;
+    boff = first_bit;
+    P = P0;
+  }
+  __device__ __forceinline__ void refill() {
+    const int32_t A = boff + P;
+    const int32_t k = A >> 5;
+    hi = __funnelshift_r(w[k - 1], w[k], uint32_t(A));
+  }
+  __device__ __forceinline__ void consume(uint32_t n) { P -= int32_t(n); }
 };
 
 // Asynchronous 16-byte global -> shared copies (cp.async, per thread groups).
@@ -378,7 +403,7 @@ constexpr int kLitWarps = 4;               // one warp per Huffman stream
 constexpr uint32_t kLitStage = 34 * 1024;  // bytes of a literals section decoded from shared memory
 struct K0Shared {
   K1Lit l;
-  uint4 stage[kLitStage / 16];
+  uint4 stage[kLitStage / 16 + 2];  // a zero chunk, the section's chunks, a zero chunk
 };
 constexpr int32_t kLitMargin = 128;  // bits decoded to synchronise a span's entry
 
@@ -485,9 +510,10 @@ __device__ __forceinline__ uint32_t huf_run(const K1Lit& sh, Win& W, int32_t sto
 // passes usually settle every lane.  A last pass writes each lane's symbols at
 // its prefix offset; the last lane decodes exactly the remaining count and
 // must end on bit 0 (the serial decoder's check).
-template <bool kSmem>
+template <bool kStaged>
 __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock& b, K1Lit& sh, uint8_t* lit,
-                                const uint8_t* words, uint64_t words_off, uint32_t* status) {
+                                const uint32_t* stage, uint64_t stage_off, uint32_t* status) {
+  using Win = typename std::conditional<kStaged, PosWin, DownWin>::type;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (b.lit_type == 0) {
     for (uint32_t i = tid; i < b.lit_regen; i += 32 * kLitWarps) lit[i] = __ldg(src + b.src + i);
@@ -550,10 +576,19 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
   uint64_t off = b.src;
   for (int k = 0; k < warp; k++) off += b.lit_len[k];
   uint8_t* out = lit + uint32_t(warp) * seg;
-  const uint8_t* sp = words + (off - words_off);  // the stream, in shared or global memory
+  const uint8_t* sp = src + off;
+  // stage bit of the stream's first bit (staged sections: global byte g is stage byte g - stage_off)
+  const int32_t first_bit = int32_t(8 * (off - stage_off));
   const uint32_t slen = b.lit_len[warp];
-  const uint32_t lastb = slen ? (kSmem ? uint32_t(sp[slen - 1]) : uint32_t(__ldg(sp + slen - 1))) : 0u;
+  const uint32_t lastb =
+      slen ? (kStaged ? (stage[(off - stage_off + slen - 1) >> 2] >> (8 * ((off - stage_off + slen - 1) & 3))) & 0xFFu
+                      : uint32_t(__ldg(sp + slen - 1)))
+           : 0u;
   bool ok = lastb != 0;
+  auto win_init = [&](Win& W, int32_t P0) {
+    if constexpr (kStaged) W.init(stage, first_bit, P0);
+    else W.init(sp, P0);
+  };
   if (ok) {
     const int32_t B = int32_t(8 * (slen - 1) + (31 - __clz(lastb)));
     // spans: one lane for short streams, else 32
@@ -568,8 +603,8 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       // top down to the first boundary at or below it.  Huffman codes
       // resynchronise within a few codewords, so this is usually the previous
       // lane's exit and the first counting pass is already exact.
-      DownWin<kSmem> W;
-      W.init(sp, min(B, start + kLitMargin));
+      Win W;
+      win_init(W, min(B, start + kLitMargin));
       huf_run(sh, W, start, uint32_t(maxbits), nullptr, -1);
       start = W.P;
     }
@@ -578,8 +613,8 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
       int32_t exitp = start;
       n = 0;
       if (active && !last) {
-        DownWin<kSmem> W;
-        W.init(sp, start);
+        Win W;
+        win_init(W, start);
         n = huf_run(sh, W, stop, uint32_t(maxbits), nullptr, -1);
         exitp = W.P;
       }
@@ -597,8 +632,8 @@ __device__ void decode_literals(const uint8_t* src, const View& v, const ZBlock&
     const uint32_t excl = incl - ((active && !last) ? n : 0u);
     bool lane_ok = true;
     if (active) {
-      DownWin<kSmem> W;
-      W.init(sp, start);
+      Win W;
+      win_init(W, start);
       if (!last) {
         lane_ok = excl + n <= count;  // a damaged stream may decode more symbols than it holds
         if (lane_ok) huf_run(sh, W, stop, uint32_t(maxbits), out + excl, -1);
@@ -1069,11 +1104,15 @@ __global__ void __launch_bounds__(32 * kLitWarps) zstd_block_literals(const uint
   const uint64_t chunks = (b.src + len - base + 15) / 16;  // the source has 16 readable bytes past its end
   if (b.lit_type == 2 && chunks <= kLitStage / 16) {
     const uint4* g = reinterpret_cast<const uint4*>(src + base);
-    for (uint32_t i = threadIdx.x; i < chunks; i += blockDim.x) sh.stage[i] = __ldg(g + i);
+    for (uint32_t i = threadIdx.x; i < chunks; i += blockDim.x) sh.stage[1 + i] = __ldg(g + i);
+    if (threadIdx.x == 0) {
+      sh.stage[0] = make_uint4(0u, 0u, 0u, 0u);
+      sh.stage[chunks + 1] = make_uint4(0u, 0u, 0u, 0u);
+    }
     // (the table build in decode_literals synchronises the CTA before any read)
-    decode_literals<true>(src, v, b, sh.l, lit, reinterpret_cast<const uint8_t*>(sh.stage), base, status);
+    decode_literals<true>(src, v, b, sh.l, lit, reinterpret_cast<const uint32_t*>(sh.stage), base - 16, status);
   } else {
-    decode_literals<false>(src, v, b, sh.l, lit, src, 0, status);
+    decode_literals<false>(src, v, b, sh.l, lit, nullptr, 0, status);
   }
 }
 
