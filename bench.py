@@ -599,10 +599,12 @@ class C4MoeEP:
     checkpoint index, top-8 softmax routing whose expert popularity follows
     Zipf(1.1) (router logits biased by c log p over a seeded permutation of
     ranks; top-8 then approximates drawing 8 distinct experts in proportion to
-    the popularity), T tokens per step.  Expert parallel: every rank routes all tokens,
-    runs the fused decode + SwiGLU of its own experts (placed by LPT over the
-    expected decode cost of the T values timed), one NCCL all-reduce sums the
-    route rows, every rank combines.  A step runs `layers` layers (one router
+    the popularity), T tokens per step.  Expert parallel: every rank routes all tokens
+    and runs the fused decode + SwiGLU of the experts it owns (placed by LPT over
+    the expected decode cost of the T values timed; with N > 1 the 8 hottest are
+    held by every rank and each routed one is computed by its least loaded
+    holder); the token-major route rows are reduce-scattered over tokens, each
+    rank combines its tokens, and an all-gather shares the combined rows.  A step runs `layers` layers (one router
     each) over the same expert set, the configuration's single layer; the
     metric is tokens per second through one layer (T x layers / step time)."""
 
@@ -613,6 +615,7 @@ class C4MoeEP:
             "router N(0, 0.02) + a log Zipf(1.1) popularity bias, tokens N(0, 1)")
     E, H, I, K = 160, 6144, 2048, 8
     PAGE = 2 << 20
+    REPLICATED = 8  # hottest experts held by every rank when N > 1
 
     def __init__(self, device, rank: int, world: int = 1, tokens=(1, 8, 64), layers: int = 4):
         import torch
@@ -640,8 +643,13 @@ class C4MoeEP:
             nw = (1.0 + 0.05 * torch.randn(H, generator=gr)).to(torch.bfloat16)
             self.routers.append((wr, nw))
         self.cost = self._expected_cost(tokens)
-        self.placement = moe.place_experts(self.cost, world)
-        self.owned = self.placement[rank]
+        # with N > 1 the REPLICATED hottest experts are held by every rank and
+        # assigned per step to the least loaded holder; the rest are placed LPT
+        self.replicated = [int(e) for e in np.argsort(-self.cost, kind="stable")[:self.REPLICATED]] if world > 1 else []
+        rest = np.array([e for e in range(E) if e not in self.replicated])
+        self.placement = [sorted(int(rest[i]) for i in b) for b in moe.place_experts(self.cost[rest], world)]
+        self.holders = moe.holders_for(self.placement, E, self.replicated)
+        self.owned = sorted(set(self.placement[rank]) | set(self.replicated))
 
         def weight(e, j):
             shape = (I, H) if j < 2 else (H, I)
@@ -656,7 +664,8 @@ class C4MoeEP:
         self.setup_s = time.perf_counter() - t0
         self.expert_bytes = {e: sum(p.frame_bytes for p in self.store.pages[e]) for e in self.owned}
         self.layers = [moe.ExpertParallelMoeLayer(self.store, wr.to(device), nw.to(device), top_k=self.K,
-                                                  router_bias=self.bias) for wr, nw in self.routers]
+                                                  router_bias=self.bias, holders=self.holders, rank=rank,
+                                                  world=world) for wr, nw in self.routers]
 
     def _expected_cost(self, tokens) -> np.ndarray:
         """Expected page decodes per expert and step, averaged over the timed T
@@ -688,10 +697,16 @@ class C4MoeEP:
                 "local_page_bytes_raw": int(raw), "ratio": round(raw / max(1, self.store.compressed_bytes), 4),
                 "popularity": f"Zipf(1.1) over a seeded permutation, router bias {self.bias_scale:.3f} log p "
                               "(top-8 ~ 8 distinct draws in proportion to the popularity)",
-                "placement": "LPT over expected page decodes per step (mean over the timed T)",
-                "experts_per_rank": [len(b) for b in self.placement],
-                "combine": "NCCL all-reduce of the BF16 route rows (one nonzero contributor per row), "
-                           "ordered BF16 combine on every rank",
+                "placement": ("LPT over expected page decodes per step (mean over the timed T)" +
+                              (f"; the {len(self.replicated)} hottest experts held by every rank, each routed one "
+                               "computed by its least loaded holder (rule evaluated on the device)"
+                               if self.replicated else "")),
+                "experts_per_rank": [len(b) + len(self.replicated) for b in self.placement],
+                "replicated_experts": len(self.replicated),
+                "combine": ("route rows in token-major order (zero where another rank computes them), NCCL "
+                            "reduce-scatter over tokens, ordered BF16 combine of each rank's tokens, NCCL "
+                            "all-gather of the combined rows" if self.world > 1 else
+                            "ordered BF16 combine (one GPU)"),
                 "page_build_s": round(self.setup_s, 2),
                 "l2": "flushed between steps (512 MiB write); the page set exceeds L2"}
 
@@ -712,7 +727,8 @@ class C4Step:
         self.y_host = torch.empty_like(self.x_host).pin_memory()
         self.units_per_step = T * c4.L
         self.algo_bytes = None
-        self.launches_per_step = 9 * c4.L  # router logits, top-k, plan, 2x gate/up, act, 2x down, combine
+        # router logits, top-k, plan, owners, 2x gate/up, act, 2x down, token-major rows, combine
+        self.launches_per_step = 11 * c4.L
         self.nccl_ms = 0.0
 
     def _run(self, x, timing: bool = False):
@@ -721,15 +737,21 @@ class C4Step:
         for i, layer in enumerate(self.c4.layers):
             out = self.bufs[i % 2]
             if timing and self.c4.world > 1:
-                a, b = self.torch.cuda.Event(enable_timing=True), self.torch.cuda.Event(enable_timing=True)
-                y = layer.experts(cur)
-                a.record()
                 import torch.distributed as dist
 
-                dist.all_reduce(y, op=dist.ReduceOp.SUM)
-                b.record()
-                layer.combine(cur, y, out)
-                ev.append((a, b))
+                ab = [self.torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                y = layer.experts(cur)
+                _, _, shard, part, full = layer.buffers(self.T)
+                ts = layer.t_pad(self.T) // self.c4.world
+                ab[0].record()
+                dist.reduce_scatter_tensor(shard, y)
+                ab[1].record()
+                layer.combine(cur, shard, part, self.c4.rank * ts, ts)
+                ab[2].record()
+                dist.all_gather_into_tensor(full, part)
+                ab[3].record()
+                out.copy_(full[:self.T])
+                ev += [(ab[0], ab[1]), (ab[2], ab[3])]
             else:
                 layer(cur, out=out)
             cur = out
@@ -750,15 +772,18 @@ class C4Step:
         (read from the route tables) + the activations in and out."""
         torch = self.torch
         torch.cuda.synchronize()
-        owned = set(self.c4.owned)
+        from voom_b200.runtime import moe
+
         n_local, byt, distinct = 0, 0, []
         for layer in self.c4.layers:
-            s, _ = layer.buffers(self.T)
-            words = s[:16 + 4 * 520].view(torch.int32).cpu().numpy()
+            s = layer.buffers(self.T)[0]
+            words = s[:4 * (4 + 2 * 513)].view(torch.int32).cpu().numpy()
             nu = int(words[0])
             ex = [int(e) for e in words[4:4 + nu]]
+            ntok = [int(n) for n in words[4 + 513:4 + 513 + nu]]
             distinct.append(nu)
-            mine = [e for e in ex if e in owned]
+            owner = moe.assign_owners(ex, ntok, self.c4.holders, self.c4.world)  # the device's rule
+            mine = [e for e, o in zip(ex, owner) if o == self.c4.rank]
             n_local += len(mine)
             byt += sum(self.c4.expert_bytes[e] for e in mine)
         self.local_routed = n_local
@@ -1454,7 +1479,8 @@ def moe_record(w, r: dict, world: int, peaks, peaks_kind, cpu: dict | None, extr
            "cpu_baseline": cpu, "clocks": r["clocks"],
            "gpu_launches": getattr(w, "launches_per_step", 1) * 1}
     if r.get("coll_ms") is not None:
-        rec["collective"] = {"op": "NCCL all-reduce of the route rows", "ms_per_step": round(r["coll_ms"], 5),
+        rec["collective"] = {"op": "NCCL reduce-scatter of the token-major route rows + all-gather of the combined "
+                                   "rows (waits for the slowest rank included)", "ms_per_step": round(r["coll_ms"], 5),
                              "share_of_step": round(r["coll_ms"] / ms, 4)}
     rec.update(extra)
     return rec

@@ -485,6 +485,44 @@ int voom_moe_experts_v(const voom_moe_variant* v, const voom_expert_pages* d_pag
                        uint32_t T, uint32_t H, uint32_t I, uint32_t top_k, uint32_t gate_tiles, uint32_t down_tiles,
                        uint16_t* d_y, void* d_scratch, uint64_t scratch_bytes, uint32_t* d_status, void* stream);
 
+/* Expert parallelism over `world` GPUs (one process each) with an exchange
+ * that scales: every rank routes all T tokens (the same routes on every
+ * rank), each routed expert is computed by exactly one rank -- the one that
+ * holds its pages, or, for an expert several ranks hold (replicated hot
+ * experts), the least loaded of them by a rule every rank evaluates alike --
+ * and only the owned experts' work is launched.  d_y_tm (t_pad * rows_per_token
+ * rows of H BF16, rows_per_token = top_k + 1 with a shared expert) receives the
+ * route rows in token-major order (row t * rows_per_token + j = token t's j-th
+ * route in the combine's order, the shared expert last), zero where another
+ * rank computes the row and for padding tokens t >= T.  A reduce-scatter of
+ * d_y_tm over ranks (sum; every row has one nonzero contributor, so the sum
+ * is exact) leaves rank r the rows of tokens [r * t_pad / world, (r + 1) *
+ * t_pad / world); voom_moe_combine_tm combines those, and an all-gather of the
+ * combined rows gives every rank the layer output, bit-identical to
+ * voom_moe_layer_v on one GPU.  d_holders: n_experts words (n_experts + 1 with
+ * a shared expert, its entry last), bit r = rank r holds the expert's pages
+ * (world <= 32); t_pad >= T, a multiple of world.  Status bit 16: a routed
+ * expert no rank holds (its rows stay zero).
+ * Replaces: runtime/layer_runner.py:347-394 across GPUs (the reference has no
+ * multi-device path). */
+typedef struct voom_moe_ep {
+  const uint32_t* d_holders;
+  uint32_t rank, world;
+  uint32_t t_pad;
+} voom_moe_ep;
+int voom_moe_experts_ep(const voom_moe_variant* v, const voom_moe_ep* ep, const voom_expert_pages* d_pages,
+                        uint32_t n_experts, const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps,
+                        const uint16_t* d_x, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k,
+                        uint32_t gate_tiles, uint32_t down_tiles, uint16_t* d_y_tm, void* d_scratch,
+                        uint64_t scratch_bytes, uint32_t* d_status, void* stream);
+/* The combine of voom_moe_layer_v for tokens [t0, t0 + t_count) from their
+ * token-major rows d_y_shard (t_count * rows_per_token rows), with the routes
+ * voom_moe_experts_ep left in d_scratch; d_out_shard receives t_count rows of
+ * H (tokens t >= T: zeros).  d_x holds all T input rows (the residual). */
+int voom_moe_combine_tm(const void* d_scratch, const uint16_t* d_y_shard, const uint16_t* d_x,
+                        uint16_t* d_out_shard, uint32_t t0, uint32_t t_count, uint32_t H, uint32_t residual,
+                        void* stream);
+
 /* voom_moe_layer without any device allocation, for callers that cannot
  * allocate device memory themselves: runtimes that own every byte of the GPU
  * through their own pool, serving loops that must not hit the allocator (and

@@ -1,7 +1,9 @@
-"""Expert-parallel host logic on CPU ranks (gloo, world size 2): placement,
-replicated routing, zero rows for remote experts, sum over ranks, ordered
-combine -- the same composition the GPU layer runs with NCCL -- must equal
-the single-process layer.  The expert math here is the oracle (torch CPU)."""
+"""Expert-parallel host logic on CPU ranks (gloo, world size 2): placement with
+replicated hot experts, owners assigned by the device's rule, replicated
+routing, token-major route rows (zero where another rank computes them),
+reduce-scatter over tokens, the ordered combine of each rank's tokens and the
+all-gather -- the composition the GPU layer runs with NCCL -- must equal the
+single-process layer.  The expert math here is the oracle (torch CPU)."""
 
 from __future__ import annotations
 
@@ -14,7 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from voom_b200.runtime.moe import place_experts, route_rows, zipf_popularity
+from voom_b200.runtime.moe import assign_owners, holders_for, place_experts, route_rows, zipf_popularity
 
 
 def _free_port() -> int:
@@ -32,32 +34,51 @@ def _make(E=12, H=64, I=32, seed=3):
     return ex, wr, x
 
 
-def _ep_forward(rank: int, world: int, ex, wr, x, k: int):
+def _ep_forward(rank: int, world: int, ex, wr, x, k: int, replicated=(0, 5)):
     from oracle import moe as om
 
-    owned = place_experts(np.ones(len(ex)), world)[rank]
+    holders = holders_for(place_experts(np.ones(len(ex)), world), len(ex), replicated)
+    T, H = x.shape
     h = x
     idx, pw = om.route(h, wr, k, True)
     order, ntok, uoff, upair, tok_order = route_rows(idx.numpy())
-    y = torch.zeros((x.shape[0] * k, x.shape[1]), dtype=torch.float32)
+    owner = assign_owners(order, ntok, holders, world)
+    unit_of = {q: u for u in range(len(order)) for q in range(uoff[u], uoff[u + 1])}
+    rows = {}
     for u, e in enumerate(order):
-        if e in owned:
-            rows = list(range(uoff[u], uoff[u + 1]))
-            y[rows] = om.swiglu(h[[upair[q] for q in rows]], *ex[e]).float()
-    dist.all_reduce(y)  # exact: one nonzero contributor per row
+        if owner[u] == rank:
+            qs = list(range(uoff[u], uoff[u + 1]))
+            for q, yq in zip(qs, om.swiglu(h[[upair[q] for q in qs]], *ex[e]).float()):
+                rows[q] = yq
+    tp = -(-T // world) * world
+    ts = tp // world
+    y_tm = torch.zeros((tp * k, H), dtype=torch.float32)  # token-major: row t * k + j
+    for t in range(T):
+        for j, q in enumerate(tok_order[t]):
+            if owner[unit_of[q]] == rank:
+                y_tm[t * k + j] = rows[q]
+    shard = torch.zeros((ts * k, H), dtype=torch.float32)
+    dist.reduce_scatter_tensor(shard, y_tm)  # exact: one nonzero contributor per row
     wrow = torch.zeros(len(upair))
-    for t in range(x.shape[0]):
+    for t in range(T):
         for j in range(k):
-            e = int(idx[t, j])
-            u = order.index(e)
+            u = order.index(int(idx[t, j]))
             q = next(q for q in range(uoff[u], uoff[u + 1]) if upair[q] == t)
             wrow[q] = float(pw[t, j])
-    out = torch.zeros_like(x)
-    for t in range(x.shape[0]):
-        for q in tok_order[t]:
-            contrib = (y[q].to(torch.bfloat16).float() * wrow[q].to(torch.bfloat16).float()).to(torch.bfloat16)
-            out[t] = (out[t].float() + contrib.float()).to(torch.bfloat16)
-    return (x.float() + out.float()).to(torch.bfloat16)
+    part = torch.zeros((ts, H), dtype=torch.bfloat16)
+    for tl in range(ts):
+        t = rank * ts + tl
+        if t >= T:
+            continue
+        o = torch.zeros(H, dtype=torch.bfloat16)
+        for j, q in enumerate(tok_order[t]):
+            yq = shard[tl * k + j].to(torch.bfloat16).float()
+            contrib = (yq * wrow[q].to(torch.bfloat16).float()).to(torch.bfloat16)
+            o = (o.float() + contrib.float()).to(torch.bfloat16)
+        part[tl] = (x[t].float() + o.float()).to(torch.bfloat16)
+    full = torch.zeros((tp, H), dtype=torch.bfloat16)
+    dist.all_gather_into_tensor(full, part)
+    return full[:T]
 
 
 def _worker(rank, world, port, q):
@@ -105,3 +126,13 @@ def test_route_rows_matches_reference_order():
     assert order == [3, 1, 2, 0] and ntok == [2, 2, 1, 1]
     assert list(uoff) == [0, 2, 4, 5, 6] and upair == [0, 2, 0, 1, 1, 2]
     assert tok_order == [[0, 2], [3, 4], [1, 5]]
+
+
+def test_owner_rule_balances_replicated_experts():
+    # units 0, 2 single-holder on rank 0; units 1, 3, 4 replicated: they go to rank 1 first
+    holders = np.array([1, 3, 1, 3, 3], dtype=np.uint32)
+    owner = assign_owners([0, 1, 2, 3, 4], [1, 1, 1, 1, 1], holders, 2)
+    assert owner == [0, 1, 0, 1, 0]  # loads after the single-holder pass: 34 vs 0
+    assert assign_owners([0, 1], [1, 1], np.array([0, 2], np.uint32), 2) == [2, 1]  # no holder: nobody
+    h = holders_for([[0, 2], [1, 3]], 5, replicated=(4,))
+    assert list(h) == [1, 2, 1, 2, 3]

@@ -297,10 +297,13 @@ def test_families_match_pinned_oracle(built_lib, family, shape):
 
 
 @pytest.mark.parametrize("family", ["qwen35", "glm"])
-def test_family_expert_parallel_split_is_exact(built_lib, family):
-    """The expert-parallel phases on one GPU with the experts split in two
-    stores (one holding the shared expert): the summed route rows and the
-    combine reproduce the single layer bit for bit."""
+@pytest.mark.parametrize("T", [8, 5])
+def test_family_expert_parallel_split_is_exact(built_lib, family, T):
+    """The expert-parallel phases of two ranks emulated on one GPU: experts
+    split over two stores, experts 0-3 held by both (replicated: the device
+    assigns each routed one to one rank), the shared expert on rank 0.  The
+    summed token-major route rows, combined whole or as the two ranks' token
+    shards, reproduce the single layer bit for bit (T = 5 pads to 6 tokens)."""
     from voom_b200.runtime import moe
 
     E, H, I = 32, 512, 256
@@ -308,21 +311,32 @@ def test_family_expert_parallel_split_is_exact(built_lib, family):
     full = moe.MoeLayer(store, wr.cuda(), nw.cuda(), top_k=4, **extra)
     table = [tuple(bits(w) for w in e) for e in ex]
     shared = tuple(bits(w) for w in ref["shared"])
-    halves = []
+    holders = np.array([3 if i < 4 else 1 << (i % 2) for i in range(E)] + [1], dtype=np.uint32)
+    ranks = []
     for r in range(2):
-        mine = [t if i % 2 == r else None for i, t in enumerate(table)]
+        mine = [t if holders[i] >> r & 1 else None for i, t in enumerate(table)]
         mine.append(shared if r == 0 else None)  # the shared expert's pages live on rank 0
-        halves.append(moe.ExpertParallelMoeLayer(moe.ExpertStore(mine, "cuda:0"), wr.cuda(), nw.cuda(), top_k=4,
-                                                 **extra))
-    x = torch.randn((8, H), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+        ranks.append(moe.ExpertParallelMoeLayer(moe.ExpertStore(mine, "cuda:0"), wr.cuda(), nw.cuda(), top_k=4,
+                                                holders=holders, rank=r, world=2, **extra))
+    x = torch.randn((T, H), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
     want = full(x)
-    ys = [hl.experts(x) for hl in halves]
+    ys = [lay.experts(x) for lay in ranks]
     y = ys[0] + ys[1]  # exactly one nonzero contributor per row
-    out = torch.empty_like(x)
-    halves[0].combine(x, y, out)
-    assert torch.equal(out, want)
-    for hl in halves:
-        hl.check_status()
+    tp, rpt = ranks[0].t_pad(T), ranks[0].rows_per_token
+    assert tp == T + T % 2 and y.shape[0] == tp * rpt
+    nz = [(yy.view(tp, rpt, H).abs().sum(-1) > 0) for yy in ys]
+    assert not (nz[0] & nz[1]).any()  # no route row computed twice
+    out = torch.empty((tp, H), dtype=torch.bfloat16, device="cuda")
+    ranks[0].combine(x, y, out, 0, tp)
+    assert torch.equal(out[:T], want)
+    ts = tp // 2
+    for r in range(2):
+        part = torch.empty((ts, H), dtype=torch.bfloat16, device="cuda")
+        ranks[r].combine(x, y[r * ts * rpt:(r + 1) * ts * rpt], part, r * ts, ts)
+        got = part[:max(0, min(ts, T - r * ts))]
+        assert torch.equal(got, want[r * ts:r * ts + got.shape[0]])
+    for lay in ranks:
+        lay.check_status()
 
 
 @pytest.mark.parametrize("counts", [(9, 1, 16), (64, 3, 40), (300, 8, 2)])

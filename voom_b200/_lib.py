@@ -64,6 +64,15 @@ class MoeVariant(ctypes.Structure):
     ]
 
 
+class MoeEp(ctypes.Structure):
+    _fields_ = [
+        ("d_holders", ctypes.c_void_p),
+        ("rank", ctypes.c_uint32),
+        ("world", ctypes.c_uint32),
+        ("t_pad", ctypes.c_uint32),
+    ]
+
+
 class RansPlanInfo(ctypes.Structure):
     _fields_ = [
         ("raw_size", ctypes.c_uint64),
@@ -118,6 +127,9 @@ SIGNATURES: dict[str, tuple] = {
                                 _u32, _u32, _vp, _u64, _vp, _vp]),
     "voom_moe_experts_v": (_i32, [_vp, _vp, _u32, _vp, _vp, ctypes.c_float, _vp, _u32, _u32, _u32, _u32, _u32,
                                   _u32, _vp, _vp, _u64, _vp, _vp]),
+    "voom_moe_experts_ep": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp, ctypes.c_float, _vp, _u32, _u32, _u32, _u32,
+                                   _u32, _u32, _vp, _vp, _u64, _vp, _vp]),
+    "voom_moe_combine_tm": (_i32, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
     "voom_moe_layer_noalloc": (_i32, [_vp, _u32, _vp, _vp, ctypes.c_float, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                       _u32, _u32, _u32, _vp, _vp]),
     "voom_nf12_decode": (_i32, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _u64, _vp, _vp]),

@@ -313,6 +313,7 @@ __global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, 
     for (uint32_t q = 0; q < p; q++) rank += (s_idx[q] == e) ? 1u : 0u;
     const uint32_t row = s_scan[u] + rank;
     r->upair[row] = p / k;
+    r->row_u[row] = uint16_t(u);
     r->w_bf16[row] = uint16_t(f2bf(r->w[p]));
     r->w_row[row] = r->w[p];
     // this token's routes ordered by unique index (experts of a token are distinct)
@@ -321,8 +322,15 @@ __global__ void __launch_bounds__(kMaxTK) moe_route_plan(Routes* r, uint32_t T, 
     for (uint32_t j = 0; j < k; j++) pos += (s_u[t0 + j] < u) ? 1u : 0u;
     r->tok_order[t0 + pos] = row;
   }
+  // every unique expert runs here unless moe_route_owners assigns owners
+  for (uint32_t q = p; q < nu + (has_shared ? 1u : 0u); q += blockDim.x) {
+    r->owned[q] = q;
+    r->mine[q] = 1;
+  }
+  if (p == 0) r->n_owned = nu + (has_shared ? 1u : 0u);
   if (has_shared) {
     for (uint32_t t = p; t < T; t += blockDim.x) {
+      r->row_u[n + t] = uint16_t(nu);
       r->upair[n + t] = t;
       r->w_bf16[n + t] = 0x3F80u;  // 1.0
       r->w_row[n + t] = 1.f;
@@ -338,7 +346,12 @@ __global__ void moe_route_offsets(Routes* r, uint32_t n_unique, uint32_t T) {
   r->family = VOOM_MOE_GENERIC;
   r->shared_u = kNoShared;
   r->uoff[0] = 0;
-  for (uint32_t u = 0; u < n_unique; u++) r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
+  for (uint32_t u = 0; u < n_unique; u++) {
+    r->uoff[u + 1] = r->uoff[u] + r->ntok[u];
+    r->owned[u] = u;
+    r->mine[u] = 1;
+  }
+  r->n_owned = n_unique;
   r->n_rows = r->uoff[n_unique];
 }
 
@@ -396,6 +409,107 @@ __global__ void moe_combine(const Routes* __restrict__ R, const uint16_t* __rest
   }
   const float base = residual ? bf2f(x[size_t(t) * H + c]) : 0.f;
   x_out[size_t(t) * H + c] = uint16_t(f2bf(base + o));
+}
+
+// Expert parallelism: the rank that computes each unique expert's rows.  An
+// expert whose pages one rank holds goes to that rank; an expert several ranks
+// hold (a replicated hot expert) goes, in unique order after every
+// single-holder expert is counted, to the least loaded of its holders (the
+// lowest rank on a tie).  Every rank runs this on the same routes, so every
+// route row is computed by exactly one rank.  Load of a unique expert = its
+// page decode (kPageLoad) + its tokens.  holders[e] (e < n_experts, and
+// n_experts for the shared expert): bit r = rank r holds the pages.  An
+// expert nobody holds is computed nowhere (its rows stay zero) and flagged.
+constexpr uint32_t kPageLoad = 16;
+
+__global__ void moe_route_owners(Routes* r, const uint32_t* __restrict__ holders, uint32_t rank, uint32_t world,
+                                 uint32_t* status) {
+  __shared__ uint32_t s_owner[kMaxU];
+  if (threadIdx.x == 0) {
+    uint32_t load[32];
+    for (uint32_t q = 0; q < 32; q++) load[q] = 0;
+    const uint32_t nu = r->n_unique, mask = world >= 32 ? 0xFFFFFFFFu : (1u << world) - 1u;
+    for (uint32_t u = 0; u < nu; u++) {
+      const uint32_t h = holders[r->expert[u]] & mask;
+      s_owner[u] = world;  // nobody (no holder), or decided in the second pass
+      if (h && !(h & (h - 1u))) {
+        const uint32_t o = uint32_t(__ffs(int(h))) - 1u;
+        s_owner[u] = o;
+        load[o] += kPageLoad + r->ntok[u];
+      } else if (!h) {
+        atomicOr(status, kStatusNoHolder);
+      }
+    }
+    for (uint32_t u = 0; u < nu; u++) {
+      uint32_t h = holders[r->expert[u]] & mask;
+      if (!h || !(h & (h - 1u))) continue;
+      uint32_t best = 0xFFFFFFFFu, bl = 0xFFFFFFFFu;
+      for (; h; h &= h - 1u) {
+        const uint32_t o = uint32_t(__ffs(int(h))) - 1u;
+        if (load[o] < bl) {
+          bl = load[o];
+          best = o;
+        }
+      }
+      s_owner[u] = best;
+      load[best] += kPageLoad + r->ntok[u];
+    }
+    uint32_t n = 0;
+    for (uint32_t u = 0; u < nu; u++) {
+      const bool m = s_owner[u] == rank;
+      r->mine[u] = m ? 1 : 0;
+      if (m) r->owned[n++] = u;
+    }
+    r->n_owned = n;
+  }
+}
+
+// Route rows in token-major order for the ranks' exchange: row t * rpt + j =
+// token t's j-th route in the combine's order (j = top_k: the shared expert),
+// zero when another rank computes it or t >= T (padding).  8 columns per thread.
+__global__ void moe_rows_token_major(const Routes* __restrict__ R, const uint16_t* __restrict__ y,
+                                     uint16_t* __restrict__ y_tm, uint32_t H) {
+  const uint32_t row = blockIdx.y, c = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c >= H) return;
+  const uint32_t k = R->k, rpt = k + (R->shared_u != kNoShared ? 1u : 0u);
+  const uint32_t t = row / rpt, j = row - t * rpt;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (t < R->T) {
+    const uint32_t q = j < k ? R->tok_order[t * k + j] : R->uoff[R->shared_u] + t;
+    if (R->mine[R->row_u[q]]) v = *reinterpret_cast<const uint4*>(y + size_t(q) * H + c);
+  }
+  *reinterpret_cast<uint4*>(y_tm + size_t(row) * H + c) = v;
+}
+
+// moe_combine over tokens t0 .. t0 + gridDim.y - 1 from token-major rows
+// (row (t - t0) * rpt + j); the same arithmetic, in the same order.  Rows of
+// tokens past T write zeros.
+__global__ void moe_combine_tm(const Routes* __restrict__ R, const uint16_t* __restrict__ y_tm,
+                               const uint16_t* __restrict__ x, uint16_t* __restrict__ x_out, uint32_t t0, uint32_t H,
+                               uint32_t residual) {
+  const uint32_t tl = blockIdx.y, t = t0 + tl;
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  if (t >= R->T) {
+    x_out[size_t(tl) * H + c] = 0;
+    return;
+  }
+  const uint32_t k = R->k, rpt = k + (R->shared_u != kNoShared ? 1u : 0u);
+  const bool fp32_w = R->family == VOOM_MOE_GLM;
+  const uint16_t* yr = y_tm + size_t(tl) * rpt * H + c;
+  float o = 0.f;
+  for (uint32_t j = 0; j < k; j++) {
+    const uint32_t q = R->tok_order[t * k + j];
+    const float w = fp32_w ? R->w_row[q] : bf2f(R->w_bf16[q]);
+    o = rbf(o + rbf(bf2f(yr[size_t(j) * H]) * w));
+  }
+  if (R->shared_u != kNoShared) {
+    float ys = bf2f(yr[size_t(k) * H]);
+    if (R->family == VOOM_MOE_QWEN35) ys = rbf(bf2f(R->sgate[t]) * ys);
+    o = rbf(o + ys);
+  }
+  const float base = residual ? bf2f(x[size_t(t) * H + c]) : 0.f;
+  x_out[size_t(tl) * H + c] = uint16_t(f2bf(base + o));
 }
 
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
@@ -677,6 +791,53 @@ VOOM_API int voom_moe_combine(const void* d_scratch, const uint16_t* d_y, const 
   const Routes* R = reinterpret_cast<const Routes*>(d_scratch);  // routes sit at the start of the scratch
   moe_combine<<<dim3((H + 255) / 256, T), 256, 0, static_cast<cudaStream_t>(stream)>>>(R, d_y, d_x, d_x_out, H,
                                                                                         residual);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+// Expert parallelism (one process per GPU): routing on every rank, each
+// routed expert computed by one rank (moe_route_owners), the route rows
+// returned in token-major order for a reduce-scatter over tokens; see the
+// header.
+VOOM_API int voom_moe_experts_ep(const voom_moe_variant* v, const voom_moe_ep* ep, const voom_expert_pages* d_pages,
+                                 uint32_t n_experts, const uint16_t* d_router_w, const uint16_t* d_norm_w, float eps,
+                                 const uint16_t* d_x, uint32_t T, uint32_t H, uint32_t I, uint32_t top_k,
+                                 uint32_t gate_tiles, uint32_t down_tiles, uint16_t* d_y_tm, void* d_scratch,
+                                 uint64_t scratch_bytes, uint32_t* d_status, void* stream) {
+  int rc = check_variant(v, n_experts);
+  if (rc != VOOM_OK) return rc;
+  if (!ep || !ep->d_holders || ep->world == 0 || ep->world > 32 || ep->rank >= ep->world || ep->t_pad < T ||
+      ep->t_pad % ep->world)
+    return VOOM_E_INVALID_ARG;
+  if (!d_pages || !d_router_w || !d_x || !d_y_tm || !d_scratch || !d_status) return VOOM_E_INVALID_ARG;
+  rc = check_shape(n_experts, T, H, I, top_k);
+  if (rc != VOOM_OK) return rc;
+  const uint32_t rpt = rows_per_token(*v, top_k);
+  const ScratchLayout L = layout(T, H, I, rpt);
+  if (scratch_bytes < L.total) return VOOM_E_CAPACITY;
+  uint8_t* s = static_cast<uint8_t*>(d_scratch);
+  Routes* R = reinterpret_cast<Routes*>(s + L.routes);
+  uint16_t* h = reinterpret_cast<uint16_t*>(s + L.h);
+  uint16_t* act = reinterpret_cast<uint16_t*>(s + L.act);
+  uint16_t* y = reinterpret_cast<uint16_t*>(s + L.y);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* logits = reinterpret_cast<float*>(s + L.logits);
+  launch_front(*v, d_router_w, d_norm_w, eps, d_x, n_experts, T, H, top_k, R, h, logits, st);
+  moe_route_owners<<<1, 32, 0, st>>>(R, ep->d_holders, ep->rank, ep->world, d_status);
+  const uint32_t max_unique = min(n_experts, T * top_k) + (v->shared_expert >= 0 ? 1u : 0u);
+  rc = launch_gemv(d_pages, R, h, act, y, y, H, I, max_unique, T * rpt, T, gate_tiles, down_tiles, s + L.seams,
+                   d_status, st);
+  if (rc != VOOM_OK) return rc;
+  moe_rows_token_major<<<dim3((H / 8 + 127) / 128, ep->t_pad * rpt), 128, 0, st>>>(R, y, d_y_tm, H);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
+VOOM_API int voom_moe_combine_tm(const void* d_scratch, const uint16_t* d_y_shard, const uint16_t* d_x,
+                                 uint16_t* d_out_shard, uint32_t t0, uint32_t t_count, uint32_t H, uint32_t residual,
+                                 void* stream) {
+  if (!d_scratch || !d_y_shard || !d_x || !d_out_shard || t_count == 0) return VOOM_E_INVALID_ARG;
+  const Routes* R = reinterpret_cast<const Routes*>(d_scratch);  // routes sit at the start of the scratch
+  moe_combine_tm<<<dim3((H + 255) / 256, t_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      R, d_y_shard, d_x, d_out_shard, t0, H, residual);
   return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
 }
 

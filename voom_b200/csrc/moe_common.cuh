@@ -36,6 +36,12 @@ struct Routes {
   uint16_t sgate[kMaxTK];       // qwen35: bf16(sigmoid(bf16(h_t . Wsg))) per token
   uint32_t shared_u;            // unique index of the shared expert, or kNoShared
   uint32_t n_rows;              // route rows in use
+  // the unique experts this GPU computes (all of them unless expert
+  // parallelism assigns owners): owned[0 .. n_owned), and mine[u] = 1 for those
+  uint32_t n_owned;
+  uint32_t owned[kMaxU];
+  uint8_t mine[kMaxU];
+  uint16_t row_u[kMaxRows];     // [route row] unique expert of the row
 };
 
 __device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }

@@ -52,6 +52,7 @@ constexpr uint32_t kStatusPage = 1u;      // a segment missed its checkpoint (da
 constexpr uint32_t kStatusRoutes = 2u;    // an expert has more tokens than the launch covers
 constexpr uint32_t kStatusGeometry = 4u;  // page geometry the kernels do not take
 constexpr uint32_t kStatusTimeout = 8u;   // a tensor-core completion wait ran out
+constexpr uint32_t kStatusNoHolder = 16u;  // expert parallelism: a routed expert no rank holds
 
 __host__ __device__ inline uint32_t every_rule(uint32_t cols) {
   uint32_t e = VOOM_EVERY_MAX;
@@ -340,16 +341,16 @@ __global__ void __launch_bounds__(kThreads, 4) moe_proj_cc(const voom_expert_pag
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   CcShared& sh = *reinterpret_cast<CcShared*>(smem_raw);
   __shared__ uint32_t s_item;
-  const uint32_t per_u = n_proj * nbpp, total = R->n_unique * per_u;
+  const uint32_t per_u = n_proj * nbpp, total = R->n_owned * per_u;
   for (;;) {
     if (threadIdx.x == 0) s_item = atomicAdd(counter, 1u);
     __syncthreads();
     const uint32_t item = s_item;
     __syncthreads();
     if (item >= total) break;
-    const uint32_t u = item / per_u;
-    cc_item<NT>(sh, pages, R, which, u, item - u * per_u, act, ld_in, out0, out1, ld_out, nbpp, cpt, tiles_hint,
-                seams, status);
+    const uint32_t o = item / per_u;
+    cc_item<NT>(sh, pages, R, which, R->owned[o], item - o * per_u, act, ld_in, out0, out1, ld_out, nbpp, cpt,
+                tiles_hint, seams, status);
   }
 }
 
@@ -486,8 +487,8 @@ __global__ void __launch_bounds__(kThreads, 2) moe_proj_mma(const voom_expert_pa
                                                             uint32_t ld_out, uint32_t nbpp, uint32_t ncap,
                                                             uint32_t* status) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t u = blockIdx.y;
-  if (u >= R->n_unique) return;
+  if (blockIdx.y >= R->n_owned) return;
+  const uint32_t u = R->owned[blockIdx.y];
   const uint32_t n = R->ntok[u];
   if (n <= uint32_t(kTok)) return;  // moe_proj_cc serves this expert
   const uint32_t j0 = blockIdx.z * kMmaMaxN;

@@ -39,6 +39,7 @@ STATUS_PAGE = 1    # a compressed expert page failed its checkpoint verification
 STATUS_ROUTES = 2  # an expert got more route rows than the launch covered
 STATUS_GEOMETRY = 4  # page geometry the kernels do not take (segment length, tile size or count)
 STATUS_TIMEOUT = 8  # a tensor-core completion wait ran out (reported, never observed)
+STATUS_NO_HOLDER = 16  # expert parallelism: a routed expert that no rank holds
 
 
 def raise_on_status(status: torch.Tensor, what: str) -> None:
@@ -58,6 +59,8 @@ def raise_on_status(status: torch.Tensor, what: str) -> None:
             parts.append("an expert page has a geometry the fused kernels do not take")
         if v & STATUS_TIMEOUT:
             parts.append("a tensor-core completion wait ran out")
+        if v & STATUS_NO_HOLDER:
+            parts.append("a routed expert is held by no rank")
         raise ValueError(f"{what}: " + "; ".join(parts or [f"status 0x{v:x}"]))
 
 
@@ -347,20 +350,76 @@ def place_experts(load, world: int) -> list[list[int]]:
     return [sorted(b) for b in bins]
 
 
+PAGE_LOAD = 16  # load of one expert's page decode, in tokens (kPageLoad in csrc/expert.cu)
+
+
+def assign_owners(unit_experts, ntok, holders, world: int) -> list[int]:
+    """Owner rank of each unique expert under expert parallelism, as
+    moe_route_owners computes it on the device: an expert one rank holds is
+    that rank's; the others, in unique order after all single-holder experts
+    are counted, go to their least loaded holder (lowest rank on a tie); load
+    of a unique expert = PAGE_LOAD + its tokens.  `holders[e]`: bit r = rank r
+    holds expert e.  An expert no rank holds gets `world` (computed nowhere)."""
+    mask = (1 << world) - 1
+    load = [0] * world
+    owner = [world] * len(unit_experts)
+    for u, e in enumerate(unit_experts):
+        h = int(holders[e]) & mask
+        if h and not h & (h - 1):
+            owner[u] = h.bit_length() - 1
+            load[owner[u]] += PAGE_LOAD + int(ntok[u])
+    for u, e in enumerate(unit_experts):
+        h = int(holders[e]) & mask
+        if not h or not h & (h - 1):
+            continue
+        best = min((o for o in range(world) if h >> o & 1), key=lambda o: (load[o], o))
+        owner[u] = best
+        load[best] += PAGE_LOAD + int(ntok[u])
+    return owner
+
+
+def holders_for(placement: list[list[int]], n_entries: int, replicated=()) -> np.ndarray:
+    """Holder masks (bit r = rank r holds the expert) from per-rank expert
+    lists, with the `replicated` experts held by every rank."""
+    h = np.zeros(n_entries, dtype=np.uint32)
+    for r, experts in enumerate(placement):
+        for e in experts:
+            h[e] |= np.uint32(1 << r)
+    for e in replicated:
+        h[e] = np.uint32((1 << len(placement)) - 1)
+    return h
+
+
 class ExpertParallelMoeLayer:
     """MoE layer with experts spread over the ranks of a process group (NCCL).
 
-    Every rank routes all tokens (replicated router), runs the fused decode +
-    SwiGLU for its own experts only (and the shared expert, on the rank that
-    holds its pages), the route rows are summed over ranks with one
-    all-reduce (each row has exactly one nonzero contributor, so the sum is
-    exact), and every rank applies the same ordered combine.  Same family
+    Every rank routes all tokens (replicated router) and computes only the
+    routed experts it owns: an expert whose pages one rank holds is that
+    rank's; an expert several ranks hold (replicated hot experts) goes to the
+    least loaded of its holders by a rule every rank evaluates alike on the
+    device, so each route row is computed exactly once and only owned experts
+    launch work.  The route rows come back in token-major order; a
+    reduce-scatter over tokens (every row has one nonzero contributor, so the
+    sum is exact) gives each rank the rows of its share of the tokens, the
+    rank applies the ordered combine to them, and an all-gather of the
+    combined rows gives every rank the layer output -- bit-identical to
+    MoeLayer on one GPU, for about (1 + 1/rows_per_token) / 2 of the bytes an
+    all-reduce of the route rows would move.
+
+    Which ranks hold which experts is gathered once at construction from the
+    ranks' stores (`holders`, one bit mask per store entry, overrides it; with
+    `rank` and `world` it lets one process emulate a rank).  Same family
     options as MoeLayer."""
 
     def __init__(self, store: ExpertStore, router_w: torch.Tensor, norm_w: torch.Tensor | None, *, top_k: int,
                  norm_topk: bool = True, eps: float = 1e-6, group=None, router_bias: torch.Tensor | None = None,
                  family: str = "generic", shared: int | None = None, shared_gate_w: torch.Tensor | None = None,
-                 routed_scale: float = 1.0):
+                 routed_scale: float = 1.0, holders: np.ndarray | None = None, rank: int | None = None,
+                 world: int | None = None):
+        import torch.distributed as dist
+
+        from .._lib import MoeEp
+
         self.store = store
         self.router_w = router_w.contiguous()
         self.n_experts = int(self.router_w.shape[0])
@@ -374,49 +433,90 @@ class ExpertParallelMoeLayer:
         self.shared_gate_w = None if shared_gate_w is None else shared_gate_w.contiguous()
         self.variant = _variant(family, self.norm_topk, routed_scale, shared, self.shared_gate_w, self.router_bias)
         self.rows_per_token = self.top_k + (0 if shared is None else 1)
+        on = dist.is_available() and dist.is_initialized()
+        self.world = int(world) if world is not None else (dist.get_world_size(group) if on else 1)
+        self.rank = int(rank) if rank is not None else (dist.get_rank(group) if on else 0)
+        if not 0 <= self.rank < self.world <= 32:
+            raise ValueError(f"rank {self.rank} of {self.world}: expert parallelism takes 1..32 ranks")
+        if holders is None:
+            mine = torch.zeros(len(store), dtype=torch.int64, device=store.device)
+            if store.local:
+                mine[torch.tensor(store.local, device=store.device)] = 1 << self.rank
+            if self.world > 1:
+                dist.all_reduce(mine, group=group)  # distinct bits: the sum is the OR
+            holders = mine.cpu().numpy()
+        holders = np.asarray(holders, dtype=np.int64).astype(np.uint32)
+        if holders.shape != (len(store),):
+            raise ValueError(f"holders: one mask per store entry ({len(store)}), got {holders.shape}")
+        self.holders = _device.tensor_from_numpy(holders, store.device)
+        self._ep = {}
+        self._MoeEp = MoeEp
         self._scratch: dict[int, torch.Tensor] = {}
-        self._y: dict[int, torch.Tensor] = {}
+        self._bufs: dict[int, tuple] = {}
         self.status = torch.zeros(1, dtype=torch.int32, device=store.device)
         self.last_collective_bytes = 0
 
-    def buffers(self, T: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """(scratch, route-row buffer) for T tokens, allocated once."""
+    def t_pad(self, T: int) -> int:
+        return -(-T // self.world) * self.world
+
+    def buffers(self, T: int) -> tuple:
+        """(scratch, token-major rows, this rank's rows, this rank's combined
+        rows, combined rows of all ranks) for T tokens, allocated once."""
         st = self.store
         if T not in self._scratch:
             n = load().voom_moe_scratch_bytes_v(ctypes.byref(self.variant), T, st.H, st.I, self.top_k)
             self._scratch[T] = torch.empty(int(n), dtype=torch.uint8, device=st.device)
-            self._y[T] = torch.empty((T * self.rows_per_token, st.H), dtype=torch.bfloat16, device=st.device)
-        return self._scratch[T], self._y[T]
+            tp = self.t_pad(T)
+            ts = tp // self.world
+            self._bufs[T] = (torch.empty((tp * self.rows_per_token, st.H), dtype=torch.bfloat16, device=st.device),
+                             torch.empty((ts * self.rows_per_token, st.H), dtype=torch.bfloat16, device=st.device),
+                             torch.empty((ts, st.H), dtype=torch.bfloat16, device=st.device),
+                             torch.empty((tp, st.H), dtype=torch.bfloat16, device=st.device))
+            self._ep[T] = self._MoeEp(self.holders.data_ptr(), self.rank, self.world, tp)
+        return (self._scratch[T], *self._bufs[T])
 
     def experts(self, x: torch.Tensor) -> torch.Tensor:
-        """Phase 1 on this rank: routes + this rank's expert rows (others zero)."""
+        """Phase 1 on this rank: routes + this rank's route rows, token-major
+        (t_pad(T) * rows_per_token rows; other ranks' rows zero)."""
         T, H = x.shape
         st = self.store
-        s, y = self.buffers(T)
-        check(load().voom_moe_experts_v(ctypes.byref(self.variant), st.table.data_ptr(), self.n_experts,
-                                        self.router_w.data_ptr(),
-                                        None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
-                                        x.data_ptr(), T, H, st.I, self.top_k, st.gate_tiles, st.down_tiles,
-                                        y.data_ptr(), s.data_ptr(), s.numel(), self.status.data_ptr(),
-                                        _device.stream_ptr(st.device, None)), "voom_moe_experts_v")
-        return y
+        s, y_tm = self.buffers(T)[:2]
+        check(load().voom_moe_experts_ep(ctypes.byref(self.variant), ctypes.byref(self._ep[T]), st.table.data_ptr(),
+                                         self.n_experts, self.router_w.data_ptr(),
+                                         None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                         x.data_ptr(), T, H, st.I, self.top_k, st.gate_tiles, st.down_tiles,
+                                         y_tm.data_ptr(), s.data_ptr(), s.numel(), self.status.data_ptr(),
+                                         _device.stream_ptr(st.device, None)), "voom_moe_experts_ep")
+        return y_tm
 
-    def combine(self, x: torch.Tensor, y: torch.Tensor, out: torch.Tensor, residual: bool = True) -> None:
+    def combine(self, x: torch.Tensor, rows: torch.Tensor, out: torch.Tensor, t0: int, count: int,
+                residual: bool = True) -> None:
+        """Phase 2: the ordered combine of tokens [t0, t0 + count) from their
+        token-major rows into `out` (count rows)."""
         T, H = x.shape
-        s, _ = self.buffers(T)
-        check(load().voom_moe_combine(s.data_ptr(), y.data_ptr(), x.data_ptr(), out.data_ptr(), T, H, int(residual),
-                                      _device.stream_ptr(self.store.device, None)), "voom_moe_combine")
+        s = self.buffers(T)[0]
+        check(load().voom_moe_combine_tm(s.data_ptr(), rows.data_ptr(), x.data_ptr(), out.data_ptr(), t0, count, H,
+                                         int(residual), _device.stream_ptr(self.store.device, None)),
+              "voom_moe_combine_tm")
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, residual: bool = True) -> torch.Tensor:
         import torch.distributed as dist
 
         x = x.contiguous()
+        T, H = x.shape
         out = torch.empty_like(x) if out is None else out
-        y = self.experts(x)
-        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
-            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
-            self.last_collective_bytes = y.numel() * y.element_size()
-        self.combine(x, y, out, residual)
+        y_tm = self.experts(x)
+        _, _, shard, part, full = self.buffers(T)
+        ts = self.t_pad(T) // self.world
+        if self.world > 1:
+            dist.reduce_scatter_tensor(shard, y_tm, group=self.group)
+            self.combine(x, shard, part, self.rank * ts, ts, residual)
+            dist.all_gather_into_tensor(full, part, group=self.group)
+            self.last_collective_bytes = (y_tm.numel() + full.numel()) * 2
+        else:
+            self.combine(x, y_tm, full, 0, ts, residual)
+            self.last_collective_bytes = 0
+        out.copy_(full[:T])
         return out
 
     __call__ = forward
