@@ -2,9 +2,9 @@
 // zstd frames (src.bin, jobs.bin as voom_zstd_job records, raw.bin = expected
 // output) with voom_zstd_plan_create / voom_zstd_decode, three times, then
 // checks every status word and the bytes.  No Python: ncu can attach to it.
-// Inputs: `python -m voom_b200.cabi_example.make_kv_frames DIR` (config 5 KV
-// pages) or `python -m voom_b200.cabi_example.make_vpack_bodies DIR` (config 2
-// vpack bodies, interleaved jobs).
+// Inputs: any host script that writes the compressed bytes, the job records
+// (voom_b200.formats.packed.body_job gives a vpack body's interleaved job) and
+// the expected output image with the jobs' outputs packed end to end.
 //   nvcc -O2 -std=c++17 -I include -o voom_b200/cabi_example/kv_decode \
 //        voom_b200/cabi_example/kv_decode.cpp -L voom_b200 -lvoom_b200 \
 //        -Xlinker -rpath -Xlinker '$ORIGIN/..'
