@@ -171,3 +171,66 @@ def test_verify_generation_decodes_every_body(archive_dir):
     rep = verify_generation(archive_dir)
     assert len(rep["errors"]) == 1 and rep["errors"][0].startswith(f"decode failure at {name}: ")
     assert rep["decoded"] == len(index) - 1
+
+
+def test_gpu_repack_bodies_decode_through_reference_path(built_lib):
+    """bodies_gpu (hi planes encoded on the GPU): every body decodes through
+    the reference's decode_body (restated: libzstd + numpy interleave) and
+    through the GPU decoder to the original bytes, for device and host inputs,
+    odd and tiny sizes and a raw dtype; BF16 weight bodies stay within 3 % of
+    host zstd level 1."""
+    from voom_b200 import synthetic
+    from voom_b200.formats import packed
+
+    dev = torch.device("cuda", 0)
+    specs = [((256, 192), 1), ((1, 2), 2), ((3, 5), 3), ((4096, 576), 4), ((7,), 5)]
+    raws = [synthetic.bf16_normal(shape, 0.02, seed).view(np.uint8).reshape(-1) for shape, seed in specs]
+    raws.append(np.arange(37, dtype=np.float32).view(np.uint8))
+    dtypes = ["BF16"] * len(specs) + ["F32"]
+    items = [(dt, torch.from_numpy(r.copy()).to(dev) if i % 2 == 0 else r.tobytes())
+             for i, (dt, r) in enumerate(zip(dtypes, raws))]
+    bodies = packed.bodies_gpu(items)
+    heads = [h for h, _ in bodies]
+    for (head, body), raw, dt in zip(bodies, raws, dtypes):
+        assert np.array_equal(ov.decode_body(head, body), raw), head
+        if dt == "BF16":
+            assert head["lo"] == raw.size // 2 and len(body) == head["hi_z"] + head["lo"]
+    blob = b"".join(b for _, b in bodies)
+    offs = np.cumsum([0] + [len(b) for _, b in bodies[:-1]]).tolist()
+    out, spans = packed.decode_bodies(heads, np.frombuffer(blob, np.uint8), offs, [len(b) for _, b in bodies],
+                                      device=dev)
+    got = out.cpu().numpy()
+    for (o, n), raw in zip(spans, raws):
+        assert np.array_equal(got[o:o + n], raw)
+    big = raws[3]
+    ours = len(bodies[3][1])
+    ref = len(packed.body_for("BF16", big, 1)[1])
+    assert ours <= 1.03 * ref, (ours, ref)
+
+
+def test_pack_model_gpu_encoder_round_trip(built_lib, tmp_path):
+    """pack_model(encoder='gpu') writes the reference layout (fused expert
+    split, raw dtypes) whose every tensor the reference's decode path and the
+    GPU reader give back exactly."""
+    from tests.golden.make_golden import write_safetensors
+    from tests.test_vpack_cpu import source_tensors
+    from voom_b200.formats import packed
+
+    src = tmp_path / "model"
+    src.mkdir()
+    tensors = source_tensors()
+    write_safetensors(src / "model.safetensors", tensors)
+    out = packed.pack_model(src, tmp_path / "gpu.vpack", encoder="gpu", batch_bytes=64 << 10)
+    host = packed.pack_model(src, tmp_path / "host.vpack")
+    man = json.loads((out / "manifest.json").read_text())
+    assert man == json.loads((host / "manifest.json").read_text())
+    by_name = {n: raw for n, _, _, raw in tensors}
+    for name, fname in man.items():
+        data = (out / fname).read_bytes()
+        n = int.from_bytes(data[:8], "little")
+        head = json.loads(data[8:8 + n])
+        raw = ov.decode_body(head, np.frombuffer(data[8 + n:], np.uint8))
+        _, t = packed.read_tensor_bytes(out, fname)
+        assert np.array_equal(t.cpu().numpy(), raw)
+        if name in by_name:
+            assert raw.tobytes() == by_name[name]

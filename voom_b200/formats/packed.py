@@ -5,7 +5,8 @@ an 8-byte little-endian header length, a JSON head, then the body.  For
 BF16/F16 the body is `hi_z` (zstd of the odd bytes) followed by `lo` (the even
 bytes, raw); tensors above STREAM_THRESHOLD use the streamed variant (lo raw
 first, then one zstd stream of the hi plane to EOF); other dtypes are stored
-raw.  `pack_model` writes that layout (pack side, host zstd);
+raw.  `pack_model` writes that layout (host zstd, or the GPU encoder for a
+fast repack: `bodies_gpu`);
 `read_tensor_bytes` and `to_torch` decode on the GPU.
 
 Reference interface replaced: formats/packed.py:63-81 (streamed pack),
@@ -46,6 +47,89 @@ def body_for(dtype: str, raw, level: int = 1) -> tuple[dict, bytes]:
     return {"raw": a.size}, a.tobytes()
 
 
+def bodies_gpu(items, device=None) -> list[tuple[dict, bytes]]:
+    """(head, body) of many tensors in ordinary vpack form, with every hi plane
+    compressed on the GPU: a fast repack path (the reference packs with host
+    zstd level 1, formats/packed.py:125-358).  The frames come from
+    voom_zstd_encode (Huffman-literal blocks, Raw or RLE where smaller): valid
+    zstd frames that the reference's decode_body reads back exactly, not
+    libzstd's bytes.  `items`: (dtype, data) pairs, data a CUDA tensor or host
+    bytes / uint8 array; plane dtypes are split into byte planes on the device
+    (hi = odd bytes, lo = even bytes), other dtypes are stored raw.  All hi
+    planes are encoded in one batch and every host transfer is one copy."""
+    from .. import _device
+    from . import zstd_gpu
+
+    dev = _device.require_cuda(device)
+    flat, host_idx = [], []
+    for i, (_, data) in enumerate(items):
+        if isinstance(data, torch.Tensor):
+            flat.append(data.reshape(-1).view(torch.uint8).to(dev))
+        else:
+            flat.append(None)
+            host_idx.append(i)
+    if host_idx:  # host data: one pinned staging buffer, one upload
+        arrs = [np.frombuffer(items[i][1], np.uint8) if not isinstance(items[i][1], np.ndarray)
+                else items[i][1].reshape(-1).view(np.uint8) for i in host_idx]
+        pinned = _device.pinned_empty(max(1, sum(a.size for a in arrs)))
+        pn = pinned.numpy()
+        pos, spans = 0, []
+        for a in arrs:
+            pn[pos:pos + a.size] = a
+            spans.append((pos, a.size))
+            pos += a.size
+        up = pinned[:pos].to(dev, non_blocking=True) if pos else torch.empty(0, dtype=torch.uint8, device=dev)
+        for i, (o, n) in zip(host_idx, spans):
+            flat[i] = up[o:o + n]
+    plane = [items[i][0] in PLANE_DTYPES for i in range(len(items))]
+    # hi planes at 16-byte aligned offsets (the encoder's source rule), lo planes and raw tensors packed
+    hi_offs, hi_lens, lo_spans, raw_spans = [], [], [], []
+    hpos = lpos = 0
+    for i, u8 in enumerate(flat):
+        n = int(u8.numel())
+        if plane[i]:
+            hi_offs.append(hpos)
+            hi_lens.append(n // 2)
+            hpos += (n // 2 + 15) // 16 * 16
+            lo_spans.append((lpos, n - n // 2))
+            lpos += n - n // 2
+        else:
+            raw_spans.append((lpos, n))
+            lpos += n
+    hi_buf = torch.empty(max(hpos, 16), dtype=torch.uint8, device=dev)
+    rest = torch.empty(max(lpos, 1), dtype=torch.uint8, device=dev)
+    k = 0
+    for i, u8 in enumerate(flat):
+        if plane[i]:
+            o, n = hi_offs[k], hi_lens[k]
+            hi_buf[o:o + n].copy_(u8[1::2])
+            lo, ln = lo_spans[k]
+            rest[lo:lo + ln].copy_(u8[0::2])
+            k += 1
+    kr = 0
+    for i, u8 in enumerate(flat):
+        if not plane[i]:
+            o, n = raw_spans[kr]
+            rest[o:o + n].copy_(u8)
+            kr += 1
+    frames = zstd_gpu.compress_many(hi_buf, hi_offs, hi_lens) if hi_offs else []
+    rest_h = _device.pinned_empty(max(lpos, 1))
+    rest_h.copy_(rest)
+    mv = memoryview(rest_h.numpy())
+    out, k, kr = [], 0, 0
+    for i in range(len(items)):
+        if plane[i]:
+            lo, ln = lo_spans[k]
+            hz = frames[k]
+            out.append(({"hi_z": len(hz), "lo": ln}, hz + bytes(mv[lo:lo + ln])))
+            k += 1
+        else:
+            o, n = raw_spans[kr]
+            out.append(({"raw": n}, bytes(mv[o:o + n])))
+            kr += 1
+    return out
+
+
 def streamed_body(raw, level: int = 1, chunk: int = CHUNK) -> tuple[dict, bytes]:
     """Streamed variant (formats/packed.py:63-81): lo raw, then the hi zstd stream."""
     a = np.frombuffer(raw, np.uint8) if not isinstance(raw, np.ndarray) else raw.reshape(-1).view(np.uint8)
@@ -77,16 +161,43 @@ def _iter_safetensors(path: Path):
             yield name, meta, f.read(b - a)
 
 
-def pack_model(model_dir: str | Path, out_dir: str | Path | None = None, level: int = 1) -> Path:
+def pack_model(model_dir: str | Path, out_dir: str | Path | None = None, level: int = 1,
+               encoder: str = "host", batch_bytes: int = 512 << 20) -> Path:
     """Pack every *.safetensors tensor of model_dir into a vpack directory
     (formats/packed.py:125-358 layout, including the per-expert split of fused
-    BF16 MoE tensors and the streamed variant above STREAM_THRESHOLD)."""
+    BF16 MoE tensors and the streamed variant above STREAM_THRESHOLD).
+    encoder="gpu" encodes the ordinary bodies' hi planes on the GPU (bodies_gpu,
+    batches of about `batch_bytes`); streamed bodies use host zstd either way."""
+    if encoder not in ("host", "gpu"):
+        raise ValueError(f"encoder must be 'host' or 'gpu', got {encoder!r}")
     model_dir = Path(model_dir)
     out = Path(out_dir) if out_dir else model_dir / "weights.vpack"
     out.mkdir(parents=True, exist_ok=True)
     manifest: dict[str, str] = {}
     t0 = time.perf_counter()
     total_in = total_out = 0
+    pending: list = []  # ordinary bodies waiting for a GPU batch: (name, fname, dtype, shape, raw)
+
+    def emit(name, fname, dtype, shape, raw):
+        nonlocal total_out
+        if encoder == "gpu":
+            pending.append((name, fname, dtype, shape, raw))
+            if sum(len(p[4]) for p in pending) >= batch_bytes:
+                flush()
+            return
+        head, body = body_for(dtype, raw, level)
+        total_out += write_vt(out / fname, {"dtype": dtype, "shape": shape, **head}, body)
+        manifest[name] = fname
+
+    def flush():
+        nonlocal total_out
+        if not pending:
+            return
+        for (name, fname, dtype, shape, _), (head, body) in zip(pending, bodies_gpu([(p[2], p[4]) for p in pending])):
+            total_out += write_vt(out / fname, {"dtype": dtype, "shape": shape, **head}, body)
+            manifest[name] = fname
+        pending.clear()
+
     for shard in sorted(model_dir.glob("*.safetensors")):
         for name, meta, raw in _iter_safetensors(shard):
             fused = _FUSED_BF16_EXPERT_RE.match(name)
@@ -103,20 +214,18 @@ def pack_model(model_dir: str | Path, out_dir: str | Path | None = None, level: 
                         parts = (("down_proj.weight", list(meta["shape"][1:]), raw_e),)
                     for proj, shape, sub in parts:
                         sub_name = f"{fused.group(1)}.{e}.{proj}"
-                        head, body = body_for(meta["dtype"], sub, level)
-                        fname = sub_name.replace("/", "__") + ".vt"
-                        total_out += write_vt(out / fname, {"dtype": meta["dtype"], "shape": shape, **head}, body)
-                        manifest[sub_name] = fname
+                        emit(sub_name, sub_name.replace("/", "__") + ".vt", meta["dtype"], shape, sub)
                 total_in += len(raw)
                 continue
             fname = name.replace("/", "__") + ".vt"
             if meta["dtype"] in PLANE_DTYPES and len(raw) > STREAM_THRESHOLD:
                 head, body = streamed_body(raw, level)
+                total_out += write_vt(out / fname, {"dtype": meta["dtype"], "shape": meta["shape"], **head}, body)
+                manifest[name] = fname
             else:
-                head, body = body_for(meta["dtype"], raw, level)
-            total_out += write_vt(out / fname, {"dtype": meta["dtype"], "shape": meta["shape"], **head}, body)
-            manifest[name] = fname
+                emit(name, fname, meta["dtype"], meta["shape"], raw)
             total_in += len(raw)
+    flush()
     (out / "manifest.json").write_text(json.dumps(manifest))
     dt = time.perf_counter() - t0
     print(f"packed {total_in / 1e9:.3f}GB -> {total_out / 1e9:.3f}GB "
