@@ -434,6 +434,68 @@ class C2Vpack:
                           f"({self.local_raw} B decoded per pass) with decode_body restated (libzstd + numpy) "
                           f"on {threads} thread(s), {dt:.1f} s"}
 
+    def repack_leg(self, threads: int, reps: int = 3) -> dict:
+        """The GPU repack of this archive's tensors (packed.bodies_gpu: byte
+        planes split on the device, hi planes encoded by the GPU zstd encoder)
+        against host zstd level 1 (the reference's pack call) on `threads`
+        threads: raw tensor bytes per second, and the bodies' total size."""
+        torch = self.torch
+        from concurrent.futures import ThreadPoolExecutor
+
+        from voom_b200.formats import packed, zstd_gpu, zstd_host
+
+        names = self.names
+        dev_t = [torch.from_numpy(self.raws[n].reshape(-1).view(np.uint8).copy()).to(self.dev) for n in names]
+        raw_bytes = sum(int(t.numel()) for t in dev_t)
+        items = [("BF16", t) for t in dev_t]
+        bodies = packed.bodies_gpu(items)  # warm-up (and the size)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            bodies = packed.bodies_gpu(items)
+        e2e_s = (time.perf_counter() - t0) / reps
+        gpu_bytes = sum(len(b) for _, b in bodies)
+        # device encode alone: the hi planes at 16-byte offsets, one EncodePlan, CUDA events
+        offs, lens, pos = [], [], 0
+        for t in dev_t:
+            offs.append(pos)
+            lens.append(int(t.numel()) // 2)
+            pos += (int(t.numel()) // 2 + 15) // 16 * 16
+        hi = torch.empty(pos, dtype=torch.uint8, device=self.dev)
+        for o, n, t in zip(offs, lens, dev_t):
+            hi[o:o + n].copy_(t[1::2])
+        plan = zstd_gpu.EncodePlan(offs, lens, self.dev)
+        plan.run(hi)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            plan.run(hi)
+        b.record()
+        torch.cuda.synchronize()
+        dev_ms = a.elapsed_time(b) / reps
+        # host: zstd level 1 of the hi planes (+ the lo plane copy), bounded sample
+        host_items = [self.raws[n].reshape(-1).view(np.uint8) for n in names]
+
+        def one(arr):
+            return len(zstd_host.compress(np.ascontiguousarray(arr[1::2]), 1)) + arr.size // 2
+
+        done = host_bytes = 0
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            while time.perf_counter() - t0 < 2.0 or done == 0:
+                host_bytes = sum(pool.map(one, host_items))
+                done += 1
+        host_s = (time.perf_counter() - t0) / done
+        del dev_t, hi
+        return {"metric": "vpack repack GB/s (raw tensor bytes in, bodies out)", "unit": "GB/s",
+                "device_encode": round(raw_bytes / (dev_ms * 1e-3) / 1e9, 3),
+                "device_encode_ms": round(dev_ms, 4),
+                "e2e": round(raw_bytes / e2e_s / 1e9, 3),
+                "e2e_note": "packed.bodies_gpu: plane split and encode on the device, bodies in host memory",
+                "host_libzstd_level1": round(raw_bytes / host_s / 1e9, 3), "host_threads": threads,
+                "body_bytes_gpu": int(gpu_bytes), "body_bytes_host_level1": int(host_bytes),
+                "tensors": len(names), "raw_bytes": int(raw_bytes)}
+
     def config(self) -> dict:
         return {"workload": self.name, "tensors": len(self.all_names), "zstd_blocks_this_rank": self.n_blocks,
                 "archive_bytes": int(self.archive_bytes), "raw_bytes": int(self.raw_bytes),
@@ -1524,6 +1586,8 @@ def headline(args, world, rank, local, dev):
         "decode_ms_per_step": round(dec_ms, 5),
         **({"kernel_ms": kernel_ms} if kernel_ms is not None else {}),
     }
+    if world == 1 and not args.no_cpu:
+        line["repack"] = w.repack_leg(host_threads)
     if world > 1:
         line["collective"] = {"op": "NCCL all-gather of the decoded bodies", "bytes_per_rank": int(w.gather_bytes),
                               "ms_per_step": round(ms - dec_ms, 5), "share_of_step": round(1 - dec_ms / ms, 4)}
@@ -1677,7 +1741,7 @@ def main():
     ap.add_argument("--c4-layers", type=int, default=4, help="config-4 routers per step")
     ap.add_argument("--kv-pages", type=int, default=65536, help="c6_kv_paged: KV pages (65536 = config 5)")
     ap.add_argument("--no-moe", action="store_true", help="default run: config 2 only")
-    ap.add_argument("--no-cpu", action="store_true", help="--workload runs: skip the CPU baseline leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs and the repack leg")
     ap.add_argument("--kernel-times", action="store_true",
                     help="zstd workloads: after the timed steps, time `--steps` more steps with a CUDA event after "
                          "every kernel launch and report the mean ms per kernel per step ('kernel_ms')")

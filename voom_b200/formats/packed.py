@@ -82,51 +82,54 @@ def bodies_gpu(items, device=None) -> list[tuple[dict, bytes]]:
         for i, (o, n) in zip(host_idx, spans):
             flat[i] = up[o:o + n]
     plane = [items[i][0] in PLANE_DTYPES for i in range(len(items))]
-    # hi planes at 16-byte aligned offsets (the encoder's source rule), lo planes and raw tensors packed
-    hi_offs, hi_lens, lo_spans, raw_spans = [], [], [], []
-    hpos = lpos = 0
+    # the encoder's source: hi planes at 16-byte aligned offsets
+    hi_offs, hi_lens, hpos = [], [], 0
     for i, u8 in enumerate(flat):
-        n = int(u8.numel())
         if plane[i]:
             hi_offs.append(hpos)
-            hi_lens.append(n // 2)
-            hpos += (n // 2 + 15) // 16 * 16
-            lo_spans.append((lpos, n - n // 2))
-            lpos += n - n // 2
-        else:
-            raw_spans.append((lpos, n))
-            lpos += n
+            hi_lens.append(int(u8.numel()) // 2)
+            hpos += (hi_lens[-1] + 15) // 16 * 16
     hi_buf = torch.empty(max(hpos, 16), dtype=torch.uint8, device=dev)
-    rest = torch.empty(max(lpos, 1), dtype=torch.uint8, device=dev)
     k = 0
     for i, u8 in enumerate(flat):
         if plane[i]:
-            o, n = hi_offs[k], hi_lens[k]
-            hi_buf[o:o + n].copy_(u8[1::2])
-            lo, ln = lo_spans[k]
-            rest[lo:lo + ln].copy_(u8[0::2])
+            hi_buf[hi_offs[k]:hi_offs[k] + hi_lens[k]].copy_(u8[1::2])
             k += 1
-    kr = 0
+    plan = zstd_gpu.EncodePlan(hi_offs, hi_lens, dev)
+    plan.run(hi_buf)
+    sz = plan.block_sizes()  # waits for the encode
+    flen = [int(v) for v in np.add.reduceat(sz[:, 1], plan.first)] if plan.n_blocks else []
+    # the bodies assembled on the device (frame, then lo plane; or raw bytes), one copy to the host
+    sizes, k = [], 0
     for i, u8 in enumerate(flat):
-        if not plane[i]:
-            o, n = raw_spans[kr]
-            rest[o:o + n].copy_(u8)
-            kr += 1
-    frames = zstd_gpu.compress_many(hi_buf, hi_offs, hi_lens) if hi_offs else []
-    rest_h = _device.pinned_empty(max(lpos, 1))
-    rest_h.copy_(rest)
-    mv = memoryview(rest_h.numpy())
-    out, k, kr = [], 0, 0
-    for i in range(len(items)):
+        n = int(u8.numel())
+        sizes.append(flen[k] + n - n // 2 if plane[i] else n)
+        k += plane[i]
+    starts = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    total = int(starts[-1])
+    bodies = torch.empty(max(total, 1), dtype=torch.uint8, device=dev)
+    frame_dst = [int(starts[i]) for i in range(len(items)) if plane[i]]
+    if plan.n_blocks:
+        zstd_gpu.pack_blocks(plan, sz, frame_dst, bodies)
+    k = 0
+    for i, u8 in enumerate(flat):
+        n, o = int(u8.numel()), int(starts[i])
         if plane[i]:
-            lo, ln = lo_spans[k]
-            hz = frames[k]
-            out.append(({"hi_z": len(hz), "lo": ln}, hz + bytes(mv[lo:lo + ln])))
+            bodies[o + flen[k]:o + flen[k] + n - n // 2].copy_(u8[0::2])
             k += 1
         else:
-            o, n = raw_spans[kr]
+            bodies[o:o + n].copy_(u8)
+    host = _device.pinned_empty(max(total, 1))
+    host.copy_(bodies)
+    mv = memoryview(host.numpy())
+    out, k = [], 0
+    for i, u8 in enumerate(flat):
+        n, o = int(u8.numel()), int(starts[i])
+        if plane[i]:
+            out.append(({"hi_z": flen[k], "lo": n - n // 2}, bytes(mv[o:o + sizes[i]])))
+            k += 1
+        else:
             out.append(({"raw": n}, bytes(mv[o:o + n])))
-            kr += 1
     return out
 
 

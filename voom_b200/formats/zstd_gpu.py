@@ -262,6 +262,28 @@ class EncodePlan:
         return sz
 
 
+def pack_blocks(plan: EncodePlan, sz: np.ndarray, frame_dst, out: torch.Tensor,
+                stream: torch.cuda.Stream | None = None) -> np.ndarray:
+    """Packs every frame's encoded blocks (after plan.run; `sz` =
+    plan.block_sizes()) into the device buffer `out`, frame i starting at byte
+    frame_dst[i].  Returns the frames' lengths."""
+    n = plan.n_blocks
+    flen = np.add.reduceat(sz[:, 1], plan.first) if n else np.zeros(0, np.int64)
+    if n == 0:
+        return flen
+    fr = np.repeat(np.arange(len(plan.first)), plan.nb)
+    cs = np.cumsum(sz[:, 1]) - sz[:, 1]
+    dst = (np.asarray(frame_dst, np.int64)[fr] + cs - cs[plan.first[fr]]).astype(np.uint64)
+    rel = sz.copy()
+    rel[:, 0] -= np.arange(n, dtype=np.int64) * plan.slot
+    dev = out.device
+    d_sizes = _device.tensor_from_numpy(rel.astype(np.uint32), dev)
+    d_dst = _device.tensor_from_numpy(dst, dev)
+    check(load().voom_zstd_encode_pack(plan.slots.data_ptr(), d_sizes.data_ptr(), d_dst.data_ptr(), n,
+                                       out.data_ptr(), _device.stream_ptr(dev, stream)), "voom_zstd_encode_pack")
+    return flen
+
+
 def compress_device(d_src: torch.Tensor, offsets, lengths, *, stream: torch.cuda.Stream | None = None
                     ) -> tuple[torch.Tensor, np.ndarray, list[tuple[int, int]]]:
     """Compress many byte ranges of one device buffer, each into its own zstd
