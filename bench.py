@@ -789,8 +789,8 @@ class C4Step:
         self.y_host = torch.empty_like(self.x_host).pin_memory()
         self.units_per_step = T * c4.L
         self.algo_bytes = None
-        # router logits, top-k, plan, owners, 2x gate/up, act, 2x down, token-major rows, combine
-        self.launches_per_step = 11 * c4.L
+        # router logits, top-k, plan, 2x gate/up, act, 2x down, combine (+ owners and token-major rows with N > 1)
+        self.launches_per_step = (11 if c4.world > 1 else 9) * c4.L
         self.nccl_ms = 0.0
 
     def _run(self, x, timing: bool = False):

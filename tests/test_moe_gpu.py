@@ -335,7 +335,10 @@ def test_family_expert_parallel_split_is_exact(built_lib, family, T):
         ranks[r].combine(x, y[r * ts * rpt:(r + 1) * ts * rpt], part, r * ts, ts)
         got = part[:max(0, min(ts, T - r * ts))]
         assert torch.equal(got, want[r * ts:r * ts + got.shape[0]])
-    for lay in ranks:
+    one = moe.ExpertParallelMoeLayer(store, wr.cuda(), nw.cuda(), top_k=4, holders=np.ones(E + 1, np.uint32),
+                                     rank=0, world=1, **extra)
+    assert torch.equal(one(x), want)  # one rank: the fused single-GPU layer
+    for lay in ranks + [one]:
         lay.check_status()
 
 

@@ -28,8 +28,9 @@
 // Tiles may be any multiple of 2 * every bytes; a block of rows may span two
 // tiles (their decode tables both sit in shared memory).  The tensor-core
 // kernel needs tiles of at least 128 rows.  The segment length must follow
-// the rule of every_rule() (the largest power of two <= 512 dividing cols),
-// which fixes the row blocks on the host.
+// the rule of every_rule() (the largest power of two dividing cols, up to 256,
+// or 512 for projections of 4M weights or more), which fixes the row blocks on
+// the host.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -46,6 +47,13 @@ using namespace voom::rans;
 #ifndef VOOM_EVERY_MAX
 #define VOOM_EVERY_MAX 256
 #endif
+// projections of at least this many weights take segments of up to 2 x
+// VOOM_EVERY_MAX symbols: they have work items enough to fill the GPU, and
+// longer segments halve the per-segment setup; smaller projections keep the
+// shorter chains, which is where their decode's parallelism comes from
+#ifndef VOOM_EVERY_LARGE
+#define VOOM_EVERY_LARGE (4u << 20)
+#endif
 
 constexpr int kPairs = kThreads / 2;   // lane pairs of a CTA: one segment each
 constexpr uint32_t kStatusPage = 1u;      // a segment missed its checkpoint (damaged page)
@@ -54,15 +62,15 @@ constexpr uint32_t kStatusGeometry = 4u;  // page geometry the kernels do not ta
 constexpr uint32_t kStatusTimeout = 8u;   // a tensor-core completion wait ran out
 constexpr uint32_t kStatusNoHolder = 16u;  // expert parallelism: a routed expert no rank holds
 
-__host__ __device__ inline uint32_t every_rule(uint32_t cols) {
-  uint32_t e = VOOM_EVERY_MAX;
+__host__ __device__ inline uint32_t every_rule(uint32_t rows, uint32_t cols) {
+  uint32_t e = uint64_t(rows) * cols >= VOOM_EVERY_LARGE ? 2u * VOOM_EVERY_MAX : VOOM_EVERY_MAX;
   while (e > 64 && cols % e) e >>= 1;
   return cols % e ? 0u : e;
 }
 
 // Rows per moe_proj_cc block: as many whole rows as 128 segments hold.
-__host__ __device__ inline uint32_t cc_rows(uint32_t cols) {
-  const uint32_t e = every_rule(cols), spr = e ? cols / e : 1u;
+__host__ __device__ inline uint32_t cc_rows(uint32_t rows, uint32_t cols) {
+  const uint32_t e = every_rule(rows, cols), spr = e ? cols / e : 1u;
   return spr >= uint32_t(kPairs) ? 1u : uint32_t(kPairs) / spr;
 }
 
@@ -151,7 +159,7 @@ struct SeamCell {
 };
 
 __host__ __device__ inline uint32_t cc_chunks_per_tile(uint32_t rows, uint32_t cols, uint32_t n_tiles) {
-  const uint32_t rb = cc_rows(cols);
+  const uint32_t rb = cc_rows(rows, cols);
   if (n_tiles <= 1) return (rows + rb - 1) / rb;
   const uint32_t rows_touch = (rows + n_tiles - 2) / (n_tiles - 1) + 2;  // rows meeting one tile, at most
   return (rows_touch + rb - 1) / rb;
@@ -191,9 +199,9 @@ __device__ __forceinline__ void cc_item(CcShared& sh, const voom_expert_pages* _
   const voom_expert_proj& P = pick_proj(pages[R->expert[u]], which, nbpp, bx, &second, &slot_blk);
   if (P.n_tiles == 0) return;  // this expert's pages live on another GPU
   const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1;
-  const uint32_t every = P.every, spr = P.cols / every, rb = cc_rows(P.cols);
+  const uint32_t every = P.every, spr = P.cols / every, rb = cc_rows(P.rows, P.cols);
   const uint32_t spt = P.tiles[0].raw_len / (2u * every);
-  if (P.n_tiles > tiles_hint || P.n_tiles > kSeams + 1 || every != every_rule(P.cols) || spt < spr) {
+  if (P.n_tiles > tiles_hint || P.n_tiles > kSeams + 1 || every != every_rule(P.rows, P.cols) || spt < spr) {
     if (tid == 0 && slot_blk == 0) atomicOr(status, kStatusGeometry);
     return;
   }
@@ -506,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 2) moe_proj_mma(const voom_expert_pa
   const uint32_t spt = P.tiles[0].raw_len / (2u * every);
   const uint32_t t0 = spt ? (r0 * spr) / spt : 0u, t1 = spt ? (r1 * spr - 1u) / spt : 0u;
   const uint32_t tid = threadIdx.x, lane = tid & 1u, p = tid >> 1, warp = tid >> 5;
-  if (N > ncap || spt == 0 || t1 - t0 > 1u || every != every_rule(K) || (every & 15u)) {
+  if (N > ncap || spt == 0 || t1 - t0 > 1u || every != every_rule(P.rows, K) || (every & 15u)) {
     if (tid == 0) atomicOr(status, kStatusGeometry);
     return;
   }

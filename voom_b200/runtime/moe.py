@@ -64,12 +64,18 @@ def raise_on_status(status: torch.Tensor, what: str) -> None:
         raise ValueError(f"{what}: " + "; ".join(parts or [f"status 0x{v:x}"]))
 
 
-def every_for(cols: int, longest: int = 256) -> int:
-    """Checkpoint interval for rows of `cols` elements: the longest power of
-    two <= `longest` (and >= 64) dividing the row, so a lane pair of the
-    fused kernels decodes whole row segments.  The fused kernels size their
+EVERY_LARGE = 4 << 20  # projections of this many weights or more take 512-symbol segments
+
+
+def every_for(rows: int, cols: int, longest: int | None = None) -> int:
+    """Checkpoint interval of a rows x cols projection: the longest power of
+    two <= `longest` (and >= 64) dividing the row, so a lane pair of the fused
+    kernels decodes whole row segments; `longest` is 512 for projections of
+    EVERY_LARGE weights or more (they have work items enough, and longer
+    segments halve the per-segment setup), else 256 (shorter chains are where a
+    small projection's parallelism comes from).  The fused kernels size their
     row blocks from this rule (every_rule in csrc/moe_proj.cuh)."""
-    e = longest
+    e = longest if longest is not None else (512 if rows * cols >= EVERY_LARGE else 256)
     while e > 64 and cols % e:
         e //= 2
     if cols % e:
@@ -96,7 +102,7 @@ class ProjPage:
                  tile_bytes: int | None = None, stream: torch.cuda.Stream | None = None):
         rows, cols = w_bits.shape
         self.rows, self.cols = int(rows), int(cols)
-        every = every or every_for(self.cols)
+        every = every or every_for(self.rows, self.cols)
         if frame is None:
             frame, _ = bf16_rans.encode(np.ascontiguousarray(w_bits).view(np.uint8),
                                         tile_bytes=tile_bytes or tile_bytes_for(cols))
@@ -120,7 +126,7 @@ class ExpertStore:
     kernels skip it).  `alias` maps an expert id to another expert whose pages it
     shares (tests that route many experts over a few page sets).  Every
     projection is one VRN1 frame with tiles of `tile_bytes` (default
-    tile_bytes_for(cols)) and a checkpoint every every_for(cols) symbols.  A
+    tile_bytes_for(cols)) and a checkpoint every every_for(rows, cols) symbols.  A
     weight may also be a callable returning the bit array (generated when its
     page is built); `threads` > 1 builds pages concurrently."""
 
@@ -505,6 +511,18 @@ class ExpertParallelMoeLayer:
         x = x.contiguous()
         T, H = x.shape
         out = torch.empty_like(x) if out is None else out
+        if self.world == 1:  # one rank: the fused single-GPU layer (no owners, no exchange)
+            s = self.buffers(T)[0]
+            st = self.store
+            check(load().voom_moe_layer_v(ctypes.byref(self.variant), st.table.data_ptr(), self.n_experts,
+                                          self.router_w.data_ptr(),
+                                          None if self.norm_w is None else self.norm_w.data_ptr(), self.eps,
+                                          x.data_ptr(), out.data_ptr(), T, H, st.I, self.top_k, st.gate_tiles,
+                                          st.down_tiles, int(residual), s.data_ptr(), s.numel(),
+                                          self.status.data_ptr(), _device.stream_ptr(st.device, None)),
+                  "voom_moe_layer_v")
+            self.last_collective_bytes = 0
+            return out
         y_tm = self.experts(x)
         _, _, shard, part, full = self.buffers(T)
         ts = self.t_pad(T) // self.world
