@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 #include <vector>
@@ -1117,13 +1118,19 @@ __global__ void __launch_bounds__(32 * kLitWarps) zstd_block_literals(const uint
 }
 
 // K1: the sequences section of every block of the segment's block list, one
-// warp per block (one-warp CTAs spread over the SMs' schedulers two to a
-// scheduler), and every block's runtime record.
+// warp per block, and every block's runtime record.  One-warp CTAs take the
+// SMs' warp slots in launch order, so the first `wave` CTAs (4 per SM) get a
+// scheduler each and the rest pair up with them; CTA c < wave walks the c-th
+// longest block and CTA wave + i the i-th shortest, so a long walk shares its
+// scheduler with a short one and then runs alone (a walk sharing its scheduler
+// takes about 120 cycles per sequence, alone about 90).
 __global__ void __launch_bounds__(32) zstd_block_decode(const uint8_t* __restrict__ src, const uint8_t* img,
-                                                        uint8_t* scratch, uint32_t bl0) {
+                                                        uint8_t* scratch, uint32_t bl0, uint32_t n_bl,
+                                                        uint32_t wave) {
   __shared__ K1Walk sh;
   const View v = make_view(img, scratch);
-  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
+  const uint32_t c = blockIdx.x, pos = c < wave ? c : n_bl - 1u - (c - wave);
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_k1list)[bl0 + pos];
   const ZBlock b = v.blocks[bi];
   ZBlockRt* rt = v.rt + bi;
   uint32_t st = 0;
@@ -1961,6 +1968,20 @@ void tmark(cudaStream_t s, uint32_t id) {
   if (g_ntev > 0) g_tid[g_ntev - 1] = id;
   cudaEventRecord(g_tev[g_ntev++], s);
 }
+// First-wave size of zstd_block_decode: 4 one-warp CTAs per SM of the current
+// device (one per scheduler), at most the block count.
+uint32_t k1_wave(uint32_t n_bl) {
+  static int sms[64] = {0};
+  int dev = 0;
+  int n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64) {
+    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms[dev] = 0;
+    if (sms[dev] > 0) n = sms[dev];
+  }
+  return std::min<uint32_t>(n_bl, 4u * uint32_t(n));
+}
+
 // The literal decode (K0) runs on a side stream beside the sequence walk
 // (K1): the walks are one warp per block and bound by their serial chains, so
 // K0's CTAs use the SMs' spare issue slots instead of adding their time.  One
@@ -2055,13 +2076,13 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
         if (ss) {  // K1 on the caller's stream (dispatched first), K0 beside it
           if (cudaEventRecord(ss->fork, s) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
             return VOOM_E_CUDA;
-          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0);
+          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0, g.n_bl, k1_wave(g.n_bl));
           zstd_block_literals<<<g.n_bl, 32 * kLitWarps, 0, ss->s>>>(d_src, img, scr, d_out, d_status, g.bl0);
           if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(s, ss->join, 0) != cudaSuccess)
             return VOOM_E_CUDA;
         } else {
           zstd_block_literals<<<g.n_bl, 32 * kLitWarps, 0, s>>>(d_src, img, scr, d_out, d_status, g.bl0);
-          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0);
+          zstd_block_decode<<<g.n_bl, 32, 0, s>>>(d_src, img, scr, g.bl0, g.n_bl, k1_wave(g.n_bl));
         }
       }
       tmark(s, VOOM_ZSTD_K_BLOCK_DECODE);  // literals and sequences together

@@ -711,6 +711,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   h.off_tiles = o; o = align_up(o + sizeof(ZOutTile) * uint64_t(run.t), 256);
   h.off_dlit = o; o = align_up(o + sizeof(uint32_t) * uint64_t(run.dl), 256);
   h.off_blist = o; o = align_up(o + sizeof(uint32_t) * uint64_t(run.bl), 256);
+  h.off_k1list = o; o = align_up(o + sizeof(uint32_t) * uint64_t(run.bl), 256);
   P->image_bytes = o;
   h.lit_bytes = run.lit;
   h.n_seq = run.seq;
@@ -735,7 +736,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   }
   uint8_t* img = P->image.get();
   // the alignment gaps between the arrays are zero
-  const uint64_t ends[9][2] = {{sizeof(ZPlanHeader), h.off_jobs},
+  const uint64_t ends[10][2] = {{sizeof(ZPlanHeader), h.off_jobs},
                                {h.off_jobs + sizeof(ZJob) * uint64_t(n_jobs), h.off_frames},
                                {h.off_frames + sizeof(ZFrame) * uint64_t(run.f), h.off_blocks},
                                {h.off_blocks + sizeof(ZBlock) * uint64_t(run.b), h.off_huf},
@@ -743,7 +744,8 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
                                {h.off_fse + sizeof(ZFse) * uint64_t(run.s), h.off_tiles},
                                {h.off_tiles + sizeof(ZOutTile) * uint64_t(run.t), h.off_dlit},
                                {h.off_dlit + sizeof(uint32_t) * uint64_t(run.dl), h.off_blist},
-                               {h.off_blist + sizeof(uint32_t) * uint64_t(run.bl), P->image_bytes}};
+                               {h.off_blist + sizeof(uint32_t) * uint64_t(run.bl), h.off_k1list},
+                               {h.off_k1list + sizeof(uint32_t) * uint64_t(run.bl), P->image_bytes}};
   for (const auto& g : ends) memset(img + g[0], 0, g[1] - g[0]);
   memcpy(img, &h, sizeof h);
   ZJob* J = reinterpret_cast<ZJob*>(img + h.off_jobs);
@@ -829,6 +831,15 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     }
     J[j] = zj;
   });
+  // each segment's block list ordered by sequence count, most first (stable)
+  uint32_t* K1 = reinterpret_cast<uint32_t*>(img + h.off_k1list);
+  for (const ZSegment& g : P->segs) {
+    std::copy(BL + g.bl0, BL + g.bl0 + g.n_bl, K1 + g.bl0);
+    std::stable_sort(K1 + g.bl0, K1 + g.bl0 + g.n_bl, [&](uint32_t a, uint32_t b) {
+      const uint32_t na = B[a].type == 2 ? B[a].nseq : 0u, nb = B[b].type == 2 ? B[b].nseq : 0u;
+      return na > nb;
+    });
+  }
   return P;
 }
 

@@ -102,6 +102,9 @@ struct ZPlanHeader {
   // scan and block execute kernels run on this list, segment by segment
   uint32_t n_blist, pad_blist;
   uint64_t off_blist;
+  // the same block list, each segment's range ordered by sequence count
+  // (most first): the order zstd_block_decode pairs its walkers in
+  uint64_t off_k1list;
   uint64_t lit_bytes, n_seq, zbytes;
   // scratch layout (byte offsets into d_scratch)
   uint64_t s_res, s_lit, s_seq, s_blk, s_ctr, s_list, s_total;
