@@ -151,3 +151,40 @@ def test_planner_direct_decision_edges(built_lib):
             plan = Z.ZstdPlan(np.frombuffer(frame + bytes(n + extra), np.uint8), job)
             assert plan.info.n_direct_jobs == int(want), (name, extra, flags)
             assert plan.plan_status[0] == 0
+
+
+def test_planner_orders_blocks_for_the_sequence_walk(built_lib):
+    """The plan image's walk order (the block list ordered by sequence count,
+    most first, that zstd_block_decode pairs its walkers from) is a
+    permutation of the block list, sorted, over frames of many blocks."""
+    from voom_b200.formats import zstd_gpu as Z
+
+    rng = np.random.default_rng(9)
+    # small alphabets: many short matches, their count varying with the alphabet
+    datas = [rng.integers(0, a, 300_000, dtype=np.uint8).tobytes() for a in (4, 12, 40)]
+    datas.append(bytes(range(256)) * 700)  # very repetitive: few, long sequences
+    from oracle import vpack as ov
+
+    frames = [ov.zstd_compress(d, 1) for d in datas]
+    jobs = np.zeros(len(frames), dtype=Z.JOB_DTYPE)
+    off = dst = 0
+    for i, (fr, d) in enumerate(zip(frames, datas)):
+        jobs[i] = (off, len(fr), dst, len(d), 0, 0, 0)
+        off += len(fr)
+        dst += len(d)
+    plan = Z.ZstdPlan(np.frombuffer(b"".join(frames), np.uint8), jobs)
+    img = plan.image
+    hdr = img[:128]
+    n_blocks = int(hdr[8:12].view(np.uint32)[0])
+    off_blocks = int(hdr[40:48].view(np.uint64)[0])
+    n_blist = int(hdr[88:92].view(np.uint32)[0])
+    off_blist, off_k1 = (int(x) for x in hdr[96:112].view(np.uint64))
+    assert n_blist >= 4  # the blocks of jobs with sequences (direct jobs are not listed)
+    blist = img[off_blist:off_blist + 4 * n_blist].view(np.uint32)
+    k1 = img[off_k1:off_k1 + 4 * n_blist].view(np.uint32)
+    rec = img[off_blocks:off_blocks + 112 * n_blocks].reshape(n_blocks, 112)
+    btype = rec[:, 40:44].copy().view(np.uint32).reshape(-1)
+    nseq = np.where(btype == 2, rec[:, 88:92].copy().view(np.uint32).reshape(-1), 0)
+    assert sorted(k1.tolist()) == sorted(blist.tolist())  # one segment here
+    walk = nseq[k1]
+    assert (np.diff(walk.astype(np.int64)) <= 0).all() and walk[0] > walk[-1]
