@@ -371,7 +371,7 @@ class C2Vpack:
         self.algo_bytes = self.archive.size + self.local_raw  # this rank's decode
         self.gather_bytes = cap * (world - 1) if world > 1 else 0
         self.n_blocks = int(self.plan.info.n_blocks)
-        self.launches_per_step = 12  # K1 K1b K2 K3 6xK4 K5 K6 (+ the NCCL all-gather with N > 1)
+        self.launches_per_step = 13  # K0 K1 K1b K2 K3 K5 5xK4 patch K6 (+ the NCCL all-gather with N > 1)
         self.scaling = "strong" if world > 1 else "weak"
         self.replicated_units = True  # value = the one archive's bytes, not x N
 
@@ -1159,7 +1159,7 @@ class C6KvPaged:
         self.algo_bytes = self.comp.size + self.raw_bytes
         self.n_blocks = int(self.plan.info.n_blocks)
         self.n_seq = int(self.plan.info.n_seq)
-        self.launches_per_step = 12
+        self.launches_per_step = 14  # direct literals, K0 K1 K1b K2 K3 K5 5xK4 patch K6
 
     def step_device(self, stream_ptr: int):
         self.batch.run(self.src, self.out, self.torch.cuda.current_stream(self.dev))

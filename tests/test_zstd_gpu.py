@@ -276,3 +276,18 @@ def test_frame_longer_than_its_job_leaves_the_next_job_intact(Z, first_len):
         got = out.cpu().numpy()
         assert got[d1:d1 + len(ok_raw)].tobytes() == ok_raw
         assert (got[d1 + len(ok_raw):] == 0xA5).all()  # nothing written past the last job
+
+
+def test_long_chains_take_the_worklist_overflow_path(built_lib):
+    """8 MiB copied from two bytes back: after the output pass almost every
+    byte is still a link (its chain is far longer than 16 hops), many more
+    than worklist 0 holds, so the resolve passes rescan the tiles (pointer
+    jumping with path compression) and the patch pass rewrites them.  The
+    output is exact and the job's status clean."""
+    from voom_b200.formats import zstd_gpu
+    from voom_b200.formats import zstd_host as zh
+
+    for data in (b"ab" * (4 << 20), b"xyz" * (3 << 20)):
+        fr = zh.compress(data, 1)
+        got = zstd_gpu.decompress_device(fr, len(data)).cpu().numpy().tobytes()
+        assert got == data

@@ -1,12 +1,13 @@
 // GPU Zstandard (RFC 8878) decoder for vpack hi planes and kv_paged pages.
 //
 // Pipeline over a planned batch of jobs (host plan: zstd_plan.cpp):
-//   K1 block decode  - one CTA per block.  Four warps build the Huffman table
-//                      and decode the literal streams (one warp per stream,
-//                      32 lanes on spans that settle on codeword boundaries);
-//                      the fifth warp builds the LL/OF/ML FSE tables and walks
-//                      the sequence bitstream, storing each sequence's literal
-//                      length, match length and offset value.
+//   K0 block literals - one CTA per block, a warp per Huffman stream: the
+//                      literals section staged in shared memory, 32 lanes per
+//                      stream on spans that settle on codeword boundaries (on a
+//                      side stream, beside K1).
+//   K1 block decode  - one warp per block builds the LL/OF/ML FSE tables and
+//                      walks the sequence bitstream, storing each sequence's
+//                      literal length, match length and offset value.
 //   K1b seq scan     - one CTA per block: repeat-offset rules on symbolic slots
 //                      (each of the 3 repeat slots as "block-start slot minus
 //                      d" or a constant) and output / literal positions by a
@@ -1775,8 +1776,11 @@ __global__ void __launch_bounds__(256) zstd_output(const uint8_t* __restrict__ s
   if (threadIdx.x == 0) v.dirty[ti] = s_unres ? (kPatch | s_unres) : 0u;
 }
 
+// One resolve pass.  Grid-stride over the worklist, or (worklist 0
+// overflowed) over the segment's tiles: a few CTAs per SM, so a pass over an
+// empty list costs one small launch.
 __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t* scratch, int pass,
-                                                    uint32_t tile0) {
+                                                    uint32_t tile0, uint32_t n_tiles) {
   __shared__ uint32_t s_unres;
   const View v = make_view(img, scratch);
   uint32_t* ctr = v.dirty + v.h->n_tiles;
@@ -1795,24 +1799,26 @@ __global__ void __launch_bounds__(256) zstd_resolve(const uint8_t* img, uint8_t*
     }
     return;
   }
-  const uint32_t ti = tile0 + blockIdx.x;
-  const ZOutTile t = v.tiles[ti];
-  const ZJob job = v.jobs[t.job];
-  if (job.bad || !(v.dirty[ti] & ~kPatch)) return;
-  if (threadIdx.x == 0) s_unres = 0;
-  __syncthreads();
-  uint32_t unres = 0;
-  for (uint64_t k = t.begin + threadIdx.x; k < t.begin + t.len; k += blockDim.x) {
-    const uint64_t z = job.zoff + k;
-    uint32_t u = v.res[z];
-    if (u & kResolved) continue;
-    u = chase(v, u, zmax);
-    v.res[z] = u;
-    unres += !(u & kResolved);
+  for (uint32_t ti = tile0 + blockIdx.x; ti < tile0 + n_tiles; ti += gridDim.x) {
+    const ZOutTile t = v.tiles[ti];
+    const ZJob job = v.jobs[t.job];
+    if (job.bad || !(v.dirty[ti] & ~kPatch)) continue;  // the same for every thread
+    if (threadIdx.x == 0) s_unres = 0;
+    __syncthreads();
+    uint32_t unres = 0;
+    for (uint64_t k = t.begin + threadIdx.x; k < t.begin + t.len; k += blockDim.x) {
+      const uint64_t z = job.zoff + k;
+      uint32_t u = v.res[z];
+      if (u & kResolved) continue;
+      u = chase(v, u, zmax);
+      v.res[z] = u;
+      unres += !(u & kResolved);
+    }
+    if (unres) atomicAdd(&s_unres, unres);
+    __syncthreads();
+    if (threadIdx.x == 0) v.dirty[ti] = kPatch | s_unres;
+    __syncthreads();  // s_unres is reused for the next tile
   }
-  if (unres) atomicAdd(&s_unres, unres);
-  __syncthreads();
-  if (threadIdx.x == 0) v.dirty[ti] = kPatch | s_unres;
 }
 
 __global__ void __launch_bounds__(256) zstd_patch(const uint8_t* __restrict__ src, const uint8_t* img,
@@ -2097,7 +2103,8 @@ VOOM_API int voom_zstd_decode(const uint8_t* d_src, const void* d_plan, const vo
     if (g.n_tiles) {
       zstd_output<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, g.tile0);
       tmark(s, VOOM_ZSTD_K_OUTPUT);
-      for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<g.n_tiles, 256, 0, s>>>(img, scr, p, g.tile0);
+      const uint32_t rgrid = std::min<uint32_t>(g.n_tiles, k1_wave(g.n_tiles));  // <= 4 CTAs per SM
+      for (int p = 1; p < kResolvePasses; p++) zstd_resolve<<<rgrid, 256, 0, s>>>(img, scr, p, g.tile0, g.n_tiles);
       tmark(s, VOOM_ZSTD_K_RESOLVE);
       zstd_patch<<<g.n_tiles, 256, 0, s>>>(d_src, img, scr, d_out, d_status, g.tile0);
       tmark(s, VOOM_ZSTD_K_PATCH);
