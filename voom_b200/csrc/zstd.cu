@@ -1151,15 +1151,15 @@ __global__ void __launch_bounds__(32) zstd_block_decode(const uint8_t* __restric
 
 // Per compressed block with sequences, after zstd_block_decode: the repeat-
 // offset rules and output / literal positions of every sequence (RFC 8878
-// 3.1.2.5).  Rounds of 256 x 4 consecutive records: each thread applies the
+// 3.1.2.5).  Rounds of 128 x 4 consecutive records: each thread applies the
 // rules of its 4 records to symbolic slots (slot = block-start slot minus d,
 // or a constant), giving its transform and length sums; warps scan the
-// transforms, the 8 warp totals are scanned by warp 0, and each thread,
+// transforms, the 4 warp totals are scanned by warp 0, and each thread,
 // starting from its carry-in (all earlier records composed), replays its 4
 // records on those slots to get each one's offset and positions.  Also the
 // block's output size, its repeat transform for the job scan, and the
 // literal-count check.
-constexpr int kSeqScanThreads = 256;
+constexpr int kSeqScanThreads = 128;  // 8 CTAs per SM at 61 registers
 constexpr int kSeqPerThread = 4;
 
 __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* img, uint8_t* scratch,
@@ -1171,7 +1171,9 @@ __global__ void __launch_bounds__(kSeqScanThreads) zstd_seq_scan(const uint8_t* 
   __shared__ uint32_t s_ck[kW + 1][3], s_cd[kW + 1][3];
   __shared__ uint32_t s_cl[kW + 1], s_cm[kW + 1];
   const View v = make_view(img, scratch);
-  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_blist)[bl0 + blockIdx.x];
+  // blocks in walk order (most sequences first): the CTAs of the longest
+  // blocks start in the first wave
+  const uint32_t bi = reinterpret_cast<const uint32_t*>(img + v.h->off_k1list)[bl0 + blockIdx.x];
   const ZBlock b = v.blocks[bi];
   if (b.type != 2 || b.nseq == 0) return;
   ZBlockRt* rt = v.rt + bi;
