@@ -225,7 +225,8 @@ typedef struct voom_zstd_plan_info {
  * headers, decodes Huffman tree descriptions and FSE table descriptions; the
  * entropy-coded payloads are left to the GPU.  Returns an opaque handle (NULL
  * on bad arguments).  Jobs with a structural error are marked in the plan and
- * skipped by the decoder.  `threads` <= 0 uses all cores.
+ * skipped by the decoder.  `threads` <= 0 uses up to 8 host threads, fewer
+ * for small batches (each thread takes at least 64 blocks or 32 jobs).
  * Replaces: the frame/block header walk inside libzstd ZSTD_decompress as
  * reached from formats/packed2.py:178-191 and runtime/kv_paged.py:98-113. */
 void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, const voom_zstd_job* jobs,
@@ -283,6 +284,16 @@ int voom_zstd_encode(const uint8_t* d_src, const voom_zenc_block* d_blocks, uint
  * reference (it writes frames from host memory). */
 int voom_zstd_encode_pack(const uint8_t* d_slots, const uint32_t* d_sizes, const uint64_t* d_dst, uint32_t n_blocks,
                           uint8_t* d_out, void* stream);
+
+/* Copies n bytes of pinned host memory (allocated or registered with the CUDA
+ * runtime, so mapped into the device's address space) to device memory with a
+ * kernel on `stream`: the SMs read the host memory directly, so the copy does
+ * not wait on a copy engine behind transfers enqueued before it (used for
+ * plan images while body uploads are in flight).  [h_src, h_src + n) must lie
+ * in ONE such allocation, as for cudaMemcpyAsync.  VOOM_E_INVALID_ARG when it
+ * is not mapped pinned memory (nothing is launched; use cudaMemcpyAsync).  No
+ * counterpart in the reference. */
+int voom_copy_from_host(void* d_dst, const void* h_src, uint64_t n, void* stream);
 
 /* Per-kernel timing of voom_zstd_decode (diagnostics; no counterpart in the
  * reference).  voom_zstd_set_timing(1) makes every later voom_zstd_decode

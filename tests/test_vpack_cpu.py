@@ -185,3 +185,27 @@ def test_verify_generation_extents_and_hashes(tmp_path):
     end = index[last]["off"] + index[last]["len"]
     assert rep["errors"] == [f"archive size {end - 5} != indexed extent end {end}",
                              f"hash mismatch at {name}", f"short read at {last}"]
+
+
+def test_body_groups_for_the_pipelined_upload():
+    """Groups of consecutive bodies with about equal compressed bytes, every
+    group non-empty; one group for small batches (under GROUP_BYTES per group)
+    and for bodies out of order or overlapping."""
+    from voom_b200.formats import packed
+
+    lens = [5, 1, 1, 1, 8, 2, 2, 9, 3, 1]
+    offs = np.cumsum([0] + lens[:-1]).tolist()
+    for g in range(1, len(lens) + 1):
+        parts = packed.body_groups(offs, lens, g)
+        assert len(parts) == g
+        assert [i for p in parts for i in p] == list(range(len(lens)))
+        assert all(parts)
+    # about equal bytes: no group of the 3-way cut holds more than half
+    assert max(sum(lens[i] for i in p) for p in packed.body_groups(offs, lens, 3)) <= 17
+    assert packed.body_groups(offs, lens, 99) == [[i] for i in range(len(lens))]
+    assert packed.body_groups(offs, lens) == [list(range(len(lens)))]  # 33 bytes: one group
+    big = [packed.GROUP_BYTES] * 10
+    assert len(packed.body_groups(np.cumsum([0] + big[:-1]).tolist(), big)) == packed.MAX_GROUPS
+    assert packed.body_groups([10, 0], [10, 10], 2) == [[0, 1]]  # out of order
+    assert packed.body_groups([0, 5], [10, 10], 2) == [[0, 1]]  # overlapping
+

@@ -131,6 +131,77 @@ def test_smollm2_scaled_archive(built_lib):
         assert np.array_equal(got[d:d + n], r)
 
 
+def test_grouped_upload_decode_matches_single_dma(built_lib):
+    """From a pinned buffer the bodies go up in groups on a copy stream, each
+    group's decode waiting for its own bytes only: the output equals the
+    single-DMA decode byte for byte (raw-stored bodies included), and a damaged
+    body in the last group raises the same error."""
+    from voom_b200 import synthetic
+    from voom_b200.formats import packed
+    from voom_b200.formats.zstd_gpu import ZstdError
+
+    cfg = dict(synthetic.SMOLLM2_135M, layers=2)
+    heads, bodies, raws = [], [], []
+    for i, (name, shape) in enumerate(synthetic.smollm2_tensors(cfg)):
+        bits = synthetic.bf16_normal(shape, 0.02, 70 + i)
+        h, b = packed.body_for("BF16", bits.view(np.uint8))
+        heads.append({"dtype": "BF16", "shape": list(shape), **h})
+        bodies.append(b)
+        raws.append(bits.view(np.uint8).reshape(-1))
+        if i == 3:  # a raw-stored (F32) body between the BF16 ones
+            f = np.random.default_rng(5).standard_normal(4099).astype(np.float32)
+            h, b = packed.body_for("F32", f.view(np.uint8))
+            heads.append({"dtype": "F32", "shape": [4099], **h})
+            bodies.append(b)
+            raws.append(f.view(np.uint8))
+    offs = np.cumsum([0] + [len(b) for b in bodies[:-1]]).tolist()
+    lens = [len(b) for b in bodies]
+    pinned = torch.empty(sum(lens), dtype=torch.uint8, pin_memory=True)
+    pinned.numpy()[:] = np.frombuffer(b"".join(bodies), np.uint8)
+    ref, spans = packed.decode_bodies(heads, pinned, offs, lens, groups=1)
+    for g in (2, 3, 5):
+        assert len(packed.body_groups(offs, lens, g)) == g
+        out, spans_g = packed.decode_bodies(heads, pinned, offs, lens, groups=g)
+        assert spans_g == spans
+        for d, n in spans:  # the alignment gaps between bodies are not written
+            assert torch.equal(out[d:d + n], ref[d:d + n])
+    got = ref.cpu().numpy()
+    for (d, n), r in zip(spans, raws):
+        assert np.array_equal(got[d:d + n], r)
+    last = len(bodies) - 1
+    pinned[offs[last]:offs[last] + 4] ^= 0xFF  # the last body's hi-plane frame magic
+    with pytest.raises(ZstdError) as one:
+        packed.decode_bodies(heads, pinned, offs, lens, groups=1)
+    with pytest.raises(ZstdError) as grouped:
+        packed.decode_bodies(heads, pinned, offs, lens, groups=3)
+    assert str(grouped.value) == str(one.value)
+
+
+def test_copy_from_host_reads_mapped_pinned_memory(built_lib):
+    """voom_copy_from_host: a pinned buffer (aligned and odd offsets and
+    lengths) lands byte for byte; pageable memory is refused with
+    VOOM_E_INVALID_ARG and nothing is launched."""
+    from voom_b200 import _device
+    from voom_b200._lib import load
+
+    lib = load()
+    rng = np.random.default_rng(11)
+    host = torch.empty(300_007, dtype=torch.uint8, pin_memory=True)
+    host.numpy()[:] = rng.integers(0, 256, host.numel(), dtype=np.uint8)
+    dev = torch.device("cuda", 0)
+    s = _device.stream_ptr(dev)
+    for off, n in ((0, 300_000), (3, 70_001), (16, 16), (5, 1)):
+        out = torch.zeros(n + 32, dtype=torch.uint8, device=dev)
+        assert lib.voom_copy_from_host(out.data_ptr() + 7 * (off & 1), host.data_ptr() + off, n, s) == 0
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()[7 * (off & 1):7 * (off & 1) + n]
+        assert np.array_equal(got, host.numpy()[off:off + n])
+    pageable = np.zeros(4096, np.uint8)
+    out = torch.zeros(4096, dtype=torch.uint8, device=dev)
+    assert lib.voom_copy_from_host(out.data_ptr(), pageable.ctypes.data, 4096, s) != 0
+    assert lib.voom_copy_from_host(out.data_ptr(), host.data_ptr(), 0, s) == 0
+
+
 def test_packed_weight_store_fetch(archive_dir, decoded):
     """WeightStore leg over the reference's archive: canonical -> stored name
     translation at the archive boundary, duplicates fetched once, every page

@@ -111,6 +111,7 @@ SIGNATURES: dict[str, tuple] = {
     "voom_zstd_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "voom_kvz_gather": (_i32, [_vp, _vp, _vp, _u32, _vp, _vp, _i32]),
     "voom_zstd_set_timing": (_i32, [_i32]),
+    "voom_copy_from_host": (_i32, [_vp, _vp, _u64, _vp]),
     "voom_zstd_encode_slot_bytes": (_u64, []),
     "voom_zstd_encode_block_bytes": (_u32, []),
     "voom_zstd_encode": (_i32, [_vp, _vp, _u32, _vp, _vp, _vp]),

@@ -2017,6 +2017,47 @@ SideStream* side_stream_locked() {
 }
 }  // namespace
 
+// n bytes from device-mapped pinned host memory into device memory, read by
+// the SMs: unlike cudaMemcpyAsync it does not queue on a copy engine behind
+// earlier transfers (a small plan image would otherwise wait for every body
+// upload enqueued before it).
+__global__ void __launch_bounds__(256) zstd_copy_mapped(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src,
+                                                        uint64_t n) {
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  const uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0) {
+    const uint64_t n16 = n / 16;
+    for (uint64_t i = t; i < n16; i += stride)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+    for (uint64_t i = n16 * 16 + t; i < n; i += stride) dst[i] = src[i];
+  } else {
+    for (uint64_t i = t; i < n; i += stride) dst[i] = src[i];
+  }
+}
+
+VOOM_API int voom_copy_from_host(void* d_dst, const void* h_src, uint64_t n, void* stream) {
+  if (!n) return VOOM_OK;
+  if (!d_dst || !h_src) return VOOM_E_INVALID_ARG;
+  // the whole range must lie in one pinned allocation mapped into this device
+  cudaPointerAttributes a{};
+  void* d_src = nullptr;
+  if (cudaPointerGetAttributes(&a, h_src) != cudaSuccess || a.type != cudaMemoryTypeHost ||
+      cudaHostGetDevicePointer(&d_src, const_cast<void*>(h_src), 0) != cudaSuccess || !d_src) {
+    cudaGetLastError();  // clear the lookup's error: the caller falls back to a plain copy
+    return VOOM_E_INVALID_ARG;
+  }
+  void* d_last = nullptr;
+  if (cudaHostGetDevicePointer(&d_last, static_cast<uint8_t*>(const_cast<void*>(h_src)) + (n - 1), 0) != cudaSuccess ||
+      static_cast<uint8_t*>(d_last) != static_cast<uint8_t*>(d_src) + (n - 1)) {
+    cudaGetLastError();
+    return VOOM_E_INVALID_ARG;
+  }
+  const uint64_t blocks = std::min<uint64_t>((n + 16 * 256 - 1) / (16 * 256), 148 * 2);
+  zstd_copy_mapped<<<uint32_t(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(d_dst), static_cast<const uint8_t*>(d_src), n);
+  return cudaGetLastError() == cudaSuccess ? VOOM_OK : VOOM_E_CUDA;
+}
+
 VOOM_API int voom_zstd_set_timing(int on) {
   if (on && !g_time_on) {
     int dev = -1;

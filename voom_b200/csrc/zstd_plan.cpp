@@ -352,10 +352,11 @@ bool plan_compressed(const uint8_t* base, uint64_t at, size_t n, ZBlock& b, Bloc
       memset(&f, 0, sizeof f);
       int al;
       size_t u;
+      // counts that read_ncount accepts fill the table exactly, so the spread
+      // always closes (its step is odd, hence coprime with the table size):
+      // the device builds the decode table from them
       const int ns = read_ncount(p + hsz, n - hsz, kMaxAl[k], kMaxSym[k], f.norm, &al, &u);
       if (ns < 0) return false;
-      FseCell tmp[512];
-      if (!fse_build(f.norm, ns, al, tmp)) return false;
       f.nsym = uint16_t(ns);
       f.al = uint8_t(al);
       T.fse_kind[k] = 1;
@@ -566,10 +567,14 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   Plan* P = new (std::nothrow) Plan();
   if (!P) return nullptr;
   std::vector<JobPlan> jp(n_jobs);
-  const int nt_all = threads > 0 ? threads : int(std::max(1u, std::thread::hardware_concurrency()));
-  // runs f(i) for i in [0, n) on up to nt_all threads (dynamic assignment)
-  auto parallel = [&](uint64_t n, auto&& f) {
-    const int nt = int(std::max<uint64_t>(1, std::min<uint64_t>(uint64_t(nt_all), n)));
+  // threads: up to 8 by default (starting a thread costs about as much as
+  // planning a few dozen blocks, and more threads measured slower)
+  const int nt_all =
+      threads > 0 ? threads : int(std::min(8u, std::max(1u, std::thread::hardware_concurrency())));
+  // runs f(i) for i in [0, n) on up to nt_all threads, at least `grain`
+  // items each (dynamic assignment)
+  auto parallel = [&](uint64_t n, uint64_t grain, auto&& f) {
+    const int nt = int(std::max<uint64_t>(1, std::min<uint64_t>(uint64_t(nt_all), n / grain)));
     std::atomic<uint64_t> next{0};
     auto run = [&]() {
       for (uint64_t i = next.fetch_add(1); i < n; i = next.fetch_add(1)) f(i);
@@ -580,7 +585,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     for (auto& t : pool) t.join();
   };
   // 1. frame / block walk per job
-  parallel(n_jobs, [&](uint64_t j) {
+  parallel(n_jobs, 32, [&](uint64_t j) {
     if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; return; }
     walk_job(h_src, jobs[j], jp[j]);
   });
@@ -592,23 +597,29 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   std::unique_ptr<uint8_t[]> okb(new uint8_t[std::max<uint64_t>(1, bstart[n_jobs])]);
   std::vector<uint8_t> direct(n_jobs, 0);
   std::vector<JobSpan> span(n_jobs);
-  parallel(n_jobs, [&](uint64_t j) {
+  // the blocks' sections in parallel over all blocks (one large job would
+  // otherwise hold a thread for all of its blocks)
+  std::vector<uint32_t> bjob(bstart[n_jobs]);
+  for (uint32_t j = 0; j < n_jobs; j++)
+    for (uint64_t g = bstart[j]; g < bstart[j + 1]; g++) bjob[g] = j;
+  parallel(bstart[n_jobs], 64, [&](uint64_t g) {
+    const uint32_t j = bjob[g];
+    ZBlock& b = jp[j].blocks[g - bstart[j]];
+    okb[g] = 1;
+    if (b.type != 2) return;
+    const uint64_t at = b.src;
+    const size_t bs = b.size;
+    b.src = 0;
+    b.size = 0;
+    okb[g] = plan_compressed(h_src, at, bs, b, tabs[g]) ? 1 : 0;
+  });
+  parallel(n_jobs, 32, [&](uint64_t j) {
     JobPlan& q = jp[j];
     JobSpan& c = span[j];
     memset(&c, 0, sizeof c);
     if (q.bad) return;
     BlockTables* T = tabs.get() + bstart[j];
     uint8_t* ok = okb.get() + bstart[j];
-    for (size_t i = 0; i < q.blocks.size(); i++) {
-      ZBlock& b = q.blocks[i];
-      ok[i] = 1;
-      if (b.type != 2) continue;
-      const uint64_t at = b.src;
-      const size_t bs = b.size;
-      b.src = 0;
-      b.size = 0;
-      ok[i] = plan_compressed(h_src, at, bs, b, T[i]) ? 1 : 0;
-    }
     resolve_job(q, T, ok);
     direct[j] = make_direct(q, jobs[j]) ? 1 : 0;
     if (q.bad) return;
@@ -766,7 +777,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     f.al = uint8_t(k == 1 ? 5 : 6);
     S[k] = f;
   }
-  parallel(n_jobs, [&](uint64_t jj) {
+  parallel(n_jobs, 32, [&](uint64_t jj) {
     const uint32_t j = uint32_t(jj);
     ZJob zj;
     memset(&zj, 0, sizeof zj);

@@ -236,56 +236,130 @@ def pack_model(model_dir: str | Path, out_dir: str | Path | None = None, level: 
     return out
 
 
-def body_job(head: dict, body_off: int, body_len: int, dst: int) -> tuple[np.ndarray | None, int]:
-    """GPU job for one vpack body held at body_off in a source buffer:
-    returns (job record or None for raw bodies, decoded byte count)."""
+def _job_row(head: dict, body_off: int, body_len: int, dst: int) -> tuple[tuple | None, int]:
+    """body_job's record as a plain tuple (JOB_DTYPE field order)."""
     if "raw" in head:
         return None, int(head["raw"])
     lo = int(head["lo"])
-    job = np.zeros(1, dtype=JOB_DTYPE)
     if head.get("streamed"):
-        job[0] = (body_off + lo, body_len - lo, dst, lo, body_off, INTERLEAVE, 0)
-    else:
-        hz = int(head["hi_z"])
-        job[0] = (body_off, hz, dst, lo, body_off + hz, INTERLEAVE, 0)
-    return job, 2 * lo
+        return (body_off + lo, body_len - lo, dst, lo, body_off, INTERLEAVE, 0), 2 * lo
+    hz = int(head["hi_z"])
+    return (body_off, hz, dst, lo, body_off + hz, INTERLEAVE, 0), 2 * lo
+
+
+def body_job(head: dict, body_off: int, body_len: int, dst: int) -> tuple[np.ndarray | None, int]:
+    """GPU job for one vpack body held at body_off in a source buffer:
+    returns (job record or None for raw bodies, decoded byte count)."""
+    row, n = _job_row(head, body_off, body_len, dst)
+    return (None if row is None else np.array([row], dtype=JOB_DTYPE)), n
+
+
+GROUP_BYTES = 64 << 20  # compressed bytes per pipelined group (at most MAX_GROUPS groups)
+MAX_GROUPS = 4
+_streams: dict = {}
+_planners = None  # host threads that build the groups' plans side by side
+
+
+def _plan_pool():
+    global _planners
+    if _planners is None:
+        import concurrent.futures as cf
+
+        _planners = cf.ThreadPoolExecutor(max_workers=MAX_GROUPS * 2, thread_name_prefix="voom-plan")
+    return _planners
+
+
+def _side_streams(dev: torch.device, n: int) -> list[torch.cuda.Stream]:
+    """n cached streams of the device (a copy stream and the group streams)."""
+    have = _streams.setdefault(dev.index, [])
+    while len(have) < n:
+        have.append(torch.cuda.Stream(dev))
+    return have[:n]
+
+
+def body_groups(offsets: list[int], lengths: list[int], groups: int | None = None) -> list[list[int]]:
+    """Consecutive bodies cut into groups of about equal compressed bytes, for
+    a decode that overlaps the upload of one group with the decode of the one
+    before.  `groups` None: one group per GROUP_BYTES, at most MAX_GROUPS.
+    One group when the bodies do not lie in ascending, non-overlapping order
+    (the groups' byte ranges must not overlap)."""
+    n = len(offsets)
+    total = sum(lengths)
+    g = groups if groups is not None else min(MAX_GROUPS, total // GROUP_BYTES)
+    g = max(1, min(int(g), n))
+    ordered = all(offsets[i] + lengths[i] <= offsets[i + 1] for i in range(n - 1))
+    if g == 1 or not ordered:
+        return [list(range(n))]
+    out, cur, acc = [], [], 0
+    for i, ln in enumerate(lengths):
+        cur.append(i)
+        acc += ln
+        # close the group once it holds its share, or when the bodies left
+        # are just enough for one per group still to open
+        after, left = g - len(out) - 1, n - i - 1
+        if after > 0 and left >= after and (acc >= total * (len(out) + 1) / g or left == after):
+            out.append(cur)
+            cur = []
+    if cur:
+        out.append(cur)
+    return out
 
 
 def decode_bodies(heads: list[dict], host_buf: np.ndarray, offsets: list[int], lengths: list[int], *,
                   device=None, src_dev: torch.Tensor | None = None, align: int = 256,
-                  stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, list[tuple[int, int]]]:
+                  stream: torch.cuda.Stream | None = None,
+                  groups: int | None = None) -> tuple[torch.Tensor, list[tuple[int, int]]]:
     """Decode many vpack bodies that sit in one host buffer (numpy, bytes or a
-    CPU tensor; a pinned tensor is copied in one asynchronous DMA) and
-    optionally already in `src_dev`, with one batched GPU decode.  Returns the
-    device output buffer and each body's (offset, length) in it."""
+    CPU tensor; a pinned tensor is copied in asynchronous DMAs) and optionally
+    already in `src_dev`, with batched GPU decodes.  Returns the device output
+    buffer and each body's (offset, length) in it.
+
+    The upload is enqueued before any host work, so the job records and the
+    plan are built while it runs.  From a pinned host tensor the bodies go up
+    in groups (`body_groups`; `groups` overrides the automatic count) on a
+    copy stream, and each group's decode starts when its bytes have landed, so
+    the upload of one group overlaps the decode of the groups before it."""
     from .. import _device
 
     dev = _device.require_cuda(device)
     upload_src = host_buf
     host_buf = _device.as_u8(host_buf)
-    jobs, spans, raw_copies = [], [], []
-    dst = 0
-    for head, off, ln in zip(heads, offsets, lengths):
-        job, n = body_job(head, off, ln, dst)
-        if job is None:
-            if ln < n:
-                raise EOFError("vpack raw body shorter than its head")
-            raw_copies.append((off, dst, n))
-        else:
-            if "streamed" not in head and int(head["hi_z"]) + int(head["lo"]) > ln:
-                raise EOFError("vpack body shorter than its head")
-            jobs.append(job)
-        spans.append((dst, n))
-        dst += (n + align - 1) // align * align
+    pinned = isinstance(upload_src, torch.Tensor) and upload_src.device.type == "cpu" and upload_src.is_pinned()
+    parts = None
+    if src_dev is None and pinned and any("raw" not in h for h in heads):
+        parts = body_groups(list(offsets), list(lengths), groups)
     with torch.cuda.device(dev):
-        if src_dev is None:
+        comp = stream if stream is not None else torch.cuda.current_stream(dev)
+        events = None
+        if parts is not None and len(parts) > 1:
+            src_dev, events = _upload_groups(dev, upload_src.reshape(-1).view(torch.uint8), offsets, lengths,
+                                             parts, comp)
+        elif src_dev is None:
             src_dev = _device.upload(upload_src, dev, stream=stream)
+        rows, spans, raw_copies, job_of = [], [], [], {}
+        dst = 0
+        for i, (head, off, ln) in enumerate(zip(heads, offsets, lengths)):
+            row, n = _job_row(head, off, ln, dst)
+            if row is None:
+                if ln < n:
+                    raise EOFError("vpack raw body shorter than its head")
+                raw_copies.append((off, dst, n))
+            else:
+                if "streamed" not in head and int(head["hi_z"]) + int(head["lo"]) > ln:
+                    raise EOFError("vpack body shorter than its head")
+                job_of[i] = len(rows)
+                rows.append(row)
+            spans.append((dst, n))
+            dst += (n + align - 1) // align * align
+        jobs = np.array(rows, dtype=JOB_DTYPE) if rows else np.zeros(0, dtype=JOB_DTYPE)
+        if events is not None:
+            out = _decode_grouped(dev, src_dev, events, host_buf, parts, jobs, job_of, raw_copies, dst, comp)
+            return out, spans
         out = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
         for off, d, n in raw_copies:
             out[d:d + n].copy_(src_dev[off:off + n])
-        if jobs:
-            jarr = np.concatenate(jobs)
-            plan = ZstdPlan(host_buf, jarr)
+        if rows:
+            plan = ZstdPlan(host_buf, jobs)
             batch = ZstdBatch(plan, dev)
             batch.run(src_dev, out, stream)
             st = batch.job_status()
@@ -293,6 +367,75 @@ def decode_bodies(heads: list[dict], host_buf: np.ndarray, offsets: list[int], l
                 bad = int(np.nonzero(st)[0][0])
                 raise ZstdError(describe(int(st[bad])))
     return out, spans
+
+
+def _upload_groups(dev, pinned: torch.Tensor, offsets, lengths, parts, comp) -> tuple[torch.Tensor, list]:
+    """The source buffer on the device, each group's byte range copied on the
+    copy stream (in group order) with an event after it."""
+    from .. import _device
+
+    cs = _side_streams(dev, 1)[0]
+    n_src = int(pinned.numel())
+    with torch.cuda.stream(comp):
+        src_dev = torch.empty(n_src + _device.PAD, dtype=torch.uint8, device=dev)
+        src_dev[n_src:].zero_()
+    cs.wait_stream(comp)  # the buffer exists before the copies write it
+    events = []
+    for part in parts:
+        lo = offsets[part[0]]
+        hi = offsets[part[-1]] + lengths[part[-1]]
+        with torch.cuda.stream(cs):
+            src_dev[lo:hi].copy_(pinned[lo:hi], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+        events.append(ev)
+    src_dev.record_stream(cs)
+    return src_dev, events
+
+
+def _decode_grouped(dev, src_dev: torch.Tensor, events: list, host_buf: np.ndarray, parts, jobs: np.ndarray,
+                    job_of: dict, raw_copies, dst: int, comp) -> torch.Tensor:
+    """decode_bodies over body groups: group g's decode runs on a stream of its
+    own once its copy has landed, so the decodes of the groups overlap one
+    another as well as the later copies.  Every kernel read of a body stays
+    inside the source buffer; bytes past a body's end (the next group's,
+    possibly still in flight) never reach its output, as with any neighbouring
+    body.  One status read at the end raises the first failing body's fault."""
+    gs = _side_streams(dev, 1 + len(parts))[1:]
+    with torch.cuda.stream(comp):
+        out = torch.empty(max(dst, 1), dtype=torch.uint8, device=dev)
+    # the plans are built side by side, one host thread each (the native
+    # planner runs without the GIL and starts no threads of its own for
+    # threads=1); each group's decode is enqueued as soon as its plan is ready
+    futs = []
+    for part in parts:
+        idx = [job_of[i] for i in part if i in job_of]
+        futs.append(_plan_pool().submit(ZstdPlan, host_buf, jobs[idx], 1) if idx else None)
+    batches = []
+    for fut, ev, g in zip(futs, events, gs):
+        if fut is None:
+            continue
+        plan = fut.result()
+        g.wait_stream(comp)
+        g.wait_event(ev)
+        with torch.cuda.stream(g):
+            batch = ZstdBatch(plan, dev, stream=g)
+            batch.run(src_dev, out, g)
+        batches.append((batch, g))
+    for b, g in batches:
+        comp.wait_stream(g)
+        for t in (src_dev, out, b.scratch, b.status, b.d_plan):
+            t.record_stream(g)
+    with torch.cuda.stream(comp):
+        comp.wait_event(events[-1])
+        for off, d, n in raw_copies:
+            out[d:d + n].copy_(src_dev[off:off + n])
+        st = torch.cat([b.status[:b.plan.jobs.size] for b, _ in batches]).cpu().numpy().view(np.uint32)
+    st = st | np.concatenate([b.plan.plan_status[:b.plan.jobs.size] for b, _ in batches])
+    if st.any():
+        bad = int(np.nonzero(st)[0][0])
+        raise ZstdError(describe(int(st[bad])))
+    return out
 
 
 def read_tensor_bytes(vpack_dir: str | Path, fname: str, *, device=None) -> tuple[dict, torch.Tensor]:

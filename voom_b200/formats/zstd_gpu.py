@@ -121,10 +121,26 @@ class ZstdPlan:
 class ZstdBatch:
     """A planned batch resident on one device: plan image + scratch."""
 
-    def __init__(self, plan: ZstdPlan, device, scratch: torch.Tensor | None = None):
+    def __init__(self, plan: ZstdPlan, device, scratch: torch.Tensor | None = None,
+                 stream: torch.cuda.Stream | None = None):
+        """`stream` given: the plan image goes up from a pinned copy on that
+        stream without the host waiting for the stream's earlier work (as a
+        pageable upload would), read by a kernel from the mapped pinned copy
+        so that it does not queue behind uploads already on a copy engine."""
         self.plan = plan
         self.device = device
-        self.d_plan = _device.tensor_from_numpy(plan.image, device)
+        if stream is None:
+            self.d_plan = _device.tensor_from_numpy(plan.image, device)
+        else:
+            n = plan.image.nbytes
+            self._h_plan = _device.pinned_empty(n)  # held until the batch is dropped
+            self._h_plan.numpy()[:] = plan.image.reshape(-1).view(np.uint8)
+            self.d_plan = torch.empty(n, dtype=torch.uint8, device=device)
+            rc = load().voom_copy_from_host(self.d_plan.data_ptr(), self._h_plan.data_ptr(), n,
+                                            _device.stream_ptr(device, stream))
+            if rc != 0:  # not mapped pinned memory: an ordinary asynchronous copy
+                with torch.cuda.stream(stream):
+                    self.d_plan.copy_(self._h_plan, non_blocking=True)
         need = int(plan.info.scratch_bytes)
         if scratch is None or scratch.numel() < need:
             scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
