@@ -126,5 +126,7 @@ def upload(host, device: torch.device, *, pad: int = PAD, stream: torch.cuda.Str
 def tensor_from_numpy(arr: np.ndarray, device: torch.device) -> torch.Tensor:
     """Small control arrays (plans, descriptors) -> device uint8 tensor."""
     raw = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
-    host = torch.from_numpy(raw.copy())
+    # a synchronous copy: the array is read before this returns, so a
+    # writable one is wrapped as it is (large plan images are tens of MB)
+    host = torch.from_numpy(raw if raw.flags.writeable else raw.copy())
     return host.to(device, non_blocking=False)

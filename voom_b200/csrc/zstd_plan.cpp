@@ -15,6 +15,7 @@
 #include <new>
 #include <atomic>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/voom_b200.h"
@@ -567,10 +568,10 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   Plan* P = new (std::nothrow) Plan();
   if (!P) return nullptr;
   std::vector<JobPlan> jp(n_jobs);
-  // threads: up to 8 by default (starting a thread costs about as much as
-  // planning a few dozen blocks, and more threads measured slower)
-  const int nt_all =
-      threads > 0 ? threads : int(std::min(8u, std::max(1u, std::thread::hardware_concurrency())));
+  // threads: every core by default, but each thread takes at least a grain
+  // of work (starting a thread costs about as much as planning a few dozen
+  // blocks: 16 threads on a 1,147-block batch measured slower than 8)
+  const int nt_all = threads > 0 ? threads : int(std::max(1u, std::thread::hardware_concurrency()));
   // runs f(i) for i in [0, n) on up to nt_all threads, at least `grain`
   // items each (dynamic assignment)
   auto parallel = [&](uint64_t n, uint64_t grain, auto&& f) {
@@ -585,7 +586,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     for (auto& t : pool) t.join();
   };
   // 1. frame / block walk per job
-  parallel(n_jobs, 32, [&](uint64_t j) {
+  parallel(n_jobs, 256, [&](uint64_t j) {
     if (jobs[j].src + jobs[j].src_len > src_len) { jp[j].bad = true; return; }
     walk_job(h_src, jobs[j], jp[j]);
   });
@@ -593,7 +594,14 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   // direct check and the job's counts
   std::vector<uint64_t> bstart(n_jobs + 1, 0);
   for (uint32_t j = 0; j < n_jobs; j++) bstart[j + 1] = bstart[j] + (jp[j].bad ? 0 : jp[j].blocks.size());
-  std::unique_ptr<BlockTables[]> tabs(new BlockTables[std::max<uint64_t>(1, bstart[n_jobs])]);
+  // uninitialised here: each block's entry is initialised by the thread that
+  // plans it (one thread touching ~700 bytes per block cost milliseconds)
+  static_assert(std::is_trivially_destructible<BlockTables>::value, "freed without destructors");
+  struct FreeTabs {
+    void operator()(BlockTables* t) const { ::operator delete[](t); }
+  };
+  std::unique_ptr<BlockTables, FreeTabs> tabs(static_cast<BlockTables*>(
+      ::operator new[](sizeof(BlockTables) * std::max<uint64_t>(1, bstart[n_jobs]))));
   std::unique_ptr<uint8_t[]> okb(new uint8_t[std::max<uint64_t>(1, bstart[n_jobs])]);
   std::vector<uint8_t> direct(n_jobs, 0);
   std::vector<JobSpan> span(n_jobs);
@@ -602,18 +610,19 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
   std::vector<uint32_t> bjob(bstart[n_jobs]);
   for (uint32_t j = 0; j < n_jobs; j++)
     for (uint64_t g = bstart[j]; g < bstart[j + 1]; g++) bjob[g] = j;
-  parallel(bstart[n_jobs], 64, [&](uint64_t g) {
+  parallel(bstart[n_jobs], 128, [&](uint64_t g) {
     const uint32_t j = bjob[g];
     ZBlock& b = jp[j].blocks[g - bstart[j]];
+    new (tabs.get() + g) BlockTables();
     okb[g] = 1;
     if (b.type != 2) return;
     const uint64_t at = b.src;
     const size_t bs = b.size;
     b.src = 0;
     b.size = 0;
-    okb[g] = plan_compressed(h_src, at, bs, b, tabs[g]) ? 1 : 0;
+    okb[g] = plan_compressed(h_src, at, bs, b, tabs.get()[g]) ? 1 : 0;
   });
-  parallel(n_jobs, 32, [&](uint64_t j) {
+  parallel(n_jobs, 256, [&](uint64_t j) {
     JobPlan& q = jp[j];
     JobSpan& c = span[j];
     memset(&c, 0, sizeof c);
@@ -777,7 +786,7 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     f.al = uint8_t(k == 1 ? 5 : 6);
     S[k] = f;
   }
-  parallel(n_jobs, 32, [&](uint64_t jj) {
+  parallel(n_jobs, 256, [&](uint64_t jj) {
     const uint32_t j = uint32_t(jj);
     ZJob zj;
     memset(&zj, 0, sizeof zj);
@@ -842,6 +851,9 @@ VOOM_API void* voom_zstd_plan_create(const uint8_t* h_src, uint64_t src_len, con
     }
     J[j] = zj;
   });
+  // the per-job lists are released by the workers too (one thread freeing
+  // four small vectors per job took milliseconds on KV page batches)
+  parallel(n_jobs, 256, [&](uint64_t j) { jp[j] = JobPlan(); });
   // each segment's block list ordered by sequence count, most first (stable)
   uint32_t* K1 = reinterpret_cast<uint32_t*>(img + h.off_k1list);
   for (const ZSegment& g : P->segs) {

@@ -153,7 +153,8 @@ def _reload(blobs: list, dev: torch.device, same_shape: bool):
     """Gather the .kvz pages into the device's pinned arena, walk their
     pickles (pages the native walker does not read are unpickled here), plan
     every K and V frame, upload once and decode in one batch.  Returns the
-    output buffer, each page's (shape, K offset, V offset, bytes)."""
+    output buffer, each page's shape (a list), and arrays of each page's K
+    offset, K-to-V distance and bytes per plane."""
     n = len(blobs)
     blobs = list(blobs)
     lens = np.fromiter(map(len, blobs), np.uint64, n)
@@ -222,7 +223,7 @@ def _reload(blobs: list, dev: torch.device, same_shape: bool):
             st = batch.job_status()                    # waits for the decode (and the DMA)
     if st.any():
         raise ZstdError(describe(int(st[np.nonzero(st)[0][0]])))
-    return out, [(shapes[i], int(dst[i]), int(dst[i] + span[i]), int(nbytes[i])) for i in range(n)]
+    return out, shapes, dst, span, nbytes
 
 
 def load_pages(pages: list[_Page]) -> list[tuple[torch.Tensor, torch.Tensor]]:
@@ -243,10 +244,12 @@ def load_pages(pages: list[_Page]) -> list[tuple[torch.Tensor, torch.Tensor]]:
     for _, p in comp:
         with open(p.path, "rb") as f:
             blobs.append(f.read())
-    buf, spans = _reload(blobs, dev, same_shape=False)
-    for (i, _p), (shape, kd, vd, n) in zip(comp, spans):
-        out[i] = (buf[kd:kd + n].view(torch.bfloat16).reshape(shape),
-                  buf[vd:vd + n].view(torch.bfloat16).reshape(shape))
+    buf, shapes, dst, span, nbytes = _reload(blobs, dev, same_shape=False)
+    for k, (i, _p) in enumerate(comp):
+        kd, n = int(dst[k]), int(nbytes[k])
+        vd = kd + int(span[k])
+        out[i] = (buf[kd:kd + n].view(torch.bfloat16).reshape(shapes[k]),
+                  buf[vd:vd + n].view(torch.bfloat16).reshape(shapes[k]))
     return out
 
 
@@ -460,8 +463,8 @@ def reload_blobs(blobs: list[bytes], device=None) -> tuple[torch.Tensor, torch.T
     dev = _device.require_cuda(device)
     if not blobs:
         raise ValueError("reload_blobs needs at least one page")
-    buf, spans = _reload(blobs, dev, same_shape=True)
-    shape, _, _, n = spans[0]
+    buf, shapes, _, _, nbytes = _reload(blobs, dev, same_shape=True)
+    shape, n = shapes[0], int(nbytes[0])
     span = (n + 255) // 256 * 256
     if span == n:
         kv = buf[:2 * n * len(blobs)].view(torch.bfloat16).reshape(len(blobs), 2, *shape)
